@@ -1,0 +1,107 @@
+"""ctypes binding of libdragonwing_cuda.so (include/dw_cuda.h).
+
+The library is built in-tree (``python -m dragonwing_edge_rs_b200.build``).
+Loading fails loudly when it is missing: there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libdragonwing_cuda.so")
+
+# dw_status
+DW_OK = 0
+DW_ERR_INVALID_ARG = 1
+DW_ERR_SIZE_MISMATCH = 2
+DW_ERR_UNSUPPORTED = 3
+DW_ERR_OOM = 4
+DW_ERR_TIMEOUT = 5
+DW_ERR_DEVICE = 6
+DW_ERR_KERNEL_WAIT_EXPIRED = 7
+STATUS_NAMES = {
+    0: "DW_OK", 1: "DW_ERR_INVALID_ARG", 2: "DW_ERR_SIZE_MISMATCH", 3: "DW_ERR_UNSUPPORTED", 4: "DW_ERR_OOM",
+    5: "DW_ERR_TIMEOUT", 6: "DW_ERR_DEVICE", 7: "DW_ERR_KERNEL_WAIT_EXPIRED",
+}
+
+# dw_epilogue
+EPI_NONE, EPI_RELU, EPI_RELU6, EPI_SILU = 0, 1, 2, 3
+# dw_conv_path
+PATH_AUTO, PATH_DIRECT, PATH_UMMA = 0, 1, 2
+
+
+class DwConfig(ctypes.Structure):
+    _fields_ = [("wait_cap_ms", ctypes.c_uint32), ("trace", ctypes.c_int32), ("conv_path", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 5)]
+
+
+class DwConvDesc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "n", "h", "w", "c_in", "c_out", "k_h", "k_w", "stride_h", "stride_w",
+        "pad_t", "pad_l", "pad_b", "pad_r", "group", "epilogue", "q6")] + [("inv_s_out", ctypes.c_float)]
+
+
+# Every exported function with its argument types (restype is dw_status unless listed).
+vp, sz, i32, u32, f32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_float
+PDESC = ctypes.POINTER(DwConvDesc)
+PVP = ctypes.POINTER(ctypes.c_void_p)
+SIGNATURES = {
+    "dw_name": ([], ctypes.c_char_p),
+    "dw_version": ([], ctypes.c_char_p),
+    "dw_create": ([i32, ctypes.POINTER(DwConfig), PVP], i32),
+    "dw_destroy": ([vp], None),
+    "dw_last_error": ([vp], ctypes.c_char_p),
+    "dw_alloc": ([vp, sz, PVP], i32),
+    "dw_buf_wrap": ([vp, vp, sz, PVP], i32),
+    "dw_free": ([vp, vp], i32),
+    "dw_buf_len": ([vp], sz),
+    "dw_buf_device_ptr": ([vp], vp),
+    "dw_upload": ([vp, vp, vp, sz], i32),
+    "dw_download": ([vp, vp, vp, sz], i32),
+    "dw_upload_async": ([vp, vp, sz, vp, sz], i32),
+    "dw_download_async": ([vp, vp, sz, vp, sz], i32),
+    "dw_synchronize": ([vp, u32], i32),
+    "dw_host_alloc": ([vp, sz, PVP], i32),
+    "dw_host_free": ([vp, vp], i32),
+    "dw_stream": ([vp], vp),
+    "dw_sm_count": ([vp], i32),
+    "dw_launch_count": ([vp], ctypes.c_uint64),
+    "dw_debug_expire_wait": ([vp, u32], i32),
+    "dw_prepare_weights_i8": ([vp, PDESC, vp, PVP], i32),
+    "dw_conv2d_i8": ([vp, PDESC, vp, vp, vp, vp, vp, vp], i32),
+    "dw_conv2d_requant_relu_i8": ([vp, vp, vp, vp] + [sz] * 11 + [f32, i32], i32),
+    "dw_conv2d_i8_nhwc": ([vp, vp, vp, vp] + [sz] * 11, i32),
+    "dw_gemm_i8": ([vp, vp, vp, vp, sz, sz, sz], i32),
+    "dw_prepare_gemm_b_i8": ([vp, vp, sz, sz, PVP], i32),
+    "dw_qgemm_i8": ([vp, vp, vp, vp, vp, vp, sz, sz, sz, i32, i32], i32),
+    "dw_requantize_i32_to_i8": ([vp, vp, vp, f32], i32),
+    "dw_relu_i8": ([vp, vp, vp], i32),
+    "dw_add_i8": ([vp, vp, vp, vp, f32, f32], i32),
+    "dw_quantize_f32_to_i8": ([vp, vp, vp, f32], i32),
+    "dw_quantize_u8_to_i8": ([vp, vp, vp, f32], i32),
+    "dw_dequantize_i8_to_f32": ([vp, vp, vp, f32], i32),
+    "dw_maxpool_i8": ([vp, vp, vp] + [sz] * 12, i32),
+    "dw_concat_i8": ([vp, PVP, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, sz, vp], i32),
+    "dw_slice_c_i8": ([vp, vp, vp, sz, sz, sz, sz], i32),
+    "dw_resize_nearest_i8": ([vp, vp, vp] + [sz] * 6, i32),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads the in-tree library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m dragonwing_edge_rs_b200.build` "
+                "(the B200 backend has no CPU fallback)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = lib
+    return _lib

@@ -1,0 +1,103 @@
+// dw_internal.h -- private types shared by the translation units of
+// libdragonwing_cuda.so (backend state, buffers, error plumbing, launchers).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "dw_cuda.h"
+
+// Device-side error record written by kernels whose bounded waits expire
+// (never by trapping).  word[0] = error code (0 = none), word[1] = site,
+// word[2] = block, word[3] = detail.
+enum dw_dev_err : int32_t {
+    DW_DEV_OK = 0,
+    DW_DEV_WAIT_EXPIRED = 1,
+    DW_DEV_BAD_ARG = 2,
+};
+constexpr int kDevErrWords = 4;
+
+struct dw_buf {
+    void *ptr = nullptr;
+    size_t len = 0;
+    bool owned = false;
+};
+
+using PFN_encodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                     const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                     CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                     CUtensorMapFloatOOBfill);
+
+struct dw_backend {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    dw_config cfg{};
+    std::string last_error;
+    int32_t *dev_err = nullptr;       // kDevErrWords ints in device memory
+    int sm_count = 0;
+    uint64_t wait_cap_ns = 0;         // device wait limit, nanoseconds (globaltimer)
+    uint64_t launches = 0;
+    PFN_encodeTiled encode_tiled = nullptr;
+    void *scratch = nullptr;          // per-backend device scratch (tile counters etc.)
+    size_t scratch_len = 0;
+};
+
+// Records an error message on the backend and returns `st`.
+dw_status dw_fail(dw_backend *be, dw_status st, const char *fmt, ...) __attribute__((format(printf, 3, 4)));
+// Maps a CUDA error to DW_ERR_DEVICE with context; DW_OK if e == cudaSuccess.
+dw_status dw_cuda_check(dw_backend *be, cudaError_t e, const char *what);
+// Checks the launch that was just made, counts it, traces it when enabled.
+dw_status dw_after_launch(dw_backend *be, const char *what);
+// Grows (never shrinks) the backend scratch to at least `len` bytes.
+dw_status dw_scratch(dw_backend *be, size_t len, void **out);
+
+// ---- launchers implemented in the kernel translation units ----
+namespace dw {
+
+struct EpiParams {
+    const int32_t *bias;  // may be null
+    const float *M;       // per-channel requant scale (NONE/RELU/RELU6)
+    const float *D;       // per-channel dequant scale (SILU)
+    int32_t epilogue;
+    int32_t q6;
+    float inv_s_out;
+};
+
+// elementwise.cu
+dw_status launch_requantize(dw_backend *be, const int32_t *in, int8_t *out, size_t n, float scale);
+dw_status launch_relu_i8(dw_backend *be, const int8_t *in, int8_t *out, size_t n);
+dw_status launch_add_i8(dw_backend *be, const int8_t *a, const int8_t *b, int8_t *out, size_t n, float ra,
+                        float rb);
+dw_status launch_quantize_f32(dw_backend *be, const float *in, int8_t *out, size_t n, float scale);
+dw_status launch_quantize_u8(dw_backend *be, const uint8_t *in, int8_t *out, size_t n, float scale);
+dw_status launch_dequantize(dw_backend *be, const int8_t *in, float *out, size_t n, float scale);
+dw_status launch_maxpool_i8(dw_backend *be, const int8_t *x, int8_t *y, int n, int h, int w, int c, int kh,
+                            int kw, int sh, int sw, int pt, int pl, int ho, int wo);
+dw_status launch_concat_i8(dw_backend *be, const int8_t *const *xs, const int32_t *cs, int count,
+                           size_t pixels, int8_t *y);
+dw_status launch_slice_c_i8(dw_backend *be, const int8_t *x, int8_t *y, size_t pixels, int c_total, int c0,
+                            int c_len);
+dw_status launch_resize_nearest_i8(dw_backend *be, const int8_t *x, int8_t *y, int n, int hi, int wi, int ho,
+                                   int wo, int c);
+dw_status launch_repack_hwio_to_ohwi(dw_backend *be, const int8_t *w, int8_t *out, int taps, int c_in,
+                                     int c_out);
+dw_status launch_transpose_kn_to_nk(dw_backend *be, const int8_t *b, int8_t *out, int k, int n);
+dw_status launch_expire_wait(dw_backend *be, uint64_t cap_ns);
+
+// conv_direct.cu
+dw_status launch_conv_direct_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
+                                const int8_t *w_ohwi, const EpiParams &ep, int8_t *y, int32_t *acc_out);
+dw_status launch_dwconv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
+                           const int8_t *w_hwcm, const EpiParams &ep, int8_t *y, int32_t *acc_out);
+
+// umma_conv.cu (tcgen05 implicit GEMM)
+bool umma_supported(const dw_backend *be, const dw_conv_desc &d, int ho, int wo);
+dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
+                              const int8_t *w_ohwi, const EpiParams &ep, int8_t *y);
+
+}  // namespace dw

@@ -1,0 +1,396 @@
+// ops.cu -- op entry points of the C ABI: argument and size checks that mirror
+// the reference's (crates/dragonwing-vulkan/src/ops.rs, crates/dragonwing-cpu/src/ops.rs),
+// then dispatch to the kernels.
+
+#include <vector>
+
+#include "dw_internal.h"
+
+namespace {
+
+inline size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
+
+dw_status need(dw_backend *be, const void *p, const char *op, const char *name) {
+    if (!p) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: %s is null", op, name);
+    return DW_OK;
+}
+
+dw_status check_len(dw_backend *be, const dw_buf *b, size_t expected, const char *op, const char *name) {
+    if (b->len != expected)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "%s: %s mismatch: expected %zu, got %zu", op, name, expected, b->len);
+    return DW_OK;
+}
+
+#define DW_TRY(x)                     \
+    do {                              \
+        dw_status _st = (x);          \
+        if (_st != DW_OK) return _st; \
+    } while (0)
+
+// Validates a conv descriptor; computes the output dims.
+dw_status check_desc(dw_backend *be, const dw_conv_desc *d, int *ho, int *wo, const char *op) {
+    if (!d) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: descriptor is null", op);
+    if (d->n <= 0 || d->h <= 0 || d->w <= 0 || d->c_in <= 0 || d->c_out <= 0 || d->k_h <= 0 || d->k_w <= 0 ||
+        d->stride_h <= 0 || d->stride_w <= 0 || d->pad_t < 0 || d->pad_l < 0 || d->pad_b < 0 || d->pad_r < 0)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: dims must be positive and pads non-negative", op);
+    long hp = (long)d->h + d->pad_t + d->pad_b - d->k_h;
+    long wp = (long)d->w + d->pad_l + d->pad_r - d->k_w;
+    if (hp < 0 || wp < 0)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: kernel %dx%d larger than padded input %ldx%ld", op, d->k_h, d->k_w,
+                       hp + d->k_h, wp + d->k_w);
+    *ho = (int)(hp / d->stride_h + 1);
+    *wo = (int)(wp / d->stride_w + 1);
+    if (d->group != 1 && !(d->group == d->c_in && d->c_out % d->c_in == 0))
+        return dw_fail(be, DW_ERR_UNSUPPORTED,
+                       "%s: group=%d unsupported (only 1, or c_in=%d for depthwise with c_out a multiple of c_in)", op,
+                       d->group, d->c_in);
+    if (d->epilogue < DW_EPI_NONE || d->epilogue > DW_EPI_SILU)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: unknown epilogue %d", op, d->epilogue);
+    if (d->epilogue == DW_EPI_RELU6 && (d->q6 < 0 || d->q6 > 127))
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: q6=%d outside [0,127]", op, d->q6);
+    return DW_OK;
+}
+
+size_t weight_len(const dw_conv_desc *d) {
+    size_t taps = (size_t)d->k_h * d->k_w;
+    return d->group == 1 ? taps * d->c_in * d->c_out : taps * d->c_out;
+}
+
+}  // namespace
+
+extern "C" {
+
+DW_API dw_status dw_prepare_weights_i8(dw_backend *be, const dw_conv_desc *d, const dw_buf *w_hwio, dw_buf **out) {
+    const char *op = "prepare_weights_i8";
+    if (!be) return DW_ERR_INVALID_ARG;
+    DW_TRY(need(be, out, op, "out"));
+    *out = nullptr;
+    DW_TRY(need(be, w_hwio, op, "kernel"));
+    int ho, wo;
+    DW_TRY(check_desc(be, d, &ho, &wo, op));
+    DW_TRY(check_len(be, w_hwio, weight_len(d), op, "kernel"));
+    cudaSetDevice(be->device);
+    dw_buf *o = nullptr;
+    DW_TRY(dw_alloc(be, w_hwio->len, &o));
+    dw_status st;
+    if (d->group == 1) {
+        st = dw::launch_repack_hwio_to_ohwi(be, (const int8_t *)w_hwio->ptr, (int8_t *)o->ptr, d->k_h * d->k_w,
+                                            d->c_in, d->c_out);
+    } else {  // depthwise: [kh, kw, C, mult] is already the kernel's layout
+        st = dw_cuda_check(be, cudaMemcpyAsync(o->ptr, w_hwio->ptr, w_hwio->len, cudaMemcpyDeviceToDevice, be->stream),
+                           "prepare depthwise weights");
+    }
+    if (st != DW_OK) {
+        dw_free(be, o);
+        return st;
+    }
+    *out = o;
+    return DW_OK;
+}
+
+static dw_status conv_dispatch(dw_backend *be, const dw_conv_desc *d, int ho, int wo, const dw_buf *x,
+                               const dw_buf *w_prep, const dw::EpiParams &ep, dw_buf *y, const char *op) {
+    const int8_t *xp = (const int8_t *)x->ptr;
+    const int8_t *wp = (const int8_t *)w_prep->ptr;
+    int8_t *yp = (int8_t *)y->ptr;
+    if (d->group != 1) return dw::launch_dwconv_i8(be, *d, ho, wo, xp, wp, ep, yp, nullptr);
+    const int path = be->cfg.conv_path;
+    if (path != DW_PATH_DIRECT && dw::umma_supported(be, *d, ho, wo))
+        return dw::launch_umma_conv_i8(be, *d, ho, wo, xp, wp, ep, yp);
+    if (path == DW_PATH_UMMA)
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: shape not supported by the tensor-core kernel (c_in=%d c_out=%d)",
+                       op, d->c_in, d->c_out);
+    return dw::launch_conv_direct_i8(be, *d, ho, wo, xp, wp, ep, yp, nullptr);
+}
+
+DW_API dw_status dw_conv2d_i8(dw_backend *be, const dw_conv_desc *d, const dw_buf *x, const dw_buf *w_prep,
+                              const dw_buf *bias, const dw_buf *M, const dw_buf *D, dw_buf *y) {
+    const char *op = "conv2d_i8";
+    if (!be) return DW_ERR_INVALID_ARG;
+    int ho, wo;
+    DW_TRY(check_desc(be, d, &ho, &wo, op));
+    DW_TRY(need(be, x, op, "input"));
+    DW_TRY(need(be, w_prep, op, "kernel"));
+    DW_TRY(need(be, y, op, "output"));
+    DW_TRY(check_len(be, x, (size_t)d->n * d->h * d->w * d->c_in, op, "input"));
+    DW_TRY(check_len(be, w_prep, weight_len(d), op, "kernel"));
+    DW_TRY(check_len(be, y, (size_t)d->n * ho * wo * d->c_out, op, "output"));
+    if (bias) DW_TRY(check_len(be, bias, 4 * (size_t)d->c_out, op, "bias"));
+    if (d->epilogue == DW_EPI_SILU) {
+        DW_TRY(need(be, D, op, "D (dequant scales, required by SILU)"));
+        DW_TRY(check_len(be, D, 4 * (size_t)d->c_out, op, "D"));
+    } else {
+        DW_TRY(need(be, M, op, "M (requant scales)"));
+        DW_TRY(check_len(be, M, 4 * (size_t)d->c_out, op, "M"));
+    }
+    cudaSetDevice(be->device);
+    dw::EpiParams ep{bias ? (const int32_t *)bias->ptr : nullptr, M ? (const float *)M->ptr : nullptr,
+                     D ? (const float *)D->ptr : nullptr, d->epilogue, d->q6, d->inv_s_out};
+    return conv_dispatch(be, d, ho, wo, x, w_prep, ep, y, op);
+}
+
+DW_API dw_status dw_conv2d_requant_relu_i8(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio,
+                                           dw_buf *output, size_t n, size_t h_in, size_t w_in, size_t c_in,
+                                           size_t c_out, size_t k_h, size_t k_w, size_t stride_h, size_t stride_w,
+                                           size_t pad_h, size_t pad_w, float requant_scale, int do_relu) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!input || !kernel_hwio || !output) return dw_fail(be, DW_ERR_INVALID_ARG, "conv_fused: null buffer");
+    // crates/dragonwing-vulkan/src/ops.rs:2313-2345 (same checks, same strings)
+    if (c_in % 4 != 0) return dw_fail(be, DW_ERR_INVALID_ARG, "conv_fused: c_in=%zu must be multiple of 4", c_in);
+    if (c_out % 4 != 0)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "conv_fused: c_out=%zu must be multiple of 4 (output is packed)", c_out);
+    if (stride_h == 0 || stride_w == 0 || h_in + 2 * pad_h < k_h || w_in + 2 * pad_w < k_w || n == 0 || k_h == 0 ||
+        k_w == 0)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "conv_fused: invalid geometry");
+    size_t h_out = (h_in + 2 * pad_h - k_h) / stride_h + 1;
+    size_t w_out = (w_in + 2 * pad_w - k_w) / stride_w + 1;
+    size_t expected_input = n * h_in * w_in * c_in;
+    size_t expected_kernel = k_h * k_w * c_in * c_out;
+    size_t expected_output = n * h_out * w_out * c_out;
+    if (input->len != expected_input)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "conv_fused: input mismatch: expected %zu, got %zu", expected_input,
+                       input->len);
+    if (kernel_hwio->len != expected_kernel)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "conv_fused: kernel mismatch: expected %zu, got %zu",
+                       expected_kernel, kernel_hwio->len);
+    if (output->len != expected_output)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "conv_fused: output mismatch: expected %zu, got %zu",
+                       expected_output, output->len);
+    dw_conv_desc d{};
+    d.n = (int32_t)n; d.h = (int32_t)h_in; d.w = (int32_t)w_in; d.c_in = (int32_t)c_in; d.c_out = (int32_t)c_out;
+    d.k_h = (int32_t)k_h; d.k_w = (int32_t)k_w; d.stride_h = (int32_t)stride_h; d.stride_w = (int32_t)stride_w;
+    d.pad_t = d.pad_b = (int32_t)pad_h; d.pad_l = d.pad_r = (int32_t)pad_w;
+    d.group = 1;
+    d.epilogue = do_relu ? DW_EPI_RELU : DW_EPI_NONE;
+    d.q6 = 127;
+    int ho, wo;
+    DW_TRY(check_desc(be, &d, &ho, &wo, "conv_fused"));
+    cudaSetDevice(be->device);
+    // Scratch: [prepared weights | M filled with the scalar requant_scale]
+    void *scr = nullptr;
+    size_t off_m = al256(expected_kernel);
+    DW_TRY(dw_scratch(be, off_m + 4 * c_out, &scr));
+    dw_buf wprep{scr, expected_kernel, false};
+    dw_buf mbuf{(char *)scr + off_m, 4 * c_out, false};
+    DW_TRY(dw::launch_repack_hwio_to_ohwi(be, (const int8_t *)kernel_hwio->ptr, (int8_t *)wprep.ptr, (int)(k_h * k_w),
+                                          (int)c_in, (int)c_out));
+    std::vector<float> ms(c_out, requant_scale);
+    DW_TRY(dw_cuda_check(be, cudaMemcpyAsync(mbuf.ptr, ms.data(), 4 * c_out, cudaMemcpyHostToDevice, be->stream),
+                         "conv_fused: upload requant scale"));
+    // The host vector must outlive the async copy from pageable memory: cudaMemcpyAsync
+    // from pageable memory is staged synchronously before it returns.
+    dw::EpiParams ep{nullptr, (const float *)mbuf.ptr, nullptr, d.epilogue, 127, 0.0f};
+    return conv_dispatch(be, &d, ho, wo, input, &wprep, ep, output, "conv_fused");
+}
+
+DW_API dw_status dw_conv2d_i8_nhwc(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio,
+                                   dw_buf *output_i32, size_t n, size_t h_in, size_t w_in, size_t c_in, size_t c_out,
+                                   size_t k_h, size_t k_w, size_t stride_h, size_t stride_w, size_t pad_h,
+                                   size_t pad_w) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!input || !kernel_hwio || !output_i32) return dw_fail(be, DW_ERR_INVALID_ARG, "conv2d_i8: null buffer");
+    dw_conv_desc d{};
+    d.n = (int32_t)n; d.h = (int32_t)h_in; d.w = (int32_t)w_in; d.c_in = (int32_t)c_in; d.c_out = (int32_t)c_out;
+    d.k_h = (int32_t)k_h; d.k_w = (int32_t)k_w; d.stride_h = (int32_t)stride_h; d.stride_w = (int32_t)stride_w;
+    d.pad_t = d.pad_b = (int32_t)pad_h; d.pad_l = d.pad_r = (int32_t)pad_w;
+    d.group = 1;
+    int ho, wo;
+    DW_TRY(check_desc(be, &d, &ho, &wo, "conv2d_i8"));
+    DW_TRY(check_len(be, input, n * h_in * w_in * c_in, "conv2d_i8", "input"));
+    DW_TRY(check_len(be, kernel_hwio, k_h * k_w * c_in * c_out, "conv2d_i8", "kernel"));
+    DW_TRY(check_len(be, output_i32, 4 * n * (size_t)ho * wo * c_out, "conv2d_i8", "output"));
+    cudaSetDevice(be->device);
+    void *scr = nullptr;
+    DW_TRY(dw_scratch(be, kernel_hwio->len, &scr));
+    DW_TRY(dw::launch_repack_hwio_to_ohwi(be, (const int8_t *)kernel_hwio->ptr, (int8_t *)scr, (int)(k_h * k_w),
+                                          (int)c_in, (int)c_out));
+    dw::EpiParams ep{nullptr, nullptr, nullptr, DW_EPI_NONE, 127, 0.0f};
+    return dw::launch_conv_direct_i8(be, d, ho, wo, (const int8_t *)input->ptr, (const int8_t *)scr, ep, nullptr,
+                                     (int32_t *)output_i32->ptr);
+}
+
+DW_API dw_status dw_gemm_i8(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *c_i32, size_t m, size_t n,
+                            size_t k) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!a || !b || !c_i32) return dw_fail(be, DW_ERR_INVALID_ARG, "gemm_i8: null buffer");
+    if (!m || !n || !k) return dw_fail(be, DW_ERR_INVALID_ARG, "gemm_i8: zero dimension");
+    // crates/dragonwing-cpu/src/ops.rs:2965-2967
+    DW_TRY(check_len(be, a, m * k, "gemm_i8", "A size"));
+    DW_TRY(check_len(be, b, k * n, "gemm_i8", "B size"));
+    DW_TRY(check_len(be, c_i32, 4 * m * n, "gemm_i8", "C size"));
+    cudaSetDevice(be->device);
+    void *scr = nullptr;
+    DW_TRY(dw_scratch(be, k * n, &scr));
+    DW_TRY(dw::launch_transpose_kn_to_nk(be, (const int8_t *)b->ptr, (int8_t *)scr, (int)k, (int)n));
+    dw_conv_desc d{};
+    d.n = 1; d.h = 1; d.w = (int32_t)m; d.c_in = (int32_t)k; d.c_out = (int32_t)n;
+    d.k_h = d.k_w = d.stride_h = d.stride_w = 1;
+    d.group = 1;
+    dw::EpiParams ep{nullptr, nullptr, nullptr, DW_EPI_NONE, 127, 0.0f};
+    return dw::launch_conv_direct_i8(be, d, 1, (int)m, (const int8_t *)a->ptr, (const int8_t *)scr, ep, nullptr,
+                                     (int32_t *)c_i32->ptr);
+}
+
+DW_API dw_status dw_prepare_gemm_b_i8(dw_backend *be, const dw_buf *b_kn, size_t k, size_t n, dw_buf **out) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!b_kn || !out) return dw_fail(be, DW_ERR_INVALID_ARG, "prepare_gemm_b_i8: null argument");
+    *out = nullptr;
+    if (!k || !n) return dw_fail(be, DW_ERR_INVALID_ARG, "prepare_gemm_b_i8: zero dimension");
+    DW_TRY(check_len(be, b_kn, k * n, "prepare_gemm_b_i8", "B size"));
+    cudaSetDevice(be->device);
+    dw_buf *o = nullptr;
+    DW_TRY(dw_alloc(be, k * n, &o));
+    dw_status st = dw::launch_transpose_kn_to_nk(be, (const int8_t *)b_kn->ptr, (int8_t *)o->ptr, (int)k, (int)n);
+    if (st != DW_OK) {
+        dw_free(be, o);
+        return st;
+    }
+    *out = o;
+    return DW_OK;
+}
+
+DW_API dw_status dw_qgemm_i8(dw_backend *be, const dw_buf *a, const dw_buf *b_prep, const dw_buf *bias,
+                             const dw_buf *M, dw_buf *y, size_t m, size_t n, size_t k, int epilogue, int q6) {
+    const char *op = "qgemm_i8";
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!a || !b_prep || !M || !y) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: null buffer", op);
+    if (!m || !n || !k) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: zero dimension", op);
+    if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: dimension exceeds int32", op);
+    if (epilogue == DW_EPI_SILU) return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: SILU epilogue needs D; use conv2d_i8", op);
+    dw_conv_desc d{};
+    d.n = 1; d.h = 1; d.w = (int32_t)m; d.c_in = (int32_t)k; d.c_out = (int32_t)n;
+    d.k_h = d.k_w = d.stride_h = d.stride_w = 1;
+    d.group = 1; d.epilogue = epilogue; d.q6 = q6;
+    int ho, wo;
+    DW_TRY(check_desc(be, &d, &ho, &wo, op));
+    DW_TRY(check_len(be, a, m * k, op, "A size"));
+    DW_TRY(check_len(be, b_prep, k * n, op, "B size"));
+    DW_TRY(check_len(be, y, m * n, op, "Y size"));
+    DW_TRY(check_len(be, M, 4 * n, op, "M size"));
+    if (bias) DW_TRY(check_len(be, bias, 4 * n, op, "bias size"));
+    cudaSetDevice(be->device);
+    dw::EpiParams ep{bias ? (const int32_t *)bias->ptr : nullptr, (const float *)M->ptr, nullptr, epilogue, q6, 0.0f};
+    return conv_dispatch(be, &d, ho, wo, a, b_prep, ep, y, op);
+}
+
+// ---------------------------------------------------------------------------
+// elementwise / glue
+// ---------------------------------------------------------------------------
+
+DW_API dw_status dw_requantize_i32_to_i8(dw_backend *be, const dw_buf *in_i32, dw_buf *out_i8, float scale) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!in_i32 || !out_i8) return dw_fail(be, DW_ERR_INVALID_ARG, "requantize_i32_to_i8: null buffer");
+    if (in_i32->len % 4 || in_i32->len / 4 != out_i8->len)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "requantize_i32_to_i8: length mismatch (%zu i32 bytes vs %zu i8)",
+                       in_i32->len, out_i8->len);
+    cudaSetDevice(be->device);
+    return dw::launch_requantize(be, (const int32_t *)in_i32->ptr, (int8_t *)out_i8->ptr, out_i8->len, scale);
+}
+
+DW_API dw_status dw_relu_i8(dw_backend *be, const dw_buf *in, dw_buf *out) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!in || !out) return dw_fail(be, DW_ERR_INVALID_ARG, "relu_i8: null buffer");
+    if (in->len != out->len) return dw_fail(be, DW_ERR_SIZE_MISMATCH, "relu_i8: length mismatch");
+    cudaSetDevice(be->device);
+    return dw::launch_relu_i8(be, (const int8_t *)in->ptr, (int8_t *)out->ptr, in->len);
+}
+
+DW_API dw_status dw_add_i8(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *out, float scale_a_over_y,
+                           float scale_b_over_y) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!a || !b || !out) return dw_fail(be, DW_ERR_INVALID_ARG, "add_i8: null buffer");
+    // crates/dragonwing-cpu/src/ops.rs:3183-3184
+    if (out->len != a->len) return dw_fail(be, DW_ERR_SIZE_MISMATCH, "add_i8: output/a length mismatch");
+    if (out->len != b->len) return dw_fail(be, DW_ERR_SIZE_MISMATCH, "add_i8: output/b length mismatch");
+    cudaSetDevice(be->device);
+    return dw::launch_add_i8(be, (const int8_t *)a->ptr, (const int8_t *)b->ptr, (int8_t *)out->ptr, out->len,
+                             scale_a_over_y, scale_b_over_y);
+}
+
+DW_API dw_status dw_quantize_f32_to_i8(dw_backend *be, const dw_buf *in_f32, dw_buf *out_i8, float scale) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!in_f32 || !out_i8) return dw_fail(be, DW_ERR_INVALID_ARG, "quantize_f32_to_i8: null buffer");
+    if (in_f32->len % 4 || in_f32->len / 4 != out_i8->len)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "quantize_f32_to_i8: length mismatch");
+    cudaSetDevice(be->device);
+    return dw::launch_quantize_f32(be, (const float *)in_f32->ptr, (int8_t *)out_i8->ptr, out_i8->len, scale);
+}
+
+DW_API dw_status dw_quantize_u8_to_i8(dw_backend *be, const dw_buf *in_u8, dw_buf *out_i8, float scale) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!in_u8 || !out_i8) return dw_fail(be, DW_ERR_INVALID_ARG, "quantize_u8_to_i8: null buffer");
+    if (in_u8->len != out_i8->len) return dw_fail(be, DW_ERR_SIZE_MISMATCH, "quantize_u8_to_i8: length mismatch");
+    cudaSetDevice(be->device);
+    return dw::launch_quantize_u8(be, (const uint8_t *)in_u8->ptr, (int8_t *)out_i8->ptr, out_i8->len, scale);
+}
+
+DW_API dw_status dw_dequantize_i8_to_f32(dw_backend *be, const dw_buf *in_i8, dw_buf *out_f32, float scale) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!in_i8 || !out_f32) return dw_fail(be, DW_ERR_INVALID_ARG, "dequantize_i8_to_f32: null buffer");
+    if (out_f32->len % 4 || out_f32->len / 4 != in_i8->len)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "dequantize_i8_to_f32: length mismatch");
+    cudaSetDevice(be->device);
+    return dw::launch_dequantize(be, (const int8_t *)in_i8->ptr, (float *)out_f32->ptr, in_i8->len, scale);
+}
+
+DW_API dw_status dw_maxpool_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h, size_t w, size_t c,
+                               size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t, size_t p_l, size_t p_b,
+                               size_t p_r) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x || !y) return dw_fail(be, DW_ERR_INVALID_ARG, "maxpool_i8: null buffer");
+    if (!n || !h || !w || !c || !k_h || !k_w || !s_h || !s_w || p_t >= k_h || p_b >= k_h || p_l >= k_w || p_r >= k_w ||
+        h + p_t + p_b < k_h || w + p_l + p_r < k_w)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "maxpool_i8: invalid geometry");
+    size_t ho = (h + p_t + p_b - k_h) / s_h + 1, wo = (w + p_l + p_r - k_w) / s_w + 1;
+    DW_TRY(check_len(be, x, n * h * w * c, "maxpool_i8", "input"));
+    DW_TRY(check_len(be, y, n * ho * wo * c, "maxpool_i8", "output"));
+    cudaSetDevice(be->device);
+    return dw::launch_maxpool_i8(be, (const int8_t *)x->ptr, (int8_t *)y->ptr, (int)n, (int)h, (int)w, (int)c,
+                                 (int)k_h, (int)k_w, (int)s_h, (int)s_w, (int)p_t, (int)p_l, (int)ho, (int)wo);
+}
+
+DW_API dw_status dw_concat_i8(dw_backend *be, const dw_buf *const *xs, const int32_t *channels, int32_t count,
+                              size_t pixels, dw_buf *y) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!xs || !channels || !y || count <= 0 || count > 16 || !pixels)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "concat_i8: need 1..16 inputs and a non-empty output");
+    size_t ct = 0;
+    const int8_t *ptrs[16];
+    for (int i = 0; i < count; i++) {
+        if (!xs[i] || channels[i] <= 0) return dw_fail(be, DW_ERR_INVALID_ARG, "concat_i8: input %d invalid", i);
+        if (xs[i]->len != pixels * (size_t)channels[i])
+            return dw_fail(be, DW_ERR_SIZE_MISMATCH, "concat_i8: input size mismatch (input %d)", i);
+        ct += (size_t)channels[i];
+        ptrs[i] = (const int8_t *)xs[i]->ptr;
+    }
+    DW_TRY(check_len(be, y, pixels * ct, "concat_i8", "output size"));
+    cudaSetDevice(be->device);
+    return dw::launch_concat_i8(be, ptrs, channels, count, pixels, (int8_t *)y->ptr);
+}
+
+DW_API dw_status dw_slice_c_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_t pixels, size_t c_total, size_t c0,
+                               size_t c_len) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x || !y || !pixels || !c_len || c0 + c_len > c_total)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "slice_c_i8: invalid range");
+    DW_TRY(check_len(be, x, pixels * c_total, "slice_c_i8", "input"));
+    DW_TRY(check_len(be, y, pixels * c_len, "slice_c_i8", "output"));
+    cudaSetDevice(be->device);
+    return dw::launch_slice_c_i8(be, (const int8_t *)x->ptr, (int8_t *)y->ptr, pixels, (int)c_total, (int)c0,
+                                 (int)c_len);
+}
+
+DW_API dw_status dw_resize_nearest_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h_in,
+                                      size_t w_in, size_t h_out, size_t w_out, size_t c) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x || !y || !n || !h_in || !w_in || !h_out || !w_out || !c)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "resize_nearest_i8: invalid geometry");
+    DW_TRY(check_len(be, x, n * h_in * w_in * c, "resize_nearest_i8", "input"));
+    DW_TRY(check_len(be, y, n * h_out * w_out * c, "resize_nearest_i8", "output"));
+    cudaSetDevice(be->device);
+    return dw::launch_resize_nearest_i8(be, (const int8_t *)x->ptr, (int8_t *)y->ptr, (int)n, (int)h_in, (int)w_in,
+                                        (int)h_out, (int)w_out, (int)c);
+}
+
+}  // extern "C"

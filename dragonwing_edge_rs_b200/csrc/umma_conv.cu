@@ -1,0 +1,550 @@
+// umma_conv.cu -- tcgen05 (5th-gen tensor core) implicit-GEMM int8 convolution
+// with the fused requantisation epilogue, for sm_100a.
+//
+// GEMM view: rows = output pixels (M), columns = output channels (N),
+// K = (kh, kw, c_in).  One CTA per SM (persistent), warp-specialised:
+//   warp 0      : TMA producer -- per k-block, one A box (activations) and one
+//                 B box (weights) into a ring of shared-memory stages;
+//   warp 1      : TMEM allocator + MMA issuer -- tcgen05.mma.cta_group::1.kind::i8,
+//                 128 x BN x 32 per instruction, int32 accumulators in TMEM,
+//                 double-buffered so the epilogue of tile i overlaps tile i+1;
+//   warps 2..9  : epilogue -- tcgen05.ld accumulators, bias + per-channel
+//                 requant (bit-exact with the reference scalar path) + ReLU/ReLU6/SiLU,
+//                 int8 stores to NHWC.
+//
+// Activation tiles come from TMA boxes of the NHWC input, viewed as a 5-D tensor
+// (c', w', ph, h', n) with c' = (w mod sw)*C + c, w' = w / sw, ph = h mod sh,
+// h' = h / sh, so every box is unit-stride and a stride-s conv reads, for tap
+// (kh, kw), the box at w' = ow0 + floor((kw-pl)/sw), parity (kw-pl) mod sw (and
+// the same along h).  Out-of-range coordinates (the conv's zero padding) are
+// zero-filled by TMA.  1x1 stride-1 convs and QGemm use a flat 2-D view
+// [pixels, C] instead (no spatial tile waste).  The weight operand is the
+// prepared OHWI tensor viewed as (c_in, tap, c_out); channels past c_in in the
+// last k-block are zero-filled, so whatever the A box holds there contributes 0.
+//
+// Every mbarrier wait is bounded (globaltimer); on expiry the CTA records the
+// failure in the backend's device error word, stops issuing, waits (bounded)
+// for its own TMA copies in flight, frees its TMEM and exits.  No multicast
+// TMA is used anywhere (the same code runs on 1..8 GPUs).
+
+#include <algorithm>
+
+#include "dw_device.cuh"
+
+namespace dw {
+namespace {
+
+constexpr int kBM = 128;            // MMA M (rows per tile = pixels)
+constexpr int kEpiWarps = 8;        // epilogue warps (2 per TMEM lane quarter)
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kMaxStages = 12;
+
+struct UmmaParams {
+    // geometry
+    int mode;            // 0 = flat GEMM rows, 1 = spatial tiles
+    int n_img, ho, wo, c_out;
+    int tw, th;          // spatial tile (tw*th <= 128)
+    int tiles_w, tiles_h;
+    int m_tiles, n_tiles, num_tiles;
+    long long rows;      // flat mode: total pixels
+    int taps, kw, sh, sw, pt, pl, c_in;
+    int cblocks;         // k-blocks per tap
+    int bk;              // bytes of K per stage (32/64/128)
+    int bn;              // N per tile
+    int stages;
+    uint32_t a_stage_bytes, b_stage_bytes;  // smem per stage (1 KiB aligned)
+    uint32_t a_tx_bytes, b_tx_bytes;        // bytes TMA delivers per stage
+    uint32_t idesc;
+    uint64_t desc_hi;    // constant upper 32 bits of the smem descriptors
+    uint32_t tmem_cols;
+    uint64_t wait_cap_ns;
+    int32_t *err;
+    EpiParams ep;
+    int8_t *y;
+};
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: true when the phase with `parity` completed; false when the
+// CTA is aborting or the cap expired (then the failure is recorded).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const UmmaParams &p,
+                                          volatile int *abort_flag, int site) {
+#pragma unroll 1
+    for (int i = 0; i < 256; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > p.wait_cap_ns) {
+            *abort_flag = 1;
+            record_error(p.err, DW_DEV_WAIT_EXPIRED, site, (int)parity);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            dst),
+        "l"(map), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
+                                            int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(dst),
+        "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, "
+        "%7}], [%2];" ::"r"(dst),
+        "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 lanes x 16 columns of 32-bit accumulators -> 16 registers per thread.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, int32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (K-major, swizzled): start address >> 4 in
+// bits [0,14); leading-byte offset (unused for swizzled K-major) = 1; the
+// constant high word (stride-byte offset = 8 rows * row bytes, version 1,
+// swizzle mode) is precomputed on the host.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint64_t hi) {
+    return hi | (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16);
+}
+
+// ------------------------------------------------------------------- kernel
+__global__ void __launch_bounds__(kThreads, 1)
+    k_umma_conv_i8(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                   const __grid_constant__ UmmaParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1 KiB-aligned base (swizzle patterns repeat every 1 KiB).
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *a_smem = smem;
+    uint8_t *b_smem = smem + (size_t)p.stages * p.a_stage_bytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(b_smem + (size_t)p.stages * p.b_stage_bytes);
+    uint64_t *full_bar = bars;                      // [stages]
+    uint64_t *empty_bar = bars + kMaxStages;        // [stages]
+    uint64_t *tfull_bar = bars + 2 * kMaxStages;    // [2]
+    uint64_t *tempty_bar = tfull_bar + 2;           // [2]
+    uint64_t *drain_bar = tempty_bar + 2;           // [1] MMA drain on abort
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.stages; s++) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(smem_u32(&tfull_bar[a]), 1);
+            mbar_init(smem_u32(&tempty_bar[a]), kEpiWarps);
+        }
+        mbar_init(smem_u32(drain_bar), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(p.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int k_iters = p.taps * p.cblocks;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_a) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_b) : "memory");
+            int s = 0;
+            uint32_t ph = 0;
+            uint32_t issued_mask = 0, last_parity = 0;  // per stage: issued at least once / parity of last issue
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+                const int n0 = nt * p.bn;
+                int img = 0, oh0 = 0, ow0 = 0;
+                if (p.mode == 1) {
+                    const int tw_i = mt % p.tiles_w;
+                    const int t2 = mt / p.tiles_w;
+                    oh0 = (t2 % p.tiles_h) * p.th;
+                    img = t2 / p.tiles_h;
+                    ow0 = tw_i * p.tw;
+                }
+                for (int it = 0; it < k_iters; it++) {
+                    if (!mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1, p, abort_flag, 1)) { ok = false; break; }
+                    const int tap = it / p.cblocks, cb = it % p.cblocks;
+                    const uint32_t fb = smem_u32(&full_bar[s]);
+                    mbar_expect_tx(fb, p.a_tx_bytes + p.b_tx_bytes);
+                    const uint32_t a_dst = smem_u32(a_smem + (size_t)s * p.a_stage_bytes);
+                    const uint32_t b_dst = smem_u32(b_smem + (size_t)s * p.b_stage_bytes);
+                    if (p.mode == 0) {
+                        tma_load_2d(a_dst, &tmap_a, fb, cb * p.bk, mt * kBM);
+                    } else {
+                        const int kh = tap / p.kw, kw = tap % p.kw;
+                        const int dh = kh - p.pt, dwc = kw - p.pl;
+                        const int par_h = ((dh % p.sh) + p.sh) % p.sh, par_w = ((dwc % p.sw) + p.sw) % p.sw;
+                        const int hq = (dh - par_h) / p.sh, wq = (dwc - par_w) / p.sw;
+                        tma_load_5d(a_dst, &tmap_a, fb, par_w * p.c_in + cb * p.bk, ow0 + wq, par_h, oh0 + hq, img);
+                    }
+                    tma_load_3d(b_dst, &tmap_b, fb, cb * p.bk, tap, n0);
+                    issued_mask |= 1u << s;
+                    last_parity = (last_parity & ~(1u << s)) | (ph << s);
+                    if (++s == p.stages) { s = 0; ph ^= 1; }
+                }
+            }
+            if (!ok) {
+                // Abort: wait (bounded) for this CTA's own copies still in flight.
+                for (int st = 0; st < p.stages; st++) {
+                    if (!(issued_mask & (1u << st))) continue;
+                    const uint32_t par = (last_parity >> st) & 1u;
+                    const uint64_t t0 = globaltimer_ns();
+                    while (!mbar_try_wait(smem_u32(&full_bar[st]), par) && globaltimer_ns() - t0 < p.wait_cap_ns) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int local = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, local++) {
+                const int acc = local & 1;
+                const uint32_t acc_ph = (local >> 1) & 1;
+                if (!mbar_wait(smem_u32(&tempty_bar[acc]), acc_ph ^ 1, p, abort_flag, 2)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * p.bn);
+                for (int it = 0; it < k_iters; it++) {
+                    if (!mbar_wait(smem_u32(&full_bar[s]), ph, p, abort_flag, 3)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(a_smem + (size_t)s * p.a_stage_bytes);
+                    const uint32_t b_addr = smem_u32(b_smem + (size_t)s * p.b_stage_bytes);
+                    for (int k = 0; k < p.bk / 32; k++) {
+                        const uint64_t ad = smem_desc(a_addr + 32 * k, p.desc_hi);
+                        const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
+                        tc_mma_i8(d_tmem, ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
+                    }
+                    tc_commit(smem_u32(&empty_bar[s]));  // frees the stage when these MMAs finish
+                    if (++s == p.stages) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                tc_commit(smem_u32(&tfull_bar[acc]));  // accumulator ready for the epilogue
+            }
+            if (!ok) {
+                // Abort: wait (bounded) until the MMAs already issued have retired,
+                // so TMEM is not freed under them.
+                tc_commit(smem_u32(drain_bar));
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(smem_u32(drain_bar), 0) && globaltimer_ns() - t0 < p.wait_cap_ns) {
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int e = warp - 2;               // 0..7
+        const int quarter = warp & 3;         // TMEM lanes this warp may access
+        const int half = e >> 2;              // which half of the columns
+        const int row = quarter * 32 + lane;  // tile row = pixel
+        const EpiParams ep = p.ep;
+        int local = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, local++) {
+            const int acc = local & 1;
+            const uint32_t acc_ph = (local >> 1) & 1;
+            const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+            const int n0 = nt * p.bn;
+            // output pixel of this row
+            long long pix = -1;
+            if (p.mode == 0) {
+                const long long r = (long long)mt * kBM + row;
+                if (r < p.rows) pix = r;
+            } else {
+                const int tw_i = mt % p.tiles_w;
+                const int t2 = mt / p.tiles_w;
+                const int oh = (t2 % p.tiles_h) * p.th + row / p.tw;
+                const int img = t2 / p.tiles_h;
+                const int ow = tw_i * p.tw + row % p.tw;
+                if (row < p.tw * p.th && oh < p.ho && ow < p.wo) pix = ((long long)img * p.ho + oh) * p.wo + ow;
+            }
+            if (!mbar_wait(smem_u32(&tfull_bar[acc]), acc_ph, p, abort_flag, 4)) { ok = false; break; }
+            tc_fence_after();
+            const int chunks = p.bn / 16;
+            const int c_begin = half * ((chunks + 1) / 2), c_end = min(chunks, c_begin + (chunks + 1) / 2);
+            for (int c = c_begin; c < c_end; c++) {
+                int32_t v[16];
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn + c * 16);
+                tc_ld16(taddr, v);
+                tc_wait_ld();
+                const int oc0 = n0 + c * 16;
+                if (pix >= 0 && oc0 < p.c_out) {
+                    uint32_t w4[4];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        uint32_t packed = 0;
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const int oc = oc0 + q * 4 + j;
+                            const int32_t bias = ep.bias ? __ldg(ep.bias + oc) : 0;
+                            const float m = ep.M ? __ldg(ep.M + oc) : 0.0f;
+                            const float dsc = ep.D ? __ldg(ep.D + oc) : 0.0f;
+                            packed |= (uint32_t)(uint8_t)epilogue_one(v[q * 4 + j], bias, m, dsc, ep.epilogue, ep.q6,
+                                                                      ep.inv_s_out)
+                                      << (8 * j);
+                        }
+                        w4[q] = packed;
+                    }
+                    *reinterpret_cast<int4 *>(p.y + pix * p.c_out + oc0) = make_int4(w4[0], w4[1], w4[2], w4[3]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(p.tmem_cols)
+                     : "memory");
+    }
+}
+
+// ------------------------------------------------------------------- host side
+struct Plan {
+    int mode, tw, th, bk, bn, stages;
+};
+
+int pick_bk(int c_in) {
+    // minimise padded K per tap (ceil(c/bk)*bk); prefer the wider block on ties
+    int best = 128;
+    long best_pad = (long)((c_in + 127) / 128) * 128;
+    for (int bk : {64, 32}) {
+        long pad = (long)((c_in + bk - 1) / bk) * bk;
+        if (pad < best_pad) { best = bk; best_pad = pad; }
+    }
+    return best;
+}
+
+int pick_bn(int c_out) {
+    if (c_out <= 256) return c_out;  // c_out % 16 == 0 is required
+    int best = 16;
+    long best_cost = -1;
+    for (int bn = 256; bn >= 64; bn -= 16) {
+        long tiles = (c_out + bn - 1) / bn;
+        long cost = tiles * bn;  // padded columns
+        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; }
+    }
+    return best;
+}
+
+// Spatial tile: tw*th <= 128 minimising the number of tiles (then prefer wider rows).
+void pick_tile(int ho, int wo, int *tw, int *th) {
+    long best = -1;
+    for (int w = std::min(wo, 128); w >= 1; w--) {
+        int h = std::min(128 / w, ho);
+        if (h < 1) continue;
+        long tiles = (long)((wo + w - 1) / w) * ((ho + h - 1) / h);
+        if (best < 0 || tiles < best) { best = tiles; *tw = w; *th = h; }
+    }
+}
+
+size_t al1k(size_t v) { return (v + 1023) & ~size_t(1023); }
+
+uint32_t swizzle_layout(int bk) { return bk == 128 ? 2u : (bk == 64 ? 4u : 6u); }  // SW128 / SW64 / SW32
+
+CUtensorMapSwizzle swizzle_enum(int bk) {
+    return bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+constexpr size_t kSmemLimit = 227 * 1024;
+
+}  // namespace
+
+bool umma_supported(const dw_backend *be, const dw_conv_desc &d, int ho, int wo) {
+    if (!be->encode_tiled) return false;
+    if (d.group != 1 || d.c_in % 16 || d.c_out % 16) return false;
+    const bool flat = d.k_h == 1 && d.k_w == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_t == 0 &&
+                      d.pad_l == 0 && d.pad_b == 0 && d.pad_r == 0;
+    if (!flat && (d.h % d.stride_h || d.w % d.stride_w)) return false;
+    if ((long long)d.n * ho * wo >= (1ll << 31)) return false;
+    if ((long long)d.k_h * d.k_w >= (1 << 16) || d.k_h * d.k_w * (long long)d.c_in >= (1ll << 31)) return false;
+    return true;
+}
+
+dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
+                              const int8_t *w_ohwi, const EpiParams &ep, int8_t *y) {
+    if (((uintptr_t)x & 15) || ((uintptr_t)w_ohwi & 15) || ((uintptr_t)y & 15))
+        return dw_fail(be, DW_ERR_INVALID_ARG, "conv2d_i8 (tensor-core path): buffers must be 16-byte aligned");
+    UmmaParams p{};
+    const bool flat = d.k_h == 1 && d.k_w == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_t == 0 &&
+                      d.pad_l == 0 && d.pad_b == 0 && d.pad_r == 0;
+    p.mode = flat ? 0 : 1;
+    p.n_img = d.n; p.ho = ho; p.wo = wo; p.c_out = d.c_out;
+    p.taps = d.k_h * d.k_w; p.kw = d.k_w; p.sh = d.stride_h; p.sw = d.stride_w; p.pt = d.pad_t; p.pl = d.pad_l;
+    p.c_in = d.c_in;
+    p.bk = pick_bk(d.c_in);
+    p.bn = pick_bn(d.c_out);
+    p.cblocks = (d.c_in + p.bk - 1) / p.bk;
+    p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
+    if (flat) {
+        p.rows = (long long)d.n * d.h * d.w;
+        p.m_tiles = (int)((p.rows + kBM - 1) / kBM);
+        p.tw = kBM; p.th = 1;
+        p.a_tx_bytes = (uint32_t)(kBM * p.bk);
+    } else {
+        pick_tile(ho, wo, &p.tw, &p.th);
+        p.tiles_w = (wo + p.tw - 1) / p.tw;
+        p.tiles_h = (ho + p.th - 1) / p.th;
+        p.m_tiles = d.n * p.tiles_w * p.tiles_h;
+        p.a_tx_bytes = (uint32_t)(p.tw * p.th * p.bk);
+    }
+    p.num_tiles = p.m_tiles * p.n_tiles;
+    p.b_tx_bytes = (uint32_t)(p.bn * p.bk);
+    p.a_stage_bytes = (uint32_t)al1k((size_t)kBM * p.bk);
+    p.b_stage_bytes = (uint32_t)al1k((size_t)p.bn * p.bk);
+    const size_t fixed = 1024 /*align slack*/ + 256 /*barriers*/;
+    int stages = (int)((kSmemLimit - fixed) / (p.a_stage_bytes + p.b_stage_bytes));
+    p.stages = std::max(2, std::min(stages, kMaxStages));
+    // At least 116 KiB so that a second CTA never fits on the SM: one CTA per SM
+    // owns the tensor memory (its tcgen05.alloc never waits on a neighbour).
+    const size_t smem = std::max<size_t>(fixed + (size_t)p.stages * (p.a_stage_bytes + p.b_stage_bytes), 116 * 1024);
+    if (smem > kSmemLimit) return dw_fail(be, DW_ERR_UNSUPPORTED, "conv2d_i8: tile does not fit in shared memory");
+    // tcgen05 instruction descriptor, kind::i8: D = s32 (bits 4-5 = 2), A = B = s8
+    // (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+    p.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+    // descriptor high word: SBO = 8 rows * bk bytes (>> 4) at bits 32-45, version 1 at bit 46,
+    // swizzle layout at bits 61-63.
+    p.desc_hi = ((uint64_t)((8 * p.bk) >> 4) << 32) | (1ull << 46) | ((uint64_t)swizzle_layout(p.bk) << 61);
+    uint32_t cols = 32;
+    while (cols < (uint32_t)(2 * p.bn)) cols <<= 1;
+    p.tmem_cols = cols;
+    p.wait_cap_ns = be->wait_cap_ns;
+    p.err = be->dev_err;
+    p.ep = ep;
+    p.y = y;
+
+    // ---- tensor maps
+    CUtensorMap ta, tb;
+    CUresult r;
+    const CUtensorMapSwizzle sw = swizzle_enum(p.bk);
+    if (flat) {
+        cuuint64_t dims[2] = {(cuuint64_t)d.c_in, (cuuint64_t)p.rows};
+        cuuint64_t strides[1] = {(cuuint64_t)d.c_in};
+        cuuint32_t box[2] = {(cuuint32_t)p.bk, (cuuint32_t)kBM};
+        cuuint32_t estr[2] = {1, 1};
+        r = be->encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)x, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const int sh = d.stride_h, swd = d.stride_w;
+        cuuint64_t dims[5] = {(cuuint64_t)swd * d.c_in, (cuuint64_t)(d.w / swd), (cuuint64_t)sh, (cuuint64_t)(d.h / sh),
+                              (cuuint64_t)d.n};
+        cuuint64_t strides[4] = {(cuuint64_t)swd * d.c_in, (cuuint64_t)d.w * d.c_in, (cuuint64_t)sh * d.w * d.c_in,
+                                 (cuuint64_t)d.h * d.w * d.c_in};
+        cuuint32_t box[5] = {(cuuint32_t)p.bk, (cuuint32_t)p.tw, 1, (cuuint32_t)p.th, 1};
+        cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+        r = be->encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, (void *)x, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "conv2d_i8: activation tensor map rejected (%d)", (int)r);
+    {
+        cuuint64_t dims[3] = {(cuuint64_t)d.c_in, (cuuint64_t)p.taps, (cuuint64_t)d.c_out};
+        cuuint64_t strides[2] = {(cuuint64_t)d.c_in, (cuuint64_t)p.taps * d.c_in};
+        cuuint32_t box[3] = {(cuuint32_t)p.bk, 1, (cuuint32_t)p.bn};
+        cuuint32_t estr[3] = {1, 1, 1};
+        r = be->encode_tiled(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void *)w_ohwi, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "conv2d_i8: weight tensor map rejected (%d)", (int)r);
+
+    static bool attr_set[16] = {};
+    int dev = be->device;
+    if (dev < 16 && !attr_set[dev]) {
+        cudaFuncSetAttribute(k_umma_conv_i8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+        attr_set[dev] = true;
+    }
+    const int grid = std::min(p.num_tiles, be->sm_count);
+    k_umma_conv_i8<<<grid, kThreads, smem, be->stream>>>(ta, tb, p);
+    return dw_after_launch(be, "umma_conv_i8");
+}
+
+}  // namespace dw

@@ -1,0 +1,168 @@
+"""Op free functions of the B200 backend.
+
+The names, argument order and argument meaning follow the reference's op
+functions (``dragonwing_vulkan::ops`` in crates/dragonwing-vulkan/src/ops.rs and
+``dragonwing_cpu::ops`` in crates/dragonwing-cpu/src/ops.rs): free functions
+taking the backend, input buffers, the output buffer and the NHWC dims.  Every
+function enqueues device work on the backend's stream and raises
+``BackendError`` on any argument or size problem.  The ``*_i8`` functions
+without a reference counterpart implement the build's superset contract of
+the fused op (int32 bias, per-channel requant, ReLU6/SiLU, depthwise).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+from . import _lib as L
+from .backend import CudaBackend, CudaBuffer
+
+EPI_NONE, EPI_RELU, EPI_RELU6, EPI_SILU = L.EPI_NONE, L.EPI_RELU, L.EPI_RELU6, L.EPI_SILU
+
+
+def _h(buf):
+    return None if buf is None else buf.handle
+
+
+# ---------------------------------------------------------------------------
+# Reference op signatures (crates/dragonwing-vulkan/src/ops.rs)
+# ---------------------------------------------------------------------------
+
+def conv2d_requant_relu_i8_packed(backend: CudaBackend, input_packed: CudaBuffer, kernel_packed: CudaBuffer,
+                                  output_packed: CudaBuffer, n, h_in, w_in, c_in, c_out, k_h, k_w,
+                                  stride_h, stride_w, pad_h, pad_w, requant_scale: float, do_relu: bool):
+    """ops.rs:2294-2417: fused int8 conv -> requant(scalar) -> optional ReLU.
+
+    Kernel layout is HWIO (the graph's layout after convert_nchw_to_nhwc)."""
+    backend._check(L.load().dw_conv2d_requant_relu_i8(
+        backend.handle, input_packed.handle, kernel_packed.handle, output_packed.handle,
+        n, h_in, w_in, c_in, c_out, k_h, k_w, stride_h, stride_w, pad_h, pad_w, float(requant_scale),
+        1 if do_relu else 0))
+
+
+def conv2d_i8_nhwc_packed(backend, input_packed, kernel_packed, output_i32, n, h_in, w_in, c_in, c_out,
+                          k_h, k_w, stride_h, stride_w, pad_h, pad_w):
+    """ops.rs:1822: int8 conv to int32 accumulators (HWIO kernel)."""
+    backend._check(L.load().dw_conv2d_i8_nhwc(
+        backend.handle, input_packed.handle, kernel_packed.handle, output_i32.handle,
+        n, h_in, w_in, c_in, c_out, k_h, k_w, stride_h, stride_w, pad_h, pad_w))
+
+
+def gemm_i8_packed(backend, a_packed, b_packed, c_i32, m, n, k):
+    """ops.rs:1723: C_i32[m,n] = A[m,k] @ B[k,n] (row-major int8)."""
+    backend._check(L.load().dw_gemm_i8(backend.handle, a_packed.handle, b_packed.handle, c_i32.handle, m, n, k))
+
+
+def requantize_i32_to_i8_packed(backend, input_i32, output_packed, requant_scale: float):
+    """ops.rs:1998 (cpu ops.rs:3366-3386)."""
+    backend._check(L.load().dw_requantize_i32_to_i8(backend.handle, input_i32.handle, output_packed.handle,
+                                                    float(requant_scale)))
+
+
+def add_i8_packed(backend, a_packed, b_packed, output_packed, scale_a_over_y: float, scale_b_over_y: float):
+    """ops.rs:2105 (cpu ops.rs:3176-3209)."""
+    backend._check(L.load().dw_add_i8(backend.handle, a_packed.handle, b_packed.handle, output_packed.handle,
+                                      float(scale_a_over_y), float(scale_b_over_y)))
+
+
+def relu_i8_packed(backend, input_packed, output_packed):
+    """ops.rs:2179 (cpu ops.rs:3301-3319)."""
+    backend._check(L.load().dw_relu_i8(backend.handle, input_packed.handle, output_packed.handle))
+
+
+def quantize_f32_to_i8_packed(backend, input_f32, output_packed, scale: float):
+    """ops.rs:2032 (cpu ops.rs:3503-3525)."""
+    backend._check(L.load().dw_quantize_f32_to_i8(backend.handle, input_f32.handle, output_packed.handle,
+                                                  float(scale)))
+
+
+def dequantize_i8_packed_to_f32(backend, input_packed, output_f32, scale: float):
+    """ops.rs:2069 (cpu ops.rs:3439-3457)."""
+    backend._check(L.load().dw_dequantize_i8_to_f32(backend.handle, input_packed.handle, output_f32.handle,
+                                                    float(scale)))
+
+
+# ---------------------------------------------------------------------------
+# The fused op contract
+# ---------------------------------------------------------------------------
+
+@dataclass
+class ConvDesc:
+    """OpParams::Conv2dRequantReluI8Nhwc (crates/dragonwing-onnx/src/builder.rs:345-360)
+    plus NHWC dims, bias/per-channel requant and the extended epilogues."""
+
+    n: int
+    h: int
+    w: int
+    c_in: int
+    c_out: int
+    k_h: int = 3
+    k_w: int = 3
+    stride_h: int = 1
+    stride_w: int = 1
+    pads: tuple = (0, 0, 0, 0)  # [top, left, bottom, right]
+    group: int = 1
+    epilogue: int = EPI_NONE
+    q6: int = 127
+    inv_s_out: float = 0.0
+
+    def out_hw(self):
+        pt, pl, pb, pr = self.pads
+        return ((self.h + pt + pb - self.k_h) // self.stride_h + 1,
+                (self.w + pl + pr - self.k_w) // self.stride_w + 1)
+
+    def to_c(self) -> L.DwConvDesc:
+        pt, pl, pb, pr = self.pads
+        return L.DwConvDesc(self.n, self.h, self.w, self.c_in, self.c_out, self.k_h, self.k_w, self.stride_h,
+                            self.stride_w, pt, pl, pb, pr, self.group, self.epilogue, self.q6, self.inv_s_out)
+
+
+def prepare_weights_i8(backend: CudaBackend, desc: ConvDesc, w_hwio: CudaBuffer) -> CudaBuffer:
+    """HWIO (or depthwise [kh,kw,C,mult]) int8 kernel -> the kernels' layout (once)."""
+    out = ctypes.c_void_p()
+    d = desc.to_c()
+    backend._check(L.load().dw_prepare_weights_i8(backend.handle, ctypes.byref(d), w_hwio.handle, ctypes.byref(out)))
+    return CudaBuffer(backend, out, L.load().dw_buf_len(out))
+
+
+def conv2d_i8(backend: CudaBackend, desc: ConvDesc, x: CudaBuffer, w_prep: CudaBuffer, bias, M, D, y: CudaBuffer):
+    """Fused conv: y = epilogue(requant(conv(x, w) + bias)) (contract in include/dw_cuda.h)."""
+    d = desc.to_c()
+    backend._check(L.load().dw_conv2d_i8(backend.handle, ctypes.byref(d), x.handle, w_prep.handle, _h(bias), _h(M),
+                                         _h(D), y.handle))
+
+
+def prepare_gemm_b_i8(backend: CudaBackend, b_kn: CudaBuffer, k: int, n: int) -> CudaBuffer:
+    out = ctypes.c_void_p()
+    backend._check(L.load().dw_prepare_gemm_b_i8(backend.handle, b_kn.handle, k, n, ctypes.byref(out)))
+    return CudaBuffer(backend, out, k * n)
+
+
+def qgemm_i8(backend: CudaBackend, a, b_prep, bias, M, y, m, n, k, epilogue=EPI_NONE, q6=127):
+    """QGemm with int32 bias and per-column requant to int8."""
+    backend._check(L.load().dw_qgemm_i8(backend.handle, a.handle, b_prep.handle, _h(bias), M.handle, y.handle,
+                                        m, n, k, epilogue, q6))
+
+
+def quantize_u8_to_i8(backend, input_u8, output_i8, scale: float):
+    backend._check(L.load().dw_quantize_u8_to_i8(backend.handle, input_u8.handle, output_i8.handle, float(scale)))
+
+
+def maxpool_i8(backend, x, y, n, h, w, c, k_h, k_w, s_h, s_w, pads=(0, 0, 0, 0)):
+    pt, pl, pb, pr = pads
+    backend._check(L.load().dw_maxpool_i8(backend.handle, x.handle, y.handle, n, h, w, c, k_h, k_w, s_h, s_w,
+                                          pt, pl, pb, pr))
+
+
+def concat_i8(backend, xs, channels, pixels, y):
+    arr = (ctypes.c_void_p * len(xs))(*[b.handle.value for b in xs])
+    cs = (ctypes.c_int32 * len(channels))(*channels)
+    backend._check(L.load().dw_concat_i8(backend.handle, ctypes.cast(arr, L.PVP), cs, len(xs), pixels, y.handle))
+
+
+def slice_c_i8(backend, x, y, pixels, c_total, c0, c_len):
+    backend._check(L.load().dw_slice_c_i8(backend.handle, x.handle, y.handle, pixels, c_total, c0, c_len))
+
+
+def resize_nearest_i8(backend, x, y, n, h_in, w_in, h_out, w_out, c):
+    backend._check(L.load().dw_resize_nearest_i8(backend.handle, x.handle, y.handle, n, h_in, w_in, h_out, w_out, c))

@@ -1,0 +1,229 @@
+/*
+ * dw_cuda.h -- C ABI of libdragonwing_cuda.so, the B200 (sm_100a) backend for
+ * the fused quantized convolution path of dragonwing-edge-rs.
+ *
+ * Plain C types only (pointers, sizes, scalars); no CUDA or C++ types appear
+ * in any signature, so a Rust `extern "C"` block, ctypes or cgo can bind it.
+ * Every entry point names the reference interface it replaces (paths relative
+ * to the reference repository root).
+ *
+ * Execution model: one dw_backend per host thread and per GPU.  A backend owns
+ * one CUDA stream; every op is enqueued asynchronously on it.  dw_upload,
+ * dw_download and dw_synchronize are the blocking calls, like the reference's
+ * Backend trait (crates/dragonwing-core/src/backend.rs:127-199).  Buffers are
+ * opaque byte spans with no dtype (backend.rs:21-33).  Errors never truncate
+ * or abort: every call returns a dw_status, and dw_last_error() gives the
+ * reason string (the reference's Error::Backend(String)).
+ */
+#ifndef DW_CUDA_H
+#define DW_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DW_API __attribute__((visibility("default")))
+#else
+#define DW_API
+#endif
+
+/* Status codes.  Mirrors Result<(), Error> (crates/dragonwing-core/src/error.rs:13). */
+typedef enum dw_status {
+    DW_OK = 0,
+    DW_ERR_INVALID_ARG = 1,        /* bad shape, null pointer, unsupported parameter value */
+    DW_ERR_SIZE_MISMATCH = 2,      /* buffer length != expected (backend.rs:160-185) */
+    DW_ERR_UNSUPPORTED = 3,        /* valid op the backend does not implement */
+    DW_ERR_OOM = 4,                /* allocation failed */
+    DW_ERR_TIMEOUT = 5,            /* dw_synchronize deadline passed; work still queued */
+    DW_ERR_DEVICE = 6,             /* CUDA runtime/driver error */
+    DW_ERR_KERNEL_WAIT_EXPIRED = 7 /* a kernel's bounded device-side wait gave up */
+} dw_status;
+
+typedef struct dw_backend dw_backend; /* one GPU + one stream (impl Backend) */
+typedef struct dw_buf dw_buf;         /* device byte buffer (impl BackendBuffer) */
+
+typedef struct dw_config {
+    uint32_t wait_cap_ms; /* limit for every device-side wait (mbarrier/TMA); 0 = 2000 ms */
+    int32_t trace;        /* nonzero: synchronize and log after every op (DRAGONWING_TRACE) */
+    int32_t conv_path;    /* DW_PATH_*: which convolution kernels to use */
+    int32_t reserved[5];
+} dw_config;
+
+enum dw_conv_path {
+    DW_PATH_AUTO = 0,   /* tensor-core (tcgen05) kernels where the shape allows, else CUDA cores */
+    DW_PATH_DIRECT = 1, /* always the CUDA-core direct kernels */
+    DW_PATH_UMMA = 2    /* tensor-core kernels only; DW_ERR_UNSUPPORTED where they do not apply */
+};
+
+/* Epilogue of the fused op.  The reference has NONE and RELU (has_relu,
+ * crates/dragonwing-onnx/src/builder.rs:345-360); RELU6 and SILU extend it. */
+enum dw_epilogue { DW_EPI_NONE = 0, DW_EPI_RELU = 1, DW_EPI_RELU6 = 2, DW_EPI_SILU = 3 };
+
+/* One fused convolution.  Mirrors OpParams::Conv2dRequantReluI8Nhwc
+ * (crates/dragonwing-onnx/src/builder.rs:345-360) plus the NHWC dims the
+ * runtime reads from graph.shapes (vulkan_runtime.rs:1135-1205):
+ *   pads = [top, left, bottom, right]; dilation must be 1 (builder.rs:543-551);
+ *   group == 1 (dense) or group == c_in (depthwise, c_out = c_in * multiplier);
+ *   epilogue = dw_epilogue; q6 = ReLU6 ceiling in the output's int8 domain;
+ *   inv_s_out = 1/s_out (SiLU only). */
+typedef struct dw_conv_desc {
+    int32_t n, h, w, c_in, c_out;
+    int32_t k_h, k_w, stride_h, stride_w;
+    int32_t pad_t, pad_l, pad_b, pad_r;
+    int32_t group;
+    int32_t epilogue;
+    int32_t q6;
+    float inv_s_out;
+} dw_conv_desc;
+
+/* ---------------------------------------------------------------------- */
+/* Backend trait: crates/dragonwing-core/src/backend.rs:127-199           */
+/* ---------------------------------------------------------------------- */
+
+/* Backend::name (backend.rs:141): "cuda-sm100a". */
+DW_API const char *dw_name(void);
+/* Library version string (for logs). */
+DW_API const char *dw_version(void);
+/* Creates a backend on `device_ordinal` (VulkanBackend::new, vulkan/src/lib.rs:97).
+ * cfg may be NULL (defaults).  The DW_WAIT_CAP_MS / DW_TRACE / DW_CONV_PATH
+ * environment variables override the config. */
+DW_API dw_status dw_create(int device_ordinal, const dw_config *cfg, dw_backend **out);
+DW_API void dw_destroy(dw_backend *be);
+/* Reason string of the last failed call on this backend (Error::Backend(String)). */
+DW_API const char *dw_last_error(const dw_backend *be);
+/* Backend::alloc (backend.rs:155).  Zero-length is an error (vulkan/src/lib.rs:257-261).
+ * Contents are unspecified on return. */
+DW_API dw_status dw_alloc(dw_backend *be, size_t len_bytes, dw_buf **out);
+/* Wraps caller-owned device memory (not freed by dw_free). */
+DW_API dw_status dw_buf_wrap(dw_backend *be, void *device_ptr, size_t len_bytes, dw_buf **out);
+DW_API dw_status dw_free(dw_backend *be, dw_buf *buf);
+/* BackendBuffer::len_bytes (backend.rs:21-33). */
+DW_API size_t dw_buf_len(const dw_buf *buf);
+DW_API void *dw_buf_device_ptr(const dw_buf *buf);
+/* Backend::upload (backend.rs:166-173): src_len must equal the buffer length;
+ * complete when the call returns. */
+DW_API dw_status dw_upload(dw_backend *be, dw_buf *dst, const void *src, size_t src_len);
+/* Backend::download (backend.rs:177-185): synchronizes first, then copies. */
+DW_API dw_status dw_download(dw_backend *be, const dw_buf *src, void *dst, size_t dst_len);
+/* Asynchronous twins on the backend stream (host memory should be pinned). */
+DW_API dw_status dw_upload_async(dw_backend *be, dw_buf *dst, size_t dst_offset, const void *src, size_t len);
+DW_API dw_status dw_download_async(dw_backend *be, const dw_buf *src, size_t src_offset, void *dst, size_t len);
+/* Backend::synchronize (backend.rs:187-198) with a deadline: DW_ERR_TIMEOUT when
+ * the queued work has not finished after timeout_ms (0 = no deadline); also
+ * reports DW_ERR_KERNEL_WAIT_EXPIRED if a kernel's bounded wait gave up. */
+DW_API dw_status dw_synchronize(dw_backend *be, uint32_t timeout_ms);
+/* Page-locked host memory for the asynchronous copies. */
+DW_API dw_status dw_host_alloc(dw_backend *be, size_t len_bytes, void **out);
+DW_API dw_status dw_host_free(dw_backend *be, void *ptr);
+/* The backend's cudaStream_t, as an opaque pointer (for event timing). */
+DW_API void *dw_stream(dw_backend *be);
+/* Number of SMs of the backend's GPU. */
+DW_API int dw_sm_count(const dw_backend *be);
+/* Counts kernel launches made through this backend (diagnostics / benchmarks). */
+DW_API uint64_t dw_launch_count(const dw_backend *be);
+/* Test hook: runs one bounded device-side wait on a flag that nothing sets,
+ * with a cap of cap_us microseconds; the kernel gives up and records the
+ * failure, and the next dw_synchronize reports DW_ERR_KERNEL_WAIT_EXPIRED. */
+DW_API dw_status dw_debug_expire_wait(dw_backend *be, uint32_t cap_us);
+
+/* ---------------------------------------------------------------------- */
+/* Fused INT8 convolution (the hot path)                                   */
+/* ---------------------------------------------------------------------- */
+
+/* Repacks an HWIO int8 kernel [k_h, k_w, c_in, c_out] (the layout after
+ * convert_nchw_to_nhwc, crates/dragonwing-onnx/src/graph.rs:261-275, read by
+ * conv2d_i8_nhwc ops.rs:3129) once, at weight-prepare time, into the layout the
+ * kernels read.  Depthwise kernels are [k_h, k_w, c_in, multiplier]
+ * (ops.rs:2669-2730).  *out is a new buffer owned by the caller. */
+DW_API dw_status dw_prepare_weights_i8(dw_backend *be, const dw_conv_desc *d, const dw_buf *w_hwio,
+                                       dw_buf **out);
+
+/* The fused op: y = epilogue(requant(conv(x, w) + bias)).
+ * Replaces conv2d_requant_relu_i8_packed (crates/dragonwing-vulkan/src/ops.rs:2294-2417)
+ * with the build's superset contract:
+ *   acc  = sum x[n, oh*sh+kh-pt, ow*sw+kw-pl, ic] * w[kh,kw,ic,oc]   (i32, OOB taps skipped)
+ *   acc += bias[oc]                                                  (bias may be NULL)
+ *   NONE/RELU/RELU6: q = (int8) roundf(clamp((float)acc * M[oc], -128, 127)),
+ *                    then max(q,0) / min(max(q,0), q6)
+ *   SILU: y = (float)acc * D[oc]; q = (int8) roundf(clamp(silu(y) * inv_s_out, -128, 127))
+ * x: int8 NHWC [n,h,w,c_in]; w_prep from dw_prepare_weights_i8; bias: int32 [c_out];
+ * M, D: float32 [c_out] (M[oc] = (s_in*s_w[oc])/s_out, quantize.rs:245; D[oc] = s_in*s_w[oc]);
+ * y: int8 NHWC [n,h_out,w_out,c_out].  Bit-exact with the reference scalar path. */
+DW_API dw_status dw_conv2d_i8(dw_backend *be, const dw_conv_desc *d, const dw_buf *x, const dw_buf *w_prep,
+                              const dw_buf *bias, const dw_buf *M, const dw_buf *D, dw_buf *y);
+
+/* Exact reference parameter list of conv2d_requant_relu_i8_packed
+ * (crates/dragonwing-vulkan/src/ops.rs:2294-2345): scalar requant_scale, no bias,
+ * HWIO kernel, symmetric pads, same error strings ("conv_fused: ...").  Prepares
+ * the weights internally on every call (use dw_conv2d_i8 to prepare once). */
+DW_API dw_status dw_conv2d_requant_relu_i8(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio,
+                                           dw_buf *output, size_t n, size_t h_in, size_t w_in, size_t c_in,
+                                           size_t c_out, size_t k_h, size_t k_w, size_t stride_h,
+                                           size_t stride_w, size_t pad_h, size_t pad_w, float requant_scale,
+                                           int do_relu);
+
+/* Unfused int8 conv to int32 accumulators: conv2d_i8_nhwc_packed
+ * (crates/dragonwing-vulkan/src/ops.rs:1822), CPU twin conv2d_i8_nhwc (cpu ops.rs:3086). */
+DW_API dw_status dw_conv2d_i8_nhwc(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio,
+                                   dw_buf *output_i32, size_t n, size_t h_in, size_t w_in, size_t c_in,
+                                   size_t c_out, size_t k_h, size_t k_w, size_t stride_h, size_t stride_w,
+                                   size_t pad_h, size_t pad_w);
+
+/* ---------------------------------------------------------------------- */
+/* INT8 GEMM                                                               */
+/* ---------------------------------------------------------------------- */
+
+/* gemm_i8_packed (crates/dragonwing-vulkan/src/ops.rs:1723) / gemm_i8 (cpu ops.rs:2964):
+ * C_i32[m,n] = A[m,k] * B[k,n], both row-major int8. */
+DW_API dw_status dw_gemm_i8(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *c_i32, size_t m,
+                            size_t n, size_t k);
+/* Repacks B [k,n] row-major (a QGemm weight) once into the kernel layout. */
+DW_API dw_status dw_prepare_gemm_b_i8(dw_backend *be, const dw_buf *b_kn, size_t k, size_t n, dw_buf **out);
+/* QGemm with int32 bias[n] (may be NULL), per-column M[n] and the fused
+ * epilogue (NONE/RELU/RELU6; q6 for RELU6): y_i8[m,n].  The same contract as
+ * dw_conv2d_i8 with a 1x1 kernel over m pixels. */
+DW_API dw_status dw_qgemm_i8(dw_backend *be, const dw_buf *a, const dw_buf *b_prep, const dw_buf *bias,
+                             const dw_buf *M, dw_buf *y, size_t m, size_t n, size_t k, int epilogue, int q6);
+
+/* ---------------------------------------------------------------------- */
+/* INT8 elementwise and glue                                               */
+/* ---------------------------------------------------------------------- */
+
+/* requantize_i32_to_i8_packed (vulkan ops.rs:1998) / cpu ops.rs:3366-3386. */
+DW_API dw_status dw_requantize_i32_to_i8(dw_backend *be, const dw_buf *in_i32, dw_buf *out_i8, float scale);
+/* relu_i8_packed (vulkan ops.rs:2179) / cpu ops.rs:3301-3319. */
+DW_API dw_status dw_relu_i8(dw_backend *be, const dw_buf *in, dw_buf *out);
+/* add_i8_packed (vulkan ops.rs:2105) / cpu ops.rs:3176-3209 (OpParams::AddQuantized). */
+DW_API dw_status dw_add_i8(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *out,
+                           float scale_a_over_y, float scale_b_over_y);
+/* quantize_f32_to_i8_packed (vulkan ops.rs:2032) / cpu ops.rs:3503-3525. */
+DW_API dw_status dw_quantize_f32_to_i8(dw_backend *be, const dw_buf *in_f32, dw_buf *out_i8, float scale);
+/* Input quantisation of uint8 images: q = quantize(u8 * (1/255), s) in one pass
+ * (the YOLO input path: u8 -> /255 -> f32 -> quantize). */
+DW_API dw_status dw_quantize_u8_to_i8(dw_backend *be, const dw_buf *in_u8, dw_buf *out_i8, float scale);
+/* dequantize_i8_packed_to_f32 (vulkan ops.rs:2069) / cpu ops.rs:3439-3457. */
+DW_API dw_status dw_dequantize_i8_to_f32(dw_backend *be, const dw_buf *in_i8, dw_buf *out_f32, float scale);
+/* maxpool2d (cpu ops.rs:1513-1551) on int8 NHWC, with pads [t,l,b,r] taken as -inf. */
+DW_API dw_status dw_maxpool_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h, size_t w,
+                               size_t c, size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t,
+                               size_t p_l, size_t p_b, size_t p_r);
+/* concat along channels (cpu concat_f32 axis 3, ops.rs:2141-2246) of `count`
+ * int8 NHWC tensors with channels[i] each over `pixels` pixels. */
+DW_API dw_status dw_concat_i8(dw_backend *be, const dw_buf *const *xs, const int32_t *channels, int32_t count,
+                              size_t pixels, dw_buf *y);
+/* Channel slice [c0, c0+c_len) of an NHWC tensor with c_total channels
+ * (Split/Slice along C, cpu ops.rs:2407, 2532). */
+DW_API dw_status dw_slice_c_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_t pixels, size_t c_total,
+                               size_t c0, size_t c_len);
+/* Nearest resize (cpu resize_f32 Nearest, ops.rs:2320-2348) on int8 NHWC. */
+DW_API dw_status dw_resize_nearest_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h_in,
+                                      size_t w_in, size_t h_out, size_t w_out, size_t c);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DW_CUDA_H */

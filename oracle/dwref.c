@@ -612,3 +612,10 @@ void dwref_maxpool_f16_nhwc(uint16_t *y, const uint16_t *x, size_t n, size_t h, 
                     y[((b * h_out + oh) * w_out + ow) * c + ch] = dwref_f16_from_f32(m);
                 }
 }
+
+/* Input quantisation of a uint8 image: x = (f32)u * (1/255) (the 1/255
+ * normalisation of the YOLO input), then quantize_f32_to_i8 (ops.rs:3503-3525). */
+void dwref_quantize_u8_to_i8(int8_t *out, const uint8_t *in, size_t len, float scale) {
+    float inv255 = 1.0f / 255.0f, inv_scale = 1.0f / scale;
+    for (size_t i = 0; i < len; i++) out[i] = dwref_f32_to_i8(((float)in[i] * inv255) * inv_scale);
+}

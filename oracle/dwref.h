@@ -59,6 +59,7 @@ void dwref_add_i8(int8_t *out, const int8_t *a, const int8_t *b, size_t len,
 void dwref_quantize_f32_to_i8(int8_t *out, const float *in, size_t len, float scale);
 void dwref_dequantize_i8_to_f32(float *out, const int8_t *in, size_t len, float scale);
 int8_t dwref_f32_to_i8(float v);
+void dwref_quantize_u8_to_i8(int8_t *out, const uint8_t *in, size_t len, float scale);
 
 /* ---- crates/dragonwing-core/src/quantization.rs ---- */
 int8_t dwref_quantscale_quantize(float scale, float value);

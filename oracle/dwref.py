@@ -62,6 +62,7 @@ def _declare(L):
         "dwref_add_i8": [vp, vp, vp, sz, f32, f32],
         "dwref_quantize_f32_to_i8": [vp, vp, sz, f32],
         "dwref_dequantize_i8_to_f32": [vp, vp, sz, f32],
+        "dwref_quantize_u8_to_i8": [vp, vp, sz, f32],
         "dwref_per_channel_scales": [vp, vp, sz, sz],
         "dwref_per_channel_quantize": [vp, vp, vp, sz, sz],
         "dwref_conv2d_fused_i8": [vp, vp, vp, vp, vp, vp, ctypes.POINTER(ConvDesc), i32],
@@ -159,6 +160,14 @@ def quantize_f32_to_i8(x, scale):
     x = _c(x, np.float32)
     out = np.empty(x.size, np.int8)
     lib().dwref_quantize_f32_to_i8(_p(out), _p(x), x.size, scale)
+    return out
+
+
+def quantize_u8_to_i8(x, scale):
+    """u8 * (1/255) then quantize_f32_to_i8 (ops.rs:3503-3525)."""
+    x = _c(x, np.uint8)
+    out = np.empty(x.size, np.int8)
+    lib().dwref_quantize_u8_to_i8(_p(out), _p(x), x.size, scale)
     return out
 
 

@@ -1,0 +1,322 @@
+"""GPU parity: every op through the C ABI against the CPU oracle (bit-exact for
+int8), on seeded inputs; the reference KATs through the device path; error
+behaviour; the bounded-wait expiry path."""
+import numpy as np
+import pytest
+
+import dragonwing_edge_rs_b200 as dw
+from dragonwing_edge_rs_b200 import ops
+from dragonwing_edge_rs_b200 import quantization as Q
+from oracle import dwref
+from tests._util import conv_case, cuda_conv, mismatch_report, oracle_conv
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def be():
+    b = dw.CudaBackend(0)
+    yield b
+    b.close()
+
+
+@pytest.fixture(scope="module")
+def be_direct():
+    b = dw.CudaBackend(0, conv_path=dw.PATH_DIRECT)
+    yield b
+    b.close()
+
+
+@pytest.fixture(scope="module")
+def be_umma():
+    b = dw.CudaBackend(0, conv_path=dw.PATH_UMMA)
+    yield b
+    b.close()
+
+
+# ---------------------------------------------------------------- reference KATs
+
+def test_kat_gemm_i8(be):
+    a = be.upload_array(np.array([1, 2, 3, 4, 5, 6], np.int8))
+    b = be.upload_array(np.array([7, 8, 9, 10, 11, 12], np.int8))
+    c = be.alloc(16)
+    ops.gemm_i8_packed(be, a, b, c, 2, 2, 3)
+    assert be.download_array(c, np.int32).tolist() == [58, 64, 139, 154]  # ops.rs:1111-1125
+
+
+def test_kat_conv2d_i8_basic(be):
+    x = be.upload_array(np.ones(25, np.int8))
+    w = be.upload_array(np.ones(9, np.int8))
+    out = be.alloc(9 * 4)
+    ops.conv2d_i8_nhwc_packed(be, x, w, out, 1, 5, 5, 1, 1, 3, 3, 1, 1, 0, 0)
+    assert (be.download_array(out, np.int32) == 9).all()  # ops.rs:1148-1173
+
+
+@pytest.mark.parametrize("acc,scale,expected", [
+    ([1000, 2000, -1000, -2000, 0], 0.1, [100, 127, -100, -128, 0]),
+    ([0, 1000, 5000, -2000, -5000], 0.01, [0, 10, 50, -20, -50]),
+    ([0, 100, -100, 12700, -12700, 25400, -25400, 500, -500, 1234, -1234, 5, -5, 9999, -9999, 12700], 0.01,
+     [0, 1, -1, 127, -127, 127, -128, 5, -5, 12, -12, 0, 0, 100, -100, 127]),
+])
+def test_kat_requantize(be, acc, scale, expected):
+    bi = be.upload_array(np.array(acc, np.int32))
+    bo = be.alloc(len(acc))
+    ops.requantize_i32_to_i8_packed(be, bi, bo, scale)
+    assert be.download_array(bo, np.int8).tolist() == expected
+
+
+def test_kat_add_relu_quant_dequant(be):
+    a = be.upload_array(np.array([10, 20, 30, 40, 50], np.int8))
+    b = be.upload_array(np.array([5, 10, 15, 20, 25], np.int8))
+    o = be.alloc(5)
+    ops.add_i8_packed(be, a, b, o, 1.0, 1.0)
+    assert be.download_array(o, np.int8).tolist() == [15, 30, 45, 60, 75]
+    a = be.upload_array(np.array([100, 100, 100], np.int8))
+    o3 = be.alloc(3)
+    ops.add_i8_packed(be, a, a, o3, 0.5, 0.5)
+    assert be.download_array(o3, np.int8).tolist() == [100, 100, 100]
+    r = be.upload_array(np.array([-50, -10, 0, 10, 50], np.int8))
+    ops.relu_i8_packed(be, r, o)
+    assert be.download_array(o, np.int8).tolist() == [0, 0, 0, 10, 50]
+    f = be.upload_array(np.array([0.0, 5.0, -5.0, 200.0, -200.0], np.float32))
+    ops.quantize_f32_to_i8_packed(be, f, o, 1.0)
+    assert be.download_array(o, np.int8).tolist() == [0, 5, -5, 127, -128]
+    q = be.upload_array(np.array([0, 10, -10, 127, -128], np.int8))
+    fo = be.alloc(20)
+    ops.dequantize_i8_packed_to_f32(be, q, fo, 0.5)
+    assert be.download_array(fo, np.float32).tolist() == [0.0, 5.0, -5.0, 63.5, -64.0]
+
+
+# ---------------------------------------------------------------- elementwise parity
+
+@pytest.mark.parametrize("n", [1, 15, 16, 17, 4099, 1 << 20])
+def test_elementwise_parity(be, n):
+    rng = np.random.default_rng(n)
+    acc = rng.integers(-2**31, 2**31 - 1, n, dtype=np.int64).astype(np.int32)
+    acc[: n // 2] = rng.integers(-30000, 30000, n // 2)
+    bi = be.upload_array(acc)
+    bo = be.alloc(n)
+    for s in (0.001, 0.0123, 7.5e-6):
+        ops.requantize_i32_to_i8_packed(be, bi, bo, s)
+        assert np.array_equal(be.download_array(bo, np.int8), dwref.requantize_i32_to_i8(acc, s))
+    a = rng.integers(-128, 128, n).astype(np.int8)
+    b = rng.integers(-128, 128, n).astype(np.int8)
+    ba, bb = be.upload_array(a), be.upload_array(b)
+    ops.add_i8_packed(be, ba, bb, bo, 0.731, 1.27)
+    assert np.array_equal(be.download_array(bo, np.int8), dwref.add_i8(a, b, 0.731, 1.27))
+    ops.relu_i8_packed(be, ba, bo)
+    assert np.array_equal(be.download_array(bo, np.int8), dwref.relu_i8(a))
+    f = (rng.standard_normal(n) * 3).astype(np.float32)
+    bf = be.upload_array(f)
+    ops.quantize_f32_to_i8_packed(be, bf, bo, 0.037)
+    assert np.array_equal(be.download_array(bo, np.int8), dwref.quantize_f32_to_i8(f, 0.037))
+    bfo = be.alloc(4 * n)
+    ops.dequantize_i8_packed_to_f32(be, ba, bfo, 0.037)
+    assert np.array_equal(be.download_array(bfo, np.float32), dwref.dequantize_i8_to_f32(a, 0.037))
+    u = rng.integers(0, 256, n).astype(np.uint8)
+    bu = be.upload_array(u)
+    ops.quantize_u8_to_i8(be, bu, bo, 0.0123)
+    assert np.array_equal(be.download_array(bo, np.int8), dwref.quantize_u8_to_i8(u, 0.0123))
+
+
+# ---------------------------------------------------------------- fused conv parity
+
+def _check_conv(be, case):
+    desc, x, wt, b, M, D = case
+    y = cuda_conv(be, desc, x, wt, b, M, D)
+    ref = oracle_conv(desc, x, wt, b, M, D)
+    assert np.array_equal(y, ref), mismatch_report(y, ref)
+
+
+def test_config1_bit_exact_both_paths(be_direct, be_umma):
+    """3x3 s1 p1, 1x56x56x64 -> 64, int32 bias, per-channel M, ReLU."""
+    rng = np.random.default_rng(20250101)
+    case = conv_case(rng, 1, 56, 56, 64, 64, k=3, s=1, epilogue=dw.EPI_RELU)
+    _check_conv(be_direct, case)
+    _check_conv(be_umma, case)
+
+
+CONV_SHAPES = [
+    # n, h, w, c_in, c_out, k, s, epilogue
+    (1, 8, 8, 16, 16, 1, 1, dw.EPI_NONE),
+    (2, 13, 11, 32, 48, 1, 1, dw.EPI_RELU),
+    (1, 9, 9, 64, 64, 3, 1, dw.EPI_RELU),
+    (2, 16, 16, 48, 96, 3, 2, dw.EPI_RELU6),
+    (1, 20, 20, 96, 576, 1, 1, dw.EPI_RELU6),
+    (1, 10, 14, 576, 96, 1, 1, dw.EPI_NONE),
+    (1, 40, 40, 32, 64, 3, 2, dw.EPI_SILU),
+    (1, 12, 12, 128, 80, 3, 1, dw.EPI_SILU),
+    (3, 7, 7, 256, 256, 3, 1, dw.EPI_RELU),
+    (1, 30, 50, 16, 32, 3, 1, dw.EPI_SILU),
+    (1, 6, 6, 192, 144, 3, 1, dw.EPI_RELU6),
+    (2, 5, 5, 64, 512, 1, 1, dw.EPI_RELU),
+]
+
+
+@pytest.mark.parametrize("shape", CONV_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("path", ["umma", "direct"])
+def test_conv_parity_sweep(be_direct, be_umma, shape, path):
+    n, h, w, ci, co, k, s, epi = shape
+    rng = np.random.default_rng(hash(shape) & 0xffffffff)
+    case = conv_case(rng, n, h, w, ci, co, k=k, s=s, epilogue=epi)
+    _check_conv(be_umma if path == "umma" else be_direct, case)
+
+
+@pytest.mark.parametrize("pads,k,s", [((0, 0, 0, 0), 3, 1), ((1, 0, 2, 1), 3, 1), ((0, 1, 1, 0), 3, 2),
+                                      ((2, 2, 2, 2), 5, 1), ((1, 1, 1, 1), 3, 2)])
+def test_conv_asymmetric_pads(be, pads, k, s):
+    rng = np.random.default_rng(sum(pads) * 7 + k + s)
+    _check_conv(be, conv_case(rng, 2, 12, 10, 32, 32, k=k, s=s, pads=pads, epilogue=dw.EPI_RELU))
+
+
+def test_conv_odd_channels_direct_fallback(be):
+    """C_in=3 stem (YOLO), C_out not a multiple of 16: CUDA-core path, same contract."""
+    rng = np.random.default_rng(5)
+    _check_conv(be, conv_case(rng, 2, 32, 32, 3, 16, k=3, s=2, epilogue=dw.EPI_SILU))
+    _check_conv(be, conv_case(rng, 1, 9, 9, 8, 12, k=3, s=1, epilogue=dw.EPI_RELU))
+
+
+def test_conv_extreme_values(be_umma, be_direct):
+    """Saturating inputs/weights/bias: int32 accumulators far above 2^24."""
+    rng = np.random.default_rng(9)
+    desc, x, wt, b, M, D = conv_case(rng, 1, 8, 8, 512, 64, k=3, epilogue=dw.EPI_NONE, x_range=(-128, 127))
+    x[:] = -128
+    wt[: wt.size // 2] = -128
+    b = rng.integers(-2**30, 2**30, 64).astype(np.int32)
+    M = rng.uniform(1e-9, 1e-6, 64).astype(np.float32)
+    for be in (be_umma, be_direct):
+        _check_conv(be, (desc, x, wt, b, M, D))
+
+
+@pytest.mark.parametrize("mult,c,epi", [(1, 576, dw.EPI_RELU6), (1, 32, dw.EPI_RELU), (2, 8, dw.EPI_NONE),
+                                         (1, 24, dw.EPI_SILU)])
+def test_depthwise_parity(be, mult, c, epi):
+    rng = np.random.default_rng(c + mult)
+    case = conv_case(rng, 2, 14, 14, c, c * mult, k=3, s=1, group=c, epilogue=epi)
+    _check_conv(be, case)
+    case = conv_case(rng, 1, 15, 15, c, c * mult, k=3, s=2, group=c, epilogue=epi)
+    _check_conv(be, case)
+
+
+def test_reference_shim_exact_signature(be):
+    """conv2d_requant_relu_i8_packed with the reference parameter list (scalar scale,
+    no bias, HWIO kernel) == reference composition conv -> requantize -> relu."""
+    rng = np.random.default_rng(77)
+    for (n, h, w, ci, co, k, s, p, relu) in [(1, 32, 32, 16, 16, 3, 1, 1, True), (1, 16, 16, 64, 64, 3, 1, 1, True),
+                                             (1, 32, 32, 32, 32, 3, 1, 1, False), (2, 9, 9, 4, 8, 3, 2, 0, True)]:
+        x = rng.integers(-64, 64, n * h * w * ci).astype(np.int8)
+        wt = rng.integers(-127, 128, k * k * ci * co).astype(np.int8)
+        ho, wo = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+        bx, bw, by = be.upload_array(x), be.upload_array(wt), be.alloc(n * ho * wo * co)
+        ops.conv2d_requant_relu_i8_packed(be, bx, bw, by, n, h, w, ci, co, k, k, s, s, p, p, 0.001, relu)
+        acc = dwref.conv2d_i8_nhwc(x, wt, n, h, w, ci, co, k, k, s, s, p, p)
+        ref = dwref.requantize_i32_to_i8(acc, 0.001)
+        if relu:
+            ref = dwref.relu_i8(ref)
+        assert np.array_equal(be.download_array(by, np.int8), ref)
+
+
+def test_unfused_conv_i32(be):
+    rng = np.random.default_rng(8)
+    n, h, w, ci, co = 2, 10, 9, 12, 20
+    x = rng.integers(-128, 128, n * h * w * ci).astype(np.int8)
+    wt = rng.integers(-128, 128, 9 * ci * co).astype(np.int8)
+    bx, bw, bo = be.upload_array(x), be.upload_array(wt), be.alloc(4 * n * h * w * co)
+    ops.conv2d_i8_nhwc_packed(be, bx, bw, bo, n, h, w, ci, co, 3, 3, 1, 1, 1, 1)
+    assert np.array_equal(be.download_array(bo, np.int32), dwref.conv2d_i8_nhwc(x, wt, n, h, w, ci, co, 3, 3, 1, 1, 1, 1))
+
+
+# ---------------------------------------------------------------- QGemm
+
+@pytest.mark.parametrize("m,n,k,epi", [(128, 128, 128, dw.EPI_NONE), (200, 80, 96, dw.EPI_RELU),
+                                       (256, 512, 1024, dw.EPI_RELU6), (1000, 48, 64, dw.EPI_NONE)])
+def test_qgemm_parity(be, m, n, k, epi):
+    rng = np.random.default_rng(m * n + k)
+    a = rng.integers(-127, 128, m * k).astype(np.int8)
+    b = rng.integers(-127, 128, k * n).astype(np.int8)
+    bias = rng.integers(-1000, 1001, n).astype(np.int32)
+    M = (rng.uniform(0.001, 0.01, n) * np.float32(0.004) / np.float32(0.05)).astype(np.float32)
+    ba, bb = be.upload_array(a), be.upload_array(b)
+    bp = ops.prepare_gemm_b_i8(be, bb, k, n)
+    y = be.alloc(m * n)
+    ops.qgemm_i8(be, ba, bp, be.upload_array(bias), be.upload_array(M), y, m, n, k, epi, 100)
+    ref = dwref.qgemm_i8(a, b, bias, M, m, n, k, epi, 100, threads=8)
+    got = be.download_array(y, np.int8)
+    assert np.array_equal(got, ref), mismatch_report(got, ref)
+
+
+def test_gemm_i8_i32_random(be):
+    rng = np.random.default_rng(4)
+    m, n, k = 37, 29, 45
+    a = rng.integers(-128, 128, m * k).astype(np.int8)
+    b = rng.integers(-128, 128, k * n).astype(np.int8)
+    c = be.alloc(4 * m * n)
+    ops.gemm_i8_packed(be, be.upload_array(a), be.upload_array(b), c, m, n, k)
+    assert np.array_equal(be.download_array(c, np.int32), dwref.gemm_i8(a, b, m, n, k))
+
+
+# ---------------------------------------------------------------- glue
+
+def test_maxpool_concat_resize_slice(be):
+    rng = np.random.default_rng(12)
+    n, h, w, c = 2, 20, 20, 64
+    x = rng.integers(-128, 128, n * h * w * c).astype(np.int8)
+    bx = be.upload_array(x)
+    by = be.alloc(x.size)
+    ops.maxpool_i8(be, bx, by, n, h, w, c, 5, 5, 1, 1, (2, 2, 2, 2))  # SPPF
+    assert np.array_equal(be.download_array(by, np.int8), dwref.maxpool_i8(x, n, h, w, c, 5, 5, 1, 1, (2, 2, 2, 2)))
+    x3 = rng.integers(-128, 128, n * 11 * 13 * 5).astype(np.int8)
+    b3 = be.upload_array(x3)
+    y3 = be.alloc(n * 5 * 6 * 5)
+    ops.maxpool_i8(be, b3, y3, n, 11, 13, 5, 3, 3, 2, 2, (0, 0, 0, 0))
+    assert np.array_equal(be.download_array(y3, np.int8), dwref.maxpool_i8(x3, n, 11, 13, 5, 3, 3, 2, 2))
+    parts = [rng.integers(-128, 128, 400 * cc).astype(np.int8) for cc in (64, 32, 16, 8)]
+    bufs = [be.upload_array(p) for p in parts]
+    yc = be.alloc(400 * 120)
+    ops.concat_i8(be, bufs, [64, 32, 16, 8], 400, yc)
+    assert np.array_equal(be.download_array(yc, np.int8), dwref.concat_c_i8(parts, [64, 32, 16, 8], 400))
+    ys = be.alloc(400 * 16)
+    ops.slice_c_i8(be, yc, ys, 400, 120, 96, 16)
+    assert np.array_equal(be.download_array(ys, np.int8).reshape(400, 16),
+                          dwref.concat_c_i8(parts, [64, 32, 16, 8], 400).reshape(400, 120)[:, 96:112])
+    yr = be.alloc(n * 40 * 40 * c)
+    ops.resize_nearest_i8(be, bx, yr, n, 20, 20, 40, 40, c)
+    assert np.array_equal(be.download_array(yr, np.int8), dwref.resize_nearest_i8(x, n, 20, 20, 40, 40, c))
+    yr2 = be.alloc(n * 7 * 9 * c)
+    ops.resize_nearest_i8(be, bx, yr2, n, 20, 20, 7, 9, c)
+    assert np.array_equal(be.download_array(yr2, np.int8), dwref.resize_nearest_i8(x, n, 20, 20, 7, 9, c))
+
+
+# ---------------------------------------------------------------- errors
+
+def test_error_strings_and_no_truncation(be):
+    b4 = be.alloc(4)
+    with pytest.raises(dw.BackendError) as ei:
+        be.upload(b4, np.zeros(5, np.uint8))
+    assert ei.value.status == 2 and "length mismatch" in ei.value.message
+    with pytest.raises(dw.BackendError):
+        be.alloc(0)
+    x = be.alloc(1 * 8 * 8 * 6)
+    w = be.alloc(9 * 6 * 8)
+    y = be.alloc(8 * 8 * 8)
+    with pytest.raises(dw.BackendError) as ei:  # vulkan/src/ops.rs:2313-2317
+        ops.conv2d_requant_relu_i8_packed(be, x, w, y, 1, 8, 8, 6, 8, 3, 3, 1, 1, 1, 1, 0.01, True)
+    assert "conv_fused: c_in=6 must be multiple of 4" in ei.value.message
+    x = be.alloc(1 * 8 * 8 * 8)
+    w = be.alloc(9 * 8 * 8)
+    with pytest.raises(dw.BackendError) as ei:
+        ops.conv2d_requant_relu_i8_packed(be, x, w, be.alloc(10), 1, 8, 8, 8, 8, 3, 3, 1, 1, 1, 1, 0.01, True)
+    assert "conv_fused: output mismatch: expected 512, got 10" in ei.value.message
+    be.synchronize(5000)
+
+
+def test_bounded_wait_expiry_reports_and_recovers(be):
+    """A device wait on a flag nothing sets gives up after its cap; the host
+    sees DW_ERR_KERNEL_WAIT_EXPIRED and the context stays usable."""
+    be.synchronize(5000)
+    assert dw._lib.load().dw_debug_expire_wait(be.handle, 2000) == 0
+    with pytest.raises(dw.BackendError) as ei:
+        be.synchronize(10000)
+    assert ei.value.status == dw._lib.DW_ERR_KERNEL_WAIT_EXPIRED
+    be.synchronize(5000)  # error word cleared
+    test_kat_gemm_i8(be)
