@@ -57,10 +57,19 @@ struct UmmaParams {
     uint32_t idesc;
     uint64_t desc_hi;    // constant upper 32 bits of the smem descriptors
     uint32_t tmem_cols;
+    uint32_t off_out, off_chan, off_bars;   // shared-memory layout (bytes from the 1 KiB-aligned base)
+    long long acc_bound;                    // |acc| <= taps * c_in * 128 * 128
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
-    int8_t *y;
+};
+
+// Per-tile channel parameters staged in shared memory (structure of arrays).
+struct ChanSmem {
+    int32_t bias[2][256];
+    float m[2][256];
+    float d[2][256];
+    uint32_t cflags[2][16];  // per 16-channel chunk: bit0 = M finite, bit1 = |acc+bias| < 2^22 guaranteed
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -168,6 +177,156 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, int32_t (&r)[16]) {
 
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
+                 "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t src, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(map),
+                 "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Barrier over `nthreads` threads that also returns the OR of `pred` over them,
+// so every participant takes the same branch afterwards.
+__device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
+// ---------------------------------------------------------------- epilogue math
+// Loads channel `oc`'s parameters and derives its fast-path flags.  Called by
+// every epilogue thread (the ballot needs the whole warp); `et` selects the slot.
+__device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs, int buf, int et, int oc) {
+    int32_t bias = 0;
+    float m = 0.0f, dsc = 0.0f;
+    if (et < p.bn && oc < p.c_out) {
+        bias = p.ep.bias ? __ldg(p.ep.bias + oc) : 0;
+        m = p.ep.M ? __ldg(p.ep.M + oc) : 0.0f;
+        dsc = p.ep.D ? __ldg(p.ep.D + oc) : 0.0f;
+    }
+    const bool finite = isfinite(m);
+    const long long b = bias < 0 ? -(long long)bias : (long long)bias;
+    const bool safe = p.acc_bound + b < (1ll << 22);
+    const uint32_t bf = __ballot_sync(0xffffffffu, finite);
+    const uint32_t bs = __ballot_sync(0xffffffffu, safe);
+    if (et < p.bn) {
+        cs->bias[buf][et] = bias;
+        cs->m[buf][et] = m;
+        cs->d[buf][et] = dsc;
+    }
+    const int lane = et & 31;
+    if ((lane & 15) == 0 && et < p.bn) {
+        const uint32_t sh = lane;  // 0 or 16
+        const uint32_t f = (((bf >> sh) & 0xFFFFu) == 0xFFFFu ? 1u : 0u) | (((bs >> sh) & 0xFFFFu) == 0xFFFFu ? 2u : 0u);
+        cs->cflags[buf][et >> 4] = f;
+    }
+}
+
+// Exact requantisation of one accumulator on the fast path.  Preconditions:
+// |a| < 2^22 (so the magic-number conversion is exact) and m finite.
+//   fa = (float)a exactly; f = fa*m (RN, as the reference); c = clamp(f);
+//   roundf(c) = floor(c + 0.5) for c >= 0 and ceil(c - 0.5) for c < 0, each
+//   computed with directed-rounding adds (floor/ceil preserving), the last add
+//   placing the integer in the low mantissa bits of 1.5*2^23 + q; the low byte
+//   is q in two's complement.
+__device__ __forceinline__ uint32_t requant_fast_byte(int32_t a, float m) {
+    const float fa = __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f);
+    const float f = __fmul_rn(fa, m);
+    const float c = fminf(fmaxf(f, -128.0f), 127.0f);
+    const float hp = __fadd_rd(__fadd_rd(c, 0.5f), 12582912.0f);
+    const float hn = __fadd_ru(__fadd_ru(c, -0.5f), 12582912.0f);
+    return __float_as_uint(c >= 0.0f ? hp : hn) & 0xFFu;
+}
+
+// 16 accumulators (16 consecutive channels of one row) -> 16 int8, packed.
+__device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSmem *cs, int buf, int ch0,
+                                           const UmmaParams &p) {
+    const int epi = p.ep.epilogue;
+    const int32_t *sb = &cs->bias[buf][ch0];
+    const float *sm = &cs->m[buf][ch0];
+    uint32_t w[4];
+    if (epi == DW_EPI_SILU) {
+        const float *sd = &cs->d[buf][ch0];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            uint32_t packed = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int k = q * 4 + j;
+                packed |= (uint32_t)(uint8_t)epilogue_one(v[k], sb[k], 0.0f, sd[k], epi, p.ep.q6, p.ep.inv_s_out)
+                          << (8 * j);
+            }
+            w[q] = packed;
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    const uint32_t fl = cs->cflags[buf][ch0 >> 4];
+    const int4 b4[4] = {reinterpret_cast<const int4 *>(sb)[0], reinterpret_cast<const int4 *>(sb)[1],
+                        reinterpret_cast<const int4 *>(sb)[2], reinterpret_cast<const int4 *>(sb)[3]};
+    const float4 m4[4] = {reinterpret_cast<const float4 *>(sm)[0], reinterpret_cast<const float4 *>(sm)[1],
+                          reinterpret_cast<const float4 *>(sm)[2], reinterpret_cast<const float4 *>(sm)[3]};
+    const int32_t *bb = reinterpret_cast<const int32_t *>(b4);
+    const float *mm = reinterpret_cast<const float *>(m4);
+    int32_t a[16];
+    bool inrange = true;
+#pragma unroll
+    for (int k = 0; k < 16; k++) a[k] = (int32_t)((uint32_t)v[k] + (uint32_t)bb[k]);
+    if (!(fl & 2u)) {
+#pragma unroll
+        for (int k = 0; k < 16; k++) inrange &= (uint32_t)(a[k] + (1 << 22)) < (1u << 23);
+    }
+    if ((fl & 1u) && __all_sync(0xffffffffu, inrange)) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint32_t b0 = requant_fast_byte(a[q * 4 + 0], mm[q * 4 + 0]);
+            const uint32_t b1 = requant_fast_byte(a[q * 4 + 1], mm[q * 4 + 1]);
+            const uint32_t b2 = requant_fast_byte(a[q * 4 + 2], mm[q * 4 + 2]);
+            const uint32_t b3 = requant_fast_byte(a[q * 4 + 3], mm[q * 4 + 3]);
+            w[q] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
+        if (epi == DW_EPI_RELU) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) w[q] = __vmaxs4(w[q], 0u);
+        } else if (epi == DW_EPI_RELU6) {
+            const uint32_t c6 = 0x01010101u * (uint32_t)p.ep.q6;
+#pragma unroll
+            for (int q = 0; q < 4; q++) w[q] = __vmins4(__vmaxs4(w[q], 0u), c6);
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            uint32_t packed = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int k = q * 4 + j;
+                packed |= (uint32_t)(uint8_t)epilogue_one(v[k], bb[k], mm[k], 0.0f, epi, p.ep.q6, p.ep.inv_s_out)
+                          << (8 * j);
+            }
+            w[q] = packed;
+        }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // Shared-memory matrix descriptor (K-major, swizzled): start address >> 4 in
 // bits [0,14); leading-byte offset (unused for swizzled K-major) = 1; the
 // constant high word (stride-byte offset = 8 rows * row bytes, version 1,
@@ -179,13 +338,15 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint64_t hi) {
 // ------------------------------------------------------------------- kernel
 __global__ void __launch_bounds__(kThreads, 1)
     k_umma_conv_i8(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const __grid_constant__ UmmaParams p) {
+                   const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ UmmaParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1 KiB-aligned base (swizzle patterns repeat every 1 KiB).
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *a_smem = smem;
     uint8_t *b_smem = smem + (size_t)p.stages * p.a_stage_bytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(b_smem + (size_t)p.stages * p.b_stage_bytes);
+    uint8_t *out_stage = smem + p.off_out;                          // [128 rows][bn] int8 output tile
+    ChanSmem *chan = reinterpret_cast<ChanSmem *>(smem + p.off_chan);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bars);
     uint64_t *full_bar = bars;                      // [stages]
     uint64_t *empty_bar = bars + kMaxStages;        // [stages]
     uint64_t *tfull_bar = bars + 2 * kMaxStages;    // [2]
@@ -317,64 +478,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------------------ epilogue
         const int e = warp - 2;               // 0..7
+        const int et = threadIdx.x - 64;      // 0..255 epilogue thread index
         const int quarter = warp & 3;         // TMEM lanes this warp may access
         const int half = e >> 2;              // which half of the columns
-        const int row = quarter * 32 + lane;  // tile row = pixel
-        const EpiParams ep = p.ep;
+        const int row = quarter * 32 + lane;  // tile row
         int local = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, local++) {
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
             const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
             const int n0 = nt * p.bn;
-            // output pixel of this row
-            long long pix = -1;
-            if (p.mode == 0) {
-                const long long r = (long long)mt * kBM + row;
-                if (r < p.rows) pix = r;
-            } else {
-                const int tw_i = mt % p.tiles_w;
-                const int t2 = mt / p.tiles_w;
-                const int oh = (t2 % p.tiles_h) * p.th + row / p.tw;
-                const int img = t2 / p.tiles_h;
-                const int ow = tw_i * p.tw + row % p.tw;
-                if (row < p.tw * p.th && oh < p.ho && ow < p.wo) pix = ((long long)img * p.ho + oh) * p.wo + ow;
-            }
-            if (!mbar_wait(smem_u32(&tfull_bar[acc]), acc_ph, p, abort_flag, 4)) { ok = false; break; }
+            // Stage this tile's per-channel parameters (one channel per thread).
+            stage_channel(p, chan, acc, et, n0 + et);
+            bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), acc_ph, p, abort_flag, 4);
+            // Barrier A (epilogue threads only): all-or-none abort decision; the
+            // staging buffer is free again (the store issuer waited for the
+            // previous store's reads before arriving).
+            if (et == 0) bulk_wait_read0();
+            if (named_barrier_or(1, kEpiWarps * 32, !ok)) break;
             tc_fence_after();
             const int chunks = p.bn / 16;
-            const int c_begin = half * ((chunks + 1) / 2), c_end = min(chunks, c_begin + (chunks + 1) / 2);
+            const int per_half = (chunks + 1) / 2;
+            const int c_begin = half * per_half, c_end = min(chunks, c_begin + per_half);
+            const uint32_t trow = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
+            uint8_t *srow = out_stage + (size_t)row * p.bn;
             for (int c = c_begin; c < c_end; c++) {
                 int32_t v[16];
-                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn + c * 16);
-                tc_ld16(taddr, v);
+                tc_ld16(trow + (uint32_t)(c * 16), v);
                 tc_wait_ld();
-                const int oc0 = n0 + c * 16;
-                if (pix >= 0 && oc0 < p.c_out) {
-                    uint32_t w4[4];
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        uint32_t packed = 0;
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const int oc = oc0 + q * 4 + j;
-                            const int32_t bias = ep.bias ? __ldg(ep.bias + oc) : 0;
-                            const float m = ep.M ? __ldg(ep.M + oc) : 0.0f;
-                            const float dsc = ep.D ? __ldg(ep.D + oc) : 0.0f;
-                            packed |= (uint32_t)(uint8_t)epilogue_one(v[q * 4 + j], bias, m, dsc, ep.epilogue, ep.q6,
-                                                                      ep.inv_s_out)
-                                      << (8 * j);
-                        }
-                        w4[q] = packed;
-                    }
-                    *reinterpret_cast<int4 *>(p.y + pix * p.c_out + oc0) = make_int4(w4[0], w4[1], w4[2], w4[3]);
-                }
+                const uint4 q = requant16(v, chan, acc, c * 16, p);
+                *reinterpret_cast<uint4 *>(srow + c * 16) = q;
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+            if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));  // TMEM buffer free for the MMA warp
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging writes -> async proxy
+            named_barrier_sync(2, kEpiWarps * 32);
+            if (et == 0) {
+                if (p.mode == 0) {
+                    tma_store_2d(&tmap_y, smem_u32(out_stage), n0, mt * kBM);
+                } else {
+                    const int tw_i = mt % p.tiles_w;
+                    const int t2 = mt / p.tiles_w;
+                    tma_store_4d(&tmap_y, smem_u32(out_stage), n0, tw_i * p.tw, (t2 % p.tiles_h) * p.th,
+                                 t2 / p.tiles_h);
+                }
+                bulk_commit();
+            }
         }
+        if (et == 0) bulk_wait_all0();
     }
 
     tc_fence_before();
@@ -479,12 +631,18 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
     p.b_tx_bytes = (uint32_t)(p.bn * p.bk);
     p.a_stage_bytes = (uint32_t)al1k((size_t)kBM * p.bk);
     p.b_stage_bytes = (uint32_t)al1k((size_t)p.bn * p.bk);
-    const size_t fixed = 1024 /*align slack*/ + 256 /*barriers*/;
+    const size_t out_bytes = al1k((size_t)kBM * p.bn);
+    const size_t chan_bytes = al1k(sizeof(ChanSmem));
+    const size_t fixed = 1024 /*align slack*/ + out_bytes + chan_bytes + 256 /*barriers*/;
     int stages = (int)((kSmemLimit - fixed) / (p.a_stage_bytes + p.b_stage_bytes));
     p.stages = std::max(2, std::min(stages, kMaxStages));
+    p.off_out = (uint32_t)((size_t)p.stages * (p.a_stage_bytes + p.b_stage_bytes));
+    p.off_chan = (uint32_t)(p.off_out + out_bytes);
+    p.off_bars = (uint32_t)(p.off_chan + chan_bytes);
+    p.acc_bound = (long long)p.taps * d.c_in * 16384ll;
     // At least 116 KiB so that a second CTA never fits on the SM: one CTA per SM
     // owns the tensor memory (its tcgen05.alloc never waits on a neighbour).
-    const size_t smem = std::max<size_t>(fixed + (size_t)p.stages * (p.a_stage_bytes + p.b_stage_bytes), 116 * 1024);
+    const size_t smem = std::max<size_t>(1024 + p.off_bars + 256, 116 * 1024);
     if (smem > kSmemLimit) return dw_fail(be, DW_ERR_UNSUPPORTED, "conv2d_i8: tile does not fit in shared memory");
     // tcgen05 instruction descriptor, kind::i8: D = s32 (bits 4-5 = 2), A = B = s8
     // (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
@@ -498,7 +656,6 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
     p.wait_cap_ns = be->wait_cap_ns;
     p.err = be->dev_err;
     p.ep = ep;
-    p.y = y;
 
     // ---- tensor maps
     CUtensorMap ta, tb;
@@ -535,6 +692,26 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
     if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "conv2d_i8: weight tensor map rejected (%d)", (int)r);
+    // Output: TMA stores of the staged [rows][bn] tile; out-of-range rows/pixels are clipped.
+    CUtensorMap ty;
+    if (flat) {
+        cuuint64_t dims[2] = {(cuuint64_t)d.c_out, (cuuint64_t)p.rows};
+        cuuint64_t strides[1] = {(cuuint64_t)d.c_out};
+        cuuint32_t box[2] = {(cuuint32_t)p.bn, (cuuint32_t)kBM};
+        cuuint32_t estr[2] = {1, 1};
+        r = be->encode_tiled(&ty, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)y, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        cuuint64_t dims[4] = {(cuuint64_t)d.c_out, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)d.n};
+        cuuint64_t strides[3] = {(cuuint64_t)d.c_out, (cuuint64_t)wo * d.c_out, (cuuint64_t)ho * wo * d.c_out};
+        cuuint32_t box[4] = {(cuuint32_t)p.bn, (cuuint32_t)p.tw, (cuuint32_t)p.th, 1};
+        cuuint32_t estr[4] = {1, 1, 1, 1};
+        r = be->encode_tiled(&ty, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void *)y, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "conv2d_i8: output tensor map rejected (%d)", (int)r);
 
     static bool attr_set[16] = {};
     int dev = be->device;
@@ -543,7 +720,7 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
         attr_set[dev] = true;
     }
     const int grid = std::min(p.num_tiles, be->sm_count);
-    k_umma_conv_i8<<<grid, kThreads, smem, be->stream>>>(ta, tb, p);
+    k_umma_conv_i8<<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
     return dw_after_launch(be, "umma_conv_i8");
 }
 
