@@ -1,0 +1,459 @@
+#!/usr/bin/env python3
+"""Benchmark of the fused-INT8 convolution path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (one process per GPU)
+
+A step is one forward pass of the workload graph over one batch of synthetic
+int8 input already resident in HBM, replayed from a CUDA graph.  Each rank
+runs its own replica on its own batch slice (no collective on the data path:
+weak scaling); torch.distributed (NCCL) is used only for the barrier and the
+max-over-ranks of the device-timed region.  Rank 0 prints one JSON line.
+
+Workloads (synthetic data and weights with the configs' shapes and value
+distributions, seeded):
+  mbv2_block  MobileNetV2 inverted-residual block, batch 32 per GPU, 112x112x96,
+              1x1 expand 576 + ReLU6, depthwise 3x3 + ReLU6, 1x1 project 96,
+              residual add with requantisation.
+
+--impl reference times the reference's CPU implementation of the same
+workload (the oracle restatement of dragonwing-cpu's scalar ops, all host
+threads) on rank 0 over a bounded sample of images per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "fused INT8 conv TOPS (% peak); YOLO-shape images/sec at 1/2/4/8 B200 vs CPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling (nvidia-smi, during the timed region)
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t_start = self.t_end = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def mark_start(self):
+        self.t_start = time.time()
+
+    def mark_end(self):
+        self.t_end = time.time()
+
+    def stop(self):
+        if self.proc:
+            time.sleep(0.12)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for t, line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            rows.append((t, parts))
+        inside = [r for r in rows if self.t_start and self.t_end and self.t_start - 0.06 <= r[0] <= self.t_end + 0.06]
+        use = inside if inside else rows[-3:]
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(p[2]) for _, p in use if num(p[2]) is not None]
+        smax = [num(p[3]) for _, p in use if num(p[3]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for _, p in use:
+            for i, nm in enumerate(names):
+                if p[6 + i].lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(use), "in_region": bool(inside)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+def build_workload(name: str, batch: int, seed: int):
+    from dragonwing_edge_rs_b200 import graph as G
+    if name == "mbv2_block":
+        g = G.mobilenetv2_block(batch=batch, seed=seed)
+        cfg = {"workload": "mobilenetv2_int8_block (BASELINE config 2)", "batch_per_gpu": batch,
+               "input": "112x112x96 int8", "expand": 576, "layers": "1x1 expand+ReLU6, dw3x3+ReLU6, 1x1 project, add"}
+        return g, cfg
+    raise SystemExit(f"unknown workload {name}")
+
+
+def workload_defaults(name):
+    return {"mbv2_block": 32}[name]
+
+
+def op_bytes(graph, op):
+    """Algorithmic (compulsory) bytes of one op: inputs + weights/scales + outputs, each once."""
+    t = graph.tensors
+    total = 0
+    for i in op.inputs:
+        if i in t:
+            total += t[i].nbytes
+        elif i in graph.initializers:
+            total += graph.initializers[i].nbytes
+    for o in op.outputs:
+        total += t[o].nbytes
+    return total
+
+
+def op_flops(op):
+    if op.op_type != "Conv2dRequantReluI8Nhwc":
+        return 0
+    d = op.params["desc"]
+    ho, wo = d.out_hw()
+    return 2 * d.n * ho * wo * d.c_out * d.k_h * d.k_w * (d.c_in if d.group == 1 else 1)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    import dragonwing_edge_rs_b200 as dw
+    from dragonwing_edge_rs_b200.graph import CudaGraphRuntime
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180))
+        dist = tdist
+
+    def barrier():
+        if dist:
+            t = torch.zeros(1, device="cuda")
+            dist.all_reduce(t)
+            torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    batch = args.batch or workload_defaults(args.workload)
+    graph, cfg = build_workload(args.workload, batch, seed=1234)
+    be = dw.CudaBackend(local_rank)
+    rt = CudaGraphRuntime(graph, be)
+    rng = np.random.default_rng(1000 + rank)
+    x_name = graph.inputs[0]
+    xt = graph.tensors[x_name]
+    x_host = rng.integers(-128, 128, xt.nbytes).astype(np.int8)
+    rt.set_input_bytes(x_name, x_host)
+    kernels_per_step = rt.capture()
+    stream = torch.cuda.ExternalStream(be.stream())
+    step_ops = graph.conv_ops()
+    out_name = graph.outputs[0]
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        rt.run()
+    be.synchronize(120000)
+
+    # ---- timed region: K graph replays, inputs resident in HBM
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.2)
+    barrier()
+    be.synchronize(120000)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = be.launch_count()
+    sampler.mark_start()
+    e0.record(stream)
+    for _ in range(args.steps):
+        rt.run()
+    e1.record(stream)
+    be.synchronize(600000)
+    sampler.mark_end()
+    torch.cuda.synchronize()
+    barrier()
+    launches = be.launch_count() - launches0
+    sampler.stop()
+    ms_local = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms_local)
+    ms_per_step = ms / args.steps
+    clocks = sampler.summary()
+
+    # ---- per-op device time (eager dispatch bracketed by events on the launch stream)
+    n_ops = len(rt._dispatch)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ops + 1)] for _ in range(args.kernel_steps)]
+    be.synchronize(120000)
+    for s in range(args.kernel_steps):
+        evs[s][0].record(stream)
+        for i, fn in enumerate(rt._dispatch):
+            fn()
+            evs[s][i + 1].record(stream)
+    be.synchronize(600000)
+    op_ms = [sum(evs[s][i].elapsed_time(evs[s][i + 1]) for s in range(args.kernel_steps)) / args.kernel_steps
+             for i in range(n_ops)]
+    per_op = []
+    for op, t in zip(graph.ops, op_ms):
+        per_op.append({"op": op.name, "type": op.op_type, "ms": round(t, 5), "bytes": op_bytes(graph, op),
+                       "ops": op_flops(op)})
+
+    # ---- end to end through the public API: pinned host input -> graph -> pinned host output
+    in_bytes = xt.nbytes
+    out_bytes = graph.tensors[out_name].nbytes
+    hin_ptr, hin = be.host_alloc(in_bytes)
+    hout_ptr, hout = be.host_alloc(out_bytes)
+    hin[:] = x_host.view(np.uint8)
+    for _ in range(2):
+        be.upload_async(rt.bufs[x_name], hin_ptr, in_bytes)
+        rt.run()
+        be.download_async(rt.bufs[out_name], hout_ptr, out_bytes)
+    be.synchronize(120000)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.perf_counter()
+    f0.record(stream)
+    for _ in range(args.steps):
+        be.upload_async(rt.bufs[x_name], hin_ptr, in_bytes)
+        rt.run()
+        be.download_async(rt.bufs[out_name], hout_ptr, out_bytes)
+    f1.record(stream)
+    be.synchronize(600000)
+    t_wall = time.perf_counter() - t_wall0
+    barrier()
+    e2e_ms = max_over_ranks(max(f0.elapsed_time(f1), t_wall * 1000.0))
+    be.host_free(hin_ptr)
+    be.host_free(hout_ptr)
+
+    # ---- CPU baseline (rank 0, single GPU only): the oracle on a bounded sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(graph, x_host, args.cpu_images)
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        int8_peak = 2.0 * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        dom = max(per_op, key=lambda r: r["ms"])
+        dom_op = graph.ops[[o.name for o in graph.ops].index(dom["op"])]
+        traffic = load_traffic(dom_op)
+        # binding roof of the dominant kernel: tensor if its arithmetic intensity exceeds the ridge
+        ridge = int8_peak * 1e12 / (hbm_peak * 1e9)
+        ai = dom["ops"] / dom["bytes"] if dom["bytes"] else 0.0
+        if dom["ops"] and ai > ridge:
+            ach = dom["ops"] / (dom["ms"] * 1e-3) / 1e12
+            roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": round(int8_peak, 1), "unit": "TOP/s",
+                    "frac": round(ach / int8_peak, 4)}
+        else:
+            ach = dom["bytes"] / (dom["ms"] * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(ach / hbm_peak, 4)}
+        roof.update({"kernel": dom["op"], "kernel_ms": dom["ms"], "algorithmic_bytes": dom["bytes"],
+                     "algorithmic_ops": dom["ops"], "traffic": traffic, "peak_source": f"{peak_src} (MEASURED_PEAKS.json)"
+                     if peak_src == "measured" else "fallback", "int8_peak_note": "int8 dense peak taken as 2x the measured bf16 cuBLAS figure"})
+        images = batch * world
+        tops = step_ops * world / (ms_per_step * 1e-3) / 1e12
+        line = {
+            "metric": METRIC,
+            "value": round(tops, 3),
+            "unit": "TOPS",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int8 (i32 accumulate, f32 requant)",
+            "data": "synthetic (seeded int8 activations, He-normal weights quantised per channel)",
+            "images_per_s": round(images / (ms_per_step * 1e-3), 1),
+            "pct_of_int8_peak": round(100.0 * tops / (int8_peak * world), 2),
+            "config": dict(cfg, parallelism=f"replicas x{world} (batch-sharded, no collective)",
+                           global_batch=images, l2="working set per step >1 GB, larger than the 126 MB L2"),
+            "e2e": {"value": round(step_ops * world * args.steps / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
+                    "images_per_s": round(images * args.steps / (e2e_ms * 1e-3), 1),
+                    "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
+                    "path": "CudaGraphRuntime: dw_upload_async (pinned) -> graph -> dw_download_async (pinned)"},
+            "gpu_launches": int(launches),
+            "kernels_per_step": int(kernels_per_step),
+            "roofline": roof,
+            "per_op": per_op,
+            "clocks": clocks,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    rt.release()
+    be.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def load_traffic(op):
+    """Per-launch DRAM traffic of the dominant kernel from a committed ncu summary
+    (profiles/traffic.json: op name -> bytes), else None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d.get(op.name)
+    except Exception:
+        return None
+
+
+def cpu_baseline(graph, x_host, images):
+    """Times the oracle (C restatement of the reference's scalar ops, row-partitioned
+    over all host threads like dragonwing-cpu's pool.rs) on `images` images."""
+    from oracle import dwref
+    from oracle.graph_ref import run_graph
+    threads = dwref.num_cpus()
+    feeds = {graph.inputs[0]: x_host}
+    t0 = time.perf_counter()
+    run_graph(graph, feeds, threads=threads, batch_slice=(0, images))
+    dt = time.perf_counter() - t0
+    batch = graph.tensors[graph.inputs[0]].shape[0]
+    ops_per_image = graph.conv_ops() / batch
+    return {"value": round(ops_per_image * images / dt / 1e12, 6), "unit": "TOPS", "cores": threads, "kind": "port",
+            "images_per_s": round(images / dt, 3), "sample": f"{images} image(s) of the same workload, {dt:.1f} s",
+            "cpu": cpu_model()}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the CPU implementation (oracle restatement), rank 0 only
+# ---------------------------------------------------------------------------
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import dwref
+    from oracle.graph_ref import run_graph
+    batch = args.batch or workload_defaults(args.workload)
+    graph, cfg = build_workload(args.workload, batch, seed=1234)
+    x = np.random.default_rng(1000).integers(-128, 128, graph.tensors[graph.inputs[0]].nbytes).astype(np.int8)
+    threads = dwref.num_cpus()
+    images = args.cpu_images
+    ops_per_image = graph.conv_ops() / batch
+    t_first = None
+    for _ in range(args.warmup):
+        t = time.perf_counter()
+        run_graph(graph, {graph.inputs[0]: x}, threads=threads, batch_slice=(0, images))
+        t_first = time.perf_counter() - t
+    # Bound the whole run to a few minutes: if K steps of this sample would take
+    # longer than the budget, time fewer steps and report how many ran.
+    steps = args.steps
+    if t_first and t_first * steps > args.cpu_budget_s:
+        steps = max(1, int(args.cpu_budget_s / t_first))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run_graph(graph, {graph.inputs[0]: x}, threads=threads, batch_slice=(0, images))
+    dt = time.perf_counter() - t0
+    ms_per_step = dt * 1000.0 / steps
+    args.steps_run = steps
+    tops = ops_per_image * images / (ms_per_step * 1e-3) / 1e12
+    line = {"metric": METRIC, "value": round(tops, 6), "unit": "TOPS", "impl": "reference", "n_gpus": world,
+            "steps": args.steps_run, "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 (i32 accumulate, f32 requant)", "data": "synthetic",
+            "images_per_s": round(images / (ms_per_step * 1e-3), 4),
+            "config": dict(cfg, sample_images_per_step=images),
+            "cpu_baseline": {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port",
+                             "sample": f"{images} image(s) per step of the same workload", "cpu": cpu_model()},
+            "e2e": {"value": round(tops, 6), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference = C restatement of dragonwing-cpu's scalar ops (the Rust crate cannot be compiled here)"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="mbv2_block")
+    ap.add_argument("--batch", type=int, default=0, help="per-GPU batch (default: the workload's)")
+    ap.add_argument("--kernel-steps", type=int, default=5)
+    ap.add_argument("--cpu-images", type=int, default=1)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=150.0)
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        args.warmup = max(1, min(args.warmup, 1))
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -68,6 +68,10 @@ SIGNATURES = {
     "dw_sm_count": ([vp], i32),
     "dw_launch_count": ([vp], ctypes.c_uint64),
     "dw_debug_expire_wait": ([vp, u32], i32),
+    "dw_capture_begin": ([vp], i32),
+    "dw_capture_end": ([vp, PVP], i32),
+    "dw_graph_launch": ([vp, vp], i32),
+    "dw_graph_destroy": ([vp], None),
     "dw_prepare_weights_i8": ([vp, PDESC, vp, PVP], i32),
     "dw_conv2d_i8": ([vp, PDESC, vp, vp, vp, vp, vp, vp], i32),
     "dw_conv2d_requant_relu_i8": ([vp, vp, vp, vp] + [sz] * 11 + [f32, i32], i32),

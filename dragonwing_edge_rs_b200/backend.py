@@ -129,6 +129,22 @@ class CudaBackend:
         self.download(buf, out)
         return out if shape is None else out.reshape(shape)
 
+    def host_alloc(self, nbytes: int) -> tuple[int, np.ndarray]:
+        """Page-locked host memory: returns (pointer, uint8 numpy view)."""
+        out = ctypes.c_void_p()
+        self._check(self._lib.dw_host_alloc(self.handle, nbytes, ctypes.byref(out)))
+        arr = np.ctypeslib.as_array(ctypes.cast(out, ctypes.POINTER(ctypes.c_uint8)), shape=(nbytes,))
+        return int(out.value), arr
+
+    def host_free(self, ptr: int) -> None:
+        self._check(self._lib.dw_host_free(self.handle, ctypes.c_void_p(ptr)))
+
+    def upload_async(self, dst: CudaBuffer, host_ptr: int, nbytes: int, dst_offset: int = 0) -> None:
+        self._check(self._lib.dw_upload_async(self.handle, dst.handle, dst_offset, ctypes.c_void_p(host_ptr), nbytes))
+
+    def download_async(self, src: CudaBuffer, host_ptr: int, nbytes: int, src_offset: int = 0) -> None:
+        self._check(self._lib.dw_download_async(self.handle, src.handle, src_offset, ctypes.c_void_p(host_ptr), nbytes))
+
     def stream(self) -> int:
         return int(self._lib.dw_stream(self.handle) or 0)
 

@@ -271,6 +271,49 @@ DW_API void *dw_stream(dw_backend *be) { return be ? (void *)be->stream : nullpt
 DW_API int dw_sm_count(const dw_backend *be) { return be ? be->sm_count : 0; }
 DW_API uint64_t dw_launch_count(const dw_backend *be) { return be ? be->launches : 0; }
 
+struct dw_graph {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t kernels = 0;  // kernel launches recorded into the graph
+};
+
+DW_API dw_status dw_capture_begin(dw_backend *be) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    cudaSetDevice(be->device);
+    be->capture_mark = be->launches;
+    return dw_cuda_check(be, cudaStreamBeginCapture(be->stream, cudaStreamCaptureModeThreadLocal), "capture begin");
+}
+
+DW_API dw_status dw_capture_end(dw_backend *be, dw_graph **out) {
+    if (!be || !out) return DW_ERR_INVALID_ARG;
+    *out = nullptr;
+    auto *g = new dw_graph();
+    g->kernels = be->launches - be->capture_mark;
+    be->launches = be->capture_mark;  // recorded, not launched
+    dw_status st = dw_cuda_check(be, cudaStreamEndCapture(be->stream, &g->graph), "capture end");
+    if (st == DW_OK) st = dw_cuda_check(be, cudaGraphInstantiate(&g->exec, g->graph, 0), "graph instantiate");
+    if (st != DW_OK) {
+        if (g->graph) cudaGraphDestroy(g->graph);
+        delete g;
+        return st;
+    }
+    *out = g;
+    return DW_OK;
+}
+
+DW_API dw_status dw_graph_launch(dw_backend *be, dw_graph *g) {
+    if (!be || !g) return DW_ERR_INVALID_ARG;
+    be->launches += g->kernels;
+    return dw_cuda_check(be, cudaGraphLaunch(g->exec, be->stream), "graph launch");
+}
+
+DW_API void dw_graph_destroy(dw_graph *g) {
+    if (!g) return;
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    delete g;
+}
+
 DW_API dw_status dw_debug_expire_wait(dw_backend *be, uint32_t cap_us) {
     if (!be) return DW_ERR_INVALID_ARG;
     cudaSetDevice(be->device);

@@ -121,6 +121,119 @@ __global__ void __launch_bounds__(kThreads) k_dwconv16(ConvGeom g, const int8_t 
     }
 }
 
+// Depthwise 3x3 (multiplier 1, c % 4 == 0): one thread computes an RH x RW
+// block of output pixels for 4 channels (one 32-bit word per pixel, so a warp
+// reads and writes 128 contiguous bytes).  int8 values are converted exactly to
+// float (byte placed in the mantissa of 2^23 + 128, then 2^23 + 128 subtracted)
+// and accumulated with FP32 FMAs: every product (<= 2^14) and every 9-tap sum
+// (< 2^18) is an integer below 2^24, so the float accumulation is exact and the
+// result equals the reference's i32 sum.
+__device__ __forceinline__ void unpack4(uint32_t w, float (&f)[4]) {
+    const uint32_t u = w ^ 0x80808080u;  // int8 -> excess-128 unsigned bytes
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        f[k] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440 + k)), 8388736.0f);
+}
+
+template <int S, int RH, int RW>
+__global__ void __launch_bounds__(256) k_dwconv3x3(ConvGeom g, const int8_t *__restrict__ x,
+                                                   const int8_t *__restrict__ w, EpiParams ep,
+                                                   int8_t *__restrict__ y) {
+    // grid: x = 32-channel-group slices, y = (image, tile row); block (32, 8):
+    // threadIdx.y strides over the tile columns.  32-bit index math only.
+    const int cg_n = g.c_in / 4;
+    const int cg = blockIdx.x * 32 + threadIdx.x;
+    if (cg >= cg_n) return;
+    const int tiles_w = (g.wo + RW - 1) / RW, tiles_h = (g.ho + RH - 1) / RH;
+    const int th = (int)blockIdx.y % tiles_h;
+    const int b = (int)blockIdx.y / tiles_h;
+    constexpr int IH = (RH - 1) * S + 3, IW = (RW - 1) * S + 3;
+    float wf[9][4];
+#pragma unroll
+    for (int k = 0; k < 9; k++) unpack4(__ldg(reinterpret_cast<const uint32_t *>(w + (size_t)k * g.c_in) + cg), wf[k]);
+    // epilogue: per channel bias / M (fast exact path when |bias| < 2^21 and M finite)
+    const int c0 = cg * 4;
+    int32_t bias[4];
+    float m[4], dsc[4], biasf[4];
+    bool fast = ep.epilogue != DW_EPI_SILU;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        bias[k] = ep.bias ? __ldg(ep.bias + c0 + k) : 0;
+        m[k] = ep.M ? __ldg(ep.M + c0 + k) : 0.0f;
+        dsc[k] = ep.D ? __ldg(ep.D + c0 + k) : 0.0f;
+        fast = fast && (uint32_t)(bias[k] + (1 << 21)) < (1u << 22) && isfinite(m[k]);
+        biasf[k] = fast ? i2f_small(bias[k]) : 0.0f;
+    }
+    const uint32_t c6 = 0x01010101u * (uint32_t)ep.q6;
+    for (int tw = threadIdx.y; tw < tiles_w; tw += blockDim.y) {
+        const int oh0 = th * RH, ow0 = tw * RW;
+        float acc[RH][RW][4];
+#pragma unroll
+        for (int r = 0; r < RH; r++)
+#pragma unroll
+            for (int q = 0; q < RW; q++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) acc[r][q][k] = 0.0f;
+        const int ih0 = oh0 * S - g.pt, iw0 = ow0 * S - g.pl;
+        const uint32_t *xb = reinterpret_cast<const uint32_t *>(x + (size_t)b * g.h * g.w * g.c_in) + cg;
+        const uint32_t row_words = (uint32_t)g.w * cg_n;
+#pragma unroll
+        for (int r = 0; r < IH; r++) {
+            const int ih = ih0 + r;
+            const bool rok = ih >= 0 && ih < g.h;
+            float xr[IW][4];
+#pragma unroll
+            for (int c = 0; c < IW; c++) {
+                const int iw = iw0 + c;
+                uint32_t v = 0;
+                if (rok && iw >= 0 && iw < g.w) v = __ldg(xb + (uint32_t)ih * row_words + (uint32_t)iw * cg_n);
+                unpack4(v, xr[c]);
+            }
+#pragma unroll
+            for (int orow = 0; orow < RH; orow++) {
+                const int kh = r - orow * S;
+                if (kh < 0 || kh > 2) continue;
+#pragma unroll
+                for (int q = 0; q < RW; q++)
+#pragma unroll
+                    for (int kw = 0; kw < 3; kw++)
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            acc[orow][q][k] = __fmaf_rn(xr[q * S + kw][k], wf[kh * 3 + kw][k], acc[orow][q][k]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RH; r++) {
+            const int oh = oh0 + r;
+            if (oh >= g.ho) break;
+#pragma unroll
+            for (int q = 0; q < RW; q++) {
+                const int ow = ow0 + q;
+                if (ow >= g.wo) break;
+                uint32_t packed = 0;
+                if (fast) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float a = __fadd_rn(acc[r][q][k], biasf[k]);
+                        packed |= f32_to_i8_byte_nonan(__fmul_rn(a, m[k])) << (8 * k);
+                    }
+                    if (ep.epilogue == DW_EPI_RELU) packed = __vmaxs4(packed, 0u);
+                    else if (ep.epilogue == DW_EPI_RELU6) packed = __vmins4(__vmaxs4(packed, 0u), c6);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int32_t ai = __float_as_int(__fadd_rn(acc[r][q][k], kMagic)) - kMagicBits;
+                        packed |= (uint32_t)(uint8_t)epilogue_one(ai, bias[k], m[k], dsc[k], ep.epilogue, ep.q6,
+                                                                  ep.inv_s_out)
+                                  << (8 * k);
+                    }
+                }
+                reinterpret_cast<uint32_t *>(y + (((size_t)b * g.ho + oh) * g.wo + ow) * g.c_in)[cg] = packed;
+            }
+        }
+    }
+}
+
 // Depthwise, any multiplier: c_out = c_in * mult, oc = ic * mult + m, weights [kh][kw][c_in][mult].
 __global__ void __launch_bounds__(kThreads) k_dwconv_generic(ConvGeom g, int mult, const int8_t *__restrict__ x,
                                                              const int8_t *__restrict__ w, EpiParams ep,
@@ -178,6 +291,21 @@ dw_status launch_dwconv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo
                            const int8_t *w_hwcm, const EpiParams &ep, int8_t *y, int32_t *acc_out) {
     ConvGeom g = geom(d, ho, wo);
     const int mult = d.c_out / d.c_in;
+    const bool aligned4 = (uintptr_t)x % 4 == 0 && (uintptr_t)w_hwcm % 4 == 0 && (uintptr_t)y % 4 == 0;
+    if (mult == 1 && !acc_out && d.c_in % 4 == 0 && aligned4 && d.k_h == 3 && d.k_w == 3 &&
+        d.stride_h == d.stride_w && (d.stride_h == 1 || d.stride_h == 2)) {
+        constexpr int RH = 2, RW = 4;
+        const long long gy = (long long)d.n * ((ho + RH - 1) / RH);
+        if (gy <= 65535 && (long long)d.h * d.w * d.c_in < (1ll << 31)) {
+            dim3 grid((unsigned)((d.c_in / 4 + 31) / 32), (unsigned)gy);
+            dim3 block(32, 8);
+            if (d.stride_h == 1)
+                k_dwconv3x3<1, RH, RW><<<grid, block, 0, be->stream>>>(g, x, w_hwcm, ep, y);
+            else
+                k_dwconv3x3<2, RH, RW><<<grid, block, 0, be->stream>>>(g, x, w_hwcm, ep, y);
+            return dw_after_launch(be, "dwconv3x3_i8");
+        }
+    }
     if (mult == 1 && !acc_out && d.c_in % 16 == 0 && (uintptr_t)x % 16 == 0 && (uintptr_t)w_hwcm % 16 == 0 &&
         (uintptr_t)y % 16 == 0) {
         size_t items = (size_t)d.n * ho * wo * (d.c_in / 16);

@@ -9,12 +9,45 @@
 
 namespace dw {
 
+// Conversions and rounding here avoid the XU pipe (int<->float conversion,
+// roundf, directed-rounding adds), which on sm_100 issues at 1/8 of the FMA
+// rate; every helper is exact and uses only round-to-nearest FMA/ALU ops.
+constexpr float kMagic = 12582912.0f;          // 1.5 * 2^23: ulp 1 over [2^23, 2^24)
+constexpr int32_t kMagicBits = 0x4B400000;
+
+// (float)v, exact for |v| < 2^22 (bit pattern of kMagic + v, minus kMagic).
+__device__ __forceinline__ float i2f_small(int32_t v) {
+    return __fsub_rn(__int_as_float(v + kMagicBits), kMagic);
+}
+
+// (float)v with round-to-nearest for any int32 (the XU conversion only when needed).
+__device__ __forceinline__ float i2f_rn(int32_t v) {
+    return ((uint32_t)(v + (1 << 22)) < (1u << 23)) ? i2f_small(v) : __int2float_rn(v);
+}
+
+// roundf(c) (half away from zero) for |c| <= 2^21, returned as the float
+// kMagic + roundf(c) (its low byte is the int8 two's-complement result):
+// r = kMagic + rint_even(c) by one RN add; d = c - rint(c) is exact; a tie
+// rounded toward zero has d == copysign(0.5, c) and moves one step away.
+__device__ __forceinline__ float round_away_magic(float c) {
+    const float r = __fadd_rn(c, kMagic);
+    const float d = __fsub_rn(c, __fsub_rn(r, kMagic));
+    const float h = copysignf(0.5f, c);
+    return d == h ? __fadd_rn(r, __fadd_rn(h, h)) : r;
+}
+
 // `v.clamp(-128.0, 127.0).round() as i8` (crates/dragonwing-cpu/src/ops.rs:3383-3385):
 // clamp in f32, roundf (half away from zero), saturating cast (NaN -> 0).
 __device__ __forceinline__ int32_t f32_to_i8(float v) {
     if (v != v) return 0;
     v = fminf(fmaxf(v, -128.0f), 127.0f);
-    return (int32_t)roundf(v);
+    return __float_as_int(round_away_magic(v)) - kMagicBits;
+}
+
+// Same for a value known not to be NaN; returns the result in the low byte.
+__device__ __forceinline__ uint32_t f32_to_i8_byte_nonan(float v) {
+    v = fminf(fmaxf(v, -128.0f), 127.0f);
+    return __float_as_uint(round_away_magic(v)) & 0xFFu;
 }
 
 // The fused epilogue for one accumulator (contract in include/dw_cuda.h):
@@ -24,11 +57,11 @@ __device__ __forceinline__ int32_t epilogue_one(int32_t acc, int32_t bias, float
                                                 float inv_s_out) {
     const int32_t a = (int32_t)((uint32_t)acc + (uint32_t)bias);
     if (epi == DW_EPI_SILU) {
-        const float y = __fmul_rn(__int2float_rn(a), dsc);
+        const float y = __fmul_rn(i2f_rn(a), dsc);
         const float z = dw_silu_f32(y);
         return f32_to_i8(__fmul_rn(z, inv_s_out));
     }
-    int32_t q = f32_to_i8(__fmul_rn(__int2float_rn(a), m));
+    int32_t q = f32_to_i8(__fmul_rn(i2f_rn(a), m));
     if (epi == DW_EPI_RELU) q = q > 0 ? q : 0;
     else if (epi == DW_EPI_RELU6) q = min(q > 0 ? q : 0, q6);
     return q;

@@ -42,6 +42,7 @@ struct dw_backend {
     int sm_count = 0;
     uint64_t wait_cap_ns = 0;         // device wait limit, nanoseconds (globaltimer)
     uint64_t launches = 0;
+    uint64_t capture_mark = 0;        // launch count when the current capture began
     PFN_encodeTiled encode_tiled = nullptr;
     void *scratch = nullptr;          // per-backend device scratch (tile counters etc.)
     size_t scratch_len = 0;

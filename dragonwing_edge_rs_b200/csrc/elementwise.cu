@@ -33,15 +33,15 @@ __global__ void k_requantize(const int32_t *__restrict__ in, int8_t *__restrict_
 #pragma unroll
         for (int v = 0; v < 4; v++) {
             int4 q = __ldcs(src + v);
-            uint32_t b0 = (uint8_t)f32_to_i8(__fmul_rn(__int2float_rn(q.x), s));
-            uint32_t b1 = (uint8_t)f32_to_i8(__fmul_rn(__int2float_rn(q.y), s));
-            uint32_t b2 = (uint8_t)f32_to_i8(__fmul_rn(__int2float_rn(q.z), s));
-            uint32_t b3 = (uint8_t)f32_to_i8(__fmul_rn(__int2float_rn(q.w), s));
+            uint32_t b0 = (uint8_t)f32_to_i8(__fmul_rn(i2f_rn(q.x), s));
+            uint32_t b1 = (uint8_t)f32_to_i8(__fmul_rn(i2f_rn(q.y), s));
+            uint32_t b2 = (uint8_t)f32_to_i8(__fmul_rn(i2f_rn(q.z), s));
+            uint32_t b3 = (uint8_t)f32_to_i8(__fmul_rn(i2f_rn(q.w), s));
             packed[v] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
         }
         __stcs(reinterpret_cast<int4 *>(out + i * 16), make_int4(packed[0], packed[1], packed[2], packed[3]));
     }
-    for (size_t i = n16 * 16 + tid; i < n; i += stride) out[i] = (int8_t)f32_to_i8(__fmul_rn(__int2float_rn(in[i]), s));
+    for (size_t i = n16 * 16 + tid; i < n; i += stride) out[i] = (int8_t)f32_to_i8(__fmul_rn(i2f_rn(in[i]), s));
 }
 
 // --- relu: ops.rs:3315-3319 ------------------------------------------------
@@ -62,7 +62,7 @@ __device__ __forceinline__ uint32_t add4(uint32_t a, uint32_t b, float ra, float
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         int32_t av = (int8_t)(a >> (8 * k)), bv = (int8_t)(b >> (8 * k));
-        float y = __fadd_rn(__fmul_rn(__int2float_rn(av), ra), __fmul_rn(__int2float_rn(bv), rb));
+        float y = __fadd_rn(__fmul_rn(i2f_small(av), ra), __fmul_rn(i2f_small(bv), rb));
         r |= (uint32_t)(uint8_t)f32_to_i8(y) << (8 * k);
     }
     return r;
@@ -81,7 +81,7 @@ __global__ void k_add_i8(const int8_t *__restrict__ a, const int8_t *__restrict_
         __stcs(reinterpret_cast<int4 *>(out) + i, r);
     }
     for (size_t i = n16 * 16 + tid; i < n; i += stride) {
-        float y = __fadd_rn(__fmul_rn(__int2float_rn(a[i]), ra), __fmul_rn(__int2float_rn(b[i]), rb));
+        float y = __fadd_rn(__fmul_rn(i2f_small(a[i]), ra), __fmul_rn(i2f_small(b[i]), rb));
         out[i] = (int8_t)f32_to_i8(y);
     }
 }
@@ -111,7 +111,7 @@ __device__ __forceinline__ uint32_t quant_u8x4(uint32_t v, float inv255, float i
     uint32_t r = 0;
 #pragma unroll
     for (int k = 0; k < 4; k++) {
-        float x = __fmul_rn(__uint2float_rn((v >> (8 * k)) & 0xff), inv255);
+        float x = __fmul_rn(i2f_small((int32_t)((v >> (8 * k)) & 0xff)), inv255);
         r |= (uint32_t)(uint8_t)f32_to_i8(__fmul_rn(x, inv)) << (8 * k);
     }
     return r;
@@ -129,7 +129,7 @@ __global__ void k_quantize_u8(const uint8_t *__restrict__ in, int8_t *__restrict
         __stcs(reinterpret_cast<int4 *>(out) + i, r);
     }
     for (size_t i = n16 * 16 + tid; i < n; i += stride)
-        out[i] = (int8_t)f32_to_i8(__fmul_rn(__fmul_rn(__uint2float_rn(in[i]), inv255), inv));
+        out[i] = (int8_t)f32_to_i8(__fmul_rn(__fmul_rn(i2f_small((int32_t)in[i]), inv255), inv));
 }
 
 // --- dequantize: ops.rs:3453-3457 ---------------------------------------------
@@ -143,14 +143,14 @@ __global__ void k_dequantize(const int8_t *__restrict__ in, float *__restrict__ 
 #pragma unroll
         for (int q = 0; q < 4; q++) {
             float4 f;
-            f.x = __fmul_rn(__int2float_rn((int8_t)(w[q])), s);
-            f.y = __fmul_rn(__int2float_rn((int8_t)(w[q] >> 8)), s);
-            f.z = __fmul_rn(__int2float_rn((int8_t)(w[q] >> 16)), s);
-            f.w = __fmul_rn(__int2float_rn((int8_t)(w[q] >> 24)), s);
+            f.x = __fmul_rn(i2f_small((int8_t)(w[q])), s);
+            f.y = __fmul_rn(i2f_small((int8_t)(w[q] >> 8)), s);
+            f.z = __fmul_rn(i2f_small((int8_t)(w[q] >> 16)), s);
+            f.w = __fmul_rn(i2f_small((int8_t)(w[q] >> 24)), s);
             __stcs(dst + q, f);
         }
     }
-    for (size_t i = n16 * 16 + tid; i < n; i += stride) out[i] = __fmul_rn(__int2float_rn(in[i]), s);
+    for (size_t i = n16 * 16 + tid; i < n; i += stride) out[i] = __fmul_rn(i2f_small(in[i]), s);
 }
 
 // --- maxpool (ops.rs:1513-1551, padded taps skipped) -------------------------

@@ -242,19 +242,11 @@ __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs,
 }
 
 // Exact requantisation of one accumulator on the fast path.  Preconditions:
-// |a| < 2^22 (so the magic-number conversion is exact) and m finite.
-//   fa = (float)a exactly; f = fa*m (RN, as the reference); c = clamp(f);
-//   roundf(c) = floor(c + 0.5) for c >= 0 and ceil(c - 0.5) for c < 0, each
-//   computed with directed-rounding adds (floor/ceil preserving), the last add
-//   placing the integer in the low mantissa bits of 1.5*2^23 + q; the low byte
-//   is q in two's complement.
+// |a| < 2^22 (so the magic-number conversion is exact) and m finite (so the
+// product is never NaN).  fa = (float)a exactly; f = fa*m (RN, as the
+// reference); then clamp + roundf via round-to-nearest adds only.
 __device__ __forceinline__ uint32_t requant_fast_byte(int32_t a, float m) {
-    const float fa = __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f);
-    const float f = __fmul_rn(fa, m);
-    const float c = fminf(fmaxf(f, -128.0f), 127.0f);
-    const float hp = __fadd_rd(__fadd_rd(c, 0.5f), 12582912.0f);
-    const float hn = __fadd_ru(__fadd_ru(c, -0.5f), 12582912.0f);
-    return __float_as_uint(c >= 0.0f ? hp : hn) & 0xFFu;
+    return f32_to_i8_byte_nonan(__fmul_rn(i2f_small(a), m));
 }
 
 // 16 accumulators (16 consecutive channels of one row) -> 16 int8, packed.
@@ -295,13 +287,32 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
         for (int k = 0; k < 16; k++) inrange &= (uint32_t)(a[k] + (1 << 22)) < (1u << 23);
     }
     if ((fl & 1u) && __all_sync(0xffffffffu, inrange)) {
+        // rint-to-even for all 16 (one RN add each); a round-half-away tie can
+        // only differ from it when c - rint(c) == +-0.5 exactly: such chunks
+        // (rare) are redone with the per-element tie fix.
+        bool tie = false;
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-            const uint32_t b0 = requant_fast_byte(a[q * 4 + 0], mm[q * 4 + 0]);
-            const uint32_t b1 = requant_fast_byte(a[q * 4 + 1], mm[q * 4 + 1]);
-            const uint32_t b2 = requant_fast_byte(a[q * 4 + 2], mm[q * 4 + 2]);
-            const uint32_t b3 = requant_fast_byte(a[q * 4 + 3], mm[q * 4 + 3]);
-            w[q] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+            uint32_t bq[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float f = __fmul_rn(i2f_small(a[q * 4 + j]), mm[q * 4 + j]);
+                const float c = fminf(fmaxf(f, -128.0f), 127.0f);
+                const float r = __fadd_rn(c, kMagic);
+                tie |= fabsf(__fsub_rn(c, __fsub_rn(r, kMagic))) == 0.5f;
+                bq[j] = __float_as_uint(r);
+            }
+            w[q] = __byte_perm(__byte_perm(bq[0], bq[1], 0x0040), __byte_perm(bq[2], bq[3], 0x0040), 0x5410);
+        }
+        if (__any_sync(0xffffffffu, tie)) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const uint32_t b0 = requant_fast_byte(a[q * 4 + 0], mm[q * 4 + 0]);
+                const uint32_t b1 = requant_fast_byte(a[q * 4 + 1], mm[q * 4 + 1]);
+                const uint32_t b2 = requant_fast_byte(a[q * 4 + 2], mm[q * 4 + 2]);
+                const uint32_t b3 = requant_fast_byte(a[q * 4 + 3], mm[q * 4 + 3]);
+                w[q] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+            }
         }
         if (epi == DW_EPI_RELU) {
 #pragma unroll

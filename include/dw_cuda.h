@@ -125,6 +125,16 @@ DW_API void *dw_stream(dw_backend *be);
 DW_API int dw_sm_count(const dw_backend *be);
 /* Counts kernel launches made through this backend (diagnostics / benchmarks). */
 DW_API uint64_t dw_launch_count(const dw_backend *be);
+/* CUDA-graph capture of an op sequence enqueued on the backend stream (the
+ * reference's OpsRecorder single-command-buffer recording,
+ * crates/dragonwing-vulkan/src/record.rs:49-679): between dw_capture_begin and
+ * dw_capture_end, ops are recorded instead of executed; dw_graph_launch replays
+ * them with one launch.  No allocation may happen while capturing. */
+typedef struct dw_graph dw_graph;
+DW_API dw_status dw_capture_begin(dw_backend *be);
+DW_API dw_status dw_capture_end(dw_backend *be, dw_graph **out);
+DW_API dw_status dw_graph_launch(dw_backend *be, dw_graph *g);
+DW_API void dw_graph_destroy(dw_graph *g);
 /* Test hook: runs one bounded device-side wait on a flag that nothing sets,
  * with a cap of cap_us microseconds; the kernel gives up and records the
  * failure, and the next dw_synchronize reports DW_ERR_KERNEL_WAIT_EXPIRED. */

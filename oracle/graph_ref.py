@@ -1,0 +1,79 @@
+"""CPU execution of a fused-INT8 graph with the oracle ops.
+
+TEST INFRASTRUCTURE ONLY: the checker for CudaGraphRuntime and the timed CPU
+baseline of bench.py.  Each op maps to the oracle restatement of the
+reference op it stands for: the fused conv to the contract composition of
+conv2d_i8_nhwc / requantize / relu (crates/dragonwing-cpu/src/ops.rs:3086-3142,
+3366-3386, 3301-3319), AddQuantized to add_i8 (ops.rs:3176-3209), MaxPool to
+maxpool2d (ops.rs:1513-1551), Concat/Split to concat_f32/split_f32 on int8
+bytes (ops.rs:2141-2246, 2407), Resize to resize_f32 Nearest (ops.rs:2320-2348),
+QuantizeU8 to u8*(1/255) -> quantize_f32_to_i8 (ops.rs:3503-3525).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from oracle import dwref
+
+
+def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
+    """Runs `graph` on the CPU.  `feeds` maps input names to arrays.  With
+    `batch_slice` = (b0, b1), only images b0..b1-1 are computed (every op is
+    per-image), which bounds the CPU time of large-batch graphs."""
+    b0, b1 = batch_slice if batch_slice else (0, None)
+    vals = {}
+    for name in graph.inputs:
+        t = graph.tensors[name]
+        arr = np.asarray(feeds[name]).reshape(t.shape)
+        vals[name] = np.ascontiguousarray(arr[b0:b1])
+
+    def shape_of(name):
+        t = graph.tensors[name]
+        n = vals[graph.inputs[0]].shape[0]
+        return (n,) + tuple(t.shape[1:])
+
+    for op in graph.ops:
+        t = op.op_type
+        if t == "Conv2dRequantReluI8Nhwc":
+            d = op.params["desc"]
+            x = vals[op.inputs[0]]
+            n = x.shape[0]
+            od = dwref.conv_desc(n, d.h, d.w, d.c_in, d.c_out, d.k_h, d.k_w, d.stride_h, d.stride_w, d.pads,
+                                 d.group, d.epilogue, d.q6, d.inv_s_out)
+            w = graph.initializers[op.inputs[1]]
+            bias = graph.initializers[op.inputs[2]]
+            M = graph.initializers[op.inputs[3]]
+            D = graph.initializers[op.inputs[4]]
+            y = dwref.conv2d_fused_i8(x, w, bias, M, D if d.epilogue == dwref.EPI_SILU else None, od, threads)
+            vals[op.outputs[0]] = y.reshape(shape_of(op.outputs[0]))
+        elif t == "AddQuantized":
+            a, b = vals[op.inputs[0]], vals[op.inputs[1]]
+            y = dwref.add_i8(a, b, op.params["scale_a_over_out"], op.params["scale_b_over_out"])
+            vals[op.outputs[0]] = y.reshape(a.shape)
+        elif t == "MaxPool":
+            x = vals[op.inputs[0]]
+            n, h, w, c = x.shape
+            k, s, p = op.params["k"], op.params["s"], op.params["pad"]
+            vals[op.outputs[0]] = dwref.maxpool_i8(x, n, h, w, c, k, k, s, s, (p, p, p, p)).reshape(shape_of(op.outputs[0]))
+        elif t == "Concat":
+            xs = [vals[i] for i in op.inputs]
+            n, h, w, _ = xs[0].shape
+            vals[op.outputs[0]] = dwref.concat_c_i8(xs, op.params["channels"], n * h * w).reshape(shape_of(op.outputs[0]))
+        elif t == "Split":
+            x = vals[op.inputs[0]]
+            c0, cl = op.params["c0"], op.params["c_len"]
+            vals[op.outputs[0]] = np.ascontiguousarray(x[..., c0:c0 + cl])
+        elif t == "Resize":
+            x = vals[op.inputs[0]]
+            n, h, w, c = x.shape
+            _, ho, wo, _ = shape_of(op.outputs[0])
+            vals[op.outputs[0]] = dwref.resize_nearest_i8(x, n, h, w, ho, wo, c).reshape(n, ho, wo, c)
+        elif t == "QuantizeU8":
+            x = vals[op.inputs[0]]
+            vals[op.outputs[0]] = dwref.quantize_u8_to_i8(x, op.params["scale"]).reshape(x.shape)
+        elif t == "Dequantize":
+            x = vals[op.inputs[0]]
+            vals[op.outputs[0]] = dwref.dequantize_i8_to_f32(x, op.params["scale"]).reshape(x.shape)
+        else:
+            raise ValueError(f"unsupported op {t}")
+    return {name: vals[name] for name in graph.outputs}

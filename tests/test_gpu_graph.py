@@ -1,0 +1,52 @@
+"""GPU parity of whole graphs: CudaGraphRuntime (eager dispatch and CUDA-graph
+replay) against the oracle graph runner, bit-exact on every output; plus
+size-independent properties on the full benchmark batch."""
+import numpy as np
+import pytest
+
+import dragonwing_edge_rs_b200 as dw
+from dragonwing_edge_rs_b200 import graph as G
+from oracle.graph_ref import run_graph
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def be():
+    b = dw.CudaBackend(0)
+    yield b
+    b.close()
+
+
+def test_mobilenetv2_block_small_batch(be):
+    g = G.mobilenetv2_block(batch=2, seed=7)
+    x = np.random.default_rng(3).integers(-128, 128, g.tensors["x"].nbytes).astype(np.int8)
+    rt = G.CudaGraphRuntime(g, be)
+    rt.set_input_bytes("x", x)
+    rt.run()
+    y_eager = rt.get_output(g.outputs[0])
+    ref = run_graph(g, {"x": x}, threads=8)[g.outputs[0]]
+    assert np.array_equal(y_eager, ref.reshape(y_eager.shape))
+    kernels = rt.capture()
+    assert kernels == len(g.ops)
+    rt.run()
+    y_graph = rt.get_output(g.outputs[0])
+    assert np.array_equal(y_graph, y_eager)
+    rt.release()
+
+
+def test_mobilenetv2_block_full_batch_sampled(be):
+    """BASELINE config 2 at its full batch (32): whole batch on the GPU, two
+    sampled images checked against the oracle, and the per-image independence
+    property (image i of the batch == the same image run alone)."""
+    g = G.mobilenetv2_block(batch=32, seed=1234)
+    x = np.random.default_rng(11).integers(-128, 128, g.tensors["x"].nbytes).astype(np.int8)
+    rt = G.CudaGraphRuntime(g, be)
+    rt.set_input_bytes("x", x)
+    rt.capture()
+    rt.run()
+    y = rt.get_output(g.outputs[0])
+    for i in (0, 31):
+        ref = run_graph(g, {"x": x}, threads=8, batch_slice=(i, i + 1))[g.outputs[0]]
+        assert np.array_equal(y[i], ref.reshape(y[i].shape)), f"image {i}"
+    rt.release()

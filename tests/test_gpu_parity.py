@@ -188,6 +188,24 @@ def test_conv_extreme_values(be_umma, be_direct):
         _check_conv(be, (desc, x, wt, b, M, D))
 
 
+@pytest.mark.parametrize("k,group", [(1, 1), (3, 1), (3, "dw")])
+def test_conv_rounding_ties(be_umma, be_direct, k, group):
+    """Requant scales of 0.5 / 0.25 / 1.5 make (float)acc * M an exact .5 tie for
+    many accumulators: roundf's half-away-from-zero must be reproduced exactly."""
+    rng = np.random.default_rng(31 + k)
+    c = 64
+    g = c if group == "dw" else 1
+    desc, x, wt, b, M, D = conv_case(rng, 2, 10, 10, c, c, k=k, group=g, epilogue=dw.EPI_NONE, x_range=(-3, 3))
+    wt[:] = rng.integers(-3, 4, wt.size)
+    M = np.resize(np.array([0.5, 0.25, 1.5, -0.5], np.float32), c)
+    b = rng.integers(-7, 8, c).astype(np.int32)
+    for be in (be_umma, be_direct):
+        _check_conv(be, (desc, x, wt, b, M, D))
+    desc.epilogue = dw.EPI_RELU6
+    desc.q6 = 5
+    _check_conv(be_umma, (desc, x, wt, b, M, D))
+
+
 @pytest.mark.parametrize("mult,c,epi", [(1, 576, dw.EPI_RELU6), (1, 32, dw.EPI_RELU), (2, 8, dw.EPI_NONE),
                                          (1, 24, dw.EPI_SILU)])
 def test_depthwise_parity(be, mult, c, epi):
