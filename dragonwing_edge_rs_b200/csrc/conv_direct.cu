@@ -136,7 +136,7 @@ __device__ __forceinline__ void unpack4(uint32_t w, float (&f)[4]) {
 }
 
 template <int S, int RH, int RW>
-__global__ void __launch_bounds__(256) k_dwconv3x3(ConvGeom g, const int8_t *__restrict__ x,
+__global__ void __launch_bounds__(256, 2) k_dwconv3x3(ConvGeom g, const int8_t *__restrict__ x,
                                                    const int8_t *__restrict__ w, EpiParams ep,
                                                    int8_t *__restrict__ y) {
     // grid: x = 32-channel-group slices, y = (image, tile row); block (32, 8):
@@ -148,9 +148,7 @@ __global__ void __launch_bounds__(256) k_dwconv3x3(ConvGeom g, const int8_t *__r
     const int th = (int)blockIdx.y % tiles_h;
     const int b = (int)blockIdx.y / tiles_h;
     constexpr int IH = (RH - 1) * S + 3, IW = (RW - 1) * S + 3;
-    float wf[9][4];
-#pragma unroll
-    for (int k = 0; k < 9; k++) unpack4(__ldg(reinterpret_cast<const uint32_t *>(w + (size_t)k * g.c_in) + cg), wf[k]);
+    const uint32_t *wg = reinterpret_cast<const uint32_t *>(w) + cg;
     // epilogue: per channel bias / M (fast exact path when |bias| < 2^21 and M finite)
     const int c0 = cg * 4;
     int32_t bias[4];
@@ -167,6 +165,9 @@ __global__ void __launch_bounds__(256) k_dwconv3x3(ConvGeom g, const int8_t *__r
     const uint32_t c6 = 0x01010101u * (uint32_t)ep.q6;
     for (int tw = threadIdx.y; tw < tiles_w; tw += blockDim.y) {
         const int oh0 = th * RH, ow0 = tw * RW;
+        float wf[9][4];  // reloaded per tile (L1 hits) to keep register pressure down
+#pragma unroll
+        for (int k = 0; k < 9; k++) unpack4(__ldg(wg + (size_t)k * cg_n), wf[k]);
         float acc[RH][RW][4];
 #pragma unroll
         for (int r = 0; r < RH; r++)
