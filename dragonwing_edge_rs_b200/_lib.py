@@ -75,6 +75,7 @@ SIGNATURES = {
     "dw_prepare_weights_i8": ([vp, PDESC, vp, PVP], i32),
     "dw_conv2d_i8": ([vp, PDESC, vp, vp, vp, vp, vp, vp], i32),
     "dw_conv2d_requant_relu_i8": ([vp, vp, vp, vp] + [sz] * 11 + [f32, i32], i32),
+    "dw_conv2d_requant_relu_i8_noalloc": ([vp, vp, vp, vp] + [sz] * 11 + [f32, i32], i32),
     "dw_conv2d_i8_nhwc": ([vp, vp, vp, vp] + [sz] * 11, i32),
     "dw_gemm_i8": ([vp, vp, vp, vp, sz, sz, sz], i32),
     "dw_prepare_gemm_b_i8": ([vp, vp, sz, sz, PVP], i32),

@@ -176,6 +176,22 @@ DW_API dw_status dw_conv2d_requant_relu_i8(dw_backend *be, const dw_buf *input, 
                                            size_t stride_w, size_t pad_h, size_t pad_w, float requant_scale,
                                            int do_relu);
 
+/* Same op, parameters and checks as dw_conv2d_requant_relu_i8, for callers that
+ * must not allocate device memory per call (a fixed memory plan reserved at
+ * start-up, or a latency-critical loop where an allocator call is not allowed).
+ * No counterpart in the reference.  Its temporaries (repacked weights and the
+ * scale array) live in one fixed device array inside the library, held by every
+ * GPU that loads it until exit; it accepts kernels of at most 1 MiB
+ * (k_h*k_w*c_in*c_out bytes) and at most 4096 output channels and rejects larger
+ * ones with DW_ERR_INVALID_ARG.  The first call on a device looks the array's
+ * address up; make it before any stream capture on that device.  Calls share the
+ * array: calls that overlap on the GPU race and must be serialised. */
+DW_API dw_status dw_conv2d_requant_relu_i8_noalloc(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio,
+                                                   dw_buf *output, size_t n, size_t h_in, size_t w_in, size_t c_in,
+                                                   size_t c_out, size_t k_h, size_t k_w, size_t stride_h,
+                                                   size_t stride_w, size_t pad_h, size_t pad_w,
+                                                   float requant_scale, int do_relu);
+
 /* Unfused int8 conv to int32 accumulators: conv2d_i8_nhwc_packed
  * (crates/dragonwing-vulkan/src/ops.rs:1822), CPU twin conv2d_i8_nhwc (cpu ops.rs:3086). */
 DW_API dw_status dw_conv2d_i8_nhwc(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio,
