@@ -12,6 +12,9 @@ max-over-ranks of the device-timed region.  Rank 0 prints one JSON line.
 
 Workloads (synthetic data and weights with the configs' shapes and value
 distributions, seeded):
+  yolov8n     (default) YOLOv8n-architecture INT8 graph, 640x640 uint8 images,
+              batch 32 per GPU (256 over 8 GPUs); value = images/s
+              conv TOPS and % of int8 peak beside it.
   mbv2_block  MobileNetV2 inverted-residual block, batch 32 per GPU, 112x112x96,
               1x1 expand 576 + ReLU6, depthwise 3x3 + ReLU6, 1x1 project 96,
               residual add with requantisation.
@@ -125,18 +128,42 @@ class ClockSampler:
 # workloads
 # ---------------------------------------------------------------------------
 
+WORKLOADS = {
+    # name: (default per-GPU batch, value unit, description)
+    "yolov8n": (32, "images/s", "yolov8n_int8 640x640 (BASELINE config 4)"),
+    "mbv2_block": (32, "TOPS", "mobilenetv2_int8_block 112x112x96 (BASELINE config 2)"),
+}
+DEFAULT_WORKLOAD = "yolov8n"
+
+
 def build_workload(name: str, batch: int, seed: int):
     from dragonwing_edge_rs_b200 import graph as G
+    if name not in WORKLOADS:
+        raise SystemExit(f"unknown workload {name}")
+    desc = WORKLOADS[name][2]
     if name == "mbv2_block":
         g = G.mobilenetv2_block(batch=batch, seed=seed)
-        cfg = {"workload": "mobilenetv2_int8_block (BASELINE config 2)", "batch_per_gpu": batch,
-               "input": "112x112x96 int8", "expand": 576, "layers": "1x1 expand+ReLU6, dw3x3+ReLU6, 1x1 project, add"}
-        return g, cfg
-    raise SystemExit(f"unknown workload {name}")
+        cfg = {"workload": desc, "batch_per_gpu": batch, "expand": 576,
+               "layers": "1x1 expand+ReLU6, dw3x3+ReLU6, 1x1 project, add"}
+    else:
+        g = G.yolov8n(batch=batch, seed=seed)
+        cfg = {"workload": desc, "batch_per_gpu": batch, "width": 0.25, "depth": 0.33, "classes": 80, "reg_max": 16,
+               "layers": "63 fused int8 convs (SiLU), C2f, SPPF 5x5, PAN upsample+concat, decoupled head",
+               "input": "uint8 image /255 -> int8", "outputs": "6 head tensors dequantised to f32"}
+    return g, cfg
 
 
 def workload_defaults(name):
-    return {"mbv2_block": 32}[name]
+    return WORKLOADS[name][0]
+
+
+def make_input(graph, seed):
+    import numpy as np
+    t = graph.tensors[graph.inputs[0]]
+    rng = np.random.default_rng(seed)
+    if t.dtype == "u8":
+        return rng.integers(0, 256, t.nbytes).astype(np.uint8)
+    return rng.integers(-128, 128, t.nbytes).astype(np.int8)
 
 
 def op_bytes(graph, op):
@@ -198,15 +225,14 @@ def run_ours(args, rank, world, local_rank):
     graph, cfg = build_workload(args.workload, batch, seed=1234)
     be = dw.CudaBackend(local_rank)
     rt = CudaGraphRuntime(graph, be)
-    rng = np.random.default_rng(1000 + rank)
     x_name = graph.inputs[0]
     xt = graph.tensors[x_name]
-    x_host = rng.integers(-128, 128, xt.nbytes).astype(np.int8)
+    x_host = make_input(graph, 1000 + rank)
     rt.set_input_bytes(x_name, x_host)
     kernels_per_step = rt.capture()
     stream = torch.cuda.ExternalStream(be.stream())
     step_ops = graph.conv_ops()
-    out_name = graph.outputs[0]
+    out_names = list(graph.outputs)
 
     # ---- warm-up
     for _ in range(args.warmup):
@@ -257,14 +283,22 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- end to end through the public API: pinned host input -> graph -> pinned host output
     in_bytes = xt.nbytes
-    out_bytes = graph.tensors[out_name].nbytes
+    out_sizes = [graph.tensors[o].nbytes for o in out_names]
+    out_bytes = sum(out_sizes)
     hin_ptr, hin = be.host_alloc(in_bytes)
     hout_ptr, hout = be.host_alloc(out_bytes)
     hin[:] = x_host.view(np.uint8)
+
+    def download_outputs():
+        off = 0
+        for o, nb in zip(out_names, out_sizes):
+            be.download_async(rt.bufs[o], hout_ptr + off, nb)
+            off += nb
+
     for _ in range(2):
         be.upload_async(rt.bufs[x_name], hin_ptr, in_bytes)
         rt.run()
-        be.download_async(rt.bufs[out_name], hout_ptr, out_bytes)
+        download_outputs()
     be.synchronize(120000)
     barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -273,7 +307,7 @@ def run_ours(args, rank, world, local_rank):
     for _ in range(args.steps):
         be.upload_async(rt.bufs[x_name], hin_ptr, in_bytes)
         rt.run()
-        be.download_async(rt.bufs[out_name], hout_ptr, out_bytes)
+        download_outputs()
     f1.record(stream)
     be.synchronize(600000)
     t_wall = time.perf_counter() - t_wall0
@@ -285,7 +319,7 @@ def run_ours(args, rank, world, local_rank):
     # ---- CPU baseline (rank 0, single GPU only): the oracle on a bounded sample
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(graph, x_host, args.cpu_images)
+        cpu = cpu_baseline(graph, x_host, args.cpu_images, WORKLOADS[args.workload][1])
 
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -310,10 +344,14 @@ def run_ours(args, rank, world, local_rank):
                      if peak_src == "measured" else "fallback", "int8_peak_note": "int8 dense peak taken as 2x the measured bf16 cuBLAS figure"})
         images = batch * world
         tops = step_ops * world / (ms_per_step * 1e-3) / 1e12
+        ips = images / (ms_per_step * 1e-3)
+        unit = WORKLOADS[args.workload][1]
+        e2e_ips = images * args.steps / (e2e_ms * 1e-3)
+        e2e_tops = step_ops * world * args.steps / (e2e_ms * 1e-3) / 1e12
         line = {
             "metric": METRIC,
-            "value": round(tops, 3),
-            "unit": "TOPS",
+            "value": round(ips if unit == "images/s" else tops, 3),
+            "unit": unit,
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
@@ -323,12 +361,13 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None,
             "dtype": "int8 (i32 accumulate, f32 requant)",
             "data": "synthetic (seeded int8 activations, He-normal weights quantised per channel)",
-            "images_per_s": round(images / (ms_per_step * 1e-3), 1),
+            "images_per_s": round(ips, 1),
+            "conv_tops": round(tops, 3),
             "pct_of_int8_peak": round(100.0 * tops / (int8_peak * world), 2),
             "config": dict(cfg, parallelism=f"replicas x{world} (batch-sharded, no collective)",
-                           global_batch=images, l2="working set per step >1 GB, larger than the 126 MB L2"),
-            "e2e": {"value": round(step_ops * world * args.steps / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
-                    "images_per_s": round(images * args.steps / (e2e_ms * 1e-3), 1),
+                           global_batch=images, l2="per-step working set several GB, far larger than the 126 MB L2"),
+            "e2e": {"value": round(e2e_ips if unit == "images/s" else e2e_tops, 3), "unit": unit,
+                    "images_per_s": round(e2e_ips, 1), "conv_tops": round(e2e_tops, 3),
                     "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
                     "path": "CudaGraphRuntime: dw_upload_async (pinned) -> graph -> dw_download_async (pinned)"},
             "gpu_launches": int(launches),
@@ -358,7 +397,7 @@ def load_traffic(op):
         return None
 
 
-def cpu_baseline(graph, x_host, images):
+def cpu_baseline(graph, x_host, images, unit):
     """Times the oracle (C restatement of the reference's scalar ops, row-partitioned
     over all host threads like dragonwing-cpu's pool.rs) on `images` images."""
     from oracle import dwref
@@ -370,7 +409,8 @@ def cpu_baseline(graph, x_host, images):
     dt = time.perf_counter() - t0
     batch = graph.tensors[graph.inputs[0]].shape[0]
     ops_per_image = graph.conv_ops() / batch
-    return {"value": round(ops_per_image * images / dt / 1e12, 6), "unit": "TOPS", "cores": threads, "kind": "port",
+    value = images / dt if unit == "images/s" else ops_per_image * images / dt / 1e12
+    return {"value": round(value, 6), "unit": unit, "cores": threads, "kind": "port",
             "images_per_s": round(images / dt, 3), "sample": f"{images} image(s) of the same workload, {dt:.1f} s",
             "cpu": cpu_model()}
 
@@ -398,7 +438,7 @@ def run_reference(args, rank, world):
     from oracle.graph_ref import run_graph
     batch = args.batch or workload_defaults(args.workload)
     graph, cfg = build_workload(args.workload, batch, seed=1234)
-    x = np.random.default_rng(1000).integers(-128, 128, graph.tensors[graph.inputs[0]].nbytes).astype(np.int8)
+    x = make_input(graph, 1000)
     threads = dwref.num_cpus()
     images = args.cpu_images
     ops_per_image = graph.conv_ops() / batch
@@ -419,15 +459,18 @@ def run_reference(args, rank, world):
     ms_per_step = dt * 1000.0 / steps
     args.steps_run = steps
     tops = ops_per_image * images / (ms_per_step * 1e-3) / 1e12
-    line = {"metric": METRIC, "value": round(tops, 6), "unit": "TOPS", "impl": "reference", "n_gpus": world,
+    unit = WORKLOADS[args.workload][1]
+    value = images / (ms_per_step * 1e-3) if unit == "images/s" else tops
+    line = {"metric": METRIC, "value": round(value, 6), "unit": unit, "impl": "reference", "n_gpus": world,
             "steps": args.steps_run, "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 (i32 accumulate, f32 requant)", "data": "synthetic",
             "images_per_s": round(images / (ms_per_step * 1e-3), 4),
             "config": dict(cfg, sample_images_per_step=images),
-            "cpu_baseline": {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port",
+            "conv_tops": round(tops, 6),
+            "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads, "kind": "port",
                              "sample": f"{images} image(s) per step of the same workload", "cpu": cpu_model()},
-            "e2e": {"value": round(tops, 6), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference = C restatement of dragonwing-cpu's scalar ops (the Rust crate cannot be compiled here)"}
     print(json.dumps(line), flush=True)
 
@@ -438,7 +481,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="mbv2_block")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--batch", type=int, default=0, help="per-GPU batch (default: the workload's)")
     ap.add_argument("--kernel-steps", type=int, default=5)
     ap.add_argument("--cpu-images", type=int, default=1)

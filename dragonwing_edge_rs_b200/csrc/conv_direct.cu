@@ -68,6 +68,87 @@ __global__ void __launch_bounds__(kThreads) k_conv_direct(ConvGeom g, const int8
     }
 }
 
+// One output element's epilogue with the certified SiLU fast path (exact result).
+__device__ __forceinline__ uint32_t epilogue_byte(int32_t acc, int32_t bias, float m, float dsc, const EpiParams &ep) {
+    if (ep.epilogue == DW_EPI_SILU) {
+        const int32_t a = (int32_t)((uint32_t)acc + (uint32_t)bias);
+        if ((uint32_t)(a + (1 << 22)) < (1u << 23) && isfinite(dsc) && isfinite(ep.inv_s_out)) {
+            bool u = false;
+            const uint32_t bits = silu_fast_bits(i2f_small(a), dsc, ep.inv_s_out, u);
+            if (!u) return bits & 0xFFu;
+        }
+    }
+    return (uint8_t)epilogue_one(acc, bias, m, dsc, ep.epilogue, ep.q6, ep.inv_s_out);
+}
+
+// Dense conv with few input channels (the 3-channel stem, or any c_in the
+// tensor-core path does not take), c_out % 16 == 0: one thread = one output
+// pixel x 16 output channels.  Weights are staged once per block in shared
+// memory as floats [tap][c_in][c_out]; int8 products (<= 2^14) summed over
+// k_h*k_w*c_in <= 1024 taps stay below 2^24, so the FP32 accumulation is exact.
+__global__ void __launch_bounds__(256) k_conv_smallc(ConvGeom g, const int8_t *__restrict__ x,
+                                                     const int8_t *__restrict__ w_ohwi, EpiParams ep,
+                                                     int8_t *__restrict__ y) {
+    extern __shared__ float sw[];
+    const int K = g.kh * g.kw * g.c_in;
+    for (int i = threadIdx.x; i < K * g.c_out; i += blockDim.x) {
+        const int oc = i % g.c_out, kk = i / g.c_out;
+        sw[i] = (float)w_ohwi[(size_t)oc * K + kk];
+    }
+    __syncthreads();
+    const int groups = g.c_out / 16;
+    const uint32_t total = (uint32_t)g.n * g.ho * g.wo * groups;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int cg = (int)(i % groups);
+        const uint32_t p = i / groups;
+        const int ow = (int)(p % g.wo);
+        const uint32_t t = p / g.wo;
+        const int oh = (int)(t % g.ho);
+        const int b = (int)(t / g.ho);
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) acc[j] = 0.0f;
+        for (int a = 0; a < g.kh; a++) {
+            const int ih = oh * g.sh + a - g.pt;
+            if (ih < 0 || ih >= g.h) continue;
+            for (int q = 0; q < g.kw; q++) {
+                const int iw = ow * g.sw + q - g.pl;
+                if (iw < 0 || iw >= g.w) continue;
+                const int8_t *px = x + (((size_t)b * g.h + ih) * g.w + iw) * g.c_in;
+                const float *ws = sw + (size_t)((a * g.kw + q) * g.c_in) * g.c_out + cg * 16;
+                for (int c = 0; c < g.c_in; c++) {
+                    const float xv = i2f_small(px[c]);
+                    const float4 *w4 = reinterpret_cast<const float4 *>(ws + (size_t)c * g.c_out);
+#pragma unroll
+                    for (int j4 = 0; j4 < 4; j4++) {
+                        const float4 wv = w4[j4];
+                        acc[j4 * 4 + 0] = __fmaf_rn(xv, wv.x, acc[j4 * 4 + 0]);
+                        acc[j4 * 4 + 1] = __fmaf_rn(xv, wv.y, acc[j4 * 4 + 1]);
+                        acc[j4 * 4 + 2] = __fmaf_rn(xv, wv.z, acc[j4 * 4 + 2]);
+                        acc[j4 * 4 + 3] = __fmaf_rn(xv, wv.w, acc[j4 * 4 + 3]);
+                    }
+                }
+            }
+        }
+        uint32_t out[4];
+#pragma unroll
+        for (int j4 = 0; j4 < 4; j4++) {
+            uint32_t packed = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int oc = cg * 16 + j4 * 4 + j;
+                const int32_t ai = __float_as_int(__fadd_rn(acc[j4 * 4 + j], kMagic)) - kMagicBits;
+                const int32_t bias = ep.bias ? __ldg(ep.bias + oc) : 0;
+                const float m = ep.M ? __ldg(ep.M + oc) : 0.0f;
+                const float dsc = ep.D ? __ldg(ep.D + oc) : 0.0f;
+                packed |= epilogue_byte(ai, bias, m, dsc, ep) << (8 * j);
+            }
+            out[j4] = packed;
+        }
+        *reinterpret_cast<uint4 *>(y + (size_t)p * g.c_out + cg * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+    }
+}
+
 // Depthwise, multiplier 1, 16 channels per thread; weights [kh*kw][c].
 __global__ void __launch_bounds__(kThreads) k_dwconv16(ConvGeom g, const int8_t *__restrict__ x,
                                                        const int8_t *__restrict__ w, EpiParams ep,
@@ -280,6 +361,15 @@ dw_status launch_conv_direct_i8(dw_backend *be, const dw_conv_desc &d, int ho, i
                                 const int8_t *w_ohwi, const EpiParams &ep, int8_t *y, int32_t *acc_out) {
     ConvGeom g = geom(d, ho, wo);
     size_t items = (size_t)d.n * ho * wo * d.c_out;
+    const int K = d.k_h * d.k_w * d.c_in;
+    const size_t sw_bytes = (size_t)K * d.c_out * sizeof(float);
+    if (!acc_out && d.group == 1 && d.c_out % 16 == 0 && K <= 256 && sw_bytes <= 48 * 1024 &&
+        items / 16 < (1u << 31) && (uintptr_t)y % 16 == 0) {
+        const size_t threads_needed = items / 16;
+        const int grid = (int)std::max<size_t>(1, std::min((threads_needed + 255) / 256, (size_t)be->sm_count * 8));
+        k_conv_smallc<<<grid, 256, sw_bytes, be->stream>>>(g, x, w_ohwi, ep, y);
+        return dw_after_launch(be, "conv_smallc_i8");
+    }
     bool vec4 = (d.c_in % 4 == 0) && ((uintptr_t)x % 4 == 0) && ((uintptr_t)w_ohwi % 4 == 0);
     if (vec4)
         k_conv_direct<true><<<grid_for(be, items), kThreads, 0, be->stream>>>(g, x, w_ohwi, ep, y, acc_out);

@@ -50,6 +50,48 @@ __device__ __forceinline__ uint32_t f32_to_i8_byte_nonan(float v) {
     return __float_as_uint(round_away_magic(v)) & 0xFFu;
 }
 
+// ---- SiLU fast path with a certified result -------------------------------
+// t = fl(fl(y * fl(1/fl(1 + exp(-y)))) * inv_s_out) computed with the PTX
+// approximations ex2.approx / rcp.approx instead of the exact exp and division.
+// Error analysis (relative error of t_fast against the exact chain):
+//   * exp(-y) = 2^(y * -log2(e)): the argument is one RN product (relative error
+//     <= 1.5 * 2^-24, i.e. <= 2.2e-6 absolute for |y| <= 17), and ex2.approx adds
+//     ~2^-22.5; for |y| <= 17 this is <= 2e-6 relative in e;
+//   * for y > 17, e < 2^-24.5 so 1 + e rounds to 1 (or its neighbour) either way;
+//     for y < -17, |t| < 1e-4 * |inv_s_out| / 100 is far from any rounding boundary;
+//   * the remaining ops (1 + e, the reciprocal, two products) add a few 2^-24 each.
+// So |t_fast - t| <= 2^-17 * |t| with a margin of about 3x.  The int8 result of
+// t_fast is certified when no rounding boundary (a half-integer) lies within
+// that distance; otherwise the caller recomputes the element exactly.
+constexpr float kSiluRelErr = 7.62939453125e-06f;  // 2^-17
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// Returns kMagic + rint(clamp(t_fast)) as float bits (low byte = the int8 result)
+// and sets `uncertain` when the result is not certified.  Preconditions: fa, dsc
+// and inv finite.  When certified, rint == roundf (a tie is never certified).
+__device__ __forceinline__ uint32_t silu_fast_bits(float fa, float dsc, float inv, bool &uncertain) {
+    const float y = __fmul_rn(fa, dsc);
+    const float e = ex2_approx(__fmul_rn(y, -1.44269502162933349609375f));
+    const float sig = rcp_approx(__fadd_rn(1.0f, e));
+    const float t = __fmul_rn(__fmul_rn(y, sig), inv);
+    const float c = fminf(fmaxf(t, -128.0f), 127.0f);
+    const float r = __fadd_rn(c, kMagic);
+    const float d = fabsf(__fsub_rn(c, __fsub_rn(r, kMagic)));
+    uncertain |= !(__fsub_rn(0.5f, d) > __fmul_rn(fabsf(t), 2.0f * kSiluRelErr));
+    return __float_as_uint(r);
+}
+
 // The fused epilogue for one accumulator (contract in include/dw_cuda.h):
 // every float operation is a separately rounded IEEE op, as in the reference
 // (Rust does not contract a*b+c), so the result is bit-exact.

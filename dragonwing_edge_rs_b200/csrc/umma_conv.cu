@@ -223,7 +223,8 @@ __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs,
         m = p.ep.M ? __ldg(p.ep.M + oc) : 0.0f;
         dsc = p.ep.D ? __ldg(p.ep.D + oc) : 0.0f;
     }
-    const bool finite = isfinite(m);
+    // bit0: the fast path's float inputs are finite (M, or D and 1/s_out for SiLU)
+    const bool finite = p.ep.epilogue == DW_EPI_SILU ? (isfinite(dsc) && isfinite(p.ep.inv_s_out)) : isfinite(m);
     const long long b = bias < 0 ? -(long long)bias : (long long)bias;
     const bool safe = p.acc_bound + b < (1ll << 22);
     const uint32_t bf = __ballot_sync(0xffffffffu, finite);
@@ -255,23 +256,45 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
     const int epi = p.ep.epilogue;
     const int32_t *sb = &cs->bias[buf][ch0];
     const float *sm = &cs->m[buf][ch0];
-    uint32_t w[4];
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    const uint32_t fl = cs->cflags[buf][ch0 >> 4];
     if (epi == DW_EPI_SILU) {
         const float *sd = &cs->d[buf][ch0];
+        int32_t a[16];
+        bool inrange = true;
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            uint32_t packed = 0;
+        for (int k = 0; k < 16; k++) a[k] = (int32_t)((uint32_t)v[k] + (uint32_t)sb[k]);
+        if (!(fl & 2u)) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int k = q * 4 + j;
-                packed |= (uint32_t)(uint8_t)epilogue_one(v[k], sb[k], 0.0f, sd[k], epi, p.ep.q6, p.ep.inv_s_out)
-                          << (8 * j);
+            for (int k = 0; k < 16; k++) inrange &= (uint32_t)(a[k] + (1 << 22)) < (1u << 23);
+        }
+        uint32_t unc = 0xFFFFu;  // elements still to compute exactly
+        if ((fl & 1u) && __all_sync(0xffffffffu, inrange)) {
+            unc = 0;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                uint32_t bq[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    bool u = false;
+                    bq[j] = silu_fast_bits(i2f_small(a[q * 4 + j]), sd[q * 4 + j], p.ep.inv_s_out, u);
+                    unc |= (uint32_t)u << (q * 4 + j);
+                }
+                w[q] = __byte_perm(__byte_perm(bq[0], bq[1], 0x0040), __byte_perm(bq[2], bq[3], 0x0040), 0x5410);
             }
-            w[q] = packed;
+        }
+        if (__any_sync(0xffffffffu, unc != 0)) {
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (unc & (1u << k)) {
+                    const uint32_t b = (uint8_t)epilogue_one(v[k], sb[k], 0.0f, sd[k], epi, p.ep.q6, p.ep.inv_s_out);
+                    const int q = k >> 2, sh = 8 * (k & 3);
+                    w[q] = (w[q] & ~(0xFFu << sh)) | (b << sh);
+                }
+            }
         }
         return make_uint4(w[0], w[1], w[2], w[3]);
     }
-    const uint32_t fl = cs->cflags[buf][ch0 >> 4];
     const int4 b4[4] = {reinterpret_cast<const int4 *>(sb)[0], reinterpret_cast<const int4 *>(sb)[1],
                         reinterpret_cast<const int4 *>(sb)[2], reinterpret_cast<const int4 *>(sb)[3]};
     const float4 m4[4] = {reinterpret_cast<const float4 *>(sm)[0], reinterpret_cast<const float4 *>(sm)[1],

@@ -222,6 +222,89 @@ def mobilenetv2_block(batch=32, h=112, w=112, c=96, expand=6, seed=2):
     return b.g
 
 
+def yolov8n(batch=1, size=640, nc=80, reg_max=16, seed=8, width=0.25, depth=0.33):
+    """YOLOv8n-architecture INT8 graph (BASELINE config 4): width 0.25, depth 0.33;
+    CSPDarknet backbone of Conv(+folded BN)+SiLU layers and C2f blocks, SPPF with
+    5x5 max pooling, PAN neck with nearest 2x upsampling and channel concat, and
+    the decoupled detection head (box branch 4*reg_max channels, class branch nc
+    channels) at strides 8/16/32.  The graph input is the uint8 image, normalised
+    by 1/255 and quantised (QuantizeU8); the six head outputs are dequantised to
+    f32.  Tensors joined by a concat share one activation scale, so the concat
+    moves bytes unchanged (the builder passes the scale to their producers)."""
+    ch = lambda c: int(round(c * width))  # noqa: E731
+    rep = lambda n: max(round(n * depth), 1)  # noqa: E731
+    b = GraphBuilder(seed, act_scale_range=(0.01, 0.1))
+    img = b.input("image", (batch, size, size, 3), "u8", None)
+    s_img = float(np.float32(1.0) / np.float32(127.0))
+    x = b.g.add_tensor("image_q", (batch, size, size, 3), "i8", s_img)
+    b.g.ops.append(CompiledOp("quantize_input", "QuantizeU8", [img], [x], {"scale": s_img}))
+
+    def conv(t, c, k=3, s=1, act="silu", out_scale=None):
+        return b.conv(t, c, k=k, s=s, act=act, out_scale=out_scale)
+
+    def c2f(t, c_out, n, shortcut, out_scale=None):
+        c = c_out // 2
+        s_mid = b.act_scale()                       # cv1 output, both halves and the m outputs share it
+        y = conv(t, 2 * c, k=1, out_scale=s_mid)
+        parts = b.split(y, [c, c])
+        outs = list(parts)
+        cur = parts[1]
+        for _ in range(n):
+            h = conv(cur, c, k=3)
+            if shortcut:
+                h2 = conv(h, c, k=3)
+                cur = b.add(cur, h2, out_scale=s_mid)
+            else:
+                cur = conv(h, c, k=3, out_scale=s_mid)
+            outs.append(cur)
+        cat = b.concat(outs)
+        return conv(cat, c_out, k=1, out_scale=out_scale)
+
+    def sppf(t, c_out, out_scale=None):
+        c_ = b.g.tensors[t].shape[3] // 2
+        s_mid = b.act_scale()
+        y = conv(t, c_, k=1, out_scale=s_mid)
+        ys = [y]
+        for _ in range(3):
+            ys.append(b.maxpool(ys[-1], 5, 1, 2))
+        return conv(b.concat(ys), c_out, k=1, out_scale=out_scale)
+
+    s_a = b.act_scale()  # shared by P4, P5 and the N4'->N5 downsample (joined by concats)
+    s_b = b.act_scale()  # shared by P3, N4 and the N3->N4' downsample
+    x = conv(x, ch(64), 3, 2)                        # 0  P1/2
+    x = conv(x, ch(128), 3, 2)                       # 1  P2/4
+    x = c2f(x, ch(128), rep(3), True)                # 2
+    x = conv(x, ch(256), 3, 2)                       # 3  P3/8
+    p3 = c2f(x, ch(256), rep(6), True, out_scale=s_b)  # 4
+    x = conv(p3, ch(512), 3, 2)                      # 5  P4/16
+    p4 = c2f(x, ch(512), rep(6), True, out_scale=s_a)  # 6
+    x = conv(p4, ch(1024), 3, 2)                     # 7  P5/32
+    x = c2f(x, ch(1024), rep(3), True)               # 8
+    p5 = sppf(x, ch(1024), out_scale=s_a)            # 9
+    x = b.concat([b.upsample2(p5), p4])              # 10, 11
+    n4 = c2f(x, ch(512), rep(3), False, out_scale=s_b)  # 12
+    x = b.concat([b.upsample2(n4), p3])              # 13, 14
+    out3 = c2f(x, ch(256), rep(3), False)            # 15 (P3/8)
+    x = b.concat([conv(out3, ch(256), 3, 2, out_scale=s_b), n4])  # 16, 17
+    out4 = c2f(x, ch(512), rep(3), False)            # 18 (P4/16)
+    x = b.concat([conv(out4, ch(512), 3, 2, out_scale=s_a), p5])  # 19, 20
+    out5 = c2f(x, ch(1024), rep(3), False)           # 21 (P5/32)
+
+    c_box = max(16, ch(256) // 4, reg_max * 4)
+    c_cls = max(ch(256), min(nc, 100))
+    for i, t in enumerate((out3, out4, out5)):
+        r = conv(conv(t, c_box, 3), c_box, 3)
+        r = conv(r, 4 * reg_max, k=1, act="none")
+        c = conv(conv(t, c_cls, 3), c_cls, 3)
+        c = conv(c, nc, k=1, act="none")
+        for name, tq in ((f"box{i}", r), (f"cls{i}", c)):
+            ti = b.g.tensors[tq]
+            out = b.g.add_tensor(name, ti.shape, "f32", None)
+            b.g.ops.append(CompiledOp(f"dequantize_{name}", "Dequantize", [tq], [out], {"scale": ti.scale}))
+            b.output(out)
+    return b.g
+
+
 # ---------------------------------------------------------------------------
 # runtime
 # ---------------------------------------------------------------------------

@@ -35,6 +35,40 @@ def test_mobilenetv2_block_small_batch(be):
     rt.release()
 
 
+def test_yolov8n_int8_batch1_bit_exact(be):
+    """BASELINE config 4 architecture at 640x640, batch 1: all six head outputs
+    (dequantised int8) identical to the oracle graph run."""
+    g = G.yolov8n(batch=1, seed=8)
+    img = np.random.default_rng(5).integers(0, 256, g.tensors["image"].nbytes).astype(np.uint8)
+    rt = G.CudaGraphRuntime(g, be)
+    rt.set_input_bytes("image", img)
+    rt.capture()
+    rt.run()
+    ref = run_graph(g, {"image": img}, threads=8)
+    for name in g.outputs:
+        got = rt.get_output(name)
+        exp = ref[name].reshape(got.shape)
+        assert np.array_equal(got, exp), f"{name}: {int((got != exp).sum())} of {got.size} differ"
+    rt.release()
+
+
+def test_yolov8n_batch_independence(be):
+    """Batch 4: image i of the batch equals the same image run in a batch of 1
+    (per-image independence, the property the multi-GPU sharding relies on)."""
+    g4 = G.yolov8n(batch=4, seed=8)
+    g1 = G.yolov8n(batch=1, seed=8)
+    imgs = np.random.default_rng(6).integers(0, 256, g4.tensors["image"].nbytes).astype(np.uint8)
+    rt4, rt1 = G.CudaGraphRuntime(g4, be), G.CudaGraphRuntime(g1, be)
+    rt4.set_input_bytes("image", imgs)
+    rt4.run()
+    per = imgs.reshape(4, -1)
+    for i in (0, 3):
+        rt1.set_input_bytes("image", per[i])
+        rt1.run()
+        for name in g1.outputs:
+            assert np.array_equal(rt4.get_output(name)[i], rt1.get_output(name)[0]), (i, name)
+
+
 def test_mobilenetv2_block_full_batch_sampled(be):
     """BASELINE config 2 at its full batch (32): whole batch on the GPU, two
     sampled images checked against the oracle, and the per-image independence

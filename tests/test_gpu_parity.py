@@ -206,6 +206,23 @@ def test_conv_rounding_ties(be_umma, be_direct, k, group):
     _check_conv(be_umma, (desc, x, wt, b, M, D))
 
 
+@pytest.mark.parametrize("c_in,k,s", [(64, 1, 1), (32, 3, 1), (3, 3, 2)])
+def test_silu_stress_full_range(be, be_direct, c_in, k, s):
+    """SiLU over y in about [-20, 20] with t = silu(y)/s_out spanning the whole
+    int8 range (many outputs near rounding boundaries): the certified fast path
+    plus exact fallback must equal the oracle (shared exact exp) bit for bit,
+    on the tensor-core, small-c_in and generic direct kernels."""
+    rng = np.random.default_rng(77 + c_in + k)
+    n, h, w, c_out = 2, 48, 48, 64
+    desc, x, wt, b, M, D = conv_case(rng, n, h, w, c_in, c_out, k=k, s=s, epilogue=dw.EPI_SILU, x_range=(-128, 127))
+    acc_scale = np.sqrt(k * k * c_in) * 74.0 * 73.0
+    D = (rng.uniform(5.0, 20.0, c_out) / acc_scale).astype(np.float32)
+    s_out = np.float32(0.0932)
+    desc.inv_s_out = float(np.float32(1.0) / s_out)
+    for b_ in (be, be_direct):
+        _check_conv(b_, (desc, x, wt, b, M, D))
+
+
 @pytest.mark.parametrize("mult,c,epi", [(1, 576, dw.EPI_RELU6), (1, 32, dw.EPI_RELU), (2, 8, dw.EPI_NONE),
                                          (1, 24, dw.EPI_SILU)])
 def test_depthwise_parity(be, mult, c, epi):
