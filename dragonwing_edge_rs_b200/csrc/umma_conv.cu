@@ -59,17 +59,23 @@ struct UmmaParams {
     uint32_t tmem_cols;
     uint32_t off_out, off_chan, off_bars;   // shared-memory layout (bytes from the 1 KiB-aligned base)
     long long acc_bound;                    // |acc| <= taps * c_in * 128 * 128
+    int R;                                  // 128-row blocks per tile (R * bn <= 256)
+    int chan_all;                           // 1: every output channel's parameters staged once per CTA
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
 };
 
-// Per-tile channel parameters staged in shared memory (structure of arrays).
+// Channel parameters staged in shared memory (structure of arrays).  With
+// c_out <= kChanSlots every channel is staged once when the CTA starts (slot =
+// channel); otherwise each tile stages its bn channels into half `acc` of the
+// slots (slot = acc * kChanSlots / 2 + local channel).
+constexpr int kChanSlots = 1024;
 struct ChanSmem {
-    int32_t bias[2][256];
-    float m[2][256];
-    float d[2][256];
-    uint32_t cflags[2][16];  // per 16-channel chunk: bit0 = M finite, bit1 = |acc+bias| < 2^22 guaranteed
+    int32_t bias[kChanSlots];
+    float m[kChanSlots];
+    float d[kChanSlots];
+    uint32_t cflags[kChanSlots / 16];  // per 16 slots: bit0 = fast-path inputs finite, bit1 = |acc+bias| < 2^22 certain
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -213,12 +219,14 @@ __device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred
 }
 
 // ---------------------------------------------------------------- epilogue math
-// Loads channel `oc`'s parameters and derives its fast-path flags.  Called by
-// every epilogue thread (the ballot needs the whole warp); `et` selects the slot.
-__device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs, int buf, int et, int oc) {
+// Loads channel `oc`'s parameters into `slot` and derives the per-16-slot
+// fast-path flags.  Called by every epilogue thread (the ballots need whole
+// warps; 16 consecutive slots live in one half-warp); `write` selects the
+// threads that own a slot.
+__device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs, int slot, int oc, bool write) {
     int32_t bias = 0;
     float m = 0.0f, dsc = 0.0f;
-    if (et < p.bn && oc < p.c_out) {
+    if (write && oc < p.c_out) {
         bias = p.ep.bias ? __ldg(p.ep.bias + oc) : 0;
         m = p.ep.M ? __ldg(p.ep.M + oc) : 0.0f;
         dsc = p.ep.D ? __ldg(p.ep.D + oc) : 0.0f;
@@ -229,16 +237,16 @@ __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs,
     const bool safe = p.acc_bound + b < (1ll << 22);
     const uint32_t bf = __ballot_sync(0xffffffffu, finite);
     const uint32_t bs = __ballot_sync(0xffffffffu, safe);
-    if (et < p.bn) {
-        cs->bias[buf][et] = bias;
-        cs->m[buf][et] = m;
-        cs->d[buf][et] = dsc;
+    if (write) {
+        cs->bias[slot] = bias;
+        cs->m[slot] = m;
+        cs->d[slot] = dsc;
     }
-    const int lane = et & 31;
-    if ((lane & 15) == 0 && et < p.bn) {
+    const int lane = threadIdx.x & 31;
+    if ((lane & 15) == 0 && write) {
         const uint32_t sh = lane;  // 0 or 16
         const uint32_t f = (((bf >> sh) & 0xFFFFu) == 0xFFFFu ? 1u : 0u) | (((bs >> sh) & 0xFFFFu) == 0xFFFFu ? 2u : 0u);
-        cs->cflags[buf][et >> 4] = f;
+        cs->cflags[slot >> 4] = f;
     }
 }
 
@@ -251,15 +259,15 @@ __device__ __forceinline__ uint32_t requant_fast_byte(int32_t a, float m) {
 }
 
 // 16 accumulators (16 consecutive channels of one row) -> 16 int8, packed.
-__device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSmem *cs, int buf, int ch0,
+__device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSmem *cs, int slot0,
                                            const UmmaParams &p) {
     const int epi = p.ep.epilogue;
-    const int32_t *sb = &cs->bias[buf][ch0];
-    const float *sm = &cs->m[buf][ch0];
+    const int32_t *sb = &cs->bias[slot0];
+    const float *sm = &cs->m[slot0];
     uint32_t w[4] = {0u, 0u, 0u, 0u};
-    const uint32_t fl = cs->cflags[buf][ch0 >> 4];
+    const uint32_t fl = cs->cflags[slot0 >> 4];
     if (epi == DW_EPI_SILU) {
-        const float *sd = &cs->d[buf][ch0];
+        const float *sd = &cs->d[slot0];
         int32_t a[16];
         bool inrange = true;
 #pragma unroll
@@ -370,6 +378,42 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint64_t hi) {
 }
 
 // ------------------------------------------------------------------- kernel
+// Tile = R blocks of 128 output pixels x bn output channels.  Row block r of a
+// tile covers pixels [tile_m0 + 128 r, +128) in flat mode, or the spatial
+// sub-tile (tw x th) starting at output row oh0 + r*th in spatial mode; its
+// accumulators sit in TMEM columns [acc*R*bn + r*bn, +bn).
+struct TileCoord {
+    int mt, nt, n0, img, oh0, ow0;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const UmmaParams &p, int tile) {
+    TileCoord t;
+    t.mt = tile / p.n_tiles;
+    t.nt = tile % p.n_tiles;
+    t.n0 = t.nt * p.bn;
+    t.img = t.oh0 = t.ow0 = 0;
+    if (p.mode == 1) {
+        const int tw_i = t.mt % p.tiles_w;
+        const int t2 = t.mt / p.tiles_w;
+        t.oh0 = (t2 % p.tiles_h) * p.th * p.R;
+        t.img = t2 / p.tiles_h;
+        t.ow0 = tw_i * p.tw;
+    }
+    return t;
+}
+
+// Row blocks of the tile that hold at least one in-range output pixel (the
+// others are neither loaded nor stored).
+__device__ __forceinline__ int valid_blocks(const UmmaParams &p, const TileCoord &t) {
+    if (p.mode == 0) {
+        const long long first = (long long)t.mt * p.R * kBM;
+        const long long left = (p.rows - first + kBM - 1) / kBM;
+        return (int)(left < p.R ? left : p.R);
+    }
+    const int left = (p.ho - t.oh0 + p.th - 1) / p.th;
+    return left < p.R ? left : p.R;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     k_umma_conv_i8(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ UmmaParams p) {
@@ -378,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *a_smem = smem;
     uint8_t *b_smem = smem + (size_t)p.stages * p.a_stage_bytes;
-    uint8_t *out_stage = smem + p.off_out;                          // [128 rows][bn] int8 output tile
+    uint8_t *out_stage = smem + p.off_out;                          // [R*128 rows][bn] int8 output tile
     ChanSmem *chan = reinterpret_cast<ChanSmem *>(smem + p.off_chan);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bars);
     uint64_t *full_bar = bars;                      // [stages]
@@ -412,11 +456,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    if (warp >= 2 && p.chan_all) {
+        // every output channel's parameters, once (all 256 epilogue threads take
+        // part in every round: the flags use warp ballots)
+        const int et = threadIdx.x - 64;
+        for (int base = 0; base < p.c_out; base += kEpiWarps * 32)
+            stage_channel(p, chan, base + et, base + et, base + et < p.c_out);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int k_iters = p.taps * p.cblocks;
+    const uint32_t acc_cols = (uint32_t)(p.R * p.bn);
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -428,33 +480,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t issued_mask = 0, last_parity = 0;  // per stage: issued at least once / parity of last issue
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-                const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
-                const int n0 = nt * p.bn;
-                int img = 0, oh0 = 0, ow0 = 0;
-                if (p.mode == 1) {
-                    const int tw_i = mt % p.tiles_w;
-                    const int t2 = mt / p.tiles_w;
-                    oh0 = (t2 % p.tiles_h) * p.th;
-                    img = t2 / p.tiles_h;
-                    ow0 = tw_i * p.tw;
-                }
+                const TileCoord tc = tile_coord(p, tile);
+                const int nrb = valid_blocks(p, tc);
                 for (int it = 0; it < k_iters; it++) {
                     if (!mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1, p, abort_flag, 1)) { ok = false; break; }
                     const int tap = it / p.cblocks, cb = it % p.cblocks;
                     const uint32_t fb = smem_u32(&full_bar[s]);
-                    mbar_expect_tx(fb, p.a_tx_bytes + p.b_tx_bytes);
+                    mbar_expect_tx(fb, (uint32_t)nrb * p.a_tx_bytes + p.b_tx_bytes);
                     const uint32_t a_dst = smem_u32(a_smem + (size_t)s * p.a_stage_bytes);
                     const uint32_t b_dst = smem_u32(b_smem + (size_t)s * p.b_stage_bytes);
                     if (p.mode == 0) {
-                        tma_load_2d(a_dst, &tmap_a, fb, cb * p.bk, mt * kBM);
+                        for (int r = 0; r < nrb; r++)
+                            tma_load_2d(a_dst + (uint32_t)(r * kBM * p.bk), &tmap_a, fb, cb * p.bk,
+                                        (tc.mt * p.R + r) * kBM);
                     } else {
                         const int kh = tap / p.kw, kw = tap % p.kw;
                         const int dh = kh - p.pt, dwc = kw - p.pl;
                         const int par_h = ((dh % p.sh) + p.sh) % p.sh, par_w = ((dwc % p.sw) + p.sw) % p.sw;
                         const int hq = (dh - par_h) / p.sh, wq = (dwc - par_w) / p.sw;
-                        tma_load_5d(a_dst, &tmap_a, fb, par_w * p.c_in + cb * p.bk, ow0 + wq, par_h, oh0 + hq, img);
+                        for (int r = 0; r < nrb; r++)
+                            tma_load_5d(a_dst + (uint32_t)(r * kBM * p.bk), &tmap_a, fb, par_w * p.c_in + cb * p.bk,
+                                        tc.ow0 + wq, par_h, tc.oh0 + r * p.th + hq, tc.img);
                     }
-                    tma_load_3d(b_dst, &tmap_b, fb, cb * p.bk, tap, n0);
+                    tma_load_3d(b_dst, &tmap_b, fb, cb * p.bk, tap, tc.n0);
                     issued_mask |= 1u << s;
                     last_parity = (last_parity & ~(1u << s)) | (ph << s);
                     if (++s == p.stages) { s = 0; ph ^= 1; }
@@ -483,22 +531,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t acc_ph = (local >> 1) & 1;
                 if (!mbar_wait(smem_u32(&tempty_bar[acc]), acc_ph ^ 1, p, abort_flag, 2)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * p.bn);
+                const uint32_t d_tmem = tmem_base + (uint32_t)acc * acc_cols;
                 for (int it = 0; it < k_iters; it++) {
                     if (!mbar_wait(smem_u32(&full_bar[s]), ph, p, abort_flag, 3)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(a_smem + (size_t)s * p.a_stage_bytes);
                     const uint32_t b_addr = smem_u32(b_smem + (size_t)s * p.b_stage_bytes);
                     for (int k = 0; k < p.bk / 32; k++) {
-                        const uint64_t ad = smem_desc(a_addr + 32 * k, p.desc_hi);
                         const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
-                        tc_mma_i8(d_tmem, ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
+                        for (int r = 0; r < p.R; r++) {
+                            const uint64_t ad = smem_desc(a_addr + (uint32_t)(r * kBM * p.bk) + 32 * k, p.desc_hi);
+                            tc_mma_i8(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
+                        }
                     }
                     tc_commit(smem_u32(&empty_bar[s]));  // frees the stage when these MMAs finish
                     if (++s == p.stages) { s = 0; ph ^= 1; }
                 }
                 if (!ok) break;
-                tc_commit(smem_u32(&tfull_bar[acc]));  // accumulator ready for the epilogue
+                tc_commit(smem_u32(&tfull_bar[acc]));  // accumulators ready for the epilogue
             }
             if (!ok) {
                 // Abort: wait (bounded) until the MMAs already issued have retired,
@@ -514,34 +564,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int e = warp - 2;               // 0..7
         const int et = threadIdx.x - 64;      // 0..255 epilogue thread index
         const int quarter = warp & 3;         // TMEM lanes this warp may access
-        const int half = e >> 2;              // which half of the columns
-        const int row = quarter * 32 + lane;  // tile row
+        const int half = e >> 2;              // which half of the (row block, chunk) items
+        const int row = quarter * 32 + lane;  // row within a 128-row block
+        const int chunks = p.bn / 16;
+        const int items = p.R * chunks;
         int local = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
-            const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
-            const int n0 = nt * p.bn;
-            // Stage this tile's per-channel parameters (one channel per thread).
-            stage_channel(p, chan, acc, et, n0 + et);
+            const TileCoord tc = tile_coord(p, tile);
+            int slot_base = tc.n0;
+            if (!p.chan_all) {  // this tile's channels into half `acc` of the slots
+                slot_base = acc * (kChanSlots / 2);
+                stage_channel(p, chan, slot_base + et, tc.n0 + et, et < p.bn);
+            }
             bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), acc_ph, p, abort_flag, 4);
             // Barrier A (epilogue threads only): all-or-none abort decision; the
             // staging buffer is free again (the store issuer waited for the
-            // previous store's reads before arriving).
+            // previous stores' reads before arriving).
             if (et == 0) bulk_wait_read0();
             if (named_barrier_or(1, kEpiWarps * 32, !ok)) break;
             tc_fence_after();
-            const int chunks = p.bn / 16;
-            const int per_half = (chunks + 1) / 2;
-            const int c_begin = half * per_half, c_end = min(chunks, c_begin + per_half);
-            const uint32_t trow = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
-            uint8_t *srow = out_stage + (size_t)row * p.bn;
-            for (int c = c_begin; c < c_end; c++) {
-                int32_t v[16];
-                tc_ld16(trow + (uint32_t)(c * 16), v);
+            const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * acc_cols;
+            // items i = half, half + 2, ...: two TMEM loads in flight per wait
+            for (int i = half; i < items; i += 4) {
+                const int i2 = i + 2;
+                const bool two = i2 < items;
+                const int r1 = i / chunks, c1 = i % chunks;
+                const int r2 = two ? i2 / chunks : r1, c2 = two ? i2 % chunks : c1;
+                int32_t v1[16], v2[16];
+                tc_ld16(tacc + (uint32_t)(r1 * p.bn + c1 * 16), v1);
+                tc_ld16(tacc + (uint32_t)(r2 * p.bn + c2 * 16), v2);
                 tc_wait_ld();
-                const uint4 q = requant16(v, chan, acc, c * 16, p);
-                *reinterpret_cast<uint4 *>(srow + c * 16) = q;
+                const uint4 q1 = requant16(v1, chan, slot_base + c1 * 16, p);
+                *reinterpret_cast<uint4 *>(out_stage + ((size_t)(r1 * kBM + row)) * p.bn + c1 * 16) = q1;
+                if (two) {
+                    const uint4 q2 = requant16(v2, chan, slot_base + c2 * 16, p);
+                    *reinterpret_cast<uint4 *>(out_stage + ((size_t)(r2 * kBM + row)) * p.bn + c2 * 16) = q2;
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -549,13 +609,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging writes -> async proxy
             named_barrier_sync(2, kEpiWarps * 32);
             if (et == 0) {
-                if (p.mode == 0) {
-                    tma_store_2d(&tmap_y, smem_u32(out_stage), n0, mt * kBM);
-                } else {
-                    const int tw_i = mt % p.tiles_w;
-                    const int t2 = mt / p.tiles_w;
-                    tma_store_4d(&tmap_y, smem_u32(out_stage), n0, tw_i * p.tw, (t2 % p.tiles_h) * p.th,
-                                 t2 / p.tiles_h);
+                const int nrb = valid_blocks(p, tc);
+                for (int r = 0; r < nrb; r++) {
+                    const uint32_t src = smem_u32(out_stage + (size_t)r * kBM * p.bn);
+                    if (p.mode == 0)
+                        tma_store_2d(&tmap_y, src, tc.n0, (tc.mt * p.R + r) * kBM);
+                    else
+                        tma_store_4d(&tmap_y, src, tc.n0, tc.ow0, tc.oh0 + r * p.th, tc.img);
                 }
                 bulk_commit();
             }
@@ -649,23 +709,32 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
     p.bn = pick_bn(d.c_out);
     p.cblocks = (d.c_in + p.bk - 1) / p.bk;
     p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
+    // Row blocks per tile: R * bn <= 256 (two TMEM accumulator buffers within 512
+    // columns), at most 8, and an A stage (R * 128 rows * bk) of at most 32 KiB.
+    int R = std::max(1, std::min({8, 256 / p.bn, 32768 / (kBM * p.bk)}));
     if (flat) {
         p.rows = (long long)d.n * d.h * d.w;
-        p.m_tiles = (int)((p.rows + kBM - 1) / kBM);
+        const long long blocks = (p.rows + kBM - 1) / kBM;
+        R = (int)std::min<long long>(R, blocks);
+        p.R = R;
+        p.m_tiles = (int)((blocks + R - 1) / R);
         p.tw = kBM; p.th = 1;
         p.a_tx_bytes = (uint32_t)(kBM * p.bk);
     } else {
         pick_tile(ho, wo, &p.tw, &p.th);
+        R = std::min(R, (ho + p.th - 1) / p.th);
+        p.R = R;
         p.tiles_w = (wo + p.tw - 1) / p.tw;
-        p.tiles_h = (ho + p.th - 1) / p.th;
+        p.tiles_h = (ho + p.th * R - 1) / (p.th * R);
         p.m_tiles = d.n * p.tiles_w * p.tiles_h;
         p.a_tx_bytes = (uint32_t)(p.tw * p.th * p.bk);
     }
     p.num_tiles = p.m_tiles * p.n_tiles;
+    p.chan_all = p.n_tiles * p.bn <= kChanSlots ? 1 : 0;  // every slot a tile reads lies in the arrays
     p.b_tx_bytes = (uint32_t)(p.bn * p.bk);
-    p.a_stage_bytes = (uint32_t)al1k((size_t)kBM * p.bk);
+    p.a_stage_bytes = (uint32_t)al1k((size_t)p.R * kBM * p.bk);
     p.b_stage_bytes = (uint32_t)al1k((size_t)p.bn * p.bk);
-    const size_t out_bytes = al1k((size_t)kBM * p.bn);
+    const size_t out_bytes = al1k((size_t)p.R * kBM * p.bn);
     const size_t chan_bytes = al1k(sizeof(ChanSmem));
     const size_t fixed = 1024 /*align slack*/ + out_bytes + chan_bytes + 256 /*barriers*/;
     int stages = (int)((kSmemLimit - fixed) / (p.a_stage_bytes + p.b_stage_bytes));
@@ -685,7 +754,7 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
     // swizzle layout at bits 61-63.
     p.desc_hi = ((uint64_t)((8 * p.bk) >> 4) << 32) | (1ull << 46) | ((uint64_t)swizzle_layout(p.bk) << 61);
     uint32_t cols = 32;
-    while (cols < (uint32_t)(2 * p.bn)) cols <<= 1;
+    while (cols < (uint32_t)(2 * p.R * p.bn)) cols <<= 1;
     p.tmem_cols = cols;
     p.wait_cap_ns = be->wait_cap_ns;
     p.err = be->dev_err;
