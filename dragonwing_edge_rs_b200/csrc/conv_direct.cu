@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(kThreads) k_conv_direct(ConvGeom g, const int8
             const int32_t bias = ep.bias ? __ldg(ep.bias + oc) : 0;
             const float m = ep.M ? __ldg(ep.M + oc) : 0.0f;
             const float dsc = ep.D ? __ldg(ep.D + oc) : 0.0f;
-            y[i] = (int8_t)epilogue_one(acc, bias, m, dsc, ep.epilogue, ep.q6, ep.inv_s_out);
+            y[i] = (int8_t)epilogue_one_slow(acc, bias, m, dsc, ep.epilogue, ep.q6, ep.inv_s_out);
         }
     }
 }
@@ -78,7 +78,7 @@ __device__ __forceinline__ uint32_t epilogue_byte(int32_t acc, int32_t bias, flo
             if (!u) return bits & 0xFFu;
         }
     }
-    return (uint8_t)epilogue_one(acc, bias, m, dsc, ep.epilogue, ep.q6, ep.inv_s_out);
+    return (uint8_t)epilogue_one_slow(acc, bias, m, dsc, ep.epilogue, ep.q6, ep.inv_s_out);
 }
 
 // Dense conv with few input channels (the 3-channel stem, or any c_in the
@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kThreads) k_dwconv16(ConvGeom g, const int8_t 
                 const int32_t bias = ep.bias ? __ldg(ep.bias + c) : 0;
                 const float m = ep.M ? __ldg(ep.M + c) : 0.0f;
                 const float dsc = ep.D ? __ldg(ep.D + c) : 0.0f;
-                packed |= (uint32_t)(uint8_t)epilogue_one(acc[v * 4 + k], bias, m, dsc, ep.epilogue, ep.q6,
+                packed |= (uint32_t)(uint8_t)epilogue_one_slow(acc[v * 4 + k], bias, m, dsc, ep.epilogue, ep.q6,
                                                           ep.inv_s_out)
                           << (8 * k);
             }
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(256, 2) k_dwconv3x3(ConvGeom g, const int8_t *
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
                         const int32_t ai = __float_as_int(__fadd_rn(acc[r][q][k], kMagic)) - kMagicBits;
-                        packed |= (uint32_t)(uint8_t)epilogue_one(ai, bias[k], m[k], dsc[k], ep.epilogue, ep.q6,
+                        packed |= (uint32_t)(uint8_t)epilogue_one_slow(ai, bias[k], m[k], dsc[k], ep.epilogue, ep.q6,
                                                                   ep.inv_s_out)
                                   << (8 * k);
                     }
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kThreads) k_dwconv_generic(ConvGeom g, int mul
             const int32_t bias = ep.bias ? __ldg(ep.bias + oc) : 0;
             const float mm = ep.M ? __ldg(ep.M + oc) : 0.0f;
             const float dsc = ep.D ? __ldg(ep.D + oc) : 0.0f;
-            y[i] = (int8_t)epilogue_one(acc, bias, mm, dsc, ep.epilogue, ep.q6, ep.inv_s_out);
+            y[i] = (int8_t)epilogue_one_slow(acc, bias, mm, dsc, ep.epilogue, ep.q6, ep.inv_s_out);
         }
     }
 }

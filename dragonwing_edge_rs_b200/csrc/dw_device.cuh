@@ -109,6 +109,14 @@ __device__ __forceinline__ int32_t epilogue_one(int32_t acc, int32_t bias, float
     return q;
 }
 
+// Out-of-line copy of epilogue_one for the rare exact fallbacks (ties, large
+// accumulators, uncertain SiLU results): keeps the double-precision exp and the
+// generic paths out of the hot loops' instruction stream.
+static __device__ __noinline__ int32_t epilogue_one_slow(int32_t acc, int32_t bias, float m, float dsc, int epi, int q6,
+                                                  float inv_s_out) {
+    return epilogue_one(acc, bias, m, dsc, epi, q6, inv_s_out);
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

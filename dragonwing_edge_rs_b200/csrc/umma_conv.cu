@@ -28,6 +28,7 @@
 // TMA is used anywhere (the same code runs on 1..8 GPUs).
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "dw_device.cuh"
 
@@ -259,14 +260,17 @@ __device__ __forceinline__ uint32_t requant_fast_byte(int32_t a, float m) {
 }
 
 // 16 accumulators (16 consecutive channels of one row) -> 16 int8, packed.
+// kSilu selects the SiLU epilogue at compile time (separate kernel instances keep
+// each epilogue's code out of the other's instruction stream).
+template <bool kSilu>
 __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSmem *cs, int slot0,
                                            const UmmaParams &p) {
-    const int epi = p.ep.epilogue;
+    const int epi = kSilu ? DW_EPI_SILU : p.ep.epilogue;
     const int32_t *sb = &cs->bias[slot0];
     const float *sm = &cs->m[slot0];
     uint32_t w[4] = {0u, 0u, 0u, 0u};
     const uint32_t fl = cs->cflags[slot0 >> 4];
-    if (epi == DW_EPI_SILU) {
+    if (kSilu) {
         const float *sd = &cs->d[slot0];
         int32_t a[16];
         bool inrange = true;
@@ -295,7 +299,7 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
 #pragma unroll
             for (int k = 0; k < 16; k++) {
                 if (unc & (1u << k)) {
-                    const uint32_t b = (uint8_t)epilogue_one(v[k], sb[k], 0.0f, sd[k], epi, p.ep.q6, p.ep.inv_s_out);
+                    const uint32_t b = (uint8_t)epilogue_one_slow(v[k], sb[k], 0.0f, sd[k], epi, p.ep.q6, p.ep.inv_s_out);
                     const int q = k >> 2, sh = 8 * (k & 3);
                     w[q] = (w[q] & ~(0xFFu << sh)) | (b << sh);
                 }
@@ -360,7 +364,7 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const int k = q * 4 + j;
-                packed |= (uint32_t)(uint8_t)epilogue_one(v[k], bb[k], mm[k], 0.0f, epi, p.ep.q6, p.ep.inv_s_out)
+                packed |= (uint32_t)(uint8_t)epilogue_one_slow(v[k], bb[k], mm[k], 0.0f, epi, p.ep.q6, p.ep.inv_s_out)
                           << (8 * j);
             }
             w[q] = packed;
@@ -414,6 +418,7 @@ __device__ __forceinline__ int valid_blocks(const UmmaParams &p, const TileCoord
     return left < p.R ? left : p.R;
 }
 
+template <bool kSilu>
 __global__ void __launch_bounds__(kThreads, 1)
     k_umma_conv_i8(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ UmmaParams p) {
@@ -455,13 +460,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                      "r"(p.tmem_cols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    if (warp >= 2 && p.chan_all) {
-        // every output channel's parameters, once (all 256 epilogue threads take
-        // part in every round: the flags use warp ballots)
-        const int et = threadIdx.x - 64;
-        for (int base = 0; base < p.c_out; base += kEpiWarps * 32)
-            stage_channel(p, chan, base + et, base + et, base + et < p.c_out);
     }
     tc_fence_before();
     __syncthreads();
@@ -537,6 +535,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(a_smem + (size_t)s * p.a_stage_bytes);
                     const uint32_t b_addr = smem_u32(b_smem + (size_t)s * p.b_stage_bytes);
+                    if (p.R == 1) {  // the common single-block issue loop (measurably faster)
+                        for (int k = 0; k < p.bk / 32; k++) {
+                            const uint64_t ad = smem_desc(a_addr + 32 * k, p.desc_hi);
+                            const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
+                            tc_mma_i8(d_tmem, ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
+                        }
+                    } else
                     for (int k = 0; k < p.bk / 32; k++) {
                         const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
                         for (int r = 0; r < p.R; r++) {
@@ -569,39 +574,72 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int chunks = p.bn / 16;
         const int items = p.R * chunks;
         int local = 0;
+        if (p.chan_all) {
+            // every output channel's parameters, once, while the first tile's MMAs
+            // run (all 256 epilogue threads take part in every round: the flags use
+            // warp ballots; barrier A of the first tile publishes them)
+            for (int base = 0; base < p.c_out; base += kEpiWarps * 32)
+                stage_channel(p, chan, base + et, base + et, base + et < p.c_out);
+        }
+        // Per-tile channel mode: a tile's channels are staged into half `acc` of
+        // the slots one tile ahead (the global loads overlap the previous tile).
+        if (!p.chan_all && (int)blockIdx.x < p.num_tiles)
+            stage_channel(p, chan, et, tile_coord(p, blockIdx.x).n0 + et, et < p.bn);
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
             const TileCoord tc = tile_coord(p, tile);
-            int slot_base = tc.n0;
-            if (!p.chan_all) {  // this tile's channels into half `acc` of the slots
-                slot_base = acc * (kChanSlots / 2);
-                stage_channel(p, chan, slot_base + et, tc.n0 + et, et < p.bn);
-            }
+            const int slot_base = p.chan_all ? tc.n0 : acc * (kChanSlots / 2);
             bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), acc_ph, p, abort_flag, 4);
             // Barrier A (epilogue threads only): all-or-none abort decision; the
             // staging buffer is free again (the store issuer waited for the
-            // previous stores' reads before arriving).
+            // previous stores' reads before arriving); this tile's staged
+            // channel parameters are visible.
             if (et == 0) bulk_wait_read0();
             if (named_barrier_or(1, kEpiWarps * 32, !ok)) break;
+            if (!p.chan_all) {  // next tile's channels into the other half (its readers finished before barrier A)
+                const int next = tile + (int)gridDim.x;
+                if (next < p.num_tiles)
+                    stage_channel(p, chan, (acc ^ 1) * (kChanSlots / 2) + et, tile_coord(p, next).n0 + et,
+                                  et < p.bn);
+            }
             tc_fence_after();
             const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * acc_cols;
-            // items i = half, half + 2, ...: two TMEM loads in flight per wait
-            for (int i = half; i < items; i += 4) {
-                const int i2 = i + 2;
-                const bool two = i2 < items;
-                const int r1 = i / chunks, c1 = i % chunks;
-                const int r2 = two ? i2 / chunks : r1, c2 = two ? i2 % chunks : c1;
+            // each half of the warps takes a contiguous run of (row block, chunk)
+            // items, two TMEM loads in flight per wait; (r, c) advance without division.
+            if (p.R == 1) {  // one row block: contiguous chunk halves, one TMEM load per wait
+                const int per1 = (chunks + 1) / 2;
+                const int cb = half * per1, ce = min(chunks, cb + per1);
+                for (int c = cb; c < ce; c++) {
+                    int32_t v[16];
+                    tc_ld16(tacc + (uint32_t)(c * 16), v);
+                    tc_wait_ld();
+                    const uint4 q = requant16<kSilu>(v, chan, slot_base + c * 16, p);
+                    *reinterpret_cast<uint4 *>(out_stage + (size_t)row * p.bn + c * 16) = q;
+                }
+            } else {
+            const int per = (items + 1) / 2;
+            const int i_begin = half * per, i_end = min(items, i_begin + per);
+            int r1 = 0, c1 = i_begin;
+            while (c1 >= chunks) { c1 -= chunks; r1++; }
+            for (int i = i_begin; i < i_end; i += 2) {
+                const bool two = i + 1 < i_end;
+                int r2 = r1, c2 = c1 + 1;
+                if (c2 >= chunks) { c2 -= chunks; r2++; }
+                if (!two) { r2 = r1; c2 = c1; }
                 int32_t v1[16], v2[16];
                 tc_ld16(tacc + (uint32_t)(r1 * p.bn + c1 * 16), v1);
                 tc_ld16(tacc + (uint32_t)(r2 * p.bn + c2 * 16), v2);
                 tc_wait_ld();
-                const uint4 q1 = requant16(v1, chan, slot_base + c1 * 16, p);
+                const uint4 q1 = requant16<kSilu>(v1, chan, slot_base + c1 * 16, p);
                 *reinterpret_cast<uint4 *>(out_stage + ((size_t)(r1 * kBM + row)) * p.bn + c1 * 16) = q1;
                 if (two) {
-                    const uint4 q2 = requant16(v2, chan, slot_base + c2 * 16, p);
+                    const uint4 q2 = requant16<kSilu>(v2, chan, slot_base + c2 * 16, p);
                     *reinterpret_cast<uint4 *>(out_stage + ((size_t)(r2 * kBM + row)) * p.bn + c2 * 16) = q2;
                 }
+                c1 += 2;
+                while (c1 >= chunks) { c1 -= chunks; r1++; }
+            }
             }
             tc_fence_before();
             __syncwarp();
@@ -706,6 +744,10 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
     p.taps = d.k_h * d.k_w; p.kw = d.k_w; p.sh = d.stride_h; p.sw = d.stride_w; p.pt = d.pad_t; p.pl = d.pad_l;
     p.c_in = d.c_in;
     p.bk = pick_bk(d.c_in);
+    if (const char *e = getenv("DW_UMMA_BK")) {  // tuning override: 32, 64 or 128 bytes of K per stage
+        const int v = atoi(e);
+        if (v == 32 || v == 64 || v == 128) p.bk = v;
+    }
     p.bn = pick_bn(d.c_out);
     p.cblocks = (d.c_in + p.bk - 1) / p.bk;
     p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
@@ -819,11 +861,15 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
     static bool attr_set[16] = {};
     int dev = be->device;
     if (dev < 16 && !attr_set[dev]) {
-        cudaFuncSetAttribute(k_umma_conv_i8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
         attr_set[dev] = true;
     }
     const int grid = std::min(p.num_tiles, be->sm_count);
-    k_umma_conv_i8<<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
+    if (ep.epilogue == DW_EPI_SILU)
+        k_umma_conv_i8<true><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
+    else
+        k_umma_conv_i8<false><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
     return dw_after_launch(be, "umma_conv_i8");
 }
 
