@@ -214,12 +214,10 @@ def run_ours(args, rank, world, local_rank):
             dist.all_reduce(t)
             torch.cuda.synchronize()
 
+    from dragonwing_edge_rs_b200 import replicas
+
     def max_over_ranks(v: float) -> float:
-        if not dist:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return replicas.max_over_ranks(dist, v, device="cuda")
 
     batch = args.batch or workload_defaults(args.workload)
     graph, cfg = build_workload(args.workload, batch, seed=1234)
@@ -257,7 +255,7 @@ def run_ours(args, rank, world, local_rank):
     sampler.mark_end()
     torch.cuda.synchronize()
     barrier()
-    launches = be.launch_count() - launches0
+    launches = replicas.sum_over_ranks(dist, be.launch_count() - launches0, device="cuda")
     sampler.stop()
     ms_local = e0.elapsed_time(e1)
     ms = max_over_ranks(ms_local)
@@ -370,7 +368,7 @@ def run_ours(args, rank, world, local_rank):
                     "images_per_s": round(e2e_ips, 1), "conv_tops": round(e2e_tops, 3),
                     "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
                     "path": "CudaGraphRuntime: dw_upload_async (pinned) -> graph -> dw_download_async (pinned)"},
-            "gpu_launches": int(launches),
+            "gpu_launches": int(launches),  # all ranks
             "kernels_per_step": int(kernels_per_step),
             "roofline": roof,
             "per_op": per_op,
@@ -379,8 +377,12 @@ def run_ours(args, rank, world, local_rank):
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    # every rank reports its backend status; a failed rank fails the run on all ranks
+    statuses = replicas.exchange_status(dist, 0)
     rt.release()
     be.close()
+    if any(not st.ok for st in statuses):
+        raise SystemExit(f"rank failures: {[(st.rank, st.status, st.message) for st in statuses if not st.ok]}")
     if dist:
         dist.destroy_process_group()
 
