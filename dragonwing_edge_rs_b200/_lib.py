@@ -90,6 +90,20 @@ SIGNATURES = {
     "dw_concat_i8": ([vp, PVP, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, sz, vp], i32),
     "dw_slice_c_i8": ([vp, vp, vp, sz, sz, sz, sz], i32),
     "dw_resize_nearest_i8": ([vp, vp, vp] + [sz] * 6, i32),
+    # fp16 path
+    "dw_prepare_weights_f16": ([vp, ctypes.POINTER(DwConvDesc), vp, PVP], i32),
+    "dw_conv2d_f16": ([vp, ctypes.POINTER(DwConvDesc), vp, vp, vp, vp], i32),
+    "dw_conv2d_fp16_nhwc": ([vp, vp, vp, vp] + [sz] * 11, i32),
+    "dw_gemm_f16": ([vp, vp, vp, vp, sz, sz, sz], i32),
+    "dw_prepare_gemm_b_f16": ([vp, vp, sz, sz, PVP], i32),
+    "dw_gemm_f16_bias": ([vp, vp, vp, vp, vp, sz, sz, sz, i32], i32),
+    "dw_add_f16": ([vp, vp, vp, vp], i32),
+    "dw_add_relu_f16": ([vp, vp, vp, vp], i32),
+    "dw_relu_f16": ([vp, vp], i32),
+    "dw_maxpool_f16": ([vp, vp, vp] + [sz] * 12, i32),
+    "dw_global_avgpool_f16": ([vp, vp, vp] + [sz] * 4, i32),
+    "dw_cast_f32_to_f16": ([vp, vp, vp, sz, sz, sz], i32),
+    "dw_cast_f16_to_f32": ([vp, vp, vp], i32),
 }
 
 _lib = None

@@ -2,6 +2,8 @@
 // requantisation epilogue, bounded waits and the device error record.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include <cstdint>
 
 #include "dw_expf.h"
@@ -115,6 +117,32 @@ __device__ __forceinline__ int32_t epilogue_one(int32_t acc, int32_t bias, float
 static __device__ __noinline__ int32_t epilogue_one_slow(int32_t acc, int32_t bias, float m, float dsc, int epi, int q6,
                                                   float inv_s_out) {
     return epilogue_one(acc, bias, m, dsc, epi, q6, inv_s_out);
+}
+
+// ---- fp16 conversions with the reference's exact results ---------------------
+// F16::to_f32 (crates/dragonwing-core/src/dtype.rs:225-263) is exact for normal
+// halves, infinities and zeros; a subnormal half converts to exactly half its
+// value (the renormalisation loop's exponent is one too small), and a NaN keeps
+// its payload with the quiet bit set.  Every fp16 kernel that follows a CPU op
+// converting with to_f32 uses this to stay bit-identical with it.
+__device__ __forceinline__ float f16_to_f32_ref(uint16_t h) {
+    const uint32_t e = h & 0x7C00u;
+    if (e == 0x7C00u && (h & 0x03FFu))
+        return __uint_as_float(((uint32_t)(h & 0x8000u) << 16) | 0x7FC00000u | ((uint32_t)(h & 0x03FFu) << 13));
+    const float f = __half2float(__ushort_as_half(h));
+    return e == 0 ? __fmul_rn(f, 0.5f) : f;
+}
+
+// F16::from_f32 (dtype.rs:164-222): round to nearest even with subnormals and
+// overflow to infinity, which is cvt.rn.f16.f32 for every non-NaN input; a NaN
+// maps to sign | 0x7E00 | min(payload >> 13, 0x1FF).
+__device__ __forceinline__ uint16_t f32_to_f16_ref(float v) {
+    if (v != v) {
+        const uint32_t b = __float_as_uint(v);
+        const uint32_t m = min((b & 0x007FFFFFu) >> 13, 0x1FFu);
+        return (uint16_t)(((b >> 16) & 0x8000u) | 0x7E00u | m);
+    }
+    return __half_as_ushort(__float2half_rn(v));
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

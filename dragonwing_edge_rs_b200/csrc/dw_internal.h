@@ -98,7 +98,26 @@ dw_status launch_dwconv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo
 
 // umma_conv.cu (tcgen05 implicit GEMM)
 bool umma_supported(const dw_backend *be, const dw_conv_desc &d, int ho, int wo);
+bool umma_supported_f16(const dw_backend *be, const dw_conv_desc &d, int ho, int wo);
 dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
                               const int8_t *w_ohwi, const EpiParams &ep, int8_t *y);
+dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,
+                               const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y);
+
+// fp16.cu (CUDA-core fp16 kernels)
+dw_status launch_conv_direct_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,
+                                 const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y);
+dw_status launch_dwconv_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,
+                            const uint16_t *w_hwcm, const uint16_t *bias, int relu, uint16_t *y);
+dw_status launch_add_f16(dw_backend *be, const uint16_t *a, const uint16_t *b, uint16_t *y, size_t n, int relu);
+dw_status launch_relu_f16(dw_backend *be, const uint16_t *x, uint16_t *y, size_t n);
+dw_status launch_maxpool_f16(dw_backend *be, const uint16_t *x, uint16_t *y, int n, int h, int w, int c, int kh,
+                             int kw, int sh, int sw, int pt, int pl, int ho, int wo);
+dw_status launch_gap_f16(dw_backend *be, const uint16_t *x, uint16_t *y, int n, int h, int w, int c);
+dw_status launch_repack_hwio_to_ohwi_f16(dw_backend *be, const uint16_t *w, uint16_t *out, int taps, int c_in,
+                                         int c_out);
+dw_status launch_transpose_kn_to_nk_f16(dw_backend *be, const uint16_t *b, uint16_t *out, int k, int n);
+dw_status launch_cast_f32_to_f16(dw_backend *be, const float *x, uint16_t *y, size_t pixels, int c_src, int c_dst);
+dw_status launch_cast_f16_to_f32(dw_backend *be, const uint16_t *x, float *y, size_t n);
 
 }  // namespace dw

@@ -267,10 +267,10 @@ __global__ void k_resize_nearest_i8(const int8_t *__restrict__ x, int8_t *__rest
     }
 }
 
-// --- weight repacks ------------------------------------------------------------
+// --- weight repacks (int8 and fp16 element types) ------------------------------------------------------------
 // HWIO [taps][c_in][c_out] -> OHWI [c_out][taps][c_in] (K-major rows for the MMA B operand).
-__global__ void k_repack_hwio_to_ohwi(const int8_t *__restrict__ w, int8_t *__restrict__ o, int taps, int c_in,
-                                      int c_out) {
+template <typename T>
+__global__ void k_repack_hwio_to_ohwi(const T *__restrict__ w, T *__restrict__ o, int taps, int c_in, int c_out) {
     const size_t total = (size_t)taps * c_in * c_out;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         // i indexes the output: i = (oc * taps + t) * c_in + ic
@@ -283,8 +283,9 @@ __global__ void k_repack_hwio_to_ohwi(const int8_t *__restrict__ w, int8_t *__re
 }
 
 // B [k][n] row-major -> [n][k] (K-major).
-__global__ void k_transpose_kn_to_nk(const int8_t *__restrict__ b, int8_t *__restrict__ o, int k, int n) {
-    __shared__ int8_t tile[32][33];
+template <typename T>
+__global__ void k_transpose_kn_to_nk(const T *__restrict__ b, T *__restrict__ o, int k, int n) {
+    __shared__ T tile[32][33];
     for (int n0 = blockIdx.x * 32; n0 < n; n0 += gridDim.x * 32)
         for (int k0 = blockIdx.y * 32; k0 < k; k0 += gridDim.y * 32) {
             int tx = threadIdx.x, ty = threadIdx.y;
@@ -426,15 +427,29 @@ dw_status launch_resize_nearest_i8(dw_backend *be, const int8_t *x, int8_t *y, i
 
 dw_status launch_repack_hwio_to_ohwi(dw_backend *be, const int8_t *w, int8_t *out, int taps, int c_in, int c_out) {
     size_t items = (size_t)taps * c_in * c_out;
-    k_repack_hwio_to_ohwi<<<grid_for(be, items), kThreads, 0, be->stream>>>(w, out, taps, c_in, c_out);
+    k_repack_hwio_to_ohwi<int8_t><<<grid_for(be, items), kThreads, 0, be->stream>>>(w, out, taps, c_in, c_out);
     return dw_after_launch(be, "repack_hwio_to_ohwi");
+}
+
+dw_status launch_repack_hwio_to_ohwi_f16(dw_backend *be, const uint16_t *w, uint16_t *out, int taps, int c_in,
+                                         int c_out) {
+    size_t items = (size_t)taps * c_in * c_out;
+    k_repack_hwio_to_ohwi<uint16_t><<<grid_for(be, items), kThreads, 0, be->stream>>>(w, out, taps, c_in, c_out);
+    return dw_after_launch(be, "repack_hwio_to_ohwi_f16");
 }
 
 dw_status launch_transpose_kn_to_nk(dw_backend *be, const int8_t *b, int8_t *out, int k, int n) {
     dim3 block(32, 8);
     dim3 grid((unsigned)std::min((n + 31) / 32, 1024), (unsigned)std::min((k + 31) / 32, 1024));
-    k_transpose_kn_to_nk<<<grid, block, 0, be->stream>>>(b, out, k, n);
+    k_transpose_kn_to_nk<int8_t><<<grid, block, 0, be->stream>>>(b, out, k, n);
     return dw_after_launch(be, "transpose_kn_to_nk");
+}
+
+dw_status launch_transpose_kn_to_nk_f16(dw_backend *be, const uint16_t *b, uint16_t *out, int k, int n) {
+    dim3 block(32, 8);
+    dim3 grid((unsigned)std::min((n + 31) / 32, 1024), (unsigned)std::min((k + 31) / 32, 1024));
+    k_transpose_kn_to_nk<uint16_t><<<grid, block, 0, be->stream>>>(b, out, k, n);
+    return dw_after_launch(be, "transpose_kn_to_nk_f16");
 }
 
 dw_status launch_expire_wait(dw_backend *be, uint64_t cap_ns) {

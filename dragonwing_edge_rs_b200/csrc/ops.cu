@@ -393,4 +393,265 @@ DW_API dw_status dw_resize_nearest_i8(dw_backend *be, const dw_buf *x, dw_buf *y
                                         (int)h_out, (int)w_out, (int)c);
 }
 
+// ---------------------------------------------------------------------------
+// fp16 path
+// ---------------------------------------------------------------------------
+
+DW_API dw_status dw_prepare_weights_f16(dw_backend *be, const dw_conv_desc *d, const dw_buf *w_hwio, dw_buf **out) {
+    const char *op = "prepare_weights_f16";
+    if (!be) return DW_ERR_INVALID_ARG;
+    DW_TRY(need(be, out, op, "out"));
+    *out = nullptr;
+    DW_TRY(need(be, w_hwio, op, "kernel"));
+    int ho, wo;
+    DW_TRY(check_desc(be, d, &ho, &wo, op));
+    DW_TRY(check_len(be, w_hwio, 2 * weight_len(d), op, "kernel"));
+    cudaSetDevice(be->device);
+    dw_buf *o = nullptr;
+    DW_TRY(dw_alloc(be, w_hwio->len, &o));
+    dw_status st;
+    if (d->group == 1) {
+        st = dw::launch_repack_hwio_to_ohwi_f16(be, (const uint16_t *)w_hwio->ptr, (uint16_t *)o->ptr,
+                                                d->k_h * d->k_w, d->c_in, d->c_out);
+    } else {
+        st = dw_cuda_check(be, cudaMemcpyAsync(o->ptr, w_hwio->ptr, w_hwio->len, cudaMemcpyDeviceToDevice, be->stream),
+                           "prepare depthwise weights");
+    }
+    if (st != DW_OK) {
+        dw_free(be, o);
+        return st;
+    }
+    *out = o;
+    return DW_OK;
+}
+
+static dw_status conv_dispatch_f16(dw_backend *be, const dw_conv_desc *d, int ho, int wo, const dw_buf *x,
+                                   const dw_buf *w_prep, const dw_buf *bias, dw_buf *y, const char *op) {
+    const uint16_t *xp = (const uint16_t *)x->ptr;
+    const uint16_t *wp = (const uint16_t *)w_prep->ptr;
+    const uint16_t *bp = bias ? (const uint16_t *)bias->ptr : nullptr;
+    uint16_t *yp = (uint16_t *)y->ptr;
+    const int relu = d->epilogue == DW_EPI_RELU ? 1 : 0;
+    if (d->group != 1) return dw::launch_dwconv_f16(be, *d, ho, wo, xp, wp, bp, relu, yp);
+    const int path = be->cfg.conv_path;
+    if (path != DW_PATH_DIRECT && dw::umma_supported_f16(be, *d, ho, wo))
+        return dw::launch_umma_conv_f16(be, *d, ho, wo, xp, wp, bp, relu, yp);
+    if (path == DW_PATH_UMMA)
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: shape not supported by the tensor-core kernel (c_in=%d c_out=%d)",
+                       op, d->c_in, d->c_out);
+    return dw::launch_conv_direct_f16(be, *d, ho, wo, xp, wp, bp, relu, yp);
+}
+
+DW_API dw_status dw_conv2d_f16(dw_backend *be, const dw_conv_desc *d, const dw_buf *x, const dw_buf *w_prep,
+                               const dw_buf *bias_or_null, dw_buf *y) {
+    const char *op = "conv2d_f16";
+    if (!be) return DW_ERR_INVALID_ARG;
+    int ho, wo;
+    DW_TRY(check_desc(be, d, &ho, &wo, op));
+    if (d->epilogue != DW_EPI_NONE && d->epilogue != DW_EPI_RELU)
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: epilogue %d unsupported (NONE or RELU)", op, d->epilogue);
+    DW_TRY(need(be, x, op, "input"));
+    DW_TRY(need(be, w_prep, op, "kernel"));
+    DW_TRY(need(be, y, op, "output"));
+    DW_TRY(check_len(be, x, 2 * (size_t)d->n * d->h * d->w * d->c_in, op, "input"));
+    DW_TRY(check_len(be, w_prep, 2 * weight_len(d), op, "kernel"));
+    DW_TRY(check_len(be, y, 2 * (size_t)d->n * ho * wo * d->c_out, op, "output"));
+    if (bias_or_null) DW_TRY(check_len(be, bias_or_null, 2 * (size_t)d->c_out, op, "bias"));
+    cudaSetDevice(be->device);
+    return conv_dispatch_f16(be, d, ho, wo, x, w_prep, bias_or_null, y, op);
+}
+
+DW_API dw_status dw_conv2d_fp16_nhwc(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio, dw_buf *output,
+                                     size_t n, size_t h_in, size_t w_in, size_t c_in, size_t c_out, size_t k_h,
+                                     size_t k_w, size_t stride_h, size_t stride_w, size_t pad_h, size_t pad_w) {
+    const char *op = "conv2d_fp16";
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!input || !kernel_hwio || !output) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: null buffer", op);
+    if (stride_h == 0 || stride_w == 0 || h_in + 2 * pad_h < k_h || w_in + 2 * pad_w < k_w || n == 0 || k_h == 0 ||
+        k_w == 0 || c_in == 0 || c_out == 0)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: invalid geometry", op);
+    // crates/dragonwing-vulkan/src/ops.rs:1401-1416 (same checks, same strings)
+    const size_t h_out = (h_in + 2 * pad_h - k_h) / stride_h + 1;
+    const size_t w_out = (w_in + 2 * pad_w - k_w) / stride_w + 1;
+    const size_t expected_input = n * h_in * w_in * c_in * 2;
+    const size_t expected_kernel = k_h * k_w * c_in * c_out * 2;
+    const size_t expected_output = n * h_out * w_out * c_out * 2;
+    if (input->len != expected_input)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "%s: input size mismatch: expected %zu, got %zu", op, expected_input,
+                       input->len);
+    if (kernel_hwio->len != expected_kernel)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "%s: kernel size mismatch: expected %zu, got %zu", op,
+                       expected_kernel, kernel_hwio->len);
+    if (output->len != expected_output)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "%s: output size mismatch: expected %zu, got %zu", op,
+                       expected_output, output->len);
+    dw_conv_desc d{};
+    d.n = (int32_t)n; d.h = (int32_t)h_in; d.w = (int32_t)w_in; d.c_in = (int32_t)c_in; d.c_out = (int32_t)c_out;
+    d.k_h = (int32_t)k_h; d.k_w = (int32_t)k_w; d.stride_h = (int32_t)stride_h; d.stride_w = (int32_t)stride_w;
+    d.pad_t = d.pad_b = (int32_t)pad_h; d.pad_l = d.pad_r = (int32_t)pad_w;
+    d.group = 1;
+    d.epilogue = DW_EPI_NONE;
+    int ho, wo;
+    DW_TRY(check_desc(be, &d, &ho, &wo, op));
+    cudaSetDevice(be->device);
+    void *scr = nullptr;
+    DW_TRY(dw_scratch(be, expected_kernel, &scr));
+    dw_buf wprep{scr, expected_kernel, false};
+    DW_TRY(dw::launch_repack_hwio_to_ohwi_f16(be, (const uint16_t *)kernel_hwio->ptr, (uint16_t *)scr,
+                                              (int)(k_h * k_w), (int)c_in, (int)c_out));
+    return conv_dispatch_f16(be, &d, ho, wo, input, &wprep, nullptr, output, op);
+}
+
+static dw_status gemm_f16_run(dw_backend *be, const dw_buf *a, const dw_buf *b_nk, const dw_buf *bias, dw_buf *y,
+                              size_t m, size_t n, size_t k, int relu, const char *op) {
+    dw_conv_desc d{};
+    d.n = 1; d.h = 1; d.w = (int32_t)m; d.c_in = (int32_t)k; d.c_out = (int32_t)n;
+    d.k_h = d.k_w = d.stride_h = d.stride_w = 1;
+    d.group = 1;
+    d.epilogue = relu ? DW_EPI_RELU : DW_EPI_NONE;
+    int ho, wo;
+    DW_TRY(check_desc(be, &d, &ho, &wo, op));
+    return conv_dispatch_f16(be, &d, ho, wo, a, b_nk, bias, y, op);
+}
+
+DW_API dw_status dw_gemm_f16(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *c, size_t m, size_t n,
+                             size_t k) {
+    const char *op = "gemm_fp16";
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!a || !b || !c) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: null buffer", op);
+    if (!m || !n || !k) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: zero dimension", op);
+    if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: dimension exceeds int32", op);
+    // crates/dragonwing-vulkan/src/ops.rs:1193-1213 (same checks, same strings)
+    if (a->len != m * k * 2)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "%s: A size mismatch: expected %zu got %zu", op, m * k * 2, a->len);
+    if (b->len != k * n * 2)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "%s: B size mismatch: expected %zu got %zu", op, k * n * 2, b->len);
+    if (c->len != m * n * 2)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "%s: C size mismatch: expected %zu got %zu", op, m * n * 2, c->len);
+    cudaSetDevice(be->device);
+    void *scr = nullptr;
+    DW_TRY(dw_scratch(be, k * n * 2, &scr));
+    DW_TRY(dw::launch_transpose_kn_to_nk_f16(be, (const uint16_t *)b->ptr, (uint16_t *)scr, (int)k, (int)n));
+    dw_buf bprep{scr, k * n * 2, false};
+    return gemm_f16_run(be, a, &bprep, nullptr, c, m, n, k, 0, op);
+}
+
+DW_API dw_status dw_prepare_gemm_b_f16(dw_backend *be, const dw_buf *b_kn, size_t k, size_t n, dw_buf **out) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!b_kn || !out) return dw_fail(be, DW_ERR_INVALID_ARG, "prepare_gemm_b_f16: null argument");
+    *out = nullptr;
+    if (!k || !n) return dw_fail(be, DW_ERR_INVALID_ARG, "prepare_gemm_b_f16: zero dimension");
+    if (k > 0x7fffffff || n > 0x7fffffff)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "prepare_gemm_b_f16: dimension exceeds int32");
+    DW_TRY(check_len(be, b_kn, k * n * 2, "prepare_gemm_b_f16", "B size"));
+    cudaSetDevice(be->device);
+    dw_buf *o = nullptr;
+    DW_TRY(dw_alloc(be, k * n * 2, &o));
+    dw_status st =
+        dw::launch_transpose_kn_to_nk_f16(be, (const uint16_t *)b_kn->ptr, (uint16_t *)o->ptr, (int)k, (int)n);
+    if (st != DW_OK) {
+        dw_free(be, o);
+        return st;
+    }
+    *out = o;
+    return DW_OK;
+}
+
+DW_API dw_status dw_gemm_f16_bias(dw_backend *be, const dw_buf *a, const dw_buf *b_prep, const dw_buf *bias,
+                                  dw_buf *y, size_t m, size_t n, size_t k, int relu) {
+    const char *op = "gemm_f16";
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!a || !b_prep || !y) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: null buffer", op);
+    if (!m || !n || !k) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: zero dimension", op);
+    if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: dimension exceeds int32", op);
+    DW_TRY(check_len(be, a, m * k * 2, op, "A size"));
+    DW_TRY(check_len(be, b_prep, k * n * 2, op, "B size"));
+    DW_TRY(check_len(be, y, m * n * 2, op, "Y size"));
+    if (bias) DW_TRY(check_len(be, bias, n * 2, op, "bias size"));
+    cudaSetDevice(be->device);
+    return gemm_f16_run(be, a, b_prep, bias, y, m, n, k, relu, op);
+}
+
+static dw_status add_f16_common(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *y, int relu,
+                                const char *op) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!a || !b || !y) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: null buffer", op);
+    // crates/dragonwing-vulkan/src/ops.rs:939-947 (same checks, same strings)
+    if (a->len != b->len || a->len != y->len) return dw_fail(be, DW_ERR_SIZE_MISMATCH, "%s: buffer size mismatch", op);
+    if (a->len % 2) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: buffer size must be multiple of 2", op);
+    cudaSetDevice(be->device);
+    return dw::launch_add_f16(be, (const uint16_t *)a->ptr, (const uint16_t *)b->ptr, (uint16_t *)y->ptr, a->len / 2,
+                              relu);
+}
+
+DW_API dw_status dw_add_f16(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *y) {
+    return add_f16_common(be, a, b, y, 0, "add_fp16");
+}
+
+DW_API dw_status dw_add_relu_f16(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *y) {
+    return add_f16_common(be, a, b, y, 1, "add_relu_fp16");
+}
+
+DW_API dw_status dw_relu_f16(dw_backend *be, dw_buf *x) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x) return dw_fail(be, DW_ERR_INVALID_ARG, "relu_fp16: null buffer");
+    // crates/dragonwing-vulkan/src/ops.rs:857-862
+    if (x->len % 2) return dw_fail(be, DW_ERR_INVALID_ARG, "relu_fp16: buffer size must be multiple of 2");
+    cudaSetDevice(be->device);
+    return dw::launch_relu_f16(be, (const uint16_t *)x->ptr, (uint16_t *)x->ptr, x->len / 2);
+}
+
+DW_API dw_status dw_maxpool_f16(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h, size_t w, size_t c,
+                                size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t, size_t p_l, size_t p_b,
+                                size_t p_r) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x || !y) return dw_fail(be, DW_ERR_INVALID_ARG, "maxpool_f16: null buffer");
+    if (!n || !h || !w || !c || !k_h || !k_w || !s_h || !s_w || p_t >= k_h || p_b >= k_h || p_l >= k_w || p_r >= k_w ||
+        h + p_t + p_b < k_h || w + p_l + p_r < k_w)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "maxpool_f16: invalid geometry");
+    size_t ho = (h + p_t + p_b - k_h) / s_h + 1, wo = (w + p_l + p_r - k_w) / s_w + 1;
+    DW_TRY(check_len(be, x, 2 * n * h * w * c, "maxpool_f16", "input"));
+    DW_TRY(check_len(be, y, 2 * n * ho * wo * c, "maxpool_f16", "output"));
+    cudaSetDevice(be->device);
+    return dw::launch_maxpool_f16(be, (const uint16_t *)x->ptr, (uint16_t *)y->ptr, (int)n, (int)h, (int)w, (int)c,
+                                  (int)k_h, (int)k_w, (int)s_h, (int)s_w, (int)p_t, (int)p_l, (int)ho, (int)wo);
+}
+
+DW_API dw_status dw_global_avgpool_f16(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h, size_t w,
+                                       size_t c) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x || !y) return dw_fail(be, DW_ERR_INVALID_ARG, "global_avgpool_f16: null buffer");
+    if (!n || !h || !w || !c || h * w > 0x7fffffff)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "global_avgpool_f16: invalid geometry");
+    DW_TRY(check_len(be, x, 2 * n * h * w * c, "global_avgpool_f16", "input"));
+    DW_TRY(check_len(be, y, 2 * n * c, "global_avgpool_f16", "output"));
+    cudaSetDevice(be->device);
+    return dw::launch_gap_f16(be, (const uint16_t *)x->ptr, (uint16_t *)y->ptr, (int)n, (int)h, (int)w, (int)c);
+}
+
+DW_API dw_status dw_cast_f32_to_f16(dw_backend *be, const dw_buf *x_f32, dw_buf *y_f16, size_t pixels, size_t c_src,
+                                    size_t c_dst) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x_f32 || !y_f16) return dw_fail(be, DW_ERR_INVALID_ARG, "cast_f32_to_f16: null buffer");
+    if (!c_src || c_dst < c_src || c_dst > 0x7fffffff)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "cast_f32_to_f16: need 0 < c_src <= c_dst");
+    DW_TRY(check_len(be, x_f32, 4 * pixels * c_src, "cast_f32_to_f16", "input"));
+    DW_TRY(check_len(be, y_f16, 2 * pixels * c_dst, "cast_f32_to_f16", "output"));
+    cudaSetDevice(be->device);
+    return dw::launch_cast_f32_to_f16(be, (const float *)x_f32->ptr, (uint16_t *)y_f16->ptr, pixels, (int)c_src,
+                                      (int)c_dst);
+}
+
+DW_API dw_status dw_cast_f16_to_f32(dw_backend *be, const dw_buf *x_f16, dw_buf *y_f32) {
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x_f16 || !y_f32) return dw_fail(be, DW_ERR_INVALID_ARG, "cast_f16_to_f32: null buffer");
+    if (x_f16->len % 2 || y_f32->len != 2 * x_f16->len)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "cast_f16_to_f32: length mismatch (%zu f16 bytes vs %zu f32 bytes)",
+                       x_f16->len, y_f32->len);
+    cudaSetDevice(be->device);
+    return dw::launch_cast_f16_to_f32(be, (const uint16_t *)x_f16->ptr, (float *)y_f32->ptr, x_f16->len / 2);
+}
+
 }  // extern "C"

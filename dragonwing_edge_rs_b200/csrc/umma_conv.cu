@@ -62,6 +62,10 @@ struct UmmaParams {
     long long acc_bound;                    // |acc| <= taps * c_in * 128 * 128
     int R;                                  // 128-row blocks per tile (R * bn <= 256)
     int chan_all;                           // 1: every output channel's parameters staged once per CTA
+    int esize;                              // element bytes: 1 (int8) or 2 (fp16)
+    int bk_elems;                           // bk / esize: K elements per stage
+    const uint16_t *bias_f16;               // fp16 path: bias [c_out] (may be null)
+    int relu;                               // fp16 path: ReLU after the bias
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
@@ -167,6 +171,26 @@ __device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint6
         : "memory");
 }
 
+// kind::f16: A = B = fp16 (instruction descriptor formats 0), D = f32 in TMEM.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+template <bool kF16>
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    if (kF16)
+        tc_mma_f16(d_tmem, adesc, bdesc, idesc, accumulate);
+    else
+        tc_mma_i8(d_tmem, adesc, bdesc, idesc, accumulate);
+}
+
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -227,6 +251,13 @@ __device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred
 __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs, int slot, int oc, bool write) {
     int32_t bias = 0;
     float m = 0.0f, dsc = 0.0f;
+    if (p.esize == 2) {  // fp16 path: the slot's `m` holds the f16 bias as a float
+        if (write) {
+            cs->m[slot] = (oc < p.c_out && p.bias_f16) ? f16_to_f32_ref(p.bias_f16[oc]) : 0.0f;
+            if ((slot & 15) == 0) cs->cflags[slot >> 4] = 0;
+        }
+        return;
+    }
     if (write && oc < p.c_out) {
         bias = p.ep.bias ? __ldg(p.ep.bias + oc) : 0;
         m = p.ep.M ? __ldg(p.ep.M + oc) : 0.0f;
@@ -373,6 +404,34 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// fp16 epilogue for 16 f32 accumulators (16 consecutive channels of one row),
+// in the order the reference's CPU runtime applies it: the conv result stored
+// as f16 (F16::from_f32, round to nearest even), then the f16 bias added in f32
+// and rounded to f16 again (crates/dragonwing-onnx/src/runtime.rs:1483-1497),
+// then ReLU as relu_fp16 (x > 0 ? x : 0, crates/dragonwing-cpu/src/ops.rs:345-352).
+// Writes 32 bytes (16 halves) to dst.
+__device__ __forceinline__ void f16_epilogue16(const int32_t (&v)[16], const ChanSmem *cs, int slot0,
+                                               const UmmaParams &p, uint8_t *dst) {
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 16; k += 2) {
+        uint16_t h[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            uint16_t x = f32_to_f16_ref(__int_as_float(v[k + j]));
+            if (p.bias_f16) x = f32_to_f16_ref(__fadd_rn(f16_to_f32_ref(x), cs->m[slot0 + k + j]));
+            if (p.relu) {
+                const float f = f16_to_f32_ref(x);
+                x = f32_to_f16_ref(f > 0.0f ? f : 0.0f);
+            }
+            h[j] = x;
+        }
+        w[k / 2] = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+    }
+    reinterpret_cast<uint4 *>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<uint4 *>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 // Shared-memory matrix descriptor (K-major, swizzled): start address >> 4 in
 // bits [0,14); leading-byte offset (unused for swizzled K-major) = 1; the
 // constant high word (stride-byte offset = 8 rows * row bytes, version 1,
@@ -418,7 +477,7 @@ __device__ __forceinline__ int valid_blocks(const UmmaParams &p, const TileCoord
     return left < p.R ? left : p.R;
 }
 
-template <bool kSilu>
+template <bool kSilu, bool kF16>
 __global__ void __launch_bounds__(kThreads, 1)
     k_umma_conv_i8(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ UmmaParams p) {
@@ -489,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t b_dst = smem_u32(b_smem + (size_t)s * p.b_stage_bytes);
                     if (p.mode == 0) {
                         for (int r = 0; r < nrb; r++)
-                            tma_load_2d(a_dst + (uint32_t)(r * kBM * p.bk), &tmap_a, fb, cb * p.bk,
+                            tma_load_2d(a_dst + (uint32_t)(r * kBM * p.bk), &tmap_a, fb, cb * p.bk_elems,
                                         (tc.mt * p.R + r) * kBM);
                     } else {
                         const int kh = tap / p.kw, kw = tap % p.kw;
@@ -497,10 +556,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int par_h = ((dh % p.sh) + p.sh) % p.sh, par_w = ((dwc % p.sw) + p.sw) % p.sw;
                         const int hq = (dh - par_h) / p.sh, wq = (dwc - par_w) / p.sw;
                         for (int r = 0; r < nrb; r++)
-                            tma_load_5d(a_dst + (uint32_t)(r * kBM * p.bk), &tmap_a, fb, par_w * p.c_in + cb * p.bk,
+                            tma_load_5d(a_dst + (uint32_t)(r * kBM * p.bk), &tmap_a, fb, par_w * p.c_in + cb * p.bk_elems,
                                         tc.ow0 + wq, par_h, tc.oh0 + r * p.th + hq, tc.img);
                     }
-                    tma_load_3d(b_dst, &tmap_b, fb, cb * p.bk, tap, tc.n0);
+                    tma_load_3d(b_dst, &tmap_b, fb, cb * p.bk_elems, tap, tc.n0);
                     issued_mask |= 1u << s;
                     last_parity = (last_parity & ~(1u << s)) | (ph << s);
                     if (++s == p.stages) { s = 0; ph ^= 1; }
@@ -539,14 +598,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int k = 0; k < p.bk / 32; k++) {
                             const uint64_t ad = smem_desc(a_addr + 32 * k, p.desc_hi);
                             const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
-                            tc_mma_i8(d_tmem, ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
+                            tc_mma<kF16>(d_tmem, ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
                         }
                     } else
                     for (int k = 0; k < p.bk / 32; k++) {
                         const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
                         for (int r = 0; r < p.R; r++) {
                             const uint64_t ad = smem_desc(a_addr + (uint32_t)(r * kBM * p.bk) + 32 * k, p.desc_hi);
-                            tc_mma_i8(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
+                            tc_mma<kF16>(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
                         }
                     }
                     tc_commit(smem_u32(&empty_bar[s]));  // frees the stage when these MMAs finish
@@ -614,8 +673,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int32_t v[16];
                     tc_ld16(tacc + (uint32_t)(c * 16), v);
                     tc_wait_ld();
-                    const uint4 q = requant16<kSilu>(v, chan, slot_base + c * 16, p);
-                    *reinterpret_cast<uint4 *>(out_stage + (size_t)row * p.bn + c * 16) = q;
+                    uint8_t *dst = out_stage + ((size_t)row * p.bn + c * 16) * (kF16 ? 2 : 1);
+                    if (kF16)
+                        f16_epilogue16(v, chan, slot_base + c * 16, p, dst);
+                    else
+                        *reinterpret_cast<uint4 *>(dst) = requant16<kSilu>(v, chan, slot_base + c * 16, p);
                 }
             } else {
             const int per = (items + 1) / 2;
@@ -631,11 +693,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_ld16(tacc + (uint32_t)(r1 * p.bn + c1 * 16), v1);
                 tc_ld16(tacc + (uint32_t)(r2 * p.bn + c2 * 16), v2);
                 tc_wait_ld();
-                const uint4 q1 = requant16<kSilu>(v1, chan, slot_base + c1 * 16, p);
-                *reinterpret_cast<uint4 *>(out_stage + ((size_t)(r1 * kBM + row)) * p.bn + c1 * 16) = q1;
+                uint8_t *dst1 = out_stage + (((size_t)(r1 * kBM + row)) * p.bn + c1 * 16) * (kF16 ? 2 : 1);
+                if (kF16)
+                    f16_epilogue16(v1, chan, slot_base + c1 * 16, p, dst1);
+                else
+                    *reinterpret_cast<uint4 *>(dst1) = requant16<kSilu>(v1, chan, slot_base + c1 * 16, p);
                 if (two) {
-                    const uint4 q2 = requant16<kSilu>(v2, chan, slot_base + c2 * 16, p);
-                    *reinterpret_cast<uint4 *>(out_stage + ((size_t)(r2 * kBM + row)) * p.bn + c2 * 16) = q2;
+                    uint8_t *dst2 = out_stage + (((size_t)(r2 * kBM + row)) * p.bn + c2 * 16) * (kF16 ? 2 : 1);
+                    if (kF16)
+                        f16_epilogue16(v2, chan, slot_base + c2 * 16, p, dst2);
+                    else
+                        *reinterpret_cast<uint4 *>(dst2) = requant16<kSilu>(v2, chan, slot_base + c2 * 16, p);
                 }
                 c1 += 2;
                 while (c1 >= chunks) { c1 -= chunks; r1++; }
@@ -649,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (et == 0) {
                 const int nrb = valid_blocks(p, tc);
                 for (int r = 0; r < nrb; r++) {
-                    const uint32_t src = smem_u32(out_stage + (size_t)r * kBM * p.bn);
+                    const uint32_t src = smem_u32(out_stage + (size_t)r * kBM * p.bn * (kF16 ? 2 : 1));
                     if (p.mode == 0)
                         tma_store_2d(&tmap_y, src, tc.n0, (tc.mt * p.R + r) * kBM);
                     else
@@ -732,24 +800,52 @@ bool umma_supported(const dw_backend *be, const dw_conv_desc &d, int ho, int wo)
     return true;
 }
 
-dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
-                              const int8_t *w_ohwi, const EpiParams &ep, int8_t *y) {
+bool umma_supported_f16(const dw_backend *be, const dw_conv_desc &d, int ho, int wo) {
+    if (!be->encode_tiled) return false;
+    // 16-byte TMA strides: c_in, c_out multiples of 8 halves
+    if (d.group != 1 || d.c_in % 8 || d.c_out % 8) return false;
+    const bool flat = d.k_h == 1 && d.k_w == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_t == 0 &&
+                      d.pad_l == 0 && d.pad_b == 0 && d.pad_r == 0;
+    if (!flat && (d.h % d.stride_h || d.w % d.stride_w)) return false;
+    // With stride_w > 1 the activation view's innermost dimension holds the
+    // stride_w column phases side by side; a K block wider than the channels
+    // left would read the next phase's values.  Their weights are zero, but
+    // 0 * inf is NaN in floating point, so K blocks must divide c_in (32-byte
+    // blocks divide c_in when c_in % 16 == 0).
+    if (!flat && d.stride_w > 1 && d.c_in % 16) return false;
+    if ((long long)d.n * ho * wo >= (1ll << 31)) return false;
+    if ((long long)d.k_h * d.k_w >= (1 << 16) || d.k_h * d.k_w * (long long)d.c_in >= (1ll << 31)) return false;
+    return true;
+}
+
+namespace {
+
+// Shared launcher: esize 1 = int8 (kind::i8, requant epilogue), 2 = fp16
+// (kind::f16, f16 epilogue with bias and ReLU).
+dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const void *x, const void *w_ohwi,
+                           const EpiParams &ep, void *y, int esize, const uint16_t *bias_f16, int relu) {
+    const char *op = esize == 2 ? "conv2d_f16" : "conv2d_i8";
     if (((uintptr_t)x & 15) || ((uintptr_t)w_ohwi & 15) || ((uintptr_t)y & 15))
-        return dw_fail(be, DW_ERR_INVALID_ARG, "conv2d_i8 (tensor-core path): buffers must be 16-byte aligned");
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s (tensor-core path): buffers must be 16-byte aligned", op);
     UmmaParams p{};
     const bool flat = d.k_h == 1 && d.k_w == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_t == 0 &&
                       d.pad_l == 0 && d.pad_b == 0 && d.pad_r == 0;
     p.mode = flat ? 0 : 1;
+    p.esize = esize;
+    p.bias_f16 = bias_f16;
+    p.relu = relu;
     p.n_img = d.n; p.ho = ho; p.wo = wo; p.c_out = d.c_out;
     p.taps = d.k_h * d.k_w; p.kw = d.k_w; p.sh = d.stride_h; p.sw = d.stride_w; p.pt = d.pad_t; p.pl = d.pad_l;
     p.c_in = d.c_in;
-    p.bk = pick_bk(d.c_in);
+    p.bk = pick_bk(d.c_in * esize);
     if (const char *e = getenv("DW_UMMA_BK")) {  // tuning override: 32, 64 or 128 bytes of K per stage
         const int v = atoi(e);
         if (v == 32 || v == 64 || v == 128) p.bk = v;
     }
-    p.bn = pick_bn(d.c_out);
-    p.cblocks = (d.c_in + p.bk - 1) / p.bk;
+    if (esize == 2 && !flat && d.stride_w > 1 && (d.c_in * esize) % p.bk) p.bk = pick_bk(d.c_in * esize);
+    p.bk_elems = p.bk / esize;
+    p.bn = pick_bn(((d.c_out + 15) / 16) * 16);
+    p.cblocks = (d.c_in + p.bk_elems - 1) / p.bk_elems;
     p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
     // Row blocks per tile: R * bn <= 256 (two TMEM accumulator buffers within 512
     // columns), at most 8, and an A stage (R * 128 rows * bk) of at most 32 KiB.
@@ -776,7 +872,7 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
     p.b_tx_bytes = (uint32_t)(p.bn * p.bk);
     p.a_stage_bytes = (uint32_t)al1k((size_t)p.R * kBM * p.bk);
     p.b_stage_bytes = (uint32_t)al1k((size_t)p.bn * p.bk);
-    const size_t out_bytes = al1k((size_t)p.R * kBM * p.bn);
+    const size_t out_bytes = al1k((size_t)p.R * kBM * p.bn * esize);
     const size_t chan_bytes = al1k(sizeof(ChanSmem));
     const size_t fixed = 1024 /*align slack*/ + out_bytes + chan_bytes + 256 /*barriers*/;
     int stages = (int)((kSmemLimit - fixed) / (p.a_stage_bytes + p.b_stage_bytes));
@@ -788,10 +884,12 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
     // At least 116 KiB so that a second CTA never fits on the SM: one CTA per SM
     // owns the tensor memory (its tcgen05.alloc never waits on a neighbour).
     const size_t smem = std::max<size_t>(1024 + p.off_bars + 256, 116 * 1024);
-    if (smem > kSmemLimit) return dw_fail(be, DW_ERR_UNSUPPORTED, "conv2d_i8: tile does not fit in shared memory");
-    // tcgen05 instruction descriptor, kind::i8: D = s32 (bits 4-5 = 2), A = B = s8
-    // (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
-    p.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+    if (smem > kSmemLimit) return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: tile does not fit in shared memory", op);
+    // tcgen05 instruction descriptor: kind::i8: D = s32 (bits 4-5 = 2), A = B = s8
+    // (bits 7-9, 10-12 = 1); kind::f16: D = f32 (bits 4-5 = 1), A = B = f16 (0).
+    // Both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+    const uint32_t fmt = esize == 2 ? ((1u << 4)) : ((2u << 4) | (1u << 7) | (1u << 10));
+    p.idesc = fmt | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
     // descriptor high word: SBO = 8 rows * bk bytes (>> 4) at bits 32-45, version 1 at bit 46,
     // swizzle layout at bits 61-63.
     p.desc_hi = ((uint64_t)((8 * p.bk) >> 4) << 32) | (1ull << 46) | ((uint64_t)swizzle_layout(p.bk) << 61);
@@ -802,75 +900,92 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
     p.err = be->dev_err;
     p.ep = ep;
 
-    // ---- tensor maps
+    // ---- tensor maps (dims in elements, strides in bytes)
+    const CUtensorMapDataType dt = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    const cuuint64_t es = (cuuint64_t)esize;
     CUtensorMap ta, tb;
     CUresult r;
     const CUtensorMapSwizzle sw = swizzle_enum(p.bk);
     if (flat) {
         cuuint64_t dims[2] = {(cuuint64_t)d.c_in, (cuuint64_t)p.rows};
-        cuuint64_t strides[1] = {(cuuint64_t)d.c_in};
-        cuuint32_t box[2] = {(cuuint32_t)p.bk, (cuuint32_t)kBM};
+        cuuint64_t strides[1] = {(cuuint64_t)d.c_in * es};
+        cuuint32_t box[2] = {(cuuint32_t)p.bk_elems, (cuuint32_t)kBM};
         cuuint32_t estr[2] = {1, 1};
-        r = be->encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)x, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        r = be->encode_tiled(&ta, dt, 2, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
         const int sh = d.stride_h, swd = d.stride_w;
         cuuint64_t dims[5] = {(cuuint64_t)swd * d.c_in, (cuuint64_t)(d.w / swd), (cuuint64_t)sh, (cuuint64_t)(d.h / sh),
                               (cuuint64_t)d.n};
-        cuuint64_t strides[4] = {(cuuint64_t)swd * d.c_in, (cuuint64_t)d.w * d.c_in, (cuuint64_t)sh * d.w * d.c_in,
-                                 (cuuint64_t)d.h * d.w * d.c_in};
-        cuuint32_t box[5] = {(cuuint32_t)p.bk, (cuuint32_t)p.tw, 1, (cuuint32_t)p.th, 1};
+        cuuint64_t strides[4] = {(cuuint64_t)swd * d.c_in * es, (cuuint64_t)d.w * d.c_in * es,
+                                 (cuuint64_t)sh * d.w * d.c_in * es, (cuuint64_t)d.h * d.w * d.c_in * es};
+        cuuint32_t box[5] = {(cuuint32_t)p.bk_elems, (cuuint32_t)p.tw, 1, (cuuint32_t)p.th, 1};
         cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-        r = be->encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, (void *)x, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        r = be->encode_tiled(&ta, dt, 5, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
-    if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "conv2d_i8: activation tensor map rejected (%d)", (int)r);
+    if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: activation tensor map rejected (%d)", op, (int)r);
     {
         cuuint64_t dims[3] = {(cuuint64_t)d.c_in, (cuuint64_t)p.taps, (cuuint64_t)d.c_out};
-        cuuint64_t strides[2] = {(cuuint64_t)d.c_in, (cuuint64_t)p.taps * d.c_in};
-        cuuint32_t box[3] = {(cuuint32_t)p.bk, 1, (cuuint32_t)p.bn};
+        cuuint64_t strides[2] = {(cuuint64_t)d.c_in * es, (cuuint64_t)p.taps * d.c_in * es};
+        cuuint32_t box[3] = {(cuuint32_t)p.bk_elems, 1, (cuuint32_t)p.bn};
         cuuint32_t estr[3] = {1, 1, 1};
-        r = be->encode_tiled(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void *)w_ohwi, dims, strides, box, estr,
+        r = be->encode_tiled(&tb, dt, 3, const_cast<void *>(w_ohwi), dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
-    if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "conv2d_i8: weight tensor map rejected (%d)", (int)r);
-    // Output: TMA stores of the staged [rows][bn] tile; out-of-range rows/pixels are clipped.
+    if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: weight tensor map rejected (%d)", op, (int)r);
+    // Output: TMA stores of the staged [rows][bn] tile; out-of-range rows/pixels/channels are clipped.
     CUtensorMap ty;
     if (flat) {
         cuuint64_t dims[2] = {(cuuint64_t)d.c_out, (cuuint64_t)p.rows};
-        cuuint64_t strides[1] = {(cuuint64_t)d.c_out};
+        cuuint64_t strides[1] = {(cuuint64_t)d.c_out * es};
         cuuint32_t box[2] = {(cuuint32_t)p.bn, (cuuint32_t)kBM};
         cuuint32_t estr[2] = {1, 1};
-        r = be->encode_tiled(&ty, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)y, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        r = be->encode_tiled(&ty, dt, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
         cuuint64_t dims[4] = {(cuuint64_t)d.c_out, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)d.n};
-        cuuint64_t strides[3] = {(cuuint64_t)d.c_out, (cuuint64_t)wo * d.c_out, (cuuint64_t)ho * wo * d.c_out};
+        cuuint64_t strides[3] = {(cuuint64_t)d.c_out * es, (cuuint64_t)wo * d.c_out * es,
+                                 (cuuint64_t)ho * wo * d.c_out * es};
         cuuint32_t box[4] = {(cuuint32_t)p.bn, (cuuint32_t)p.tw, (cuuint32_t)p.th, 1};
         cuuint32_t estr[4] = {1, 1, 1, 1};
-        r = be->encode_tiled(&ty, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void *)y, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        r = be->encode_tiled(&ty, dt, 4, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
-    if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "conv2d_i8: output tensor map rejected (%d)", (int)r);
+    if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: output tensor map rejected (%d)", op, (int)r);
 
     static bool attr_set[16] = {};
     int dev = be->device;
     if (dev < 16 && !attr_set[dev]) {
-        cudaFuncSetAttribute(k_umma_conv_i8<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
-        cudaFuncSetAttribute(k_umma_conv_i8<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
         attr_set[dev] = true;
     }
     const int grid = std::min(p.num_tiles, be->sm_count);
-    if (ep.epilogue == DW_EPI_SILU)
-        k_umma_conv_i8<true><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
+    if (esize == 2)
+        k_umma_conv_i8<false, true><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
+    else if (ep.epilogue == DW_EPI_SILU)
+        k_umma_conv_i8<true, false><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
     else
-        k_umma_conv_i8<false><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
-    return dw_after_launch(be, "umma_conv_i8");
+        k_umma_conv_i8<false, false><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
+    return dw_after_launch(be, esize == 2 ? "umma_conv_f16" : "umma_conv_i8");
+}
+
+}  // namespace
+
+dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
+                              const int8_t *w_ohwi, const EpiParams &ep, int8_t *y) {
+    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 1, nullptr, 0);
+}
+
+dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,
+                               const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y) {
+    EpiParams ep{nullptr, nullptr, nullptr, DW_EPI_NONE, 127, 0.0f};
+    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 2, bias, relu);
 }
 
 }  // namespace dw

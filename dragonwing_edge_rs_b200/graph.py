@@ -1,4 +1,4 @@
-"""Graph IR and CUDA graph runtime for fused-INT8 networks.
+"""Graph IR and CUDA graph runtime for fused-INT8 and fp16 networks.
 
 The IR mirrors the reference's compiled op list: ``CompiledOp`` with
 ``op_type`` / ``inputs`` / ``outputs`` / ``params``
@@ -27,7 +27,7 @@ from . import quantization as Q
 from .backend import BackendError, CudaBackend, CudaBuffer
 from .ops import ConvDesc
 
-_NP = {"i8": np.int8, "u8": np.uint8, "f32": np.float32, "i32": np.int32}
+_NP = {"i8": np.int8, "u8": np.uint8, "f32": np.float32, "i32": np.int32, "f16": np.float16}
 
 
 @dataclass
@@ -67,15 +67,19 @@ class Graph:
         self.tensors[name] = TensorInfo(name, tuple(int(s) for s in shape), dtype, scale)
         return name
 
-    # ---- work accounting (algorithmic ops = 2*MACs, padding taps included) ----
+    # ---- work accounting (algorithmic ops = 2*MACs, padding taps included;
+    # a conv whose input channels were zero-padded counts its real channels) ----
     def conv_ops(self):
         total = 0
         for op in self.ops:
-            if op.op_type == "Conv2dRequantReluI8Nhwc":
+            if op.op_type in ("Conv2dRequantReluI8Nhwc", "Conv2dF16"):
                 d: ConvDesc = op.params["desc"]
                 ho, wo = d.out_hw()
-                per = d.k_h * d.k_w * (d.c_in if d.group == 1 else 1)
+                c_in = op.params.get("c_in_real", d.c_in)
+                per = d.k_h * d.k_w * (c_in if d.group == 1 else 1)
                 total += 2 * d.n * ho * wo * d.c_out * per
+            elif op.op_type == "GemmF16":
+                total += 2 * op.params["m"] * op.params["n"] * op.params["k"]
         return total
 
 
@@ -205,9 +209,139 @@ class GraphBuilder:
         self.g.outputs.append(name)
 
 
+class F16GraphBuilder:
+    """Builds an fp16 graph (the reference's F16 CPU-runtime path) with seeded
+    random weights: He-normal conv weights with BN folded into them and into
+    an f16 bias, as the reference's loader folds BN (crates/dragonwing-onnx/src/
+    graph.rs:597-613).  Weights are generated in f32 and stored as f16 with
+    round-to-nearest-even (F16::from_f32); tensors are NHWC."""
+
+    def __init__(self, seed: int):
+        self.rng = np.random.default_rng(seed)
+        self.g = Graph({}, [], {}, [], [])
+        self._n = 0
+
+    def _name(self, base):
+        self._n += 1
+        return f"{base}_{self._n}"
+
+    @staticmethod
+    def _f16(a):
+        return np.asarray(a, np.float32).astype(np.float16)
+
+    def input_f32(self, name, shape, pad_channels_to=None):
+        """f32 NHWC graph input and its F16 conversion (runtime.rs:842-851).
+        With `pad_channels_to`, the f16 tensor carries extra zero channels so a
+        3-channel image meets the tensor-core kernel's channel alignment."""
+        g = self.g
+        g.add_tensor(name, shape, "f32")
+        g.inputs.append(name)
+        n, h, w, c = shape
+        c_dst = pad_channels_to or c
+        y = g.add_tensor(name + "_f16", (n, h, w, c_dst), "f16")
+        g.ops.append(CompiledOp("cast_input", "CastF32ToF16", [name], [y], {"c_src": c, "c_dst": c_dst}))
+        return y
+
+    def conv(self, x, c_out, k=3, s=1, pad=None, relu=True, gamma=1.0, c_in_real=None, name=None):
+        g = self.g
+        n, h, w, c_in = g.tensors[x].shape
+        c_real = c_in_real or c_in
+        p = k // 2 if pad is None else pad
+        name = name or self._name("conv")
+        wf = self.rng.normal(0.0, np.sqrt(2.0 / (k * k * c_real)), (k, k, c_real, c_out)).astype(np.float32)
+        wf *= np.float32(gamma)
+        if c_real < c_in:  # zero weights for the padded input channels
+            wf = np.concatenate([wf, np.zeros((k, k, c_in - c_real, c_out), np.float32)], axis=2)
+        bias = self.rng.normal(0.0, 0.05, c_out).astype(np.float32)
+        desc = ConvDesc(n, h, w, c_in, c_out, k, k, s, s, (p, p, p, p), 1, L.EPI_RELU if relu else L.EPI_NONE)
+        ho, wo = desc.out_hw()
+        y = g.add_tensor(name + "_out", (n, ho, wo, c_out), "f16")
+        g.initializers[name + "_w"] = self._f16(wf)
+        g.initializers[name + "_b"] = self._f16(bias)
+        params = {"desc": desc}
+        if c_real < c_in:
+            params["c_in_real"] = c_real
+        g.ops.append(CompiledOp(name, "Conv2dF16", [x, name + "_w", name + "_b"], [y], params))
+        return y
+
+    def add_relu(self, a, b, name=None):
+        g = self.g
+        assert g.tensors[a].shape == g.tensors[b].shape
+        name = name or self._name("add")
+        y = g.add_tensor(name + "_out", g.tensors[a].shape, "f16")
+        g.ops.append(CompiledOp(name, "AddF16", [a, b], [y], {"relu": True}))
+        return y
+
+    def maxpool(self, x, k, s, pad, name=None):
+        g = self.g
+        n, h, w, c = g.tensors[x].shape
+        name = name or self._name("maxpool")
+        ho, wo = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+        y = g.add_tensor(name + "_out", (n, ho, wo, c), "f16")
+        g.ops.append(CompiledOp(name, "MaxPoolF16", [x], [y], {"k": k, "s": s, "pad": pad}))
+        return y
+
+    def global_avgpool(self, x, name=None):
+        g = self.g
+        n, h, w, c = g.tensors[x].shape
+        name = name or self._name("gap")
+        y = g.add_tensor(name + "_out", (n, c), "f16")
+        g.ops.append(CompiledOp(name, "GlobalAveragePoolF16", [x], [y], {}))
+        return y
+
+    def fc(self, x, n_out, name=None):
+        """Gemm F16 with bias (runtime.rs:1247-1275): [m, k] @ [k, n_out] + bias."""
+        g = self.g
+        m, k = g.tensors[x].shape
+        name = name or self._name("fc")
+        wf = self.rng.normal(0.0, np.sqrt(1.0 / k), (k, n_out)).astype(np.float32)
+        bias = self.rng.normal(0.0, 0.05, n_out).astype(np.float32)
+        y = g.add_tensor(name + "_out", (m, n_out), "f16")
+        g.initializers[name + "_w"] = self._f16(wf)
+        g.initializers[name + "_b"] = self._f16(bias)
+        g.ops.append(CompiledOp(name, "GemmF16", [x, name + "_w", name + "_b"], [y], {"m": m, "n": n_out, "k": k}))
+        return y
+
+    def output_f32(self, x, name):
+        g = self.g
+        y = g.add_tensor(name, g.tensors[x].shape, "f32")
+        g.ops.append(CompiledOp("cast_" + name, "CastF16ToF32", [x], [y], {}))
+        g.outputs.append(y)
+        return y
+
+
 # ---------------------------------------------------------------------------
 # network builders (synthetic weights with the published architectures' shapes)
 # ---------------------------------------------------------------------------
+
+def resnet50_fp16(batch=128, size=224, classes=1000, seed=50, stages=(3, 4, 6, 3)):
+    """ResNet-50-architecture fp16 graph: 7x7/2 stem + 3x3/2 max pool, bottleneck
+    stages [3, 4, 6, 3] at output widths 256/512/1024/2048 (stride 2 in the 3x3
+    conv of each stage's first block, 1x1 projection shortcut there), BN folded
+    into every conv, ReLU, global average pool, FC to `classes`.  Input f32 NHWC
+    (3 channels, zero-padded to 16 in its f16 copy); output f32 logits.  The
+    last conv of each residual branch carries a folded-BN scale of 0.5 so the
+    residual stream of random weights stays well inside the f16 range."""
+    b = F16GraphBuilder(seed)
+    x = b.input_f32("image", (batch, size, size, 3), pad_channels_to=16)
+    x = b.conv(x, 64, k=7, s=2, c_in_real=3, name="stem")
+    x = b.maxpool(x, 3, 2, 1, name="stem_pool")
+    c = 64
+    for si, (nb, width) in enumerate(zip(stages, (64, 128, 256, 512))):
+        for bi in range(nb):
+            s = 2 if (bi == 0 and si > 0) else 1
+            pre = f"s{si + 1}b{bi + 1}"
+            y = b.conv(x, width, k=1, name=pre + "_a")
+            y = b.conv(y, width, k=3, s=s, name=pre + "_b")
+            y = b.conv(y, 4 * width, k=1, relu=False, gamma=0.5, name=pre + "_c")
+            sc = b.conv(x, 4 * width, k=1, s=s, relu=False, name=pre + "_proj") if bi == 0 else x
+            x = b.add_relu(y, sc, name=pre + "_add")
+            c = 4 * width
+    x = b.global_avgpool(x, name="gap")
+    x = b.fc(x, classes, name="fc")
+    b.output_f32(x, "logits")
+    return b.g
+
 
 def mobilenetv2_block(batch=32, h=112, w=112, c=96, expand=6, seed=2):
     """MobileNetV2 inverted-residual block: 1x1 expand + ReLU6, depthwise 3x3 s1
@@ -374,6 +508,43 @@ class CudaGraphRuntime:
             x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
             s = op.params["scale"]
             return lambda: ops.dequantize_i8_packed_to_f32(be, x, y, s)
+        # ---- fp16 path
+        if t == "CastF32ToF16":
+            x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
+            n, h, w, _ = self.graph.tensors[op.inputs[0]].shape
+            cs, cd = op.params["c_src"], op.params["c_dst"]
+            return lambda: ops.cast_f32_to_f16(be, x, y, n * h * w, cs, cd)
+        if t == "Conv2dF16":
+            desc = op.params["desc"]
+            x, wn, bn = op.inputs
+            wp = ops.prepare_weights_f16(be, desc, consts[wn])
+            consts[wn + "_prep"] = wp
+            bx, bb, y = bufs[x], consts[bn], bufs[op.outputs[0]]
+            return lambda: ops.conv2d_f16(be, desc, bx, wp, bb, y)
+        if t == "AddF16":
+            a, b_ = bufs[op.inputs[0]], bufs[op.inputs[1]]
+            y = bufs[op.outputs[0]]
+            fn = ops.add_relu_fp16 if op.params.get("relu") else ops.add_fp16
+            return lambda: fn(be, a, b_, y)
+        if t == "MaxPoolF16":
+            n, h, w, c = self.graph.tensors[op.inputs[0]].shape
+            k, s, p = op.params["k"], op.params["s"], op.params["pad"]
+            x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
+            return lambda: ops.maxpool_f16(be, x, y, n, h, w, c, k, k, s, s, (p, p, p, p))
+        if t == "GlobalAveragePoolF16":
+            n, h, w, c = self.graph.tensors[op.inputs[0]].shape
+            x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
+            return lambda: ops.global_avgpool_f16(be, x, y, n, h, w, c)
+        if t == "GemmF16":
+            m, n, k = op.params["m"], op.params["n"], op.params["k"]
+            x, wn, bn = op.inputs
+            wp = ops.prepare_gemm_b_f16(be, consts[wn], k, n)
+            consts[wn + "_prep"] = wp
+            bx, bb, y = bufs[x], consts[bn], bufs[op.outputs[0]]
+            return lambda: ops.gemm_f16_bias(be, bx, wp, bb, y, m, n, k)
+        if t == "CastF16ToF32":
+            x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
+            return lambda: ops.cast_f16_to_f32(be, x, y)
         raise BackendError(L.DW_ERR_UNSUPPORTED, f"unsupported op type {t} ({op.name})")
 
     # -- reference-style API ----------------------------------------------------

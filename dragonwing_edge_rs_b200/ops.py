@@ -166,3 +166,82 @@ def slice_c_i8(backend, x, y, pixels, c_total, c0, c_len):
 
 def resize_nearest_i8(backend, x, y, n, h_in, w_in, h_out, w_out, c):
     backend._check(L.load().dw_resize_nearest_i8(backend.handle, x.handle, y.handle, n, h_in, w_in, h_out, w_out, c))
+
+
+# ---------------------------------------------------------------------------
+# fp16 path (binary16 buffers; conversions as F16::from_f32 / F16::to_f32,
+# crates/dragonwing-core/src/dtype.rs:164-263)
+# ---------------------------------------------------------------------------
+
+def conv2d_fp16_nhwc(backend, input, kernel, output, n, h_in, w_in, c_in, c_out, k_h, k_w, stride_h, stride_w,
+                     pad_h, pad_w):
+    """crates/dragonwing-vulkan/src/ops.rs:1385: fp16 conv, f32 accumulation, HWIO kernel."""
+    backend._check(L.load().dw_conv2d_fp16_nhwc(backend.handle, input.handle, kernel.handle, output.handle,
+                                                n, h_in, w_in, c_in, c_out, k_h, k_w, stride_h, stride_w, pad_h, pad_w))
+
+
+def gemm_fp16(backend, a, b, c, m, n, k):
+    """crates/dragonwing-vulkan/src/ops.rs:1184: C[m,n] = A[m,k] @ B[k,n] in fp16, f32 accumulation."""
+    backend._check(L.load().dw_gemm_f16(backend.handle, a.handle, b.handle, c.handle, m, n, k))
+
+
+def add_fp16(backend, a, b, y):
+    """crates/dragonwing-vulkan/src/ops.rs:933: y = a + b (fp16)."""
+    backend._check(L.load().dw_add_f16(backend.handle, a.handle, b.handle, y.handle))
+
+
+def relu_fp16(backend, x):
+    """crates/dragonwing-vulkan/src/ops.rs:856: in-place ReLU (fp16)."""
+    backend._check(L.load().dw_relu_f16(backend.handle, x.handle))
+
+
+def add_relu_fp16(backend, a, b, y):
+    """add_fp16 then relu_fp16 in one pass."""
+    backend._check(L.load().dw_add_relu_f16(backend.handle, a.handle, b.handle, y.handle))
+
+
+def prepare_weights_f16(backend: CudaBackend, desc: ConvDesc, w_hwio: CudaBuffer) -> CudaBuffer:
+    """HWIO (or depthwise [kh,kw,C,mult]) fp16 kernel -> the kernels' layout (once)."""
+    out = ctypes.c_void_p()
+    d = desc.to_c()
+    backend._check(L.load().dw_prepare_weights_f16(backend.handle, ctypes.byref(d), w_hwio.handle, ctypes.byref(out)))
+    return CudaBuffer(backend, out, L.load().dw_buf_len(out))
+
+
+def conv2d_f16(backend: CudaBackend, desc: ConvDesc, x: CudaBuffer, w_prep: CudaBuffer, bias, y: CudaBuffer):
+    """fp16 conv + f16 bias (rounded as the CPU runtime does) + optional ReLU
+    (desc.epilogue EPI_NONE or EPI_RELU)."""
+    d = desc.to_c()
+    backend._check(L.load().dw_conv2d_f16(backend.handle, ctypes.byref(d), x.handle, w_prep.handle, _h(bias),
+                                          y.handle))
+
+
+def prepare_gemm_b_f16(backend: CudaBackend, b_kn: CudaBuffer, k: int, n: int) -> CudaBuffer:
+    out = ctypes.c_void_p()
+    backend._check(L.load().dw_prepare_gemm_b_f16(backend.handle, b_kn.handle, k, n, ctypes.byref(out)))
+    return CudaBuffer(backend, out, 2 * k * n)
+
+
+def gemm_f16_bias(backend: CudaBackend, a, b_prep, bias, y, m, n, k, relu=False):
+    """Gemm F16 + bias as the CPU runtime runs it (runtime.rs:1247-1275)."""
+    backend._check(L.load().dw_gemm_f16_bias(backend.handle, a.handle, b_prep.handle, _h(bias), y.handle, m, n, k,
+                                             1 if relu else 0))
+
+
+def maxpool_f16(backend, x, y, n, h, w, c, k_h, k_w, s_h, s_w, pads=(0, 0, 0, 0)):
+    pt, pl, pb, pr = pads
+    backend._check(L.load().dw_maxpool_f16(backend.handle, x.handle, y.handle, n, h, w, c, k_h, k_w, s_h, s_w,
+                                           pt, pl, pb, pr))
+
+
+def global_avgpool_f16(backend, x, y, n, h, w, c):
+    backend._check(L.load().dw_global_avgpool_f16(backend.handle, x.handle, y.handle, n, h, w, c))
+
+
+def cast_f32_to_f16(backend, x, y, pixels, c_src, c_dst=None):
+    backend._check(L.load().dw_cast_f32_to_f16(backend.handle, x.handle, y.handle, pixels, c_src,
+                                               c_src if c_dst is None else c_dst))
+
+
+def cast_f16_to_f32(backend, x, y):
+    backend._check(L.load().dw_cast_f16_to_f32(backend.handle, x.handle, y.handle))

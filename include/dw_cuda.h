@@ -249,6 +249,63 @@ DW_API dw_status dw_slice_c_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_
 DW_API dw_status dw_resize_nearest_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h_in,
                                       size_t w_in, size_t h_out, size_t w_out, size_t c);
 
+/* ---------------------------------------------------------------------- */
+/* FP16 path (binary16 buffers, f32 accumulation)                           */
+/* ---------------------------------------------------------------------- */
+/* Conversions follow F16::from_f32 / F16::to_f32 (crates/dragonwing-core/src/
+ * dtype.rs:164-263) exactly, including to_f32's halving of subnormal halves,
+ * so the elementwise, pooling, depthwise and direct-conv ops are bit-identical
+ * with the CPU ops; the tensor-core conv/GEMM sums in a different order and
+ * meets a stated tolerance instead. */
+
+/* Repacks an fp16 conv kernel: HWIO [kh,kw,c_in,c_out] -> the kernel layout
+ * (group == 1), or copies a depthwise kernel [kh,kw,C,mult]. */
+DW_API dw_status dw_prepare_weights_f16(dw_backend *be, const dw_conv_desc *d, const dw_buf *w_hwio,
+                                        dw_buf **out);
+/* Conv2D in fp16, NHWC: f32 accumulation, result stored as f16, then the f16
+ * bias[c_out] (may be NULL) added as the CPU runtime adds it (runtime.rs:
+ * 1483-1497: stored f16 + bias, rounded again), then ReLU when
+ * d->epilogue == DW_EPI_RELU (DW_EPI_NONE otherwise).  d->group: 1, or c_in
+ * (depthwise).  Tensor-core path: c_in % 8 == 0 (% 16 when strided), c_out % 8
+ * == 0; other shapes run the direct kernel unless the path is DW_PATH_UMMA. */
+DW_API dw_status dw_conv2d_f16(dw_backend *be, const dw_conv_desc *d, const dw_buf *x, const dw_buf *w_prep,
+                               const dw_buf *bias_or_null, dw_buf *y);
+/* conv2d_fp16_nhwc (crates/dragonwing-vulkan/src/ops.rs:1385-1420): the
+ * reference's parameter list, HWIO kernel, symmetric pads, no bias. */
+DW_API dw_status dw_conv2d_fp16_nhwc(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio,
+                                     dw_buf *output, size_t n, size_t h_in, size_t w_in, size_t c_in,
+                                     size_t c_out, size_t k_h, size_t k_w, size_t stride_h, size_t stride_w,
+                                     size_t pad_h, size_t pad_w);
+/* gemm_fp16 (vulkan ops.rs:1184-1215, cpu ops.rs:461-481): C[m,n] = A[m,k] *
+ * B[k,n], row-major f16, f32 accumulation. */
+DW_API dw_status dw_gemm_f16(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *c, size_t m, size_t n,
+                             size_t k);
+/* Repacks B [k,n] row-major (an fp16 Gemm weight) once into the kernel layout. */
+DW_API dw_status dw_prepare_gemm_b_f16(dw_backend *be, const dw_buf *b_kn, size_t k, size_t n, dw_buf **out);
+/* Gemm F16 with bias as the CPU runtime runs it (runtime.rs:1247-1275): f16
+ * product, then + bias[n] (may be NULL) rounded again, then ReLU if `relu`. */
+DW_API dw_status dw_gemm_f16_bias(dw_backend *be, const dw_buf *a, const dw_buf *b_prep, const dw_buf *bias,
+                                  dw_buf *y, size_t m, size_t n, size_t k, int relu);
+/* add_fp16 (vulkan ops.rs:933-960, cpu ops.rs:434-446): y = a + b. */
+DW_API dw_status dw_add_f16(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *y);
+/* add_fp16 followed by relu_fp16 in one pass (the Add -> Relu of a residual). */
+DW_API dw_status dw_add_relu_f16(dw_backend *be, const dw_buf *a, const dw_buf *b, dw_buf *y);
+/* relu_fp16 (vulkan ops.rs:856, in place; cpu ops.rs:345-352). */
+DW_API dw_status dw_relu_f16(dw_backend *be, dw_buf *x);
+/* F16 MaxPool (runtime.rs:1545-1563) on NHWC, pads [t,l,b,r] taken as -inf. */
+DW_API dw_status dw_maxpool_f16(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h, size_t w,
+                                size_t c, size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t,
+                                size_t p_l, size_t p_b, size_t p_r);
+/* F16 GlobalAveragePool (runtime.rs:1155-1170): NHWC -> [n, c]. */
+DW_API dw_status dw_global_avgpool_f16(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h,
+                                       size_t w, size_t c);
+/* f32 [pixels, c_src] -> f16 [pixels, c_dst] with F16::from_f32 (the runtime's
+ * F16 input conversion, runtime.rs:842-851); channels c_src..c_dst-1 are 0. */
+DW_API dw_status dw_cast_f32_to_f16(dw_backend *be, const dw_buf *x_f32, dw_buf *y_f16, size_t pixels,
+                                    size_t c_src, size_t c_dst);
+/* f16 -> f32 with F16::to_f32. */
+DW_API dw_status dw_cast_f16_to_f32(dw_backend *be, const dw_buf *x_f16, dw_buf *y_f32);
+
 #ifdef __cplusplus
 }
 #endif

@@ -530,13 +530,14 @@ void dwref_conv2d_f16_nhwc(uint16_t *y, const uint16_t *x, const uint16_t *w_hwi
 }
 
 /* ops.rs:2819-2937 depthwise_conv2d_fp16_nhwc_mt: kernel [kh, kw, C, mult]. */
-void dwref_dwconv_f16_nhwc(uint16_t *y, const uint16_t *x, const uint16_t *w, int relu,
+void dwref_dwconv_f16_nhwc(uint16_t *y, const uint16_t *x, const uint16_t *w,
+                           const uint16_t *bias_or_null, int relu,
                            size_t n, size_t h_in, size_t w_in, size_t c_in, size_t mult,
                            size_t k_h, size_t k_w, size_t stride_h, size_t stride_w,
                            size_t pad_h, size_t pad_w, int threads) {
     f16conv_ctx c;
     memset(&c, 0, sizeof c);
-    c.y = y; c.x = x; c.w = w; c.relu = relu; c.dw = 1; c.mult = mult;
+    c.y = y; c.x = x; c.w = w; c.bias = bias_or_null; c.relu = relu; c.dw = 1; c.mult = mult;
     c.n = n; c.h_in = h_in; c.w_in = w_in; c.c_in = c_in; c.c_out = c_in * mult;
     c.k_h = k_h; c.k_w = k_w; c.s_h = stride_h; c.s_w = stride_w; c.p_h = pad_h; c.p_w = pad_w;
     c.h_out = (h_in + 2 * pad_h - k_h) / stride_h + 1;
@@ -562,6 +563,32 @@ void dwref_gemm_f16(uint16_t *c, const uint16_t *a, const uint16_t *b, size_t m,
                     int threads) {
     f16gemm_ctx g = {c, a, b, m, n, k};
     parallel_for(threads, m, f16gemm_rows, &g);
+}
+
+/* The bias step of the CPU runtime's F16 Gemm and Conv (runtime.rs:1264-1275,
+ * 1483-1497): out = from_f32(to_f32(out) + to_f32(bias[j])) over [rows, c], in
+ * place; then, with `relu`, the Relu op (runtime.rs:967-971 / ops.rs:345-352). */
+void dwref_bias_relu_f16(uint16_t *y, const uint16_t *bias_or_null, int relu, size_t rows, size_t c) {
+    for (size_t i = 0; i < rows; i++)
+        for (size_t j = 0; j < c; j++) {
+            uint16_t o = y[i * c + j];
+            if (bias_or_null) o = dwref_f16_from_f32(dwref_f16_to_f32(o) + dwref_f16_to_f32(bias_or_null[j]));
+            if (relu) {
+                float v = dwref_f16_to_f32(o);
+                o = dwref_f16_from_f32(v > 0.0f ? v : 0.0f);
+            }
+            y[i * c + j] = o;
+        }
+}
+
+/* Element-wise F16::from_f32 / F16::to_f32 (the runtime's input conversion,
+ * runtime.rs:842-851, and output read-back). */
+void dwref_f16_from_f32_array(uint16_t *y, const float *x, size_t len) {
+    for (size_t i = 0; i < len; i++) y[i] = dwref_f16_from_f32(x[i]);
+}
+
+void dwref_f16_to_f32_array(float *y, const uint16_t *x, size_t len) {
+    for (size_t i = 0; i < len; i++) y[i] = dwref_f16_to_f32(x[i]);
 }
 
 /* ops.rs:434-446 add_fp16. */

@@ -99,12 +99,16 @@ void dwref_conv2d_f16_nhwc(uint16_t *y, const uint16_t *x, const uint16_t *w_hwi
                            size_t n, size_t h_in, size_t w_in, size_t c_in, size_t c_out,
                            size_t k_h, size_t k_w, size_t stride_h, size_t stride_w,
                            size_t pad_h, size_t pad_w, int threads);
-void dwref_dwconv_f16_nhwc(uint16_t *y, const uint16_t *x, const uint16_t *w, int relu,
+void dwref_dwconv_f16_nhwc(uint16_t *y, const uint16_t *x, const uint16_t *w,
+                           const uint16_t *bias_or_null, int relu,
                            size_t n, size_t h_in, size_t w_in, size_t c_in, size_t mult,
                            size_t k_h, size_t k_w, size_t stride_h, size_t stride_w,
                            size_t pad_h, size_t pad_w, int threads);
 void dwref_gemm_f16(uint16_t *c, const uint16_t *a, const uint16_t *b, size_t m, size_t n, size_t k,
                     int threads);
+void dwref_bias_relu_f16(uint16_t *y, const uint16_t *bias_or_null, int relu, size_t rows, size_t c);
+void dwref_f16_from_f32_array(uint16_t *y, const float *x, size_t len);
+void dwref_f16_to_f32_array(float *y, const uint16_t *x, size_t len);
 void dwref_add_f16(uint16_t *y, const uint16_t *a, const uint16_t *b, size_t len);
 void dwref_relu_f16(uint16_t *y, const uint16_t *x, size_t len);
 void dwref_gap_f16(uint16_t *y, const uint16_t *x, size_t n, size_t h, size_t w, size_t c);

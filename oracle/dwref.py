@@ -72,7 +72,10 @@ def _declare(L):
         "dwref_concat_c_i8": [vp, vp, vp, ctypes.c_int32, sz],
         "dwref_resize_nearest_i8": [vp, vp] + [sz] * 6,
         "dwref_conv2d_f16_nhwc": [vp, vp, vp, vp, i32] + [sz] * 11 + [i32],
-        "dwref_dwconv_f16_nhwc": [vp, vp, vp, i32] + [sz] * 11 + [i32],
+        "dwref_dwconv_f16_nhwc": [vp, vp, vp, vp, i32] + [sz] * 11 + [i32],
+        "dwref_bias_relu_f16": [vp, vp, i32, sz, sz],
+        "dwref_f16_from_f32_array": [vp, vp, sz],
+        "dwref_f16_to_f32_array": [vp, vp, sz],
         "dwref_gemm_f16": [vp, vp, vp, sz, sz, sz, i32],
         "dwref_add_f16": [vp, vp, vp, sz],
         "dwref_relu_f16": [vp, vp, sz],
@@ -311,13 +314,37 @@ def conv2d_f16(x, w_hwio, bias, relu, n, h, w, c_in, c_out, k_h, k_w, s_h, s_w, 
     return y
 
 
-def dwconv_f16(x, w, relu, n, h, wd, c, mult, k_h, k_w, s_h, s_w, p_h, p_w, threads=1):
+def dwconv_f16(x, w, relu, n, h, wd, c, mult, k_h, k_w, s_h, s_w, p_h, p_w, threads=1, bias=None):
+    """ops.rs:2819-2937 depthwise fp16 (+ runtime.rs:1483-1497 bias, relu)."""
     x, wt = _c(x, np.uint16), _c(w, np.uint16)
+    b = None if bias is None else _c(bias, np.uint16)
     ho = (h + 2 * p_h - k_h) // s_h + 1
     wo = (wd + 2 * p_w - k_w) // s_w + 1
     y = np.empty(n * ho * wo * c * mult, np.uint16)
-    lib().dwref_dwconv_f16_nhwc(_p(y), _p(x), _p(wt), int(relu), n, h, wd, c, mult, k_h, k_w, s_h, s_w,
+    lib().dwref_dwconv_f16_nhwc(_p(y), _p(x), _p(wt), _p(b), int(relu), n, h, wd, c, mult, k_h, k_w, s_h, s_w,
                                 p_h, p_w, threads)
+    return y
+
+
+def bias_relu_f16(y, bias, relu, rows, c):
+    """runtime.rs:1264-1275 / 1483-1497 bias step (+ Relu), on a copy of y."""
+    y = np.array(_c(y, np.uint16), copy=True)
+    b = None if bias is None else _c(bias, np.uint16)
+    lib().dwref_bias_relu_f16(_p(y), _p(b), int(relu), rows, c)
+    return y
+
+
+def f16_from_f32_array(x):
+    x = _c(x, np.float32)
+    y = np.empty(x.size, np.uint16)
+    lib().dwref_f16_from_f32_array(_p(y), _p(x), x.size)
+    return y
+
+
+def f16_to_f32_array(x):
+    x = _c(x, np.uint16)
+    y = np.empty(x.size, np.float32)
+    lib().dwref_f16_to_f32_array(_p(y), _p(x), x.size)
     return y
 
 

@@ -8,6 +8,17 @@ conv2d_i8_nhwc / requantize / relu (crates/dragonwing-cpu/src/ops.rs:3086-3142,
 maxpool2d (ops.rs:1513-1551), Concat/Split to concat_f32/split_f32 on int8
 bytes (ops.rs:2141-2246, 2407), Resize to resize_f32 Nearest (ops.rs:2320-2348),
 QuantizeU8 to u8*(1/255) -> quantize_f32_to_i8 (ops.rs:3503-3525).
+
+fp16 graphs follow the reference's F16 CPU runtime: CastF32ToF16 is the input
+conversion (runtime.rs:842-851), Conv2dF16 is conv2d_fp16_nhwc (ops.rs:1442-1511)
+plus the runtime's bias and Relu steps (runtime.rs:1483-1497, 967-971),
+AddF16 is add_fp16 (ops.rs:434-446) + Relu, MaxPoolF16 and
+GlobalAveragePoolF16 are runtime.rs:1545-1563 and 1155-1170, GemmF16 is
+gemm_fp16 (ops.rs:461-481) + the bias step (runtime.rs:1264-1275).  fp16
+tensors are held as uint16 bit patterns.  A CastF32ToF16 that pads channels
+(for the device kernels' alignment) is run without the padding here, and the
+conv that consumes it uses only its real input channels (`c_in_real`), so the
+CPU does exactly the reference's work.
 """
 from __future__ import annotations
 
@@ -74,6 +85,64 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
         elif t == "Dequantize":
             x = vals[op.inputs[0]]
             vals[op.outputs[0]] = dwref.dequantize_i8_to_f32(x, op.params["scale"]).reshape(x.shape)
+        elif t == "CastF32ToF16":
+            x = vals[op.inputs[0]]
+            vals[op.outputs[0]] = dwref.f16_from_f32_array(x).reshape(x.shape)
+        elif t == "Conv2dF16":
+            vals[op.outputs[0]] = conv_f16_op(graph, op, vals[op.inputs[0]], threads)
+        elif t == "AddF16":
+            a, b = vals[op.inputs[0]], vals[op.inputs[1]]
+            y = dwref.add_f16(a, b)
+            if op.params.get("relu"):
+                y = dwref.relu_f16(y)
+            vals[op.outputs[0]] = y.reshape(a.shape)
+        elif t == "MaxPoolF16":
+            x = vals[op.inputs[0]]
+            n, h, w, c = x.shape
+            k, s, p = op.params["k"], op.params["s"], op.params["pad"]
+            y = dwref.maxpool_f16(x, n, h, w, c, k, k, s, s, (p, p, p, p))
+            vals[op.outputs[0]] = y.reshape(shape_of(op.outputs[0]))
+        elif t == "GlobalAveragePoolF16":
+            x = vals[op.inputs[0]]
+            n, h, w, c = x.shape
+            vals[op.outputs[0]] = dwref.gap_f16(x, n, h, w, c).reshape(n, c)
+        elif t == "GemmF16":
+            vals[op.outputs[0]] = gemm_f16_op(graph, op, vals[op.inputs[0]], threads)
+        elif t == "CastF16ToF32":
+            x = vals[op.inputs[0]]
+            vals[op.outputs[0]] = dwref.f16_to_f32_array(x).reshape(x.shape)
         else:
             raise ValueError(f"unsupported op {t}")
     return {name: vals[name] for name in graph.outputs}
+
+
+def conv_f16_op(graph, op, x, threads=1):
+    """One Conv2dF16 op on uint16 NHWC input `x` (its real channels only)."""
+    d = op.params["desc"]
+    n, h, w, c_x = x.shape
+    c_in = op.params.get("c_in_real", d.c_in)
+    if c_x != c_in:  # a device-side tensor with zero padding channels
+        x = np.ascontiguousarray(x[..., :c_in])
+    wt = graph.initializers[op.inputs[1]].view(np.uint16)[:, :, :c_in, :]
+    bias = graph.initializers[op.inputs[2]].view(np.uint16)
+    pt, pl, pb, pr = d.pads
+    assert pt == pb and pl == pr, "the CPU conv takes symmetric pads"
+    relu = d.epilogue == dwref.EPI_RELU
+    ho, wo = d.out_hw()
+    if d.group == 1:
+        y = dwref.conv2d_f16(x, wt, bias, relu, n, h, w, c_in, d.c_out, d.k_h, d.k_w, d.stride_h, d.stride_w,
+                             pt, pl, threads)
+    else:
+        y = dwref.dwconv_f16(x, wt, relu, n, h, w, c_in, d.c_out // c_in, d.k_h, d.k_w, d.stride_h, d.stride_w,
+                             pt, pl, threads, bias=bias)
+    return y.reshape(n, ho, wo, d.c_out)
+
+
+def gemm_f16_op(graph, op, x, threads=1):
+    """One GemmF16 op: gemm_fp16 then the runtime's bias step."""
+    m = x.shape[0]
+    n, k = op.params["n"], op.params["k"]
+    wt = graph.initializers[op.inputs[1]].view(np.uint16)
+    bias = graph.initializers[op.inputs[2]].view(np.uint16)
+    y = dwref.gemm_f16(x, wt, m, n, k, threads)
+    return dwref.bias_relu_f16(y, bias, False, m, n).reshape(m, n)
