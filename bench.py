@@ -18,6 +18,10 @@ distributions, seeded):
   mbv2_block  MobileNetV2 inverted-residual block, batch 32 per GPU, 112x112x96,
               1x1 expand 576 + ReLU6, depthwise 3x3 + ReLU6, 1x1 project 96,
               residual add with requantisation.
+  resnet50_fp16  ResNet-50-architecture fp16 graph, 224x224x3 f32 input
+              normal(0,1), batch 128 per GPU (1024 over 8 GPUs); value =
+              images/s, conv TFLOP/s and % of the fp16
+              (= bf16) tensor peak beside it.
 
 --impl reference times the reference's CPU implementation of the same
 workload (the oracle restatement of dragonwing-cpu's scalar ops, all host
@@ -132,7 +136,9 @@ WORKLOADS = {
     # name: (default per-GPU batch, value unit, description)
     "yolov8n": (32, "images/s", "yolov8n_int8 640x640 (BASELINE config 4)"),
     "mbv2_block": (32, "TOPS", "mobilenetv2_int8_block 112x112x96 (BASELINE config 2)"),
+    "resnet50_fp16": (128, "images/s", "resnet50_fp16 224x224 (BASELINE config 5)"),
 }
+FP16_WORKLOADS = {"resnet50_fp16"}
 DEFAULT_WORKLOAD = "yolov8n"
 
 
@@ -141,7 +147,12 @@ def build_workload(name: str, batch: int, seed: int):
     if name not in WORKLOADS:
         raise SystemExit(f"unknown workload {name}")
     desc = WORKLOADS[name][2]
-    if name == "mbv2_block":
+    if name == "resnet50_fp16":
+        g = G.resnet50_fp16(batch=batch, seed=seed)
+        cfg = {"workload": desc, "batch_per_gpu": batch, "stages": [3, 4, 6, 3], "classes": 1000,
+               "layers": "53 fp16 convs (BN folded, bias, ReLU), 3x3/2 max pool, 16 residual add+ReLU, GAP, FC 1000",
+               "input": "f32 NHWC normal(0,1) -> f16 (3 channels zero-padded to 16)", "outputs": "f32 logits"}
+    elif name == "mbv2_block":
         g = G.mobilenetv2_block(batch=batch, seed=seed)
         cfg = {"workload": desc, "batch_per_gpu": batch, "expand": 576,
                "layers": "1x1 expand+ReLU6, dw3x3+ReLU6, 1x1 project, add"}
@@ -163,6 +174,8 @@ def make_input(graph, seed):
     rng = np.random.default_rng(seed)
     if t.dtype == "u8":
         return rng.integers(0, 256, t.nbytes).astype(np.uint8)
+    if t.dtype == "f32":
+        return rng.standard_normal(t.nbytes // 4).astype(np.float32)
     return rng.integers(-128, 128, t.nbytes).astype(np.int8)
 
 
@@ -181,11 +194,15 @@ def op_bytes(graph, op):
 
 
 def op_flops(op):
-    if op.op_type != "Conv2dRequantReluI8Nhwc":
+    """Algorithmic ops (2 x MACs; a zero-padded input channel does not count)."""
+    if op.op_type == "GemmF16":
+        return 2 * op.params["m"] * op.params["n"] * op.params["k"]
+    if op.op_type not in ("Conv2dRequantReluI8Nhwc", "Conv2dF16", "Conv2dAddF16"):
         return 0
     d = op.params["desc"]
     ho, wo = d.out_hw()
-    return 2 * d.n * ho * wo * d.c_out * d.k_h * d.k_w * (d.c_in if d.group == 1 else 1)
+    c_in = op.params.get("c_in_real", d.c_in)
+    return 2 * d.n * ho * wo * d.c_out * d.k_h * d.k_w * (c_in if d.group == 1 else 1)
 
 
 # ---------------------------------------------------------------------------
@@ -223,6 +240,7 @@ def run_ours(args, rank, world, local_rank):
     graph, cfg = build_workload(args.workload, batch, seed=1234)
     be = dw.CudaBackend(local_rank)
     rt = CudaGraphRuntime(graph, be)
+    graph = rt.graph  # after the device passes (fusion, input unfold); same work, fewer ops
     x_name = graph.inputs[0]
     xt = graph.tensors[x_name]
     x_host = make_input(graph, 1000 + rank)
@@ -322,7 +340,10 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0:
         peaks, peak_src = load_peaks()
         hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
-        int8_peak = 2.0 * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        f16 = args.workload in FP16_WORKLOADS
+        bf16_peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        # the tensor roof: dense fp16 = bf16 (measured cuBLAS); dense int8 = 2x that
+        int8_peak = bf16_peak if f16 else 2.0 * bf16_peak
         dom = max(per_op, key=lambda r: r["ms"])
         dom_op = graph.ops[[o.name for o in graph.ops].index(dom["op"])]
         traffic = load_traffic(dom_op)
@@ -331,15 +352,17 @@ def run_ours(args, rank, world, local_rank):
         ai = dom["ops"] / dom["bytes"] if dom["bytes"] else 0.0
         if dom["ops"] and ai > ridge:
             ach = dom["ops"] / (dom["ms"] * 1e-3) / 1e12
-            roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": round(int8_peak, 1), "unit": "TOP/s",
-                    "frac": round(ach / int8_peak, 4)}
+            roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": round(int8_peak, 1),
+                    "unit": "TFLOP/s" if f16 else "TOP/s", "frac": round(ach / int8_peak, 4)}
         else:
             ach = dom["bytes"] / (dom["ms"] * 1e-3) / 1e9
             roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                     "frac": round(ach / hbm_peak, 4)}
         roof.update({"kernel": dom["op"], "kernel_ms": dom["ms"], "algorithmic_bytes": dom["bytes"],
                      "algorithmic_ops": dom["ops"], "traffic": traffic, "peak_source": f"{peak_src} (MEASURED_PEAKS.json)"
-                     if peak_src == "measured" else "fallback", "int8_peak_note": "int8 dense peak taken as 2x the measured bf16 cuBLAS figure"})
+                     if peak_src == "measured" else "fallback",
+                     "peak_note": "fp16 dense peak = the measured bf16 cuBLAS figure" if f16 else
+                     "int8 dense peak taken as 2x the measured bf16 cuBLAS figure"})
         images = batch * world
         tops = step_ops * world / (ms_per_step * 1e-3) / 1e12
         ips = images / (ms_per_step * 1e-3)
@@ -357,11 +380,12 @@ def run_ours(args, rank, world, local_rank):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "int8 (i32 accumulate, f32 requant)",
-            "data": "synthetic (seeded int8 activations, He-normal weights quantised per channel)",
+            "dtype": "f16 (f32 accumulate)" if f16 else "int8 (i32 accumulate, f32 requant)",
+            "data": "synthetic (seeded normal(0,1) f32 images, He-normal f16 weights, BN folded)" if f16 else
+                    "synthetic (seeded int8 activations, He-normal weights quantised per channel)",
             "images_per_s": round(ips, 1),
             "conv_tops": round(tops, 3),
-            "pct_of_int8_peak": round(100.0 * tops / (int8_peak * world), 2),
+            "pct_of_tensor_peak": round(100.0 * tops / (int8_peak * world), 2),
             "config": dict(cfg, parallelism=f"replicas x{world} (batch-sharded, no collective)",
                            global_batch=images, l2="per-step working set several GB, far larger than the 126 MB L2"),
             "e2e": {"value": round(e2e_ips if unit == "images/s" else e2e_tops, 3), "unit": unit,
@@ -466,7 +490,8 @@ def run_reference(args, rank, world):
     line = {"metric": METRIC, "value": round(value, 6), "unit": unit, "impl": "reference", "n_gpus": world,
             "steps": args.steps_run, "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8 (i32 accumulate, f32 requant)", "data": "synthetic",
+            "dtype": "f16 (f32 accumulate)" if args.workload in FP16_WORKLOADS else "int8 (i32 accumulate, f32 requant)",
+            "data": "synthetic",
             "images_per_s": round(images / (ms_per_step * 1e-3), 4),
             "config": dict(cfg, sample_images_per_step=images),
             "conv_tops": round(tops, 6),

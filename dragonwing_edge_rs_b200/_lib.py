@@ -93,6 +93,7 @@ SIGNATURES = {
     # fp16 path
     "dw_prepare_weights_f16": ([vp, ctypes.POINTER(DwConvDesc), vp, PVP], i32),
     "dw_conv2d_f16": ([vp, ctypes.POINTER(DwConvDesc), vp, vp, vp, vp], i32),
+    "dw_conv2d_add_f16": ([vp, ctypes.POINTER(DwConvDesc), vp, vp, vp, vp, vp], i32),
     "dw_conv2d_fp16_nhwc": ([vp, vp, vp, vp] + [sz] * 11, i32),
     "dw_gemm_f16": ([vp, vp, vp, vp, sz, sz, sz], i32),
     "dw_prepare_gemm_b_f16": ([vp, vp, sz, sz, PVP], i32),
@@ -104,6 +105,7 @@ SIGNATURES = {
     "dw_global_avgpool_f16": ([vp, vp, vp] + [sz] * 4, i32),
     "dw_cast_f32_to_f16": ([vp, vp, vp, sz, sz, sz], i32),
     "dw_cast_f16_to_f32": ([vp, vp, vp], i32),
+    "dw_unfold_w_f32_to_f16": ([vp, vp, vp] + [sz] * 9, i32),
 }
 
 _lib = None

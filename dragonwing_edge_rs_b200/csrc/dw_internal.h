@@ -102,7 +102,8 @@ bool umma_supported_f16(const dw_backend *be, const dw_conv_desc &d, int ho, int
 dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
                               const int8_t *w_ohwi, const EpiParams &ep, int8_t *y);
 dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,
-                               const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y);
+                               const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y,
+                               const uint16_t *residual);
 
 // fp16.cu (CUDA-core fp16 kernels)
 dw_status launch_conv_direct_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,
@@ -119,5 +120,7 @@ dw_status launch_repack_hwio_to_ohwi_f16(dw_backend *be, const uint16_t *w, uint
 dw_status launch_transpose_kn_to_nk_f16(dw_backend *be, const uint16_t *b, uint16_t *out, int k, int n);
 dw_status launch_cast_f32_to_f16(dw_backend *be, const float *x, uint16_t *y, size_t pixels, int c_src, int c_dst);
 dw_status launch_cast_f16_to_f32(dw_backend *be, const uint16_t *x, float *y, size_t n);
+dw_status launch_unfold_w_f32_to_f16(dw_backend *be, const float *x, uint16_t *y, int n, int h, int w, int c, int kw,
+                                    int sw, int pl, int wo, int c_dst);
 
 }  // namespace dw

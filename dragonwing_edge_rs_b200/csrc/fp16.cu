@@ -133,8 +133,8 @@ __device__ __forceinline__ uint32_t relu_pair(uint32_t a) {
 
 // n halves; `vec` = 1 when all three pointers are 16-byte aligned (8 halves per
 // step, scalar tail), else scalar throughout.  `b` null = ReLU only.
-__global__ void k_add_relu_f16(const uint16_t *__restrict__ a, const uint16_t *__restrict__ b, uint16_t *y, size_t n,
-                               int relu, int vec) {
+__global__ void k_add_relu_f16(const uint16_t *a, const uint16_t *__restrict__ b, uint16_t *y, size_t n, int relu,
+                               int vec) {  // a may alias y (in-place)
     const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     size_t head = 0;
@@ -184,6 +184,88 @@ __global__ void k_maxpool_f16(const uint16_t *__restrict__ x, uint16_t *__restri
             }
         }
         y[i] = f32_to_f16_ref(m);
+    }
+}
+
+// Same max pool, 8 channels per thread (c % 8 == 0, 16-byte aligned buffers):
+// the max of F16::to_f32 values is F16::to_f32 of the max in f16 order
+// (to_f32 is monotonic: it only halves subnormals, which stay below every
+// normal value), and __hmax2 ignores a NaN operand like f32::max; the result
+// then goes through to_f32 / from_f32 as the CPU does, which only changes a
+// nonzero subnormal.
+__global__ void k_maxpool_f16_v8(const uint4 *__restrict__ x, uint4 *__restrict__ y, int n, int h, int w, int cg,
+                                 int kh, int kw, int sh, int sw, int pt, int pl, int ho, int wo) {
+    const size_t total = (size_t)n * ho * wo * cg;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int g = (int)(i % cg);
+        size_t p = i / cg;
+        const int ow = (int)(p % wo);
+        p /= wo;
+        const int oh = (int)(p % ho);
+        const int b = (int)(p / ho);
+        __half2 m[4];
+        const __half2 ninf = __halves2half2(__ushort_as_half(0xFC00), __ushort_as_half(0xFC00));
+        for (int k = 0; k < 4; k++) m[k] = ninf;
+        for (int a = 0; a < kh; a++) {
+            const int ih = oh * sh + a - pt;
+            if (ih < 0 || ih >= h) continue;
+            for (int q = 0; q < kw; q++) {
+                const int iw = ow * sw + q - pl;
+                if (iw < 0 || iw >= w) continue;
+                const uint4 v = __ldg(x + (((size_t)b * h + ih) * w + iw) * cg + g);
+                const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+                for (int k = 0; k < 4; k++) m[k] = __hmax2(m[k], *reinterpret_cast<const __half2 *>(&vv[k]));
+            }
+        }
+        uint32_t o[4];
+        for (int k = 0; k < 4; k++) {
+            uint32_t u = *reinterpret_cast<uint32_t *>(&m[k]);
+            const uint16_t lo = (uint16_t)(u & 0xFFFFu), hi = (uint16_t)(u >> 16);
+            const bool slo = (lo & 0x7C00u) == 0 && (lo & 0x03FFu), shi = (hi & 0x7C00u) == 0 && (hi & 0x03FFu);
+            if (slo || shi)
+                u = (uint32_t)f32_to_f16_ref(f16_to_f32_ref(lo)) | ((uint32_t)f32_to_f16_ref(f16_to_f32_ref(hi)) << 16);
+            o[k] = u;
+        }
+        y[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// Horizontal unfold of an f32 NHWC image into f16 (F16::from_f32), fused
+// with the input conversion: y[n][r][j][q*c + ch] = x[n][r][j*sw + q - pl][ch]
+// for q < kw (0 outside the image), channels kw*c .. c_dst-1 zero.  A k_h x
+// k_w conv with horizontal stride sw on x equals a k_h x 1 conv with
+// horizontal stride 1 on y whose kernel rows hold the k_w taps side by side:
+// the same products, with whole rows of kw*c channels per tap for the
+// tensor-core loads instead of c (= 3 for an image) channels.
+__global__ void k_unfold_w_f32_to_f16(const float *__restrict__ x, uint16_t *__restrict__ y, int n, int h, int w,
+                                      int c, int kw, int sw, int pl, int wo, int c_dst) {
+    // One thread per output pixel (n, r, j): its kw*c values are the contiguous
+    // run x[n][r][j*sw - pl ..][*] of the input row (k = q*c + ch indexes it
+    // directly), zero where the run leaves the row.
+    const size_t total = (size_t)n * h * wo;
+    const int kc = kw * c, row_len = w * c;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int j = (int)(i % wo);
+        const size_t row = i / wo;  // n * h + r
+        const float *xr = x + row * (size_t)row_len;
+        const int base = (j * sw - pl) * c;
+        uint4 *dst = reinterpret_cast<uint4 *>(y + i * (size_t)c_dst);
+        for (int g = 0; g < c_dst; g += 8) {
+            uint32_t o[4];
+#pragma unroll
+            for (int k2 = 0; k2 < 4; k2++) {
+                uint32_t pair = 0;
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int k = g + 2 * k2 + e, idx = base + k;
+                    const uint16_t hv =
+                        (k < kc && idx >= 0 && idx < row_len) ? f32_to_f16_ref(__ldg(xr + idx)) : (uint16_t)0;
+                    pair |= (uint32_t)hv << (16 * e);
+                }
+                o[k2] = pair;
+            }
+            dst[g / 8] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
     }
 }
 
@@ -256,6 +338,13 @@ dw_status launch_relu_f16(dw_backend *be, const uint16_t *x, uint16_t *y, size_t
 
 dw_status launch_maxpool_f16(dw_backend *be, const uint16_t *x, uint16_t *y, int n, int h, int w, int c, int kh,
                              int kw, int sh, int sw, int pt, int pl, int ho, int wo) {
+    if (c % 8 == 0 && al16(x) && al16(y)) {
+        const size_t items = (size_t)n * ho * wo * (c / 8);
+        k_maxpool_f16_v8<<<grid_for(be, items), kThreads, 0, be->stream>>>(
+            reinterpret_cast<const uint4 *>(x), reinterpret_cast<uint4 *>(y), n, h, w, c / 8, kh, kw, sh, sw, pt, pl,
+            ho, wo);
+        return dw_after_launch(be, "maxpool_f16");
+    }
     const size_t items = (size_t)n * ho * wo * c;
     k_maxpool_f16<<<grid_for(be, items), kThreads, 0, be->stream>>>(x, y, n, h, w, c, kh, kw, sh, sw, pt, pl, ho, wo);
     return dw_after_launch(be, "maxpool_f16");
@@ -269,6 +358,13 @@ dw_status launch_gap_f16(dw_backend *be, const uint16_t *x, uint16_t *y, int n, 
 dw_status launch_cast_f32_to_f16(dw_backend *be, const float *x, uint16_t *y, size_t pixels, int c_src, int c_dst) {
     k_cast_f32_to_f16<<<grid_for(be, pixels * c_dst), kThreads, 0, be->stream>>>(x, y, pixels, c_src, c_dst);
     return dw_after_launch(be, "cast_f32_to_f16");
+}
+
+dw_status launch_unfold_w_f32_to_f16(dw_backend *be, const float *x, uint16_t *y, int n, int h, int w, int c, int kw,
+                                    int sw, int pl, int wo, int c_dst) {
+    const size_t items = (size_t)n * h * wo;
+    k_unfold_w_f32_to_f16<<<grid_for(be, items), kThreads, 0, be->stream>>>(x, y, n, h, w, c, kw, sw, pl, wo, c_dst);
+    return dw_after_launch(be, "unfold_w_f32_to_f16");
 }
 
 dw_status launch_cast_f16_to_f32(dw_backend *be, const uint16_t *x, float *y, size_t n) {

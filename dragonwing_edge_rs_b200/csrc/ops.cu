@@ -425,21 +425,37 @@ DW_API dw_status dw_prepare_weights_f16(dw_backend *be, const dw_conv_desc *d, c
     return DW_OK;
 }
 
+// fp16 conv (+ bias) (+ residual) (+ ReLU).  The tensor-core kernel fuses the
+// residual into its epilogue for 1x1 stride-1 convs; elsewhere the residual
+// is added (with the ReLU) by a second pass over y, with the same arithmetic.
 static dw_status conv_dispatch_f16(dw_backend *be, const dw_conv_desc *d, int ho, int wo, const dw_buf *x,
-                                   const dw_buf *w_prep, const dw_buf *bias, dw_buf *y, const char *op) {
+                                   const dw_buf *w_prep, const dw_buf *bias, dw_buf *y, const char *op,
+                                   const dw_buf *residual = nullptr) {
     const uint16_t *xp = (const uint16_t *)x->ptr;
     const uint16_t *wp = (const uint16_t *)w_prep->ptr;
     const uint16_t *bp = bias ? (const uint16_t *)bias->ptr : nullptr;
+    const uint16_t *rp = residual ? (const uint16_t *)residual->ptr : nullptr;
     uint16_t *yp = (uint16_t *)y->ptr;
     const int relu = d->epilogue == DW_EPI_RELU ? 1 : 0;
-    if (d->group != 1) return dw::launch_dwconv_f16(be, *d, ho, wo, xp, wp, bp, relu, yp);
+    const bool flat = d->k_h == 1 && d->k_w == 1 && d->stride_h == 1 && d->stride_w == 1 && d->pad_t == 0 &&
+                      d->pad_l == 0 && d->pad_b == 0 && d->pad_r == 0;
     const int path = be->cfg.conv_path;
-    if (path != DW_PATH_DIRECT && dw::umma_supported_f16(be, *d, ho, wo))
-        return dw::launch_umma_conv_f16(be, *d, ho, wo, xp, wp, bp, relu, yp);
-    if (path == DW_PATH_UMMA)
+    const bool umma = d->group == 1 && path != DW_PATH_DIRECT && dw::umma_supported_f16(be, *d, ho, wo);
+    if (d->group == 1 && !umma && path == DW_PATH_UMMA)
         return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: shape not supported by the tensor-core kernel (c_in=%d c_out=%d)",
                        op, d->c_in, d->c_out);
-    return dw::launch_conv_direct_f16(be, *d, ho, wo, xp, wp, bp, relu, yp);
+    if (umma && (!rp || (flat && ((uintptr_t)rp & 15) == 0)))
+        return dw::launch_umma_conv_f16(be, *d, ho, wo, xp, wp, bp, relu, yp, rp);
+    const int relu1 = rp ? 0 : relu;
+    dw_status st;
+    if (d->group != 1)
+        st = dw::launch_dwconv_f16(be, *d, ho, wo, xp, wp, bp, relu1, yp);
+    else if (umma)
+        st = dw::launch_umma_conv_f16(be, *d, ho, wo, xp, wp, bp, relu1, yp, nullptr);
+    else
+        st = dw::launch_conv_direct_f16(be, *d, ho, wo, xp, wp, bp, relu1, yp);
+    if (st != DW_OK || !rp) return st;
+    return dw::launch_add_f16(be, yp, rp, yp, y->len / 2, relu);
 }
 
 DW_API dw_status dw_conv2d_f16(dw_backend *be, const dw_conv_desc *d, const dw_buf *x, const dw_buf *w_prep,
@@ -459,6 +475,28 @@ DW_API dw_status dw_conv2d_f16(dw_backend *be, const dw_conv_desc *d, const dw_b
     if (bias_or_null) DW_TRY(check_len(be, bias_or_null, 2 * (size_t)d->c_out, op, "bias"));
     cudaSetDevice(be->device);
     return conv_dispatch_f16(be, d, ho, wo, x, w_prep, bias_or_null, y, op);
+}
+
+DW_API dw_status dw_conv2d_add_f16(dw_backend *be, const dw_conv_desc *d, const dw_buf *x, const dw_buf *w_prep,
+                                   const dw_buf *bias_or_null, const dw_buf *residual, dw_buf *y) {
+    const char *op = "conv2d_add_f16";
+    if (!be) return DW_ERR_INVALID_ARG;
+    int ho, wo;
+    DW_TRY(check_desc(be, d, &ho, &wo, op));
+    if (d->epilogue != DW_EPI_NONE && d->epilogue != DW_EPI_RELU)
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: epilogue %d unsupported (NONE or RELU)", op, d->epilogue);
+    DW_TRY(need(be, x, op, "input"));
+    DW_TRY(need(be, w_prep, op, "kernel"));
+    DW_TRY(need(be, residual, op, "residual"));
+    DW_TRY(need(be, y, op, "output"));
+    DW_TRY(check_len(be, x, 2 * (size_t)d->n * d->h * d->w * d->c_in, op, "input"));
+    DW_TRY(check_len(be, w_prep, 2 * weight_len(d), op, "kernel"));
+    DW_TRY(check_len(be, y, 2 * (size_t)d->n * ho * wo * d->c_out, op, "output"));
+    DW_TRY(check_len(be, residual, y->len, op, "residual"));
+    if (bias_or_null) DW_TRY(check_len(be, bias_or_null, 2 * (size_t)d->c_out, op, "bias"));
+    if (residual->ptr == y->ptr) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: residual must not alias the output", op);
+    cudaSetDevice(be->device);
+    return conv_dispatch_f16(be, d, ho, wo, x, w_prep, bias_or_null, y, op, residual);
 }
 
 DW_API dw_status dw_conv2d_fp16_nhwc(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio, dw_buf *output,
@@ -642,6 +680,24 @@ DW_API dw_status dw_cast_f32_to_f16(dw_backend *be, const dw_buf *x_f32, dw_buf 
     cudaSetDevice(be->device);
     return dw::launch_cast_f32_to_f16(be, (const float *)x_f32->ptr, (uint16_t *)y_f16->ptr, pixels, (int)c_src,
                                       (int)c_dst);
+}
+
+DW_API dw_status dw_unfold_w_f32_to_f16(dw_backend *be, const dw_buf *x_f32, dw_buf *y_f16, size_t n, size_t h,
+                                        size_t w, size_t c, size_t k_w, size_t stride_w, size_t pad_l, size_t w_out,
+                                        size_t c_dst) {
+    const char *op = "unfold_w_f32_to_f16";
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x_f32 || !y_f16) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: null buffer", op);
+    if (!n || !h || !w || !c || !k_w || !stride_w || !w_out || c_dst % 8 || c_dst < k_w * c || c_dst > 4096 ||
+        n * h * w > 0x7fffffff || n * h * w_out > 0x7fffffff)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: invalid geometry (c_dst must be a multiple of 8 >= k_w*c)", op);
+    DW_TRY(check_len(be, x_f32, 4 * n * h * w * c, op, "input"));
+    DW_TRY(check_len(be, y_f16, 2 * n * h * w_out * c_dst, op, "output"));
+    if (((uintptr_t)y_f16->ptr & 15)) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: output must be 16-byte aligned", op);
+    cudaSetDevice(be->device);
+    return dw::launch_unfold_w_f32_to_f16(be, (const float *)x_f32->ptr, (uint16_t *)y_f16->ptr, (int)n, (int)h,
+                                          (int)w, (int)c, (int)k_w, (int)stride_w, (int)pad_l, (int)w_out,
+                                          (int)c_dst);
 }
 
 DW_API dw_status dw_cast_f16_to_f32(dw_backend *be, const dw_buf *x_f16, dw_buf *y_f32) {

@@ -65,7 +65,9 @@ struct UmmaParams {
     int esize;                              // element bytes: 1 (int8) or 2 (fp16)
     int bk_elems;                           // bk / esize: K elements per stage
     const uint16_t *bias_f16;               // fp16 path: bias [c_out] (may be null)
-    int relu;                               // fp16 path: ReLU after the bias
+    const uint16_t *res_f16;                // fp16 path, flat mode: residual [rows][c_out] added (may be null)
+    int relu;                               // fp16 path: ReLU last (after the bias and the residual)
+    int swz;                                // fp16 path: staging in 64-channel slabs, 128-byte swizzle (bn % 64 == 0)
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
@@ -251,11 +253,22 @@ __device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred
 __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs, int slot, int oc, bool write) {
     int32_t bias = 0;
     float m = 0.0f, dsc = 0.0f;
-    if (p.esize == 2) {  // fp16 path: the slot's `m` holds the f16 bias as a float
+    if (p.esize == 2) {
+        // fp16 path: `bias` holds the f16 bias bits, `m` the bias as F16::to_f32
+        // gives it; flag bit0 = some bias of the 16-slot group is a nonzero
+        // subnormal or a NaN (the packed fast path does not reproduce those).
+        const uint16_t hb = (write && oc < p.c_out && p.bias_f16) ? p.bias_f16[oc] : (uint16_t)0;
+        const bool special = ((hb & 0x7C00u) == 0 && (hb & 0x03FFu) != 0) || ((hb & 0x7C00u) == 0x7C00u && (hb & 0x03FFu));
+        const uint32_t bsp = __ballot_sync(0xffffffffu, special);
+        const uint32_t hb_next = __shfl_down_sync(0xffffffffu, (uint32_t)hb, 1);
         if (write) {
-            cs->m[slot] = (oc < p.c_out && p.bias_f16) ? f16_to_f32_ref(p.bias_f16[oc]) : 0.0f;
-            if ((slot & 15) == 0) cs->cflags[slot >> 4] = 0;
+            cs->bias[slot] = hb;
+            cs->m[slot] = f16_to_f32_ref(hb);
+            // packed (even, odd) channel pairs for the epilogue's half2 loads
+            if ((slot & 1) == 0) reinterpret_cast<uint32_t *>(cs->d)[slot >> 1] = (uint32_t)hb | (hb_next << 16);
         }
+        const int ln = threadIdx.x & 31;
+        if ((ln & 15) == 0 && write) cs->cflags[slot >> 4] = ((bsp >> ln) & 0xFFFFu) ? 1u : 0u;
         return;
     }
     if (write && oc < p.c_out) {
@@ -405,31 +418,109 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
 }
 
 // fp16 epilogue for 16 f32 accumulators (16 consecutive channels of one row),
-// in the order the reference's CPU runtime applies it: the conv result stored
-// as f16 (F16::from_f32, round to nearest even), then the f16 bias added in f32
-// and rounded to f16 again (crates/dragonwing-onnx/src/runtime.rs:1483-1497),
-// then ReLU as relu_fp16 (x > 0 ? x : 0, crates/dragonwing-cpu/src/ops.rs:345-352).
-// Writes 32 bytes (16 halves) to dst.
-__device__ __forceinline__ void f16_epilogue16(const int32_t (&v)[16], const ChanSmem *cs, int slot0,
-                                               const UmmaParams &p, uint8_t *dst) {
-    uint32_t w[8];
-#pragma unroll
-    for (int k = 0; k < 16; k += 2) {
-        uint16_t h[2];
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-            uint16_t x = f32_to_f16_ref(__int_as_float(v[k + j]));
-            if (p.bias_f16) x = f32_to_f16_ref(__fadd_rn(f16_to_f32_ref(x), cs->m[slot0 + k + j]));
-            if (p.relu) {
-                const float f = f16_to_f32_ref(x);
-                x = f32_to_f16_ref(f > 0.0f ? f : 0.0f);
-            }
-            h[j] = x;
-        }
-        w[k / 2] = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+// in the order the reference's CPU runtime applies the ops: the conv result
+// stored as f16 (F16::from_f32, round to nearest even), the f16 bias added in
+// f32 and rounded to f16 again (crates/dragonwing-onnx/src/runtime.rs:1483-1497),
+// the residual added as add_fp16 does it (crates/dragonwing-cpu/src/ops.rs:434-446),
+// then ReLU (x > 0 ? x : 0, ops.rs:345-352 / runtime.rs:967-971).
+//
+// Packed-half path, branch-free: an add of two f16 values done in f32 and
+// rounded to f16 equals the f16 add rounded once (f32 has 24 >= 2*11 + 2
+// significand bits, so the double rounding is innocuous; sums below 2^-14 are
+// exact in both).  The reference's F16::to_f32 halves a subnormal operand, so
+// a step whose operand is below 2^-14 (zero included: halving it is harmless)
+// scales that operand by 0.5 inside one fused multiply-add, which rounds
+// once as the f32 path does: fma(x, 0.5, b) for the bias, the residual add
+// with the subnormal operand in the multiplied slot, and x * 0.5 before the
+// ReLU.  What this cannot express -- both residual-add operands subnormal, a
+// NaN result without a final ReLU, a subnormal or NaN bias -- goes to the
+// exact per-element path.
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// Per half 0xFFFF when |x| < 2^-14 (subnormal or zero).
+__device__ __forceinline__ uint32_t h2_tiny_mask(uint32_t x) {
+    return __hlt2_mask(__habs2(bits_h2(x)), bits_h2(0x04000400u));
+}
+
+// Per half: 0.5 where the mask is set, else 1.0.
+__device__ __forceinline__ uint32_t half_scale(uint32_t mask) { return 0x3C003C00u ^ (mask & 0x04000400u); }
+
+// One element on the exact path (every step through F16::to_f32 / from_f32).
+// Scalar arguments, out of line: the hot loop keeps its accumulators in
+// registers and the rare exact path out of its instruction stream.
+static __device__ __noinline__ uint32_t f16_exact_one(float acc, float bias, uint32_t res, uint32_t flags) {
+    uint16_t x = f32_to_f16_ref(acc);
+    if (flags & 1u) x = f32_to_f16_ref(__fadd_rn(f16_to_f32_ref(x), bias));
+    if (flags & 2u) x = f32_to_f16_ref(__fadd_rn(f16_to_f32_ref(x), f16_to_f32_ref((uint16_t)res)));
+    if (flags & 4u) {
+        const float f = f16_to_f32_ref(x);
+        x = f32_to_f16_ref(f > 0.0f ? f : 0.0f);
     }
-    reinterpret_cast<uint4 *>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    reinterpret_cast<uint4 *>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    return x;
+}
+
+// The 16 outputs as 8 packed pairs in w.  `rw` = the 16 residual halves as 8
+// packed pairs (read when p.res_f16 is set).
+// kFm: bit 0 = bias, bit 1 = residual, bit 2 = ReLU (one kernel instance each).
+template <int kFm>
+__device__ __forceinline__ void f16_epilogue16(const int32_t (&v)[16], const ChanSmem *cs, int slot0,
+                                               const UmmaParams &p, const uint32_t (&rw)[8], uint32_t (&w)[8]) {
+    constexpr bool has_bias = kFm & 1, has_res = kFm & 2, relu = kFm & 4;
+    uint32_t bq[8];
+    if (has_bias) {
+        const uint4 b0 = reinterpret_cast<const uint4 *>(cs->d)[slot0 >> 3];
+        const uint4 b1 = reinterpret_cast<const uint4 *>(cs->d)[(slot0 >> 3) + 1];
+        bq[0] = b0.x; bq[1] = b0.y; bq[2] = b0.z; bq[3] = b0.w;
+        bq[4] = b1.x; bq[5] = b1.y; bq[6] = b1.z; bq[7] = b1.w;
+    }
+    uint32_t badbits = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        uint32_t o = h2_bits(__floats2half2_rn(__int_as_float(v[2 * k]), __int_as_float(v[2 * k + 1])));
+        uint32_t bad = 0;
+        if (has_bias) o = h2_bits(__hfma2(bits_h2(o), bits_h2(half_scale(h2_tiny_mask(o))), bits_h2(bq[k])));
+        if (has_res) {
+            const uint32_t r = rw[k];
+            const uint32_t my = h2_tiny_mask(o);
+            const uint32_t mr = h2_tiny_mask(r) & __hne2_mask(bits_h2(r), bits_h2(0u));  // nonzero subnormal
+            bad |= my & mr;
+            const uint32_t a = (mr & r) | (~mr & o), c = (mr & o) | (~mr & r);
+            o = h2_bits(__hfma2(bits_h2(a), bits_h2(half_scale(my | mr)), bits_h2(c)));
+        }
+        if (relu) {
+            const uint32_t pos = __hgt2_mask(bits_h2(o), bits_h2(0u));
+            o = h2_bits(__hmul2(bits_h2(o), bits_h2(half_scale(h2_tiny_mask(o))))) & pos;
+        } else {
+            bad |= __hneu2_mask(bits_h2(o), bits_h2(o));  // NaN: the reference keeps its payload bits
+        }
+        w[k] = o;
+        badbits |= (bad & 1u) << (2 * k) | ((bad >> 16) & 1u) << (2 * k + 1);
+    }
+    if (has_bias && (cs->cflags[slot0 >> 4] & 1u)) badbits = 0xFFFFu;  // a subnormal or NaN bias in this group
+    if (badbits) {
+        const uint32_t fl = (uint32_t)kFm;
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            if (badbits & (1u << j)) {
+                const uint32_t r = (rw[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+                const uint32_t h = f16_exact_one(__int_as_float(v[j]), cs->m[slot0 + j], r, fl);
+                w[j >> 1] = (j & 1) ? ((w[j >> 1] & 0x0000FFFFu) | (h << 16)) : ((w[j >> 1] & 0xFFFF0000u) | h);
+            }
+        }
+    }
+}
+
+// Address of 16-byte unit h (0 or 1) of fp16 chunk c (16 channels) of staging
+// row `row` in row block r.  Swizzled layout: [r][64-channel slab][128 rows]
+// [128 bytes], unit u of a row at (u ^ (row & 7)) * 16 -- the 128-byte TMA
+// swizzle, so the 32 rows a warp writes at once fall in distinct banks.
+__device__ __forceinline__ uint8_t *f16_stage_unit(uint8_t *out_stage, const UmmaParams &p, int r, int row, int c,
+                                                   int h) {
+    if (p.swz)
+        return out_stage + (size_t)r * kBM * p.bn * 2 + (size_t)(c >> 2) * (kBM * 128) + row * 128 +
+               ((((c & 3) * 2 + h) ^ (row & 7)) << 4);
+    return out_stage + ((size_t)(r * kBM + row) * p.bn + c * 16) * 2 + h * 16;
 }
 
 // Shared-memory matrix descriptor (K-major, swizzled): start address >> 4 in
@@ -477,10 +568,13 @@ __device__ __forceinline__ int valid_blocks(const UmmaParams &p, const TileCoord
     return left < p.R ? left : p.R;
 }
 
-template <bool kSilu, bool kF16>
+// kSilu: int8 SiLU epilogue.  kF16: fp16 operands (kind::f16) with the fp16
+// epilogue; kFm its bias / residual / ReLU flags.
+template <bool kSilu, bool kF16, int kFm>
 __global__ void __launch_bounds__(kThreads, 1)
     k_umma_conv_i8(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ UmmaParams p) {
+                   const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_r,
+                   const __grid_constant__ UmmaParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1 KiB-aligned base (swizzle patterns repeat every 1 KiB).
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -494,7 +588,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *tfull_bar = bars + 2 * kMaxStages;    // [2]
     uint64_t *tempty_bar = tfull_bar + 2;           // [2]
     uint64_t *drain_bar = tempty_bar + 2;           // [1] MMA drain on abort
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+    uint64_t *res_bar = drain_bar + 1;              // [1] fp16 residual tile landed in the staging buffer
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(res_bar + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -510,6 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&tempty_bar[a]), kEpiWarps);
         }
         mbar_init(smem_u32(drain_bar), 1);
+        mbar_init(smem_u32(res_bar), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -644,18 +740,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the slots one tile ahead (the global loads overlap the previous tile).
         if (!p.chan_all && (int)blockIdx.x < p.num_tiles)
             stage_channel(p, chan, et, tile_coord(p, blockIdx.x).n0 + et, et < p.bn);
+        // fp16 residual (flat mode): the tile's residual rows are brought into the
+        // staging buffer by TMA while the tile's MMAs run; each thread reads its
+        // 16 residual halves from the spot its 16 outputs then overwrite.
+        constexpr bool res_tma = kF16 && (kFm & 2);
+        uint32_t res_phase = 0;
+        bool res_pending = false;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
             const TileCoord tc = tile_coord(p, tile);
             const int slot_base = p.chan_all ? tc.n0 : acc * (kChanSlots / 2);
+            if (et == 0) {
+                bulk_wait_read0();  // the previous tile's stores have read the staging buffer
+                if (res_tma) {
+                    const int nrb = valid_blocks(p, tc);
+                    mbar_expect_tx(smem_u32(res_bar), (uint32_t)(nrb * kBM * p.bn * 2));
+                    const int slabs = p.swz ? p.bn / 64 : 1, sw_ch = p.swz ? 64 : p.bn;
+                    for (int r = 0; r < nrb; r++)
+                        for (int sl = 0; sl < slabs; sl++)
+                            tma_load_2d(smem_u32(out_stage + (size_t)r * kBM * p.bn * 2 + (size_t)sl * kBM * sw_ch * 2),
+                                        &tmap_r, smem_u32(res_bar), tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
+                    res_pending = true;
+                }
+            }
             bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), acc_ph, p, abort_flag, 4);
+            if (res_tma && ok) ok = mbar_wait(smem_u32(res_bar), res_phase, p, abort_flag, 5);
             // Barrier A (epilogue threads only): all-or-none abort decision; the
-            // staging buffer is free again (the store issuer waited for the
-            // previous stores' reads before arriving); this tile's staged
-            // channel parameters are visible.
-            if (et == 0) bulk_wait_read0();
-            if (named_barrier_or(1, kEpiWarps * 32, !ok)) break;
+            // staging buffer is free again and holds this tile's residual; this
+            // tile's staged channel parameters are visible.
+            if (named_barrier_or(1, kEpiWarps * 32, !ok)) {
+                if (et == 0 && res_pending) {  // let the residual copy land before the CTA exits
+                    const uint64_t t0 = globaltimer_ns();
+                    while (!mbar_try_wait(smem_u32(res_bar), res_phase) && globaltimer_ns() - t0 < p.wait_cap_ns) {
+                    }
+                }
+                break;
+            }
+            res_phase ^= 1u;
+            res_pending = false;
             if (!p.chan_all) {  // next tile's channels into the other half (its readers finished before barrier A)
                 const int next = tile + (int)gridDim.x;
                 if (next < p.num_tiles)
@@ -666,18 +789,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * acc_cols;
             // each half of the warps takes a contiguous run of (row block, chunk)
             // items, two TMEM loads in flight per wait; (r, c) advance without division.
-            if (p.R == 1) {  // one row block: contiguous chunk halves, one TMEM load per wait
+            if constexpr (kF16) {
+                // fp16: each half of the warps takes a contiguous run of (row block,
+                // chunk) items, four TMEM loads in flight per wait.
+                const int per = (items + 1) / 2;
+                const int i_begin = half * per, i_end = min(items, i_begin + per);
+                for (int i = i_begin; i < i_end; i += 4) {
+                    int32_t v[4][16];
+                    int rr[4], cc[4];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const int it = min(i + q, i_end - 1);  // warp-uniform (the loads are collective)
+                        rr[q] = it / chunks;
+                        cc[q] = it - rr[q] * chunks;
+                        tc_ld16(tacc + (uint32_t)(rr[q] * p.bn + cc[q] * 16), v[q]);
+                    }
+                    uint32_t rw[4][8];
+                    if (res_tma) {
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            const uint4 r0 = *reinterpret_cast<const uint4 *>(f16_stage_unit(out_stage, p, rr[q], row, cc[q], 0));
+                            const uint4 r1 = *reinterpret_cast<const uint4 *>(f16_stage_unit(out_stage, p, rr[q], row, cc[q], 1));
+                            rw[q][0] = r0.x; rw[q][1] = r0.y; rw[q][2] = r0.z; rw[q][3] = r0.w;
+                            rw[q][4] = r1.x; rw[q][5] = r1.y; rw[q][6] = r1.z; rw[q][7] = r1.w;
+                        }
+                    }
+                    tc_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        if (i + q < i_end) {
+                            uint32_t w[8];
+                            f16_epilogue16<kFm>(v[q], chan, slot_base + cc[q] * 16, p, rw[q], w);
+                            *reinterpret_cast<uint4 *>(f16_stage_unit(out_stage, p, rr[q], row, cc[q], 0)) =
+                                make_uint4(w[0], w[1], w[2], w[3]);
+                            *reinterpret_cast<uint4 *>(f16_stage_unit(out_stage, p, rr[q], row, cc[q], 1)) =
+                                make_uint4(w[4], w[5], w[6], w[7]);
+                        }
+                    }
+                }
+            } else if (p.R == 1) {  // one row block: contiguous chunk halves, one TMEM load per wait
                 const int per1 = (chunks + 1) / 2;
                 const int cb = half * per1, ce = min(chunks, cb + per1);
                 for (int c = cb; c < ce; c++) {
                     int32_t v[16];
                     tc_ld16(tacc + (uint32_t)(c * 16), v);
+                    uint8_t *dst = out_stage + (size_t)row * p.bn + c * 16;
                     tc_wait_ld();
-                    uint8_t *dst = out_stage + ((size_t)row * p.bn + c * 16) * (kF16 ? 2 : 1);
-                    if (kF16)
-                        f16_epilogue16(v, chan, slot_base + c * 16, p, dst);
-                    else
-                        *reinterpret_cast<uint4 *>(dst) = requant16<kSilu>(v, chan, slot_base + c * 16, p);
+                    *reinterpret_cast<uint4 *>(dst) = requant16<kSilu>(v, chan, slot_base + c * 16, p);
                 }
             } else {
             const int per = (items + 1) / 2;
@@ -692,18 +850,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int32_t v1[16], v2[16];
                 tc_ld16(tacc + (uint32_t)(r1 * p.bn + c1 * 16), v1);
                 tc_ld16(tacc + (uint32_t)(r2 * p.bn + c2 * 16), v2);
+                uint8_t *dst1 = out_stage + ((size_t)(r1 * kBM + row)) * p.bn + c1 * 16;
                 tc_wait_ld();
-                uint8_t *dst1 = out_stage + (((size_t)(r1 * kBM + row)) * p.bn + c1 * 16) * (kF16 ? 2 : 1);
-                if (kF16)
-                    f16_epilogue16(v1, chan, slot_base + c1 * 16, p, dst1);
-                else
-                    *reinterpret_cast<uint4 *>(dst1) = requant16<kSilu>(v1, chan, slot_base + c1 * 16, p);
+                *reinterpret_cast<uint4 *>(dst1) = requant16<kSilu>(v1, chan, slot_base + c1 * 16, p);
                 if (two) {
-                    uint8_t *dst2 = out_stage + (((size_t)(r2 * kBM + row)) * p.bn + c2 * 16) * (kF16 ? 2 : 1);
-                    if (kF16)
-                        f16_epilogue16(v2, chan, slot_base + c2 * 16, p, dst2);
-                    else
-                        *reinterpret_cast<uint4 *>(dst2) = requant16<kSilu>(v2, chan, slot_base + c2 * 16, p);
+                    uint8_t *dst2 = out_stage + ((size_t)(r2 * kBM + row)) * p.bn + c2 * 16;
+                    *reinterpret_cast<uint4 *>(dst2) = requant16<kSilu>(v2, chan, slot_base + c2 * 16, p);
                 }
                 c1 += 2;
                 while (c1 >= chunks) { c1 -= chunks; r1++; }
@@ -716,12 +868,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_barrier_sync(2, kEpiWarps * 32);
             if (et == 0) {
                 const int nrb = valid_blocks(p, tc);
+                const int slabs = (kF16 && p.swz) ? p.bn / 64 : 1, sw_ch = (kF16 && p.swz) ? 64 : p.bn;
                 for (int r = 0; r < nrb; r++) {
-                    const uint32_t src = smem_u32(out_stage + (size_t)r * kBM * p.bn * (kF16 ? 2 : 1));
-                    if (p.mode == 0)
-                        tma_store_2d(&tmap_y, src, tc.n0, (tc.mt * p.R + r) * kBM);
-                    else
-                        tma_store_4d(&tmap_y, src, tc.n0, tc.ow0, tc.oh0 + r * p.th, tc.img);
+                    for (int sl = 0; sl < slabs; sl++) {
+                        const uint32_t src = smem_u32(out_stage + (size_t)r * kBM * p.bn * (kF16 ? 2 : 1) +
+                                                      (size_t)sl * kBM * sw_ch * (kF16 ? 2 : 1));
+                        if (p.mode == 0)
+                            tma_store_2d(&tmap_y, src, tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
+                        else
+                            tma_store_4d(&tmap_y, src, tc.n0 + sl * sw_ch, tc.ow0, tc.oh0 + r * p.th, tc.img);
+                    }
                 }
                 bulk_commit();
             }
@@ -823,7 +979,8 @@ namespace {
 // Shared launcher: esize 1 = int8 (kind::i8, requant epilogue), 2 = fp16
 // (kind::f16, f16 epilogue with bias and ReLU).
 dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const void *x, const void *w_ohwi,
-                           const EpiParams &ep, void *y, int esize, const uint16_t *bias_f16, int relu) {
+                           const EpiParams &ep, void *y, int esize, const uint16_t *bias_f16, int relu,
+                           const uint16_t *res_f16) {
     const char *op = esize == 2 ? "conv2d_f16" : "conv2d_i8";
     if (((uintptr_t)x & 15) || ((uintptr_t)w_ohwi & 15) || ((uintptr_t)y & 15))
         return dw_fail(be, DW_ERR_INVALID_ARG, "%s (tensor-core path): buffers must be 16-byte aligned", op);
@@ -833,7 +990,11 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     p.mode = flat ? 0 : 1;
     p.esize = esize;
     p.bias_f16 = bias_f16;
+    p.res_f16 = res_f16;
     p.relu = relu;
+    p.swz = 0;
+    if (res_f16 && (!flat || ((uintptr_t)res_f16 & 15)))
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: a fused residual needs a 1x1 stride-1 conv and a 16-byte aligned buffer", op);
     p.n_img = d.n; p.ho = ho; p.wo = wo; p.c_out = d.c_out;
     p.taps = d.k_h * d.k_w; p.kw = d.k_w; p.sh = d.stride_h; p.sw = d.stride_w; p.pt = d.pad_t; p.pl = d.pad_l;
     p.c_in = d.c_in;
@@ -868,6 +1029,9 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         p.a_tx_bytes = (uint32_t)(p.tw * p.th * p.bk);
     }
     p.num_tiles = p.m_tiles * p.n_tiles;
+    // fp16 staging in swizzled 64-channel slabs (conflict-free epilogue stores)
+    // when every tile's channels split into whole slabs.
+    if (esize == 2 && p.bn % 64 == 0 && !getenv("DW_F16_NOSWZ")) p.swz = 1;
     p.chan_all = p.n_tiles * p.bn <= kChanSlots ? 1 : 0;  // every slot a tile reads lies in the arrays
     p.b_tx_bytes = (uint32_t)(p.bn * p.bk);
     p.a_stage_bytes = (uint32_t)al1k((size_t)p.R * kBM * p.bk);
@@ -935,43 +1099,66 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
     if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: weight tensor map rejected (%d)", op, (int)r);
-    // Output: TMA stores of the staged [rows][bn] tile; out-of-range rows/pixels/channels are clipped.
+    // Output: TMA stores of the staged [rows][bn] tile (swizzled fp16 staging:
+    // one store per 64-channel slab); out-of-range rows/pixels/channels are clipped.
     CUtensorMap ty;
+    const cuuint32_t st_ch = p.swz ? 64u : (cuuint32_t)p.bn;
+    const CUtensorMapSwizzle st_sw = p.swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
     if (flat) {
         cuuint64_t dims[2] = {(cuuint64_t)d.c_out, (cuuint64_t)p.rows};
         cuuint64_t strides[1] = {(cuuint64_t)d.c_out * es};
-        cuuint32_t box[2] = {(cuuint32_t)p.bn, (cuuint32_t)kBM};
+        cuuint32_t box[2] = {st_ch, (cuuint32_t)kBM};
         cuuint32_t estr[2] = {1, 1};
-        r = be->encode_tiled(&ty, dt, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        r = be->encode_tiled(&ty, dt, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, st_sw,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
         cuuint64_t dims[4] = {(cuuint64_t)d.c_out, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)d.n};
         cuuint64_t strides[3] = {(cuuint64_t)d.c_out * es, (cuuint64_t)wo * d.c_out * es,
                                  (cuuint64_t)ho * wo * d.c_out * es};
-        cuuint32_t box[4] = {(cuuint32_t)p.bn, (cuuint32_t)p.tw, (cuuint32_t)p.th, 1};
+        cuuint32_t box[4] = {st_ch, (cuuint32_t)p.tw, (cuuint32_t)p.th, 1};
         cuuint32_t estr[4] = {1, 1, 1, 1};
-        r = be->encode_tiled(&ty, dt, 4, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        r = be->encode_tiled(&ty, dt, 4, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, st_sw,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
     if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: output tensor map rejected (%d)", op, (int)r);
+    // fp16 residual: the output's 2-D view over the residual buffer (loads into the staging tile)
+    CUtensorMap tr = ty;
+    if (res_f16) {
+        cuuint64_t dims[2] = {(cuuint64_t)d.c_out, (cuuint64_t)p.rows};
+        cuuint64_t strides[1] = {(cuuint64_t)d.c_out * es};
+        cuuint32_t box[2] = {st_ch, (cuuint32_t)kBM};
+        cuuint32_t estr[2] = {1, 1};
+        r = be->encode_tiled(&tr, dt, 2, const_cast<uint16_t *>(res_f16), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, st_sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: residual tensor map rejected (%d)", op, (int)r);
+    }
 
+    using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, UmmaParams);
+    static const KernelFn f16_kernels[8] = {
+        k_umma_conv_i8<false, true, 0>, k_umma_conv_i8<false, true, 1>, k_umma_conv_i8<false, true, 2>,
+        k_umma_conv_i8<false, true, 3>, k_umma_conv_i8<false, true, 4>, k_umma_conv_i8<false, true, 5>,
+        k_umma_conv_i8<false, true, 6>, k_umma_conv_i8<false, true, 7>};
     static bool attr_set[16] = {};
     int dev = be->device;
     if (dev < 16 && !attr_set[dev]) {
-        cudaFuncSetAttribute(k_umma_conv_i8<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
-        cudaFuncSetAttribute(k_umma_conv_i8<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
-        cudaFuncSetAttribute(k_umma_conv_i8<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<false, false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<true, false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemLimit);
+        for (KernelFn f : f16_kernels)
+            cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
         attr_set[dev] = true;
     }
     const int grid = std::min(p.num_tiles, be->sm_count);
-    if (esize == 2)
-        k_umma_conv_i8<false, true><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
-    else if (ep.epilogue == DW_EPI_SILU)
-        k_umma_conv_i8<true, false><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
-    else
-        k_umma_conv_i8<false, false><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, p);
+    if (esize == 2) {
+        const int fm = (bias_f16 ? 1 : 0) | (res_f16 ? 2 : 0) | (relu ? 4 : 0);
+        f16_kernels[fm]<<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, tr, p);
+    } else if (ep.epilogue == DW_EPI_SILU) {
+        k_umma_conv_i8<true, false, 0><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, tr, p);
+    } else {
+        k_umma_conv_i8<false, false, 0><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, tr, p);
+    }
     return dw_after_launch(be, esize == 2 ? "umma_conv_f16" : "umma_conv_i8");
 }
 
@@ -979,13 +1166,14 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
 
 dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
                               const int8_t *w_ohwi, const EpiParams &ep, int8_t *y) {
-    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 1, nullptr, 0);
+    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 1, nullptr, 0, nullptr);
 }
 
 dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,
-                               const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y) {
+                               const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y,
+                               const uint16_t *residual) {
     EpiParams ep{nullptr, nullptr, nullptr, DW_EPI_NONE, 127, 0.0f};
-    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 2, bias, relu);
+    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 2, bias, relu, residual);
 }
 
 }  // namespace dw

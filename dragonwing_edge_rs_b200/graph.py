@@ -72,10 +72,10 @@ class Graph:
     def conv_ops(self):
         total = 0
         for op in self.ops:
-            if op.op_type in ("Conv2dRequantReluI8Nhwc", "Conv2dF16"):
+            if op.op_type in ("Conv2dRequantReluI8Nhwc", "Conv2dF16", "Conv2dAddF16"):
                 d: ConvDesc = op.params["desc"]
                 ho, wo = d.out_hw()
-                c_in = op.params.get("c_in_real", d.c_in)
+                c_in = op.params.get("c_in_real", d.c_in)  # a lowered conv counts its real channels
                 per = d.k_h * d.k_w * (c_in if d.group == 1 else 1)
                 total += 2 * d.n * ho * wo * d.c_out * per
             elif op.op_type == "GemmF16":
@@ -229,39 +229,30 @@ class F16GraphBuilder:
     def _f16(a):
         return np.asarray(a, np.float32).astype(np.float16)
 
-    def input_f32(self, name, shape, pad_channels_to=None):
-        """f32 NHWC graph input and its F16 conversion (runtime.rs:842-851).
-        With `pad_channels_to`, the f16 tensor carries extra zero channels so a
-        3-channel image meets the tensor-core kernel's channel alignment."""
+    def input_f32(self, name, shape):
+        """f32 NHWC graph input and its F16 conversion (runtime.rs:842-851)."""
         g = self.g
         g.add_tensor(name, shape, "f32")
         g.inputs.append(name)
         n, h, w, c = shape
-        c_dst = pad_channels_to or c
-        y = g.add_tensor(name + "_f16", (n, h, w, c_dst), "f16")
-        g.ops.append(CompiledOp("cast_input", "CastF32ToF16", [name], [y], {"c_src": c, "c_dst": c_dst}))
+        y = g.add_tensor(name + "_f16", (n, h, w, c), "f16")
+        g.ops.append(CompiledOp("cast_input", "CastF32ToF16", [name], [y], {"c_src": c, "c_dst": c}))
         return y
 
-    def conv(self, x, c_out, k=3, s=1, pad=None, relu=True, gamma=1.0, c_in_real=None, name=None):
+    def conv(self, x, c_out, k=3, s=1, pad=None, relu=True, gamma=1.0, name=None):
         g = self.g
         n, h, w, c_in = g.tensors[x].shape
-        c_real = c_in_real or c_in
         p = k // 2 if pad is None else pad
         name = name or self._name("conv")
-        wf = self.rng.normal(0.0, np.sqrt(2.0 / (k * k * c_real)), (k, k, c_real, c_out)).astype(np.float32)
+        wf = self.rng.normal(0.0, np.sqrt(2.0 / (k * k * c_in)), (k, k, c_in, c_out)).astype(np.float32)
         wf *= np.float32(gamma)
-        if c_real < c_in:  # zero weights for the padded input channels
-            wf = np.concatenate([wf, np.zeros((k, k, c_in - c_real, c_out), np.float32)], axis=2)
         bias = self.rng.normal(0.0, 0.05, c_out).astype(np.float32)
         desc = ConvDesc(n, h, w, c_in, c_out, k, k, s, s, (p, p, p, p), 1, L.EPI_RELU if relu else L.EPI_NONE)
         ho, wo = desc.out_hw()
         y = g.add_tensor(name + "_out", (n, ho, wo, c_out), "f16")
         g.initializers[name + "_w"] = self._f16(wf)
         g.initializers[name + "_b"] = self._f16(bias)
-        params = {"desc": desc}
-        if c_real < c_in:
-            params["c_in_real"] = c_real
-        g.ops.append(CompiledOp(name, "Conv2dF16", [x, name + "_w", name + "_b"], [y], params))
+        g.ops.append(CompiledOp(name, "Conv2dF16", [x, name + "_w", name + "_b"], [y], {"desc": desc}))
         return y
 
     def add_relu(self, a, b, name=None):
@@ -310,6 +301,133 @@ class F16GraphBuilder:
         return y
 
 
+def fuse_residual_f16(graph: Graph) -> Graph:
+    """Op-fusion pass for the fp16 path (the counterpart of the reference's
+    conv fusion, crates/dragonwing-core/src/fusion.rs): Conv2dF16 (no ReLU) ->
+    AddF16 (+ReLU) becomes one Conv2dAddF16 op whose epilogue adds the other
+    operand of the add and applies the add's ReLU.  The conv picked is a 1x1
+    stride-1 conv when the add has one (its epilogue fuses on the tensor
+    cores); the other operand's producer moves before it when needed.  Returns a
+    new Graph; the arithmetic is unchanged (conv, bias, add, ReLU in the same
+    order and rounding)."""
+    ops_ = list(graph.ops)
+    producer = {o: i for i, op in enumerate(ops_) for o in op.outputs}
+    consumers: dict = {}
+    for op in ops_:
+        for i in op.inputs:
+            consumers.setdefault(i, []).append(op)
+    tensors = dict(graph.tensors)
+    fused_any = True
+    while fused_any:
+        fused_any = False
+        for ai, add in enumerate(ops_):
+            if add.op_type != "AddF16":
+                continue
+            cands = []
+            for k, t in enumerate(add.inputs):
+                pi = producer.get(t)
+                if pi is None:
+                    continue
+                cv = ops_[pi]
+                if (cv.op_type != "Conv2dF16" or cv.params["desc"].epilogue != L.EPI_NONE
+                        or len(consumers.get(t, [])) != 1 or t in graph.outputs):
+                    continue
+                d = cv.params["desc"]
+                flat = d.k_h == 1 and d.k_w == 1 and d.stride_h == 1 and d.stride_w == 1 and d.pads == (0, 0, 0, 0)
+                cands.append((0 if flat else 1, pi, k))
+            if not cands:
+                continue
+            _, ci, k = min(cands)
+            cv = ops_[ci]
+            res = add.inputs[1 - k]
+            ri = producer.get(res, -1)
+            new_list = [op for j, op in enumerate(ops_) if j != ai]
+            conv_pos = new_list.index(cv)
+            if ri > ci:  # the residual is produced later: move its producer before the conv if it can be
+                rop = ops_[ri]
+                ready = all(producer.get(i, -1) < ci for i in rop.inputs if i in producer)
+                if not ready:
+                    continue
+                new_list.remove(rop)
+                conv_pos = new_list.index(cv)
+                new_list.insert(conv_pos, rop)
+                conv_pos += 1
+            d0 = cv.params["desc"]
+            d = ConvDesc(d0.n, d0.h, d0.w, d0.c_in, d0.c_out, d0.k_h, d0.k_w, d0.stride_h, d0.stride_w, d0.pads,
+                         d0.group, L.EPI_RELU if add.params.get("relu") else L.EPI_NONE)
+            params = dict(cv.params, desc=d)
+            fused = CompiledOp(cv.name + "+" + add.name, "Conv2dAddF16", list(cv.inputs) + [res], list(add.outputs),
+                               params)
+            new_list[conv_pos] = fused
+            tensors.pop(cv.outputs[0], None)
+            ops_ = new_list
+            producer = {o: i for i, op in enumerate(ops_) for o in op.outputs}
+            consumers = {}
+            for op in ops_:
+                for i in op.inputs:
+                    consumers.setdefault(i, []).append(op)
+            fused_any = True
+            break
+    return Graph(tensors, ops_, graph.initializers, list(graph.inputs), list(graph.outputs))
+
+
+def lower_unfold_stem_f16(graph: Graph) -> Graph:
+    """Device lowering of a network's first conv on a few-channel f16 image:
+    CastF32ToF16 (c channels, c % 8 != 0) -> Conv2dF16 (k_h x k_w, stride
+    (s_h, s_w)) becomes UnfoldF32ToF16 (the cast fused with a horizontal
+    unfold, c_u = k_w * c rounded up to 16 channels) -> Conv2dF16 (k_h x 1,
+    stride (s_h, 1)) whose kernel rows hold the k_w taps side by side.  The
+    products are the same, summed in the same (kh, kw, c) order; the tensor
+    cores then load rows of c_u channels instead of c (= 3).  Returns a new
+    Graph; the source graph keeps the reference ops."""
+    ops_ = list(graph.ops)
+    consumers: dict = {}
+    for op in ops_:
+        for i in op.inputs:
+            consumers.setdefault(i, []).append(op)
+    tensors, inits = dict(graph.tensors), dict(graph.initializers)
+    for ci, cast in enumerate(ops_):
+        if cast.op_type != "CastF32ToF16" or cast.params["c_dst"] % 8 == 0:
+            continue
+        users = consumers.get(cast.outputs[0], [])
+        if len(users) != 1 or users[0].op_type != "Conv2dF16" or cast.outputs[0] in graph.outputs:
+            continue
+        conv = users[0]
+        d = conv.params["desc"]
+        c = cast.params["c_src"]
+        if d.group != 1 or d.k_w == 1 or d.k_w * c > 64:
+            continue
+        _, wo = d.out_hw()
+        c_u = (d.k_w * c + 15) // 16 * 16
+        pt, pl, pb, pr = d.pads
+        if d.h % d.stride_h:
+            continue
+        u = cast.outputs[0] + "_unfold"
+        tensors[u] = TensorInfo(u, (d.n, d.h, wo, c_u), "f16")
+        tensors.pop(cast.outputs[0], None)
+        w = graph.initializers[conv.inputs[1]].view(np.uint16).reshape(d.k_h, d.k_w * c, d.c_out)
+        wu = np.zeros((d.k_h, 1, c_u, d.c_out), np.uint16)
+        wu[:, 0, :d.k_w * c, :] = w
+        inits[conv.inputs[1] + "_unfold"] = wu.view(np.float16)
+        unfold = CompiledOp(cast.name + "_unfold", "UnfoldF32ToF16", list(cast.inputs), [u],
+                            {"k_w": d.k_w, "stride_w": d.stride_w, "pad_l": pl, "w_out": wo, "c_src": c, "c_dst": c_u})
+        d2 = ConvDesc(d.n, d.h, wo, c_u, d.c_out, d.k_h, 1, d.stride_h, 1, (pt, 0, pb, 0), 1, d.epilogue)
+        conv2 = CompiledOp(conv.name, "Conv2dF16", [u, conv.inputs[1] + "_unfold"] + list(conv.inputs[2:]),
+                           list(conv.outputs), dict(conv.params, desc=d2, c_in_real=c * d.k_w))
+        ops_ = [unfold if op is cast else conv2 if op is conv else op for op in ops_]
+        break  # a network has one such input conv
+    return Graph(tensors, ops_, inits, list(graph.inputs), list(graph.outputs))
+
+
+def lower_for_device(graph: Graph) -> Graph:
+    """The device passes: residual fusion, then the input-conv unfold."""
+    if any(op.op_type == "AddF16" for op in graph.ops):
+        graph = fuse_residual_f16(graph)
+    if any(op.op_type == "CastF32ToF16" for op in graph.ops):
+        graph = lower_unfold_stem_f16(graph)
+    return graph
+
+
 # ---------------------------------------------------------------------------
 # network builders (synthetic weights with the published architectures' shapes)
 # ---------------------------------------------------------------------------
@@ -319,12 +437,12 @@ def resnet50_fp16(batch=128, size=224, classes=1000, seed=50, stages=(3, 4, 6, 3
     stages [3, 4, 6, 3] at output widths 256/512/1024/2048 (stride 2 in the 3x3
     conv of each stage's first block, 1x1 projection shortcut there), BN folded
     into every conv, ReLU, global average pool, FC to `classes`.  Input f32 NHWC
-    (3 channels, zero-padded to 16 in its f16 copy); output f32 logits.  The
+    (3 channels); output f32 logits.  The
     last conv of each residual branch carries a folded-BN scale of 0.5 so the
     residual stream of random weights stays well inside the f16 range."""
     b = F16GraphBuilder(seed)
-    x = b.input_f32("image", (batch, size, size, 3), pad_channels_to=16)
-    x = b.conv(x, 64, k=7, s=2, c_in_real=3, name="stem")
+    x = b.input_f32("image", (batch, size, size, 3))
+    x = b.conv(x, 64, k=7, s=2, name="stem")
     x = b.maxpool(x, 3, 2, 1, name="stem_pool")
     c = 64
     for si, (nb, width) in enumerate(zip(stages, (64, 128, 256, 512))):
@@ -447,7 +565,9 @@ class CudaGraphRuntime:
     """Executes a Graph on one GPU (VulkanGraphRuntime::new / set_input_bytes /
     run / get_output_bytes, vulkan_runtime.rs:115, 359)."""
 
-    def __init__(self, graph: Graph, backend: CudaBackend):
+    def __init__(self, graph: Graph, backend: CudaBackend, fuse: bool = True):
+        if fuse:
+            graph = lower_for_device(graph)
         self.graph = graph
         self.be = backend
         self.bufs: dict[str, CudaBuffer] = {}
@@ -514,6 +634,12 @@ class CudaGraphRuntime:
             n, h, w, _ = self.graph.tensors[op.inputs[0]].shape
             cs, cd = op.params["c_src"], op.params["c_dst"]
             return lambda: ops.cast_f32_to_f16(be, x, y, n * h * w, cs, cd)
+        if t == "UnfoldF32ToF16":
+            x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
+            n, h, w, c = self.graph.tensors[op.inputs[0]].shape
+            pr = op.params
+            return lambda: ops.unfold_w_f32_to_f16(be, x, y, n, h, w, c, pr["k_w"], pr["stride_w"], pr["pad_l"],
+                                                   pr["w_out"], pr["c_dst"])
         if t == "Conv2dF16":
             desc = op.params["desc"]
             x, wn, bn = op.inputs
@@ -521,6 +647,13 @@ class CudaGraphRuntime:
             consts[wn + "_prep"] = wp
             bx, bb, y = bufs[x], consts[bn], bufs[op.outputs[0]]
             return lambda: ops.conv2d_f16(be, desc, bx, wp, bb, y)
+        if t == "Conv2dAddF16":
+            desc = op.params["desc"]
+            x, wn, bn, rn = op.inputs
+            wp = ops.prepare_weights_f16(be, desc, consts[wn])
+            consts[wn + "_prep"] = wp
+            bx, bb, br, y = bufs[x], consts[bn], bufs[rn], bufs[op.outputs[0]]
+            return lambda: ops.conv2d_add_f16(be, desc, bx, wp, bb, br, y)
         if t == "AddF16":
             a, b_ = bufs[op.inputs[0]], bufs[op.inputs[1]]
             y = bufs[op.outputs[0]]

@@ -216,6 +216,15 @@ def conv2d_f16(backend: CudaBackend, desc: ConvDesc, x: CudaBuffer, w_prep: Cuda
                                           y.handle))
 
 
+def conv2d_add_f16(backend: CudaBackend, desc: ConvDesc, x: CudaBuffer, w_prep: CudaBuffer, bias, residual,
+                   y: CudaBuffer):
+    """fp16 conv + bias, then + residual (add_fp16), then ReLU if desc.epilogue
+    is EPI_RELU: the Conv -> Add -> Relu of a residual block in one op."""
+    d = desc.to_c()
+    backend._check(L.load().dw_conv2d_add_f16(backend.handle, ctypes.byref(d), x.handle, w_prep.handle, _h(bias),
+                                              residual.handle, y.handle))
+
+
 def prepare_gemm_b_f16(backend: CudaBackend, b_kn: CudaBuffer, k: int, n: int) -> CudaBuffer:
     out = ctypes.c_void_p()
     backend._check(L.load().dw_prepare_gemm_b_f16(backend.handle, b_kn.handle, k, n, ctypes.byref(out)))
@@ -245,3 +254,10 @@ def cast_f32_to_f16(backend, x, y, pixels, c_src, c_dst=None):
 
 def cast_f16_to_f32(backend, x, y):
     backend._check(L.load().dw_cast_f16_to_f32(backend.handle, x.handle, y.handle))
+
+
+def unfold_w_f32_to_f16(backend, x, y, n, h, w, c, k_w, stride_w, pad_l, w_out, c_dst):
+    """Horizontal unfold + F16 conversion of a few-channel f32 image (the
+    first conv's input layout for the tensor cores; contract in include/dw_cuda.h)."""
+    backend._check(L.load().dw_unfold_w_f32_to_f16(backend.handle, x.handle, y.handle, n, h, w, c, k_w, stride_w,
+                                                   pad_l, w_out, c_dst))

@@ -270,6 +270,14 @@ DW_API dw_status dw_prepare_weights_f16(dw_backend *be, const dw_conv_desc *d, c
  * == 0; other shapes run the direct kernel unless the path is DW_PATH_UMMA. */
 DW_API dw_status dw_conv2d_f16(dw_backend *be, const dw_conv_desc *d, const dw_buf *x, const dw_buf *w_prep,
                                const dw_buf *bias_or_null, dw_buf *y);
+/* dw_conv2d_f16 followed by the residual add of a bottleneck block, fused:
+ * y = relu?(from_f32(to_f32(conv_bias) + to_f32(residual))), i.e. the CPU
+ * runtime's Conv -> Add (add_fp16, cpu ops.rs:434-446) -> Relu sequence with
+ * the ReLU (d->epilogue == DW_EPI_RELU) applied after the add.  residual has
+ * y's shape and must not alias it.  The tensor-core kernel fuses the add into
+ * its epilogue for 1x1 stride-1 convs; other shapes add in a second pass. */
+DW_API dw_status dw_conv2d_add_f16(dw_backend *be, const dw_conv_desc *d, const dw_buf *x, const dw_buf *w_prep,
+                                   const dw_buf *bias_or_null, const dw_buf *residual, dw_buf *y);
 /* conv2d_fp16_nhwc (crates/dragonwing-vulkan/src/ops.rs:1385-1420): the
  * reference's parameter list, HWIO kernel, symmetric pads, no bias. */
 DW_API dw_status dw_conv2d_fp16_nhwc(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio,
@@ -303,6 +311,18 @@ DW_API dw_status dw_global_avgpool_f16(dw_backend *be, const dw_buf *x, dw_buf *
  * F16 input conversion, runtime.rs:842-851); channels c_src..c_dst-1 are 0. */
 DW_API dw_status dw_cast_f32_to_f16(dw_backend *be, const dw_buf *x_f32, dw_buf *y_f16, size_t pixels,
                                     size_t c_src, size_t c_dst);
+/* Horizontal unfold fused with the F16 input conversion, for the first conv
+ * of a network on a few-channel image: y[n][r][j][q*c + ch] =
+ * from_f32(x[n][r][j*stride_w + q - pad_l][ch]) for q < k_w (0 outside the
+ * image), channels k_w*c .. c_dst-1 zero; y is [n, h, w_out, c_dst] f16.  A
+ * k_h x k_w conv with stride (s_h, stride_w) and pads (t, pad_l, b, r) on x
+ * equals a k_h x 1 conv with stride (s_h, 1), pads (t, 0, b, 0) on y whose
+ * kernel [kh][0][q*c + ch][oc] = original [kh][q][ch][oc] (zero rows for the
+ * padding channels): the same products, fed to the tensor cores in rows of
+ * k_w*c channels. */
+DW_API dw_status dw_unfold_w_f32_to_f16(dw_backend *be, const dw_buf *x_f32, dw_buf *y_f16, size_t n, size_t h,
+                                        size_t w, size_t c, size_t k_w, size_t stride_w, size_t pad_l, size_t w_out,
+                                        size_t c_dst);
 /* f16 -> f32 with F16::to_f32. */
 DW_API dw_status dw_cast_f16_to_f32(dw_backend *be, const dw_buf *x_f16, dw_buf *y_f32);
 

@@ -9,17 +9,16 @@ maxpool2d (ops.rs:1513-1551), Concat/Split to concat_f32/split_f32 on int8
 bytes (ops.rs:2141-2246, 2407), Resize to resize_f32 Nearest (ops.rs:2320-2348),
 QuantizeU8 to u8*(1/255) -> quantize_f32_to_i8 (ops.rs:3503-3525).
 
-fp16 graphs follow the reference's F16 CPU runtime: CastF32ToF16 is the input
+UnfoldF32ToF16 (a device lowering of the input conv, see
+dragonwing_edge_rs_b200.graph.lower_unfold_stem_f16) is the input conversion
+laid out as a horizontal unfold.  fp16 graphs follow the reference's F16 CPU
+runtime: CastF32ToF16 is the input
 conversion (runtime.rs:842-851), Conv2dF16 is conv2d_fp16_nhwc (ops.rs:1442-1511)
 plus the runtime's bias and Relu steps (runtime.rs:1483-1497, 967-971),
 AddF16 is add_fp16 (ops.rs:434-446) + Relu, MaxPoolF16 and
 GlobalAveragePoolF16 are runtime.rs:1545-1563 and 1155-1170, GemmF16 is
 gemm_fp16 (ops.rs:461-481) + the bias step (runtime.rs:1264-1275).  fp16
-tensors are held as uint16 bit patterns.  A CastF32ToF16 that pads channels
-(for the device kernels' alignment) is run without the padding here, and the
-conv that consumes it uses only its real input channels (`c_in_real`), so the
-CPU does exactly the reference's work.
-"""
+tensors are held as uint16 bit patterns.  """
 from __future__ import annotations
 
 import numpy as np
@@ -88,8 +87,16 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
         elif t == "CastF32ToF16":
             x = vals[op.inputs[0]]
             vals[op.outputs[0]] = dwref.f16_from_f32_array(x).reshape(x.shape)
+        elif t == "UnfoldF32ToF16":
+            vals[op.outputs[0]] = unfold_f16_op(op, vals[op.inputs[0]])
         elif t == "Conv2dF16":
             vals[op.outputs[0]] = conv_f16_op(graph, op, vals[op.inputs[0]], threads)
+        elif t == "Conv2dAddF16":  # Conv2dF16 (no ReLU) -> AddF16 (ReLU per desc), fused on the device
+            y = conv_f16_op(graph, op, vals[op.inputs[0]], threads, relu=False)
+            y = dwref.add_f16(y, vals[op.inputs[3]])
+            if op.params["desc"].epilogue == dwref.EPI_RELU:
+                y = dwref.relu_f16(y)
+            vals[op.outputs[0]] = y.reshape(shape_of(op.outputs[0]))
         elif t == "AddF16":
             a, b = vals[op.inputs[0]], vals[op.inputs[1]]
             y = dwref.add_f16(a, b)
@@ -116,18 +123,17 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
     return {name: vals[name] for name in graph.outputs}
 
 
-def conv_f16_op(graph, op, x, threads=1):
-    """One Conv2dF16 op on uint16 NHWC input `x` (its real channels only)."""
+def conv_f16_op(graph, op, x, threads=1, relu=None):
+    """One Conv2dF16 op on uint16 NHWC input `x` (its real channels only);
+    `relu` overrides the descriptor's epilogue."""
     d = op.params["desc"]
-    n, h, w, c_x = x.shape
-    c_in = op.params.get("c_in_real", d.c_in)
-    if c_x != c_in:  # a device-side tensor with zero padding channels
-        x = np.ascontiguousarray(x[..., :c_in])
-    wt = graph.initializers[op.inputs[1]].view(np.uint16)[:, :, :c_in, :]
+    n, h, w, c_in = x.shape
+    wt = graph.initializers[op.inputs[1]].view(np.uint16)
     bias = graph.initializers[op.inputs[2]].view(np.uint16)
     pt, pl, pb, pr = d.pads
     assert pt == pb and pl == pr, "the CPU conv takes symmetric pads"
-    relu = d.epilogue == dwref.EPI_RELU
+    if relu is None:
+        relu = d.epilogue == dwref.EPI_RELU
     ho, wo = d.out_hw()
     if d.group == 1:
         y = dwref.conv2d_f16(x, wt, bias, relu, n, h, w, c_in, d.c_out, d.k_h, d.k_w, d.stride_h, d.stride_w,
@@ -146,3 +152,17 @@ def gemm_f16_op(graph, op, x, threads=1):
     bias = graph.initializers[op.inputs[2]].view(np.uint16)
     y = dwref.gemm_f16(x, wt, m, n, k, threads)
     return dwref.bias_relu_f16(y, bias, False, m, n).reshape(m, n)
+
+
+def unfold_f16_op(op, x):
+    """UnfoldF32ToF16 on an f32 NHWC array: y[n,r,j,q*c+ch] = from_f32(x[n,r,j*sw+q-pl,ch])."""
+    pr = op.params
+    n, h, w, c = x.shape
+    kw, sw, pl, wo, cd = pr["k_w"], pr["stride_w"], pr["pad_l"], pr["w_out"], pr["c_dst"]
+    xp = np.zeros((n, h, w + kw + sw * wo, c), np.float32)
+    xp[:, :, pl:pl + w, :] = x
+    y = np.zeros((n, h, wo, cd), np.uint16)
+    for q in range(kw):
+        cols = xp[:, :, q:q + sw * wo:sw, :][:, :, :wo, :]
+        y[..., q * c:(q + 1) * c] = dwref.f16_from_f32_array(cols).reshape(n, h, wo, c)
+    return y

@@ -5,9 +5,11 @@ add / add+ReLU / ReLU / max pool / global average pool, the direct and
 depthwise convolutions (same f32 FMA order as ops.rs:1442-1511, 2819-2937).
 
 Tolerance (the tensor-core conv/GEMM sum in another order): per layer, fed
-identical inputs, max |gpu - cpu| <= 5e-3 * max |cpu| and at most 0.1% of
-elements more than 1 f16 ulp apart; whole-network logits within 5e-2 of
-max |logit|."""
+identical inputs, max |gpu - cpu| <= 5e-3 * max |cpu| and a relative L2 error
+<= 1e-3; whole-network logits within 5e-2 of max |logit|.  The ULP histogram
+is printed: both sides round an f32 sum to f16, and the CPU's sequential f32
+sum carries its own error (about sqrt(K) * 2^-24 of the sum of |terms|), so
+outputs that cancel to small values can sit several f16 ulps apart."""
 import numpy as np
 import pytest
 
@@ -17,13 +19,13 @@ from dragonwing_edge_rs_b200 import ops
 from dragonwing_edge_rs_b200.backend import BackendError
 from dragonwing_edge_rs_b200.ops import ConvDesc
 from oracle import dwref
-from oracle.graph_ref import conv_f16_op, gemm_f16_op, run_graph
+from oracle.graph_ref import conv_f16_op, gemm_f16_op, run_graph, unfold_f16_op
 
 pytestmark = pytest.mark.gpu
 
 LAYER_REL_TOL = 5e-3      # docs/parity-testing.md:120 (per layer, relative)
 LOGITS_REL_TOL = 5e-2     # docs/parity-testing.md:138 (network output, relative)
-MAX_FRAC_OVER_1ULP = 1e-3
+LAYER_REL_L2_TOL = 1e-3
 
 
 @pytest.fixture(scope="module")
@@ -74,10 +76,13 @@ def tol_check(got, exp, what):
     e = exp.view(np.float16).astype(np.float64)
     scale = np.abs(e).max()
     err = np.abs(g - e).max()
-    over = float(np.mean(ulp_diff(got, exp) > 1))
-    msg = f"{what}: max|d|={err:.3g} max|ref|={scale:.3g} rel={err / max(scale, 1e-30):.3g} >1ulp={over:.2e}"
+    l2 = np.linalg.norm(g - e) / max(np.linalg.norm(e), 1e-30)
+    u = ulp_diff(got, exp)
+    hist = [float(np.mean(u == 0)), float(np.mean(u == 1)), float(np.mean(u == 2)), float(np.mean(u > 2))]
+    msg = (f"{what}: max|d|={err:.3g} max|ref|={scale:.3g} rel={err / max(scale, 1e-30):.3g} relL2={l2:.3g} "
+           f"ulp 0/1/2/>2 = {hist[0]:.4f}/{hist[1]:.4f}/{hist[2]:.4f}/{hist[3]:.4f}")
     assert np.isfinite(g).all() and err <= LAYER_REL_TOL * scale, msg
-    assert over <= MAX_FRAC_OVER_1ULP, msg
+    assert l2 <= LAYER_REL_L2_TOL, msg
     return msg
 
 
@@ -152,6 +157,22 @@ def test_cast_pads_channels_with_zero(be):
     assert not got[:, 3:].any()
 
 
+@pytest.mark.parametrize("geo", [(2, 224, 224, 3, 7, 2, 3, 112, 32), (1, 9, 13, 3, 3, 1, 1, 13, 16),
+                                 (1, 8, 10, 5, 2, 2, 0, 5, 16)])
+def test_unfold_w_f32_to_f16(be, geo):
+    n, h, w, c, kw, sw, pl, wo, cd = geo
+    rng = np.random.default_rng(sum(geo))
+    x = rng.standard_normal((n, h, w, c)).astype(np.float32)
+    bx, by = be.upload_array(x), be.alloc(2 * n * h * wo * cd)
+    ops.unfold_w_f32_to_f16(be, bx, by, n, h, w, c, kw, sw, pl, wo, cd)
+    got = be.download_array(by, np.uint16)
+
+    class _Op:
+        params = {"k_w": kw, "stride_w": sw, "pad_l": pl, "w_out": wo, "c_dst": cd}
+    exp = unfold_f16_op(_Op, x).ravel()
+    assert np.array_equal(got, exp), bits_report(got, exp)
+
+
 # ------------------------------------------------------------- glue (bit-exact)
 
 def glue_data(rng, n):
@@ -197,7 +218,7 @@ def test_relu_f16_unaligned_view(be):
     rng = np.random.default_rng(12)
     x = glue_data(rng, 1001)
     big = be.upload_array(np.concatenate([np.zeros(1, np.uint16), x]))
-    view = be.wrap(big.device_ptr() + 2, 2 * x.size)
+    view = be.wrap(big.device_ptr + 2, 2 * x.size)
     ops.relu_fp16(be, view)
     got = be.download_array(big, np.uint16)[1:]
     assert np.array_equal(got, dwref.relu_f16(x))
@@ -305,6 +326,72 @@ def test_conv_f16_inf_input_stays_local(be_umma):
     assert np.array_equal(nonfinite_got.any(axis=2), nonfinite_exp.any(axis=2))
 
 
+@pytest.mark.parametrize("case", [(2, 28, 28, 64, 256, 1, 1, 0, True), (2, 28, 28, 64, 256, 1, 1, 0, False),
+                                  (1, 28, 28, 64, 128, 1, 2, 0, True), (1, 14, 14, 32, 32, 3, 1, 1, True)])
+def test_conv_add_f16_equals_conv_then_add(be, case):
+    """The fused residual epilogue gives the same bits as conv2d_f16 (no ReLU)
+    followed by add_fp16 (+relu_fp16)."""
+    n, h, w, ci, co, k, s, p, relu = case
+    rng = np.random.default_rng(sum(case) + 7)
+    desc = ConvDesc(n, h, w, ci, co, k, k, s, s, (p,) * 4, 1, dw.EPI_RELU if relu else dw.EPI_NONE)
+    x, wt, b = conv_inputs(rng, desc)
+    ho, wo = desc.out_hw()
+    r = h16(rng, n * ho * wo * co, 2.0)
+    bx, bw, bb, br = be.upload_array(x), be.upload_array(wt), be.upload_array(b), be.upload_array(r)
+    wp = ops.prepare_weights_f16(be, desc, bw)
+    by = be.alloc(2 * n * ho * wo * co)
+    ops.conv2d_add_f16(be, desc, bx, wp, bb, br, by)
+    fused = be.download_array(by, np.uint16)
+    d0 = ConvDesc(n, h, w, ci, co, k, k, s, s, (p,) * 4, 1, dw.EPI_NONE)
+    tmp = be.alloc(2 * n * ho * wo * co)
+    ops.conv2d_f16(be, d0, bx, wp, bb, tmp)
+    (ops.add_relu_fp16 if relu else ops.add_fp16)(be, tmp, br, by)
+    two = be.download_array(by, np.uint16)
+    assert np.array_equal(fused, two), bits_report(fused, two)
+    conv = be.download_array(tmp, np.uint16)
+    exp = dwref.add_f16(conv, r)
+    exp = dwref.relu_f16(exp) if relu else exp
+    assert np.array_equal(fused, exp), bits_report(fused, exp)
+
+
+@pytest.mark.parametrize("bias_kind", ["subnormal", "normal"])
+@pytest.mark.parametrize("relu", [False, True])
+@pytest.mark.parametrize("residual", [False, True])
+def test_f16_epilogue_subnormal_operands_bit_exact(be_umma, relu, residual, bias_kind):
+    """Inputs on a 2^-12 grid make every sum exact in f32 on both sides, so the
+    tensor-core result must equal the CPU's bit for bit -- including outputs,
+    biases and residuals that are f16 subnormals, which F16::to_f32 halves
+    (the packed path scales such operands by 0.5 inside an FMA; subnormal
+    biases take the exact path)."""
+    rng = np.random.default_rng(40 + relu + 2 * residual + 4 * (bias_kind == "normal"))
+    n, h, w, ci, co = 1, 16, 16, 16, 64
+    desc = ConvDesc(n, h, w, ci, co, 1, 1, 1, 1, (0,) * 4, 1, dw.EPI_RELU if relu else dw.EPI_NONE)
+    x = (rng.integers(-8, 9, n * h * w * ci) * 2.0 ** -12).astype(np.float16).view(np.uint16)
+    wt = (rng.integers(-8, 9, ci * co) * 2.0 ** -12).astype(np.float16).view(np.uint16)
+    b = (rng.integers(-600, 601, co) * 2.0 ** -24).astype(np.float16).view(np.uint16)
+    b[::5] = (rng.standard_normal(len(b[::5])) * 1e-3).astype(np.float16).view(np.uint16)
+    if bias_kind == "normal":  # normal biases of the outputs' size: the packed path handles every element
+        b = (np.sign(rng.standard_normal(co)) * rng.uniform(2.0 ** -14, 2.0 ** -12, co)).astype(np.float16)
+        b = b.view(np.uint16)
+    bx, bw, bb = be_umma.upload_array(x), be_umma.upload_array(wt), be_umma.upload_array(b)
+    wp = ops.prepare_weights_f16(be_umma, desc, bw)
+    by = be_umma.alloc(2 * n * h * w * co)
+    if residual:
+        r = (rng.integers(-900, 901, n * h * w * co) * 2.0 ** -24).astype(np.float16).view(np.uint16)
+        ops.conv2d_add_f16(be_umma, desc, bx, wp, bb, be_umma.upload_array(r), by)
+        conv = dwref.conv2d_f16(x, wt, b, False, n, h, w, ci, co, 1, 1, 1, 1, 0, 0)
+        exp = dwref.add_f16(conv, r)
+        exp = dwref.relu_f16(exp) if relu else exp
+    else:
+        ops.conv2d_f16(be_umma, desc, bx, wp, bb, by)
+        exp = dwref.conv2d_f16(x, wt, b, relu, n, h, w, ci, co, 1, 1, 1, 1, 0, 0)
+    got = be_umma.download_array(by, np.uint16)
+    pre = dwref.conv2d_f16(x, wt, None, False, n, h, w, ci, co, 1, 1, 1, 1, 0, 0)  # the conv before its bias
+    sub = np.mean(((pre & 0x7C00) == 0) & ((pre & 0x3FF) != 0))
+    assert sub > 0.2, f"test data should produce many subnormal conv results ({sub:.2f})"
+    assert np.array_equal(got, exp), bits_report(got, exp)
+
+
 def test_shim_conv2d_fp16_nhwc_matches_conv2d_f16(be):
     rng = np.random.default_rng(31)
     desc = ConvDesc(2, 28, 28, 64, 64, 3, 3, 1, 1, (1,) * 4, 1, dw.EPI_NONE)
@@ -362,7 +449,18 @@ def _per_layer_check(g, rt):
     for op in g.ops:
         t = op.op_type
         out = op.outputs[0]
-        if t == "Conv2dF16":
+        if t == "UnfoldF32ToF16":
+            x = rt.get_output(op.inputs[0])
+            got = rt.get_output(out).view(np.uint16).ravel()
+            assert np.array_equal(got, unfold_f16_op(op, x).ravel()), op.name
+        elif t == "Conv2dAddF16":
+            x = rt.get_output(op.inputs[0]).view(np.uint16)
+            r = rt.get_output(op.inputs[3]).view(np.uint16)
+            got = rt.get_output(out).view(np.uint16).ravel()
+            y = dwref.add_f16(conv_f16_op(g, op, x, threads=dwref.num_cpus(), relu=False).ravel(), r.ravel())
+            exp = dwref.relu_f16(y) if op.params["desc"].epilogue == dw.EPI_RELU else y
+            tol_check(got, exp, op.name)
+        elif t == "Conv2dF16":
             x = rt.get_output(op.inputs[0]).view(np.uint16)
             got = rt.get_output(out).view(np.uint16).ravel()
             exp = conv_f16_op(g, op, x, threads=dwref.num_cpus()).ravel()
@@ -398,7 +496,9 @@ def test_resnet50_fp16_small_batch_per_layer_and_logits(be):
     rt = G.CudaGraphRuntime(g, be)
     rt.set_input_bytes("image", x)
     rt.run()
-    worst = _per_layer_check(g, rt)
+    assert sum(op.op_type == "Conv2dAddF16" for op in rt.graph.ops) == 16  # every residual add fused
+    assert rt.graph.ops[0].op_type == "UnfoldF32ToF16"  # the stem's input is unfolded for the tensor cores
+    worst = _per_layer_check(rt.graph, rt)
     logits = rt.get_output("logits")
     ref = run_graph(g, {"image": x}, threads=dwref.num_cpus())["logits"]
     rel = np.abs(logits - ref).max() / np.abs(ref).max()
@@ -415,7 +515,7 @@ def test_resnet50_fp16_full_size_logits_and_graph_replay(be):
     rt.run()
     eager = rt.get_output("logits").copy()
     launches = rt.capture()
-    assert launches >= len(g.ops)
+    assert launches >= len(rt.graph.ops)
     rt.run()
     assert np.array_equal(rt.get_output("logits"), eager)
     ref = run_graph(g, {"image": x}, threads=dwref.num_cpus(), batch_slice=(1, 2))["logits"]
