@@ -44,7 +44,7 @@ struct UmmaParams {
     // geometry
     int mode;            // 0 = flat GEMM rows, 1 = spatial tiles
     int n_img, ho, wo, c_out;
-    int tw, th;          // spatial tile (tw*th <= 128)
+    int tw, th, nb;      // spatial tile: tw x th pixels of nb images (tw*th*nb <= 128; nb > 1 only for whole images)
     int tiles_w, tiles_h;
     int m_tiles, n_tiles, num_tiles;
     long long rows;      // flat mode: total pixels
@@ -511,18 +511,6 @@ __device__ __forceinline__ void f16_epilogue16(const int32_t (&v)[16], const Cha
     }
 }
 
-// Address of 16-byte unit h (0 or 1) of fp16 chunk c (16 channels) of staging
-// row `row` in row block r.  Swizzled layout: [r][64-channel slab][128 rows]
-// [128 bytes], unit u of a row at (u ^ (row & 7)) * 16 -- the 128-byte TMA
-// swizzle, so the 32 rows a warp writes at once fall in distinct banks.
-__device__ __forceinline__ uint8_t *f16_stage_unit(uint8_t *out_stage, const UmmaParams &p, int r, int row, int c,
-                                                   int h) {
-    if (p.swz)
-        return out_stage + (size_t)r * kBM * p.bn * 2 + (size_t)(c >> 2) * (kBM * 128) + row * 128 +
-               ((((c & 3) * 2 + h) ^ (row & 7)) << 4);
-    return out_stage + ((size_t)(r * kBM + row) * p.bn + c * 16) * 2 + h * 16;
-}
-
 // Shared-memory matrix descriptor (K-major, swizzled): start address >> 4 in
 // bits [0,14); leading-byte offset (unused for swizzled K-major) = 1; the
 // constant high word (stride-byte offset = 8 rows * row bytes, version 1,
@@ -550,7 +538,7 @@ __device__ __forceinline__ TileCoord tile_coord(const UmmaParams &p, int tile) {
         const int tw_i = t.mt % p.tiles_w;
         const int t2 = t.mt / p.tiles_w;
         t.oh0 = (t2 % p.tiles_h) * p.th * p.R;
-        t.img = t2 / p.tiles_h;
+        t.img = (t2 / p.tiles_h) * p.nb;
         t.ow0 = tw_i * p.tw;
     }
     return t;
@@ -791,27 +779,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             // items, two TMEM loads in flight per wait; (r, c) advance without division.
             if constexpr (kF16) {
                 // fp16: each half of the warps takes a contiguous run of (row block,
-                // chunk) items, four TMEM loads in flight per wait.
+                // chunk) items, four TMEM loads in flight per wait; (r, c) advance
+                // without division.
                 const int per = (items + 1) / 2;
                 const int i_begin = half * per, i_end = min(items, i_begin + per);
+                int r0 = i_begin / chunks, c0 = i_begin - (i_begin / chunks) * chunks;
+                const uint32_t r7 = (uint32_t)(row & 7);
                 for (int i = i_begin; i < i_end; i += 4) {
-                    int32_t v[4][16];
                     int rr[4], cc[4];
+                    rr[0] = r0; cc[0] = c0;
+#pragma unroll
+                    for (int q = 1; q < 4; q++) {  // the next items; past the end repeat the last (the loads are collective)
+                        int r = rr[q - 1], c = cc[q - 1] + 1;
+                        if (c == chunks) { c = 0; r++; }
+                        const bool in = i + q < i_end;
+                        rr[q] = in ? r : rr[q - 1];
+                        cc[q] = in ? c : cc[q - 1];
+                    }
+                    {
+                        int r = rr[3], c = cc[3] + 1;
+                        if (c == chunks) { c = 0; r++; }
+                        r0 = r; c0 = c;
+                    }
+                    // Staging address of the chunk's first 16-byte unit.  Swizzled
+                    // layout: [row block][64-channel slab][128 rows][128 bytes], unit u
+                    // of a row stored at (u ^ (row & 7)) * 16 -- the TMA 128-byte
+                    // swizzle, so the 32 rows a warp writes at once fall in distinct banks.
+                    int32_t v[4][16];
+                    uint8_t *u0[4];
 #pragma unroll
                     for (int q = 0; q < 4; q++) {
-                        const int it = min(i + q, i_end - 1);  // warp-uniform (the loads are collective)
-                        rr[q] = it / chunks;
-                        cc[q] = it - rr[q] * chunks;
                         tc_ld16(tacc + (uint32_t)(rr[q] * p.bn + cc[q] * 16), v[q]);
+                        u0[q] = p.swz ? out_stage + (size_t)rr[q] * kBM * p.bn * 2 + (size_t)(cc[q] >> 2) * (kBM * 128) +
+                                            row * 128 + (((((uint32_t)cc[q] & 3u) << 1) ^ r7) << 4)
+                                      : out_stage + ((size_t)(rr[q] * kBM + row) * p.bn + cc[q] * 16) * 2;
                     }
+                    // the second 16-byte unit: the next unit (linear), or unit ^ 1 (swizzled)
+                    const uintptr_t u1x = p.swz ? 16u : 0u;
                     uint32_t rw[4][8];
                     if (res_tma) {
 #pragma unroll
                         for (int q = 0; q < 4; q++) {
-                            const uint4 r0 = *reinterpret_cast<const uint4 *>(f16_stage_unit(out_stage, p, rr[q], row, cc[q], 0));
-                            const uint4 r1 = *reinterpret_cast<const uint4 *>(f16_stage_unit(out_stage, p, rr[q], row, cc[q], 1));
-                            rw[q][0] = r0.x; rw[q][1] = r0.y; rw[q][2] = r0.z; rw[q][3] = r0.w;
-                            rw[q][4] = r1.x; rw[q][5] = r1.y; rw[q][6] = r1.z; rw[q][7] = r1.w;
+                            const uint4 a0 = *reinterpret_cast<const uint4 *>(u0[q]);
+                            const uint4 a1 = *reinterpret_cast<const uint4 *>(
+                                u1x ? (uint8_t *)((uintptr_t)u0[q] ^ u1x) : u0[q] + 16);
+                            rw[q][0] = a0.x; rw[q][1] = a0.y; rw[q][2] = a0.z; rw[q][3] = a0.w;
+                            rw[q][4] = a1.x; rw[q][5] = a1.y; rw[q][6] = a1.z; rw[q][7] = a1.w;
                         }
                     }
                     tc_wait_ld();
@@ -820,9 +833,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (i + q < i_end) {
                             uint32_t w[8];
                             f16_epilogue16<kFm>(v[q], chan, slot_base + cc[q] * 16, p, rw[q], w);
-                            *reinterpret_cast<uint4 *>(f16_stage_unit(out_stage, p, rr[q], row, cc[q], 0)) =
-                                make_uint4(w[0], w[1], w[2], w[3]);
-                            *reinterpret_cast<uint4 *>(f16_stage_unit(out_stage, p, rr[q], row, cc[q], 1)) =
+                            *reinterpret_cast<uint4 *>(u0[q]) = make_uint4(w[0], w[1], w[2], w[3]);
+                            *reinterpret_cast<uint4 *>(u1x ? (uint8_t *)((uintptr_t)u0[q] ^ u1x) : u0[q] + 16) =
                                 make_uint4(w[4], w[5], w[6], w[7]);
                         }
                     }
@@ -1017,16 +1029,18 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         R = (int)std::min<long long>(R, blocks);
         p.R = R;
         p.m_tiles = (int)((blocks + R - 1) / R);
-        p.tw = kBM; p.th = 1;
+        p.tw = kBM; p.th = 1; p.nb = 1;
         p.a_tx_bytes = (uint32_t)(kBM * p.bk);
     } else {
         pick_tile(ho, wo, &p.tw, &p.th);
+        // small maps: a row block holds whole images side by side (7x7: 2 per block)
+        p.nb = (p.tw == wo && p.th == ho) ? std::max(1, std::min(kBM / (wo * ho), d.n)) : 1;
         R = std::min(R, (ho + p.th - 1) / p.th);
         p.R = R;
         p.tiles_w = (wo + p.tw - 1) / p.tw;
         p.tiles_h = (ho + p.th * R - 1) / (p.th * R);
-        p.m_tiles = d.n * p.tiles_w * p.tiles_h;
-        p.a_tx_bytes = (uint32_t)(p.tw * p.th * p.bk);
+        p.m_tiles = ((d.n + p.nb - 1) / p.nb) * p.tiles_w * p.tiles_h;
+        p.a_tx_bytes = (uint32_t)(p.tw * p.th * p.nb * p.bk);
     }
     p.num_tiles = p.m_tiles * p.n_tiles;
     // fp16 staging in swizzled 64-channel slabs (conflict-free epilogue stores)
@@ -1083,7 +1097,7 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
                               (cuuint64_t)d.n};
         cuuint64_t strides[4] = {(cuuint64_t)swd * d.c_in * es, (cuuint64_t)d.w * d.c_in * es,
                                  (cuuint64_t)sh * d.w * d.c_in * es, (cuuint64_t)d.h * d.w * d.c_in * es};
-        cuuint32_t box[5] = {(cuuint32_t)p.bk_elems, (cuuint32_t)p.tw, 1, (cuuint32_t)p.th, 1};
+        cuuint32_t box[5] = {(cuuint32_t)p.bk_elems, (cuuint32_t)p.tw, 1, (cuuint32_t)p.th, (cuuint32_t)p.nb};
         cuuint32_t estr[5] = {1, 1, 1, 1, 1};
         r = be->encode_tiled(&ta, dt, 5, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                              sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1115,7 +1129,7 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         cuuint64_t dims[4] = {(cuuint64_t)d.c_out, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)d.n};
         cuuint64_t strides[3] = {(cuuint64_t)d.c_out * es, (cuuint64_t)wo * d.c_out * es,
                                  (cuuint64_t)ho * wo * d.c_out * es};
-        cuuint32_t box[4] = {st_ch, (cuuint32_t)p.tw, (cuuint32_t)p.th, 1};
+        cuuint32_t box[4] = {st_ch, (cuuint32_t)p.tw, (cuuint32_t)p.th, (cuuint32_t)p.nb};
         cuuint32_t estr[4] = {1, 1, 1, 1};
         r = be->encode_tiled(&ty, dt, 4, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, st_sw,
                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

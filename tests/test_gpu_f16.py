@@ -297,6 +297,9 @@ UMMA_CASES = [
     (1, 64, 64, 16, 64, 7, 2, 3, True),   # the padded stem
     (1, 9, 11, 8, 24, 3, 1, 1, True),     # c_in 8, ragged tiles
     (3, 10, 10, 40, 72, 3, 1, 1, False),
+    (3, 7, 7, 512, 512, 3, 1, 1, True),   # two whole 7x7 images per row block
+    (3, 14, 14, 256, 512, 1, 2, 0, False),
+    (5, 6, 6, 32, 64, 3, 1, 1, True),
 ]
 
 

@@ -150,6 +150,8 @@ CONV_SHAPES = [
     (1, 30, 50, 16, 32, 3, 1, dw.EPI_SILU),
     (1, 6, 6, 192, 144, 3, 1, dw.EPI_RELU6),
     (2, 5, 5, 64, 512, 1, 1, dw.EPI_RELU),
+    (4, 6, 6, 64, 64, 3, 1, dw.EPI_RELU6),   # three whole images per row block (last block ragged)
+    (3, 14, 14, 64, 128, 3, 2, dw.EPI_RELU),  # strided to 7x7: two images per row block
 ]
 
 
