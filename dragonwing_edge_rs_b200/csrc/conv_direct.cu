@@ -355,6 +355,173 @@ ConvGeom geom(const dw_conv_desc &d, int ho, int wo) {
     return ConvGeom{d.n, d.h, d.w, d.c_in, d.c_out, d.k_h, d.k_w, d.stride_h, d.stride_w, d.pad_t, d.pad_l, ho, wo};
 }
 
+// ---- depthwise 3x3, stride 1: integer dot products on per-channel column packs
+// One thread: 4 channels (one 32-bit word per pixel) x 4 output columns x a
+// segment of SEG output rows, sliding down the input one row at a time.  The 6
+// input words of a row (columns ow0-1 .. ow0+4, 4 channels each) are
+// transposed with byte permutes into, per channel, the 6 columns as bytes;
+// the 3-column window of output column j is then a funnel shift, and one
+// __dp4a against (w[kh][0], w[kh][1], w[kh][2], 0) adds a whole kernel row.
+// Each input row feeds three output rows (kh = 0, 1, 2); the accumulator of
+// the row that took its kh = 2 contribution is complete and goes through the
+// requantisation epilogue.  The int32 sums are exact, as in the reference
+// (sum over kh, kw of x * w; ops.rs:2669-2730 index order, integer arithmetic).
+__device__ __forceinline__ void dw_row_dp4a(const uint32_t (&X)[6], const int32_t (&wk)[3][4], int32_t (&a0)[4][4],
+                                            int32_t (&a1)[4][4], int32_t (&a2)[4][4]) {
+    const uint32_t ta = __byte_perm(X[0], X[1], 0x5140), tb = __byte_perm(X[0], X[1], 0x7362);
+    const uint32_t tc = __byte_perm(X[2], X[3], 0x5140), td = __byte_perm(X[2], X[3], 0x7362);
+    const uint32_t te = __byte_perm(X[4], X[5], 0x5140), tf = __byte_perm(X[4], X[5], 0x7362);
+    uint32_t P0[4], P1[4];
+    P0[0] = __byte_perm(ta, tc, 0x5410);
+    P0[1] = __byte_perm(ta, tc, 0x7632);
+    P0[2] = __byte_perm(tb, td, 0x5410);
+    P0[3] = __byte_perm(tb, td, 0x7632);
+    P1[0] = te;
+    P1[1] = te >> 16;
+    P1[2] = tf;
+    P1[3] = tf >> 16;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int win = (int)(j == 0 ? P0[k] : __funnelshift_r(P0[k], P1[k], 8 * j));
+            a2[j][k] = __dp4a(win, wk[2][k], a2[j][k]);
+            a1[j][k] = __dp4a(win, wk[1][k], a1[j][k]);
+            a0[j][k] = __dp4a(win, wk[0][k], a0[j][k]);
+        }
+    }
+}
+
+template <int SEG>
+__global__ void __launch_bounds__(128) k_dwconv3x3_s1_dp4a(ConvGeom g, const int8_t *__restrict__ x,
+                                                           const int8_t *__restrict__ w, EpiParams ep,
+                                                           int8_t *__restrict__ y) {
+    const int cg_n = g.c_in >> 2;
+    const int strips = (g.wo + 3) >> 2;
+    const int segs = (g.ho + SEG - 1) / SEG;
+    int idx = blockIdx.x * blockDim.x + threadIdx.x;  // the host checks the total fits in int
+    if (idx >= cg_n * strips * segs * g.n) return;
+    const int cg = idx % cg_n;
+    idx /= cg_n;
+    const int strip = idx % strips;
+    idx /= strips;
+    const int seg = idx % segs;
+    const int b = idx / segs;
+    const int ow0 = strip * 4, o0 = seg * SEG;
+
+    // per channel k and kernel row kh: (w[kh][0][c], w[kh][1][c], w[kh][2][c], 0)
+    const uint32_t *wq = reinterpret_cast<const uint32_t *>(w) + cg;
+    int32_t wk[3][4];
+#pragma unroll
+    for (int kh = 0; kh < 3; kh++) {
+        const uint32_t k0 = __ldg(wq + (size_t)(kh * 3 + 0) * cg_n), k1 = __ldg(wq + (size_t)(kh * 3 + 1) * cg_n);
+        const uint32_t k2 = __ldg(wq + (size_t)(kh * 3 + 2) * cg_n);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t t01 = __byte_perm(k0, k1, (uint32_t)((4 + k) << 4 | k));
+            wk[kh][k] = (int32_t)(__byte_perm(t01, k2, (uint32_t)((4 + k) << 8 | 0x10)) & 0x00FFFFFFu);
+        }
+    }
+    const int c0 = cg * 4;
+    int32_t bias[4];
+    float m[4], dsc[4], biasf[4];
+    bool fast = ep.epilogue != DW_EPI_SILU;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        bias[k] = ep.bias ? __ldg(ep.bias + c0 + k) : 0;
+        m[k] = ep.M ? __ldg(ep.M + c0 + k) : 0.0f;
+        dsc[k] = ep.D ? __ldg(ep.D + c0 + k) : 0.0f;
+        fast = fast && (uint32_t)(bias[k] + (1 << 21)) < (1u << 22) && isfinite(m[k]);
+        biasf[k] = fast ? i2f_small(bias[k]) : 0.0f;
+    }
+    const uint32_t c6 = 0x01010101u * (uint32_t)ep.q6;
+    const uint32_t *xb = reinterpret_cast<const uint32_t *>(x + (size_t)b * g.h * g.w * g.c_in) + cg;
+    uint32_t *yb = reinterpret_cast<uint32_t *>(y + (size_t)b * g.ho * g.wo * g.c_in) + cg;
+
+    // ReLU / ReLU6 clamp before rounding: roundf commutes with a clamp to
+    // integer bounds, so clamp(roundf(v), lo, hi) == roundf(clamp(v, lo, hi)).
+    const float lo = (ep.epilogue == DW_EPI_RELU || ep.epilogue == DW_EPI_RELU6) ? 0.0f : -128.0f;
+    const float hi = ep.epilogue == DW_EPI_RELU6 ? (float)ep.q6 : 127.0f;
+
+    auto load_row = [&](int t, uint32_t (&X)[6]) {
+        const int ih = o0 - g.pt + t;
+        const bool rok = ih >= 0 && ih < g.h;
+#pragma unroll
+        for (int c = 0; c < 6; c++) {
+            const int iw = ow0 - g.pl + c;
+            X[c] = (rok && iw >= 0 && iw < g.w) ? __ldg(xb + ((size_t)ih * g.w + iw) * cg_n) : 0u;
+        }
+    };
+    // accumulators start at the bias on the fast path (|acc + bias| < 2^22 there)
+    auto reset = [&](int32_t (&acc)[4][4]) {
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) acc[j][k] = fast ? bias[k] : 0;
+    };
+    auto finish = [&](int t, int32_t (&acc)[4][4]) {
+        const int oh = o0 + t - 2;
+        if (t >= 2 && oh < o0 + SEG && oh < g.ho) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int ow = ow0 + j;
+                if (ow < g.wo) {
+                    uint32_t packed = 0;
+                    if (fast) {
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            // roundf(clamp(fl(a * M))) via one RN add of 1.5 * 2^23 and the tie fix
+                            const float v = fminf(fmaxf(__fmul_rn(i2f_small(acc[j][k]), m[k]), lo), hi);
+                            const float r = __fadd_rn(v, kMagic);
+                            const float dlt = __fsub_rn(v, __fsub_rn(r, kMagic));
+                            const uint32_t q = __float_as_uint(r) + (dlt == copysignf(0.5f, v) ? (v > 0.0f ? 1u : 0xFFFFFFFFu) : 0u);
+                            packed |= (q & 0xFFu) << (8 * k);
+                        }
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            packed |= (uint32_t)(uint8_t)epilogue_one_slow(acc[j][k], bias[k], m[k], dsc[k], ep.epilogue,
+                                                                          ep.q6, ep.inv_s_out)
+                                      << (8 * k);
+                    }
+                    yb[((size_t)oh * g.wo + ow) * cg_n] = packed;
+                }
+            }
+        }
+        reset(acc);
+    };
+    int32_t A[4][4], B[4][4], C[4][4];
+    reset(A);
+    reset(B);
+    reset(C);
+    // step t reads input row o0 - pt + t; the kh = 0 / 1 / 2 accumulators hold
+    // output rows o0 + t, o0 + t - 1, o0 + t - 2 (the roles rotate every step).
+    // The next three rows are loaded while the current three are computed.
+    uint32_t X0[6], X1[6], X2[6];
+    load_row(0, X0);
+    load_row(1, X1);
+    load_row(2, X2);
+#pragma unroll 1
+    for (int t = 0; t < SEG + 2; t += 3) {
+        uint32_t N0[6], N1[6], N2[6];
+        load_row(t + 3, N0);
+        load_row(t + 4, N1);
+        load_row(t + 5, N2);
+        dw_row_dp4a(X0, wk, A, B, C);
+        finish(t, C);
+        dw_row_dp4a(X1, wk, C, A, B);
+        finish(t + 1, B);
+        dw_row_dp4a(X2, wk, B, C, A);
+        finish(t + 2, A);
+#pragma unroll
+        for (int c = 0; c < 6; c++) {
+            X0[c] = N0[c];
+            X1[c] = N1[c];
+            X2[c] = N2[c];
+        }
+    }
+}
+
 }  // namespace
 
 dw_status launch_conv_direct_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
@@ -383,6 +550,20 @@ dw_status launch_dwconv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     ConvGeom g = geom(d, ho, wo);
     const int mult = d.c_out / d.c_in;
     const bool aligned4 = (uintptr_t)x % 4 == 0 && (uintptr_t)w_hwcm % 4 == 0 && (uintptr_t)y % 4 == 0;
+    if (mult == 1 && !acc_out && be->cfg.conv_path != DW_PATH_DIRECT) {  // DIRECT: the register-fed kernels
+        const dw_status st = launch_dwconv3x3_tma_i8(be, d, ho, wo, x, w_hwcm, ep, y);
+        if (st != DW_ERR_UNSUPPORTED) return st;
+    }
+    if (mult == 1 && !acc_out && d.c_in % 4 == 0 && aligned4 && d.k_h == 3 && d.k_w == 3 && d.stride_h == 1 &&
+        d.stride_w == 1) {
+        constexpr int SEG = 28;
+        const long long threads = (long long)(d.c_in / 4) * ((wo + 3) / 4) * ((ho + SEG - 1) / SEG) * d.n;
+        if (threads < (1ll << 31) - 256 && (long long)d.h * d.w * d.c_in < (1ll << 31)) {
+            const unsigned blocks = (unsigned)((threads + 127) / 128);
+            k_dwconv3x3_s1_dp4a<SEG><<<blocks, 128, 0, be->stream>>>(g, x, w_hwcm, ep, y);
+            return dw_after_launch(be, "dwconv3x3_s1_dp4a_i8");
+        }
+    }
     if (mult == 1 && !acc_out && d.c_in % 4 == 0 && aligned4 && d.k_h == 3 && d.k_w == 3 &&
         d.stride_h == d.stride_w && (d.stride_h == 1 || d.stride_h == 2)) {
         constexpr int RH = 2, RW = 4;

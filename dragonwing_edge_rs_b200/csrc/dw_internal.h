@@ -105,6 +105,10 @@ dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, in
                                const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y,
                                const uint16_t *residual);
 
+// dwconv_tma.cu (TMA-fed int8 depthwise 3x3 stride 1; DW_ERR_UNSUPPORTED when the shape does not fit)
+dw_status launch_dwconv3x3_tma_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
+                                  const int8_t *w_hwcm, const EpiParams &ep, int8_t *y);
+
 // fp16.cu (CUDA-core fp16 kernels)
 dw_status launch_conv_direct_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,
                                  const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y);

@@ -235,6 +235,23 @@ def test_depthwise_parity(be, mult, c, epi):
     _check_conv(be, case)
 
 
+@pytest.mark.parametrize("shape", [(2, 57, 30, 576, (1, 1, 1, 1)), (1, 29, 9, 8, (1, 1, 1, 1)),
+                                   (1, 31, 13, 12, (0, 2, 1, 0)), (3, 112, 7, 4, (1, 1, 1, 1)),
+                                   (2, 30, 27, 128, (0, 2, 1, 0)), (1, 60, 120, 64, (1, 1, 1, 1))],
+                         ids=lambda s: f"{s[0]}x{s[1]}x{s[2]}x{s[3]}p{''.join(map(str, s[4]))}")
+@pytest.mark.parametrize("epi", [dw.EPI_RELU6, dw.EPI_SILU, dw.EPI_NONE])
+def test_depthwise_s1_segments_and_edges(be, be_direct, shape, epi):
+    """Stride-1 depthwise over row segments and 4-column strips: heights that
+    are not multiples of the segment, widths not multiples of 4, asymmetric
+    pads; bit-exact against the oracle on the TMA-fed kernel (64-channel
+    slabs, default path) and the register-fed one (DW_PATH_DIRECT)."""
+    n, h, w, c, pads = shape
+    rng = np.random.default_rng(h * w + c + epi)
+    case = conv_case(rng, n, h, w, c, c, k=3, s=1, pads=pads, group=c, epilogue=epi)
+    _check_conv(be, case)
+    _check_conv(be_direct, case)
+
+
 def test_reference_shim_exact_signature(be):
     """conv2d_requant_relu_i8_packed with the reference parameter list (scalar scale,
     no bias, HWIO kernel) == reference composition conv -> requantize -> relu."""
