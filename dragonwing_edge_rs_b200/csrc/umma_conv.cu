@@ -38,7 +38,8 @@ namespace {
 
 constexpr int kBM = 128;            // MMA M (rows per tile = pixels)
 constexpr int kEpiWarps = 8;        // epilogue warps (2 per TMEM lane quarter)
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStoreWarp = 2 + kEpiWarps;   // stores the staged tiles, fetches fp16 residuals
+constexpr int kThreads = 64 + 32 * kEpiWarps + 32;
 constexpr int kMaxStages = 12;
 
 struct UmmaParams {
@@ -69,6 +70,8 @@ struct UmmaParams {
     const uint16_t *res_f16;                // fp16 path, flat mode: residual [rows][c_out] added (may be null)
     int relu;                               // fp16 path: ReLU last (after the bias and the residual)
     int swz;                                // fp16 path: staging in 64-channel slabs, 128-byte swizzle (bn % 64 == 0)
+    int nbuf;                               // staging buffers (2: a tile's store overlaps the next tile's epilogue)
+    uint32_t out_bytes;                     // bytes of one staging buffer
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
@@ -209,7 +212,9 @@ __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs,
     if (write) {
         cs->bias[slot] = bias;
         cs->m[slot] = m;
-        cs->d[slot] = dsc;
+        // SiLU: the dequant scale; otherwise the bias plus the bit pattern of
+        // 1.5 * 2^23, so acc + d read as a float is 1.5 * 2^23 + acc + bias
+        cs->d[slot] = p.ep.epilogue == DW_EPI_SILU ? dsc : __int_as_float(bias + kMagicBits);
     }
     const int lane = threadIdx.x & 31;
     if ((lane & 15) == 0 && write) {
@@ -219,13 +224,6 @@ __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs,
     }
 }
 
-// Exact requantisation of one accumulator on the fast path.  Preconditions:
-// |a| < 2^22 (so the magic-number conversion is exact) and m finite (so the
-// product is never NaN).  fa = (float)a exactly; f = fa*m (RN, as the
-// reference); then clamp + roundf via round-to-nearest adds only.
-__device__ __forceinline__ uint32_t requant_fast_byte(int32_t a, float m) {
-    return f32_to_i8_byte_nonan(__fmul_rn(i2f_small(a), m));
-}
 
 // 16 accumulators (16 consecutive channels of one row) -> 16 int8, packed.
 // kSilu selects the SiLU epilogue at compile time (separate kernel instances keep
@@ -281,49 +279,62 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
                           reinterpret_cast<const float4 *>(sm)[2], reinterpret_cast<const float4 *>(sm)[3]};
     const int32_t *bb = reinterpret_cast<const int32_t *>(b4);
     const float *mm = reinterpret_cast<const float *>(m4);
-    int32_t a[16];
     bool inrange = true;
-#pragma unroll
-    for (int k = 0; k < 16; k++) a[k] = (int32_t)((uint32_t)v[k] + (uint32_t)bb[k]);
     if (!(fl & 2u)) {
 #pragma unroll
-        for (int k = 0; k < 16; k++) inrange &= (uint32_t)(a[k] + (1 << 22)) < (1u << 23);
+        for (int k = 0; k < 16; k++)
+            inrange &= (uint32_t)((int32_t)((uint32_t)v[k] + (uint32_t)bb[k]) + (1 << 22)) < (1u << 23);
     }
     if ((fl & 1u) && __all_sync(0xffffffffu, inrange)) {
-        // rint-to-even for all 16 (one RN add each); a round-half-away tie can
-        // only differ from it when c - rint(c) == +-0.5 exactly: such chunks
-        // (rare) are redone with the per-element tie fix.
+        // Packed f32x2: acc + (bias + magic bits) read as a float is 1.5 * 2^23 +
+        // acc + bias exactly; minus 1.5 * 2^23 gives the float, times M rounded
+        // once; the clamp (ReLU / ReLU6 bounds included: roundf commutes with a
+        // clamp to integer bounds) and rint-to-even by one RN add.  A
+        // round-half-away tie can only differ from it when c - rint(c) == +-0.5
+        // exactly: such chunks (rare) are redone with the per-element tie fix.
+        const int4 d4[4] = {reinterpret_cast<const int4 *>(&cs->d[slot0])[0],
+                            reinterpret_cast<const int4 *>(&cs->d[slot0])[1],
+                            reinterpret_cast<const int4 *>(&cs->d[slot0])[2],
+                            reinterpret_cast<const int4 *>(&cs->d[slot0])[3]};
+        const int32_t *bm = reinterpret_cast<const int32_t *>(d4);
+        const float lo = (epi == DW_EPI_RELU || epi == DW_EPI_RELU6) ? 0.0f : -128.0f;
+        const float hi = epi == DW_EPI_RELU6 ? (float)p.ep.q6 : 127.0f;
+        const float2 mag = make_float2(kMagic, kMagic), nmag = make_float2(-kMagic, -kMagic);
+        const float2 neg1 = make_float2(-1.0f, -1.0f);
         bool tie = false;
 #pragma unroll
         for (int q = 0; q < 4; q++) {
             uint32_t bq[4];
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float f = __fmul_rn(i2f_small(a[q * 4 + j]), mm[q * 4 + j]);
-                const float c = fminf(fmaxf(f, -128.0f), 127.0f);
-                const float r = __fadd_rn(c, kMagic);
-                tie |= fabsf(__fsub_rn(c, __fsub_rn(r, kMagic))) == 0.5f;
-                bq[j] = __float_as_uint(r);
+            for (int h = 0; h < 2; h++) {
+                const int k0 = q * 4 + 2 * h;
+                const float2 f = __fadd2_rn(make_float2(__int_as_float((int32_t)((uint32_t)v[k0] + (uint32_t)bm[k0])),
+                                                        __int_as_float((int32_t)((uint32_t)v[k0 + 1] + (uint32_t)bm[k0 + 1]))),
+                                            nmag);
+                float2 c = __fmul2_rn(f, make_float2(mm[k0], mm[k0 + 1]));
+                c.x = fminf(fmaxf(c.x, lo), hi);
+                c.y = fminf(fmaxf(c.y, lo), hi);
+                const float2 r = __fadd2_rn(c, mag);
+                const float2 d = __ffma2_rn(__fadd2_rn(r, nmag), neg1, c);  // c - rint(c), exact
+                tie |= fmaxf(fabsf(d.x), fabsf(d.y)) == 0.5f;
+                bq[2 * h] = __float_as_uint(r.x);
+                bq[2 * h + 1] = __float_as_uint(r.y);
             }
             w[q] = __byte_perm(__byte_perm(bq[0], bq[1], 0x0040), __byte_perm(bq[2], bq[3], 0x0040), 0x5410);
         }
         if (__any_sync(0xffffffffu, tie)) {
 #pragma unroll
             for (int q = 0; q < 4; q++) {
-                const uint32_t b0 = requant_fast_byte(a[q * 4 + 0], mm[q * 4 + 0]);
-                const uint32_t b1 = requant_fast_byte(a[q * 4 + 1], mm[q * 4 + 1]);
-                const uint32_t b2 = requant_fast_byte(a[q * 4 + 2], mm[q * 4 + 2]);
-                const uint32_t b3 = requant_fast_byte(a[q * 4 + 3], mm[q * 4 + 3]);
-                w[q] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+                uint32_t packed = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int k = q * 4 + j;
+                    packed |= (uint32_t)(uint8_t)epilogue_one_slow(v[k], bb[k], mm[k], 0.0f, epi, p.ep.q6,
+                                                                  p.ep.inv_s_out)
+                              << (8 * j);
+                }
+                w[q] = packed;
             }
-        }
-        if (epi == DW_EPI_RELU) {
-#pragma unroll
-            for (int q = 0; q < 4; q++) w[q] = __vmaxs4(w[q], 0u);
-        } else if (epi == DW_EPI_RELU6) {
-            const uint32_t c6 = 0x01010101u * (uint32_t)p.ep.q6;
-#pragma unroll
-            for (int q = 0; q < 4; q++) w[q] = __vmins4(__vmaxs4(w[q], 0u), c6);
         }
     } else {
 #pragma unroll
@@ -492,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *a_smem = smem;
     uint8_t *b_smem = smem + (size_t)p.stages * p.a_stage_bytes;
-    uint8_t *out_stage = smem + p.off_out;                          // [R*128 rows][bn] int8 output tile
+    uint8_t *out_stage = smem + p.off_out;                          // nbuf x [R*128 rows][bn] output tiles
     ChanSmem *chan = reinterpret_cast<ChanSmem *>(smem + p.off_chan);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.off_bars);
     uint64_t *full_bar = bars;                      // [stages]
@@ -500,8 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *tfull_bar = bars + 2 * kMaxStages;    // [2]
     uint64_t *tempty_bar = tfull_bar + 2;           // [2]
     uint64_t *drain_bar = tempty_bar + 2;           // [1] MMA drain on abort
-    uint64_t *res_bar = drain_bar + 1;              // [1] fp16 residual tile landed in the staging buffer
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(res_bar + 1);
+    uint64_t *res_bar = drain_bar + 1;              // [2] staging buffer free for the next tile (fp16: residual in)
+    uint64_t *ready_bar = res_bar + 2;              // [2] staging buffer holds a finished tile
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ready_bar + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -517,7 +529,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&tempty_bar[a]), kEpiWarps);
         }
         mbar_init(smem_u32(drain_bar), 1);
-        mbar_init(smem_u32(res_bar), 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(smem_u32(&res_bar[b]), 1);
+            mbar_init(smem_u32(&ready_bar[b]), kEpiWarps);
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -631,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else {
+    } else if (warp < kStoreWarp) {
         // ------------------------------------------------------------ epilogue
         const int e = warp - 2;               // 0..7
         const int et = threadIdx.x - 64;      // 0..255 epilogue thread index
@@ -652,45 +667,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the slots one tile ahead (the global loads overlap the previous tile).
         if (!p.chan_all && (int)blockIdx.x < p.num_tiles)
             stage_channel(p, chan, et, tile_coord(p, blockIdx.x).n0 + et, et < p.bn);
-        // fp16 residual (flat mode): the tile's residual rows are brought into the
-        // staging buffer by TMA while the tile's MMAs run; each thread reads its
-        // 16 residual halves from the spot its 16 outputs then overwrite.
+        // Staging: tile `local` goes to buffer local % nbuf once the store warp
+        // has released it (res_bar; for an fp16 residual the buffer then holds
+        // the tile's residual rows, which each thread reads from the spot its
+        // 16 outputs overwrite); ready_bar hands the finished tile back.
         constexpr bool res_tma = kF16 && (kFm & 2);
-        uint32_t res_phase = 0;
-        bool res_pending = false;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
+            const int sb = p.nbuf == 2 ? (local & 1) : 0;
+            const uint32_t sb_ph = p.nbuf == 2 ? ((local >> 1) & 1) : (local & 1);
+            uint8_t *const stage = out_stage + (size_t)sb * p.out_bytes;
             const TileCoord tc = tile_coord(p, tile);
             const int slot_base = p.chan_all ? tc.n0 : acc * (kChanSlots / 2);
-            if (et == 0) {
-                bulk_wait_read0();  // the previous tile's stores have read the staging buffer
-                if (res_tma) {
-                    const int nrb = valid_blocks(p, tc);
-                    mbar_expect_tx(smem_u32(res_bar), (uint32_t)(nrb * kBM * p.bn * 2));
-                    const int slabs = p.swz ? p.bn / 64 : 1, sw_ch = p.swz ? 64 : p.bn;
-                    for (int r = 0; r < nrb; r++)
-                        for (int sl = 0; sl < slabs; sl++)
-                            tma_load_2d(smem_u32(out_stage + (size_t)r * kBM * p.bn * 2 + (size_t)sl * kBM * sw_ch * 2),
-                                        &tmap_r, smem_u32(res_bar), tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
-                    res_pending = true;
-                }
-            }
             bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), acc_ph, p, abort_flag, 4);
-            if (res_tma && ok) ok = mbar_wait(smem_u32(res_bar), res_phase, p, abort_flag, 5);
-            // Barrier A (epilogue threads only): all-or-none abort decision; the
-            // staging buffer is free again and holds this tile's residual; this
+            if (ok) ok = mbar_wait(smem_u32(&res_bar[sb]), sb_ph, p, abort_flag, 5);
+            // Barrier A (epilogue threads only): all-or-none abort decision; this
             // tile's staged channel parameters are visible.
-            if (named_barrier_or(1, kEpiWarps * 32, !ok)) {
-                if (et == 0 && res_pending) {  // let the residual copy land before the CTA exits
-                    const uint64_t t0 = globaltimer_ns();
-                    while (!mbar_try_wait(smem_u32(res_bar), res_phase) && globaltimer_ns() - t0 < p.wait_cap_ns) {
-                    }
-                }
-                break;
-            }
-            res_phase ^= 1u;
-            res_pending = false;
+            if (named_barrier_or(1, kEpiWarps * 32, !ok)) break;
             if (!p.chan_all) {  // next tile's channels into the other half (its readers finished before barrier A)
                 const int next = tile + (int)gridDim.x;
                 if (next < p.num_tiles)
@@ -734,9 +728,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int q = 0; q < 4; q++) {
                         tc_ld16(tacc + (uint32_t)(rr[q] * p.bn + cc[q] * 16), v[q]);
-                        u0[q] = p.swz ? out_stage + (size_t)rr[q] * kBM * p.bn * 2 + (size_t)(cc[q] >> 2) * (kBM * 128) +
+                        u0[q] = p.swz ? stage + (size_t)rr[q] * kBM * p.bn * 2 + (size_t)(cc[q] >> 2) * (kBM * 128) +
                                             row * 128 + (((((uint32_t)cc[q] & 3u) << 1) ^ r7) << 4)
-                                      : out_stage + ((size_t)(rr[q] * kBM + row) * p.bn + cc[q] * 16) * 2;
+                                      : stage + ((size_t)(rr[q] * kBM + row) * p.bn + cc[q] * 16) * 2;
                     }
                     // the second 16-byte unit: the next unit (linear), or unit ^ 1 (swizzled)
                     const uintptr_t u1x = p.swz ? 16u : 0u;
@@ -769,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = cb; c < ce; c++) {
                     int32_t v[16];
                     tc_ld16(tacc + (uint32_t)(c * 16), v);
-                    uint8_t *dst = out_stage + (size_t)row * p.bn + c * 16;
+                    uint8_t *dst = stage + (size_t)row * p.bn + c * 16;
                     tc_wait_ld();
                     *reinterpret_cast<uint4 *>(dst) = requant16<kSilu>(v, chan, slot_base + c * 16, p);
                 }
@@ -786,11 +780,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int32_t v1[16], v2[16];
                 tc_ld16(tacc + (uint32_t)(r1 * p.bn + c1 * 16), v1);
                 tc_ld16(tacc + (uint32_t)(r2 * p.bn + c2 * 16), v2);
-                uint8_t *dst1 = out_stage + ((size_t)(r1 * kBM + row)) * p.bn + c1 * 16;
+                uint8_t *dst1 = stage + ((size_t)(r1 * kBM + row)) * p.bn + c1 * 16;
                 tc_wait_ld();
                 *reinterpret_cast<uint4 *>(dst1) = requant16<kSilu>(v1, chan, slot_base + c1 * 16, p);
                 if (two) {
-                    uint8_t *dst2 = out_stage + ((size_t)(r2 * kBM + row)) * p.bn + c2 * 16;
+                    uint8_t *dst2 = stage + ((size_t)(r2 * kBM + row)) * p.bn + c2 * 16;
                     *reinterpret_cast<uint4 *>(dst2) = requant16<kSilu>(v2, chan, slot_base + c2 * 16, p);
                 }
                 c1 += 2;
@@ -798,17 +792,58 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             }
             tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));  // TMEM buffer free for the MMA warp
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging writes -> async proxy
-            named_barrier_sync(2, kEpiWarps * 32);
-            if (et == 0) {
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(smem_u32(&tempty_bar[acc]));  // TMEM buffer free for the MMA warp
+                mbar_arrive(smem_u32(&ready_bar[sb]));    // staged tile ready for the store warp
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ store warp
+        // Issues each finished tile's TMA stores, then -- once they have read the
+        // buffer -- releases it for the tile nbuf tiles later (fetching that
+        // tile's fp16 residual into it first).
+        if (lane == 0) {
+            constexpr bool res_tma = kF16 && (kFm & 2);
+            constexpr int es = kF16 ? 2 : 1;
+            const int slabs = (kF16 && p.swz) ? p.bn / 64 : 1, sw_ch = (kF16 && p.swz) ? 64 : p.bn;
+            uint32_t res_ph[2] = {0u, 0u};
+            bool res_out[2] = {false, false};
+            auto prepare = [&](int tile, int sb) {
+                const uint32_t bar = smem_u32(&res_bar[sb]);
+                if (res_tma) {
+                    const TileCoord tc = tile_coord(p, tile);
+                    const int nrb = valid_blocks(p, tc);
+                    uint8_t *stage = out_stage + (size_t)sb * p.out_bytes;
+                    mbar_expect_tx(bar, (uint32_t)(nrb * kBM * p.bn * 2));
+                    for (int r = 0; r < nrb; r++)
+                        for (int sl = 0; sl < slabs; sl++)
+                            tma_load_2d(smem_u32(stage + (size_t)r * kBM * p.bn * 2 + (size_t)sl * kBM * sw_ch * 2),
+                                        &tmap_r, bar, tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
+                    res_out[sb] = true;
+                } else {
+                    mbar_arrive(bar);
+                }
+                res_ph[sb] ^= 1u;
+            };
+            for (int k = 0; k < p.nbuf; k++) {
+                const int t = (int)blockIdx.x + k * (int)gridDim.x;
+                if (t < p.num_tiles) prepare(t, k);
+            }
+            int local = 0;
+            for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
+                const int sb = p.nbuf == 2 ? (local & 1) : 0;
+                const uint32_t sb_ph = p.nbuf == 2 ? ((local >> 1) & 1) : (local & 1);
+                if (!mbar_wait(smem_u32(&ready_bar[sb]), sb_ph, p, abort_flag, 6)) break;
+                res_out[sb] = false;  // the epilogue waited for this buffer's residual before filling it
+                const TileCoord tc = tile_coord(p, tile);
                 const int nrb = valid_blocks(p, tc);
-                const int slabs = (kF16 && p.swz) ? p.bn / 64 : 1, sw_ch = (kF16 && p.swz) ? 64 : p.bn;
+                uint8_t *stage = out_stage + (size_t)sb * p.out_bytes;
                 for (int r = 0; r < nrb; r++) {
                     for (int sl = 0; sl < slabs; sl++) {
-                        const uint32_t src = smem_u32(out_stage + (size_t)r * kBM * p.bn * (kF16 ? 2 : 1) +
-                                                      (size_t)sl * kBM * sw_ch * (kF16 ? 2 : 1));
+                        const uint32_t src =
+                            smem_u32(stage + (size_t)r * kBM * p.bn * es + (size_t)sl * kBM * sw_ch * es);
                         if (p.mode == 0)
                             tma_store_2d(&tmap_y, src, tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
                         else
@@ -816,9 +851,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 bulk_commit();
+                const int next = tile + p.nbuf * (int)gridDim.x;
+                if (next < p.num_tiles) {
+                    bulk_wait_read0();  // the stores have read the buffer
+                    prepare(next, sb);
+                }
+            }
+            bulk_wait_all0();
+            // residual copies issued for tiles the epilogue never took (abort): let them land
+            for (int b = 0; b < 2; b++) {
+                if (!res_out[b]) continue;
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(smem_u32(&res_bar[b]), res_ph[b] ^ 1u) && globaltimer_ns() - t0 < p.wait_cap_ns) {
+                }
             }
         }
-        if (et == 0) bulk_wait_all0();
     }
 
     tc_fence_before();
@@ -940,8 +987,27 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         if (v == 32 || v == 64 || v == 128) p.bk = v;
     }
     if (esize == 2 && !flat && d.stride_w > 1 && (d.c_in * esize) % p.bk) p.bk = pick_bk(d.c_in * esize);
-    p.bk_elems = p.bk / esize;
     p.bn = pick_bn(((d.c_out + 15) / 16) * 16);
+    // 1x1 convs (epilogue-bound: few K steps per tile): a narrower K block when
+    // that lets the staging be double-buffered (the fp16 staging of a 128 x 256
+    // tile is 64 KiB) -- more K steps, but a tile's stores overlap the next
+    // tile's epilogue.
+    if (d.k_h * d.k_w == 1) {
+        const size_t chan = al1k(sizeof(ChanSmem));
+        auto fits2 = [&](int bk) {
+            const int r = std::max(1, std::min({8, 256 / p.bn, 32768 / (kBM * bk)}));
+            const size_t ob = al1k((size_t)r * kBM * p.bn * esize);
+            const size_t sp = al1k((size_t)r * kBM * bk) + al1k((size_t)p.bn * bk);
+            return 1024 + 2 * ob + chan + 512 + 2 * sp <= kSmemLimit;
+        };
+        if (!fits2(p.bk))
+            for (int bk = p.bk / 2; bk >= 32; bk /= 2)
+                if (fits2(bk)) {
+                    p.bk = bk;
+                    break;
+                }
+    }
+    p.bk_elems = p.bk / esize;
     p.cblocks = (d.c_in + p.bk_elems - 1) / p.bk_elems;
     p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
     // Row blocks per tile: R * bn <= 256 (two TMEM accumulator buffers within 512
@@ -976,16 +1042,20 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     p.b_stage_bytes = (uint32_t)al1k((size_t)p.bn * p.bk);
     const size_t out_bytes = al1k((size_t)p.R * kBM * p.bn * esize);
     const size_t chan_bytes = al1k(sizeof(ChanSmem));
-    const size_t fixed = 1024 /*align slack*/ + out_bytes + chan_bytes + 256 /*barriers*/;
-    int stages = (int)((kSmemLimit - fixed) / (p.a_stage_bytes + p.b_stage_bytes));
+    // two staging buffers when they fit beside at least two pipeline stages
+    const size_t stage_pair = p.a_stage_bytes + p.b_stage_bytes;
+    p.nbuf = (1024 + 2 * out_bytes + chan_bytes + 512 + 2 * stage_pair <= kSmemLimit) ? 2 : 1;
+    p.out_bytes = (uint32_t)out_bytes;
+    const size_t fixed = 1024 /*align slack*/ + p.nbuf * out_bytes + chan_bytes + 512 /*barriers*/;
+    int stages = (int)((kSmemLimit - fixed) / stage_pair);
     p.stages = std::max(2, std::min(stages, kMaxStages));
-    p.off_out = (uint32_t)((size_t)p.stages * (p.a_stage_bytes + p.b_stage_bytes));
-    p.off_chan = (uint32_t)(p.off_out + out_bytes);
+    p.off_out = (uint32_t)((size_t)p.stages * stage_pair);
+    p.off_chan = (uint32_t)(p.off_out + p.nbuf * out_bytes);
     p.off_bars = (uint32_t)(p.off_chan + chan_bytes);
     p.acc_bound = (long long)p.taps * d.c_in * 16384ll;
     // At least 116 KiB so that a second CTA never fits on the SM: one CTA per SM
     // owns the tensor memory (its tcgen05.alloc never waits on a neighbour).
-    const size_t smem = std::max<size_t>(1024 + p.off_bars + 256, 116 * 1024);
+    const size_t smem = std::max<size_t>(1024 + p.off_bars + 512, 116 * 1024);
     if (smem > kSmemLimit) return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: tile does not fit in shared memory", op);
     // tcgen05 instruction descriptor: kind::i8: D = s32 (bits 4-5 = 2), A = B = s8
     // (bits 7-9, 10-12 = 1); kind::f16: D = f32 (bits 4-5 = 1), A = B = f16 (0).
