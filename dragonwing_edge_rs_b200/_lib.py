@@ -106,6 +106,7 @@ SIGNATURES = {
     "dw_cast_f32_to_f16": ([vp, vp, vp, sz, sz, sz], i32),
     "dw_cast_f16_to_f32": ([vp, vp, vp], i32),
     "dw_unfold_w_f32_to_f16": ([vp, vp, vp] + [sz] * 9, i32),
+    "dw_im2col_u8_to_i8": ([vp, vp, vp] + [sz] * 13 + [f32], i32),
 }
 
 _lib = None

@@ -132,6 +132,57 @@ __global__ void k_quantize_u8(const uint8_t *__restrict__ in, int8_t *__restrict
         out[i] = (int8_t)f32_to_i8(__fmul_rn(__fmul_rn(i2f_small((int32_t)in[i]), inv255), inv));
 }
 
+// --- im2col of a uint8 image fused with its quantisation ---------------------
+// y[b][i][j][(a * kw + q) * c + ch] = quant(x[b][i*sh + a - pt][j*sw + q - pl][ch])
+// (0 in the padding and in channels kh*kw*c .. c_dst-1), quant(u) = the
+// QuantizeU8 result for byte u (computed exactly as k_quantize_u8 does, once
+// per block into a 256-entry table).  A conv of the quantised image equals a
+// 1x1 conv of y with the kernel rows flattened in (kh, kw, c) order: the same
+// integer products.
+template <int C, int KH, int KW>  // C = 0: runtime c, kh, kw
+__global__ void k_im2col_u8_i8(const uint8_t *__restrict__ x, int8_t *__restrict__ y, int n, int h, int w, int c_rt,
+                               int kh_rt, int kw_rt, int sh, int sw, int pt, int pl, int ho, int wo, int c_dst,
+                               float inv255, float inv) {
+    __shared__ int8_t lut[256];
+    for (int u = threadIdx.x; u < 256; u += blockDim.x)
+        lut[u] = (int8_t)f32_to_i8(__fmul_rn(__fmul_rn(i2f_small(u), inv255), inv));
+    __syncthreads();
+    const int c = C ? C : c_rt, kh = C ? KH : kh_rt, kw = C ? KW : kw_rt;
+    const size_t total = (size_t)n * ho * wo;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int j = (int)(i % wo);
+        const size_t t = i / wo;
+        const int oi = (int)(t % ho);
+        const int b = (int)(t / ho);
+        const uint8_t *xb = x + (size_t)b * h * w * c;
+        uint32_t wd[16] = {};  // up to 64 output bytes
+        const int ih0 = oi * sh - pt, iw0 = j * sw - pl;
+#pragma unroll
+        for (int a = 0; a < (C ? KH : 8); a++) {
+            if (!C && a >= kh) break;
+            const int ih = ih0 + a;
+            if (ih < 0 || ih >= h) continue;
+#pragma unroll
+            for (int q = 0; q < (C ? KW : 8); q++) {
+                if (!C && q >= kw) break;
+                const int iw = iw0 + q;
+                if (iw < 0 || iw >= w) continue;
+                const uint8_t *px = xb + ((size_t)ih * w + iw) * c;
+#pragma unroll
+                for (int ch = 0; ch < (C ? C : 8); ch++) {
+                    if (!C && ch >= c) break;
+                    const int k = (a * kw + q) * c + ch;
+                    if (k < 64) wd[k >> 2] |= (uint32_t)(uint8_t)lut[__ldg(px + ch)] << (8 * (k & 3));
+                }
+            }
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(y + i * (size_t)c_dst);
+#pragma unroll
+        for (int g = 0; g < 4; g++)
+            if (g * 16 < c_dst) dst[g] = make_uint4(wd[4 * g], wd[4 * g + 1], wd[4 * g + 2], wd[4 * g + 3]);
+    }
+}
+
 // --- dequantize: ops.rs:3453-3457 ---------------------------------------------
 __global__ void k_dequantize(const int8_t *__restrict__ in, float *__restrict__ out, size_t n, float s) {
     size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
@@ -353,6 +404,19 @@ dw_status launch_quantize_u8(dw_backend *be, const uint8_t *in, int8_t *out, siz
     const float inv255 = 1.0f / 255.0f, inv = 1.0f / scale;
     k_quantize_u8<<<grid_for(be, (n + 15) / 16), kThreads, 0, be->stream>>>(in, out, n, inv255, inv);
     return dw_after_launch(be, "quantize_u8_to_i8");
+}
+
+dw_status launch_im2col_u8_i8(dw_backend *be, const uint8_t *x, int8_t *y, int n, int h, int w, int c, int kh, int kw,
+                              int sh, int sw, int pt, int pl, int ho, int wo, int c_dst, float scale) {
+    const float inv255 = 1.0f / 255.0f, inv = 1.0f / scale;
+    const int grid = grid_for(be, (size_t)n * ho * wo);
+    if (c == 3 && kh == 3 && kw == 3)  // the usual image stem
+        k_im2col_u8_i8<3, 3, 3><<<grid, kThreads, 0, be->stream>>>(x, y, n, h, w, c, kh, kw, sh, sw, pt, pl, ho, wo,
+                                                                    c_dst, inv255, inv);
+    else
+        k_im2col_u8_i8<0, 0, 0><<<grid, kThreads, 0, be->stream>>>(x, y, n, h, w, c, kh, kw, sh, sw, pt, pl, ho, wo,
+                                                                    c_dst, inv255, inv);
+    return dw_after_launch(be, "im2col_u8_i8");
 }
 
 dw_status launch_dequantize(dw_backend *be, const int8_t *in, float *out, size_t n, float scale) {

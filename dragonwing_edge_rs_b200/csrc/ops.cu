@@ -325,6 +325,25 @@ DW_API dw_status dw_quantize_u8_to_i8(dw_backend *be, const dw_buf *in_u8, dw_bu
     return dw::launch_quantize_u8(be, (const uint8_t *)in_u8->ptr, (int8_t *)out_i8->ptr, out_i8->len, scale);
 }
 
+DW_API dw_status dw_im2col_u8_to_i8(dw_backend *be, const dw_buf *x_u8, dw_buf *y_i8, size_t n, size_t h, size_t w,
+                                    size_t c, size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t, size_t p_l,
+                                    size_t h_out, size_t w_out, size_t c_dst, float scale) {
+    const char *op = "im2col_u8_to_i8";
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!x_u8 || !y_i8) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: null buffer", op);
+    if (!n || !h || !w || !c || !k_h || !k_w || !s_h || !s_w || !h_out || !w_out || c_dst % 16 || c_dst > 64 ||
+        k_h > 8 || k_w > 8 || c > 8 ||
+        k_h * k_w * c > c_dst || n * h_out * w_out > 0x7fffffff || n * h * w * c > 0x7fffffffffffll)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: invalid geometry (c_dst a multiple of 16 >= k_h*k_w*c)", op);
+    DW_TRY(check_len(be, x_u8, n * h * w * c, op, "input"));
+    DW_TRY(check_len(be, y_i8, n * h_out * w_out * c_dst, op, "output"));
+    if ((uintptr_t)y_i8->ptr & 15) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: output must be 16-byte aligned", op);
+    cudaSetDevice(be->device);
+    return dw::launch_im2col_u8_i8(be, (const uint8_t *)x_u8->ptr, (int8_t *)y_i8->ptr, (int)n, (int)h, (int)w, (int)c,
+                                   (int)k_h, (int)k_w, (int)s_h, (int)s_w, (int)p_t, (int)p_l, (int)h_out, (int)w_out,
+                                   (int)c_dst, scale);
+}
+
 DW_API dw_status dw_dequantize_i8_to_f32(dw_backend *be, const dw_buf *in_i8, dw_buf *out_f32, float scale) {
     if (!be) return DW_ERR_INVALID_ARG;
     if (!in_i8 || !out_f32) return dw_fail(be, DW_ERR_INVALID_ARG, "dequantize_i8_to_f32: null buffer");

@@ -419,12 +419,63 @@ def lower_unfold_stem_f16(graph: Graph) -> Graph:
     return Graph(tensors, ops_, inits, list(graph.inputs), list(graph.outputs))
 
 
+def lower_im2col_input_i8(graph: Graph) -> Graph:
+    """Device lowering of an int8 network's first conv on a few-channel image:
+    QuantizeU8 (c channels, c % 16 != 0) -> Conv2dRequantReluI8Nhwc (k_h x k_w,
+    k_h*k_w*c <= 64) becomes Im2colU8ToI8 (the quantisation fused with an
+    im2col into c_dst = k_h*k_w*c rounded up to 16 channels) -> a 1x1 conv
+    whose kernel rows are the original taps in (kh, kw, c) order, zero rows for
+    the padding channels.  The integer products are the same, so the result is
+    bit-identical; the tensor cores then see 16-byte-aligned channel rows."""
+    ops_ = list(graph.ops)
+    consumers: dict = {}
+    for op in ops_:
+        for i in op.inputs:
+            consumers.setdefault(i, []).append(op)
+    tensors, inits = dict(graph.tensors), dict(graph.initializers)
+    for q in ops_:
+        if q.op_type != "QuantizeU8":
+            continue
+        t = tensors[q.outputs[0]]
+        n, h, w, c = t.shape
+        users = consumers.get(q.outputs[0], [])
+        if c % 16 == 0 or len(users) != 1 or users[0].op_type != "Conv2dRequantReluI8Nhwc" or q.outputs[0] in graph.outputs:
+            continue
+        conv = users[0]
+        d = conv.params["desc"]
+        kc = d.k_h * d.k_w * c
+        if d.group != 1 or kc > 64:
+            continue
+        ho, wo = d.out_hw()
+        c_dst = (kc + 15) // 16 * 16
+        u = q.outputs[0] + "_im2col"
+        tensors[u] = TensorInfo(u, (n, ho, wo, c_dst), "i8", t.scale)
+        tensors.pop(q.outputs[0], None)
+        wt = graph.initializers[conv.inputs[1]].reshape(kc, d.c_out)
+        wu = np.zeros((1, 1, c_dst, d.c_out), np.int8)
+        wu[0, 0, :kc, :] = wt
+        inits[conv.inputs[1] + "_im2col"] = wu
+        pt, pl, _, _ = d.pads
+        im2col = CompiledOp(q.name + "_im2col", "Im2colU8ToI8", list(q.inputs), [u],
+                            {"k_h": d.k_h, "k_w": d.k_w, "s_h": d.stride_h, "s_w": d.stride_w, "p_t": pt, "p_l": pl,
+                             "h_out": ho, "w_out": wo, "c_dst": c_dst, "scale": q.params["scale"]})
+        d2 = ConvDesc(n, ho, wo, c_dst, d.c_out, 1, 1, 1, 1, (0, 0, 0, 0), 1, d.epilogue)
+        d2.q6, d2.inv_s_out = d.q6, d.inv_s_out
+        conv2 = CompiledOp(conv.name, conv.op_type, [u, conv.inputs[1] + "_im2col"] + list(conv.inputs[2:]),
+                           list(conv.outputs), dict(conv.params, desc=d2, c_in_real=kc))
+        ops_ = [im2col if op is q else conv2 if op is conv else op for op in ops_]
+        break
+    return Graph(tensors, ops_, inits, list(graph.inputs), list(graph.outputs))
+
+
 def lower_for_device(graph: Graph) -> Graph:
-    """The device passes: residual fusion, then the input-conv unfold."""
+    """The device passes: residual fusion, then the input-conv unfold / im2col."""
     if any(op.op_type == "AddF16" for op in graph.ops):
         graph = fuse_residual_f16(graph)
     if any(op.op_type == "CastF32ToF16" for op in graph.ops):
         graph = lower_unfold_stem_f16(graph)
+    if any(op.op_type == "QuantizeU8" for op in graph.ops):
+        graph = lower_im2col_input_i8(graph)
     return graph
 
 
@@ -620,6 +671,12 @@ class CudaGraphRuntime:
             _, ho, wo, _ = self.graph.tensors[op.outputs[0]].shape
             x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
             return lambda: ops.resize_nearest_i8(be, x, y, n, h, w, ho, wo, c)
+        if t == "Im2colU8ToI8":
+            x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
+            n, h, w, c = self.graph.tensors[op.inputs[0]].shape
+            pr = op.params
+            return lambda: ops.im2col_u8_to_i8(be, x, y, n, h, w, c, pr["k_h"], pr["k_w"], pr["s_h"], pr["s_w"], pr["p_t"],
+                                               pr["p_l"], pr["h_out"], pr["w_out"], pr["c_dst"], pr["scale"])
         if t == "QuantizeU8":
             x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
             s = op.params["scale"]

@@ -261,3 +261,9 @@ def unfold_w_f32_to_f16(backend, x, y, n, h, w, c, k_w, stride_w, pad_l, w_out, 
     first conv's input layout for the tensor cores; contract in include/dw_cuda.h)."""
     backend._check(L.load().dw_unfold_w_f32_to_f16(backend.handle, x.handle, y.handle, n, h, w, c, k_w, stride_w,
                                                    pad_l, w_out, c_dst))
+
+
+def im2col_u8_to_i8(backend, x, y, n, h, w, c, k_h, k_w, s_h, s_w, p_t, p_l, h_out, w_out, c_dst, scale):
+    """im2col of a uint8 image fused with its quantisation (contract in include/dw_cuda.h)."""
+    backend._check(L.load().dw_im2col_u8_to_i8(backend.handle, x.handle, y.handle, n, h, w, c, k_h, k_w, s_h, s_w,
+                                               p_t, p_l, h_out, w_out, c_dst, float(scale)))

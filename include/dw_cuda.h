@@ -231,6 +231,16 @@ DW_API dw_status dw_quantize_f32_to_i8(dw_backend *be, const dw_buf *in_f32, dw_
 /* Input quantisation of uint8 images: q = quantize(u8 * (1/255), s) in one pass
  * (the YOLO input path: u8 -> /255 -> f32 -> quantize). */
 DW_API dw_status dw_quantize_u8_to_i8(dw_backend *be, const dw_buf *in_u8, dw_buf *out_i8, float scale);
+/* im2col of a uint8 NHWC image fused with its quantisation: y [n, h_out,
+ * w_out, c_dst] int8 with y[b][i][j][(a*k_w + q)*c + ch] = the
+ * dw_quantize_u8_to_i8 value of x[b][i*s_h + a - p_t][j*s_w + q - p_l][ch]
+ * (0 in the padding and in channels k_h*k_w*c .. c_dst-1); c, k_h, k_w <= 8,
+ * c_dst <= 64 and a multiple of 16.  The first conv of
+ * a network on a few-channel image then runs as a 1x1 conv over c_dst
+ * channels on the tensor cores, with the same integer products. */
+DW_API dw_status dw_im2col_u8_to_i8(dw_backend *be, const dw_buf *x_u8, dw_buf *y_i8, size_t n, size_t h, size_t w,
+                                    size_t c, size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t, size_t p_l,
+                                    size_t h_out, size_t w_out, size_t c_dst, float scale);
 /* dequantize_i8_packed_to_f32 (vulkan ops.rs:2069) / cpu ops.rs:3439-3457. */
 DW_API dw_status dw_dequantize_i8_to_f32(dw_backend *be, const dw_buf *in_i8, dw_buf *out_f32, float scale);
 /* maxpool2d (cpu ops.rs:1513-1551) on int8 NHWC, with pads [t,l,b,r] taken as -inf. */

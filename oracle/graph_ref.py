@@ -78,6 +78,8 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
             n, h, w, c = x.shape
             _, ho, wo, _ = shape_of(op.outputs[0])
             vals[op.outputs[0]] = dwref.resize_nearest_i8(x, n, h, w, ho, wo, c).reshape(n, ho, wo, c)
+        elif t == "Im2colU8ToI8":  # device lowering of QuantizeU8 + the input conv (same integers)
+            vals[op.outputs[0]] = im2col_u8_op(op, vals[op.inputs[0]])
         elif t == "QuantizeU8":
             x = vals[op.inputs[0]]
             vals[op.outputs[0]] = dwref.quantize_u8_to_i8(x, op.params["scale"]).reshape(x.shape)
@@ -165,4 +167,21 @@ def unfold_f16_op(op, x):
     for q in range(kw):
         cols = xp[:, :, q:q + sw * wo:sw, :][:, :, :wo, :]
         y[..., q * c:(q + 1) * c] = dwref.f16_from_f32_array(cols).reshape(n, h, wo, c)
+    return y
+
+
+def im2col_u8_op(op, x):
+    """Im2colU8ToI8 on a uint8 NHWC image: quantize_u8_to_i8 then the im2col gather."""
+    pr = op.params
+    n, h, w, c = x.shape
+    q = dwref.quantize_u8_to_i8(x, pr["scale"]).reshape(n, h, w, c)
+    kh, kw, sh, sw, pt, pl = pr["k_h"], pr["k_w"], pr["s_h"], pr["s_w"], pr["p_t"], pr["p_l"]
+    ho, wo, cd = pr["h_out"], pr["w_out"], pr["c_dst"]
+    qp = np.zeros((n, h + kh + sh * ho, w + kw + sw * wo, c), np.int8)
+    qp[:, pt:pt + h, pl:pl + w, :] = q
+    y = np.zeros((n, ho, wo, cd), np.int8)
+    for a in range(kh):
+        for b_ in range(kw):
+            k0 = (a * kw + b_) * c
+            y[..., k0:k0 + c] = qp[:, a:a + sh * ho:sh, b_:b_ + sw * wo:sw, :][:, :ho, :wo, :]
     return y

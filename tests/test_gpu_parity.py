@@ -252,6 +252,27 @@ def test_depthwise_s1_segments_and_edges(be, be_direct, shape, epi):
     _check_conv(be_direct, case)
 
 
+@pytest.mark.parametrize("geo", [(2, 64, 48, 3, 3, 3, 2, 2, 1, 1, 32), (1, 17, 9, 3, 3, 3, 1, 1, 1, 1, 32),
+                                 (1, 20, 20, 5, 2, 3, 2, 1, 0, 1, 32), (1, 30, 30, 3, 7, 3, 2, 2, 3, 3, 64)])
+def test_im2col_u8_to_i8(be, geo):
+    """Quantise + im2col of a uint8 image (the input conv's device lowering) is
+    bit-exact against quantize_u8_to_i8 followed by the gather."""
+    from oracle.graph_ref import im2col_u8_op
+    n, h, w, c, kh, kw, sh, sw, pt, pl, cd = geo
+    ho, wo = (h + 2 * pt - kh) // sh + 1, (w + 2 * pl - kw) // sw + 1
+    rng = np.random.default_rng(sum(geo))
+    x = rng.integers(0, 256, n * h * w * c).astype(np.uint8)
+    bx, by = be.upload_array(x), be.alloc(n * ho * wo * cd)
+    ops.im2col_u8_to_i8(be, bx, by, n, h, w, c, kh, kw, sh, sw, pt, pl, ho, wo, cd, 1.0 / 127.0)
+    got = be.download_array(by, np.int8)
+
+    class _Op:
+        params = {"k_h": kh, "k_w": kw, "s_h": sh, "s_w": sw, "p_t": pt, "p_l": pl, "h_out": ho, "w_out": wo,
+                  "c_dst": cd, "scale": 1.0 / 127.0}
+    exp = im2col_u8_op(_Op, x.reshape(n, h, w, c)).ravel()
+    assert np.array_equal(got, exp), mismatch_report(got, exp)
+
+
 def test_reference_shim_exact_signature(be):
     """conv2d_requant_relu_i8_packed with the reference parameter list (scalar scale,
     no bias, HWIO kernel) == reference composition conv -> requantize -> relu."""
