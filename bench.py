@@ -137,7 +137,13 @@ WORKLOADS = {
     "yolov8n": (32, "images/s", "yolov8n_int8 640x640 (BASELINE config 4)"),
     "mbv2_block": (32, "TOPS", "mobilenetv2_int8_block 112x112x96 (BASELINE config 2)"),
     "resnet50_fp16": (128, "images/s", "resnet50_fp16 224x224 (BASELINE config 5)"),
+    "conv3x3_int8": (1, "TOPS", "fused int8 conv 3x3 s1 p1 56x56x64->64 + bias + per-channel requant + ReLU (BASELINE config 1)"),
+    "qgemm_int8_4096": (1, "TOPS", "int8 QGemm M=N=K=4096, int32 bias, per-column requant (BASELINE config 3)"),
+    "qgemm_int8_8192x1024x4096": (1, "TOPS", "int8 QGemm M=8192 N=1024 K=4096 (BASELINE config 3)"),
+    "qgemm_int8_256x4096x11008": (1, "TOPS", "int8 QGemm M=256 N=4096 K=11008 (BASELINE config 3)"),
 }
+QGEMM_SHAPES = {"qgemm_int8_4096": (4096, 4096, 4096), "qgemm_int8_8192x1024x4096": (8192, 1024, 4096),
+                "qgemm_int8_256x4096x11008": (256, 4096, 11008)}
 FP16_WORKLOADS = {"resnet50_fp16"}
 DEFAULT_WORKLOAD = "yolov8n"
 
@@ -147,6 +153,18 @@ def build_workload(name: str, batch: int, seed: int):
     if name not in WORKLOADS:
         raise SystemExit(f"unknown workload {name}")
     desc = WORKLOADS[name][2]
+    if name == "conv3x3_int8":
+        b = G.GraphBuilder(seed)
+        x = b.input("x", (batch, 56, 56, 64), "i8", 0.02)
+        b.output(b.conv(x, 64, k=3, act="relu", out_scale=0.05, name="conv"))
+        return b.g, {"workload": desc, "batch_per_gpu": batch, "layers": "one fused conv (input scale 0.02, output 0.05)"}
+    if name in QGEMM_SHAPES:
+        m, n, k = QGEMM_SHAPES[name]
+        b = G.GraphBuilder(seed, act_scale_range=(0.001, 0.01))
+        x = b.input("a", (batch, 1, m, k), "i8", 0.005)
+        b.output(b.conv(x, n, k=1, act="none", name="qgemm"))
+        return b.g, {"workload": desc, "batch_per_gpu": batch, "m": m, "n": n, "k": k,
+                     "layers": "QGemm as a 1x1 conv over M rows (int32 bias, per-column M)"}
     if name == "resnet50_fp16":
         g = G.resnet50_fp16(batch=batch, seed=seed)
         cfg = {"workload": desc, "batch_per_gpu": batch, "stages": [3, 4, 6, 3], "classes": 1000,
@@ -240,7 +258,7 @@ def run_ours(args, rank, world, local_rank):
     graph, cfg = build_workload(args.workload, batch, seed=1234)
     be = dw.CudaBackend(local_rank)
     rt = CudaGraphRuntime(graph, be)
-    graph = rt.graph  # after the device passes (fusion, input unfold); same work, fewer ops
+    graph0, graph = graph, rt.graph  # after the device passes (fusion, input unfold); same work, fewer ops
     x_name = graph.inputs[0]
     xt = graph.tensors[x_name]
     x_host = make_input(graph, 1000 + rank)
@@ -335,7 +353,7 @@ def run_ours(args, rank, world, local_rank):
     # ---- CPU baseline (rank 0, single GPU only): the oracle on a bounded sample
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(graph, x_host, args.cpu_images, WORKLOADS[args.workload][1])
+        cpu = cpu_baseline(graph0, x_host, args.cpu_images, WORKLOADS[args.workload][1])  # the reference's ops
 
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -364,6 +382,9 @@ def run_ours(args, rank, world, local_rank):
                      "peak_note": "fp16 dense peak = the measured bf16 cuBLAS figure" if f16 else
                      "int8 dense peak taken as 2x the measured bf16 cuBLAS figure"})
         images = batch * world
+        ws = sum(t.nbytes for t in graph.tensors.values()) + sum(a.nbytes for a in graph.initializers.values())
+        l2_note = (f"per-step working set {ws / 1e6:.0f} MB, larger than the 126 MB L2 (no flush needed)"
+                   if ws > 126e6 else f"per-step working set {ws / 1e6:.1f} MB fits in the 126 MB L2: cache-warm figure")
         tops = step_ops * world / (ms_per_step * 1e-3) / 1e12
         ips = images / (ms_per_step * 1e-3)
         unit = WORKLOADS[args.workload][1]
@@ -387,7 +408,7 @@ def run_ours(args, rank, world, local_rank):
             "conv_tops": round(tops, 3),
             "pct_of_tensor_peak": round(100.0 * tops / (int8_peak * world), 2),
             "config": dict(cfg, parallelism=f"replicas x{world} (batch-sharded, no collective)",
-                           global_batch=images, l2="per-step working set several GB, far larger than the 126 MB L2"),
+                           global_batch=images, l2=l2_note),
             "e2e": {"value": round(e2e_ips if unit == "images/s" else e2e_tops, 3), "unit": unit,
                     "images_per_s": round(e2e_ips, 1), "conv_tops": round(e2e_tops, 3),
                     "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
@@ -423,17 +444,23 @@ def load_traffic(op):
         return None
 
 
-def cpu_baseline(graph, x_host, images, unit):
+def cpu_baseline(graph, x_host, images, unit, target_s=15.0):
     """Times the oracle (C restatement of the reference's scalar ops, row-partitioned
-    over all host threads like dragonwing-cpu's pool.rs) on `images` images."""
+    over all host threads like dragonwing-cpu's pool.rs) on a bounded sample: one
+    image to size it, then as many images of the batch as take about `target_s`
+    seconds (at least `images`)."""
     from oracle import dwref
     from oracle.graph_ref import run_graph
     threads = dwref.num_cpus()
     feeds = {graph.inputs[0]: x_host}
+    batch = graph.tensors[graph.inputs[0]].shape[0]
+    t0 = time.perf_counter()
+    run_graph(graph, feeds, threads=threads, batch_slice=(0, 1))
+    t1 = time.perf_counter() - t0
+    images = max(images, min(batch, int(target_s / max(t1, 1e-3))))
     t0 = time.perf_counter()
     run_graph(graph, feeds, threads=threads, batch_slice=(0, images))
     dt = time.perf_counter() - t0
-    batch = graph.tensors[graph.inputs[0]].shape[0]
     ops_per_image = graph.conv_ops() / batch
     value = images / dt if unit == "images/s" else ops_per_image * images / dt / 1e12
     return {"value": round(value, 6), "unit": unit, "cores": threads, "kind": "port",
@@ -502,6 +529,34 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def profile_op(args):
+    """Runs one op of the workload graph (after the device passes) eagerly:
+    one untimed launch, then --steps launches.  No timing, no JSON."""
+    import dragonwing_edge_rs_b200 as dw
+    from dragonwing_edge_rs_b200.graph import CudaGraphRuntime
+    batch = args.batch or workload_defaults(args.workload)
+    graph, _ = build_workload(args.workload, batch, seed=1234)
+    be = dw.CudaBackend(0)
+    rt = CudaGraphRuntime(graph, be)
+    rt.set_input_bytes(graph.inputs[0], make_input(graph, 1000))
+    rt.run()  # every tensor holds real data
+    names = [op.name for op in rt.graph.ops]
+    if args.profile_op not in names:
+        raise SystemExit(f"unknown op {args.profile_op}; ops: {' '.join(names)}")
+    fn = rt._dispatch[names.index(args.profile_op)]
+    be.synchronize(120000)
+    import torch
+    torch.cuda.set_device(0)
+    torch.cuda.profiler.start()  # for `ncu --profile-from-start off`: only this op's launches
+    for _ in range(1 + args.steps):
+        fn()
+    be.synchronize(120000)
+    torch.cuda.profiler.stop()
+    print(f"profiled {args.profile_op} x{1 + args.steps} ({args.workload}, batch {batch})")
+    rt.release()
+    be.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -514,7 +569,14 @@ def main():
     ap.add_argument("--cpu-images", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=150.0)
+    ap.add_argument("--profile-op", default="",
+                    help="profiling aid: run the workload graph once, then only this op (of the graph after the "
+                         "device passes) 1 + --steps times inside cudaProfilerStart/Stop, and exit "
+                         "(for ncu --profile-from-start off captures of one kernel)")
     args = ap.parse_args()
+    if args.profile_op:
+        profile_op(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
