@@ -90,6 +90,11 @@ SIGNATURES = {
     "dw_concat_i8": ([vp, PVP, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, sz, vp], i32),
     "dw_slice_c_i8": ([vp, vp, vp, sz, sz, sz, sz], i32),
     "dw_resize_nearest_i8": ([vp, vp, vp] + [sz] * 6, i32),
+    "dw_copy_async": ([vp, vp, sz, vp, sz, sz], i32),
+    "dw_event_create": ([vp, PVP], i32),
+    "dw_event_destroy": ([vp], None),
+    "dw_event_record": ([vp, vp], i32),
+    "dw_stream_wait_event": ([vp, vp], i32),
     # fp16 path
     "dw_prepare_weights_f16": ([vp, ctypes.POINTER(DwConvDesc), vp, PVP], i32),
     "dw_conv2d_f16": ([vp, ctypes.POINTER(DwConvDesc), vp, vp, vp, vp], i32),

@@ -72,6 +72,27 @@ def _host_view(data) -> tuple[ctypes.c_void_p, int, object]:
     raise TypeError(f"unsupported host buffer type {type(data)!r}")
 
 
+class CudaEvent:
+    """A stream-ordering point between backends (streams) of one GPU."""
+
+    def __init__(self, backend: "CudaBackend"):
+        self._lib = L.load()
+        out = ctypes.c_void_p()
+        backend._check(self._lib.dw_event_create(backend.handle, ctypes.byref(out)))
+        self.handle = out
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.dw_event_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class CudaBackend:
     """One B200 GPU and one CUDA stream (``impl Backend for CudaBackend``)."""
 
@@ -144,6 +165,21 @@ class CudaBackend:
 
     def download_async(self, src: CudaBuffer, host_ptr: int, nbytes: int, src_offset: int = 0) -> None:
         self._check(self._lib.dw_download_async(self.handle, src.handle, src_offset, ctypes.c_void_p(host_ptr), nbytes))
+
+    def copy_async(self, dst: CudaBuffer, src: CudaBuffer, nbytes: int, dst_offset: int = 0,
+                   src_offset: int = 0) -> None:
+        self._check(self._lib.dw_copy_async(self.handle, dst.handle, dst_offset, src.handle, src_offset, nbytes))
+
+    def event(self) -> "CudaEvent":
+        return CudaEvent(self)
+
+    def record(self, ev: "CudaEvent") -> None:
+        """Records `ev` at the current end of this backend's stream."""
+        self._check(self._lib.dw_event_record(self.handle, ev.handle))
+
+    def wait(self, ev: "CudaEvent") -> None:
+        """Work enqueued on this backend after the call waits for `ev`."""
+        self._check(self._lib.dw_stream_wait_event(self.handle, ev.handle))
 
     def stream(self) -> int:
         return int(self._lib.dw_stream(self.handle) or 0)

@@ -216,6 +216,50 @@ DW_API dw_status dw_download_async(dw_backend *be, const dw_buf *src, size_t src
         "download_async");
 }
 
+DW_API dw_status dw_copy_async(dw_backend *be, dw_buf *dst, size_t dst_offset, const dw_buf *src, size_t src_offset,
+                               size_t len) {
+    if (!be || !dst || !src) return DW_ERR_INVALID_ARG;
+    if (dst_offset > dst->len || len > dst->len - dst_offset || src_offset > src->len || len > src->len - src_offset)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "copy_async: range of %zu bytes outside a buffer", len);
+    return dw_cuda_check(be,
+                         cudaMemcpyAsync((char *)dst->ptr + dst_offset, (const char *)src->ptr + src_offset, len,
+                                         cudaMemcpyDeviceToDevice, be->stream),
+                         "copy_async");
+}
+
+struct dw_event {
+    cudaEvent_t ev = nullptr;
+    int device = 0;
+};
+
+DW_API dw_status dw_event_create(dw_backend *be, dw_event **out) {
+    if (!be || !out) return DW_ERR_INVALID_ARG;
+    *out = nullptr;
+    cudaSetDevice(be->device);
+    cudaEvent_t ev;
+    dw_status st = dw_cuda_check(be, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event_create");
+    if (st != DW_OK) return st;
+    *out = new dw_event{ev, be->device};
+    return DW_OK;
+}
+
+DW_API void dw_event_destroy(dw_event *ev) {
+    if (!ev) return;
+    cudaSetDevice(ev->device);
+    cudaEventDestroy(ev->ev);
+    delete ev;
+}
+
+DW_API dw_status dw_event_record(dw_backend *be, dw_event *ev) {
+    if (!be || !ev) return DW_ERR_INVALID_ARG;
+    return dw_cuda_check(be, cudaEventRecord(ev->ev, be->stream), "event_record");
+}
+
+DW_API dw_status dw_stream_wait_event(dw_backend *be, dw_event *ev) {
+    if (!be || !ev) return DW_ERR_INVALID_ARG;
+    return dw_cuda_check(be, cudaStreamWaitEvent(be->stream, ev->ev, 0), "stream_wait_event");
+}
+
 DW_API dw_status dw_synchronize(dw_backend *be, uint32_t timeout_ms) {
     if (!be) return DW_ERR_INVALID_ARG;
     cudaSetDevice(be->device);

@@ -785,3 +785,70 @@ class CudaGraphRuntime:
             self.release()
         except Exception:
             pass
+
+
+class PipelinedRunner:
+    """Serving loop over a CudaGraphRuntime with the host copies overlapped.
+
+    Two copy backends (their own streams on the same GPU) move data while the
+    compute backend runs: step i's input is uploaded into a device staging slot
+    while step i-1 computes, and step i's outputs are copied on the device into
+    a staging slot and read back while step i+1 computes.  `depth` slots of each;
+    events order the three streams.  Every step still copies its whole input to
+    the device and its whole output to the host (what `run_steps` returns)."""
+
+    def __init__(self, rt: "CudaGraphRuntime", depth: int = 2):
+        self.rt, self.depth = rt, depth
+        be = rt.be
+        self.up, self.down = CudaBackend(be.device), CudaBackend(be.device)
+        g = rt.graph
+        if len(g.inputs) != 1:
+            raise BackendError(L.DW_ERR_UNSUPPORTED, "PipelinedRunner: one graph input expected")
+        self.in_name = g.inputs[0]
+        self.in_bytes = g.tensors[self.in_name].nbytes
+        self.out_names = list(g.outputs)
+        self.out_sizes = [g.tensors[o].nbytes for o in self.out_names]
+        self.out_bytes = sum(self.out_sizes)
+        self.stage_in = [be.alloc(self.in_bytes) for _ in range(depth)]
+        self.stage_out = [[be.alloc(n) for n in self.out_sizes] for _ in range(depth)]
+        ev = lambda b: [b.event() for _ in range(depth)]  # noqa: E731
+        self.h2d_done, self.in_free = ev(self.up), ev(be)
+        self.out_ready, self.d2h_done = ev(be), ev(self.down)
+        self.steps = 0
+
+    def step(self, host_in_ptr: int, host_out_ptr: int) -> None:
+        """Enqueues one step: upload `in_bytes` from pinned `host_in_ptr`, run the
+        graph, read all outputs back (concatenated) into pinned `host_out_ptr`."""
+        i, d, be, rt = self.steps, self.steps % self.depth, self.rt.be, self.rt
+        if i >= self.depth:
+            self.up.wait(self.in_free[d])  # the slot's previous input was copied into the graph
+        self.up.upload_async(self.stage_in[d], host_in_ptr, self.in_bytes)
+        self.up.record(self.h2d_done[d])
+        be.wait(self.h2d_done[d])
+        be.copy_async(rt.bufs[self.in_name], self.stage_in[d], self.in_bytes)
+        be.record(self.in_free[d])
+        rt.run()
+        if i >= self.depth:
+            be.wait(self.d2h_done[d])  # the slot's previous outputs reached the host
+        for o, n, dst in zip(self.out_names, self.out_sizes, self.stage_out[d]):
+            be.copy_async(dst, rt.bufs[o], n)
+        be.record(self.out_ready[d])
+        self.down.wait(self.out_ready[d])
+        off = 0
+        for n, src in zip(self.out_sizes, self.stage_out[d]):
+            self.down.download_async(src, host_out_ptr + off, n)
+            off += n
+        self.down.record(self.d2h_done[d])
+        self.steps += 1
+
+    def synchronize(self, timeout_ms: int = 600000) -> None:
+        for b in (self.up, self.rt.be, self.down):
+            b.synchronize(timeout_ms)
+
+    def close(self) -> None:
+        self.synchronize()
+        for evs in (self.h2d_done, self.in_free, self.out_ready, self.d2h_done):
+            for e in evs:
+                e.close()
+        self.up.close()
+        self.down.close()

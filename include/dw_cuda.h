@@ -112,6 +112,19 @@ DW_API dw_status dw_download(dw_backend *be, const dw_buf *src, void *dst, size_
 /* Asynchronous twins on the backend stream (host memory should be pinned). */
 DW_API dw_status dw_upload_async(dw_backend *be, dw_buf *dst, size_t dst_offset, const void *src, size_t len);
 DW_API dw_status dw_download_async(dw_backend *be, const dw_buf *src, size_t src_offset, void *dst, size_t len);
+/* Device-to-device copy on the backend stream (staging for pipelined serving). */
+DW_API dw_status dw_copy_async(dw_backend *be, dw_buf *dst, size_t dst_offset, const dw_buf *src,
+                               size_t src_offset, size_t len);
+/* Stream ordering between backends on one GPU (each backend owns a stream): a
+ * copy backend can upload step i+1's input and read back step i's output while
+ * the compute backend runs.  Buffers of one GPU may be used by any backend on it. */
+typedef struct dw_event dw_event;
+DW_API dw_status dw_event_create(dw_backend *be, dw_event **out);
+DW_API void dw_event_destroy(dw_event *ev);
+/* Records `ev` at the current end of be's stream. */
+DW_API dw_status dw_event_record(dw_backend *be, dw_event *ev);
+/* Work enqueued on be's stream after this call waits for `ev`. */
+DW_API dw_status dw_stream_wait_event(dw_backend *be, dw_event *ev);
 /* Backend::synchronize (backend.rs:187-198) with a deadline: DW_ERR_TIMEOUT when
  * the queued work has not finished after timeout_ms (0 = no deadline); also
  * reports DW_ERR_KERNEL_WAIT_EXPIRED if a kernel's bounded wait gave up. */
