@@ -29,11 +29,13 @@ STATUS_NAMES = {
 EPI_NONE, EPI_RELU, EPI_RELU6, EPI_SILU = 0, 1, 2, 3
 # dw_conv_path
 PATH_AUTO, PATH_DIRECT, PATH_UMMA = 0, 1, 2
+# dw_dw_variant
+DWV_AUTO, DWV_SLAB, DWV_STREAM2, DWV_STREAM2X2, DWV_STREAM4, DWV_WS = 0, 1, 2, 3, 4, 5
 
 
 class DwConfig(ctypes.Structure):
     _fields_ = [("wait_cap_ms", ctypes.c_uint32), ("trace", ctypes.c_int32), ("conv_path", ctypes.c_int32),
-                ("reserved", ctypes.c_int32 * 5)]
+                ("dw_variant", ctypes.c_int32), ("reserved", ctypes.c_int32 * 4)]
 
 
 class DwConvDesc(ctypes.Structure):

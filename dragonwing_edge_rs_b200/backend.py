@@ -96,12 +96,14 @@ class CudaEvent:
 class CudaBackend:
     """One B200 GPU and one CUDA stream (``impl Backend for CudaBackend``)."""
 
-    def __init__(self, device: int = 0, wait_cap_ms: int = 0, trace: bool = False, conv_path: int = L.PATH_AUTO):
+    def __init__(self, device: int = 0, wait_cap_ms: int = 0, trace: bool = False, conv_path: int = L.PATH_AUTO,
+                 dw_variant: int = 0):
         self._lib = L.load()
         cfg = L.DwConfig()
         cfg.wait_cap_ms = wait_cap_ms
         cfg.trace = 1 if trace else 0
         cfg.conv_path = conv_path
+        cfg.dw_variant = dw_variant
         out = ctypes.c_void_p()
         st = self._lib.dw_create(device, ctypes.byref(cfg), ctypes.byref(out))
         if st != L.DW_OK:

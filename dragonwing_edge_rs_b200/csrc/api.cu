@@ -91,6 +91,7 @@ DW_API dw_status dw_create(int device_ordinal, const dw_config *cfg, dw_backend 
     be->cfg.wait_cap_ms = (uint32_t)env_int("DW_WAIT_CAP_MS", be->cfg.wait_cap_ms ? (int)be->cfg.wait_cap_ms : 2000);
     be->cfg.trace = env_int("DW_TRACE", be->cfg.trace);
     be->cfg.conv_path = env_int("DW_CONV_PATH", be->cfg.conv_path);
+    be->cfg.dw_variant = env_int("DW_DW_VARIANT", be->cfg.dw_variant);
     be->wait_cap_ns = (uint64_t)be->cfg.wait_cap_ms * 1000000ull;
     if (cudaSetDevice(device_ordinal) != cudaSuccess) { delete be; return DW_ERR_DEVICE; }
     cudaDeviceProp prop;

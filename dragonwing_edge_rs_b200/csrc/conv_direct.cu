@@ -551,6 +551,13 @@ dw_status launch_dwconv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     const int mult = d.c_out / d.c_in;
     const bool aligned4 = (uintptr_t)x % 4 == 0 && (uintptr_t)w_hwcm % 4 == 0 && (uintptr_t)y % 4 == 0;
     if (mult == 1 && !acc_out && be->cfg.conv_path != DW_PATH_DIRECT) {  // DIRECT: the register-fed kernels
+        const int v = be->cfg.dw_variant;
+        if (v != DW_DWV_SLAB) {
+            // auto: the 2-column streaming kernel with 18 consumer warps (fastest measured)
+            const int shape = v == DW_DWV_STREAM2X2 ? 1 : v == DW_DWV_STREAM4 ? 2 : v == DW_DWV_WS ? 3 : 0;
+            const dw_status st = launch_dwconv3x3_stream_i8(be, d, ho, wo, x, w_hwcm, ep, y, shape);
+            if (st != DW_ERR_UNSUPPORTED) return st;
+        }
         const dw_status st = launch_dwconv3x3_tma_i8(be, d, ho, wo, x, w_hwcm, ep, y);
         if (st != DW_ERR_UNSUPPORTED) return st;
     }

@@ -109,6 +109,8 @@ dw_status launch_im2col_u8_i8(dw_backend *be, const uint8_t *x, int8_t *y, int n
                               int sh, int sw, int pt, int pl, int ho, int wo, int c_dst, float scale);
 
 // dwconv_tma.cu (TMA-fed int8 depthwise 3x3 stride 1; DW_ERR_UNSUPPORTED when the shape does not fit)
+dw_status launch_dwconv3x3_stream_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
+                                     const int8_t *w_hwcm, const EpiParams &ep, int8_t *y, int shape);
 dw_status launch_dwconv3x3_tma_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
                                   const int8_t *w_hwcm, const EpiParams &ep, int8_t *y);
 

@@ -50,8 +50,18 @@ typedef struct dw_config {
     uint32_t wait_cap_ms; /* limit for every device-side wait (mbarrier/TMA); 0 = 2000 ms */
     int32_t trace;        /* nonzero: synchronize and log after every op (DRAGONWING_TRACE) */
     int32_t conv_path;    /* DW_PATH_*: which convolution kernels to use */
-    int32_t reserved[5];
+    int32_t dw_variant;   /* int8 depthwise 3x3 s1 kernel: 0 auto, DW_DWV_* to force one (tuning, tests) */
+    int32_t reserved[4];
 } dw_config;
+
+enum dw_dw_variant {
+    DW_DWV_AUTO = 0,
+    DW_DWV_SLAB = 1,     /* 64-channel slabs, one row per copy */
+    DW_DWV_STREAM2 = 2,   /* persistent whole-pixel streaming, 4 channels x 2 columns per thread, 18 warps (the default) */
+    DW_DWV_STREAM2X2 = 3, /* the same, two CTAs of 9 consumer warps per SM */
+    DW_DWV_STREAM4 = 4,   /* 4 channels x 4 columns per thread, 9 consumer warps */
+    DW_DWV_WS = 5         /* warp-specialised: 9 dp4a warps + 9 requantisation warps */
+};
 
 enum dw_conv_path {
     DW_PATH_AUTO = 0,   /* tensor-core (tcgen05) kernels where the shape allows, else CUDA cores */

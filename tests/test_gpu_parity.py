@@ -27,6 +27,15 @@ def be_direct():
     b.close()
 
 
+@pytest.fixture(scope="module", params=[dw.DWV_SLAB, dw.DWV_STREAM2, dw.DWV_STREAM2X2, dw.DWV_STREAM4, dw.DWV_WS],
+                ids=["slab", "stream2", "stream2x2", "stream4", "ws"])
+def be_dwv(request):
+    """A backend forced onto one int8 depthwise 3x3 s1 kernel variant."""
+    b = dw.CudaBackend(0, dw_variant=request.param)
+    yield b
+    b.close()
+
+
 @pytest.fixture(scope="module")
 def be_umma():
     b = dw.CudaBackend(0, conv_path=dw.PATH_UMMA)
@@ -240,16 +249,60 @@ def test_depthwise_parity(be, mult, c, epi):
                                    (2, 30, 27, 128, (0, 2, 1, 0)), (1, 60, 120, 64, (1, 1, 1, 1))],
                          ids=lambda s: f"{s[0]}x{s[1]}x{s[2]}x{s[3]}p{''.join(map(str, s[4]))}")
 @pytest.mark.parametrize("epi", [dw.EPI_RELU6, dw.EPI_SILU, dw.EPI_NONE])
-def test_depthwise_s1_segments_and_edges(be, be_direct, shape, epi):
-    """Stride-1 depthwise over row segments and 4-column strips: heights that
+def test_depthwise_s1_segments_and_edges(be, be_direct, be_dwv, shape, epi):
+    """Stride-1 depthwise over row segments and column strips: heights that
     are not multiples of the segment, widths not multiples of 4, asymmetric
-    pads; bit-exact against the oracle on the TMA-fed kernel (64-channel
-    slabs, default path) and the register-fed one (DW_PATH_DIRECT)."""
+    pads; bit-exact against the oracle on the default path, the register-fed
+    kernel (DW_PATH_DIRECT) and each TMA-fed variant (64-channel slabs; the
+    persistent whole-pixel streaming kernel with 2 or 4 columns per thread)."""
     n, h, w, c, pads = shape
     rng = np.random.default_rng(h * w + c + epi)
     case = conv_case(rng, n, h, w, c, c, k=3, s=1, pads=pads, group=c, epilogue=epi)
     _check_conv(be, case)
     _check_conv(be_direct, case)
+    _check_conv(be_dwv, case)
+
+
+@pytest.mark.parametrize("shape", [(5, 9, 9, 64), (7, 3, 5, 16), (2, 112, 112, 32), (4, 14, 14, 960),
+                                   (3, 7, 7, 160), (2, 28, 28, 144), (1, 56, 56, 96), (9, 1, 12, 48)],
+                         ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("epi", [dw.EPI_RELU6, dw.EPI_RELU, dw.EPI_NONE])
+def test_depthwise_stream_shapes(be_dwv, shape, epi):
+    """MobileNet-style channel counts (16 .. 960: one or several channel groups
+    per lane), small maps where one CTA's row range crosses several images,
+    a one-row image; bit-exact on every variant."""
+    n, h, w, c = shape
+    rng = np.random.default_rng(n * h * w + c + 7 * epi)
+    case = conv_case(rng, n, h, w, c, c, k=3, s=1, group=c, epilogue=epi)
+    _check_conv(be_dwv, case)
+
+
+@pytest.mark.parametrize("epi", [dw.EPI_RELU6, dw.EPI_RELU, dw.EPI_NONE])
+def test_depthwise_requant_ties_and_slow_channels(be, be_dwv, epi):
+    """Requantisation edge cases of the depthwise kernels: M = 1/8 and 1/4
+    (every fourth / second odd accumulator lands exactly on a .5 tie), channels
+    whose |M| or bias leave the fast range (exact per-element path), a zero
+    and a negative M, large negative biases (results clamp at the bounds), and
+    a ReLU6 ceiling of 0."""
+    c = 64
+    rng = np.random.default_rng(4242 + epi)
+    desc, x, wt, b, M, D = conv_case(rng, 3, 17, 23, c, c, k=3, s=1, group=c, epilogue=epi, x_range=(-128, 127))
+    M = M.copy()
+    M[0:16] = np.float32(0.125)
+    M[16:24] = np.float32(0.25)
+    M[24] = np.float32(1.0)        # |M| * max|acc| beyond the fast range
+    M[25] = np.float32(0.0)
+    M[26] = np.float32(-0.01)
+    M[27] = np.float32(3.0e-5)
+    b = b.copy()
+    b[28] = 3_000_000              # |bias| >= 2^21: exact path
+    b[29] = -2_500_000
+    b[30:34] = -60_000
+    b[34:38] = 60_000
+    for q6 in (desc.q6, 0):
+        desc.q6 = q6
+        _check_conv(be, (desc, x, wt, b, M, D))
+        _check_conv(be_dwv, (desc, x, wt, b, M, D))
 
 
 @pytest.mark.parametrize("geo", [(2, 64, 48, 3, 3, 3, 2, 2, 1, 1, 32), (1, 17, 9, 3, 3, 3, 1, 1, 1, 1, 32),
