@@ -9,11 +9,11 @@ call raises.
 """
 from . import ops, quantization
 from ._lib import EPI_NONE, EPI_RELU, EPI_RELU6, EPI_SILU, PATH_AUTO, PATH_DIRECT, PATH_UMMA
-from ._lib import DWV_AUTO, DWV_SLAB, DWV_STREAM2, DWV_STREAM2X2, DWV_STREAM4, DWV_WS
+from ._lib import DWV_AUTO, DWV_SLAB, DWV_STREAM2, DWV_STREAM2X2, DWV_STREAM4
 from .backend import BackendError, BufferKind, CudaBackend, CudaBuffer, device_count
 from .ops import ConvDesc
 
 __all__ = [
     "BackendError", "BufferKind", "CudaBackend", "CudaBuffer", "ConvDesc", "device_count", "ops", "quantization",
-    "EPI_NONE", "EPI_RELU", "EPI_RELU6", "EPI_SILU", "PATH_AUTO", "PATH_DIRECT", "PATH_UMMA", "DWV_AUTO", "DWV_SLAB", "DWV_STREAM2", "DWV_STREAM2X2", "DWV_STREAM4", "DWV_WS",
+    "EPI_NONE", "EPI_RELU", "EPI_RELU6", "EPI_SILU", "PATH_AUTO", "PATH_DIRECT", "PATH_UMMA", "DWV_AUTO", "DWV_SLAB", "DWV_STREAM2", "DWV_STREAM2X2", "DWV_STREAM4",
 ]

@@ -30,7 +30,7 @@ EPI_NONE, EPI_RELU, EPI_RELU6, EPI_SILU = 0, 1, 2, 3
 # dw_conv_path
 PATH_AUTO, PATH_DIRECT, PATH_UMMA = 0, 1, 2
 # dw_dw_variant
-DWV_AUTO, DWV_SLAB, DWV_STREAM2, DWV_STREAM2X2, DWV_STREAM4, DWV_WS = 0, 1, 2, 3, 4, 5
+DWV_AUTO, DWV_SLAB, DWV_STREAM2, DWV_STREAM2X2, DWV_STREAM4 = 0, 1, 2, 3, 4
 
 
 class DwConfig(ctypes.Structure):

@@ -554,7 +554,7 @@ dw_status launch_dwconv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         const int v = be->cfg.dw_variant;
         if (v != DW_DWV_SLAB) {
             // auto: the 2-column streaming kernel with 18 consumer warps (fastest measured)
-            const int shape = v == DW_DWV_STREAM2X2 ? 1 : v == DW_DWV_STREAM4 ? 2 : v == DW_DWV_WS ? 3 : 0;
+            const int shape = v == DW_DWV_STREAM2X2 ? 1 : v == DW_DWV_STREAM4 ? 2 : 0;
             const dw_status st = launch_dwconv3x3_stream_i8(be, d, ho, wo, x, w_hwcm, ep, y, shape);
             if (st != DW_ERR_UNSUPPORTED) return st;
         }

@@ -1,34 +1,45 @@
 // dwconv_stream.cu -- int8 depthwise 3x3 stride-1 convolution, persistent and
 // streaming over whole pixels.
 //
-// Work is a list of output rows ordered lane-major, where a lane is a column
-// strip of `cw` output columns over a channel group of `cg` channels (all the
-// channels when they fit): row index g -> lane g / (n*ho), image, output row.
-// Each CTA takes one contiguous range of that list (the ranges are equal to
-// within one row, so the SMs finish together) and streams it: a producer lane
-// loads stages of three input rows, each row the strip's cw + 2 columns of
-// whole cg-channel pixels (contiguous in NHWC when cg == c), through the
-// tensor map into a ring of shared-memory slots; zero fill supplies the
-// padding.  A run of rows inside one image is a segment; crossing into the
-// next image restarts the rotation with two halo rows.
+// Work layout.  A lane is a column strip of `cw` output columns over a channel
+// group of `cg` channels (all the channels when they fit).  The grid is
+// lanes x per_lane CTAs: CTA i streams lane i % lanes, output rows
+// [k R / per_lane, (k + 1) R / per_lane) of it (k = i / lanes, R = n * ho,
+// rows counted image after image), so CTAs that run side by side cover the
+// same image rows of neighbouring strips (their halo columns meet in L2 and
+// whole image rows are in flight together).  A run of rows inside one image is
+// a segment; crossing into the next image restarts the row rotation with two
+// halo rows.
 //
-// Consumer threads own 4 channels x kCPT output columns.  Per input row a
-// thread reads its kCPT + 2 words, transposes them with byte permutes into
-// per-channel column packs, and adds each kernel row to three output rows with
-// one __dp4a per output and kernel row -- exact int32 sums, as in the
-// reference (crates/dragonwing-cpu/src/ops.rs:2669-2730 index order).  An
-// output row whose three kernel rows are in is requantised (the contract of
-// include/dw_cuda.h) and stored with coalesced 32-bit stores (consecutive
-// threads own consecutive channel words of a pixel).
+// Data movement.  A producer lane loads stages of three input rows through the
+// tensor map -- each row the strip's cw + 2 columns of whole cg-channel pixels,
+// contiguous in NHWC when cg == c -- into a ring of shared-memory slots; zero
+// fill supplies the padding rows and columns.
 //
-// ReLU / ReLU6 requantisation fast path, exact: v = fl(fl(acc) * M) as the
-// reference, then floor(v + 0.5) by two packed adds rounded toward zero (the
-// second one places the integer in the low mantissa bits of 1.5 * 2^23); for
-// v >= 0 that is roundf(v), and below zero both are <= 0, which the ReLU bound
-// maps to 0.  The bounds are applied to the packed int16 pair with one
-// max(min(x, hi), 0); clamping the integer after rounding equals rounding after
-// clamping because the bounds are integers.  |v| < 2^15 on the fast path;
-// channels outside it take the exact per-element epilogue.
+// Arithmetic.  Consumer threads own 4 channels x kCPT output columns.  Per
+// input row a thread reads its kCPT + 2 words, transposes them with byte
+// permutes into per-channel column packs, and adds each kernel row to three
+// output rows with one __dp4a per output and kernel row: exact int32 sums, as
+// in the reference (crates/dragonwing-cpu/src/ops.rs:2669-2730 index order).
+// An output row whose three kernel rows are in is requantised and stored with
+// coalesced 32-bit stores (consecutive threads own consecutive channel words
+// of a pixel).
+//
+// Requantisation (the contract of include/dw_cuda.h), exact on every path:
+//  * ReLU / ReLU6: v = fl(fl(acc + bias) * M) as the reference, then
+//    floor(v + 0.5) by two packed adds rounded toward zero (the second places
+//    the integer in the low mantissa bits of 1.5 * 2^23).  For v >= 0 that is
+//    roundf(v); below zero both are <= 0, which the ReLU bound maps to 0.  The
+//    bounds go on the packed int16 pair with one max(min(x, hi), 0); clamping
+//    the integer after rounding equals rounding after clamping because the
+//    bounds are integers.
+//  * no activation: clamp to [-128, 127] in f32, rint by the magic add, ties
+//    moved away from zero.
+//  The fast paths need |acc + bias| < 2^22, a finite M and, for the int16
+//  pairs, |v| < 2^15.  A thread whose channels miss that (pathological scales
+//  or biases) recomputes its outputs after the stream, element by element with
+//  the reference epilogue, over its own earlier stores; the hot loop carries
+//  no exact path.  SiLU is not taken here (the slab kernel handles it).
 //
 // Every wait is bounded (globaltimer); a wait that gives up records
 // DW_DEV_WAIT_EXPIRED, the CTA stops, and the producer lets its copies in
@@ -45,31 +56,31 @@ namespace {
 constexpr int kStreamMaxSlots = 8;
 
 // CTA shapes: columns per thread, the most consumer threads (plus one producer
-// warp) and the CTAs per SM the register budget is compiled for.
+// warp) and the CTAs per SM the register budget is compiled for.  19 warps on
+// an SM leave 96 registers a thread (the register file is split four ways).
 struct StShape {
     int cpt, max_cons, min_blocks;
 };
 constexpr StShape kStShapes[3] = {
-    {2, 576, 1},  // 18 consumer warps, <= 96 registers
+    {2, 576, 1},  // 18 consumer warps (the default)
     {2, 288, 2},  // two CTAs of 9 consumer warps
-    {4, 288, 1},  // 9 consumer warps, 4 x 4 tiles, <= 168 registers
+    {4, 288, 1},  // 9 consumer warps with 4 x 4 tiles
 };
 
 struct DwStreamParams {
     int n, h, w, c, ho, wo, pt, pl;
-    int cg;        // channels per lane
-    int words;     // cg / 4
-    int groups;    // c / cg
-    int cw;        // output columns per strip
-    int strips;    // column strips per row
-    int bw;        // input columns per stage row: cw + 2
-    int q_per;     // column groups per strip: cw / kCPT
-    uint32_t row_bytes;    // bw * cg
-    uint32_t stage_bytes;  // 3 * row_bytes (the box)
+    int cg;                // channels per lane
+    int words;             // cg / 4
+    int groups;            // c / cg
+    int cw;                // output columns per strip
+    int strips;            // column strips per row
+    int bw;                // input columns per stage row: cw + 2
+    uint32_t stage_bytes;  // 3 * bw * cg (the box)
     uint32_t slot_bytes;   // stage_bytes rounded up to 128
     int slots;
-    int cons_threads;      // words * q_per
-    int per_lane;          // CTAs per lane (each takes n * ho / per_lane rows of it)
+    int cons_threads;      // words * cw / kCPT
+    int per_lane;          // CTAs per lane
+    const int8_t *x;       // the input (the exact recomputation reads it directly)
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
@@ -91,6 +102,12 @@ __device__ __forceinline__ bool st_wait(uint32_t bar, uint32_t parity, const DwS
             return false;
         }
     }
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
 }
 
 // Per-channel column packs of one input row and the three kernel-row dot
@@ -144,17 +161,14 @@ __device__ __forceinline__ void st_row(const uint32_t (&X)[kCPT + 2], const int3
     }
 }
 
-// ReLU-family fast requantisation of 4 channels (header comment), exact and
-// branchless; returns the 4 result bytes.  The accumulators start at bias +
-// the bit pattern of 1.5 * 2^23, so reading them as floats and subtracting
-// 1.5 * 2^23 gives acc + bias exactly; v = fl(that * M) as the reference.
-// u = v + 0.5 rounded toward zero keeps floor(u) == floor(v + 0.5) (integers
-// are representable, so rounding toward zero never crosses one), and
-// u + 1.5 * 2^23 rounded toward zero is 1.5 * 2^23 + floor(u) (|u| < 2^22),
-// whose low 16 bits are floor(v + 0.5) as int16.  For v >= 0 that is roundf(v);
-// for v < 0 it is <= 0 like roundf(v), and the ReLU bound maps both to 0.  The
-// last step applies [0, hi] to both int16 lanes.  The packed directed-rounding
-// adds issue on the FMA pipe at the full f32x2 rate.
+// ReLU-family fast requantisation of 4 channels (header comment); returns the
+// 4 result bytes.  The accumulators start at bias + the bit pattern of
+// 1.5 * 2^23, so reading them as floats and subtracting 1.5 * 2^23 gives
+// acc + bias exactly.  u = v + 0.5 rounded toward zero keeps floor(u) ==
+// floor(v + 0.5) (integers are representable, so rounding toward zero never
+// crosses one), and u + 1.5 * 2^23 rounded toward zero is 1.5 * 2^23 +
+// floor(u) (|u| < 2^22), whose low 16 bits are floor(v + 0.5) as int16.  The
+// packed directed-rounding adds issue on the FMA pipe at the full f32x2 rate.
 __device__ __forceinline__ uint32_t requant_relu4(const int32_t (&a)[4], const float2 (&m)[2], uint32_t hi2) {
     const float2 half = make_float2(0.5f, 0.5f), mag = make_float2(kMagic, kMagic);
     uint32_t c[2];
@@ -194,50 +208,30 @@ __device__ __forceinline__ uint32_t requant_signed4(const int32_t (&a)[4], const
     return __byte_perm(pk[0], pk[1], 0x5410);
 }
 
-// The exact per-element epilogue for 4 channels starting at c0 (threads whose
-// channels are outside the fast range); loads its own parameters so that the
-// hot loop keeps none of them in registers.
-static __device__ __noinline__ uint32_t dw_slow4(int32_t a0, int32_t a1, int32_t a2, int32_t a3, int c0,
-                                                 const int32_t *__restrict__ bias, const float *__restrict__ M,
-                                                 const float *__restrict__ D, int epi, int q6, float inv_s_out) {
-    const int32_t a[4] = {a0, a1, a2, a3};
-    uint32_t packed = 0;
+// The thread's kernel rows for channel word gw: (w0, w1, w2, 0) bytes per channel.
+__device__ __forceinline__ void load_kernel_rows(const int8_t *__restrict__ w, int cwords, int gw,
+                                                 int32_t (&wk)[3][4]) {
+    const uint32_t *w32 = reinterpret_cast<const uint32_t *>(w);
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-        const int32_t b = bias ? __ldg(bias + c0 + k) : 0;
-        const float m = M ? __ldg(M + c0 + k) : 0.0f;
-        const float dsc = D ? __ldg(D + c0 + k) : 0.0f;
-        packed |= (uint32_t)(uint8_t)epilogue_one(a[k], b, m, dsc, epi, q6, inv_s_out) << (8 * k);
+    for (int kh = 0; kh < 3; kh++) {
+        const uint32_t k0 = __ldg(w32 + (size_t)(kh * 3 + 0) * cwords + gw);
+        const uint32_t k1 = __ldg(w32 + (size_t)(kh * 3 + 1) * cwords + gw);
+        const uint32_t k2 = __ldg(w32 + (size_t)(kh * 3 + 2) * cwords + gw);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t t01 = __byte_perm(k0, k1, (uint32_t)((4 + k) << 4 | k));
+            wk[kh][k] = (int32_t)(__byte_perm(t01, k2, (uint32_t)((4 + k) << 8 | 0x10)) & 0x00FFFFFFu);
+        }
     }
-    return packed;
 }
 
-// Exact ReLU / ReLU6 epilogue of 4 channels starting at c0, inlined (no call,
-// so the live accumulators stay in registers): roundf(clamp(fl(fl(acc + bias) * M)))
-// then max(q, 0) and min(q, hi), as in include/dw_cuda.h.
-__device__ __forceinline__ uint32_t relu_exact4(const int32_t (&a)[4], int c0, const EpiParams &ep, int hi) {
-    uint32_t packed = 0;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        const int32_t b = ep.bias ? __ldg(ep.bias + c0 + k) : 0;
-        const float m = ep.M ? __ldg(ep.M + c0 + k) : 0.0f;
-        const int32_t q = f32_to_i8(__fmul_rn(i2f_rn((int32_t)((uint32_t)a[k] + (uint32_t)b)), m));
-        packed |= (uint32_t)(uint8_t)min(max(q, 0), hi) << (8 * k);
-    }
-    return packed;
-}
-
-// Thread state for one lane (channel group) that the segment loop reads.
+// Thread state the segment loop reads.
 struct StThread {
     int32_t wk[3][4];  // kernel rows: (w0, w1, w2, 0) bytes per channel
-    int32_t init[4];   // accumulator start: bias + the magic bits (fast modes) or 0
+    int32_t init[4];   // accumulator start: bias + the magic bits
     float2 m2[2];      // M of channels 0,1 and 2,3
     uint32_t hi2;      // ReLU ceiling in both int16 lanes
-    int hi;            // the same as an int (exact ReLU path)
-    int c0;            // first channel (exact path)
 };
-
-enum { kModeExact = 0, kModeRelu = 1, kModeSigned = 2, kModeReluExact = 3 };
 
 // Position in the ring of input stages, advanced without divisions.
 struct RingPos {
@@ -247,35 +241,21 @@ struct RingPos {
     uint32_t ph;         // barrier phase parity of the current pass over the ring
 };
 
-__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-
 // One segment: `count` input rows from the ring position `rp` on; output rows
 // are stored from the third input row on.  kFull: every column of the thread
 // is inside the image (no per-store test).  Returns false when a wait gave up.
-template <int kCPT, int kMode, bool kFull>
+template <int kCPT, bool kRelu, bool kFull>
 __device__ __forceinline__ bool st_segment(const DwStreamParams &p, const StThread &ts, int count, RingPos &rp,
                                            uint32_t slot0_addr, uint32_t full0, uint32_t empty0,
                                            const uint32_t (&coff)[kCPT + 2], uint32_t rw4, uint32_t *yb,
                                            size_t row_words, int colmask, volatile int *abort_flag, int lane) {
     const int cwords = p.c >> 2;
-    auto requant = [&](const int32_t (&acc)[4]) -> uint32_t {
-        if constexpr (kMode == kModeRelu) return requant_relu4(acc, ts.m2, ts.hi2);
-        else if constexpr (kMode == kModeSigned) return requant_signed4(acc, ts.m2);
-        else if constexpr (kMode == kModeReluExact) return relu_exact4(acc, ts.c0, p.ep, ts.hi);
-        else
-            return dw_slow4(acc[0], acc[1], acc[2], acc[3], ts.c0, p.ep.bias, p.ep.M, p.ep.D, p.ep.epilogue,
-                            p.ep.q6, p.ep.inv_s_out);
-    };
     uint32_t *yr = yb - 2 * row_words;  // output row of input row t is t - 2
     auto finish = [&](int t, const int32_t (&acc)[kCPT][4]) {
         if (t >= 2) {
 #pragma unroll
             for (int j = 0; j < kCPT; j++) {
-                const uint32_t v = requant(acc[j]);
+                const uint32_t v = kRelu ? requant_relu4(acc[j], ts.m2, ts.hi2) : requant_signed4(acc[j], ts.m2);
                 if (kFull || (colmask & (1 << j))) yr[(size_t)j * cwords] = v;
             }
         }
@@ -321,10 +301,45 @@ __device__ __forceinline__ bool st_segment(const DwStreamParams &p, const StThre
     return true;
 }
 
-// CTA ranges: ctas = lanes * per_lane; CTA i works on lane i % lanes, rows
-// [k * R / per_lane, (k + 1) * R / per_lane) of it (k = i / lanes, R = n * ho),
-// so CTAs running side by side cover the same image rows of neighbouring
-// strips (shared halo columns in L2, whole image rows in flight).
+// Exact recomputation of a thread's outputs (4 channels from c0, columns ow0 ..
+// ow0 + kCPT - 1, output rows [r0, r1) of the lane) for channels outside the
+// fast range: direct 3x3 sums from the input in global memory and the
+// reference epilogue per element.  Cold code, kept out of line.
+template <int kCPT>
+static __device__ __noinline__ void st_exact_outputs(const DwStreamParams &p, const int8_t *__restrict__ w,
+                                                     int8_t *__restrict__ y, int c0, int ow0, int r0, int r1) {
+    const EpiParams &ep = p.ep;
+#pragma unroll 1
+    for (int r = r0; r < r1; r++) {
+        const int b = r / p.ho, oh = r - b * p.ho;
+#pragma unroll 1
+        for (int j = 0; j < kCPT; j++) {
+            const int ow = ow0 + j;
+            if (ow >= p.wo) break;
+#pragma unroll 1
+            for (int k = 0; k < 4; k++) {
+                const int ch = c0 + k;
+                int32_t acc = 0;
+                for (int kh = 0; kh < 3; kh++) {
+                    const int ih = oh - p.pt + kh;
+                    if (ih < 0 || ih >= p.h) continue;
+                    for (int kw = 0; kw < 3; kw++) {
+                        const int iw = ow - p.pl + kw;
+                        if (iw < 0 || iw >= p.w) continue;
+                        acc += (int32_t)p.x[(((size_t)b * p.h + ih) * p.w + iw) * p.c + ch] *
+                               (int32_t)w[(size_t)(kh * 3 + kw) * p.c + ch];
+                    }
+                }
+                const int32_t bias = ep.bias ? ep.bias[ch] : 0;
+                const float m = ep.M ? ep.M[ch] : 0.0f;
+                const float dsc = ep.D ? ep.D[ch] : 0.0f;
+                y[(((size_t)b * p.ho + oh) * p.wo + ow) * p.c + ch] =
+                    (int8_t)epilogue_one_slow(acc, bias, m, dsc, ep.epilogue, ep.q6, ep.inv_s_out);
+            }
+        }
+    }
+}
+
 template <int kShape, bool kRelu>
 __global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kShape].min_blocks)
     k_dwconv3x3_stream(const __grid_constant__ CUtensorMap tx, const int8_t *__restrict__ w, int8_t *__restrict__ y,
@@ -380,9 +395,9 @@ __global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kSh
             }
             // let the copies still in flight land before the CTA can exit
             for (int t = max(0, it - p.slots); t < it; t++) {
-                const int s = t % p.slots;
+                const int sl = t % p.slots;
                 const uint64_t t0 = globaltimer_ns();
-                while (!mbar_try_wait(smem_u32(&full[s]), (uint32_t)((t / p.slots) & 1)) &&
+                while (!mbar_try_wait(smem_u32(&full[sl]), (uint32_t)((t / p.slots) & 1)) &&
                        globaltimer_ns() - t0 < p.wait_cap_ns) {
                 }
             }
@@ -397,50 +412,31 @@ __global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kSh
     const int cwords = p.c >> 2;
     const EpiParams &ep = p.ep;
     const int gw = grp * p.words + g;  // the thread's channel word
+    const int c0 = gw * 4;
 
     StThread ts;
-    bool fast;
+    bool fast = kRelu || ep.epilogue == DW_EPI_NONE;
     {
-        const uint32_t *w32 = reinterpret_cast<const uint32_t *>(w);
-#pragma unroll
-        for (int kh = 0; kh < 3; kh++) {
-            const uint32_t k0 = __ldg(w32 + (size_t)(kh * 3 + 0) * cwords + gw);
-            const uint32_t k1 = __ldg(w32 + (size_t)(kh * 3 + 1) * cwords + gw);
-            const uint32_t k2 = __ldg(w32 + (size_t)(kh * 3 + 2) * cwords + gw);
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const uint32_t t01 = __byte_perm(k0, k1, (uint32_t)((4 + k) << 4 | k));
-                ts.wk[kh][k] = (int32_t)(__byte_perm(t01, k2, (uint32_t)((4 + k) << 8 | 0x10)) & 0x00FFFFFFu);
-            }
-        }
-        ts.c0 = gw * 4;
-        const int q6 = ep.q6;
-        fast = kRelu ? (ep.epilogue == DW_EPI_RELU || q6 >= 0) : ep.epilogue == DW_EPI_NONE;
+        load_kernel_rows(w, cwords, gw, ts.wk);
         int32_t bias[4];
         float m[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            bias[k] = ep.bias ? __ldg(ep.bias + ts.c0 + k) : 0;
-            m[k] = ep.M ? __ldg(ep.M + ts.c0 + k) : 0.0f;
+            bias[k] = ep.bias ? __ldg(ep.bias + c0 + k) : 0;
+            m[k] = ep.M ? __ldg(ep.M + c0 + k) : 0.0f;
             // |acc| <= 9 * 128 * 128; the fast paths need |acc + bias| < 2^22 and, for
             // the int16 pairs, |v| < 2^15 (kept below 30000)
             const float amax = 147456.0f + fabsf((float)bias[k]);
             fast = fast && (uint32_t)(bias[k] + (1 << 21)) < (1u << 22) && isfinite(m[k]) &&
                    (!kRelu || fabsf(m[k]) * amax < 30000.0f);
+            ts.init[k] = (int32_t)((uint32_t)bias[k] + (uint32_t)kMagicBits);
         }
         ts.m2[0] = make_float2(m[0], m[1]);
         ts.m2[1] = make_float2(m[2], m[3]);
-#pragma unroll
-        for (int k = 0; k < 4; k++) ts.init[k] = bias[k] + kMagicBits;
-        // the ReLU6 ceiling; min(max(q, 0), q6) keeps q6 itself when it is negative
-        ts.hi = ep.epilogue == DW_EPI_RELU6 ? min(q6, 127) : 127;
-        ts.hi2 = (uint32_t)(ts.hi & 0xFFFF) | ((uint32_t)ts.hi << 16);
-    }
-    // one code path per warp: the fast one when all its threads' channels allow it
-    const bool wfast = __all_sync(0xFFFFFFFFu, fast);
-    if (!wfast) {
-#pragma unroll
-        for (int k = 0; k < 4; k++) ts.init[k] = 0;  // the exact path adds the bias itself
+        // a negative ReLU6 ceiling leaves the fast range (min(max(q, 0), q6) is q6 itself)
+        if (kRelu && ep.epilogue == DW_EPI_RELU6 && ep.q6 < 0) fast = false;
+        const int hi = ep.epilogue == DW_EPI_RELU6 ? min(max(ep.q6, 0), 127) : 127;
+        ts.hi2 = (uint32_t)hi | ((uint32_t)hi << 16);
     }
 
     const int ow0 = strip * p.cw + q * kCPT;  // the thread's first output column
@@ -459,37 +455,33 @@ __global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kSh
     RingPos rp{slot0, full0, 0, 0u};
     const size_t row_words = (size_t)p.wo * cwords;
     uint32_t *y32 = reinterpret_cast<uint32_t *>(y);
+    bool ok = true;
 #pragma unroll 1
-    for (int r = r0; r < r1;) {
+    for (int r = r0; r < r1 && ok;) {
         const int b = r / p.ho, o0 = r - b * p.ho;
         const int len = min(r1 - r, p.ho - o0);
         r += len;
         // output word of (image b, row o0, column ow0, the thread's channel word)
         uint32_t *yb = y32 + ((size_t)b * p.ho * p.wo + (size_t)o0 * p.wo + ow0) * cwords + gw;
-        bool ok;
-        if (wfast && wfull)
-            ok = st_segment<kCPT, kRelu ? kModeRelu : kModeSigned, true>(p, ts, len + 2, rp, slot0, full0, empty0,
-                                                                         coff, rw4, yb, row_words, colmask,
-                                                                         abort_flag, lane);
-        else if (wfast)
-            ok = st_segment<kCPT, kRelu ? kModeRelu : kModeSigned, false>(p, ts, len + 2, rp, slot0, full0, empty0,
-                                                                          coff, rw4, yb, row_words, colmask,
-                                                                          abort_flag, lane);
+        if (wfull)
+            ok = st_segment<kCPT, kRelu, true>(p, ts, len + 2, rp, slot0, full0, empty0, coff, rw4, yb, row_words,
+                                               colmask, abort_flag, lane);
         else
-            ok = st_segment<kCPT, kRelu ? kModeReluExact : kModeExact, false>(p, ts, len + 2, rp, slot0, full0, empty0,
-                                                                              coff, rw4, yb, row_words, colmask,
-                                                                              abort_flag, lane);
-        if (!ok) break;
+            ok = st_segment<kCPT, kRelu, false>(p, ts, len + 2, rp, slot0, full0, empty0, coff, rw4, yb, row_words,
+                                                colmask, abort_flag, lane);
     }
+    // channels outside the fast range: exact outputs over the fast ones (same
+    // thread, same addresses, later in program order)
+    if (ok && !fast) st_exact_outputs<kCPT>(p, w, y, c0, ow0, r0, r1);
 }
 
 struct StreamPlan {
-    int cpt = 0, cg = 0, groups = 0, cw = 0, q_per = 0, strips = 0;
+    int cg = 0, groups = 0, cw = 0, q_per = 0, strips = 0;
 };
 
 // Picks the channel group (fewest groups), then the strip width: consumer
-// threads words * q_per a multiple of 32 and at most kStreamMaxCons, the
-// least padding past the last output column, then the widest strip.
+// threads words * q_per a multiple of 32 and at most max_cons, the least
+// padding past the last output column, then the widest strip.
 StreamPlan plan_stream(int c, int wo, int cpt, int max_cons) {
     StreamPlan best;
     for (int groups = 1; groups <= c / 16; groups++) {
@@ -505,7 +497,7 @@ StreamPlan plan_stream(int c, int wo, int cpt, int max_cons) {
             const long long waste = (long long)strips * cw - wo;
             if (best_waste < 0 || waste < best_waste || (waste == best_waste && cw > best.cw)) {
                 best_waste = waste;
-                best = StreamPlan{cpt, cg, groups, cw, qp, strips};
+                best = StreamPlan{cg, groups, cw, qp, strips};
             }
             if (cw >= wo_r) break;  // wider strips only add idle columns
         }
@@ -522,7 +514,8 @@ int stream_occupancy(int device, int threads, size_t smem) {
     static int cached[16][20][64] = {};
     if (device < 0 || device >= 16) return 1;
     if (!attr_set[device]) {
-        cudaFuncSetAttribute(k_dwconv3x3_stream<kShape, kRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_dwconv3x3_stream<kShape, kRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024);
         attr_set[device] = true;
     }
     int &c = cached[device][std::min(19, threads / 32)][std::min<size_t>(63, smem / 4096)];
@@ -553,281 +546,18 @@ dw_status launch_stream(dw_backend *be, const CUtensorMap &tx, const int8_t *w, 
     return dw_after_launch(be, "dwconv3x3_stream_i8");
 }
 
-// ---------------------------------------------------------------------------
-// Warp-specialised variant: the consumer work of one 4-channel x 4-column tile
-// is split between a math warp (shared-memory loads, byte transposes, __dp4a
-// rotation) and an epilogue warp (requantisation and stores) that own the same
-// tiles.  A finished output row's 16 int32 accumulators per thread go through a
-// ring of kAccSlots shared-memory slots laid out [column j][thread][4 channels]
-// (consecutive threads touch consecutive 16-byte words: no bank conflicts).
-// Twice the warps of the single-role kernel hide the dependency latencies, and
-// each role fits the register budget of 19 warps on one SM.
-constexpr int kAccSlots = 3;
-constexpr int kWsMaxCons = 288;  // math threads (= epilogue threads) per CTA
-
-struct WsThread {
-    int g, q;           // channel word in the group, column group in the strip
-    bool fast;          // this thread's channels take the fast requantisation
-};
-
-template <bool kRelu>
-__global__ void __launch_bounds__(2 * kWsMaxCons + 32, 1)
-    k_dwconv3x3_ws(const __grid_constant__ CUtensorMap tx, const int8_t *__restrict__ w, int8_t *__restrict__ y,
-                   const __grid_constant__ DwStreamParams p) {
-    constexpr int kCPT = 4;
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int T = p.cons_threads;  // threads per role
-    const uint32_t acc_slot_bytes = (uint32_t)T * 64u;
-    uint8_t *acc_ring = smem + (size_t)p.slots * p.slot_bytes;
-    uint64_t *full = reinterpret_cast<uint64_t *>(acc_ring + (size_t)kAccSlots * acc_slot_bytes);
-    uint64_t *empty = full + kStreamMaxSlots;
-    uint64_t *afull = empty + kStreamMaxSlots;
-    uint64_t *aempty = afull + kAccSlots;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(aempty + kAccSlots);
-    const int W = T >> 5;  // warps per role
-    const int lanes = p.groups * p.strips;
-    const int my_lane = blockIdx.x % lanes, part = blockIdx.x / lanes;
-    const int R = p.n * p.ho;
-    const int r0 = (int)((long long)part * R / p.per_lane), r1 = (int)((long long)(part + 1) * R / p.per_lane);
-    const int grp = my_lane % p.groups, strip = my_lane / p.groups;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < p.slots; s++) {
-            mbar_init(smem_u32(&full[s]), 1);
-            mbar_init(smem_u32(&empty[s]), W);
-        }
-        for (int a = 0; a < kAccSlots; a++) {
-            mbar_init(smem_u32(&afull[a]), W);
-            mbar_init(smem_u32(&aempty[a]), W);
-        }
-        *abort_flag = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    }
-    __syncthreads();
-
-    if (threadIdx.x >= 2 * T) {
-        // ------------------------------------------------------------ producer
-        if (threadIdx.x == 2 * T) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&tx) : "memory");
-            int it = 0;
-            bool ok = true;
-            for (int r = r0; r < r1 && ok;) {
-                const int b = r / p.ho, o0 = r - b * p.ho;
-                const int len = min(r1 - r, p.ho - o0);
-                const int stages = (len + 2 + 2) / 3;
-                for (int k = 0; k < stages; k++, it++) {
-                    const int s = it % p.slots;
-                    if (it >= p.slots &&
-                        !st_wait(smem_u32(&empty[s]), (uint32_t)((it / p.slots - 1) & 1), p, abort_flag, 40)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_expect_tx(smem_u32(&full[s]), p.stage_bytes);
-                    tma_load_4d(smem_u32(smem + (size_t)s * p.slot_bytes), &tx, smem_u32(&full[s]),
-                                grp * (p.cg >> 3), strip * p.cw - p.pl, o0 - p.pt + 3 * k, b);
-                }
-                r += len;
-            }
-            for (int t = max(0, it - p.slots); t < it; t++) {
-                const int s = t % p.slots;
-                const uint64_t t0 = globaltimer_ns();
-                while (!mbar_try_wait(smem_u32(&full[s]), (uint32_t)((t / p.slots) & 1)) &&
-                       globaltimer_ns() - t0 < p.wait_cap_ns) {
-                }
-            }
-        }
-        return;
-    }
-
-    const bool is_math = threadIdx.x < T;
-    const int ti = is_math ? threadIdx.x : threadIdx.x - T;  // index within the role
-    const int g = ti % p.words, q = ti / p.words;
-    const int lane = threadIdx.x & 31;
-    const int cwords = p.c >> 2;
-    const EpiParams &ep = p.ep;
-    const int gw = grp * p.words + g;
-    const int c0 = gw * 4;
-
-    // the fast-path test (both roles compute it; paired warps vote alike)
-    bool fast = kRelu ? (ep.epilogue == DW_EPI_RELU || ep.q6 >= 0) : ep.epilogue == DW_EPI_NONE;
-    int32_t bias[4];
-    float m[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        bias[k] = ep.bias ? __ldg(ep.bias + c0 + k) : 0;
-        m[k] = ep.M ? __ldg(ep.M + c0 + k) : 0.0f;
-        const float amax = 147456.0f + fabsf((float)bias[k]);
-        fast = fast && (uint32_t)(bias[k] + (1 << 21)) < (1u << 22) && isfinite(m[k]) &&
-               (!kRelu || fabsf(m[k]) * amax < 30000.0f);
-    }
-    const bool wfast = __all_sync(0xFFFFFFFFu, fast);
-
-    if (is_math) {
-        // -------------------------------------------------------------- math
-        int32_t wk[3][4], init[4];
-        {
-            const uint32_t *w32 = reinterpret_cast<const uint32_t *>(w);
-#pragma unroll
-            for (int kh = 0; kh < 3; kh++) {
-                const uint32_t k0 = __ldg(w32 + (size_t)(kh * 3 + 0) * cwords + gw);
-                const uint32_t k1 = __ldg(w32 + (size_t)(kh * 3 + 1) * cwords + gw);
-                const uint32_t k2 = __ldg(w32 + (size_t)(kh * 3 + 2) * cwords + gw);
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const uint32_t t01 = __byte_perm(k0, k1, (uint32_t)((4 + k) << 4 | k));
-                    wk[kh][k] = (int32_t)(__byte_perm(t01, k2, (uint32_t)((4 + k) << 8 | 0x10)) & 0x00FFFFFFu);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < 4; k++) init[k] = wfast ? bias[k] + kMagicBits : 0;
-        }
-        const uint32_t src_off = (uint32_t)(q * kCPT * p.words + g);
-        const int rw = p.bw * p.words;
-        int4 *accw = reinterpret_cast<int4 *>(acc_ring) + ti;  // slot 0, column 0
-        int it = 0, ar = 0;
-        // hands the finished output row in `acc` to the epilogue warps
-        auto hand_off = [&](const int32_t (&acc)[kCPT][4]) -> bool {
-            const int a = ar % kAccSlots;
-            if (ar >= kAccSlots &&
-                !st_wait(smem_u32(&aempty[a]), (uint32_t)((ar / kAccSlots - 1) & 1), p, abort_flag, 41))
-                return false;
-            int4 *dst = accw + (size_t)a * (acc_slot_bytes / 16);
-#pragma unroll
-            for (int j = 0; j < kCPT; j++) dst[j * T] = make_int4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&afull[a]));
-            ar++;
-            return true;
-        };
-        int32_t A[kCPT][4], B[kCPT][4], C[kCPT][4];
-#pragma unroll 1
-        for (int r = r0; r < r1;) {
-            const int b = r / p.ho, o0 = r - b * p.ho;
-            const int len = min(r1 - r, p.ho - o0);
-            r += len;
-            const int count = len + 2;
-            const int stages = (count + 2) / 3;
-            bool ok = true;
-#pragma unroll 1
-            for (int k = 0; k < stages && ok; k++, it++) {
-                const int s = it % p.slots;
-                if (!st_wait(smem_u32(&full[s]), (uint32_t)((it / p.slots) & 1), p, abort_flag, 42)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t *src = reinterpret_cast<const uint32_t *>(smem + (size_t)s * p.slot_bytes) + src_off;
-                const int t0 = 3 * k;
-                uint32_t X[kCPT + 2];
-#pragma unroll
-                for (int c = 0; c < kCPT + 2; c++) X[c] = src[c * p.words];
-                st_row<kCPT>(X, wk, init, A, B, C);
-                if (t0 >= 2) ok = hand_off(C);
-                if (ok && t0 + 1 < count) {
-#pragma unroll
-                    for (int c = 0; c < kCPT + 2; c++) X[c] = src[rw + c * p.words];
-                    st_row<kCPT>(X, wk, init, C, A, B);
-                    if (t0 + 1 >= 2) ok = hand_off(B);
-                }
-                if (ok && t0 + 2 < count) {
-#pragma unroll
-                    for (int c = 0; c < kCPT + 2; c++) X[c] = src[2 * rw + c * p.words];
-                    st_row<kCPT>(X, wk, init, B, C, A);
-                    ok = hand_off(A);
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
-            }
-            if (!ok) break;
-        }
-        return;
-    }
-
-    // ------------------------------------------------------------------ epilogue
-    float2 m2[2] = {make_float2(m[0], m[1]), make_float2(m[2], m[3])};
-    const int hi = ep.epilogue == DW_EPI_RELU6 ? min(ep.q6, 127) : 127;
-    const uint32_t hi2 = (uint32_t)(hi & 0xFFFF) | ((uint32_t)hi << 16);
-    const int ow0 = strip * p.cw + q * kCPT;
-    int colmask = 0;
-#pragma unroll
-    for (int j = 0; j < kCPT; j++) colmask |= (ow0 + j < p.wo) ? (1 << j) : 0;
-    const size_t row_words = (size_t)p.wo * cwords;
-    uint32_t *y32 = reinterpret_cast<uint32_t *>(y);
-    const int4 *accr = reinterpret_cast<const int4 *>(acc_ring) + ti;
-    int ar = 0;
-#pragma unroll 1
-    for (int r = r0; r < r1;) {
-        const int b = r / p.ho, o0 = r - b * p.ho;
-        const int len = min(r1 - r, p.ho - o0);
-        r += len;
-        uint32_t *yr = y32 + ((size_t)b * p.ho * p.wo + (size_t)o0 * p.wo + ow0) * cwords + gw;
-        bool ok = true;
-#pragma unroll 1
-        for (int t = 0; t < len; t++, ar++, yr += row_words) {
-            const int a = ar % kAccSlots;
-            if (!st_wait(smem_u32(&afull[a]), (uint32_t)((ar / kAccSlots) & 1), p, abort_flag, 43)) {
-                ok = false;
-                break;
-            }
-            const int4 *srcv = accr + (size_t)a * (acc_slot_bytes / 16);
-            uint32_t out[kCPT];
-            if (wfast) {
-#pragma unroll
-                for (int j = 0; j < kCPT; j++) {
-                    const int4 v = srcv[j * T];
-                    const int32_t acc[4] = {v.x, v.y, v.z, v.w};
-                    out[j] = kRelu ? requant_relu4(acc, m2, hi2) : requant_signed4(acc, m2);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < kCPT; j++) {
-                    const int4 v = srcv[j * T];
-                    out[j] = dw_slow4(v.x, v.y, v.z, v.w, c0, ep.bias, ep.M, ep.D, ep.epilogue, ep.q6, ep.inv_s_out);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&aempty[a]));
-#pragma unroll
-            for (int j = 0; j < kCPT; j++)
-                if (colmask & (1 << j)) yr[(size_t)j * cwords] = out[j];
-        }
-        if (!ok) break;
-    }
-}
-
-template <bool kRelu>
-dw_status launch_ws(dw_backend *be, const CUtensorMap &tx, const int8_t *w, int8_t *y, DwStreamParams &p,
-                    size_t smem) {
-    static bool attr_set[16] = {};
-    if (be->device >= 0 && be->device < 16 && !attr_set[be->device]) {
-        cudaFuncSetAttribute(k_dwconv3x3_ws<kRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        attr_set[be->device] = true;
-    }
-    const int threads = 2 * p.cons_threads + 32;
-    const int lanes = p.groups * p.strips;
-    const int rows = p.n * p.ho;
-    p.per_lane = std::max(1, std::min(be->sm_count / lanes, rows / 24));
-    const long long ctas = (long long)lanes * p.per_lane;
-    if (ctas >= (1ll << 31)) return DW_ERR_UNSUPPORTED;
-    k_dwconv3x3_ws<kRelu><<<(unsigned)ctas, threads, smem, be->stream>>>(tx, w, y, p);
-    return dw_after_launch(be, "dwconv3x3_ws_i8");
-}
-
 }  // namespace
 
 // Returns DW_ERR_UNSUPPORTED (without launching) when the shape does not fit
-// the kernel: stride 1, 3x3, multiplier 1, c % 16 == 0 with a lane plan.
-// `shape` indexes kStShapes (0: 2 columns x 576 consumers, 1: 2 x 288 with
-// two CTAs per SM, 2: 4 x 288); 3 is the warp-specialised kernel (4 x 288 math
-// threads and as many epilogue threads).
+// the kernel: stride 1, 3x3, multiplier 1, c % 16 == 0 with a lane plan, no
+// SiLU.  `shape` indexes kStShapes.
 dw_status launch_dwconv3x3_stream_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
                                      const int8_t *w_hwcm, const EpiParams &ep, int8_t *y, int shape) {
     if (!be->encode_tiled || d.k_h != 3 || d.k_w != 3 || d.stride_h != 1 || d.stride_w != 1 ||
         d.c_out != d.c_in || d.c_in % 16 || ((uintptr_t)x & 15) || ((uintptr_t)y & 3) || ((uintptr_t)w_hwcm & 3) ||
-        shape < 0 || shape > 3)
+        shape < 0 || shape > 2 || ep.epilogue == DW_EPI_SILU)
         return DW_ERR_UNSUPPORTED;
-    const bool ws = shape == 3;
-    const StShape sh = ws ? StShape{4, kWsMaxCons, 1} : kStShapes[shape];
+    const StShape &sh = kStShapes[shape];
     const StreamPlan pl = plan_stream(d.c_in, wo, sh.cpt, sh.max_cons);
     if (!pl.cw) return DW_ERR_UNSUPPORTED;
     DwStreamParams p{};
@@ -836,21 +566,18 @@ dw_status launch_dwconv3x3_stream_i8(dw_backend *be, const dw_conv_desc &d, int 
     p.words = pl.cg / 4;
     p.groups = pl.groups;
     p.cw = pl.cw;
-    p.q_per = pl.q_per;
     p.strips = pl.strips;
     p.bw = pl.cw + 2;
-    p.row_bytes = (uint32_t)(p.bw * p.cg);
-    p.stage_bytes = 3 * p.row_bytes;
+    p.stage_bytes = 3u * (uint32_t)(p.bw * p.cg);
     p.slot_bytes = (p.stage_bytes + 127) & ~127u;
-    p.cons_threads = p.words * p.q_per;
-    // ring: 3..8 stages in about 200 KB per SM (the warp-specialised kernel
-    // also holds kAccSlots accumulator rows of 64 bytes per thread)
-    const uint32_t acc_bytes = ws ? (uint32_t)kAccSlots * 64u * (uint32_t)(pl.cg / 4 * pl.q_per) : 0u;
-    const uint32_t budget = ws ? 220u * 1024u - acc_bytes : (200u * 1024u) / (uint32_t)sh.min_blocks;
+    p.cons_threads = p.words * pl.q_per;
+    // ring: 3..8 stages in about 200 KB per SM
+    const uint32_t budget = (200u * 1024u) / (uint32_t)sh.min_blocks;
     p.slots = (int)std::min<uint32_t>(kStreamMaxSlots, budget / p.slot_bytes);
     if (p.slots < 3) return DW_ERR_UNSUPPORTED;
     if ((long long)d.n * ho >= (1ll << 31)) return DW_ERR_UNSUPPORTED;
     if (d.n == 0 || ho <= 0 || wo <= 0) return DW_OK;
+    p.x = x;
     p.wait_cap_ns = be->wait_cap_ns;
     p.err = be->dev_err;
     p.ep = ep;
@@ -866,13 +593,8 @@ dw_status launch_dwconv3x3_stream_i8(dw_backend *be, const dw_conv_desc &d, int 
                                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return DW_ERR_UNSUPPORTED;
-    const bool relu = ep.epilogue == DW_EPI_RELU || ep.epilogue == DW_EPI_RELU6;
-    if (ws) {
-        const size_t smem_ws = (size_t)p.slots * p.slot_bytes + acc_bytes +
-                               (2 * kStreamMaxSlots + 2 * kAccSlots) * sizeof(uint64_t) + 16;
-        return relu ? launch_ws<true>(be, tx, w_hwcm, y, p, smem_ws) : launch_ws<false>(be, tx, w_hwcm, y, p, smem_ws);
-    }
     const size_t smem = (size_t)p.slots * p.slot_bytes + 2 * kStreamMaxSlots * sizeof(uint64_t) + 16;
+    const bool relu = ep.epilogue == DW_EPI_RELU || ep.epilogue == DW_EPI_RELU6;
     switch (shape) {
     case 0: return relu ? launch_stream<0, true>(be, tx, w_hwcm, y, p, smem) : launch_stream<0, false>(be, tx, w_hwcm, y, p, smem);
     case 1: return relu ? launch_stream<1, true>(be, tx, w_hwcm, y, p, smem) : launch_stream<1, false>(be, tx, w_hwcm, y, p, smem);

@@ -59,8 +59,7 @@ enum dw_dw_variant {
     DW_DWV_SLAB = 1,     /* 64-channel slabs, one row per copy */
     DW_DWV_STREAM2 = 2,   /* persistent whole-pixel streaming, 4 channels x 2 columns per thread, 18 warps (the default) */
     DW_DWV_STREAM2X2 = 3, /* the same, two CTAs of 9 consumer warps per SM */
-    DW_DWV_STREAM4 = 4,   /* 4 channels x 4 columns per thread, 9 consumer warps */
-    DW_DWV_WS = 5         /* warp-specialised: 9 dp4a warps + 9 requantisation warps */
+    DW_DWV_STREAM4 = 4    /* 4 channels x 4 columns per thread, 9 consumer warps */
 };
 
 enum dw_conv_path {

@@ -27,8 +27,8 @@ def be_direct():
     b.close()
 
 
-@pytest.fixture(scope="module", params=[dw.DWV_SLAB, dw.DWV_STREAM2, dw.DWV_STREAM2X2, dw.DWV_STREAM4, dw.DWV_WS],
-                ids=["slab", "stream2", "stream2x2", "stream4", "ws"])
+@pytest.fixture(scope="module", params=[dw.DWV_SLAB, dw.DWV_STREAM2, dw.DWV_STREAM2X2, dw.DWV_STREAM4],
+                ids=["slab", "stream2", "stream2x2", "stream4"])
 def be_dwv(request):
     """A backend forced onto one int8 depthwise 3x3 s1 kernel variant."""
     b = dw.CudaBackend(0, dw_variant=request.param)
