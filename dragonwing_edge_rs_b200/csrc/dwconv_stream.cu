@@ -27,16 +27,16 @@
 //
 // Requantisation (the contract of include/dw_cuda.h), exact on every path:
 //  * ReLU / ReLU6: v = fl(fl(acc + bias) * M) as the reference, then
-//    floor(v + 0.5) by two packed adds rounded toward zero (the second places
-//    the integer in the low mantissa bits of 1.5 * 2^23).  For v >= 0 that is
-//    roundf(v); below zero both are <= 0, which the ReLU bound maps to 0.  The
-//    bounds go on the packed int16 pair with one max(min(x, hi), 0); clamping
-//    the integer after rounding equals rounding after clamping because the
-//    bounds are integers.
+//    floor(2v + 1) from one packed add rounded toward zero (it lands in the low
+//    mantissa bits of 1.5 * 2^22, where the spacing is 0.5), clamped to
+//    [0, 2 hi + 1] on the packed int16 pair and halved: clamp(floor(v + 0.5),
+//    0, hi).  For v >= 0, floor(v + 0.5) is roundf(v); below zero both are
+//    <= 0, which the ReLU bound maps to 0.  Clamping the integer after
+//    rounding equals rounding after clamping because the bounds are integers.
 //  * no activation: clamp to [-128, 127] in f32, rint by the magic add, ties
 //    moved away from zero.
 //  The fast paths need |acc + bias| < 2^22, a finite M and, for the int16
-//  pairs, |v| < 2^15.  A thread whose channels miss that (pathological scales
+//  pairs, |2v + 1| < 2^15.  A thread whose channels miss that (pathological scales
 //  or biases) recomputes its outputs after the stream, element by element with
 //  the reference epilogue, over its own earlier stores; the hot loop carries
 //  no exact path.  SiLU is not taken here (the slab kernel handles it).
@@ -164,23 +164,27 @@ __device__ __forceinline__ void st_row(const uint32_t (&X)[kCPT + 2], const int3
 // ReLU-family fast requantisation of 4 channels (header comment); returns the
 // 4 result bytes.  The accumulators start at bias + the bit pattern of
 // 1.5 * 2^23, so reading them as floats and subtracting 1.5 * 2^23 gives
-// acc + bias exactly.  u = v + 0.5 rounded toward zero keeps floor(u) ==
-// floor(v + 0.5) (integers are representable, so rounding toward zero never
-// crosses one), and u + 1.5 * 2^23 rounded toward zero is 1.5 * 2^23 +
-// floor(u) (|u| < 2^22), whose low 16 bits are floor(v + 0.5) as int16.  The
-// packed directed-rounding adds issue on the FMA pipe at the full f32x2 rate.
+// acc + bias exactly; v = fl(that * M) as the reference.  One add rounded
+// toward zero of 1.5 * 2^22 + 0.5 (exact: the spacing in [2^22, 2^23) is 0.5)
+// gives 1.5 * 2^22 + floor_half(v + 0.5), floor_half rounding down to a multiple
+// of 0.5; its low 16 bits are floor(2v + 1) as int16 (|v| < 2^14 on the fast
+// path).  Clamped to [0, 2 hi + 1] and halved, that is clamp(floor(v + 0.5), 0,
+// hi): floor(v + 0.5) == roundf(v) for v >= 0, both are <= 0 below zero, and
+// halving commutes with the clamp because 2 hi + 1 halves to hi.  The halving
+// runs on the packed bytes (every lane is at most 255 there).  The packed
+// directed-rounding add issues on the FMA pipe at the full f32x2 rate.
 __device__ __forceinline__ uint32_t requant_relu4(const int32_t (&a)[4], const float2 (&m)[2], uint32_t hi2) {
-    const float2 half = make_float2(0.5f, 0.5f), mag = make_float2(kMagic, kMagic);
+    const float2 nmag = make_float2(-kMagic, -kMagic);
+    const float2 mag = make_float2(6291456.5f, 6291456.5f);  // 1.5 * 2^22 + 0.5
     uint32_t c[2];
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        const float2 f = make_float2(__fsub_rn(__int_as_float(a[2 * h]), kMagic),
-                                     __fsub_rn(__int_as_float(a[2 * h + 1]), kMagic));
+        const float2 f = __fadd2_rn(make_float2(__int_as_float(a[2 * h]), __int_as_float(a[2 * h + 1])), nmag);
         const float2 v = __fmul2_rn(f, m[h]);
-        const float2 r = __fadd2_rz(__fadd2_rz(v, half), mag);
+        const float2 r = __fadd2_rz(v, mag);
         c[h] = __vimin_s16x2_relu(__byte_perm(__float_as_uint(r.x), __float_as_uint(r.y), 0x5410), hi2);
     }
-    return __byte_perm(c[0], c[1], 0x6420);
+    return (__byte_perm(c[0], c[1], 0x6420) >> 1) & 0x7F7F7F7Fu;
 }
 
 // Signed (no activation) fast requantisation of 4 channels: clamp to
@@ -230,7 +234,7 @@ struct StThread {
     int32_t wk[3][4];  // kernel rows: (w0, w1, w2, 0) bytes per channel
     int32_t init[4];   // accumulator start: bias + the magic bits
     float2 m2[2];      // M of channels 0,1 and 2,3
-    uint32_t hi2;      // ReLU ceiling in both int16 lanes
+    uint32_t hi2;      // 2 * (ReLU ceiling) + 1 in both int16 lanes
 };
 
 // Position in the ring of input stages, advanced without divisions.
@@ -241,53 +245,38 @@ struct RingPos {
     uint32_t ph;         // barrier phase parity of the current pass over the ring
 };
 
-// One segment: `count` input rows from the ring position `rp` on; output rows
-// are stored from the third input row on.  kFull: every column of the thread
-// is inside the image (no per-store test).  Returns false when a wait gave up.
+// One segment: `count` (>= 3) input rows from the ring position `rp` on;
+// output rows are stored from the third input row on.  The first stage (one
+// output row) and a last partial stage are peeled off, so whole stages run
+// without per-row tests.  kFull: every column of the thread is inside the
+// image (no per-store test).  Returns false when a wait gave up.
 template <int kCPT, bool kRelu, bool kFull>
 __device__ __forceinline__ bool st_segment(const DwStreamParams &p, const StThread &ts, int count, RingPos &rp,
                                            uint32_t slot0_addr, uint32_t full0, uint32_t empty0,
                                            const uint32_t (&coff)[kCPT + 2], uint32_t rw4, uint32_t *yb,
                                            size_t row_words, int colmask, volatile int *abort_flag, int lane) {
     const int cwords = p.c >> 2;
-    uint32_t *yr = yb - 2 * row_words;  // output row of input row t is t - 2
-    auto finish = [&](int t, const int32_t (&acc)[kCPT][4]) {
-        if (t >= 2) {
+    uint32_t *yr = yb;  // the next output row to store
+    int32_t A[kCPT][4], B[kCPT][4], C[kCPT][4];
+    // one input row at shared address `addr` into the rotation (a0 starts there)
+    auto row = [&](uint32_t addr, int32_t (&a0)[kCPT][4], int32_t (&a1)[kCPT][4], int32_t (&a2)[kCPT][4]) {
+        uint32_t X[kCPT + 2];
 #pragma unroll
-            for (int j = 0; j < kCPT; j++) {
-                const uint32_t v = kRelu ? requant_relu4(acc[j], ts.m2, ts.hi2) : requant_signed4(acc[j], ts.m2);
-                if (kFull || (colmask & (1 << j))) yr[(size_t)j * cwords] = v;
-            }
+        for (int c = 0; c < kCPT + 2; c++) X[c] = lds_u32(addr + coff[c]);
+        st_row<kCPT>(X, ts.wk, ts.init, a0, a1, a2);
+    };
+    auto store = [&](const int32_t (&acc)[kCPT][4]) {
+#pragma unroll
+        for (int j = 0; j < kCPT; j++) {
+            const uint32_t v = kRelu ? requant_relu4(acc[j], ts.m2, ts.hi2) : requant_signed4(acc[j], ts.m2);
+            if (kFull || (colmask & (1 << j))) yr[(size_t)j * cwords] = v;
         }
         yr += row_words;
     };
-    auto load_row = [&](uint32_t row_addr, uint32_t (&X)[kCPT + 2]) {
-#pragma unroll
-        for (int c = 0; c < kCPT + 2; c++) X[c] = lds_u32(row_addr + coff[c]);
-    };
-    int32_t A[kCPT][4], B[kCPT][4], C[kCPT][4];
-    const int stages = (count + 2) / 3;
-#pragma unroll 1
-    for (int k = 0; k < stages; k++) {
-        if (!st_wait(rp.bar, rp.ph, p, abort_flag, 31)) return false;
-        const int t0 = 3 * k;
-        uint32_t X[kCPT + 2];
-        load_row(rp.slot_addr, X);
-        st_row<kCPT>(X, ts.wk, ts.init, A, B, C);
-        finish(t0, C);
-        if (t0 + 1 < count) {
-            load_row(rp.slot_addr + rw4, X);
-            st_row<kCPT>(X, ts.wk, ts.init, C, A, B);
-            finish(t0 + 1, B);
-        }
-        if (t0 + 2 < count) {
-            load_row(rp.slot_addr + 2 * rw4, X);
-            st_row<kCPT>(X, ts.wk, ts.init, B, C, A);
-            finish(t0 + 2, A);
-        }
+    // releases the stage's slot and moves to the next one
+    auto next_slot = [&]() {
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8u * (uint32_t)rp.s);
-        // next slot
         rp.s++;
         rp.slot_addr += p.slot_bytes;
         rp.bar += 8u;
@@ -297,6 +286,36 @@ __device__ __forceinline__ bool st_segment(const DwStreamParams &p, const StThre
             rp.bar = full0;
             rp.ph ^= 1u;
         }
+    };
+    // first stage: rows 0 and 1 start output rows, row 2 completes output row 0
+    if (!st_wait(rp.bar, rp.ph, p, abort_flag, 31)) return false;
+    row(rp.slot_addr, A, B, C);
+    row(rp.slot_addr + rw4, C, A, B);
+    row(rp.slot_addr + 2 * rw4, B, C, A);
+    store(A);
+    next_slot();
+    const int whole = count / 3;  // stages of three rows
+#pragma unroll 1
+    for (int k = 1; k < whole; k++) {
+        if (!st_wait(rp.bar, rp.ph, p, abort_flag, 31)) return false;
+        row(rp.slot_addr, A, B, C);
+        store(C);
+        row(rp.slot_addr + rw4, C, A, B);
+        store(B);
+        row(rp.slot_addr + 2 * rw4, B, C, A);
+        store(A);
+        next_slot();
+    }
+    const int tail = count - 3 * whole;  // rows of a last partial stage
+    if (tail) {
+        if (!st_wait(rp.bar, rp.ph, p, abort_flag, 31)) return false;
+        row(rp.slot_addr, A, B, C);
+        store(C);
+        if (tail == 2) {
+            row(rp.slot_addr + rw4, C, A, B);
+            store(B);
+        }
+        next_slot();
     }
     return true;
 }
@@ -425,10 +444,10 @@ __global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kSh
             bias[k] = ep.bias ? __ldg(ep.bias + c0 + k) : 0;
             m[k] = ep.M ? __ldg(ep.M + c0 + k) : 0.0f;
             // |acc| <= 9 * 128 * 128; the fast paths need |acc + bias| < 2^22 and, for
-            // the int16 pairs, |v| < 2^15 (kept below 30000)
+            // the int16 pairs, |2v + 1| < 2^15 (|v| kept below 15000)
             const float amax = 147456.0f + fabsf((float)bias[k]);
             fast = fast && (uint32_t)(bias[k] + (1 << 21)) < (1u << 22) && isfinite(m[k]) &&
-                   (!kRelu || fabsf(m[k]) * amax < 30000.0f);
+                   (!kRelu || fabsf(m[k]) * amax < 15000.0f);
             ts.init[k] = (int32_t)((uint32_t)bias[k] + (uint32_t)kMagicBits);
         }
         ts.m2[0] = make_float2(m[0], m[1]);
@@ -436,7 +455,7 @@ __global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kSh
         // a negative ReLU6 ceiling leaves the fast range (min(max(q, 0), q6) is q6 itself)
         if (kRelu && ep.epilogue == DW_EPI_RELU6 && ep.q6 < 0) fast = false;
         const int hi = ep.epilogue == DW_EPI_RELU6 ? min(max(ep.q6, 0), 127) : 127;
-        ts.hi2 = (uint32_t)hi | ((uint32_t)hi << 16);
+        ts.hi2 = (uint32_t)(2 * hi + 1) | ((uint32_t)(2 * hi + 1) << 16);
     }
 
     const int ow0 = strip * p.cw + q * kCPT;  // the thread's first output column
