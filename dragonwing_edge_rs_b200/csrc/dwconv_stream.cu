@@ -2,14 +2,17 @@
 // streaming over whole pixels.
 //
 // Work layout.  A lane is a column strip of `cw` output columns over a channel
-// group of `cg` channels (all the channels when they fit).  The grid is
-// lanes x per_lane CTAs: CTA i streams lane i % lanes, output rows
-// [k R / per_lane, (k + 1) R / per_lane) of it (k = i / lanes, R = n * ho,
-// rows counted image after image), so CTAs that run side by side cover the
-// same image rows of neighbouring strips (their halo columns meet in L2 and
-// whole image rows are in flight together).  A run of rows inside one image is
-// a segment; crossing into the next image restarts the row rotation with two
-// halo rows.
+// group of `cg` channels (all the channels when they fit); its rows are the
+// R = n * ho output rows, image after image.  The first lanes x per_lane CTAs
+// are the main ones: CTA i streams lane i % lanes, rows [k Rm / per_lane,
+// (k + 1) Rm / per_lane) of it (k = i / lanes), so CTAs that run side by side
+// cover the same image rows of neighbouring strips (their halo columns meet
+// in L2 and whole image rows are in flight together).  When the SMs do not
+// divide into lanes evenly, `extra` more CTAs take the lanes' last R - Rm rows
+// (the tails, lane after lane, split evenly), so every SM streams about the
+// same number of rows.  A CTA's work is a list of pieces (lane, row range);
+// a run of rows inside one image is a segment, and crossing into the next
+// image or piece restarts the row rotation with two halo rows.
 //
 // Data movement.  A producer lane loads stages of three input rows through the
 // tensor map -- each row the strip's cw + 2 columns of whole cg-channel pixels,
@@ -79,7 +82,9 @@ struct DwStreamParams {
     uint32_t slot_bytes;   // stage_bytes rounded up to 128
     int slots;
     int cons_threads;      // words * cw / kCPT
-    int per_lane;          // CTAs per lane
+    int per_lane;          // main CTAs per lane
+    int rows_main;         // rows of each lane the main CTAs take (Rm); the rest go to the extra CTAs
+    int extra;             // extra CTAs for the lanes' tails
     const int8_t *x;       // the input (the exact recomputation reads it directly)
     uint64_t wait_cap_ns;
     int32_t *err;
@@ -359,72 +364,14 @@ static __device__ __noinline__ void st_exact_outputs(const DwStreamParams &p, co
     }
 }
 
-template <int kShape, bool kRelu>
-__global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kShape].min_blocks)
-    k_dwconv3x3_stream(const __grid_constant__ CUtensorMap tx, const int8_t *__restrict__ w, int8_t *__restrict__ y,
-                       const __grid_constant__ DwStreamParams p) {
-    constexpr int kCPT = kStShapes[kShape].cpt;
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)p.slots * p.slot_bytes);
-    uint64_t *empty = full + kStreamMaxSlots;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStreamMaxSlots);
-    const int cons_warps = p.cons_threads >> 5;
-    const int lanes = p.groups * p.strips;
-    const int my_lane = blockIdx.x % lanes, part = blockIdx.x / lanes;
-    const int R = p.n * p.ho;
-    const int r0 = (int)((long long)part * R / p.per_lane), r1 = (int)((long long)(part + 1) * R / p.per_lane);
+// One piece of a CTA's work for a consumer thread: rows [r0, r1) of lane
+// `my_lane`, from ring position rp on.  Returns false when a wait gave up.
+template <int kCPT, bool kRelu>
+__device__ __forceinline__ bool st_piece(const DwStreamParams &p, const int8_t *__restrict__ w,
+                                         int8_t *__restrict__ y, int my_lane, int r0, int r1, RingPos &rp,
+                                         uint32_t slot0, uint32_t full0, uint32_t empty0,
+                                         volatile int *abort_flag) {
     const int grp = my_lane % p.groups, strip = my_lane / p.groups;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < p.slots; s++) {
-            mbar_init(smem_u32(&full[s]), 1);
-            mbar_init(smem_u32(&empty[s]), cons_warps);
-        }
-        *abort_flag = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    }
-    __syncthreads();
-
-    if (threadIdx.x >= p.cons_threads) {
-        // ------------------------------------------------------------ producer
-        if (threadIdx.x == p.cons_threads) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&tx) : "memory");
-            int it = 0, s = 0;
-            uint32_t ph = 0;  // parity of the pass over the ring
-            bool ok = true;
-            for (int r = r0; r < r1 && ok;) {
-                const int b = r / p.ho, o0 = r - b * p.ho;
-                const int len = min(r1 - r, p.ho - o0);
-                const int stages = (len + 2 + 2) / 3;
-                for (int k = 0; k < stages; k++, it++) {
-                    if (it >= p.slots && !st_wait(smem_u32(&empty[s]), ph ^ 1u, p, abort_flag, 30)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_expect_tx(smem_u32(&full[s]), p.stage_bytes);
-                    tma_load_4d(smem_u32(smem + (size_t)s * p.slot_bytes), &tx, smem_u32(&full[s]),
-                                grp * (p.cg >> 3), strip * p.cw - p.pl, o0 - p.pt + 3 * k, b);
-                    if (++s == p.slots) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
-                }
-                r += len;
-            }
-            // let the copies still in flight land before the CTA can exit
-            for (int t = max(0, it - p.slots); t < it; t++) {
-                const int sl = t % p.slots;
-                const uint64_t t0 = globaltimer_ns();
-                while (!mbar_try_wait(smem_u32(&full[sl]), (uint32_t)((t / p.slots) & 1)) &&
-                       globaltimer_ns() - t0 < p.wait_cap_ns) {
-                }
-            }
-        }
-        return;
-    }
-
-    // ---------------------------------------------------------------- consumers
     const int g = threadIdx.x % p.words;  // channel word within the lane's group
     const int q = threadIdx.x / p.words;  // column group within the strip
     const int lane = threadIdx.x & 31;
@@ -463,15 +410,11 @@ __global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kSh
 #pragma unroll
     for (int j = 0; j < kCPT; j++) colmask |= (ow0 + j < p.wo) ? (1 << j) : 0;
     const bool wfull = __all_sync(0xFFFFFFFFu, colmask == (1 << kCPT) - 1);
-    // shared addresses: the thread's first word in slot 0, its column offsets,
-    // the stride of a stage row, the barriers
-    const uint32_t slot0 = smem_u32(smem) + 4u * (uint32_t)(q * kCPT * p.words + g);
+    // the thread's column offsets and the stride of a stage row (shared bytes)
     uint32_t coff[kCPT + 2];
 #pragma unroll
     for (int c = 0; c < kCPT + 2; c++) coff[c] = 4u * (uint32_t)(c * p.words);
     const uint32_t rw4 = 4u * (uint32_t)(p.bw * p.words);
-    const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty);
-    RingPos rp{slot0, full0, 0, 0u};
     const size_t row_words = (size_t)p.wo * cwords;
     uint32_t *y32 = reinterpret_cast<uint32_t *>(y);
     bool ok = true;
@@ -492,6 +435,118 @@ __global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kSh
     // channels outside the fast range: exact outputs over the fast ones (same
     // thread, same addresses, later in program order)
     if (ok && !fast) st_exact_outputs<kCPT>(p, w, y, c0, ow0, r0, r1);
+    return ok;
+}
+
+// The CTA's pieces of work: a lane and a row range of it (header comment).
+// Call with pi = 0, 1, ...; returns false after the last piece.
+__device__ __forceinline__ bool cta_piece(const DwStreamParams &p, int lanes, int pi, int &lane, int &r0, int &r1) {
+    const int R = p.n * p.ho;
+    const int main_ctas = lanes * p.per_lane;
+    if ((int)blockIdx.x < main_ctas) {
+        if (pi) return false;
+        const int part = blockIdx.x / lanes;
+        lane = blockIdx.x % lanes;
+        r0 = (int)((long long)part * p.rows_main / p.per_lane);
+        r1 = (int)((long long)(part + 1) * p.rows_main / p.per_lane);
+        return r0 < r1;
+    }
+    // the tails of all lanes concatenated, split evenly over the extra CTAs
+    const long long lt = R - p.rows_main, total = (long long)lanes * lt;
+    const int e = blockIdx.x - main_ctas;
+    long long g = (long long)e * total / p.extra;
+    const long long g1 = (long long)(e + 1) * total / p.extra;
+    for (int k = 0; g < g1; k++) {
+        const int ln = (int)(g / lt);
+        const long long end = std::min<long long>(g1, (long long)(ln + 1) * lt);
+        if (k == pi) {
+            lane = ln;
+            r0 = p.rows_main + (int)(g - (long long)ln * lt);
+            r1 = r0 + (int)(end - g);
+            return true;
+        }
+        g = end;
+    }
+    return false;
+}
+
+template <int kShape, bool kRelu>
+__global__ void __launch_bounds__(kStShapes[kShape].max_cons + 32, kStShapes[kShape].min_blocks)
+    k_dwconv3x3_stream(const __grid_constant__ CUtensorMap tx, const int8_t *__restrict__ w, int8_t *__restrict__ y,
+                       const __grid_constant__ DwStreamParams p) {
+    constexpr int kCPT = kStShapes[kShape].cpt;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)p.slots * p.slot_bytes);
+    uint64_t *empty = full + kStreamMaxSlots;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStreamMaxSlots);
+    const int cons_warps = p.cons_threads >> 5;
+    const int lanes = p.groups * p.strips;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.slots; s++) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), cons_warps);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (threadIdx.x >= p.cons_threads) {
+        // ------------------------------------------------------------ producer
+        if (threadIdx.x == p.cons_threads) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tx) : "memory");
+            int it = 0, s = 0;
+            uint32_t ph = 0;  // parity of the pass over the ring
+            bool ok = true;
+            int my_lane, r0, r1;
+            for (int pi = 0; ok && cta_piece(p, lanes, pi, my_lane, r0, r1); pi++) {
+            const int grp = my_lane % p.groups, strip = my_lane / p.groups;
+            for (int r = r0; r < r1 && ok;) {
+                const int b = r / p.ho, o0 = r - b * p.ho;
+                const int len = min(r1 - r, p.ho - o0);
+                const int stages = (len + 2 + 2) / 3;
+                for (int k = 0; k < stages; k++, it++) {
+                    if (it >= p.slots && !st_wait(smem_u32(&empty[s]), ph ^ 1u, p, abort_flag, 30)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(smem_u32(&full[s]), p.stage_bytes);
+                    tma_load_4d(smem_u32(smem + (size_t)s * p.slot_bytes), &tx, smem_u32(&full[s]),
+                                grp * (p.cg >> 3), strip * p.cw - p.pl, o0 - p.pt + 3 * k, b);
+                    if (++s == p.slots) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                r += len;
+            }
+            }
+            // let the copies still in flight land before the CTA can exit
+            for (int t = max(0, it - p.slots); t < it; t++) {
+                const int sl = t % p.slots;
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(smem_u32(&full[sl]), (uint32_t)((t / p.slots) & 1)) &&
+                       globaltimer_ns() - t0 < p.wait_cap_ns) {
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    const int full0 = smem_u32(full), empty0 = smem_u32(empty);
+    // the thread's first word in slot 0 (its ring position starts there)
+    const uint32_t slot0 = smem_u32(smem) + 4u * (uint32_t)((threadIdx.x / p.words) * kCPT * p.words +
+                                                            threadIdx.x % p.words);
+    RingPos rp{slot0, (uint32_t)full0, 0, 0u};
+    int my_lane, r0, r1;
+#pragma unroll 1
+    for (int pi = 0; cta_piece(p, lanes, pi, my_lane, r0, r1); pi++)
+        if (!st_piece<kCPT, kRelu>(p, w, y, my_lane, r0, r1, rp, slot0, (uint32_t)full0, (uint32_t)empty0,
+                                   abort_flag))
+            break;
 }
 
 struct StreamPlan {
@@ -556,10 +611,24 @@ dw_status launch_stream(dw_backend *be, const CUtensorMap &tx, const int8_t *w, 
     const int per_sm = stream_occupancy<kShape, kRelu>(be->device, threads, smem);
     const int lanes = p.groups * p.strips;
     const int rows = p.n * p.ho;
-    // CTAs per lane: fill the SMs once, with at least ~24 output rows per CTA so
-    // the two halo rows of a range stay a small overhead
-    p.per_lane = std::max(1, std::min((be->sm_count * per_sm) / lanes, rows / 24));
-    const long long ctas = (long long)lanes * p.per_lane;
+    const int slots_total = be->sm_count * per_sm;
+    // main CTAs per lane: fill the SMs once, with at least ~24 output rows per
+    // CTA so the two halo rows of a range stay a small overhead
+    p.per_lane = std::max(1, std::min(slots_total / lanes, rows / 24));
+    p.rows_main = rows;
+    p.extra = 0;
+    const int spare = slots_total - lanes * p.per_lane;
+    if (spare > 0 && p.per_lane == slots_total / lanes) {
+        // the spare SMs take the lanes' tails: every CTA streams about
+        // lanes * rows / slots_total rows
+        const long long main_rows = (long long)rows * lanes * p.per_lane / slots_total;
+        const long long tail_rows = (long long)lanes * (rows - main_rows);
+        if (main_rows >= p.per_lane && tail_rows / spare >= 24) {
+            p.rows_main = (int)main_rows;
+            p.extra = spare;
+        }
+    }
+    const long long ctas = (long long)lanes * p.per_lane + p.extra;
     if (ctas >= (1ll << 31)) return DW_ERR_UNSUPPORTED;
     k_dwconv3x3_stream<kShape, kRelu><<<(unsigned)ctas, threads, smem, be->stream>>>(tx, w, y, p);
     return dw_after_launch(be, "dwconv3x3_stream_i8");

@@ -264,13 +264,15 @@ def test_depthwise_s1_segments_and_edges(be, be_direct, be_dwv, shape, epi):
 
 
 @pytest.mark.parametrize("shape", [(5, 9, 9, 64), (7, 3, 5, 16), (2, 112, 112, 32), (4, 14, 14, 960),
-                                   (3, 7, 7, 160), (2, 28, 28, 144), (1, 56, 56, 96), (9, 1, 12, 48)],
+                                   (3, 7, 7, 160), (2, 28, 28, 144), (1, 56, 56, 96), (9, 1, 12, 48),
+                                   (3, 112, 112, 576), (4, 200, 56, 160)],
                          ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("epi", [dw.EPI_RELU6, dw.EPI_RELU, dw.EPI_NONE])
 def test_depthwise_stream_shapes(be_dwv, shape, epi):
     """MobileNet-style channel counts (16 .. 960: one or several channel groups
     per lane), small maps where one CTA's row range crosses several images,
-    a one-row image; bit-exact on every variant."""
+    a one-row image, and sizes where spare SMs take the lanes' last rows (one
+    such CTA spanning several lanes); bit-exact on every variant."""
     n, h, w, c = shape
     rng = np.random.default_rng(n * h * w + c + 7 * epi)
     case = conv_case(rng, n, h, w, c, c, k=3, s=1, group=c, epilogue=epi)
