@@ -86,7 +86,7 @@ struct ChanSmem {
     int32_t bias[kChanSlots];
     float m[kChanSlots];
     float d[kChanSlots];
-    uint32_t cflags[kChanSlots / 16];  // per 16 slots: bit0 = fast-path inputs finite, bit1 = |acc+bias| < 2^22 certain
+    uint32_t cflags[kChanSlots / 16];  // per 16 slots: bit0 = fast-path inputs finite, bit1 = |acc+bias| < 2^22 certain, bit2 = the one-add ReLU path applies
 };
 
 
@@ -207,8 +207,13 @@ __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs,
     const bool finite = p.ep.epilogue == DW_EPI_SILU ? (isfinite(dsc) && isfinite(p.ep.inv_s_out)) : isfinite(m);
     const long long b = bias < 0 ? -(long long)bias : (long long)bias;
     const bool safe = p.acc_bound + b < (1ll << 22);
+    // bit2: the ReLU path with one directed-rounding add applies: |v| =
+    // |(acc + bias) * M| < 2^21 for every accumulator (kept below 2e6), so
+    // v + 1.5 * 2^22 + 0.5 stays in [2^22, 2^23)
+    const bool r16 = safe && isfinite(m) && fabsf(m) * (float)(p.acc_bound + b) < 2.0e6f;
     const uint32_t bf = __ballot_sync(0xffffffffu, finite);
     const uint32_t bs = __ballot_sync(0xffffffffu, safe);
+    const uint32_t br = __ballot_sync(0xffffffffu, r16);
     if (write) {
         cs->bias[slot] = bias;
         cs->m[slot] = m;
@@ -219,7 +224,8 @@ __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs,
     const int lane = threadIdx.x & 31;
     if ((lane & 15) == 0 && write) {
         const uint32_t sh = lane;  // 0 or 16
-        const uint32_t f = (((bf >> sh) & 0xFFFFu) == 0xFFFFu ? 1u : 0u) | (((bs >> sh) & 0xFFFFu) == 0xFFFFu ? 2u : 0u);
+        const uint32_t f = (((bf >> sh) & 0xFFFFu) == 0xFFFFu ? 1u : 0u) | (((bs >> sh) & 0xFFFFu) == 0xFFFFu ? 2u : 0u) |
+                           (((br >> sh) & 0xFFFFu) == 0xFFFFu ? 4u : 0u);
         cs->cflags[slot >> 4] = f;
     }
 }
@@ -279,6 +285,41 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
                           reinterpret_cast<const float4 *>(sm)[2], reinterpret_cast<const float4 *>(sm)[3]};
     const int32_t *bb = reinterpret_cast<const int32_t *>(b4);
     const float *mm = reinterpret_cast<const float *>(m4);
+    if ((epi == DW_EPI_RELU || (epi == DW_EPI_RELU6 && p.ep.q6 >= 0)) && __all_sync(0xffffffffu, (fl & 4u) != 0)) {
+        // ReLU / ReLU6, exact and branch-free: v = fl((acc + bias) * M) as the
+        // reference (acc + bias + magic bits read as a float, minus 1.5 * 2^23);
+        // one add rounded toward zero of 1.5 * 2^22 + 0.5 (the spacing there is
+        // 0.5) gives 1.5 * 2^22 + floor(2 v + 1) / 2, whose bits minus those of
+        // 1.5 * 2^22 are floor(2 v + 1); clamped to [0, 2 hi + 1] in one integer
+        // op and halved, that is clamp(floor(v + 0.5), 0, hi), which equals the
+        // ReLU-bounded roundf(v) (floor(v + 0.5) == roundf(v) for v >= 0, both
+        // <= 0 below zero; the bounds are integers).
+        const int4 d4[4] = {reinterpret_cast<const int4 *>(&cs->d[slot0])[0],
+                            reinterpret_cast<const int4 *>(&cs->d[slot0])[1],
+                            reinterpret_cast<const int4 *>(&cs->d[slot0])[2],
+                            reinterpret_cast<const int4 *>(&cs->d[slot0])[3]};
+        const int32_t *bm = reinterpret_cast<const int32_t *>(d4);
+        const int hi = epi == DW_EPI_RELU6 ? min(p.ep.q6, 127) : 127;
+        const float2 nmag = make_float2(-kMagic, -kMagic);
+        const float2 mag = make_float2(6291456.5f, 6291456.5f);  // 1.5 * 2^22 + 0.5
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            int32_t t[4];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int k0 = q * 4 + 2 * h;
+                const float2 f = __fadd2_rn(make_float2(__int_as_float((int32_t)((uint32_t)v[k0] + (uint32_t)bm[k0])),
+                                                        __int_as_float((int32_t)((uint32_t)v[k0 + 1] + (uint32_t)bm[k0 + 1]))),
+                                            nmag);
+                const float2 r = __fadd2_rz(__fmul2_rn(f, make_float2(mm[k0], mm[k0 + 1])), mag);
+                t[2 * h] = __viaddmin_s32_relu(__float_as_int(r.x), -0x4AC00000, 2 * hi + 1);
+                t[2 * h + 1] = __viaddmin_s32_relu(__float_as_int(r.y), -0x4AC00000, 2 * hi + 1);
+            }
+            const uint32_t packed = __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
+            w[q] = (packed >> 1) & 0x7F7F7F7Fu;
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
     bool inrange = true;
     if (!(fl & 2u)) {
 #pragma unroll

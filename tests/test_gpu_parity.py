@@ -217,6 +217,32 @@ def test_conv_rounding_ties(be_umma, be_direct, k, group):
     _check_conv(be_umma, (desc, x, wt, b, M, D))
 
 
+@pytest.mark.parametrize("k", [1, 3])
+@pytest.mark.parametrize("epi,q6", [(dw.EPI_RELU, 127), (dw.EPI_RELU6, 6), (dw.EPI_RELU6, 0), (dw.EPI_RELU6, 127)])
+def test_conv_relu_requant_edges(be_umma, be_direct, k, epi, q6):
+    """ReLU / ReLU6 requantisation of the tensor-core conv over its one-add
+    path and the fall-back: scales that make .5 ties common (0.5, 0.25), zero,
+    negative and tiny scales, scales at and beyond the one-add path's range
+    (per 16-channel group), large biases, and ReLU6 ceilings of 0 and 127."""
+    rng = np.random.default_rng(77 + k + q6)
+    c_in, c_out = 32, 64
+    desc, x, wt, b, M, D = conv_case(rng, 2, 12, 12, c_in, c_out, k=k, epilogue=epi, x_range=(-128, 127))
+    M = M.copy()
+    M[0:8] = np.float32(0.5)
+    M[8:16] = np.float32(0.25)
+    M[16:18] = np.float32(0.0)
+    M[18:20] = np.float32(-0.3)
+    M[20:24] = np.float32(1e-7)
+    M[32:48] = np.float32(3.0)     # a whole 16-channel group beyond the one-add range for k = 3
+    M[48:52] = np.float32(0.05)
+    b = b.copy()
+    b[52:56] = 1_500_000
+    b[56:60] = -1_500_000
+    desc.q6 = q6
+    for be_ in (be_umma, be_direct):
+        _check_conv(be_, (desc, x, wt, b, M, D))
+
+
 @pytest.mark.parametrize("c_in,k,s", [(64, 1, 1), (32, 3, 1), (3, 3, 2)])
 def test_silu_stress_full_range(be, be_direct, c_in, k, s):
     """SiLU over y in about [-20, 20] with t = silu(y)/s_out spanning the whole
