@@ -279,12 +279,6 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
         }
         return make_uint4(w[0], w[1], w[2], w[3]);
     }
-    const int4 b4[4] = {reinterpret_cast<const int4 *>(sb)[0], reinterpret_cast<const int4 *>(sb)[1],
-                        reinterpret_cast<const int4 *>(sb)[2], reinterpret_cast<const int4 *>(sb)[3]};
-    const float4 m4[4] = {reinterpret_cast<const float4 *>(sm)[0], reinterpret_cast<const float4 *>(sm)[1],
-                          reinterpret_cast<const float4 *>(sm)[2], reinterpret_cast<const float4 *>(sm)[3]};
-    const int32_t *bb = reinterpret_cast<const int32_t *>(b4);
-    const float *mm = reinterpret_cast<const float *>(m4);
     if ((epi == DW_EPI_RELU || (epi == DW_EPI_RELU6 && p.ep.q6 >= 0)) && __all_sync(0xffffffffu, (fl & 4u) != 0)) {
         // ReLU / ReLU6, exact and branch-free: v = fl((acc + bias) * M) as the
         // reference (acc + bias + magic bits read as a float, minus 1.5 * 2^23);
@@ -294,11 +288,12 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
         // op and halved, that is clamp(floor(v + 0.5), 0, hi), which equals the
         // ReLU-bounded roundf(v) (floor(v + 0.5) == roundf(v) for v >= 0, both
         // <= 0 below zero; the bounds are integers).
-        const int4 d4[4] = {reinterpret_cast<const int4 *>(&cs->d[slot0])[0],
-                            reinterpret_cast<const int4 *>(&cs->d[slot0])[1],
-                            reinterpret_cast<const int4 *>(&cs->d[slot0])[2],
-                            reinterpret_cast<const int4 *>(&cs->d[slot0])[3]};
+        // the 16 channels' bias + magic bits and M (shared loads, the same for all lanes)
+        const uint32_t da = smem_u32(&cs->d[slot0]), ma = smem_u32(&cs->m[slot0]);
+        const uint4 d4[4] = {lds_v4(da), lds_v4(da + 16), lds_v4(da + 32), lds_v4(da + 48)};
+        const uint4 m4[4] = {lds_v4(ma), lds_v4(ma + 16), lds_v4(ma + 32), lds_v4(ma + 48)};
         const int32_t *bm = reinterpret_cast<const int32_t *>(d4);
+        const float *mm = reinterpret_cast<const float *>(m4);
         const int hi = epi == DW_EPI_RELU6 ? min(p.ep.q6, 127) : 127;
         const float2 nmag = make_float2(-kMagic, -kMagic);
         const float2 mag = make_float2(6291456.5f, 6291456.5f);  // 1.5 * 2^22 + 0.5
@@ -320,6 +315,12 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
         }
         return make_uint4(w[0], w[1], w[2], w[3]);
     }
+    const int4 b4[4] = {reinterpret_cast<const int4 *>(sb)[0], reinterpret_cast<const int4 *>(sb)[1],
+                        reinterpret_cast<const int4 *>(sb)[2], reinterpret_cast<const int4 *>(sb)[3]};
+    const float4 m4[4] = {reinterpret_cast<const float4 *>(sm)[0], reinterpret_cast<const float4 *>(sm)[1],
+                          reinterpret_cast<const float4 *>(sm)[2], reinterpret_cast<const float4 *>(sm)[3]};
+    const int32_t *bb = reinterpret_cast<const int32_t *>(b4);
+    const float *mm = reinterpret_cast<const float *>(m4);
     bool inrange = true;
     if (!(fl & 2u)) {
 #pragma unroll
@@ -801,12 +802,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else if (p.R == 1) {  // one row block: contiguous chunk halves, one TMEM load per wait
                 const int per1 = (chunks + 1) / 2;
                 const int cb = half * per1, ce = min(chunks, cb + per1);
-                for (int c = cb; c < ce; c++) {
-                    int32_t v[16];
-                    tc_ld16(tacc + (uint32_t)(c * 16), v);
-                    uint8_t *dst = stage + (size_t)row * p.bn + c * 16;
+                // two TMEM loads in flight per wait (the loads are collective: past
+                // the end the last chunk is loaded again and not stored)
+                const uint32_t dst0 = smem_u32(stage) + (uint32_t)(row * p.bn);
+                for (int c = cb; c < ce; c += 2) {
+                    const int c2 = min(c + 1, ce - 1);
+                    int32_t v1[16], v2[16];
+                    tc_ld16(tacc + (uint32_t)(c * 16), v1);
+                    tc_ld16(tacc + (uint32_t)(c2 * 16), v2);
                     tc_wait_ld();
-                    *reinterpret_cast<uint4 *>(dst) = requant16<kSilu>(v, chan, slot_base + c * 16, p);
+                    sts_v4(dst0 + (uint32_t)(c * 16), requant16<kSilu>(v1, chan, slot_base + c * 16, p));
+                    if (c + 1 < ce) sts_v4(dst0 + (uint32_t)(c2 * 16), requant16<kSilu>(v2, chan, slot_base + c2 * 16, p));
                 }
             } else {
             const int per = (items + 1) / 2;
