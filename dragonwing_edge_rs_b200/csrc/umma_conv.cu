@@ -243,11 +243,16 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
     uint32_t w[4] = {0u, 0u, 0u, 0u};
     const uint32_t fl = cs->cflags[slot0 >> 4];
     if (kSilu) {
-        const float *sd = &cs->d[slot0];
+        // the 16 channels' bias and dequant scale D (shared loads, the same for all lanes)
+        const uint32_t ba = smem_u32(sb), dd = smem_u32(&cs->d[slot0]);
+        const uint4 b4[4] = {lds_v4(ba), lds_v4(ba + 16), lds_v4(ba + 32), lds_v4(ba + 48)};
+        const uint4 s4[4] = {lds_v4(dd), lds_v4(dd + 16), lds_v4(dd + 32), lds_v4(dd + 48)};
+        const int32_t *bv = reinterpret_cast<const int32_t *>(b4);
+        const float *sd = reinterpret_cast<const float *>(s4);
         int32_t a[16];
         bool inrange = true;
 #pragma unroll
-        for (int k = 0; k < 16; k++) a[k] = (int32_t)((uint32_t)v[k] + (uint32_t)sb[k]);
+        for (int k = 0; k < 16; k++) a[k] = (int32_t)((uint32_t)v[k] + (uint32_t)bv[k]);
         if (!(fl & 2u)) {
 #pragma unroll
             for (int k = 0; k < 16; k++) inrange &= (uint32_t)(a[k] + (1 << 22)) < (1u << 23);
@@ -271,7 +276,7 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
 #pragma unroll
             for (int k = 0; k < 16; k++) {
                 if (unc & (1u << k)) {
-                    const uint32_t b = (uint8_t)epilogue_one_slow(v[k], sb[k], 0.0f, sd[k], epi, p.ep.q6, p.ep.inv_s_out);
+                    const uint32_t b = (uint8_t)epilogue_one_slow(v[k], bv[k], 0.0f, sd[k], epi, p.ep.q6, p.ep.inv_s_out);
                     const int q = k >> 2, sh = 8 * (k & 3);
                     w[q] = (w[q] & ~(0xFFu << sh)) | (b << sh);
                 }
@@ -315,10 +320,9 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
         }
         return make_uint4(w[0], w[1], w[2], w[3]);
     }
-    const int4 b4[4] = {reinterpret_cast<const int4 *>(sb)[0], reinterpret_cast<const int4 *>(sb)[1],
-                        reinterpret_cast<const int4 *>(sb)[2], reinterpret_cast<const int4 *>(sb)[3]};
-    const float4 m4[4] = {reinterpret_cast<const float4 *>(sm)[0], reinterpret_cast<const float4 *>(sm)[1],
-                          reinterpret_cast<const float4 *>(sm)[2], reinterpret_cast<const float4 *>(sm)[3]};
+    const uint32_t ba = smem_u32(sb), ma = smem_u32(sm);
+    const uint4 b4[4] = {lds_v4(ba), lds_v4(ba + 16), lds_v4(ba + 32), lds_v4(ba + 48)};
+    const uint4 m4[4] = {lds_v4(ma), lds_v4(ma + 16), lds_v4(ma + 32), lds_v4(ma + 48)};
     const int32_t *bb = reinterpret_cast<const int32_t *>(b4);
     const float *mm = reinterpret_cast<const float *>(m4);
     bool inrange = true;
@@ -334,10 +338,8 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
         // clamp to integer bounds) and rint-to-even by one RN add.  A
         // round-half-away tie can only differ from it when c - rint(c) == +-0.5
         // exactly: such chunks (rare) are redone with the per-element tie fix.
-        const int4 d4[4] = {reinterpret_cast<const int4 *>(&cs->d[slot0])[0],
-                            reinterpret_cast<const int4 *>(&cs->d[slot0])[1],
-                            reinterpret_cast<const int4 *>(&cs->d[slot0])[2],
-                            reinterpret_cast<const int4 *>(&cs->d[slot0])[3]};
+        const uint32_t da = smem_u32(&cs->d[slot0]);
+        const uint4 d4[4] = {lds_v4(da), lds_v4(da + 16), lds_v4(da + 32), lds_v4(da + 48)};
         const int32_t *bm = reinterpret_cast<const int32_t *>(d4);
         const float lo = (epi == DW_EPI_RELU || epi == DW_EPI_RELU6) ? 0.0f : -128.0f;
         const float hi = epi == DW_EPI_RELU6 ? (float)p.ep.q6 : 127.0f;
@@ -829,10 +831,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_ld16(tacc + (uint32_t)(r2 * p.bn + c2 * 16), v2);
                 uint8_t *dst1 = stage + ((size_t)(r1 * kBM + row)) * p.bn + c1 * 16;
                 tc_wait_ld();
-                *reinterpret_cast<uint4 *>(dst1) = requant16<kSilu>(v1, chan, slot_base + c1 * 16, p);
+                sts_v4(smem_u32(dst1), requant16<kSilu>(v1, chan, slot_base + c1 * 16, p));
                 if (two) {
                     uint8_t *dst2 = stage + ((size_t)(r2 * kBM + row)) * p.bn + c2 * 16;
-                    *reinterpret_cast<uint4 *>(dst2) = requant16<kSilu>(v2, chan, slot_base + c2 * 16, p);
+                    sts_v4(smem_u32(dst2), requant16<kSilu>(v2, chan, slot_base + c2 * 16, p));
                 }
                 c1 += 2;
                 while (c1 >= chunks) { c1 -= chunks; r1++; }
