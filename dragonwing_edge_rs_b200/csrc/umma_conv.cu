@@ -1058,30 +1058,41 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     }
     p.bk_elems = p.bk / esize;
     p.cblocks = (d.c_in + p.bk_elems - 1) / p.bk_elems;
-    p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
-    // Row blocks per tile: R * bn <= 256 (two TMEM accumulator buffers within 512
-    // columns), at most 8, and an A stage (R * 128 rows * bk) of at most 32 KiB.
-    int R = std::max(1, std::min({8, 256 / p.bn, 32768 / (kBM * p.bk)}));
-    if (flat) {
-        p.rows = (long long)d.n * d.h * d.w;
-        const long long blocks = (p.rows + kBM - 1) / kBM;
-        R = (int)std::min<long long>(R, blocks);
-        p.R = R;
-        p.m_tiles = (int)((blocks + R - 1) / R);
-        p.tw = kBM; p.th = 1; p.nb = 1;
-        p.a_tx_bytes = (uint32_t)(kBM * p.bk);
-    } else {
-        pick_tile(ho, wo, &p.tw, &p.th);
-        // small maps: a row block holds whole images side by side (7x7: 2 per block)
-        p.nb = (p.tw == wo && p.th == ho) ? std::max(1, std::min(kBM / (wo * ho), d.n)) : 1;
-        R = std::min(R, (ho + p.th - 1) / p.th);
-        p.R = R;
-        p.tiles_w = (wo + p.tw - 1) / p.tw;
-        p.tiles_h = (ho + p.th * R - 1) / (p.th * R);
-        p.m_tiles = ((d.n + p.nb - 1) / p.nb) * p.tiles_w * p.tiles_h;
-        p.a_tx_bytes = (uint32_t)(p.tw * p.th * p.nb * p.bk);
-    }
-    p.num_tiles = p.m_tiles * p.n_tiles;
+    // Tiles for a tile width bn and at most r_cap row blocks per tile: R * bn <=
+    // 256 (two TMEM accumulator buffers within 512 columns), at most 8, and an A
+    // stage (R * 128 rows * bk) of at most 32 KiB.
+    auto plan_tiles = [&](int bn, int r_cap) {
+        p.bn = bn;
+        p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
+        int R = std::max(1, std::min({r_cap, 8, 256 / p.bn, 32768 / (kBM * p.bk)}));
+        if (flat) {
+            p.rows = (long long)d.n * d.h * d.w;
+            const long long blocks = (p.rows + kBM - 1) / kBM;
+            R = (int)std::min<long long>(R, blocks);
+            p.R = R;
+            p.m_tiles = (int)((blocks + R - 1) / R);
+            p.tw = kBM; p.th = 1; p.nb = 1;
+            p.a_tx_bytes = (uint32_t)(kBM * p.bk);
+        } else {
+            pick_tile(ho, wo, &p.tw, &p.th);
+            // small maps: a row block holds whole images side by side (7x7: 2 per block)
+            p.nb = (p.tw == wo && p.th == ho) ? std::max(1, std::min(kBM / (wo * ho), d.n)) : 1;
+            R = std::min(R, (ho + p.th - 1) / p.th);
+            p.R = R;
+            p.tiles_w = (wo + p.tw - 1) / p.tw;
+            p.tiles_h = (ho + p.th * R - 1) / (p.th * R);
+            p.m_tiles = ((d.n + p.nb - 1) / p.nb) * p.tiles_w * p.tiles_h;
+            p.a_tx_bytes = (uint32_t)(p.tw * p.th * p.nb * p.bk);
+        }
+        p.num_tiles = p.m_tiles * p.n_tiles;
+    };
+    plan_tiles(p.bn, 8);
+    // Small problems (tiles for fewer than half the SMs): fewer row blocks per
+    // tile, then narrower tiles (down to 64 channels), until half the SMs have a
+    // tile -- more CTAs stream the long K loops side by side; the extra reads of
+    // the A tiles come from L2.
+    while (2 * p.num_tiles < be->sm_count && p.R > 1) plan_tiles(p.bn, p.R - 1);
+    while (2 * p.num_tiles < be->sm_count && p.bn >= 128 && (p.bn / 2) % 16 == 0) plan_tiles(p.bn / 2, 1);
     // fp16 staging in swizzled 64-channel slabs (conflict-free epilogue stores)
     // when every tile's channels split into whole slabs.
     if (esize == 2 && p.bn % 64 == 0 && !getenv("DW_F16_NOSWZ")) p.swz = 1;
