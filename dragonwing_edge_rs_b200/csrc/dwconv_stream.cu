@@ -177,7 +177,9 @@ __device__ __forceinline__ void st_row(const uint32_t (&X)[kCPT + 2], const int3
 // hi): floor(v + 0.5) == roundf(v) for v >= 0, both are <= 0 below zero, and
 // halving commutes with the clamp because 2 hi + 1 halves to hi.  The halving
 // runs on the packed bytes (every lane is at most 255 there).  The packed
-// directed-rounding add issues on the FMA pipe at the full f32x2 rate.
+// directed-rounding add issues on the FMA pipe at the full f32x2 rate; the
+// compiler does not fuse it with the round-to-nearest multiply before it (the
+// rounding modes differ), so v is rounded as the reference rounds it.
 __device__ __forceinline__ uint32_t requant_relu4(const int32_t (&a)[4], const float2 (&m)[2], uint32_t hi2) {
     const float2 nmag = make_float2(-kMagic, -kMagic);
     const float2 mag = make_float2(6291456.5f, 6291456.5f);  // 1.5 * 2^22 + 0.5

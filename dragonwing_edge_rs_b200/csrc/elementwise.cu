@@ -6,6 +6,8 @@
 // stores) over a grid-stride loop sized to a multiple of the SM count, with a
 // scalar tail for lengths that are not multiples of 16.
 
+#include <cmath>
+
 #include "dw_device.cuh"
 
 namespace dw {
@@ -83,6 +85,66 @@ __global__ void k_add_i8(const int8_t *__restrict__ a, const int8_t *__restrict_
     for (size_t i = n16 * 16 + tid; i < n; i += stride) {
         float y = __fadd_rn(__fmul_rn(i2f_small(a[i]), ra), __fmul_rn(i2f_small(b[i]), rb));
         out[i] = (int8_t)f32_to_i8(y);
+    }
+}
+
+// Fast path of add_i8 for 16 elements, taken when the ratios are finite and
+// below 1e30 (no overflow to infinity, so no NaN from inf - inf): the same
+// f32 operations as the reference, the conversions and rounding steps two
+// elements per packed instruction.  A
+// byte a placed in the low mantissa bits of 1.5 * 2^23 (after a ^ 0x80, i.e.
+// a + 128) reads as 1.5 * 2^23 + 128 + a, and subtracting 1.5 * 2^23 + 128
+// (exact) gives a.  y = fl(fl(a * ra) + fl(b * rb)); clamp to [-128, 127] in
+// f32; rint by the magic add; ties (c - rint(c) == +-0.5, rare) are redone
+// per element with roundf's half-away-from-zero.
+__device__ __forceinline__ uint4 add16_fast(uint4 a, uint4 b, float2 ra2, float2 rb2, float ra, float rb) {
+    const float2 off = make_float2(-(kMagic + 128.0f), -(kMagic + 128.0f));
+    const float2 mag = make_float2(kMagic, kMagic), nmag = make_float2(-kMagic, -kMagic);
+    const float2 neg1 = make_float2(-1.0f, -1.0f);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t out[4];
+    bool tie = false;
+#pragma unroll
+    for (int wd = 0; wd < 4; wd++) {
+        const uint32_t ax = aw[wd] ^ 0x80808080u, bx = bw[wd] ^ 0x80808080u;
+        uint32_t q[4];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t s0 = 0x7650u | (uint32_t)(2 * h), s1 = 0x7650u | (uint32_t)(2 * h + 1);
+            const float2 fa = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(ax, 0x4B400000u, s0)),
+                                                     __uint_as_float(__byte_perm(ax, 0x4B400000u, s1))), off);
+            const float2 fb = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(bx, 0x4B400000u, s0)),
+                                                     __uint_as_float(__byte_perm(bx, 0x4B400000u, s1))), off);
+            // scalar products and sum: a packed multiply feeding a packed
+            // round-to-nearest add can be fused into one multiply-add by the
+            // compiler, which skips the reference's rounding of the products
+            float2 c = make_float2(__fadd_rn(__fmul_rn(fa.x, ra2.x), __fmul_rn(fb.x, rb2.x)),
+                                   __fadd_rn(__fmul_rn(fa.y, ra2.y), __fmul_rn(fb.y, rb2.y)));
+            c.x = fminf(fmaxf(c.x, -128.0f), 127.0f);
+            c.y = fminf(fmaxf(c.y, -128.0f), 127.0f);
+            const float2 r = __fadd2_rn(c, mag);
+            const float2 d = __ffma2_rn(__fadd2_rn(r, nmag), neg1, c);  // c - rint(c), exact
+            tie |= fmaxf(fabsf(d.x), fabsf(d.y)) == 0.5f;
+            q[2 * h] = __float_as_uint(r.x);
+            q[2 * h + 1] = __float_as_uint(r.y);
+        }
+        out[wd] = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+    }
+    if (tie) {
+#pragma unroll
+        for (int wd = 0; wd < 4; wd++) out[wd] = add4(aw[wd], bw[wd], ra, rb);
+    }
+    return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+__global__ void k_add_i8_fast(const int8_t *__restrict__ a, const int8_t *__restrict__ b, int8_t *__restrict__ out,
+                              size_t n16, float ra, float rb) {
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+    const float2 ra2 = make_float2(ra, ra), rb2 = make_float2(rb, rb);
+    for (size_t i = tid; i < n16; i += stride) {
+        const uint4 va = __ldcs(reinterpret_cast<const uint4 *>(a) + i);
+        const uint4 vb = __ldcs(reinterpret_cast<const uint4 *>(b) + i);
+        __stcs(reinterpret_cast<uint4 *>(out) + i, add16_fast(va, vb, ra2, rb2, ra, rb));
     }
 }
 
@@ -390,6 +452,11 @@ dw_status launch_relu_i8(dw_backend *be, const int8_t *in, int8_t *out, size_t n
 }
 
 dw_status launch_add_i8(dw_backend *be, const int8_t *a, const int8_t *b, int8_t *out, size_t n, float ra, float rb) {
+    const bool aligned = ((uintptr_t)a & 15) == 0 && ((uintptr_t)b & 15) == 0 && ((uintptr_t)out & 15) == 0;
+    if (aligned && n % 16 == 0 && std::fabs(ra) < 1e30f && std::fabs(rb) < 1e30f) {
+        k_add_i8_fast<<<grid_for(be, n / 16), kThreads, 0, be->stream>>>(a, b, out, n / 16, ra, rb);
+        return dw_after_launch(be, "add_i8");
+    }
     k_add_i8<<<grid_for(be, (n + 15) / 16), kThreads, 0, be->stream>>>(a, b, out, n, ra, rb);
     return dw_after_launch(be, "add_i8");
 }

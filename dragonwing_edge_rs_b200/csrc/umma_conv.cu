@@ -292,7 +292,9 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
         // 1.5 * 2^22 are floor(2 v + 1); clamped to [0, 2 hi + 1] in one integer
         // op and halved, that is clamp(floor(v + 0.5), 0, hi), which equals the
         // ReLU-bounded roundf(v) (floor(v + 0.5) == roundf(v) for v >= 0, both
-        // <= 0 below zero; the bounds are integers).
+        // <= 0 below zero; the bounds are integers).  The compiler does not
+        // fuse the round-to-nearest multiply into the round-toward-zero add
+        // (the rounding modes differ), so v is rounded as the reference rounds it.
         // the 16 channels' bias + magic bits and M (shared loads, the same for all lanes)
         const uint32_t da = smem_u32(&cs->d[slot0]), ma = smem_u32(&cs->m[slot0]);
         const uint4 d4[4] = {lds_v4(da), lds_v4(da + 16), lds_v4(da + 32), lds_v4(da + 48)};

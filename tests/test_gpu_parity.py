@@ -128,6 +128,24 @@ def test_elementwise_parity(be, n):
     assert np.array_equal(be.download_array(bo, np.int8), dwref.quantize_u8_to_i8(u, 0.0123))
 
 
+@pytest.mark.parametrize("n", [16, 4096, 65536, 4099])
+@pytest.mark.parametrize("ra,rb", [(0.5, 0.25), (0.5, -0.5), (0.731, 1.27), (3.0e-39, 1.0), (1e30, 2.0),
+                                   (-1.5, 2.5e2)])
+def test_add_i8_ratios(be, n, ra, rb):
+    """add_i8 over ratio pairs that make .5 ties common (0.5, 0.25, -0.5), a
+    subnormal ratio, ratios at and past the packed path's limit (1e30) and
+    large ones that saturate; multiples of 16 take the packed path, 4099 the
+    per-element one.  Bit-exact against the reference's add_i8."""
+    rng = np.random.default_rng(n + int(abs(rb) * 10))
+    a = rng.integers(-128, 128, n).astype(np.int8)
+    b = rng.integers(-128, 128, n).astype(np.int8)
+    ba, bb, bo = be.upload_array(a), be.upload_array(b), be.alloc(n)
+    ra, rb = float(np.float32(ra)), float(np.float32(rb))
+    ops.add_i8_packed(be, ba, bb, bo, ra, rb)
+    got, exp = be.download_array(bo, np.int8), dwref.add_i8(a, b, ra, rb)
+    assert np.array_equal(got, exp), mismatch_report(got, exp)
+
+
 # ---------------------------------------------------------------- fused conv parity
 
 def _check_conv(be, case):
