@@ -37,9 +37,13 @@ namespace dw {
 namespace {
 
 constexpr int kBM = 128;            // MMA M (rows per tile = pixels)
-constexpr int kEpiWarps = 8;        // epilogue warps (2 per TMEM lane quarter)
-constexpr int kStoreWarp = 2 + kEpiWarps;   // stores the staged tiles, fetches fp16 residuals
-constexpr int kThreads = 64 + 32 * kEpiWarps + 32;
+// Warp roles: 0 producer, 1 MMA, then the epilogue warps (4 per part: warps
+// sharing a TMEM lane quarter split its (row block, chunk) items), then the
+// store warp.  The int8 kernels run 12 epilogue warps (three interleaved
+// requantisation streams per scheduler; 128 registers a thread); the fp16
+// kernels keep 8 (their epilogue needs more registers).
+constexpr int epi_warps(bool f16) { return f16 ? 8 : 12; }
+constexpr int umma_threads(bool f16) { return 64 + 32 * epi_warps(f16) + 32; }
 constexpr int kMaxStages = 12;
 
 struct UmmaParams {
@@ -540,10 +544,13 @@ __device__ __forceinline__ int valid_blocks(const UmmaParams &p, const TileCoord
 // kSilu: int8 SiLU epilogue.  kF16: fp16 operands (kind::f16) with the fp16
 // epilogue; kFm its bias / residual / ReLU flags.
 template <bool kSilu, bool kF16, int kFm>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(umma_threads(kF16), 1)
     k_umma_conv_i8(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_r,
                    const __grid_constant__ UmmaParams p) {
+    constexpr int kEpiWarps = epi_warps(kF16);
+    constexpr int kEpiParts = kEpiWarps / 4;
+    constexpr int kStoreWarp = 2 + kEpiWarps;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1 KiB-aligned base (swizzle patterns repeat every 1 KiB).
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -694,10 +701,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp < kStoreWarp) {
         // ------------------------------------------------------------ epilogue
-        const int e = warp - 2;               // 0..7
-        const int et = threadIdx.x - 64;      // 0..255 epilogue thread index
+        const int e = warp - 2;               // 0 .. kEpiWarps - 1
+        const int et = threadIdx.x - 64;      // epilogue thread index
         const int quarter = warp & 3;         // TMEM lanes this warp may access
-        const int half = e >> 2;              // which half of the (row block, chunk) items
+        const int part = e >> 2;              // which part of the (row block, chunk) items
         const int row = quarter * 32 + lane;  // row within a 128-row block
         const int chunks = p.bn / 16;
         const int items = p.R * chunks;
@@ -739,14 +746,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * acc_cols;
-            // each half of the warps takes a contiguous run of (row block, chunk)
+            // each part of the warps takes a contiguous run of (row block, chunk)
             // items, two TMEM loads in flight per wait; (r, c) advance without division.
             if constexpr (kF16) {
-                // fp16: each half of the warps takes a contiguous run of (row block,
+                // fp16: each part of the warps takes a contiguous run of (row block,
                 // chunk) items, four TMEM loads in flight per wait; (r, c) advance
                 // without division.
-                const int per = (items + 1) / 2;
-                const int i_begin = half * per, i_end = min(items, i_begin + per);
+                const int per = (items + kEpiParts - 1) / kEpiParts;
+                const int i_begin = part * per, i_end = min(items, i_begin + per);
                 int r0 = i_begin / chunks, c0 = i_begin - (i_begin / chunks) * chunks;
                 const uint32_t r7 = (uint32_t)(row & 7);
                 for (int i = i_begin; i < i_end; i += 4) {
@@ -804,8 +811,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else if (p.R == 1) {  // one row block: contiguous chunk halves, one TMEM load per wait
-                const int per1 = (chunks + 1) / 2;
-                const int cb = half * per1, ce = min(chunks, cb + per1);
+                const int per1 = (chunks + kEpiParts - 1) / kEpiParts;
+                const int cb = part * per1, ce = min(chunks, cb + per1);
                 // two TMEM loads in flight per wait (the loads are collective: past
                 // the end the last chunk is loaded again and not stored)
                 const uint32_t dst0 = smem_u32(stage) + (uint32_t)(row * p.bn);
@@ -819,8 +826,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (c + 1 < ce) sts_v4(dst0 + (uint32_t)(c2 * 16), requant16<kSilu>(v2, chan, slot_base + c2 * 16, p));
                 }
             } else {
-            const int per = (items + 1) / 2;
-            const int i_begin = half * per, i_end = min(items, i_begin + per);
+            const int per = (items + kEpiParts - 1) / kEpiParts;
+            const int i_begin = part * per, i_end = min(items, i_begin + per);
             int r1 = 0, c1 = i_begin;
             while (c1 >= chunks) { c1 -= chunks; r1++; }
             for (int i = i_begin; i < i_end; i += 2) {
@@ -1223,11 +1230,11 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     const int grid = std::min(p.num_tiles, be->sm_count);
     if (esize == 2) {
         const int fm = (bias_f16 ? 1 : 0) | (res_f16 ? 2 : 0) | (relu ? 4 : 0);
-        f16_kernels[fm]<<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, tr, p);
+        f16_kernels[fm]<<<grid, umma_threads(true), smem, be->stream>>>(ta, tb, ty, tr, p);
     } else if (ep.epilogue == DW_EPI_SILU) {
-        k_umma_conv_i8<true, false, 0><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, tr, p);
+        k_umma_conv_i8<true, false, 0><<<grid, umma_threads(false), smem, be->stream>>>(ta, tb, ty, tr, p);
     } else {
-        k_umma_conv_i8<false, false, 0><<<grid, kThreads, smem, be->stream>>>(ta, tb, ty, tr, p);
+        k_umma_conv_i8<false, false, 0><<<grid, umma_threads(false), smem, be->stream>>>(ta, tb, ty, tr, p);
     }
     return dw_after_launch(be, esize == 2 ? "umma_conv_f16" : "umma_conv_i8");
 }
