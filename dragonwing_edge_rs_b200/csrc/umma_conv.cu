@@ -39,10 +39,10 @@ namespace {
 constexpr int kBM = 128;            // MMA M (rows per tile = pixels)
 // Warp roles: 0 producer, 1 MMA, then the epilogue warps (4 per part: warps
 // sharing a TMEM lane quarter split its (row block, chunk) items), then the
-// store warp.  The int8 kernels run 12 epilogue warps (three interleaved
-// requantisation streams per scheduler; 128 registers a thread); the fp16
-// kernels keep 8 (their epilogue needs more registers).
-constexpr int epi_warps(bool f16) { return f16 ? 8 : 12; }
+// store warp.  12 epilogue warps: three interleaved epilogue streams per
+// scheduler, 128 registers a thread (the fp16 epilogue then keeps two TMEM
+// loads in flight per wait instead of four).
+constexpr int epi_warps(bool) { return 12; }
 constexpr int umma_threads(bool f16) { return 64 + 32 * epi_warps(f16) + 32; }
 constexpr int kMaxStages = 12;
 
@@ -549,6 +549,7 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_r,
                    const __grid_constant__ UmmaParams p) {
     constexpr int kEpiWarps = epi_warps(kF16);
+    constexpr int kF16Batch = kEpiWarps > 8 ? 2 : 4;  // fp16 TMEM loads per wait (registers)
     constexpr int kEpiParts = kEpiWarps / 4;
     constexpr int kStoreWarp = 2 + kEpiWarps;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -750,17 +751,17 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
             // items, two TMEM loads in flight per wait; (r, c) advance without division.
             if constexpr (kF16) {
                 // fp16: each part of the warps takes a contiguous run of (row block,
-                // chunk) items, four TMEM loads in flight per wait; (r, c) advance
-                // without division.
+                // chunk) items, kF16Batch TMEM loads in flight per wait; (r, c)
+                // advance without division.
                 const int per = (items + kEpiParts - 1) / kEpiParts;
                 const int i_begin = part * per, i_end = min(items, i_begin + per);
                 int r0 = i_begin / chunks, c0 = i_begin - (i_begin / chunks) * chunks;
                 const uint32_t r7 = (uint32_t)(row & 7);
-                for (int i = i_begin; i < i_end; i += 4) {
-                    int rr[4], cc[4];
+                for (int i = i_begin; i < i_end; i += kF16Batch) {
+                    int rr[kF16Batch], cc[kF16Batch];
                     rr[0] = r0; cc[0] = c0;
 #pragma unroll
-                    for (int q = 1; q < 4; q++) {  // the next items; past the end repeat the last (the loads are collective)
+                    for (int q = 1; q < kF16Batch; q++) {  // the next items; past the end repeat the last (the loads are collective)
                         int r = rr[q - 1], c = cc[q - 1] + 1;
                         if (c == chunks) { c = 0; r++; }
                         const bool in = i + q < i_end;
@@ -768,7 +769,7 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                         cc[q] = in ? c : cc[q - 1];
                     }
                     {
-                        int r = rr[3], c = cc[3] + 1;
+                        int r = rr[kF16Batch - 1], c = cc[kF16Batch - 1] + 1;
                         if (c == chunks) { c = 0; r++; }
                         r0 = r; c0 = c;
                     }
@@ -776,10 +777,10 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                     // layout: [row block][64-channel slab][128 rows][128 bytes], unit u
                     // of a row stored at (u ^ (row & 7)) * 16 -- the TMA 128-byte
                     // swizzle, so the 32 rows a warp writes at once fall in distinct banks.
-                    int32_t v[4][16];
-                    uint8_t *u0[4];
+                    int32_t v[kF16Batch][16];
+                    uint8_t *u0[kF16Batch];
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
+                    for (int q = 0; q < kF16Batch; q++) {
                         tc_ld16(tacc + (uint32_t)(rr[q] * p.bn + cc[q] * 16), v[q]);
                         u0[q] = p.swz ? stage + (size_t)rr[q] * kBM * p.bn * 2 + (size_t)(cc[q] >> 2) * (kBM * 128) +
                                             row * 128 + (((((uint32_t)cc[q] & 3u) << 1) ^ r7) << 4)
@@ -787,10 +788,10 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                     }
                     // the second 16-byte unit: the next unit (linear), or unit ^ 1 (swizzled)
                     const uintptr_t u1x = p.swz ? 16u : 0u;
-                    uint32_t rw[4][8];
+                    uint32_t rw[kF16Batch][8];
                     if (res_tma) {
 #pragma unroll
-                        for (int q = 0; q < 4; q++) {
+                        for (int q = 0; q < kF16Batch; q++) {
                             const uint4 a0 = *reinterpret_cast<const uint4 *>(u0[q]);
                             const uint4 a1 = *reinterpret_cast<const uint4 *>(
                                 u1x ? (uint8_t *)((uintptr_t)u0[q] ^ u1x) : u0[q] + 16);
@@ -800,7 +801,7 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                     }
                     tc_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
+                    for (int q = 0; q < kF16Batch; q++) {
                         if (i + q < i_end) {
                             uint32_t w[8];
                             f16_epilogue16<kFm>(v[q], chan, slot_base + cc[q] * 16, p, rw[q], w);
