@@ -13,7 +13,8 @@ max-over-ranks of the device-timed region.  Rank 0 prints one JSON line.
 Workloads (synthetic data and weights with the configs' shapes and value
 distributions, seeded):
   yolov8n     (default) YOLOv8n-architecture INT8 graph, 640x640 uint8 images,
-              batch 32 per GPU (256 over 8 GPUs); value = images/s
+              batch 32 per GPU (256 over 8 GPUs), through the Detect tail and
+              postprocess_yolo to the detections; value = images/s
               conv TOPS and % of int8 peak beside it.
   mbv2_block  MobileNetV2 inverted-residual block, batch 32 per GPU, 112x112x96,
               1x1 expand 576 + ReLU6, depthwise 3x3 + ReLU6, 1x1 project 96,
@@ -177,8 +178,11 @@ def build_workload(name: str, batch: int, seed: int):
     else:
         g = G.yolov8n(batch=batch, seed=seed)
         cfg = {"workload": desc, "batch_per_gpu": batch, "width": 0.25, "depth": 0.33, "classes": 80, "reg_max": 16,
-               "layers": "63 fused int8 convs (SiLU), C2f, SPPF 5x5, PAN upsample+concat, decoupled head",
-               "input": "uint8 image /255 -> int8", "outputs": "6 head tensors dequantised to f32"}
+               "layers": "63 fused int8 convs (SiLU), C2f, SPPF 5x5, PAN upsample+concat, decoupled head, "
+                         "Detect tail (DFL, dist2bbox, sigmoid: output0 [b, 84, 8400] f32), postprocess_yolo "
+                         "(decode, conf 0.25, class-aware NMS IoU 0.45)",
+               "input": "uint8 image /255 -> int8",
+               "outputs": "detections (24-byte records [b, 8400], zero after each image's count) + counts"}
     return g, cfg
 
 

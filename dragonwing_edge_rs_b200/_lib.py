@@ -44,6 +44,18 @@ class DwConvDesc(ctypes.Structure):
         "pad_t", "pad_l", "pad_b", "pad_r", "group", "epilogue", "q6")] + [("inv_s_out", ctypes.c_float)]
 
 
+# dw_yolo_flags
+YOLO_ANCHOR_ROWS, YOLO_NMS_AGNOSTIC, YOLO_NO_NMS = 1, 2, 4
+YOLO_MAX_LEVELS = 4
+
+
+class DwYoloDetectDesc(ctypes.Structure):
+    _fields_ = [("n", ctypes.c_int32), ("num_classes", ctypes.c_int32), ("reg_max", ctypes.c_int32),
+                ("num_levels", ctypes.c_int32), ("h", ctypes.c_int32 * YOLO_MAX_LEVELS),
+                ("w", ctypes.c_int32 * YOLO_MAX_LEVELS), ("stride", ctypes.c_float * YOLO_MAX_LEVELS),
+                ("box_scale", ctypes.c_float * YOLO_MAX_LEVELS), ("cls_scale", ctypes.c_float * YOLO_MAX_LEVELS)]
+
+
 # Every exported function with its argument types (restype is dw_status unless listed).
 vp, sz, i32, u32, f32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_float
 PDESC = ctypes.POINTER(DwConvDesc)
@@ -114,6 +126,11 @@ SIGNATURES = {
     "dw_cast_f16_to_f32": ([vp, vp, vp], i32),
     "dw_unfold_w_f32_to_f16": ([vp, vp, vp] + [sz] * 9, i32),
     "dw_im2col_u8_to_i8": ([vp, vp, vp] + [sz] * 13 + [f32], i32),
+    # YOLOv8 Detect tail and post-processing
+    "dw_prepare_yolo_detect": ([vp, ctypes.POINTER(DwYoloDetectDesc), PVP], i32),
+    "dw_yolo_detect_i8": ([vp, ctypes.POINTER(DwYoloDetectDesc), vp, PVP, PVP, vp], i32),
+    "dw_postprocess_yolo_workspace": ([sz, sz], sz),
+    "dw_postprocess_yolo": ([vp, vp, sz, sz, sz, u32, u32, f32, f32, ctypes.c_int32, vp, vp, vp], i32),
 }
 
 _lib = None

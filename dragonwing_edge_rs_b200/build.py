@@ -25,7 +25,7 @@ LIB = os.path.join(PKG, "libdragonwing_cuda.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
     "-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
-    "-Xcompiler", "-fPIC,-fvisibility=hidden,-O2",
+    "-Xcompiler", "-fPIC,-fvisibility=hidden,-O2,-ffp-contract=off",
     "-Xptxas", "-v",
     "-I" + INCLUDE, "-I" + CSRC,
 ]

@@ -46,7 +46,8 @@ class TensorInfo:
 class CompiledOp:
     """builder.rs:204 CompiledOp.  op_type values used here:
     Conv2dRequantReluI8Nhwc (fused conv), AddQuantized, MaxPool, Concat, Split,
-    Resize, QuantizeU8, Dequantize."""
+    Resize, QuantizeU8, Dequantize, YoloDetect (the Detect head's tail),
+    YoloPostprocess (postprocess_yolo), and the fp16 ops."""
 
     name: str
     op_type: str
@@ -525,15 +526,25 @@ def mobilenetv2_block(batch=32, h=112, w=112, c=96, expand=6, seed=2):
     return b.g
 
 
-def yolov8n(batch=1, size=640, nc=80, reg_max=16, seed=8, width=0.25, depth=0.33):
+# postprocess_yolo's usual arguments (postprocess.rs:313-314): 0.25 / 0.45, for a 640x640 image
+YOLO_POSTPROCESS = {"img_width": 640, "img_height": 640, "conf_threshold": 0.25, "iou_threshold": 0.45}
+
+
+def yolov8n(batch=1, size=640, nc=80, reg_max=16, seed=8, width=0.25, depth=0.33, head="detections"):
     """YOLOv8n-architecture INT8 graph (BASELINE config 4): width 0.25, depth 0.33;
     CSPDarknet backbone of Conv(+folded BN)+SiLU layers and C2f blocks, SPPF with
     5x5 max pooling, PAN neck with nearest 2x upsampling and channel concat, and
     the decoupled detection head (box branch 4*reg_max channels, class branch nc
     channels) at strides 8/16/32.  The graph input is the uint8 image, normalised
-    by 1/255 and quantised (QuantizeU8); the six head outputs are dequantised to
-    f32.  Tensors joined by a concat share one activation scale, so the concat
-    moves bytes unchanged (the builder passes the scale to their producers)."""
+    by 1/255 and quantised (QuantizeU8).  Tensors joined by a concat share one
+    activation scale, so the concat moves bytes unchanged (the builder passes
+    the scale to their producers).
+
+    head: "raw" ends with the six head outputs dequantised to f32; "detect"
+    adds the exported model's Detect tail (YoloDetect: output0 f32
+    [batch, 4 + nc, 8400]); "detections" also runs postprocess_yolo on the
+    device (YoloPostprocess: `detections` = dw_detection records [batch, 8400],
+    image i's first `num_detections[i]` records its detections, the rest zero)."""
     ch = lambda c: int(round(c * width))  # noqa: E731
     rep = lambda n: max(round(n * depth), 1)  # noqa: E731
     b = GraphBuilder(seed, act_scale_range=(0.01, 0.1))
@@ -595,16 +606,37 @@ def yolov8n(batch=1, size=640, nc=80, reg_max=16, seed=8, width=0.25, depth=0.33
 
     c_box = max(16, ch(256) // 4, reg_max * 4)
     c_cls = max(ch(256), min(nc, 100))
-    for i, t in enumerate((out3, out4, out5)):
+    heads = []
+    for t in (out3, out4, out5):
         r = conv(conv(t, c_box, 3), c_box, 3)
         r = conv(r, 4 * reg_max, k=1, act="none")
         c = conv(conv(t, c_cls, 3), c_cls, 3)
         c = conv(c, nc, k=1, act="none")
-        for name, tq in ((f"box{i}", r), (f"cls{i}", c)):
-            ti = b.g.tensors[tq]
-            out = b.g.add_tensor(name, ti.shape, "f32", None)
-            b.g.ops.append(CompiledOp(f"dequantize_{name}", "Dequantize", [tq], [out], {"scale": ti.scale}))
-            b.output(out)
+        heads.append((r, c))
+    if head == "raw":
+        for i, (r, c) in enumerate(heads):
+            for name, tq in ((f"box{i}", r), (f"cls{i}", c)):
+                ti = b.g.tensors[tq]
+                out = b.g.add_tensor(name, ti.shape, "f32", None)
+                b.g.ops.append(CompiledOp(f"dequantize_{name}", "Dequantize", [tq], [out], {"scale": ti.scale}))
+                b.output(out)
+        return b.g
+    # the exported model's Detect tail: DFL, dist2bbox x stride, sigmoid, concat
+    anchors = sum(b.g.tensors[r].shape[1] * b.g.tensors[r].shape[2] for r, _ in heads)
+    out0 = b.g.add_tensor("output0", (batch, 4 + nc, anchors), "f32", None)
+    b.g.ops.append(CompiledOp("detect", "YoloDetect", [t for pair in heads for t in pair], [out0], {
+        "nc": nc, "reg_max": reg_max, "strides": [8.0, 16.0, 32.0],
+        "box_scales": [b.g.tensors[r].scale for r, _ in heads],
+        "cls_scales": [b.g.tensors[c].scale for _, c in heads]}))
+    if head == "detect":
+        b.output(out0)
+        return b.g
+    dets = b.g.add_tensor("detections", (batch, anchors, ops.DETECTION_DTYPE.itemsize), "u8", None)
+    cnt = b.g.add_tensor("num_detections", (batch,), "i32", None)
+    b.g.ops.append(CompiledOp("postprocess", "YoloPostprocess", [out0], [dets, cnt],
+                              dict(YOLO_POSTPROCESS, nc=nc, num_detections=anchors, flags=0)))
+    b.output(dets)
+    b.output(cnt)
     return b.g
 
 
@@ -685,6 +717,26 @@ class CudaGraphRuntime:
             x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
             s = op.params["scale"]
             return lambda: ops.dequantize_i8_packed_to_f32(be, x, y, s)
+        if t == "YoloDetect":
+            pr = op.params
+            n = self.graph.tensors[op.inputs[0]].shape[0]
+            grids = [tuple(self.graph.tensors[x].shape[1:3]) for x in op.inputs[0::2]]
+            desc = ops.YoloDetectDesc(n, pr["nc"], grids, pr["strides"], pr["box_scales"], pr["cls_scales"],
+                                      pr["reg_max"])
+            tables = ops.prepare_yolo_detect(be, desc)
+            consts[op.name + "_tables"] = tables
+            boxes, clss = [bufs[x] for x in op.inputs[0::2]], [bufs[x] for x in op.inputs[1::2]]
+            y = bufs[op.outputs[0]]
+            return lambda: ops.yolo_detect_i8(be, desc, tables, boxes, clss, y)
+        if t == "YoloPostprocess":
+            pr = op.params
+            n, A = self.graph.tensors[op.inputs[0]].shape[0], pr["num_detections"]
+            ws = be.alloc(ops.postprocess_yolo_workspace(n, A))
+            consts[op.name + "_workspace"] = ws
+            x, dets, cnt = bufs[op.inputs[0]], bufs[op.outputs[0]], bufs[op.outputs[1]]
+            return lambda: ops.postprocess_yolo_device(be, x, n, pr["nc"], A, pr["img_width"], pr["img_height"],
+                                                       pr["conf_threshold"], pr["iou_threshold"], pr["flags"], ws,
+                                                       dets, cnt)
         # ---- fp16 path
         if t == "CastF32ToF16":
             x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]

@@ -14,6 +14,8 @@ from __future__ import annotations
 import ctypes
 from dataclasses import dataclass
 
+import numpy as np
+
 from . import _lib as L
 from .backend import CudaBackend, CudaBuffer
 
@@ -267,3 +269,100 @@ def im2col_u8_to_i8(backend, x, y, n, h, w, c, k_h, k_w, s_h, s_w, p_t, p_l, h_o
     """im2col of a uint8 image fused with its quantisation (contract in include/dw_cuda.h)."""
     backend._check(L.load().dw_im2col_u8_to_i8(backend.handle, x.handle, y.handle, n, h, w, c, k_h, k_w, s_h, s_w,
                                                p_t, p_l, h_out, w_out, c_dst, float(scale)))
+
+
+# ---------------------------------------------------------------------------
+# YOLOv8 Detect tail and detection post-processing
+# (crates/dragonwing-onnx/src/postprocess.rs)
+# ---------------------------------------------------------------------------
+
+YOLO_ANCHOR_ROWS, YOLO_NMS_AGNOSTIC, YOLO_NO_NMS = L.YOLO_ANCHOR_ROWS, L.YOLO_NMS_AGNOSTIC, L.YOLO_NO_NMS
+
+# Detection (postprocess.rs:12-19): bbox [x1, y1, x2, y2], class_id, confidence.
+DETECTION_DTYPE = np.dtype([("bbox", "<f4", (4,)), ("class_id", "<u4"), ("confidence", "<f4")])
+
+
+@dataclass
+class YoloDetectDesc:
+    """The Detect head after its last convolutions: per level the (h, w) grid,
+    the stride and the dequantisation scales of the int8 box tensor
+    [n, h, w, 4*reg_max] and class tensor [n, h, w, num_classes]."""
+
+    n: int
+    num_classes: int
+    grids: list
+    strides: list
+    box_scales: list
+    cls_scales: list
+    reg_max: int = 16
+
+    @property
+    def anchors(self) -> int:
+        return sum(h * w for h, w in self.grids)
+
+    def to_c(self) -> L.DwYoloDetectDesc:
+        d = L.DwYoloDetectDesc()
+        d.n, d.num_classes, d.reg_max, d.num_levels = self.n, self.num_classes, self.reg_max, len(self.grids)
+        for i, (h, w) in enumerate(self.grids):
+            d.h[i], d.w[i] = h, w
+            d.stride[i], d.box_scale[i], d.cls_scale[i] = self.strides[i], self.box_scales[i], self.cls_scales[i]
+        return d
+
+
+def prepare_yolo_detect(backend: CudaBackend, desc: YoloDetectDesc) -> CudaBuffer:
+    """The sigmoid and softmax tables of the head (once per model)."""
+    out = ctypes.c_void_p()
+    d = desc.to_c()
+    backend._check(L.load().dw_prepare_yolo_detect(backend.handle, ctypes.byref(d), ctypes.byref(out)))
+    return CudaBuffer(backend, out, L.load().dw_buf_len(out))
+
+
+def yolo_detect_i8(backend: CudaBackend, desc: YoloDetectDesc, tables: CudaBuffer, boxes, clss, out: CudaBuffer):
+    """int8 box/class head outputs -> the model output f32 [n, 4 + nc, anchors]."""
+    d = desc.to_c()
+    nb = len(boxes)
+    bx = (ctypes.c_void_p * nb)(*[b.handle.value for b in boxes])
+    cx = (ctypes.c_void_p * nb)(*[b.handle.value for b in clss])
+    backend._check(L.load().dw_yolo_detect_i8(backend.handle, ctypes.byref(d), tables.handle,
+                                              ctypes.cast(bx, L.PVP), ctypes.cast(cx, L.PVP), out.handle))
+
+
+def postprocess_yolo_workspace(n: int, num_detections: int) -> int:
+    return int(L.load().dw_postprocess_yolo_workspace(n, num_detections))
+
+
+def postprocess_yolo_device(backend: CudaBackend, raw: CudaBuffer, n: int, num_classes: int, num_detections: int,
+                            img_width: int, img_height: int, conf_threshold: float, iou_threshold: float,
+                            flags: int, workspace, dets: CudaBuffer, counts: CudaBuffer):
+    """postprocess_yolo for n images, results left on the device: image i's
+    detections are dets[i*num_detections : i*num_detections + counts[i]]."""
+    backend._check(L.load().dw_postprocess_yolo(backend.handle, raw.handle, n, num_classes, num_detections,
+                                                img_width, img_height, float(conf_threshold),
+                                                float(iou_threshold), flags, _h(workspace), _h(dets),
+                                                counts.handle))
+
+
+def detections_from_host(dets: np.ndarray, counts: np.ndarray, num_detections: int) -> list:
+    """Splits the device layout (read back) into one Detection array per image."""
+    recs = np.frombuffer(np.ascontiguousarray(dets).tobytes(), DETECTION_DTYPE)
+    return [recs[i * num_detections:i * num_detections + int(c)].copy() for i, c in enumerate(counts)]
+
+
+def postprocess_yolo(backend: CudaBackend, raw: CudaBuffer, n: int, num_classes: int, num_detections: int,
+                     img_width: int, img_height: int, conf_threshold: float, iou_threshold: float,
+                     flags: int = 0) -> list:
+    """postprocess_yolo (postprocess.rs:319-340) on a device-resident model
+    output: returns, per image, its detections as a DETECTION_DTYPE array in
+    the reference's order."""
+    counts = backend.alloc(4 * n)
+    dets = backend.alloc(n * num_detections * DETECTION_DTYPE.itemsize) if num_detections else None
+    try:
+        postprocess_yolo_device(backend, raw, n, num_classes, num_detections, img_width, img_height,
+                                conf_threshold, iou_threshold, flags, None, dets, counts)
+        cnt = backend.download_array(counts, np.int32)
+        raw_d = backend.download_array(dets, np.uint8) if dets is not None else np.zeros(0, np.uint8)
+    finally:
+        counts.free()
+        if dets is not None:
+            dets.free()
+    return detections_from_host(raw_d, cnt, num_detections)

@@ -282,6 +282,75 @@ DW_API dw_status dw_resize_nearest_i8(dw_backend *be, const dw_buf *x, dw_buf *y
                                       size_t w_in, size_t h_out, size_t w_out, size_t c);
 
 /* ---------------------------------------------------------------------- */
+/* YOLOv8 Detect head tail and detection post-processing                   */
+/* ---------------------------------------------------------------------- */
+
+#define DW_YOLO_MAX_LEVELS 4
+
+/* The Detect head of an exported YOLOv8 model after its last box and class
+ * convolutions.  Level l has a box tensor int8 NHWC [n, h[l], w[l], 4*reg_max]
+ * (dequantisation scale box_scale[l]) and a class tensor int8 NHWC
+ * [n, h[l], w[l], num_classes] (cls_scale[l]); stride[l] = input pixels per
+ * grid cell.  reg_max must be 16. */
+typedef struct dw_yolo_detect_desc {
+    int32_t n, num_classes, reg_max, num_levels;
+    int32_t h[DW_YOLO_MAX_LEVELS], w[DW_YOLO_MAX_LEVELS];
+    float stride[DW_YOLO_MAX_LEVELS], box_scale[DW_YOLO_MAX_LEVELS], cls_scale[DW_YOLO_MAX_LEVELS];
+} dw_yolo_detect_desc;
+
+/* Builds the tables dw_yolo_detect_i8 reads (once per model: per level, the
+ * 256 sigmoid values of the class levels and the 256 x 256 softmax terms
+ * exp(x_i - max) of the box levels, from the host's libm expf, the function
+ * the reference's f32::exp calls).  *tables is a new buffer owned by the caller. */
+DW_API dw_status dw_prepare_yolo_detect(dw_backend *be, const dw_yolo_detect_desc *d, dw_buf **tables);
+
+/* The tail the reference runs as f32 graph ops after DequantizeLinear
+ * (Softmax ops.rs:1609-1640, the DFL Conv ops.rs:1356-1420, Sub/Add/Div/Mul
+ * runtime.rs:1674-1850, Sigmoid ops.rs:1865-1870, Concat), fused:
+ * out f32 [n, 4 + num_classes, A], A = sum h[l]*w[l] anchors, level by level,
+ * row-major in each level.  Rows 0-3: box centre x, y, width, height in input
+ * pixels (DFL expectation over 16 bins per side, distances around the cell
+ * centre, times the stride); rows 4..: sigmoid class scores.  box[l], cls[l]
+ * are arrays of num_levels buffers.  Bit-identical with the reference's ops. */
+DW_API dw_status dw_yolo_detect_i8(dw_backend *be, const dw_yolo_detect_desc *d, const dw_buf *tables,
+                                   const dw_buf *const *box, const dw_buf *const *cls, dw_buf *out_f32);
+
+/* One detection, the layout of postprocess.rs:12-19 (24 bytes). */
+typedef struct dw_detection {
+    float bbox[4]; /* x1, y1, x2, y2 in image pixels */
+    uint32_t class_id;
+    float confidence;
+} dw_detection;
+
+enum dw_yolo_flags {
+    DW_YOLO_ANCHOR_ROWS = 1,  /* raw is [n, A, 4 + nc] (decode_detections_v8_alt, postprocess.rs:151) */
+    DW_YOLO_NMS_AGNOSTIC = 2, /* nms_agnostic (postprocess.rs:270) instead of nms */
+    DW_YOLO_NO_NMS = 4        /* decode_detections_v8 alone: candidates in anchor order */
+};
+
+/* Device bytes of the workspace dw_postprocess_yolo needs for n images of
+ * num_detections anchors. */
+DW_API size_t dw_postprocess_yolo_workspace(size_t n, size_t num_detections);
+
+/* postprocess_yolo (crates/dragonwing-onnx/src/postprocess.rs:319-340) for each
+ * of n images: decode_detections_v8 (:78-146; model size 640, best class by
+ * strict '>' from 0, skipped when best < conf_threshold, corners scaled and
+ * clamped) then nms (:227-265: stable sort by confidence, greedy same-class
+ * suppression when IoU > iou_threshold, then the swap_remove deletion, whose
+ * output order is reproduced).  raw: f32 [n, 4 + num_classes, num_detections]
+ * on the device (the model output).  dets: dw_detection [n, num_detections];
+ * image i's detections are dets[i*num_detections .. + counts[i]), the records
+ * after them are zero.  counts:
+ * int32 [n] (raw and dets may be NULL when num_detections is 0).  workspace: at least
+ * dw_postprocess_yolo_workspace bytes, or NULL to use the backend's scratch
+ * (which may grow, so pass one when capturing a CUDA graph).
+ * num_detections <= 16384. */
+DW_API dw_status dw_postprocess_yolo(dw_backend *be, const dw_buf *raw, size_t n, size_t num_classes,
+                                     size_t num_detections, uint32_t img_width, uint32_t img_height,
+                                     float conf_threshold, float iou_threshold, int32_t flags, dw_buf *workspace,
+                                     dw_buf *dets, dw_buf *counts);
+
+/* ---------------------------------------------------------------------- */
 /* FP16 path (binary16 buffers, f32 accumulation)                           */
 /* ---------------------------------------------------------------------- */
 /* Conversions follow F16::from_f32 / F16::to_f32 (crates/dragonwing-core/src/

@@ -646,3 +646,202 @@ void dwref_quantize_u8_to_i8(int8_t *out, const uint8_t *in, size_t len, float s
     float inv255 = 1.0f / 255.0f, inv_scale = 1.0f / scale;
     for (size_t i = 0; i < len; i++) out[i] = dwref_f32_to_i8(((float)in[i] * inv255) * inv_scale);
 }
+
+/* ------------------------------------------------------------------------ */
+/* YOLOv8 Detect head tail (the f32 graph ops after DequantizeLinear)         */
+/* ------------------------------------------------------------------------ */
+
+/* softmax_f32 on one row (crates/dragonwing-cpu/src/ops.rs:1609-1640):
+ * max by fold(-inf, f32::max), exp(x - max) summed in order, times 1/sum. */
+static void softmax_row(float *out, const float *in, size_t n) {
+    float max_val = -INFINITY;
+    for (size_t i = 0; i < n; i++) max_val = fmaxf(max_val, in[i]);
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; i++) {
+        float e = expf(in[i] - max_val);
+        out[i] = e;
+        sum += e;
+    }
+    float inv_sum = 1.0f / sum;
+    for (size_t i = 0; i < n; i++) out[i] *= inv_sum;
+}
+
+/* sigmoid_f32_scalar (ops.rs:1865-1870). */
+static float sigmoid_one(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+void dwref_sigmoid_f32(float *y, const float *x, size_t len) {
+    for (size_t i = 0; i < len; i++) y[i] = sigmoid_one(x[i]);
+}
+
+/* softmax_f32 (ops.rs:1609-1640) over rows of n. */
+void dwref_softmax_f32(float *out, const float *in, size_t len, size_t n) {
+    for (size_t r = 0; r + n <= len; r += n) softmax_row(out + r, in + r, n);
+}
+
+/* The exported YOLOv8 Detect tail on dequantised head outputs, per image and
+ * level: DFL = softmax over reg_max bins per box side, then the 1x1 conv with
+ * kernel [0, 1, ..., reg_max-1] (conv2d_f32_nhwc's sum from 0.0 in channel
+ * order, ops.rs:1396-1415); dist2bbox: x1y1 = anchor - lt, x2y2 = anchor + rb,
+ * centre = (x1y1 + x2y2) / 2, size = x2y2 - x1y1 (Sub/Add/Div, runtime.rs:
+ * 1736-1850), times the stride (Mul); class scores = sigmoid; concat along
+ * anchors.  Anchors are the cell centres (x + 0.5, y + 0.5), row-major.
+ * box[l]: int8 [n, h, w, 4*reg_max]; cls[l]: int8 [n, h, w, nc];
+ * out: f32 [n, 4 + nc, A]. */
+void dwref_yolo_detect_i8(float *out, const int8_t *const *box, const int8_t *const *cls,
+                          const dwref_yolo_desc *d) {
+    size_t A = 0;
+    for (int l = 0; l < d->num_levels; l++) A += (size_t)d->h[l] * d->w[l];
+    const size_t R = (size_t)d->reg_max, nc = (size_t)d->num_classes, rows = 4 + nc;
+    float x[64], p[64];
+    for (int img = 0; img < d->n; img++) {
+        size_t off = 0;
+        for (int l = 0; l < d->num_levels; l++) {
+            const size_t hw = (size_t)d->h[l] * d->w[l];
+            for (size_t local = 0; local < hw; local++) {
+                const size_t pix = (size_t)img * hw + local, a = off + local;
+                const int8_t *bq = box[l] + pix * 4 * R;
+                float dist[4];
+                for (int s = 0; s < 4; s++) {
+                    for (size_t i = 0; i < R; i++) x[i] = (float)bq[s * R + i] * d->box_scale[l];
+                    softmax_row(p, x, R);
+                    float acc = 0.0f;
+                    for (size_t i = 0; i < R; i++) acc += p[i] * (float)i;
+                    dist[s] = acc;
+                }
+                const float ax = (float)(local % (size_t)d->w[l]) + 0.5f;
+                const float ay = (float)(local / (size_t)d->w[l]) + 0.5f;
+                const float x1 = ax - dist[0], y1 = ay - dist[1], x2 = ax + dist[2], y2 = ay + dist[3];
+                const float st = d->stride[l];
+                float *o = out + (size_t)img * rows * A + a;
+                o[0] = ((x1 + x2) / 2.0f) * st;
+                o[A] = ((y1 + y2) / 2.0f) * st;
+                o[2 * A] = (x2 - x1) * st;
+                o[3 * A] = (y2 - y1) * st;
+                const int8_t *cq = cls[l] + pix * nc;
+                for (size_t c = 0; c < nc; c++) o[(4 + c) * A] = sigmoid_one((float)cq[c] * d->cls_scale[l]);
+            }
+            off += hw;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Detection post-processing (crates/dragonwing-onnx/src/postprocess.rs)      */
+/* ------------------------------------------------------------------------ */
+
+/* Detection::area (postprocess.rs:28-32). */
+float dwref_det_area(const dwref_detection *d) {
+    float w = fmaxf(d->bbox[2] - d->bbox[0], 0.0f);
+    float h = fmaxf(d->bbox[3] - d->bbox[1], 0.0f);
+    return w * h;
+}
+
+/* iou (postprocess.rs:36-55). */
+float dwref_iou(const dwref_detection *a, const dwref_detection *b) {
+    float x1 = fmaxf(a->bbox[0], b->bbox[0]);
+    float y1 = fmaxf(a->bbox[1], b->bbox[1]);
+    float x2 = fminf(a->bbox[2], b->bbox[2]);
+    float y2 = fminf(a->bbox[3], b->bbox[3]);
+    float inter_w = fmaxf(x2 - x1, 0.0f);
+    float inter_h = fmaxf(y2 - y1, 0.0f);
+    float inter_area = inter_w * inter_h;
+    float union_area = dwref_det_area(a) + dwref_det_area(b) - inter_area;
+    return union_area > 0.0f ? inter_area / union_area : 0.0f;
+}
+
+/* decode_detections_v8 (postprocess.rs:78-146; raw [4 + nc, A]) or, with alt,
+ * decode_detections_v8_alt (:151-208; raw [A, 4 + nc]).  Writes at most
+ * num_detections detections in anchor order; returns their count (0 when
+ * raw_len is short, :92-95). */
+size_t dwref_decode_detections_v8(dwref_detection *out, const float *raw, size_t raw_len, size_t num_classes,
+                                  size_t num_detections, uint32_t img_width, uint32_t img_height,
+                                  float conf_threshold, int alt) {
+    const size_t row = 4 + num_classes;
+    if (raw_len < row * num_detections) return 0;
+    const float model_size = 640.0f;
+    const float scale_x = (float)img_width / model_size, scale_y = (float)img_height / model_size;
+    const float iw = (float)img_width, ih = (float)img_height;
+    size_t n = 0;
+    for (size_t a = 0; a < num_detections; a++) {
+        const size_t step = alt ? 1 : num_detections;
+        const float *q = alt ? raw + a * row : raw + a;
+        float cx = q[0], cy = q[step], w = q[2 * step], h = q[3 * step];
+        size_t best_class = 0;
+        float best_conf = 0.0f;
+        for (size_t c = 0; c < num_classes; c++) {
+            float conf = q[(4 + c) * step];
+            if (conf > best_conf) {
+                best_conf = conf;
+                best_class = c;
+            }
+        }
+        if (best_conf < conf_threshold) continue;
+        float x1 = (cx - w / 2.0f) * scale_x, y1 = (cy - h / 2.0f) * scale_y;
+        float x2 = (cx + w / 2.0f) * scale_x, y2 = (cy + h / 2.0f) * scale_y;
+        dwref_detection *o = &out[n++];
+        o->bbox[0] = fminf(fmaxf(x1, 0.0f), iw);
+        o->bbox[1] = fminf(fmaxf(y1, 0.0f), ih);
+        o->bbox[2] = fminf(fmaxf(x2, 0.0f), iw);
+        o->bbox[3] = fminf(fmaxf(y2, 0.0f), ih);
+        o->class_id = (uint32_t)best_class;
+        o->confidence = best_conf;
+    }
+    return n;
+}
+
+/* Stable merge sort by confidence descending: Vec::sort_by with
+ * b.confidence.partial_cmp(&a.confidence) (postprocess.rs:229-231). */
+static void sort_by_conf_desc(dwref_detection *d, dwref_detection *tmp, size_t n) {
+    for (size_t width = 1; width < n; width *= 2) {
+        for (size_t lo = 0; lo < n; lo += 2 * width) {
+            size_t mid = lo + width < n ? lo + width : n, hi = lo + 2 * width < n ? lo + 2 * width : n;
+            size_t i = lo, j = mid, k = lo;
+            while (i < mid && j < hi) tmp[k++] = d[j].confidence > d[i].confidence ? d[j++] : d[i++];
+            while (i < mid) tmp[k++] = d[i++];
+            while (j < hi) tmp[k++] = d[j++];
+        }
+        memcpy(d, tmp, n * sizeof(*d));
+    }
+}
+
+/* nms (postprocess.rs:227-265) or, with agnostic, nms_agnostic (:270-300), in
+ * place: sort, greedy suppression when iou > iou_threshold, then the
+ * swap_remove deletion from the back.  Returns the new length. */
+size_t dwref_nms(dwref_detection *d, size_t n, float iou_threshold, int agnostic) {
+    if (n == 0) return 0;
+    dwref_detection *tmp = (dwref_detection *)malloc(n * sizeof(*d));
+    unsigned char *keep = (unsigned char *)malloc(n);
+    sort_by_conf_desc(d, tmp, n);
+    memset(keep, 1, n);
+    for (size_t i = 0; i < n; i++) {
+        if (!keep[i]) continue;
+        for (size_t j = i + 1; j < n; j++) {
+            if (!keep[j]) continue;
+            if (!agnostic && d[i].class_id != d[j].class_id) continue;
+            if (dwref_iou(&d[i], &d[j]) > iou_threshold) keep[j] = 0;
+        }
+    }
+    size_t len = n;
+    for (size_t i = n; i > 0;) {
+        i--;
+        if (!keep[i]) {
+            d[i] = d[len - 1]; /* Vec::swap_remove(i) */
+            len--;
+        }
+    }
+    free(tmp);
+    free(keep);
+    return len;
+}
+
+/* postprocess_yolo (postprocess.rs:319-340) on one image; out has room for
+ * num_detections entries.  flags as the device API: 1 alt layout, 2 agnostic
+ * NMS, 4 no NMS. */
+size_t dwref_postprocess_yolo(dwref_detection *out, const float *raw, size_t raw_len, size_t num_classes,
+                              size_t num_detections, uint32_t img_width, uint32_t img_height,
+                              float conf_threshold, float iou_threshold, int flags) {
+    size_t n = dwref_decode_detections_v8(out, raw, raw_len, num_classes, num_detections, img_width, img_height,
+                                          conf_threshold, flags & 1);
+    if (flags & 4) return n;
+    return dwref_nms(out, n, iou_threshold, (flags & 2) != 0);
+}

@@ -116,6 +116,31 @@ void dwref_maxpool_f16_nhwc(uint16_t *y, const uint16_t *x, size_t n, size_t h, 
                             size_t k_h, size_t k_w, size_t s_h, size_t s_w,
                             size_t p_t, size_t p_l, size_t p_b, size_t p_r);
 
+/* ---- YOLOv8 Detect tail and post-processing (crates/dragonwing-onnx/src/postprocess.rs) ---- */
+typedef struct dwref_yolo_desc { /* same fields as dw_yolo_detect_desc */
+    int32_t n, num_classes, reg_max, num_levels;
+    int32_t h[4], w[4];
+    float stride[4], box_scale[4], cls_scale[4];
+} dwref_yolo_desc;
+typedef struct dwref_detection { /* postprocess.rs:12-19 */
+    float bbox[4];
+    uint32_t class_id;
+    float confidence;
+} dwref_detection;
+void dwref_sigmoid_f32(float *y, const float *x, size_t len);
+void dwref_softmax_f32(float *out, const float *in, size_t len, size_t n);
+void dwref_yolo_detect_i8(float *out, const int8_t *const *box, const int8_t *const *cls,
+                          const dwref_yolo_desc *d);
+float dwref_det_area(const dwref_detection *d);
+float dwref_iou(const dwref_detection *a, const dwref_detection *b);
+size_t dwref_decode_detections_v8(dwref_detection *out, const float *raw, size_t raw_len, size_t num_classes,
+                                  size_t num_detections, uint32_t img_width, uint32_t img_height,
+                                  float conf_threshold, int alt);
+size_t dwref_nms(dwref_detection *d, size_t n, float iou_threshold, int agnostic);
+size_t dwref_postprocess_yolo(dwref_detection *out, const float *raw, size_t raw_len, size_t num_classes,
+                              size_t num_detections, uint32_t img_width, uint32_t img_height,
+                              float conf_threshold, float iou_threshold, int flags);
+
 int dwref_num_cpus(void);
 
 #ifdef __cplusplus

@@ -29,6 +29,18 @@ class ConvDesc(ctypes.Structure):
         "pad_t", "pad_l", "pad_b", "pad_r", "group", "epilogue", "q6")] + [("inv_s_out", ctypes.c_float)]
 
 
+class YoloDesc(ctypes.Structure):
+    """Same field meaning as ``dw_yolo_detect_desc`` in include/dw_cuda.h."""
+
+    _fields_ = [("n", ctypes.c_int32), ("num_classes", ctypes.c_int32), ("reg_max", ctypes.c_int32),
+                ("num_levels", ctypes.c_int32), ("h", ctypes.c_int32 * 4), ("w", ctypes.c_int32 * 4),
+                ("stride", ctypes.c_float * 4), ("box_scale", ctypes.c_float * 4), ("cls_scale", ctypes.c_float * 4)]
+
+
+# Detection (crates/dragonwing-onnx/src/postprocess.rs:12-19)
+DETECTION_DTYPE = np.dtype([("bbox", "<f4", (4,)), ("class_id", "<u4"), ("confidence", "<f4")])
+
+
 def build() -> str:
     """Compile the oracle with its Makefile (gcc only; seconds)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
@@ -82,6 +94,9 @@ def _declare(L):
         "dwref_gap_f16": [vp, vp, sz, sz, sz, sz],
         "dwref_maxpool_f16_nhwc": [vp, vp] + [sz] * 12,
     }
+    sig["dwref_yolo_detect_i8"] = [vp, vp, vp, ctypes.POINTER(YoloDesc)]
+    sig["dwref_sigmoid_f32"] = [vp, vp, sz]
+    sig["dwref_softmax_f32"] = [vp, vp, sz, sz]
     for name, args in sig.items():
         fn = getattr(L, name)
         fn.argtypes = args
@@ -102,6 +117,16 @@ def _declare(L):
     L.dwref_f16_from_f32.restype = ctypes.c_uint16
     L.dwref_f16_to_f32.argtypes = [ctypes.c_uint16]
     L.dwref_f16_to_f32.restype = f32
+    L.dwref_det_area.argtypes = [vp]
+    L.dwref_det_area.restype = f32
+    L.dwref_iou.argtypes = [vp, vp]
+    L.dwref_iou.restype = f32
+    L.dwref_decode_detections_v8.argtypes = [vp, vp, sz, sz, sz, ctypes.c_uint32, ctypes.c_uint32, f32, i32]
+    L.dwref_decode_detections_v8.restype = sz
+    L.dwref_nms.argtypes = [vp, sz, f32, i32]
+    L.dwref_nms.restype = sz
+    L.dwref_postprocess_yolo.argtypes = [vp, vp, sz, sz, sz, ctypes.c_uint32, ctypes.c_uint32, f32, f32, i32]
+    L.dwref_postprocess_yolo.restype = sz
     L.dwref_num_cpus.argtypes = []
     L.dwref_num_cpus.restype = ctypes.c_int
 
@@ -384,3 +409,86 @@ def maxpool_f16(x, n, h, w, c, k_h, k_w, s_h, s_w, pads=(0, 0, 0, 0)):
     y = np.empty(n * ho * wo * c, np.uint16)
     lib().dwref_maxpool_f16_nhwc(_p(y), _p(x), n, h, w, c, k_h, k_w, s_h, s_w, pt, pl, pb, pr)
     return y
+
+
+# ---- YOLOv8 Detect tail and post-processing (crates/dragonwing-onnx/src/postprocess.rs) ----
+
+def sigmoid_f32(x):
+    """sigmoid_f32_scalar (crates/dragonwing-cpu/src/ops.rs:1865-1870)."""
+    x = _c(x, np.float32)
+    y = np.empty_like(x)
+    lib().dwref_sigmoid_f32(_p(y), _p(x), x.size)
+    return y
+
+
+def softmax_f32(x, n):
+    """softmax_f32 (ops.rs:1609-1640) along rows of n."""
+    x = _c(x, np.float32)
+    y = np.empty_like(x)
+    lib().dwref_softmax_f32(_p(y), _p(x), x.size, n)
+    return y
+
+
+def yolo_detect_i8(boxes, clss, strides, box_scales, cls_scales, reg_max=16):
+    """The Detect head's f32 tail on int8 head outputs (dwref_yolo_detect_i8):
+    boxes[l] int8 [n, h, w, 4*reg_max], clss[l] int8 [n, h, w, nc] -> f32 [n, 4 + nc, A]."""
+    boxes = [_c(b, np.int8) for b in boxes]
+    clss = [_c(c, np.int8) for c in clss]
+    n, nc = boxes[0].shape[0], clss[0].shape[3]
+    d = YoloDesc()
+    d.n, d.num_classes, d.reg_max, d.num_levels = n, nc, reg_max, len(boxes)
+    A = 0
+    for i, b in enumerate(boxes):
+        d.h[i], d.w[i] = b.shape[1], b.shape[2]
+        d.stride[i], d.box_scale[i], d.cls_scale[i] = strides[i], box_scales[i], cls_scales[i]
+        A += b.shape[1] * b.shape[2]
+    out = np.empty((n, 4 + nc, A), np.float32)
+    bp = (ctypes.c_void_p * len(boxes))(*[b.ctypes.data for b in boxes])
+    cp = (ctypes.c_void_p * len(clss))(*[c.ctypes.data for c in clss])
+    lib().dwref_yolo_detect_i8(_p(out), ctypes.cast(bp, ctypes.c_void_p), ctypes.cast(cp, ctypes.c_void_p),
+                               ctypes.byref(d))
+    return out
+
+
+def detections(rows) -> np.ndarray:
+    """[(bbox4, class_id, confidence), ...] -> DETECTION_DTYPE array."""
+    return np.array([(tuple(b), c, f) for b, c, f in rows], DETECTION_DTYPE)
+
+
+def det_area(det) -> float:
+    """Detection::area (postprocess.rs:28-32)."""
+    d = np.ascontiguousarray(np.array(det, DETECTION_DTYPE).reshape(1))
+    return float(lib().dwref_det_area(_p(d)))
+
+
+def iou(a, b) -> float:
+    """iou (postprocess.rs:36-55)."""
+    da = np.ascontiguousarray(np.array(a, DETECTION_DTYPE).reshape(1))
+    db = np.ascontiguousarray(np.array(b, DETECTION_DTYPE).reshape(1))
+    return float(lib().dwref_iou(_p(da), _p(db)))
+
+
+def decode_detections_v8(raw, num_classes, num_detections, img_width, img_height, conf_threshold, alt=False):
+    """decode_detections_v8 (postprocess.rs:78-146) / _alt (:151-208) on one image."""
+    raw = _c(raw, np.float32).reshape(-1)
+    out = np.zeros(max(1, num_detections), DETECTION_DTYPE)
+    k = lib().dwref_decode_detections_v8(_p(out), _p(raw), raw.size, num_classes, num_detections, img_width,
+                                         img_height, conf_threshold, 1 if alt else 0)
+    return out[:k].copy()
+
+
+def nms(dets, iou_threshold, agnostic=False):
+    """nms (postprocess.rs:227-265) / nms_agnostic (:270-300): returns the kept list in the reference's order."""
+    d = np.ascontiguousarray(np.array(dets, DETECTION_DTYPE).reshape(-1)).copy()
+    k = lib().dwref_nms(_p(d), d.size, iou_threshold, 1 if agnostic else 0)
+    return d[:k].copy()
+
+
+def postprocess_yolo(raw, num_classes, num_detections, img_width, img_height, conf_threshold, iou_threshold,
+                     flags=0):
+    """postprocess_yolo (postprocess.rs:319-340) on one image (flags: 1 alt layout, 2 agnostic, 4 no NMS)."""
+    raw = _c(raw, np.float32).reshape(-1)
+    out = np.zeros(max(1, num_detections), DETECTION_DTYPE)
+    k = lib().dwref_postprocess_yolo(_p(out), _p(raw), raw.size, num_classes, num_detections, img_width,
+                                     img_height, conf_threshold, iou_threshold, flags)
+    return out[:k].copy()

@@ -7,7 +7,10 @@ conv2d_i8_nhwc / requantize / relu (crates/dragonwing-cpu/src/ops.rs:3086-3142,
 3366-3386, 3301-3319), AddQuantized to add_i8 (ops.rs:3176-3209), MaxPool to
 maxpool2d (ops.rs:1513-1551), Concat/Split to concat_f32/split_f32 on int8
 bytes (ops.rs:2141-2246, 2407), Resize to resize_f32 Nearest (ops.rs:2320-2348),
-QuantizeU8 to u8*(1/255) -> quantize_f32_to_i8 (ops.rs:3503-3525).
+QuantizeU8 to u8*(1/255) -> quantize_f32_to_i8 (ops.rs:3503-3525),
+YoloDetect to the exported Detect tail's f32 ops (softmax_f32, the DFL conv,
+Sub/Add/Div/Mul, sigmoid_f32_scalar; dwref_yolo_detect_i8), YoloPostprocess to
+postprocess_yolo (crates/dragonwing-onnx/src/postprocess.rs:319-340).
 
 UnfoldF32ToF16 (a device lowering of the input conv, see
 dragonwing_edge_rs_b200.graph.lower_unfold_stem_f16) is the input conversion
@@ -86,6 +89,13 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
         elif t == "Dequantize":
             x = vals[op.inputs[0]]
             vals[op.outputs[0]] = dwref.dequantize_i8_to_f32(x, op.params["scale"]).reshape(x.shape)
+        elif t == "YoloDetect":
+            pr = op.params
+            boxes, clss = [vals[x] for x in op.inputs[0::2]], [vals[x] for x in op.inputs[1::2]]
+            vals[op.outputs[0]] = dwref.yolo_detect_i8(boxes, clss, pr["strides"], pr["box_scales"],
+                                                       pr["cls_scales"], pr["reg_max"])
+        elif t == "YoloPostprocess":
+            vals[op.outputs[0]], vals[op.outputs[1]] = postprocess_op(op, vals[op.inputs[0]])
         elif t == "CastF32ToF16":
             x = vals[op.inputs[0]]
             vals[op.outputs[0]] = dwref.f16_from_f32_array(x).reshape(x.shape)
@@ -123,6 +133,22 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
         else:
             raise ValueError(f"unsupported op {t}")
     return {name: vals[name] for name in graph.outputs}
+
+
+def postprocess_op(op, raw):
+    """YoloPostprocess: postprocess_yolo per image, laid out as the device op
+    leaves it (records [n, A]; the first counts[i] of image i are its
+    detections, the rest zero)."""
+    pr = op.params
+    n, A = raw.shape[0], pr["num_detections"]
+    dets = np.zeros((n, A), dwref.DETECTION_DTYPE)
+    cnt = np.zeros(n, np.int32)
+    for i in range(n):
+        d = dwref.postprocess_yolo(raw[i], pr["nc"], A, pr["img_width"], pr["img_height"], pr["conf_threshold"],
+                                   pr["iou_threshold"], pr["flags"])
+        dets[i, :len(d)] = d
+        cnt[i] = len(d)
+    return dets.view(np.uint8).reshape(n, A, dwref.DETECTION_DTYPE.itemsize), cnt
 
 
 def conv_f16_op(graph, op, x, threads=1, relu=None):

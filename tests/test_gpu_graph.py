@@ -35,10 +35,12 @@ def test_mobilenetv2_block_small_batch(be):
     rt.release()
 
 
-def test_yolov8n_int8_batch1_bit_exact(be):
-    """BASELINE config 4 architecture at 640x640, batch 1: all six head outputs
-    (dequantised int8) identical to the oracle graph run."""
-    g = G.yolov8n(batch=1, seed=8)
+@pytest.mark.parametrize("head", ["raw", "detect", "detections"])
+def test_yolov8n_int8_batch1_bit_exact(be, head):
+    """BASELINE config 4 architecture at 640x640, batch 1, identical to the
+    oracle graph run: the six head outputs (dequantised int8), the Detect
+    tail's output0, or the post-processed detections and their counts."""
+    g = G.yolov8n(batch=1, seed=8, head=head)
     img = np.random.default_rng(5).integers(0, 256, g.tensors["image"].nbytes).astype(np.uint8)
     rt = G.CudaGraphRuntime(g, be)
     rt.set_input_bytes("image", img)
