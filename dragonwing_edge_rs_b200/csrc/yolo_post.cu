@@ -150,15 +150,18 @@ __global__ void __launch_bounds__(kDetThreads) k_yolo_detect(const DetectParams 
 //            radix sort by confidence descending (= the reference's stable
 //            sort_by), stable radix sort of that order by class (one segment
 //            per class, rank order inside it), class-ordered boxes staged
-//   nms      one CTA per (image, class segment): the greedy loop
+//   nms      the greedy loop per class segment: segments of up to 64
+//            candidates one warp each; larger ones taken from a work queue by
+//            persistent 512-thread CTAs, in batches of 128 candidates
 //   order    one CTA per image: the reference's swap_remove order, records out
 // ---------------------------------------------------------------------------
 
 constexpr int kRankThreads = 1024;
 constexpr int kSegThreads = 512;
 constexpr int kSegWarps = kSegThreads / 32;
-constexpr int kBoxCap = 2560;  // segment boxes staged in shared memory (50 KB with their areas)
+constexpr int kBoxCap = 4096;  // segment staged in shared memory: boxes, spans, lists, flags (100 KB)
 constexpr int kSmallSeg = 64;  // segments up to this size: one warp each
+constexpr int kHugeSeg = 1024; // segments over this size are taken first
 
 // Workspace, per image of A anchors (by anchor unless noted).
 struct PostWs {
@@ -175,6 +178,9 @@ struct PostWs {
     uint16_t *list1;
     uint32_t *cnt;    // [n] candidates
     uint32_t *nseg;   // [n] class segments
+    uint32_t *qhuge;  // [n * qcap] (image << 16 | segment) of segments over kHugeSeg candidates
+    uint32_t *qbig;   // [n * qcap] of segments over kSmallSeg candidates (and up to kHugeSeg)
+    uint32_t *qcnt;   // [4] items in qhuge, in qbig; items taken from each
 };
 
 struct DecodeParams {
@@ -338,23 +344,25 @@ __global__ void __launch_bounds__(kRankThreads, 1) k_yolo_rank(const RankParams 
     const size_t base = (size_t)img * A;
 
     // candidates in anchor order (the order decode_detections_v8 pushes them)
-    const int E = (A + kRankThreads - 1) / kRankThreads;
-    const int a0 = tid * E;
-    int local = 0;
-    for (int i = 0; i < E; i++) {
-        const int a = a0 + i;
-        if (a < A && p.w.flag[base + a]) local++;
-    }
+    // thread t owns anchors [16t, 16t + 16) (A <= 16384); all its loads are
+    // issued before any is used
+    const int a0 = tid * 16;
+    uint32_t fl = 0;
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+        if (a0 + i < A && p.w.flag[base + a0 + i]) fl |= 1u << i;
+    float cf[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) cf[i] = ((fl >> i) & 1u) ? p.w.conf[base + a0 + i] : 0.0f;
     int c;
-    int pos = block_excl_scan(local, wsum, &c);
-    for (int i = 0; i < E; i++) {
-        const int a = a0 + i;
-        if (a < A && p.w.flag[base + a]) {
-            ka[pos] = ~__float_as_uint(p.w.conf[base + a]);  // conf >= +0, never NaN: ascending = descending conf
-            va[pos] = (uint16_t)a;
+    int pos = block_excl_scan(__popc(fl), wsum, &c);
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+        if ((fl >> i) & 1u) {
+            ka[pos] = ~__float_as_uint(cf[i]);  // conf >= +0, never NaN: ascending = descending conf
+            va[pos] = (uint16_t)(a0 + i);
             pos++;
         }
-    }
     __syncthreads();
     if (p.sort_conf && c > 1)
         for (int sh = 0; sh < 32; sh += 8)
@@ -369,9 +377,21 @@ __global__ void __launch_bounds__(kRankThreads, 1) k_yolo_rank(const RankParams 
         return;
     }
     // class grouping: keys = class (0 for agnostic), payload = rank
-    for (int r = tid; r < c; r += kRankThreads) {
-        kb[r] = p.group ? p.w.cls[base + va[r]] : 0u;
-        vb[r] = (uint16_t)r;
+    {
+        uint32_t cl[kMaxAnchors / kRankThreads];
+#pragma unroll
+        for (int t = 0; t < kMaxAnchors / kRankThreads; t++) {
+            const int r = tid + t * kRankThreads;
+            cl[t] = (p.group && r < c) ? p.w.cls[base + va[r]] : 0u;
+        }
+#pragma unroll
+        for (int t = 0; t < kMaxAnchors / kRankThreads; t++) {
+            const int r = tid + t * kRankThreads;
+            if (r < c) {
+                kb[r] = cl[t];
+                vb[r] = (uint16_t)r;
+            }
+        }
     }
     __syncthreads();
     {
@@ -387,15 +407,26 @@ __global__ void __launch_bounds__(kRankThreads, 1) k_yolo_rank(const RankParams 
     // class-grouped ranks and boxes (the rank -> anchor map was stored above;
     // the barrier inside the sort or below makes it visible to the block)
     __syncthreads();
-    for (int k = tid; k < c; k += kRankThreads) {
-        const int r = va[k];
-        p.w.crank[base + k] = (uint16_t)r;
-        p.w.cbox[base + k] = p.w.box[base + p.w.ra[base + r]];
+    {
+        uint16_t an[kMaxAnchors / kRankThreads];
+#pragma unroll
+        for (int t = 0; t < kMaxAnchors / kRankThreads; t++) {
+            const int k = tid + t * kRankThreads;
+            an[t] = k < c ? p.w.ra[base + va[k]] : 0;
+        }
+#pragma unroll
+        for (int t = 0; t < kMaxAnchors / kRankThreads; t++) {
+            const int k = tid + t * kRankThreads;
+            if (k < c) {
+                p.w.crank[base + k] = va[k];
+                p.w.cbox[base + k] = p.w.box[base + an[t]];
+            }
+        }
     }
     // segment starts in order
     const int E2 = (c + kRankThreads - 1) / kRankThreads;
     const int k0 = tid * E2;
-    local = 0;
+    int local = 0;
     for (int i = 0; i < E2; i++) {
         const int k = k0 + i;
         if (k < c && (k == 0 || ka[k] != ka[k - 1])) local++;
@@ -411,17 +442,28 @@ __global__ void __launch_bounds__(kRankThreads, 1) k_yolo_rank(const RankParams 
         seg[nseg] = (uint32_t)c;
         p.w.nseg[img] = (uint32_t)nseg;
     }
+    __syncthreads();
+    // large segments go to the work queues of k_yolo_nms_segment
+    for (int i = tid; i < nseg; i += kRankThreads) {
+        const int m = (int)(seg[i + 1] - seg[i]);
+        if (m > kHugeSeg)
+            p.w.qhuge[atomicAdd(&p.w.qcnt[0], 1u)] = ((uint32_t)img << 16) | (uint32_t)i;
+        else if (m > kSmallSeg)
+            p.w.qbig[atomicAdd(&p.w.qcnt[1], 1u)] = ((uint32_t)img << 16) | (uint32_t)i;
+    }
 }
 
 struct SegNmsParams {
     int A, cap;     // cap: boxes staged in shared memory per segment
+    float gx, gy;   // grid cells per pixel (kGrid / image size; 0 disables the grid)
     double mid;     // halfway between the IoU threshold t and the next float above it
     bool tie_up;    // that next float has an even significand (an exact tie rounds up to it)
     bool zero_gt;   // 0.0 > t (the IoU of a pair whose union is not positive)
     PostWs w;
 };
 
-constexpr int kBatch = 32;  // candidates resolved together
+constexpr int kBatch = 32;     // candidates resolved together by one warp (small segments)
+constexpr int kBigBatch = 128; // by a block (large segments)
 
 // iou(a, b) > t (postprocess.rs:36-55, 251) without the division: the
 // reference compares q' = RN(inter / union) with t.  For union > 0, q' > t
@@ -442,6 +484,21 @@ __device__ __forceinline__ bool iou_gt(const SegNmsParams &p, float4 a, float ar
     return lhs > rhs || (lhs == rhs && p.tie_up);
 }
 
+constexpr int kGrid = 16;  // cells per image side for the overlap prefilter
+
+// The cells [xl, xh] x [yl, yh] a box's interior can touch, packed in bytes.
+// Cell of x = floor(x * gx); the ends use round-down / round-up products, so
+// the span always contains the cells of the box's points, and two boxes with
+// a common interior point have intersecting spans (a necessary condition for
+// a positive intersection, hence for IoU > t when t >= 0).
+__device__ __forceinline__ uint32_t box_span(const SegNmsParams &p, float4 b) {
+    const int xl = min(max((int)floorf(__fmul_rd(b.x, p.gx)), 0), kGrid - 1);
+    const int xh = min(max((int)floorf(__fmul_ru(b.z, p.gx)), 0), kGrid - 1);
+    const int yl = min(max((int)floorf(__fmul_rd(b.y, p.gy)), 0), kGrid - 1);
+    const int yh = min(max((int)floorf(__fmul_ru(b.w, p.gy)), 0), kGrid - 1);
+    return (uint32_t)xl | ((uint32_t)xh << 8) | ((uint32_t)yl << 16) | ((uint32_t)yh << 24);
+}
+
 // Exclusive prefix sum over a kSegThreads block (every thread calls it).
 __device__ int seg_excl_scan(int v, int *wsum, int *total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -460,119 +517,231 @@ __device__ int seg_excl_scan(int v, int *wsum, int *total) {
     return incl - v + before;
 }
 
-// nms (postprocess.rs:233-255) on one class segment, in batches.  The live
-// list holds, in rank order, the candidates no kept box has suppressed yet.
-// Its first (up to) 32 entries are resolved in order: each is kept unless an
-// earlier kept entry of the batch overlaps it by IoU > threshold (the boxes
-// kept in earlier batches have already removed everything they suppress);
-// the 32 x 32 overlap bits are computed in parallel, the order resolved on
-// bit masks.  Then the threads test the rest of the list (round-robin) against
-// the batch's kept boxes and the survivors are compacted, in order, into the
-// next list.  The kept set equals the reference's sequential greedy loop.
+// Spans (box_span) that share a cell in both directions.
+__device__ __forceinline__ bool spans_meet(uint32_t a, uint32_t b) {
+    return (a & 255u) <= ((b >> 8) & 255u) && (b & 255u) <= ((a >> 8) & 255u) &&
+           ((a >> 16) & 255u) <= (b >> 24) && ((b >> 16) & 255u) <= (a >> 24);
+}
+
+// nms (postprocess.rs:233-255) on the class segments of more than kSmallSeg
+// candidates, taken from the work queues by persistent CTAs.  A segment is
+// processed in batches.  The live list holds, in rank order, the candidates no
+// kept box has suppressed yet.  Its first (up to) 128 entries are resolved in
+// order: each is kept unless an earlier kept entry of the batch overlaps it by
+// IoU > threshold (the boxes kept in earlier batches have already removed
+// everything they suppress); the 128 x 128 overlap bits are computed in
+// parallel (pairs whose grid cells do not meet are skipped) and the order is
+// resolved on bit masks.  Then the threads test the rest of the list
+// (round-robin) against the batch's kept boxes whose grid cells meet its own
+// and the survivors are compacted, in order, into the next list.  The kept set
+// equals the reference's sequential greedy loop.
 __global__ void __launch_bounds__(kSegThreads) k_yolo_nms_segment(const SegNmsParams p) {
     extern __shared__ __align__(16) unsigned char smraw[];
-    float4 *sb = reinterpret_cast<float4 *>(smraw);  // [cap] staged boxes
-    float *sa = reinterpret_cast<float *>(sb + p.cap);  // [cap] their areas
-    __shared__ float4 bb[kBatch], kbx[kBatch];
-    __shared__ float ba[kBatch], kar[kBatch];
-    __shared__ uint32_t sup[kBatch];
-    __shared__ uint32_t s_kept;
+    float4 *sb = reinterpret_cast<float4 *>(smraw);           // [cap] staged boxes
+    uint32_t *ss = reinterpret_cast<uint32_t *>(sb + p.cap);     // [cap] cell spans
+    uint16_t *sl = reinterpret_cast<uint16_t *>(ss + p.cap);     // [2 * cap] live lists
+    uint8_t *sk = reinterpret_cast<uint8_t *>(sl + 2 * p.cap);   // [cap] kept flags
+    __shared__ float4 bb[kBigBatch];
+    __shared__ float ba[kBigBatch];
+    __shared__ uint32_t bs[kBigBatch];
+    __shared__ unsigned long long sup[2][kBigBatch];  // earlier batch entries overlapping entry b (128 bits)
+    __shared__ unsigned long long s_kept[2];
+    __shared__ __align__(16) unsigned colw[kGrid][4], roww[kGrid][4];  // kept entries touching each column / row
     __shared__ int wsum[kSegThreads / 32];
     __shared__ uint32_t smask[32 * kSegWarps];  // survivor ballots per (round, warp)
     __shared__ int soff[32 * kSegWarps];
-    const int img = blockIdx.y, si = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (si >= (int)p.w.nseg[img]) return;
-    const size_t base = (size_t)img * p.A;
-    const uint32_t *seg = p.w.seg + (size_t)img * (p.A + 1);
-    const int s = (int)seg[si], m = (int)seg[si + 1] - s;
-    if (m <= kSmallSeg) return;  // k_yolo_nms_small's
-    const float4 *gb = p.w.cbox + base + s;
-    const uint16_t *cr = p.w.crank + base + s;
-    uint16_t *cur = p.w.list0 + base + s, *nxt = p.w.list1 + base + s;
-    const bool staged = m <= p.cap;
-    for (int j = tid; j < m; j += kSegThreads) {
-        if (staged) {
-            const float4 b = gb[j];
-            sb[j] = b;
-            sa[j] = area_ref(b);
-        }
-        cur[j] = (uint16_t)j;
-        p.w.keep[base + cr[j]] = 0;
-    }
-    __syncthreads();
-    int len = m;
-    while (len > 0) {
-        const int nb = min(kBatch, len);
-        if (tid < nb) {
-            const int q = cur[tid];
-            const float4 b = staged ? sb[q] : gb[q];
-            bb[tid] = b;
-            ba[tid] = staged ? sa[q] : area_ref(b);
-            sup[tid] = 0;
+    __shared__ int s_item;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (;;) {
+        // next segment: the huge ones first
+        if (tid == 0) {
+            int it = -1;
+            const uint32_t h = atomicAdd(&p.w.qcnt[2], 1u);
+            if (h < p.w.qcnt[0]) {
+                it = (int)p.w.qhuge[h];
+            } else {
+                const uint32_t g = atomicAdd(&p.w.qcnt[3], 1u);
+                if (g < p.w.qcnt[1]) it = (int)p.w.qbig[g];
+            }
+            s_item = it;
         }
         __syncthreads();
-        for (int pr = tid; pr < kBatch * kBatch; pr += kSegThreads) {
-            const int a = pr >> 5, b = pr & 31;
-            if (a < b && b < nb && iou_gt(p, bb[a], ba[a], bb[b], ba[b])) atomicOr(&sup[b], 1u << a);
+        const int item = s_item;
+        if (item < 0) return;
+        const int img = item >> 16, si = item & 0xFFFF;
+        const size_t base = (size_t)img * p.A;
+        const uint32_t *seg = p.w.seg + (size_t)img * (p.A + 1);
+        const int s = (int)seg[si], m = (int)seg[si + 1] - s;
+        const float4 *gb = p.w.cbox + base + s;
+        const uint16_t *cr = p.w.crank + base + s;
+        const bool staged = m <= p.cap;  // boxes, spans, live lists and flags on chip
+        uint16_t *cur = staged ? sl : p.w.list0 + base + s, *nxt = staged ? sl + p.cap : p.w.list1 + base + s;
+        for (int j = tid; j < m; j += kSegThreads) {
+            if (staged) {
+                const float4 b = gb[j];
+                sb[j] = b;
+                ss[j] = box_span(p, b);
+                sk[j] = 0;
+            } else {
+                p.w.keep[base + cr[j]] = 0;
+            }
+            cur[j] = (uint16_t)j;
         }
         __syncthreads();
-        if (tid < 32) {
-            const uint32_t mine = tid < nb ? sup[tid] : 0u;
-            uint32_t K = 0;
-            for (int b = 0; b < nb; b++)
-                if (!(__shfl_sync(0xffffffffu, mine, b) & K)) K |= 1u << b;
-            if (tid == 0) s_kept = K;
-        }
-        __syncthreads();
-        const uint32_t K = s_kept;
-        const int nk = __popc(K);
-        if (tid < nb && ((K >> tid) & 1u)) {
-            const int slot = __popc(K & ((1u << tid) - 1));
-            kbx[slot] = bb[tid];
-            kar[slot] = ba[tid];
-            p.w.keep[base + cr[cur[tid]]] = 1;
-        }
-        __syncthreads();
-        // the rest of the list, round-robin over the threads (round r, thread t:
-        // entry nb + r*kSegThreads + t); survivors compacted in (round, warp,
-        // lane) = list order
-        const int rest = len - nb;
-        const int R = (rest + kSegThreads - 1) / kSegThreads;  // <= 32 (len <= 16384)
-        for (int r = 0; r < R; r++) {
-            const int idx = nb + r * kSegThreads + tid;
-            bool ok = false;
-            if (idx < len) {
-                const int j = cur[idx];
-                const float4 bj = staged ? sb[j] : gb[j];
-                const float aj = staged ? sa[j] : area_ref(bj);
-                ok = true;
-                for (int k = 0; k < nk && ok; k += 4) {
-                    const bool s0 = iou_gt(p, kbx[k], kar[k], bj, aj);
-                    const bool s1 = k + 1 < nk && iou_gt(p, kbx[k + 1], kar[k + 1], bj, aj);
-                    const bool s2 = k + 2 < nk && iou_gt(p, kbx[k + 2], kar[k + 2], bj, aj);
-                    const bool s3 = k + 3 < nk && iou_gt(p, kbx[k + 3], kar[k + 3], bj, aj);
-                    ok = !(s0 || s1 || s2 || s3);
+        int len = m;
+        while (len > 0) {
+            const int nb = min(kBigBatch, len);
+            if (tid < nb) {
+                const int q = cur[tid];
+                const float4 b = staged ? sb[q] : gb[q];
+                bb[tid] = b;
+                ba[tid] = area_ref(b);
+                bs[tid] = staged ? ss[q] : box_span(p, b);
+                sup[0][tid] = 0;
+                sup[1][tid] = 0;
+            }
+            __syncthreads();
+            {   // overlap bits: 4 threads per entry b, each over every 4th earlier entry a
+                const int b = tid & (kBigBatch - 1), q = tid >> 7;
+                unsigned long long m0 = 0, m1 = 0;
+                if (b < nb) {
+                    const float4 bx = bb[b];
+                    const float ax = ba[b];
+                    const uint32_t sx = bs[b];
+                    for (int a = q; a < b; a += kSegThreads / kBigBatch)
+                        if ((p.zero_gt || spans_meet(bs[a], sx)) && iou_gt(p, bb[a], ba[a], bx, ax)) {
+                            if (a < 64)
+                                m0 |= 1ull << a;
+                            else
+                                m1 |= 1ull << (a - 64);
+                        }
+                    if (m0) atomicOr(&sup[0][b], m0);
+                    if (m1) atomicOr(&sup[1][b], m1);
                 }
             }
-            const unsigned bal = __ballot_sync(0xffffffffu, ok);
-            if (lane == 0) smask[r * kSegWarps + warp] = bal;
+            __syncthreads();
+            // resolve the batch's order: entry b is kept unless a kept earlier entry
+            // overlaps it.  Warp 0 settles, each round, every entry whose earlier
+            // overlapping entries are all settled (the lowest unsettled one always
+            // is, so at most nb rounds); lane l owns entries l, l+32, l+64, l+96.
+            if (warp == 0) {
+                unsigned long long d0[4], d1[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int bi = lane + 32 * e;
+                    d0[e] = bi < nb ? sup[0][bi] : 0ull;
+                    d1[e] = bi < nb ? sup[1][bi] : 0ull;
+                }
+                const unsigned long long all0 = nb >= 64 ? ~0ull : ((1ull << nb) - 1);
+                const unsigned long long all1 = nb <= 64 ? 0ull : (nb == 128 ? ~0ull : ((1ull << (nb - 64)) - 1));
+                unsigned long long R0 = 0, R1 = 0, K0 = 0, K1 = 0;
+                unsigned settled = 0, kept = 0;  // bit e: entry lane + 32e
+                for (int round = 0; round < kBigBatch && ((R0 & all0) != all0 || (R1 & all1) != all1); round++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int bi = lane + 32 * e;
+                        if (bi < nb && !((settled >> e) & 1u) && !(d0[e] & ~R0) && !(d1[e] & ~R1)) {
+                            settled |= 1u << e;
+                            if (!((d0[e] & K0) | (d1[e] & K1))) kept |= 1u << e;
+                        }
+                    }
+                    const unsigned s0 = __ballot_sync(0xffffffffu, settled & 1u), s1 = __ballot_sync(0xffffffffu, settled & 2u);
+                    const unsigned s2 = __ballot_sync(0xffffffffu, settled & 4u), s3 = __ballot_sync(0xffffffffu, settled & 8u);
+                    const unsigned k0 = __ballot_sync(0xffffffffu, kept & 1u), k1 = __ballot_sync(0xffffffffu, kept & 2u);
+                    const unsigned k2 = __ballot_sync(0xffffffffu, kept & 4u), k3 = __ballot_sync(0xffffffffu, kept & 8u);
+                    R0 = (unsigned long long)s0 | ((unsigned long long)s1 << 32);
+                    R1 = (unsigned long long)s2 | ((unsigned long long)s3 << 32);
+                    K0 = (unsigned long long)k0 | ((unsigned long long)k1 << 32);
+                    K1 = (unsigned long long)k2 | ((unsigned long long)k3 << 32);
+                }
+                if (lane == 0) {
+                    s_kept[0] = K0;
+                    s_kept[1] = K1;
+                }
+            }
+            __syncthreads();
+            const unsigned long long K0 = s_kept[0], K1 = s_kept[1];
+            // kept boxes stay at their batch index; per grid column / row, which
+            // of them touch it (128 bits as 4 words, word w = entries 32w..32w+31)
+            if (tid < kBigBatch) {
+                const bool kb = tid < nb && (((tid < 64 ? K0 : K1) >> (tid & 63)) & 1ull);
+                if (kb) {
+                    if (staged)
+                        sk[cur[tid]] = 1;
+                    else
+                        p.w.keep[base + cr[cur[tid]]] = 1;
+                }
+                const uint32_t sp = bs[tid];
+#pragma unroll
+                for (int c = 0; c < kGrid; c++) {
+                    const unsigned cb = __ballot_sync(0xffffffffu, kb && (int)(sp & 255u) <= c && c <= (int)((sp >> 8) & 255u));
+                    const unsigned rb = __ballot_sync(0xffffffffu, kb && (int)((sp >> 16) & 255u) <= c && c <= (int)(sp >> 24));
+                    if (lane == 0) {
+                        colw[c][warp] = cb;
+                        roww[c][warp] = rb;
+                    }
+                }
+            }
+            __syncthreads();
+            // the rest of the list, round-robin over the threads (round r, thread
+            // t: entry nb + r*kSegThreads + t); survivors compacted in (round,
+            // warp, lane) = list order
+            const int rest = len - nb;
+            const int R = (rest + kSegThreads - 1) / kSegThreads;  // <= 32 (len <= 16384)
+            for (int r = 0; r < R; r++) {
+                const int idx = nb + r * kSegThreads + tid;
+                bool ok = false;
+                if (idx < len && !p.zero_gt) {  // zero_gt (t < 0): every pair suppresses
+                    const int j = cur[idx];
+                    const float4 bj = staged ? sb[j] : gb[j];
+                    const float aj = area_ref(bj);
+                    const uint32_t sp = staged ? ss[j] : box_span(p, bj);
+                    uint4 cm = make_uint4(0, 0, 0, 0), rm = make_uint4(0, 0, 0, 0);
+                    for (int c = sp & 255u; c <= (int)((sp >> 8) & 255u); c++) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(colw[c]);
+                        cm.x |= v.x; cm.y |= v.y; cm.z |= v.z; cm.w |= v.w;
+                    }
+                    for (int rr = (sp >> 16) & 255u; rr <= (int)(sp >> 24); rr++) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(roww[rr]);
+                        rm.x |= v.x; rm.y |= v.y; rm.z |= v.z; rm.w |= v.w;
+                    }
+                    // kept batch entries that can overlap this box
+                    unsigned cw[4] = {cm.x & rm.x, cm.y & rm.y, cm.z & rm.z, cm.w & rm.w};
+                    ok = true;
+#pragma unroll
+                    for (int w = 0; w < 4; w++) {
+                        unsigned cand = cw[w];
+                        while (cand && ok) {
+                            const int k = 32 * w + __ffs(cand) - 1;
+                            cand &= cand - 1;
+                            ok = !iou_gt(p, bb[k], ba[k], bj, aj);
+                        }
+                    }
+                }
+                const unsigned bal = __ballot_sync(0xffffffffu, ok);
+                if (lane == 0) smask[r * kSegWarps + warp] = bal;
+            }
+            __syncthreads();
+            int total;
+            const int ent = R * kSegWarps;  // <= kSegThreads
+            const int off = seg_excl_scan(tid < ent ? __popc(smask[tid]) : 0, wsum, &total);
+            if (tid < ent) soff[tid] = off;
+            __syncthreads();
+            for (int r = 0; r < R; r++) {
+                const unsigned bal = smask[r * kSegWarps + warp];
+                if ((bal >> lane) & 1u)
+                    nxt[soff[r * kSegWarps + warp] + __popc(bal & ((1u << lane) - 1))] =
+                        cur[nb + r * kSegThreads + tid];
+            }
+            __syncthreads();
+            uint16_t *t = cur;
+            cur = nxt;
+            nxt = t;
+            len = total;
         }
+        if (staged)
+            for (int j = tid; j < m; j += kSegThreads) p.w.keep[base + cr[j]] = sk[j];
         __syncthreads();
-        int total;
-        const int ent = R * kSegWarps;  // <= kSegThreads
-        const int off = seg_excl_scan(tid < ent ? __popc(smask[tid]) : 0, wsum, &total);
-        if (tid < ent) soff[tid] = off;
-        __syncthreads();
-        for (int r = 0; r < R; r++) {
-            const unsigned bal = smask[r * kSegWarps + warp];
-            if ((bal >> lane) & 1u)
-                nxt[soff[r * kSegWarps + warp] + __popc(bal & ((1u << lane) - 1))] = cur[nb + r * kSegThreads + tid];
-        }
-        __syncthreads();
-        uint16_t *t = cur;
-        cur = nxt;
-        nxt = t;
-        len = total;
     }
 }
 
@@ -673,7 +842,19 @@ __global__ void __launch_bounds__(kRankThreads, 1) k_yolo_order(const OrderParam
     const int img = blockIdx.x, tid = threadIdx.x, A = p.A;
     const size_t base = (size_t)img * A;
     const int c = (int)p.w.cnt[img];
-    for (int r = tid; r < c; r += kRankThreads) keep[r] = p.all_kept ? 1 : p.w.keep[base + r];
+    {
+        uint8_t kv[kMaxAnchors / kRankThreads];
+#pragma unroll
+        for (int t = 0; t < kMaxAnchors / kRankThreads; t++) {
+            const int r = tid + t * kRankThreads;
+            kv[t] = r < c ? (p.all_kept ? 1 : p.w.keep[base + r]) : 0;
+        }
+#pragma unroll
+        for (int t = 0; t < kMaxAnchors / kRankThreads; t++) {
+            const int r = tid + t * kRankThreads;
+            if (r < c) keep[r] = kv[t];
+        }
+    }
     __syncthreads();
     const int E = (c + kRankThreads - 1) / kRankThreads;
     const int r0 = tid * E;
@@ -775,11 +956,14 @@ dw_status check_buf(dw_backend *be, const dw_buf *b, size_t expected, const char
 
 size_t ws_part(size_t bytes) { return al256(bytes); }
 
+// segments over kSmallSeg candidates in one image: at most A / (kSmallSeg + 1)
+size_t queue_cap(size_t A) { return A / (kSmallSeg + 1) + 1; }
+
 size_t postprocess_workspace(size_t n, size_t A) {
     const size_t na = n * A;
     return ws_part(16 * na) + ws_part(4 * na) + ws_part(4 * na) + ws_part(na) + ws_part(2 * na) + ws_part(2 * na) +
            ws_part(16 * na) + ws_part(4 * n * (A + 1)) + ws_part(na) + ws_part(2 * na) + ws_part(2 * na) +
-           ws_part(4 * n) + ws_part(4 * n);
+           ws_part(4 * n) + ws_part(4 * n) + 2 * ws_part(4 * n * queue_cap(A)) + ws_part(16);
 }
 
 PostWs carve_workspace(void *p, size_t n, size_t A) {
@@ -804,6 +988,9 @@ PostWs carve_workspace(void *p, size_t n, size_t A) {
     ws.list1 = (uint16_t *)take(2 * na);
     ws.cnt = (uint32_t *)take(4 * n);
     ws.nseg = (uint32_t *)take(4 * n);
+    ws.qhuge = (uint32_t *)take(4 * n * queue_cap(A));
+    ws.qbig = (uint32_t *)take(4 * n * queue_cap(A));
+    ws.qcnt = (uint32_t *)take(16);
     return ws;
 }
 
@@ -948,6 +1135,7 @@ DW_API dw_status dw_postprocess_yolo(dw_backend *be, const dw_buf *raw, size_t n
     const size_t rank_smem = 12 * (size_t)cap + 2 * 256 * 32;
     YT(dw_cuda_check(be, cudaFuncSetAttribute(k_yolo_rank, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rank_smem),
                      "postprocess_yolo: shared memory"));
+    YT(dw_cuda_check(be, cudaMemsetAsync(w.qcnt, 0, 16, be->stream), "postprocess_yolo: queue counters"));
     k_yolo_rank<<<(unsigned)n, kRankThreads, rank_smem, be->stream>>>(rp);
     YT(dw_after_launch(be, "yolo_rank"));
 
@@ -955,6 +1143,8 @@ DW_API dw_status dw_postprocess_yolo(dw_backend *be, const dw_buf *raw, size_t n
         SegNmsParams sp{};
         sp.A = (int)A;
         sp.cap = (int)std::min<size_t>(A, kBoxCap);
+        sp.gx = img_width > 0 ? (float)kGrid / (float)img_width : 0.0f;
+        sp.gy = img_height > 0 ? (float)kGrid / (float)img_height : 0.0f;
         const float tp = std::nextafter(iou_threshold, INFINITY);
         sp.mid = ((double)iou_threshold + (double)tp) * 0.5;  // exact: two adjacent floats
         uint32_t tb;
@@ -963,14 +1153,15 @@ DW_API dw_status dw_postprocess_yolo(dw_backend *be, const dw_buf *raw, size_t n
         sp.zero_gt = 0.0f > iou_threshold;
         sp.w = w;
         const size_t segs = agnostic ? 1 : std::max<size_t>(1, std::min(num_classes, A));
-        const size_t seg_smem = 20 * (size_t)sp.cap;
+        const size_t seg_smem = 25 * (size_t)sp.cap;
         YT(dw_cuda_check(be, cudaFuncSetAttribute(k_yolo_nms_segment, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   (int)seg_smem),
                          "postprocess_yolo: shared memory"));
         k_yolo_nms_small<<<dim3((unsigned)((segs + kSmallWarps - 1) / kSmallWarps), (unsigned)n), kSmallWarps * 32, 0,
                            be->stream>>>(sp);
         YT(dw_after_launch(be, "yolo_nms_small"));
-        k_yolo_nms_segment<<<dim3((unsigned)segs, (unsigned)n), kSegThreads, seg_smem, be->stream>>>(sp);
+        const size_t workers = std::min<size_t>(2 * (size_t)be->sm_count, n * queue_cap(A));
+        k_yolo_nms_segment<<<(unsigned)workers, kSegThreads, seg_smem, be->stream>>>(sp);
         YT(dw_after_launch(be, "yolo_nms_segment"));
     }
 

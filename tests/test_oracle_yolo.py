@@ -263,7 +263,7 @@ def greedy_keep(dets, thr):
     return keep
 
 
-@pytest.mark.parametrize("seed,n,batch,thr", [(0, 10, 32, 0.45), (1, 200, 32, 0.45), (2, 300, 4, 0.3),
+@pytest.mark.parametrize("seed,n,batch,thr", [(0, 10, 32, 0.45), (1, 200, 32, 0.45), (2, 300, 4, 0.3), (6, 400, 64, 0.45), (7, 600, 128, 0.45),
                                               (3, 150, 32, 0.7), (4, 64, 1, 0.45), (5, 257, 32, 0.0)])
 def test_device_batched_nms_rule_equals_greedy(seed, n, batch, thr):
     rng = np.random.default_rng(seed)
