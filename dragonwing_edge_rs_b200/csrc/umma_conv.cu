@@ -1134,6 +1134,10 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         }
         p.num_tiles = p.m_tiles * p.n_tiles;
     };
+    if (const char *e = getenv("DW_UMMA_BN")) {  // tuning override: tile width (a multiple of 16, <= 256)
+        const int v = atoi(e);
+        if (v >= 16 && v <= 256 && v % 16 == 0) p.bn = v;
+    }
     plan_tiles(p.bn, 8);
     // Small problems (tiles for fewer than half the SMs): fewer row blocks per
     // tile, then narrower tiles (down to 64 channels), until half the SMs have a
