@@ -25,6 +25,32 @@ inline int grid_for(const dw_backend *be, size_t work_items) {
 
 __device__ __forceinline__ bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
+// Division of n < 2^31 by a run-time constant d (1 <= d < 2^31), exact and
+// without a divide: a shift for a power of two, else n / d = umulhi(n, m) >> l
+// with l = floor(log2 d) and m = ceil(2^(32+l) / d) (m < 2^32).  The error term
+// n * (m*d - 2^(32+l)) / (d * 2^(32+l)) stays below 1/d because
+// m*d - 2^(32+l) < d < 2^(l+1) and n < 2^31.  The glue kernels index with it in
+// 32 bits (a 64-bit divide costs about a hundred instructions per element).
+struct FastDiv {
+    uint32_t d, m, l, pow2;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f{d, 0u, (uint32_t)(31 - __builtin_clz(d)), (d & (d - 1)) == 0 ? 1u : 0u};
+    if (!f.pow2) f.m = (uint32_t)((((uint64_t)1 << (32 + f.l)) + d - 1) / d);
+    return f;
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
+    return f.pow2 ? (n >> f.l) : (__umulhi(n, f.m) >> f.l);
+}
+
+template <int kVec>
+__device__ __forceinline__ void copy_vec(int8_t *dst, const int8_t *src) {
+    if (kVec == 16) *reinterpret_cast<int4 *>(dst) = *reinterpret_cast<const int4 *>(src);
+    else if (kVec == 8) *reinterpret_cast<int2 *>(dst) = *reinterpret_cast<const int2 *>(src);
+    else if (kVec == 4) *reinterpret_cast<int *>(dst) = *reinterpret_cast<const int *>(src);
+    else *dst = *src;
+}
+
 // --- requantize: ops.rs:3380-3386 -----------------------------------------
 __global__ void k_requantize(const int32_t *__restrict__ in, int8_t *__restrict__ out, size_t n, float s) {
     size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
@@ -352,6 +378,28 @@ __global__ void k_slice_c_i8(const int8_t *__restrict__ x, int8_t *__restrict__ 
     }
 }
 
+// 32-bit-index twins of the copies above (element counts below 2^31).
+template <int kVec>
+__global__ void k_concat_i8_32(ConcatArgs a, uint32_t total, FastDiv fch, int8_t *__restrict__ y) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t p = fdiv(i, fch);
+        const int oc = (int)(i - p * fch.d) * kVec;
+        int s = 0;
+        while (s + 1 < a.count && oc >= a.off[s + 1]) s++;
+        copy_vec<kVec>(y + (size_t)p * a.c_total + oc, a.src[s] + (size_t)p * a.c[s] + (oc - a.off[s]));
+    }
+}
+
+template <int kVec>
+__global__ void k_slice_c_i8_32(const int8_t *__restrict__ x, int8_t *__restrict__ y, uint32_t total, FastDiv fch,
+                                int c_total, int c0, int c_len) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t p = fdiv(i, fch);
+        const int c = (int)(i - p * fch.d) * kVec;
+        copy_vec<kVec>(y + (size_t)p * c_len + c, x + (size_t)p * c_total + c0 + c);
+    }
+}
+
 // --- nearest resize (ops.rs:2320-2348, f32 index arithmetic) -----------------
 __device__ __forceinline__ int nearest_src(int o, float scale, int in_len) {
     float f = roundf(__fsub_rn(__fmul_rn(__fadd_rn((float)o, 0.5f), scale), 0.5f));
@@ -377,6 +425,51 @@ __global__ void k_resize_nearest_i8(const int8_t *__restrict__ x, int8_t *__rest
         else if (vec == 8) *reinterpret_cast<int2 *>(dst) = *reinterpret_cast<const int2 *>(src);
         else if (vec == 4) *reinterpret_cast<int *>(dst) = *reinterpret_cast<const int *>(src);
         else *dst = *src;
+    }
+}
+
+template <int kVec>
+__global__ void k_resize_nearest_i8_32(const int8_t *__restrict__ x, int8_t *__restrict__ y, int hi, int wi, int c,
+                                       float sh, float sw, uint32_t total, FastDiv fch, FastDiv fwo, FastDiv fho) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t p = fdiv(i, fch);
+        const int ch = (int)(i - p * fch.d) * kVec;
+        const uint32_t t = fdiv(p, fwo);
+        const int ow = (int)(p - t * fwo.d);
+        const uint32_t b = fdiv(t, fho);
+        const int oh = (int)(t - b * fho.d);
+        const int ih = nearest_src(oh, sh, hi), iw = nearest_src(ow, sw, wi);
+        copy_vec<kVec>(y + (size_t)p * c + ch, x + (((size_t)b * hi + ih) * wi + iw) * c + ch);
+    }
+}
+
+// maxpool on 16 channels per thread (c % 16 == 0), the window clipped to the
+// image once (padding taps are skipped, as in k_maxpool_i8; an empty window
+// leaves -128).
+__global__ void k_maxpool_i8_v16(const int8_t *__restrict__ x, int8_t *__restrict__ y, int h, int w, int c, int kh,
+                                 int kw, int sh, int sw, int pt, int pl, uint32_t total, FastDiv fcg, FastDiv fwo,
+                                 FastDiv fho) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t p = fdiv(i, fcg);
+        const int g = (int)(i - p * fcg.d);
+        const uint32_t t = fdiv(p, fwo);
+        const int ow = (int)(p - t * fwo.d);
+        const uint32_t b = fdiv(t, fho);
+        const int oh = (int)(t - b * fho.d);
+        const int h0 = oh * sh - pt, w0 = ow * sw - pl;
+        const int a0 = max(0, -h0), a1 = min(kh, h - h0), q0 = max(0, -w0), q1 = min(kw, w - w0);
+        uint4 m = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+        for (int a = a0; a < a1; a++) {
+            const int8_t *row = x + (((size_t)b * h + (h0 + a)) * w + w0) * c + g * 16;
+            for (int q = q0; q < q1; q++) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row + (size_t)q * c));
+                m.x = __vmaxs4(m.x, v.x);
+                m.y = __vmaxs4(m.y, v.y);
+                m.z = __vmaxs4(m.z, v.z);
+                m.w = __vmaxs4(m.w, v.w);
+            }
+        }
+        *reinterpret_cast<uint4 *>(y + (size_t)p * c + g * 16) = m;
     }
 }
 
@@ -493,6 +586,13 @@ dw_status launch_dequantize(dw_backend *be, const int8_t *in, float *out, size_t
 
 dw_status launch_maxpool_i8(dw_backend *be, const int8_t *x, int8_t *y, int n, int h, int w, int c, int kh, int kw,
                             int sh, int sw, int pt, int pl, int ho, int wo) {
+    const size_t groups16 = (size_t)n * ho * wo * (c / 16);
+    if (c % 16 == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)y % 16) == 0 && groups16 < (1u << 31)) {
+        k_maxpool_i8_v16<<<grid_for(be, groups16), kThreads, 0, be->stream>>>(
+            x, y, h, w, c, kh, kw, sh, sw, pt, pl, (uint32_t)groups16, make_fastdiv((uint32_t)(c / 16)),
+            make_fastdiv((uint32_t)wo), make_fastdiv((uint32_t)ho));
+        return dw_after_launch(be, "maxpool_i8");
+    }
     int vec = (c % 4 == 0 && ((uintptr_t)x % 4) == 0 && ((uintptr_t)y % 4) == 0) ? 4 : 1;
     size_t items = (size_t)n * ho * wo * (c / vec);
     k_maxpool_i8<<<grid_for(be, items), kThreads, 0, be->stream>>>(x, y, n, h, w, c, kh, kw, sh, sw, pt, pl, ho, wo,
@@ -526,6 +626,14 @@ dw_status launch_concat_i8(dw_backend *be, const int8_t *const *xs, const int32_
     }
     if (vec == 2) vec = 1;
     size_t items = pixels * (off / vec);
+    if (items < (1u << 31) && (vec == 16 || vec == 4)) {
+        const FastDiv fch = make_fastdiv((uint32_t)(off / vec));
+        if (vec == 16)
+            k_concat_i8_32<16><<<grid_for(be, items), kThreads, 0, be->stream>>>(a, (uint32_t)items, fch, y);
+        else
+            k_concat_i8_32<4><<<grid_for(be, items), kThreads, 0, be->stream>>>(a, (uint32_t)items, fch, y);
+        return dw_after_launch(be, "concat_i8");
+    }
     k_concat_i8<<<grid_for(be, items), kThreads, 0, be->stream>>>(a, pixels, y, vec);
     return dw_after_launch(be, "concat_i8");
 }
@@ -540,8 +648,18 @@ dw_status launch_slice_c_i8(dw_backend *be, const int8_t *x, int8_t *y, size_t p
         if (vec == 4) { vec = 1; break; }
     }
     if (vec == 2) vec = 1;
-    k_slice_c_i8<<<grid_for(be, pixels * (c_len / vec)), kThreads, 0, be->stream>>>(x, y, pixels, c_total, c0, c_len,
-                                                                                     vec);
+    const size_t items = pixels * (c_len / vec);
+    if (items < (1u << 31) && (vec == 16 || vec == 4)) {
+        const FastDiv fch = make_fastdiv((uint32_t)(c_len / vec));
+        if (vec == 16)
+            k_slice_c_i8_32<16><<<grid_for(be, items), kThreads, 0, be->stream>>>(x, y, (uint32_t)items, fch, c_total,
+                                                                                  c0, c_len);
+        else
+            k_slice_c_i8_32<4><<<grid_for(be, items), kThreads, 0, be->stream>>>(x, y, (uint32_t)items, fch, c_total,
+                                                                                 c0, c_len);
+        return dw_after_launch(be, "slice_c_i8");
+    }
+    k_slice_c_i8<<<grid_for(be, items), kThreads, 0, be->stream>>>(x, y, pixels, c_total, c0, c_len, vec);
     return dw_after_launch(be, "slice_c_i8");
 }
 
@@ -552,6 +670,12 @@ dw_status launch_resize_nearest_i8(dw_backend *be, const int8_t *x, int8_t *y, i
     if (vec == 2) vec = 1;
     float sh = (float)hi / (float)ho, sw = (float)wi / (float)wo;  // ops.rs:2334-2335
     size_t items = (size_t)n * ho * wo * (c / vec);
+    if (items < (1u << 31) && vec == 16) {
+        k_resize_nearest_i8_32<16><<<grid_for(be, items), kThreads, 0, be->stream>>>(
+            x, y, hi, wi, c, sh, sw, (uint32_t)items, make_fastdiv((uint32_t)(c / 16)), make_fastdiv((uint32_t)wo),
+            make_fastdiv((uint32_t)ho));
+        return dw_after_launch(be, "resize_nearest_i8");
+    }
     k_resize_nearest_i8<<<grid_for(be, items), kThreads, 0, be->stream>>>(x, y, n, hi, wi, ho, wo, c, sh, sw, vec);
     return dw_after_launch(be, "resize_nearest_i8");
 }
