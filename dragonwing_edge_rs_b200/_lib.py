@@ -56,6 +56,11 @@ class DwYoloDetectDesc(ctypes.Structure):
                 ("box_scale", ctypes.c_float * YOLO_MAX_LEVELS), ("cls_scale", ctypes.c_float * YOLO_MAX_LEVELS)]
 
 
+class DwView(ctypes.Structure):
+    """dw_view: a channel range (byte offset, pixel pitch) of a wider NHWC int8 tensor."""
+    _fields_ = [("buf", ctypes.c_void_p), ("offset", ctypes.c_size_t), ("pitch", ctypes.c_int32)]
+
+
 # Every exported function with its argument types (restype is dw_status unless listed).
 vp, sz, i32, u32, f32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_float
 PDESC = ctypes.POINTER(DwConvDesc)
@@ -126,6 +131,11 @@ SIGNATURES = {
     "dw_cast_f16_to_f32": ([vp, vp, vp], i32),
     "dw_unfold_w_f32_to_f16": ([vp, vp, vp] + [sz] * 9, i32),
     "dw_im2col_u8_to_i8": ([vp, vp, vp] + [sz] * 13 + [f32], i32),
+    # channel-range views
+    "dw_conv2d_i8_view": ([vp, PDESC, ctypes.POINTER(DwView), vp, vp, vp, vp, ctypes.POINTER(DwView)], i32),
+    "dw_add_i8_view": ([vp, ctypes.POINTER(DwView), ctypes.POINTER(DwView), ctypes.POINTER(DwView), sz, sz, f32, f32],
+                       i32),
+    "dw_maxpool_i8_view": ([vp, ctypes.POINTER(DwView), ctypes.POINTER(DwView)] + [sz] * 12, i32),
     # YOLOv8 Detect tail and post-processing
     "dw_prepare_yolo_detect": ([vp, ctypes.POINTER(DwYoloDetectDesc), PVP], i32),
     "dw_yolo_detect_i8": ([vp, ctypes.POINTER(DwYoloDetectDesc), vp, PVP, PVP, vp], i32),

@@ -99,6 +99,13 @@ dw_status launch_dwconv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo
 // umma_conv.cu (tcgen05 implicit GEMM)
 bool umma_supported(const dw_backend *be, const dw_conv_desc &d, int ho, int wo);
 bool umma_supported_f16(const dw_backend *be, const dw_conv_desc &d, int ho, int wo);
+// x / y: channel ranges of wider tensors (pitch = elements from one pixel to the next).
+dw_status launch_umma_conv_i8_view(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x, int x_pitch,
+                                   const int8_t *w_ohwi, const EpiParams &ep, int8_t *y, int y_pitch);
+dw_status launch_add_i8_view(dw_backend *be, const int8_t *a, int a_pitch, const int8_t *b, int b_pitch, int8_t *out,
+                             int out_pitch, size_t pixels, int c, float ra, float rb);
+dw_status launch_maxpool_i8_view(dw_backend *be, const int8_t *x, int x_pitch, int8_t *y, int y_pitch, int n, int h,
+                                 int w, int c, int kh, int kw, int sh, int sw, int pt, int pl, int ho, int wo);
 dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
                               const int8_t *w_ohwi, const EpiParams &ep, int8_t *y);
 dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,

@@ -174,6 +174,21 @@ __global__ void k_add_i8_fast(const int8_t *__restrict__ a, const int8_t *__rest
     }
 }
 
+// add_i8 over channel ranges of wider tensors: 16 channels of one pixel per
+// step, the same exact arithmetic as k_add_i8_fast.
+__global__ void k_add_i8_view(const int8_t *__restrict__ a, int a_pitch, const int8_t *__restrict__ b, int b_pitch,
+                              int8_t *__restrict__ out, int out_pitch, uint32_t total, FastDiv fcg, float ra,
+                              float rb) {
+    const float2 ra2 = make_float2(ra, ra), rb2 = make_float2(rb, rb);
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t p = fdiv(i, fcg);
+        const int c = (int)(i - p * fcg.d) * 16;
+        const uint4 va = __ldcs(reinterpret_cast<const uint4 *>(a + (size_t)p * a_pitch + c));
+        const uint4 vb = __ldcs(reinterpret_cast<const uint4 *>(b + (size_t)p * b_pitch + c));
+        *reinterpret_cast<uint4 *>(out + (size_t)p * out_pitch + c) = add16_fast(va, vb, ra2, rb2, ra, rb);
+    }
+}
+
 // --- quantize: ops.rs:3503-3525 (x * (1/scale)) -----------------------------
 __global__ void k_quantize_f32(const float *__restrict__ in, int8_t *__restrict__ out, size_t n, float inv) {
     size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
@@ -448,7 +463,7 @@ __global__ void k_resize_nearest_i8_32(const int8_t *__restrict__ x, int8_t *__r
 // leaves -128).
 __global__ void k_maxpool_i8_v16(const int8_t *__restrict__ x, int8_t *__restrict__ y, int h, int w, int c, int kh,
                                  int kw, int sh, int sw, int pt, int pl, uint32_t total, FastDiv fcg, FastDiv fwo,
-                                 FastDiv fho) {
+                                 FastDiv fho, int x_pitch, int y_pitch) {
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const uint32_t p = fdiv(i, fcg);
         const int g = (int)(i - p * fcg.d);
@@ -460,16 +475,16 @@ __global__ void k_maxpool_i8_v16(const int8_t *__restrict__ x, int8_t *__restric
         const int a0 = max(0, -h0), a1 = min(kh, h - h0), q0 = max(0, -w0), q1 = min(kw, w - w0);
         uint4 m = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
         for (int a = a0; a < a1; a++) {
-            const int8_t *row = x + (((size_t)b * h + (h0 + a)) * w + w0) * c + g * 16;
+            const int8_t *row = x + (((size_t)b * h + (h0 + a)) * w + w0) * x_pitch + g * 16;
             for (int q = q0; q < q1; q++) {
-                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row + (size_t)q * c));
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row + (size_t)q * x_pitch));
                 m.x = __vmaxs4(m.x, v.x);
                 m.y = __vmaxs4(m.y, v.y);
                 m.z = __vmaxs4(m.z, v.z);
                 m.w = __vmaxs4(m.w, v.w);
             }
         }
-        *reinterpret_cast<uint4 *>(y + (size_t)p * c + g * 16) = m;
+        *reinterpret_cast<uint4 *>(y + (size_t)p * y_pitch + g * 16) = m;
     }
 }
 
@@ -554,6 +569,29 @@ dw_status launch_add_i8(dw_backend *be, const int8_t *a, const int8_t *b, int8_t
     return dw_after_launch(be, "add_i8");
 }
 
+dw_status launch_add_i8_view(dw_backend *be, const int8_t *a, int a_pitch, const int8_t *b, int b_pitch, int8_t *out,
+                             int out_pitch, size_t pixels, int c, float ra, float rb) {
+    const size_t items = pixels * (size_t)(c / 16);
+    if (c % 16 || a_pitch % 16 || b_pitch % 16 || out_pitch % 16 || ((uintptr_t)a & 15) || ((uintptr_t)b & 15) ||
+        ((uintptr_t)out & 15) || !(std::fabs(ra) < 1e30f) || !(std::fabs(rb) < 1e30f) || items >= (1u << 31))
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "add_i8_view: needs 16-channel multiples, 16-byte alignment and ratios below 1e30");
+    k_add_i8_view<<<grid_for(be, items), kThreads, 0, be->stream>>>(a, a_pitch, b, b_pitch, out, out_pitch,
+                                                                     (uint32_t)items, make_fastdiv((uint32_t)(c / 16)),
+                                                                     ra, rb);
+    return dw_after_launch(be, "add_i8_view");
+}
+
+dw_status launch_maxpool_i8_view(dw_backend *be, const int8_t *x, int x_pitch, int8_t *y, int y_pitch, int n, int h,
+                                 int w, int c, int kh, int kw, int sh, int sw, int pt, int pl, int ho, int wo) {
+    const size_t groups16 = (size_t)n * ho * wo * (c / 16);
+    if (c % 16 || x_pitch % 16 || y_pitch % 16 || ((uintptr_t)x & 15) || ((uintptr_t)y & 15) || groups16 >= (1u << 31))
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "maxpool_i8_view: needs 16-channel multiples and 16-byte alignment");
+    k_maxpool_i8_v16<<<grid_for(be, groups16), kThreads, 0, be->stream>>>(
+        x, y, h, w, c, kh, kw, sh, sw, pt, pl, (uint32_t)groups16, make_fastdiv((uint32_t)(c / 16)),
+        make_fastdiv((uint32_t)wo), make_fastdiv((uint32_t)ho), x_pitch, y_pitch);
+    return dw_after_launch(be, "maxpool_i8");
+}
+
 dw_status launch_quantize_f32(dw_backend *be, const float *in, int8_t *out, size_t n, float scale) {
     const float inv = 1.0f / scale;  // ops.rs:3506, computed on the host in f32 like the reference
     k_quantize_f32<<<grid_for(be, (n + 15) / 16), kThreads, 0, be->stream>>>(in, out, n, inv);
@@ -590,7 +628,7 @@ dw_status launch_maxpool_i8(dw_backend *be, const int8_t *x, int8_t *y, int n, i
     if (c % 16 == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)y % 16) == 0 && groups16 < (1u << 31)) {
         k_maxpool_i8_v16<<<grid_for(be, groups16), kThreads, 0, be->stream>>>(
             x, y, h, w, c, kh, kw, sh, sw, pt, pl, (uint32_t)groups16, make_fastdiv((uint32_t)(c / 16)),
-            make_fastdiv((uint32_t)wo), make_fastdiv((uint32_t)ho));
+            make_fastdiv((uint32_t)wo), make_fastdiv((uint32_t)ho), c, c);
         return dw_after_launch(be, "maxpool_i8");
     }
     int vec = (c % 4 == 0 && ((uintptr_t)x % 4) == 0 && ((uintptr_t)y % 4) == 0) ? 4 : 1;

@@ -369,6 +369,81 @@ DW_API dw_status dw_maxpool_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_
                                  (int)k_h, (int)k_w, (int)s_h, (int)s_w, (int)p_t, (int)p_l, (int)ho, (int)wo);
 }
 
+namespace {
+// A view of `pixels` pixels of `c` bytes must end inside its buffer.
+dw_status check_view(dw_backend *be, const dw_view *v, size_t pixels, size_t c, const char *op, const char *name) {
+    if (!v || !v->buf) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: %s view is null", op, name);
+    if (v->pitch <= 0 || (size_t)v->pitch < c || (v->offset % 16) || (v->pitch % 16))
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: %s view pitch %d / offset %zu (16-byte multiples, pitch >= %zu)", op,
+                       name, (int)v->pitch, v->offset, c);
+    const size_t end = pixels ? v->offset + (pixels - 1) * (size_t)v->pitch + c : v->offset;
+    if (end > v->buf->len)
+        return dw_fail(be, DW_ERR_SIZE_MISMATCH, "%s: %s view ends at %zu, past the buffer's %zu bytes", op, name, end,
+                       v->buf->len);
+    return DW_OK;
+}
+}  // namespace
+
+DW_API dw_status dw_conv2d_i8_view(dw_backend *be, const dw_conv_desc *d, const dw_view *x, const dw_buf *w_prep,
+                                   const dw_buf *bias, const dw_buf *M, const dw_buf *D, const dw_view *y) {
+    const char *op = "conv2d_i8_view";
+    if (!be) return DW_ERR_INVALID_ARG;
+    int ho, wo;
+    DW_TRY(check_desc(be, d, &ho, &wo, op));
+    DW_TRY(need(be, w_prep, op, "kernel"));
+    DW_TRY(check_view(be, x, (size_t)d->n * d->h * d->w, d->c_in, op, "input"));
+    DW_TRY(check_view(be, y, (size_t)d->n * ho * wo, d->c_out, op, "output"));
+    DW_TRY(check_len(be, w_prep, weight_len(d), op, "kernel"));
+    if (bias) DW_TRY(check_len(be, bias, 4 * (size_t)d->c_out, op, "bias"));
+    if (d->epilogue == DW_EPI_SILU) {
+        DW_TRY(need(be, D, op, "D (dequant scales, required by SILU)"));
+        DW_TRY(check_len(be, D, 4 * (size_t)d->c_out, op, "D"));
+    } else {
+        DW_TRY(need(be, M, op, "M (requant scales)"));
+        DW_TRY(check_len(be, M, 4 * (size_t)d->c_out, op, "M"));
+    }
+    if (be->cfg.conv_path == DW_PATH_DIRECT || !dw::umma_supported(be, *d, ho, wo))
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: views need the tensor-core path (c_in=%d c_out=%d group=%d)", op,
+                       d->c_in, d->c_out, d->group);
+    cudaSetDevice(be->device);
+    dw::EpiParams ep{bias ? (const int32_t *)bias->ptr : nullptr, M ? (const float *)M->ptr : nullptr,
+                     D ? (const float *)D->ptr : nullptr, d->epilogue, d->q6, d->inv_s_out};
+    return dw::launch_umma_conv_i8_view(be, *d, ho, wo, (const int8_t *)x->buf->ptr + x->offset, x->pitch,
+                                        (const int8_t *)w_prep->ptr, ep, (int8_t *)y->buf->ptr + y->offset, y->pitch);
+}
+
+DW_API dw_status dw_add_i8_view(dw_backend *be, const dw_view *a, const dw_view *b, const dw_view *out, size_t pixels,
+                                size_t c, float scale_a_over_y, float scale_b_over_y) {
+    const char *op = "add_i8_view";
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!pixels || !c) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: empty tensor", op);
+    DW_TRY(check_view(be, a, pixels, c, op, "a"));
+    DW_TRY(check_view(be, b, pixels, c, op, "b"));
+    DW_TRY(check_view(be, out, pixels, c, op, "output"));
+    cudaSetDevice(be->device);
+    return dw::launch_add_i8_view(be, (const int8_t *)a->buf->ptr + a->offset, a->pitch,
+                                  (const int8_t *)b->buf->ptr + b->offset, b->pitch,
+                                  (int8_t *)out->buf->ptr + out->offset, out->pitch, pixels, (int)c, scale_a_over_y,
+                                  scale_b_over_y);
+}
+
+DW_API dw_status dw_maxpool_i8_view(dw_backend *be, const dw_view *x, const dw_view *y, size_t n, size_t h, size_t w,
+                                    size_t c, size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t, size_t p_l,
+                                    size_t p_b, size_t p_r) {
+    const char *op = "maxpool_i8_view";
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!n || !h || !w || !c || !k_h || !k_w || !s_h || !s_w || p_t >= k_h || p_b >= k_h || p_l >= k_w || p_r >= k_w ||
+        h + p_t + p_b < k_h || w + p_l + p_r < k_w)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: invalid geometry", op);
+    const size_t ho = (h + p_t + p_b - k_h) / s_h + 1, wo = (w + p_l + p_r - k_w) / s_w + 1;
+    DW_TRY(check_view(be, x, n * h * w, c, op, "input"));
+    DW_TRY(check_view(be, y, n * ho * wo, c, op, "output"));
+    cudaSetDevice(be->device);
+    return dw::launch_maxpool_i8_view(be, (const int8_t *)x->buf->ptr + x->offset, x->pitch,
+                                      (int8_t *)y->buf->ptr + y->offset, y->pitch, (int)n, (int)h, (int)w, (int)c,
+                                      (int)k_h, (int)k_w, (int)s_h, (int)s_w, (int)p_t, (int)p_l, (int)ho, (int)wo);
+}
+
 DW_API dw_status dw_concat_i8(dw_backend *be, const dw_buf *const *xs, const int32_t *channels, int32_t count,
                               size_t pixels, dw_buf *y) {
     if (!be) return DW_ERR_INVALID_ARG;

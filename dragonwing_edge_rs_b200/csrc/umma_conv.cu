@@ -1060,13 +1060,23 @@ namespace {
 // (kind::f16, f16 epilogue with bias and ReLU).
 dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const void *x, const void *w_ohwi,
                            const EpiParams &ep, void *y, int esize, const uint16_t *bias_f16, int relu,
-                           const uint16_t *res_f16) {
+                           const uint16_t *res_f16, int x_pitch, int y_pitch) {
     const char *op = esize == 2 ? "conv2d_f16" : "conv2d_i8";
     if (((uintptr_t)x & 15) || ((uintptr_t)w_ohwi & 15) || ((uintptr_t)y & 15))
         return dw_fail(be, DW_ERR_INVALID_ARG, "%s (tensor-core path): buffers must be 16-byte aligned", op);
     UmmaParams p{};
     const bool flat = d.k_h == 1 && d.k_w == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_t == 0 &&
                       d.pad_l == 0 && d.pad_b == 0 && d.pad_r == 0;
+    // Pixel pitches (elements between consecutive pixels; a channel range of a
+    // wider tensor).  The tensor maps keep the conv's own channel extents, so a
+    // K block past c_in is zero-filled, never read; a strided conv's view packs
+    // the stride's column phases side by side and needs pitch == c_in.
+    if (!x_pitch) x_pitch = d.c_in;
+    if (!y_pitch) y_pitch = d.c_out;
+    if (x_pitch < d.c_in || y_pitch < d.c_out || (x_pitch != d.c_in && d.stride_w > 1) ||
+        ((size_t)x_pitch * esize) % 16 || ((size_t)y_pitch * esize) % 16)
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s (tensor-core path): pitch %d/%d unsupported for this shape", op,
+                       x_pitch, y_pitch);
     p.mode = flat ? 0 : 1;
     p.esize = esize;
     p.bias_f16 = bias_f16;
@@ -1192,7 +1202,7 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     const CUtensorMapSwizzle sw = swizzle_enum(p.bk);
     if (flat) {
         cuuint64_t dims[2] = {(cuuint64_t)d.c_in, (cuuint64_t)p.rows};
-        cuuint64_t strides[1] = {(cuuint64_t)d.c_in * es};
+        cuuint64_t strides[1] = {(cuuint64_t)x_pitch * es};
         cuuint32_t box[2] = {(cuuint32_t)p.bk_elems, (cuuint32_t)kBM};
         cuuint32_t estr[2] = {1, 1};
         r = be->encode_tiled(&ta, dt, 2, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1201,8 +1211,8 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         const int sh = d.stride_h, swd = d.stride_w;
         cuuint64_t dims[5] = {(cuuint64_t)swd * d.c_in, (cuuint64_t)(d.w / swd), (cuuint64_t)sh, (cuuint64_t)(d.h / sh),
                               (cuuint64_t)d.n};
-        cuuint64_t strides[4] = {(cuuint64_t)swd * d.c_in * es, (cuuint64_t)d.w * d.c_in * es,
-                                 (cuuint64_t)sh * d.w * d.c_in * es, (cuuint64_t)d.h * d.w * d.c_in * es};
+        cuuint64_t strides[4] = {(cuuint64_t)swd * x_pitch * es, (cuuint64_t)d.w * x_pitch * es,
+                                 (cuuint64_t)sh * d.w * x_pitch * es, (cuuint64_t)d.h * d.w * x_pitch * es};
         cuuint32_t box[5] = {(cuuint32_t)p.bk_elems, (cuuint32_t)p.tw, 1, (cuuint32_t)p.th, (cuuint32_t)p.nb};
         cuuint32_t estr[5] = {1, 1, 1, 1, 1};
         r = be->encode_tiled(&ta, dt, 5, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1226,15 +1236,15 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     const CUtensorMapSwizzle st_sw = p.swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
     if (flat) {
         cuuint64_t dims[2] = {(cuuint64_t)d.c_out, (cuuint64_t)p.rows};
-        cuuint64_t strides[1] = {(cuuint64_t)d.c_out * es};
+        cuuint64_t strides[1] = {(cuuint64_t)y_pitch * es};
         cuuint32_t box[2] = {st_ch, (cuuint32_t)kBM};
         cuuint32_t estr[2] = {1, 1};
         r = be->encode_tiled(&ty, dt, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, st_sw,
                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
         cuuint64_t dims[4] = {(cuuint64_t)d.c_out, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)d.n};
-        cuuint64_t strides[3] = {(cuuint64_t)d.c_out * es, (cuuint64_t)wo * d.c_out * es,
-                                 (cuuint64_t)ho * wo * d.c_out * es};
+        cuuint64_t strides[3] = {(cuuint64_t)y_pitch * es, (cuuint64_t)wo * y_pitch * es,
+                                 (cuuint64_t)ho * wo * y_pitch * es};
         cuuint32_t box[4] = {st_ch, (cuuint32_t)p.tw, (cuuint32_t)p.th, (cuuint32_t)p.nb};
         cuuint32_t estr[4] = {1, 1, 1, 1};
         r = be->encode_tiled(&ty, dt, 4, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, st_sw,
@@ -1286,14 +1296,19 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
 
 dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
                               const int8_t *w_ohwi, const EpiParams &ep, int8_t *y) {
-    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 1, nullptr, 0, nullptr);
+    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 1, nullptr, 0, nullptr, 0, 0);
+}
+
+dw_status launch_umma_conv_i8_view(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x, int x_pitch,
+                                   const int8_t *w_ohwi, const EpiParams &ep, int8_t *y, int y_pitch) {
+    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 1, nullptr, 0, nullptr, x_pitch, y_pitch);
 }
 
 dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,
                                const uint16_t *w_ohwi, const uint16_t *bias, int relu, uint16_t *y,
                                const uint16_t *residual) {
     EpiParams ep{nullptr, nullptr, nullptr, DW_EPI_NONE, 127, 0.0f};
-    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 2, bias, relu, residual);
+    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 2, bias, relu, residual, 0, 0);
 }
 
 }  // namespace dw

@@ -63,6 +63,7 @@ class Graph:
     initializers: dict
     inputs: list
     outputs: list
+    views: dict = field(default_factory=dict)  # tensor -> (parent tensor, channel offset): see lower_concat_views_i8
 
     def add_tensor(self, name, shape, dtype="i8", scale=None):
         self.tensors[name] = TensorInfo(name, tuple(int(s) for s in shape), dtype, scale)
@@ -469,14 +470,97 @@ def lower_im2col_input_i8(graph: Graph) -> Graph:
     return Graph(tensors, ops_, inits, list(graph.inputs), list(graph.outputs))
 
 
+def lower_concat_views_i8(graph: Graph) -> Graph:
+    """Device lowering of int8 channel concats: when every input of a Concat is
+    written by an op that can write a channel-range view (a tensor-core conv,
+    an int8 add, a maxpool) and read only by ops that can read one (stride-1
+    tensor-core convs, adds, maxpools, or the concat), the inputs become views
+    of the concat's output buffer (producers write their channel ranges in
+    place) and the Concat disappears.  An input that is a channel Split of a
+    tensor makes that tensor a view too, and the Split disappears: this is the
+    C2f block (split, bottlenecks, concat) and SPPF (maxpools, concat) of
+    YOLOv8.  The same bytes end up in the same places, so the result is
+    bit-identical; the copies are gone."""
+    ops_ = list(graph.ops)
+    T = graph.tensors
+    producer, consumers = {}, {}
+    for op in ops_:
+        for o in op.outputs:
+            producer[o] = op
+        for i in op.inputs:
+            consumers.setdefault(i, []).append(op)
+    views = dict(graph.views)
+    protected = set(graph.inputs) | set(graph.outputs)
+    removed = set()
+
+    def tc_conv(op):
+        d = op.params["desc"]
+        return d.group == 1 and d.c_in % 16 == 0 and d.c_out % 16 == 0
+
+    def can_write(op):
+        if op.op_type == "Conv2dRequantReluI8Nhwc":
+            return tc_conv(op)
+        return op.op_type in ("AddQuantized", "MaxPool")
+
+    def can_read(op, t):
+        if op.op_type == "Conv2dRequantReluI8Nhwc":
+            return tc_conv(op) and op.inputs[0] == t and op.params["desc"].stride_w == 1
+        return op.op_type in ("AddQuantized", "MaxPool")
+
+    for cat in ops_:
+        if cat.op_type != "Concat" or cat.outputs[0] in protected:
+            continue
+        out = cat.outputs[0]
+        plan, splits, ok, off = {}, [], True, 0
+        for t in cat.inputs:
+            c = T[t].shape[3]
+            p = producer.get(t)
+            if t in protected or t in views or c % 16 or p is None:
+                ok = False
+                break
+            if p.op_type == "Split":
+                src, c0 = p.inputs[0], p.params["c0"]
+                want = (out, off - c0)
+                sp = producer.get(src)
+                if (off - c0 < 0 or src in protected or src in views or plan.get(src, want) != want or sp is None
+                        or not can_write(sp) or T[src].shape[3] % 16
+                        or any(q.op_type != "Split" or q.outputs[0] not in cat.inputs for q in consumers.get(src, []))):
+                    ok = False
+                    break
+                plan[src] = want
+                plan[t] = (src, c0)
+                splits.append(p)
+            elif can_write(p):
+                plan[t] = (out, off)
+            else:
+                ok = False
+                break
+            if any(q is not cat and q.op_type != "Split" and not can_read(q, t) for q in consumers.get(t, [])):
+                ok = False
+                break
+            off += c
+        if not ok:
+            continue
+        views.update(plan)
+        removed.add(id(cat))
+        removed.update(id(q) for q in splits)
+    if not removed:
+        return graph
+    return Graph(dict(graph.tensors), [op for op in ops_ if id(op) not in removed], dict(graph.initializers),
+                 list(graph.inputs), list(graph.outputs), views)
+
+
 def lower_for_device(graph: Graph) -> Graph:
-    """The device passes: residual fusion, then the input-conv unfold / im2col."""
+    """The device passes: residual fusion, the input-conv unfold / im2col, then
+    concat views."""
     if any(op.op_type == "AddF16" for op in graph.ops):
         graph = fuse_residual_f16(graph)
     if any(op.op_type == "CastF32ToF16" for op in graph.ops):
         graph = lower_unfold_stem_f16(graph)
     if any(op.op_type == "QuantizeU8" for op in graph.ops):
         graph = lower_im2col_input_i8(graph)
+    if any(op.op_type == "Concat" for op in graph.ops):
+        graph = lower_concat_views_i8(graph)
     return graph
 
 
@@ -657,7 +741,8 @@ class CudaGraphRuntime:
         self._dispatch = []
         self._cgraph = None
         for name, t in graph.tensors.items():
-            self.bufs[name] = backend.alloc(t.nbytes)
+            if name not in graph.views:
+                self.bufs[name] = backend.alloc(t.nbytes)
         consts = {}
         for name, arr in graph.initializers.items():
             consts[name] = backend.upload_array(np.ascontiguousarray(arr))
@@ -665,6 +750,14 @@ class CudaGraphRuntime:
         for op in graph.ops:
             self._dispatch.append(self._compile(op))
         backend.synchronize(60000)
+
+    def _loc(self, name):
+        """(buffer, byte offset, pixel pitch, is_view) of a tensor (int8)."""
+        root, off = name, 0
+        while root in self.graph.views:
+            root, o = self.graph.views[root]
+            off += o
+        return self.bufs[root], off, self.graph.tensors[root].shape[3], root != name
 
     def _compile(self, op: CompiledOp):
         be, bufs, consts = self.be, self.bufs, self._consts
@@ -674,18 +767,27 @@ class CudaGraphRuntime:
             x, wn, bn, mn, dn = op.inputs
             wp = ops.prepare_weights_i8(be, desc, consts[wn])
             consts[wn + "_prep"] = wp
-            y = bufs[op.outputs[0]]
-            bx, bb, bm, bd = bufs[x], consts[bn], consts[mn], consts[dn]
+            bb, bm, bd = consts[bn], consts[mn], consts[dn]
+            xl, yl = self._loc(x), self._loc(op.outputs[0])
+            if xl[3] or yl[3]:
+                return lambda: ops.conv2d_i8_view(be, desc, xl[:3], wp, bb, bm, bd, yl[:3])
+            bx, y = xl[0], yl[0]
             return lambda: ops.conv2d_i8(be, desc, bx, wp, bb, bm, bd, y)
         if t == "AddQuantized":
-            a, b_ = bufs[op.inputs[0]], bufs[op.inputs[1]]
-            y = bufs[op.outputs[0]]
+            al, bl, ol = self._loc(op.inputs[0]), self._loc(op.inputs[1]), self._loc(op.outputs[0])
             ra, rb = op.params["scale_a_over_out"], op.params["scale_b_over_out"]
+            if al[3] or bl[3] or ol[3]:
+                n, h, w, c = self.graph.tensors[op.outputs[0]].shape
+                return lambda: ops.add_i8_view(be, al[:3], bl[:3], ol[:3], n * h * w, c, ra, rb)
+            a, b_, y = al[0], bl[0], ol[0]
             return lambda: ops.add_i8_packed(be, a, b_, y, ra, rb)
         if t == "MaxPool":
             n, h, w, c = self.graph.tensors[op.inputs[0]].shape
             k, s, p = op.params["k"], op.params["s"], op.params["pad"]
-            x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
+            xl, yl = self._loc(op.inputs[0]), self._loc(op.outputs[0])
+            if xl[3] or yl[3]:
+                return lambda: ops.maxpool_i8_view(be, xl[:3], yl[:3], n, h, w, c, k, k, s, s, (p, p, p, p))
+            x, y = xl[0], yl[0]
             return lambda: ops.maxpool_i8(be, x, y, n, h, w, c, k, k, s, s, (p, p, p, p))
         if t == "Concat":
             xs = [bufs[i] for i in op.inputs]

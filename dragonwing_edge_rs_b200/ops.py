@@ -156,6 +156,32 @@ def maxpool_i8(backend, x, y, n, h, w, c, k_h, k_w, s_h, s_w, pads=(0, 0, 0, 0))
                                           pt, pl, pb, pr))
 
 
+def _view(v):
+    """(CudaBuffer, byte offset, pitch) -> dw_view."""
+    buf, off, pitch = v
+    return L.DwView(buf.handle.value, off, pitch)
+
+
+def conv2d_i8_view(backend: CudaBackend, desc: ConvDesc, x, w_prep: CudaBuffer, bias, M, D, y):
+    """conv2d_i8 with the input and output given as (buffer, byte offset, pixel pitch) channel-range views."""
+    d, xv, yv = desc.to_c(), _view(x), _view(y)
+    backend._check(L.load().dw_conv2d_i8_view(backend.handle, ctypes.byref(d), ctypes.byref(xv), w_prep.handle,
+                                              _h(bias), _h(M), _h(D), ctypes.byref(yv)))
+
+
+def add_i8_view(backend, a, b, out, pixels, c, ra, rb):
+    av, bv, ov = _view(a), _view(b), _view(out)
+    backend._check(L.load().dw_add_i8_view(backend.handle, ctypes.byref(av), ctypes.byref(bv), ctypes.byref(ov),
+                                           pixels, c, float(ra), float(rb)))
+
+
+def maxpool_i8_view(backend, x, y, n, h, w, c, k_h, k_w, s_h, s_w, pads):
+    xv, yv = _view(x), _view(y)
+    pt, pl, pb, pr = pads
+    backend._check(L.load().dw_maxpool_i8_view(backend.handle, ctypes.byref(xv), ctypes.byref(yv), n, h, w, c, k_h,
+                                               k_w, s_h, s_w, pt, pl, pb, pr))
+
+
 def concat_i8(backend, xs, channels, pixels, y):
     arr = (ctypes.c_void_p * len(xs))(*[b.handle.value for b in xs])
     cs = (ctypes.c_int32 * len(channels))(*channels)

@@ -281,6 +281,31 @@ DW_API dw_status dw_slice_c_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_
 DW_API dw_status dw_resize_nearest_i8(dw_backend *be, const dw_buf *x, dw_buf *y, size_t n, size_t h_in,
                                       size_t w_in, size_t h_out, size_t w_out, size_t c);
 
+/* Channel-range views.  A dw_view is a channel range of an NHWC tensor that
+ * lives inside a wider one: its element (pixel p, channel c) is the byte at
+ * offset + p * pitch + c of buf (pitch >= the view's channels; int8).  A graph
+ * runtime uses views to let producers write, and consumers read, the channel
+ * ranges of a concat's output in place (the concat and channel-split copies
+ * vanish; the values are the same). */
+typedef struct dw_view {
+    dw_buf *buf;
+    size_t offset;  /* bytes; a multiple of 16 */
+    int32_t pitch;  /* bytes from one pixel to the next; a multiple of 16 */
+} dw_view;
+
+/* dw_conv2d_i8 with the input and output as views (tensor-core path only:
+ * DW_ERR_UNSUPPORTED where it does not apply, or for an input view of a conv
+ * with stride_w > 1 whose pitch differs from c_in). */
+DW_API dw_status dw_conv2d_i8_view(dw_backend *be, const dw_conv_desc *d, const dw_view *x, const dw_buf *w_prep,
+                                   const dw_buf *bias, const dw_buf *M, const dw_buf *D, const dw_view *y);
+/* dw_add_i8 over `pixels` pixels of `c` channels (c a multiple of 16) given as views. */
+DW_API dw_status dw_add_i8_view(dw_backend *be, const dw_view *a, const dw_view *b, const dw_view *out, size_t pixels,
+                                size_t c, float scale_a_over_y, float scale_b_over_y);
+/* dw_maxpool_i8 with the input and output as views (c a multiple of 16). */
+DW_API dw_status dw_maxpool_i8_view(dw_backend *be, const dw_view *x, const dw_view *y, size_t n, size_t h, size_t w,
+                                    size_t c, size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t, size_t p_l,
+                                    size_t p_b, size_t p_r);
+
 /* ---------------------------------------------------------------------- */
 /* YOLOv8 Detect head tail and detection post-processing                   */
 /* ---------------------------------------------------------------------- */
