@@ -219,7 +219,7 @@ def op_flops(op):
     """Algorithmic ops (2 x MACs; a zero-padded input channel does not count)."""
     if op.op_type == "GemmF16":
         return 2 * op.params["m"] * op.params["n"] * op.params["k"]
-    if op.op_type not in ("Conv2dRequantReluI8Nhwc", "Conv2dF16", "Conv2dAddF16"):
+    if op.op_type not in ("Conv2dRequantReluI8Nhwc", "Conv2dAddI8", "Conv2dF16", "Conv2dAddF16"):
         return 0
     d = op.params["desc"]
     ho, wo = d.out_hw()

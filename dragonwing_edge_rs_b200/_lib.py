@@ -133,6 +133,8 @@ SIGNATURES = {
     "dw_im2col_u8_to_i8": ([vp, vp, vp] + [sz] * 13 + [f32], i32),
     # channel-range views
     "dw_conv2d_i8_view": ([vp, PDESC, ctypes.POINTER(DwView), vp, vp, vp, vp, ctypes.POINTER(DwView)], i32),
+    "dw_conv2d_add_i8_view": ([vp, PDESC, ctypes.POINTER(DwView), vp, vp, vp, vp, ctypes.POINTER(DwView), f32, f32,
+                               ctypes.POINTER(DwView)], i32),
     "dw_add_i8_view": ([vp, ctypes.POINTER(DwView), ctypes.POINTER(DwView), ctypes.POINTER(DwView), sz, sz, f32, f32],
                        i32),
     "dw_maxpool_i8_view": ([vp, ctypes.POINTER(DwView), ctypes.POINTER(DwView)] + [sz] * 12, i32),

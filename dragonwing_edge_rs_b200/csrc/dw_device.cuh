@@ -161,4 +161,66 @@ __device__ __forceinline__ void record_error(int32_t *err, int32_t code, int32_t
     }
 }
 
+// add_i8 (crates/dragonwing-cpu/src/ops.rs:3197-3209) on 4 packed int8 pairs:
+// y = fl(fl(a * ra) + fl(b * rb)), then roundf and clamp, per element.
+__device__ __forceinline__ uint32_t add4(uint32_t a, uint32_t b, float ra, float rb) {
+    uint32_t r = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        int32_t av = (int8_t)(a >> (8 * k)), bv = (int8_t)(b >> (8 * k));
+        float y = __fadd_rn(__fmul_rn(i2f_small(av), ra), __fmul_rn(i2f_small(bv), rb));
+        r |= (uint32_t)(uint8_t)f32_to_i8(y) << (8 * k);
+    }
+    return r;
+}
+
+// Fast path of add_i8 for 16 elements, taken when the ratios are finite and
+// below 1e30 (no overflow to infinity, so no NaN from inf - inf): the same
+// f32 operations as the reference, the conversions and rounding steps two
+// elements per packed instruction.  A
+// byte a placed in the low mantissa bits of 1.5 * 2^23 (after a ^ 0x80, i.e.
+// a + 128) reads as 1.5 * 2^23 + 128 + a, and subtracting 1.5 * 2^23 + 128
+// (exact) gives a.  y = fl(fl(a * ra) + fl(b * rb)); clamp to [-128, 127] in
+// f32; rint by the magic add; ties (c - rint(c) == +-0.5, rare) are redone
+// per element with roundf's half-away-from-zero.
+__device__ __forceinline__ uint4 add16_fast(uint4 a, uint4 b, float2 ra2, float2 rb2, float ra, float rb) {
+    const float2 off = make_float2(-(kMagic + 128.0f), -(kMagic + 128.0f));
+    const float2 mag = make_float2(kMagic, kMagic), nmag = make_float2(-kMagic, -kMagic);
+    const float2 neg1 = make_float2(-1.0f, -1.0f);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t out[4];
+    bool tie = false;
+#pragma unroll
+    for (int wd = 0; wd < 4; wd++) {
+        const uint32_t ax = aw[wd] ^ 0x80808080u, bx = bw[wd] ^ 0x80808080u;
+        uint32_t q[4];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t s0 = 0x7650u | (uint32_t)(2 * h), s1 = 0x7650u | (uint32_t)(2 * h + 1);
+            const float2 fa = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(ax, 0x4B400000u, s0)),
+                                                     __uint_as_float(__byte_perm(ax, 0x4B400000u, s1))), off);
+            const float2 fb = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(bx, 0x4B400000u, s0)),
+                                                     __uint_as_float(__byte_perm(bx, 0x4B400000u, s1))), off);
+            // scalar products and sum: a packed multiply feeding a packed
+            // round-to-nearest add can be fused into one multiply-add by the
+            // compiler, which skips the reference's rounding of the products
+            float2 c = make_float2(__fadd_rn(__fmul_rn(fa.x, ra2.x), __fmul_rn(fb.x, rb2.x)),
+                                   __fadd_rn(__fmul_rn(fa.y, ra2.y), __fmul_rn(fb.y, rb2.y)));
+            c.x = fminf(fmaxf(c.x, -128.0f), 127.0f);
+            c.y = fminf(fmaxf(c.y, -128.0f), 127.0f);
+            const float2 r = __fadd2_rn(c, mag);
+            const float2 d = __ffma2_rn(__fadd2_rn(r, nmag), neg1, c);  // c - rint(c), exact
+            tie |= fmaxf(fabsf(d.x), fabsf(d.y)) == 0.5f;
+            q[2 * h] = __float_as_uint(r.x);
+            q[2 * h + 1] = __float_as_uint(r.y);
+        }
+        out[wd] = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+    }
+    if (tie) {
+#pragma unroll
+        for (int wd = 0; wd < 4; wd++) out[wd] = add4(aw[wd], bw[wd], ra, rb);
+    }
+    return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 }  // namespace dw

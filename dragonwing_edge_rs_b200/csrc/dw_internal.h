@@ -102,6 +102,10 @@ bool umma_supported_f16(const dw_backend *be, const dw_conv_desc &d, int ho, int
 // x / y: channel ranges of wider tensors (pitch = elements from one pixel to the next).
 dw_status launch_umma_conv_i8_view(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x, int x_pitch,
                                    const int8_t *w_ohwi, const EpiParams &ep, int8_t *y, int y_pitch);
+// y = add_i8(res, conv(x)) with ratios ra (res) and rb (conv), fused in the epilogue.
+dw_status launch_umma_conv_add_i8_view(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
+                                       int x_pitch, const int8_t *w_ohwi, const EpiParams &ep, const int8_t *res,
+                                       int res_pitch, float ra, float rb, int8_t *y, int y_pitch);
 dw_status launch_add_i8_view(dw_backend *be, const int8_t *a, int a_pitch, const int8_t *b, int b_pitch, int8_t *out,
                              int out_pitch, size_t pixels, int c, float ra, float rb);
 dw_status launch_maxpool_i8_view(dw_backend *be, const int8_t *x, int x_pitch, int8_t *y, int y_pitch, int n, int h,

@@ -2,6 +2,7 @@
 // the reference's (crates/dragonwing-vulkan/src/ops.rs, crates/dragonwing-cpu/src/ops.rs),
 // then dispatch to the kernels.
 
+#include <cmath>
 #include <vector>
 
 #include "dw_internal.h"
@@ -410,6 +411,40 @@ DW_API dw_status dw_conv2d_i8_view(dw_backend *be, const dw_conv_desc *d, const 
                      D ? (const float *)D->ptr : nullptr, d->epilogue, d->q6, d->inv_s_out};
     return dw::launch_umma_conv_i8_view(be, *d, ho, wo, (const int8_t *)x->buf->ptr + x->offset, x->pitch,
                                         (const int8_t *)w_prep->ptr, ep, (int8_t *)y->buf->ptr + y->offset, y->pitch);
+}
+
+DW_API dw_status dw_conv2d_add_i8_view(dw_backend *be, const dw_conv_desc *d, const dw_view *x, const dw_buf *w_prep,
+                                       const dw_buf *bias, const dw_buf *M, const dw_buf *D, const dw_view *residual,
+                                       float ra, float rb, const dw_view *y) {
+    const char *op = "conv2d_add_i8_view";
+    if (!be) return DW_ERR_INVALID_ARG;
+    int ho, wo;
+    DW_TRY(check_desc(be, d, &ho, &wo, op));
+    DW_TRY(need(be, w_prep, op, "kernel"));
+    DW_TRY(check_view(be, x, (size_t)d->n * d->h * d->w, d->c_in, op, "input"));
+    DW_TRY(check_view(be, residual, (size_t)d->n * ho * wo, d->c_out, op, "residual"));
+    DW_TRY(check_view(be, y, (size_t)d->n * ho * wo, d->c_out, op, "output"));
+    DW_TRY(check_len(be, w_prep, weight_len(d), op, "kernel"));
+    if (bias) DW_TRY(check_len(be, bias, 4 * (size_t)d->c_out, op, "bias"));
+    if (d->epilogue == DW_EPI_SILU) {
+        DW_TRY(need(be, D, op, "D (dequant scales, required by SILU)"));
+        DW_TRY(check_len(be, D, 4 * (size_t)d->c_out, op, "D"));
+    } else {
+        DW_TRY(need(be, M, op, "M (requant scales)"));
+        DW_TRY(check_len(be, M, 4 * (size_t)d->c_out, op, "M"));
+    }
+    if (!(std::fabs(ra) < 1e30f) || !(std::fabs(rb) < 1e30f))
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: add ratios must be below 1e30 in magnitude", op);
+    if (be->cfg.conv_path == DW_PATH_DIRECT || !dw::umma_supported(be, *d, ho, wo) || d->c_out % 16)
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: needs the tensor-core path (c_in=%d c_out=%d group=%d)", op,
+                       d->c_in, d->c_out, d->group);
+    cudaSetDevice(be->device);
+    dw::EpiParams ep{bias ? (const int32_t *)bias->ptr : nullptr, M ? (const float *)M->ptr : nullptr,
+                     D ? (const float *)D->ptr : nullptr, d->epilogue, d->q6, d->inv_s_out};
+    return dw::launch_umma_conv_add_i8_view(be, *d, ho, wo, (const int8_t *)x->buf->ptr + x->offset, x->pitch,
+                                            (const int8_t *)w_prep->ptr, ep,
+                                            (const int8_t *)residual->buf->ptr + residual->offset, residual->pitch,
+                                            ra, rb, (int8_t *)y->buf->ptr + y->offset, y->pitch);
 }
 
 DW_API dw_status dw_add_i8_view(dw_backend *be, const dw_view *a, const dw_view *b, const dw_view *out, size_t pixels,

@@ -72,6 +72,7 @@ struct UmmaParams {
     int bk_elems;                           // bk / esize: K elements per stage
     const uint16_t *bias_f16;               // fp16 path: bias [c_out] (may be null)
     const uint16_t *res_f16;                // fp16 path, flat mode: residual [rows][c_out] added (may be null)
+    float add_ra, add_rb;                   // int8 residual (kFm & 2): y = add_i8(residual, conv) with these ratios
     int relu;                               // fp16 path: ReLU last (after the bias and the residual)
     int swz;                                // fp16 path: staging in 64-channel slabs, 128-byte swizzle (bn % 64 == 0)
     int nbuf;                               // staging buffers (2: a tile's store overlaps the next tile's epilogue)
@@ -541,6 +542,17 @@ __device__ __forceinline__ int valid_blocks(const UmmaParams &p, const TileCoord
     return left < p.R ? left : p.R;
 }
 
+// int8 residual (kFm & 2): the staging unit already holds the residual's 16
+// bytes (fetched by the store warp before the epilogue fills the buffer); the
+// tile's output is add_i8(residual, conv) with the op's ratios, exactly as the
+// separate add computes it.
+template <int kFm>
+__device__ __forceinline__ uint4 with_residual(uint4 conv, uint32_t staged, const UmmaParams &p) {
+    if (!(kFm & 2)) return conv;
+    return add16_fast(lds_v4(staged), conv, make_float2(p.add_ra, p.add_ra), make_float2(p.add_rb, p.add_rb), p.add_ra,
+                      p.add_rb);
+}
+
 constexpr int kTapTable = 64;  // taps whose view coordinates the producer keeps in shared memory
 
 // Coordinates of tap (kh, kw) in the 5-D activation view: the column phase's
@@ -849,8 +861,11 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                     tc_ld16(tacc + (uint32_t)(c * 16), v1);
                     tc_ld16(tacc + (uint32_t)(c2 * 16), v2);
                     tc_wait_ld();
-                    sts_v4(dst0 + (uint32_t)(c * 16), requant16<kSilu>(v1, chan, slot_base + c * 16, p));
-                    if (c + 1 < ce) sts_v4(dst0 + (uint32_t)(c2 * 16), requant16<kSilu>(v2, chan, slot_base + c2 * 16, p));
+                    sts_v4(dst0 + (uint32_t)(c * 16),
+                           with_residual<kFm>(requant16<kSilu>(v1, chan, slot_base + c * 16, p), dst0 + (uint32_t)(c * 16), p));
+                    if (c + 1 < ce)
+                        sts_v4(dst0 + (uint32_t)(c2 * 16), with_residual<kFm>(requant16<kSilu>(v2, chan, slot_base + c2 * 16, p),
+                                                                              dst0 + (uint32_t)(c2 * 16), p));
                 }
             } else {
             const int per = (items + kEpiParts - 1) / kEpiParts;
@@ -867,10 +882,11 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                 tc_ld16(tacc + (uint32_t)(r2 * p.bn + c2 * 16), v2);
                 uint8_t *dst1 = stage + ((size_t)(r1 * kBM + row)) * p.bn + c1 * 16;
                 tc_wait_ld();
-                sts_v4(smem_u32(dst1), requant16<kSilu>(v1, chan, slot_base + c1 * 16, p));
+                sts_v4(smem_u32(dst1), with_residual<kFm>(requant16<kSilu>(v1, chan, slot_base + c1 * 16, p), smem_u32(dst1), p));
                 if (two) {
                     uint8_t *dst2 = stage + ((size_t)(r2 * kBM + row)) * p.bn + c2 * 16;
-                    sts_v4(smem_u32(dst2), requant16<kSilu>(v2, chan, slot_base + c2 * 16, p));
+                    sts_v4(smem_u32(dst2),
+                           with_residual<kFm>(requant16<kSilu>(v2, chan, slot_base + c2 * 16, p), smem_u32(dst2), p));
                 }
                 c1 += 2;
                 while (c1 >= chunks) { c1 -= chunks; r1++; }
@@ -890,7 +906,7 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
         // buffer -- releases it for the tile nbuf tiles later (fetching that
         // tile's fp16 residual into it first).
         if (lane == 0) {
-            constexpr bool res_tma = kF16 && (kFm & 2);
+            constexpr bool res_tma = (kFm & 2) != 0;
             constexpr int es = kF16 ? 2 : 1;
             const int slabs = (kF16 && p.swz) ? p.bn / 64 : 1, sw_ch = (kF16 && p.swz) ? 64 : p.bn;
             uint32_t res_ph[2] = {0u, 0u};
@@ -901,11 +917,18 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                     const TileCoord tc = tile_coord(p, tile);
                     const int nrb = valid_blocks(p, tc);
                     uint8_t *stage = out_stage + (size_t)sb * p.out_bytes;
-                    mbar_expect_tx(bar, (uint32_t)(nrb * kBM * p.bn * 2));
+                    // bytes per row block: its box (128 rows, or tw x th x nb pixels in mode 1)
+                    const int box_rows = p.mode == 0 ? kBM : p.tw * p.th * p.nb;
+                    mbar_expect_tx(bar, (uint32_t)(nrb * box_rows * p.bn * es));
                     for (int r = 0; r < nrb; r++)
-                        for (int sl = 0; sl < slabs; sl++)
-                            tma_load_2d(smem_u32(stage + (size_t)r * kBM * p.bn * 2 + (size_t)sl * kBM * sw_ch * 2),
-                                        &tmap_r, bar, tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
+                        for (int sl = 0; sl < slabs; sl++) {
+                            const uint32_t dst =
+                                smem_u32(stage + (size_t)r * kBM * p.bn * es + (size_t)sl * kBM * sw_ch * es);
+                            if (p.mode == 0)
+                                tma_load_2d(dst, &tmap_r, bar, tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
+                            else
+                                tma_load_4d(dst, &tmap_r, bar, tc.n0 + sl * sw_ch, tc.ow0, tc.oh0 + r * p.th, tc.img);
+                        }
                     res_out[sb] = true;
                 } else {
                     mbar_arrive(bar);
@@ -1060,7 +1083,8 @@ namespace {
 // (kind::f16, f16 epilogue with bias and ReLU).
 dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const void *x, const void *w_ohwi,
                            const EpiParams &ep, void *y, int esize, const uint16_t *bias_f16, int relu,
-                           const uint16_t *res_f16, int x_pitch, int y_pitch) {
+                           const uint16_t *res_f16, int x_pitch, int y_pitch, const int8_t *res_i8 = nullptr,
+                           int res_pitch = 0, float add_ra = 0.0f, float add_rb = 0.0f) {
     const char *op = esize == 2 ? "conv2d_f16" : "conv2d_i8";
     if (((uintptr_t)x & 15) || ((uintptr_t)w_ohwi & 15) || ((uintptr_t)y & 15))
         return dw_fail(be, DW_ERR_INVALID_ARG, "%s (tensor-core path): buffers must be 16-byte aligned", op);
@@ -1081,6 +1105,11 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     p.esize = esize;
     p.bias_f16 = bias_f16;
     p.res_f16 = res_f16;
+    p.add_ra = add_ra;
+    p.add_rb = add_rb;
+    if (!res_pitch) res_pitch = d.c_out;
+    if (res_i8 && (esize != 1 || ((uintptr_t)res_i8 & 15) || res_pitch < d.c_out || res_pitch % 16))
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: an int8 residual needs 16-byte alignment and pitch", op);
     p.relu = relu;
     p.swz = 0;
     if (res_f16 && (!flat || ((uintptr_t)res_f16 & 15)))
@@ -1263,6 +1292,28 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: residual tensor map rejected (%d)", op, (int)r);
     }
+    // int8 residual: the output's map over the residual (view) buffer
+    if (res_i8) {
+        const cuuint64_t rp = (cuuint64_t)res_pitch;
+        if (flat) {
+            cuuint64_t dims[2] = {(cuuint64_t)d.c_out, (cuuint64_t)p.rows};
+            cuuint64_t strides[1] = {rp};
+            cuuint32_t box[2] = {st_ch, (cuuint32_t)kBM};
+            cuuint32_t estr[2] = {1, 1};
+            r = be->encode_tiled(&tr, dt, 2, const_cast<int8_t *>(res_i8), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, st_sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        } else {
+            cuuint64_t dims[4] = {(cuuint64_t)d.c_out, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)d.n};
+            cuuint64_t strides[3] = {rp, (cuuint64_t)wo * rp, (cuuint64_t)ho * wo * rp};
+            cuuint32_t box[4] = {st_ch, (cuuint32_t)p.tw, (cuuint32_t)p.th, (cuuint32_t)p.nb};
+            cuuint32_t estr[4] = {1, 1, 1, 1};
+            r = be->encode_tiled(&tr, dt, 4, const_cast<int8_t *>(res_i8), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, st_sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        }
+        if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: residual tensor map rejected (%d)", op, (int)r);
+    }
 
     using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, UmmaParams);
     static const KernelFn f16_kernels[8] = {
@@ -1276,6 +1327,10 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
                              (int)kSmemLimit);
         cudaFuncSetAttribute(k_umma_conv_i8<true, false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<false, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<true, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemLimit);
         for (KernelFn f : f16_kernels)
             cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
         attr_set[dev] = true;
@@ -1284,6 +1339,11 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     if (esize == 2) {
         const int fm = (bias_f16 ? 1 : 0) | (res_f16 ? 2 : 0) | (relu ? 4 : 0);
         f16_kernels[fm]<<<grid, umma_threads(true), smem, be->stream>>>(ta, tb, ty, tr, p);
+    } else if (res_i8) {
+        if (ep.epilogue == DW_EPI_SILU)
+            k_umma_conv_i8<true, false, 2><<<grid, umma_threads(false), smem, be->stream>>>(ta, tb, ty, tr, p);
+        else
+            k_umma_conv_i8<false, false, 2><<<grid, umma_threads(false), smem, be->stream>>>(ta, tb, ty, tr, p);
     } else if (ep.epilogue == DW_EPI_SILU) {
         k_umma_conv_i8<true, false, 0><<<grid, umma_threads(false), smem, be->stream>>>(ta, tb, ty, tr, p);
     } else {
@@ -1302,6 +1362,13 @@ dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int
 dw_status launch_umma_conv_i8_view(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x, int x_pitch,
                                    const int8_t *w_ohwi, const EpiParams &ep, int8_t *y, int y_pitch) {
     return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 1, nullptr, 0, nullptr, x_pitch, y_pitch);
+}
+
+dw_status launch_umma_conv_add_i8_view(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
+                                       int x_pitch, const int8_t *w_ohwi, const EpiParams &ep, const int8_t *res,
+                                       int res_pitch, float ra, float rb, int8_t *y, int y_pitch) {
+    return launch_umma_conv(be, d, ho, wo, x, w_ohwi, ep, y, 1, nullptr, 0, nullptr, x_pitch, y_pitch, res, res_pitch,
+                            ra, rb);
 }
 
 dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,

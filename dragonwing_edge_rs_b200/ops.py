@@ -169,6 +169,15 @@ def conv2d_i8_view(backend: CudaBackend, desc: ConvDesc, x, w_prep: CudaBuffer, 
                                               _h(bias), _h(M), _h(D), ctypes.byref(yv)))
 
 
+def conv2d_add_i8_view(backend: CudaBackend, desc: ConvDesc, x, w_prep: CudaBuffer, bias, M, D, residual, ra, rb, y):
+    """y = add_i8(residual, conv(x)) fused (ratios ra for the residual, rb for the conv's result); the
+    tensors as (buffer, byte offset, pixel pitch) views."""
+    d, xv, rv, yv = desc.to_c(), _view(x), _view(residual), _view(y)
+    backend._check(L.load().dw_conv2d_add_i8_view(backend.handle, ctypes.byref(d), ctypes.byref(xv), w_prep.handle,
+                                                  _h(bias), _h(M), _h(D), ctypes.byref(rv), float(ra), float(rb),
+                                                  ctypes.byref(yv)))
+
+
 def add_i8_view(backend, a, b, out, pixels, c, ra, rb):
     av, bv, ov = _view(a), _view(b), _view(out)
     backend._check(L.load().dw_add_i8_view(backend.handle, ctypes.byref(av), ctypes.byref(bv), ctypes.byref(ov),

@@ -298,6 +298,17 @@ typedef struct dw_view {
  * with stride_w > 1 whose pitch differs from c_in). */
 DW_API dw_status dw_conv2d_i8_view(dw_backend *be, const dw_conv_desc *d, const dw_view *x, const dw_buf *w_prep,
                                    const dw_buf *bias, const dw_buf *M, const dw_buf *D, const dw_view *y);
+/* Conv -> Add fused: y = add_i8(residual, conv(x)), the int8 add of the
+ * reference (crates/dragonwing-cpu/src/ops.rs:3197-3209: y = round(clamp(
+ * residual * ra + conv * rb))) applied to the fused conv's int8 result in its
+ * epilogue, with all three tensors as views (tensor-core path only; ratios
+ * below 1e30 in magnitude).  Bit-identical with dw_conv2d_i8 followed by
+ * dw_add_i8; the conv's own output never reaches memory.  y may be the
+ * residual view itself: each tile's residual is read before its output is
+ * stored, and tiles do not overlap. */
+DW_API dw_status dw_conv2d_add_i8_view(dw_backend *be, const dw_conv_desc *d, const dw_view *x, const dw_buf *w_prep,
+                                       const dw_buf *bias, const dw_buf *M, const dw_buf *D, const dw_view *residual,
+                                       float ra, float rb, const dw_view *y);
 /* dw_add_i8 over `pixels` pixels of `c` channels (c a multiple of 16) given as views. */
 DW_API dw_status dw_add_i8_view(dw_backend *be, const dw_view *a, const dw_view *b, const dw_view *out, size_t pixels,
                                 size_t c, float scale_a_over_y, float scale_b_over_y);

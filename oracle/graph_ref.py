@@ -59,6 +59,18 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
             D = graph.initializers[op.inputs[4]]
             y = dwref.conv2d_fused_i8(x, w, bias, M, D if d.epilogue == dwref.EPI_SILU else None, od, threads)
             vals[op.outputs[0]] = y.reshape(shape_of(op.outputs[0]))
+        elif t == "Conv2dAddI8":  # device fusion of Conv2dRequantReluI8Nhwc -> AddQuantized(residual, conv)
+            d = op.params["desc"]
+            x = vals[op.inputs[0]]
+            n = x.shape[0]
+            od = dwref.conv_desc(n, d.h, d.w, d.c_in, d.c_out, d.k_h, d.k_w, d.stride_h, d.stride_w, d.pads,
+                                 d.group, d.epilogue, d.q6, d.inv_s_out)
+            y = dwref.conv2d_fused_i8(x, graph.initializers[op.inputs[1]], graph.initializers[op.inputs[2]],
+                                      graph.initializers[op.inputs[3]], graph.initializers[op.inputs[4]]
+                                      if d.epilogue == dwref.EPI_SILU else None, od, threads)
+            res = vals[op.inputs[5]]
+            z = dwref.add_i8(res, y.reshape(res.shape), op.params["ra"], op.params["rb"])
+            vals[op.outputs[0]] = z.reshape(shape_of(op.outputs[0]))
         elif t == "AddQuantized":
             a, b = vals[op.inputs[0]], vals[op.inputs[1]]
             y = dwref.add_i8(a, b, op.params["scale_a_over_out"], op.params["scale_b_over_out"])

@@ -28,7 +28,7 @@ def test_mobilenetv2_block_small_batch(be):
     ref = run_graph(g, {"x": x}, threads=8)[g.outputs[0]]
     assert np.array_equal(y_eager, ref.reshape(y_eager.shape))
     kernels = rt.capture()
-    assert kernels == len(g.ops)
+    assert kernels == len(rt.graph.ops) == len(g.ops)
     rt.run()
     y_graph = rt.get_output(g.outputs[0])
     assert np.array_equal(y_graph, y_eager)
@@ -51,6 +51,23 @@ def test_yolov8n_int8_batch1_bit_exact(be, head):
         got = rt.get_output(name)
         exp = ref[name].reshape(got.shape)
         assert np.array_equal(got, exp), f"{name}: {int((got != exp).sum())} of {got.size} differ"
+    rt.release()
+
+
+def test_yolov8n_int8_residual_fusion_bit_exact(be):
+    """The opt-in int8 residual fusion (two bottleneck convs carry their
+    shortcut add, reading and writing concat views): output0 identical to
+    the oracle's unfused graph."""
+    g = G.yolov8n(batch=2, size=320, seed=8, head="detect")
+    img = np.random.default_rng(6).integers(0, 256, g.tensors["image"].nbytes).astype(np.uint8)
+    rt = G.CudaGraphRuntime(g, be, residual_i8=True)
+    assert [op.op_type for op in rt.graph.ops].count("Conv2dAddI8") == 2
+    rt.set_input_bytes("image", img)
+    rt.run()
+    ref = run_graph(g, {"image": img}, threads=8)
+    for name in g.outputs:
+        got = rt.get_output(name)
+        assert np.array_equal(got, ref[name].reshape(got.shape)), name
     rt.release()
 
 

@@ -1,5 +1,5 @@
-"""The concat-view device pass (dragonwing_edge_rs_b200.graph.lower_concat_views_i8)
-on the CPU: the lowered YOLOv8n graph, executed op by op with the oracle's
+"""The concat-view and residual-fusion device passes
+(dragonwing_edge_rs_b200.graph.lower_concat_views_i8, fuse_residual_i8) on the CPU: the lowered YOLOv8n graph, executed op by op with the oracle's
 ops and the views honoured (a producer writes its channel range of the root
 buffer, a consumer reads its range), gives exactly the unlowered graph's
 outputs; and the views are well formed."""
@@ -56,9 +56,10 @@ def run_with_views(g, feeds):
 
 def test_views_pass_yolov8n_equals_unlowered():
     g0 = G.yolov8n(batch=1, size=320, seed=8, head="detect")
-    g = G.lower_concat_views_i8(G.lower_im2col_input_i8(g0))
+    g = G.lower_concat_views_i8(G.fuse_residual_i8(G.lower_im2col_input_i8(g0)))
     kinds = [op.op_type for op in g.ops]
     assert kinds.count("Split") == 0 and kinds.count("Concat") == 4  # C2f and SPPF concats are views now
+    assert kinds.count("Conv2dAddI8") == 2 and kinds.count("AddQuantized") == 4  # c_out 16 and 128 bottlenecks
     for t, (parent, off) in g.views.items():
         assert off % 16 == 0 and off + g.tensors[t].shape[3] <= g.tensors[parent].shape[3]
         assert g.tensors[t].shape[:3] == g.tensors[parent].shape[:3]
