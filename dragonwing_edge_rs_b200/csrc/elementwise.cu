@@ -226,6 +226,59 @@ __global__ void k_im2col_u8_i8(const uint8_t *__restrict__ x, int8_t *__restrict
     }
 }
 
+// The 3-channel 3x3 stem (c_dst = 32, image width a multiple of 16): one block
+// per output row.  The block quantises the three input rows it reads into
+// shared memory once (16-byte loads, the same table), input byte e of a row at
+// shared byte 16 + e with zeros around it (the padding, and rows outside the
+// image); an output pixel's 27 bytes are then three runs of 9 bytes, taps
+// (a, 0..2) x channels of row a being contiguous in the input row, read as
+// three aligned words per row and packed into 8 words (the last 5 bytes 0).
+__global__ void k_im2col_stem3_rows(const uint8_t *__restrict__ x, int8_t *__restrict__ y, int h, int w, int sh,
+                                    int sw, int pt, int pl, int ho, int wo, int row_bytes, float inv255, float inv) {
+    extern __shared__ __align__(16) uint8_t rows[];  // [3][row_bytes], row_bytes a multiple of 16
+    __shared__ int8_t lut[256];
+    for (int u = threadIdx.x; u < 256; u += blockDim.x)
+        lut[u] = (int8_t)f32_to_i8(__fmul_rn(__fmul_rn(i2f_small(u), inv255), inv));
+    __syncthreads();
+    const int oi = blockIdx.x % ho, b = blockIdx.x / ho;
+    const int units = row_bytes / 16, data_units = w * 3 / 16;
+    for (int t = threadIdx.x; t < 3 * units; t += blockDim.x) {
+        const int a = t / units, u = t % units;
+        const int ih = oi * sh - pt + a;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (u >= 1 && u <= data_units && ih >= 0 && ih < h) {
+            const uint4 s = __ldg(reinterpret_cast<const uint4 *>(x + ((size_t)b * h + ih) * w * 3) + (u - 1));
+            const uint32_t sw4[4] = {s.x, s.y, s.z, s.w};
+            uint32_t q[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                q[k] = (uint32_t)(uint8_t)lut[sw4[k] & 0xff] | (uint32_t)(uint8_t)lut[(sw4[k] >> 8) & 0xff] << 8 |
+                       (uint32_t)(uint8_t)lut[(sw4[k] >> 16) & 0xff] << 16 | (uint32_t)(uint8_t)lut[sw4[k] >> 24] << 24;
+            v = make_uint4(q[0], q[1], q[2], q[3]);
+        }
+        *reinterpret_cast<uint4 *>(rows + a * row_bytes + u * 16) = v;
+    }
+    __syncthreads();
+    int8_t *yrow = y + ((size_t)b * ho + oi) * wo * 32;
+    for (int j = threadIdx.x; j < wo; j += blockDim.x) {
+        const int s0 = 16 + (j * sw - pl) * 3;  // first of the 9 bytes, >= 16 - 3 * pl >= 1
+        const int base = s0 & ~3, sh8 = (s0 & 3) * 8;
+        uint32_t r[3][3];
+#pragma unroll
+        for (int a = 0; a < 3; a++) {
+            const uint32_t *wp = reinterpret_cast<const uint32_t *>(rows + a * row_bytes + base);
+            const uint32_t w0 = wp[0], w1 = wp[1], w2 = wp[2];
+            r[a][0] = __funnelshift_r(w0, w1, sh8);
+            r[a][1] = __funnelshift_r(w1, w2, sh8);
+            r[a][2] = (w2 >> sh8) & 0xffu;
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(yrow + (size_t)j * 32);
+        dst[0] = make_uint4(r[0][0], r[0][1], r[0][2] | r[1][0] << 8, r[1][0] >> 24 | r[1][1] << 8);
+        dst[1] = make_uint4(r[1][1] >> 24 | r[1][2] << 8 | r[2][0] << 16, r[2][0] >> 16 | r[2][1] << 16,
+                            r[2][1] >> 16 | r[2][2] << 16, 0u);
+    }
+}
+
 // --- dequantize: ops.rs:3453-3457 ---------------------------------------------
 __global__ void k_dequantize(const int8_t *__restrict__ in, float *__restrict__ out, size_t n, float s) {
     size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
@@ -547,6 +600,18 @@ dw_status launch_quantize_u8(dw_backend *be, const uint8_t *in, int8_t *out, siz
 dw_status launch_im2col_u8_i8(dw_backend *be, const uint8_t *x, int8_t *y, int n, int h, int w, int c, int kh, int kw,
                               int sh, int sw, int pt, int pl, int ho, int wo, int c_dst, float scale) {
     const float inv255 = 1.0f / 255.0f, inv = 1.0f / scale;
+    if (c == 3 && kh == 3 && kw == 3 && c_dst == 32 && w % 16 == 0 && ((uintptr_t)x & 15) == 0 && pl >= 0 &&
+        pl <= 5 && (long long)n * ho < (1LL << 31)) {
+        // row-staged kernel: each row holds the input row at byte 16 and covers the last pixel's reads
+        const long long last = 16 + ((long long)(wo - 1) * sw - pl) * 3 + 12;
+        const long long need = std::max<long long>(16 + (long long)w * 3, last);
+        const long long row_bytes = (need + 15) / 16 * 16;
+        if (3 * row_bytes <= 40 * 1024) {
+            k_im2col_stem3_rows<<<n * ho, kThreads, (size_t)(3 * row_bytes), be->stream>>>(
+                x, y, h, w, sh, sw, pt, pl, ho, wo, (int)row_bytes, inv255, inv);
+            return dw_after_launch(be, "im2col_u8_i8");
+        }
+    }
     const int grid = grid_for(be, (size_t)n * ho * wo);
     if (c == 3 && kh == 3 && kw == 3)  // the usual image stem
         k_im2col_u8_i8<3, 3, 3><<<grid, kThreads, 0, be->stream>>>(x, y, n, h, w, c, kh, kw, sh, sw, pt, pl, ho, wo,

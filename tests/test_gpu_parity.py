@@ -352,7 +352,11 @@ def test_depthwise_requant_ties_and_slow_channels(be, be_dwv, epi):
 
 
 @pytest.mark.parametrize("geo", [(2, 64, 48, 3, 3, 3, 2, 2, 1, 1, 32), (1, 17, 9, 3, 3, 3, 1, 1, 1, 1, 32),
-                                 (1, 20, 20, 5, 2, 3, 2, 1, 0, 1, 32), (1, 30, 30, 3, 7, 3, 2, 2, 3, 3, 64)])
+                                 (1, 20, 20, 5, 2, 3, 2, 1, 0, 1, 32), (1, 30, 30, 3, 7, 3, 2, 2, 3, 3, 64),
+                                 # the row-staged stem kernel (width a multiple of 16): no padding, odd height,
+                                 # stride 1, the YOLOv8n stem
+                                 (1, 16, 32, 3, 3, 3, 2, 2, 0, 0, 32), (3, 33, 32, 3, 3, 3, 2, 2, 1, 1, 32),
+                                 (1, 18, 16, 3, 3, 3, 1, 1, 1, 1, 32), (2, 640, 640, 3, 3, 3, 2, 2, 1, 1, 32)])
 def test_im2col_u8_to_i8(be, geo):
     """Quantise + im2col of a uint8 image (the input conv's device lowering) is
     bit-exact against quantize_u8_to_i8 followed by the gather."""
