@@ -138,6 +138,7 @@ SIGNATURES = {
     "dw_add_i8_view": ([vp, ctypes.POINTER(DwView), ctypes.POINTER(DwView), ctypes.POINTER(DwView), sz, sz, f32, f32],
                        i32),
     "dw_maxpool_i8_view": ([vp, ctypes.POINTER(DwView), ctypes.POINTER(DwView)] + [sz] * 12, i32),
+    "dw_maxpool_chain_i8_view": ([vp, ctypes.POINTER(DwView), ctypes.POINTER(DwView), i32] + [sz] * 5, i32),
     # YOLOv8 Detect tail and post-processing
     "dw_prepare_yolo_detect": ([vp, ctypes.POINTER(DwYoloDetectDesc), PVP], i32),
     "dw_yolo_detect_i8": ([vp, ctypes.POINTER(DwYoloDetectDesc), vp, PVP, PVP, vp], i32),

@@ -110,6 +110,8 @@ dw_status launch_add_i8_view(dw_backend *be, const int8_t *a, int a_pitch, const
                              int out_pitch, size_t pixels, int c, float ra, float rb);
 dw_status launch_maxpool_i8_view(dw_backend *be, const int8_t *x, int x_pitch, int8_t *y, int y_pitch, int n, int h,
                                  int w, int c, int kh, int kw, int sh, int sw, int pt, int pl, int ho, int wo);
+dw_status launch_maxpool_chain_i8_view(dw_backend *be, const int8_t *x, int x_pitch, int8_t *const *ys,
+                                       const int *y_pitches, int count, int n, int h, int w, int c, int k);
 dw_status launch_umma_conv_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,
                               const int8_t *w_ohwi, const EpiParams &ep, int8_t *y);
 dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const uint16_t *x,

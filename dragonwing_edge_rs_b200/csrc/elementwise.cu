@@ -481,6 +481,51 @@ __global__ void k_maxpool_i8_v16(const int8_t *__restrict__ x, int8_t *__restric
     }
 }
 
+// `count` chained k x k stride-1 maxpools with k/2 padding (the padding taps
+// skipped), the SPPF block's y1 = pool(x), y2 = pool(y1), y3 = pool(y2): one
+// block per (image, 16-channel group) keeps the map in shared memory and pools
+// it separably (a clipped window is a rectangle, and max is associative and
+// commutative, so the row maxima's column maximum is the window maximum), writing
+// each pooled map out as it goes.  x is read once instead of pooled maps being
+// re-read from memory.
+__global__ void k_maxpool_chain_i8(const int8_t *__restrict__ x, int x_pitch, int8_t *__restrict__ y0, int8_t *__restrict__ y1,
+                                   int8_t *__restrict__ y2, int8_t *__restrict__ y3, int p0, int p1, int p2, int p3,
+                                   int count, int h, int w, int groups, int r) {
+    extern __shared__ __align__(16) uint4 maps[];  // [2][h * w]: the current map, the row maxima
+    const int hw = h * w, b = blockIdx.x / groups, g = blockIdx.x % groups;
+    uint4 *cur = maps, *rowm = maps + hw;
+    for (int p = threadIdx.x; p < hw; p += blockDim.x)
+        cur[p] = __ldg(reinterpret_cast<const uint4 *>(x + ((size_t)b * hw + p) * x_pitch + g * 16));
+    __syncthreads();
+    int8_t *const outs[4] = {y0, y1, y2, y3};
+    const int pitches[4] = {p0, p1, p2, p3};
+    for (int s = 0; s < count; s++) {
+        for (int p = threadIdx.x; p < hw; p += blockDim.x) {  // maxima along each row
+            const int oh = p / w, ow = p % w;
+            const int q0 = max(0, ow - r), q1 = min(w - 1, ow + r);
+            uint4 m = cur[oh * w + q0];
+            for (int q = q0 + 1; q <= q1; q++) {
+                const uint4 v = cur[oh * w + q];
+                m.x = __vmaxs4(m.x, v.x); m.y = __vmaxs4(m.y, v.y); m.z = __vmaxs4(m.z, v.z); m.w = __vmaxs4(m.w, v.w);
+            }
+            rowm[p] = m;
+        }
+        __syncthreads();
+        for (int p = threadIdx.x; p < hw; p += blockDim.x) {  // then along each column
+            const int oh = p / w, ow = p % w;
+            const int a0 = max(0, oh - r), a1 = min(h - 1, oh + r);
+            uint4 m = rowm[a0 * w + ow];
+            for (int a = a0 + 1; a <= a1; a++) {
+                const uint4 v = rowm[a * w + ow];
+                m.x = __vmaxs4(m.x, v.x); m.y = __vmaxs4(m.y, v.y); m.z = __vmaxs4(m.z, v.z); m.w = __vmaxs4(m.w, v.w);
+            }
+            cur[p] = m;
+            *reinterpret_cast<uint4 *>(outs[s] + ((size_t)b * hw + p) * pitches[s] + g * 16) = m;
+        }
+        __syncthreads();
+    }
+}
+
 // --- weight repacks (int8 and fp16 element types) ------------------------------------------------------------
 // HWIO [taps][c_in][c_out] -> OHWI [c_out][taps][c_in] (K-major rows for the MMA B operand).
 template <typename T>
@@ -583,6 +628,33 @@ dw_status launch_maxpool_i8_view(dw_backend *be, const int8_t *x, int x_pitch, i
         x, y, h, w, c, kh, kw, sh, sw, pt, pl, (uint32_t)groups16, make_fastdiv((uint32_t)(c / 16)),
         make_fastdiv((uint32_t)wo), make_fastdiv((uint32_t)ho), x_pitch, y_pitch);
     return dw_after_launch(be, "maxpool_i8");
+}
+
+dw_status launch_maxpool_chain_i8_view(dw_backend *be, const int8_t *x, int x_pitch, int8_t *const *ys,
+                                       const int *y_pitches, int count, int n, int h, int w, int c, int k) {
+    bool aligned = !((uintptr_t)x & 15) && x_pitch % 16 == 0;
+    for (int i = 0; i < count; i++) aligned = aligned && !((uintptr_t)ys[i] & 15) && y_pitches[i] % 16 == 0;
+    if (c % 16 || !aligned || count < 1 || count > 4 || k % 2 == 0)
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "maxpool_chain_i8_view: needs 16-channel multiples, 16-byte alignment, "
+                                               "1..4 pools and an odd window");
+    const size_t smem = (size_t)2 * h * w * 16;
+    if (smem <= 48 * 1024 && (long long)n * (c / 16) < (1LL << 31)) {
+        int8_t *y[4] = {ys[0], count > 1 ? ys[1] : nullptr, count > 2 ? ys[2] : nullptr, count > 3 ? ys[3] : nullptr};
+        int pp[4] = {y_pitches[0], count > 1 ? y_pitches[1] : 0, count > 2 ? y_pitches[2] : 0,
+                     count > 3 ? y_pitches[3] : 0};
+        k_maxpool_chain_i8<<<n * (c / 16), kThreads, smem, be->stream>>>(x, x_pitch, y[0], y[1], y[2], y[3], pp[0],
+                                                                           pp[1], pp[2], pp[3], count, h, w, c / 16,
+                                                                           k / 2);
+        return dw_after_launch(be, "maxpool_chain_i8");
+    }
+    // larger maps: one pooling launch per step, each reading the previous output
+    const int r = k / 2;
+    for (int i = 0; i < count; i++) {
+        const dw_status st = launch_maxpool_i8_view(be, i ? ys[i - 1] : x, i ? y_pitches[i - 1] : x_pitch, ys[i],
+                                                    y_pitches[i], n, h, w, c, k, k, 1, 1, r, r, h, w);
+        if (st != DW_OK) return st;
+    }
+    return DW_OK;
 }
 
 dw_status launch_quantize_f32(dw_backend *be, const float *in, int8_t *out, size_t n, float scale) {

@@ -479,6 +479,26 @@ DW_API dw_status dw_maxpool_i8_view(dw_backend *be, const dw_view *x, const dw_v
                                       (int)k_h, (int)k_w, (int)s_h, (int)s_w, (int)p_t, (int)p_l, (int)ho, (int)wo);
 }
 
+DW_API dw_status dw_maxpool_chain_i8_view(dw_backend *be, const dw_view *x, const dw_view *ys, int32_t count, size_t n,
+                                          size_t h, size_t w, size_t c, size_t k) {
+    const char *op = "maxpool_chain_i8_view";
+    if (!be) return DW_ERR_INVALID_ARG;
+    if (!ys || count < 1 || count > 4 || !n || !h || !w || !c || k % 2 == 0 || k > 255 ||
+        n * h * w >= ((size_t)1 << 31) || c > 65536)
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: invalid geometry (1..4 pools, odd k)", op);
+    DW_TRY(check_view(be, x, n * h * w, c, op, "input"));
+    int8_t *yp[4];
+    int pitches[4];
+    for (int i = 0; i < count; i++) {
+        DW_TRY(check_view(be, &ys[i], n * h * w, c, op, "output"));
+        yp[i] = (int8_t *)ys[i].buf->ptr + ys[i].offset;
+        pitches[i] = ys[i].pitch;
+    }
+    cudaSetDevice(be->device);
+    return dw::launch_maxpool_chain_i8_view(be, (const int8_t *)x->buf->ptr + x->offset, x->pitch, yp, pitches, count,
+                                            (int)n, (int)h, (int)w, (int)c, (int)k);
+}
+
 DW_API dw_status dw_concat_i8(dw_backend *be, const dw_buf *const *xs, const int32_t *channels, int32_t count,
                               size_t pixels, dw_buf *y) {
     if (!be) return DW_ERR_INVALID_ARG;

@@ -519,6 +519,45 @@ def fuse_residual_i8(graph: Graph) -> Graph:
     return Graph(tensors, out_ops, dict(graph.initializers), list(graph.inputs), list(graph.outputs), dict(graph.views))
 
 
+def fuse_maxpool_chain_i8(graph: Graph) -> Graph:
+    """Device pass: a run of 2..4 int8 MaxPools, each k x k (k odd), stride 1,
+    padding k/2, each reading the previous one's output (YOLOv8's SPPF: three
+    5x5 pools in a row), becomes one MaxPoolChainI8 that writes every pooled
+    map (dw_maxpool_chain_i8_view: the input is read once, the pooling steps
+    are the same maxima).  The intermediate maps stay outputs of the fused op,
+    so their other readers (the SPPF concat) are unchanged."""
+    ops_ = list(graph.ops)
+
+    def same_pool(op):
+        p = op.params
+        return op.op_type == "MaxPool" and p["s"] == 1 and p["k"] % 2 == 1 and p["pad"] == p["k"] // 2
+
+    readers = {}
+    for op in ops_:
+        for i in op.inputs:
+            readers.setdefault(i, []).append(op)
+    chained, head_of = set(), {}
+    for op in ops_:
+        if not same_pool(op) or id(op) in chained or graph.tensors[op.inputs[0]].shape[3] % 16:
+            continue
+        run = [op]
+        while len(run) < 4:
+            nxt = [q for q in readers.get(run[-1].outputs[0], []) if same_pool(q) and q.params["k"] == op.params["k"]]
+            if len(nxt) != 1 or id(nxt[0]) in chained:
+                break
+            run.append(nxt[0])
+        if len(run) < 2:
+            continue
+        chained.update(id(q) for q in run)
+        head_of[id(op)] = CompiledOp("+".join(q.name for q in run), "MaxPoolChainI8", [op.inputs[0]],
+                                     [q.outputs[0] for q in run], {"k": op.params["k"]})
+    if not head_of:
+        return graph
+    out_ops = [head_of.get(id(op), op) for op in ops_ if id(op) in head_of or id(op) not in chained]
+    return Graph(dict(graph.tensors), out_ops, dict(graph.initializers), list(graph.inputs), list(graph.outputs),
+                 dict(graph.views))
+
+
 def lower_concat_views_i8(graph: Graph) -> Graph:
     """Device lowering of int8 channel concats: when every input of a Concat is
     written by an op that can write a channel-range view (a tensor-core conv,
@@ -549,14 +588,14 @@ def lower_concat_views_i8(graph: Graph) -> Graph:
     def can_write(op):
         if op.op_type == "Conv2dRequantReluI8Nhwc":
             return tc_conv(op)
-        return op.op_type in ("AddQuantized", "MaxPool", "Conv2dAddI8")
+        return op.op_type in ("AddQuantized", "MaxPool", "Conv2dAddI8", "MaxPoolChainI8")
 
     def can_read(op, t):
         if op.op_type in ("Conv2dRequantReluI8Nhwc", "Conv2dAddI8"):
             if op.op_type == "Conv2dAddI8" and op.inputs[5] == t and op.inputs[0] != t:
                 return True  # the residual
             return tc_conv(op) and op.inputs[0] == t and op.params["desc"].stride_w == 1
-        return op.op_type in ("AddQuantized", "MaxPool")
+        return op.op_type in ("AddQuantized", "MaxPool", "MaxPoolChainI8")
 
     for cat in ops_:
         if cat.op_type != "Concat" or cat.outputs[0] in protected:
@@ -605,7 +644,7 @@ def lower_for_device(graph: Graph, residual_i8: bool = False) -> Graph:
     """The device passes: fp16 residual fusion, the input-conv unfold / im2col,
     int8 residual fusion (opt-in, `residual_i8`: on YOLOv8n at batch 32 the
     two pairs it takes are faster per kernel, yet the whole step measured
-    2.177 ms against 2.159 without it), then concat views."""
+    2.177 ms against 2.159 without it), chained maxpools, then concat views."""
     if any(op.op_type == "AddF16" for op in graph.ops):
         graph = fuse_residual_f16(graph)
     if any(op.op_type == "CastF32ToF16" for op in graph.ops):
@@ -614,6 +653,8 @@ def lower_for_device(graph: Graph, residual_i8: bool = False) -> Graph:
         graph = lower_im2col_input_i8(graph)
     if residual_i8 and any(op.op_type == "AddQuantized" for op in graph.ops):
         graph = fuse_residual_i8(graph)
+    if sum(op.op_type == "MaxPool" for op in graph.ops) > 1:
+        graph = fuse_maxpool_chain_i8(graph)
     if any(op.op_type == "Concat" for op in graph.ops):
         graph = lower_concat_views_i8(graph)
     return graph
@@ -845,6 +886,12 @@ class CudaGraphRuntime:
                 return lambda: ops.add_i8_view(be, al[:3], bl[:3], ol[:3], n * h * w, c, ra, rb)
             a, b_, y = al[0], bl[0], ol[0]
             return lambda: ops.add_i8_packed(be, a, b_, y, ra, rb)
+        if t == "MaxPoolChainI8":
+            n, h, w, c = self.graph.tensors[op.inputs[0]].shape
+            xl = self._loc(op.inputs[0])
+            yls = [self._loc(o)[:3] for o in op.outputs]
+            k = op.params["k"]
+            return lambda: ops.maxpool_chain_i8_view(be, xl[:3], yls, n, h, w, c, k)
         if t == "MaxPool":
             n, h, w, c = self.graph.tensors[op.inputs[0]].shape
             k, s, p = op.params["k"], op.params["s"], op.params["pad"]

@@ -184,6 +184,14 @@ def add_i8_view(backend, a, b, out, pixels, c, ra, rb):
                                            pixels, c, float(ra), float(rb)))
 
 
+def maxpool_chain_i8_view(backend, x, ys, n, h, w, c, k):
+    """len(ys) chained k x k stride-1 maxpools with k/2 padding: ys[0] = pool(x), ys[i] = pool(ys[i-1]); the
+    tensors as (buffer, byte offset, pixel pitch) views."""
+    xv = _view(x)
+    arr = (L.DwView * len(ys))(*[_view(v) for v in ys])
+    backend._check(L.load().dw_maxpool_chain_i8_view(backend.handle, ctypes.byref(xv), arr, len(ys), n, h, w, c, k))
+
+
 def maxpool_i8_view(backend, x, y, n, h, w, c, k_h, k_w, s_h, s_w, pads):
     xv, yv = _view(x), _view(y)
     pt, pl, pb, pr = pads

@@ -316,6 +316,14 @@ DW_API dw_status dw_add_i8_view(dw_backend *be, const dw_view *a, const dw_view 
 DW_API dw_status dw_maxpool_i8_view(dw_backend *be, const dw_view *x, const dw_view *y, size_t n, size_t h, size_t w,
                                     size_t c, size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t, size_t p_l,
                                     size_t p_b, size_t p_r);
+/* `count` (1..4) chained maxpools of x, each k x k (k odd), stride 1, padding
+ * k/2 on every side with the padded taps skipped (maxpool2d_f32_nhwc,
+ * crates/dragonwing-cpu/src/ops.rs:1513-1551, as YOLOv8's SPPF block runs it
+ * three times in a row): ys[0] = pool(x), ys[i] = pool(ys[i-1]), all [n, h, w,
+ * c] views (c a multiple of 16).  Identical to `count` dw_maxpool_i8_view
+ * calls; x is read once. */
+DW_API dw_status dw_maxpool_chain_i8_view(dw_backend *be, const dw_view *x, const dw_view *ys, int32_t count, size_t n,
+                                          size_t h, size_t w, size_t c, size_t k);
 
 /* ---------------------------------------------------------------------- */
 /* YOLOv8 Detect head tail and detection post-processing                   */

@@ -75,6 +75,14 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
             a, b = vals[op.inputs[0]], vals[op.inputs[1]]
             y = dwref.add_i8(a, b, op.params["scale_a_over_out"], op.params["scale_b_over_out"])
             vals[op.outputs[0]] = y.reshape(a.shape)
+        elif t == "MaxPoolChainI8":  # device fusion of chained stride-1 MaxPools (SPPF)
+            x = vals[op.inputs[0]]
+            n, h, w, c = x.shape
+            k = op.params["k"]
+            p = k // 2
+            for o in op.outputs:
+                x = dwref.maxpool_i8(x, n, h, w, c, k, k, 1, 1, (p, p, p, p)).reshape(n, h, w, c)
+                vals[o] = x
         elif t == "MaxPool":
             x = vals[op.inputs[0]]
             n, h, w, c = x.shape

@@ -150,3 +150,27 @@ def test_maxpool_i8_view(be, n, h, w, c, k, s, p):
     check_out(be, by, n * ho * wo, c, yp, 2 * c, exp)
     for buf in (bx, by):
         buf.free()
+
+
+@pytest.mark.parametrize("n,h,w,c,k,count", [(2, 20, 20, 128, 5, 3),   # YOLOv8n SPPF at 640x640
+                                             (1, 40, 48, 32, 5, 3),    # a map too large for one block: separate pools
+                                             (3, 7, 5, 16, 3, 2), (1, 4, 4, 16, 9, 1), (2, 9, 11, 48, 5, 4)])
+def test_maxpool_chain_i8_view(be, n, h, w, c, k, count):
+    """Chained k x k stride-1 pools (padding k/2) into views of one wider
+    tensor, as SPPF's concat: identical to pooling the previous output."""
+    rng = np.random.default_rng(n * h * w + c + k)
+    pix, p = n * h * w, k // 2
+    x = rng.integers(-128, 128, pix * c).astype(np.int8)
+    pitch = (count + 1) * c
+    bx = be.upload_array(embed(rng, x, pix, c, pitch, 0))
+    by = view_out(be, pix, pitch)
+    ops.maxpool_chain_i8_view(be, (bx, 0, pitch), [(by, (i + 1) * c, pitch) for i in range(count)], n, h, w, c, k)
+    got = be.download_array(by, np.int8).reshape(pix, pitch)
+    assert (got[:, :c] == SENTINEL).all()
+    cur = x
+    for i in range(count):
+        cur = dwref.maxpool_i8(cur, n, h, w, c, k, k, 1, 1, (p, p, p, p)).reshape(-1)
+        seg = np.ascontiguousarray(got[:, (i + 1) * c:(i + 2) * c]).reshape(-1)
+        assert np.array_equal(seg, cur), (i, mismatch_report(seg, cur))
+    for buf in (bx, by):
+        buf.free()

@@ -56,8 +56,9 @@ def run_with_views(g, feeds):
 
 def test_views_pass_yolov8n_equals_unlowered():
     g0 = G.yolov8n(batch=1, size=320, seed=8, head="detect")
-    g = G.lower_concat_views_i8(G.fuse_residual_i8(G.lower_im2col_input_i8(g0)))
+    g = G.lower_concat_views_i8(G.fuse_maxpool_chain_i8(G.fuse_residual_i8(G.lower_im2col_input_i8(g0))))
     kinds = [op.op_type for op in g.ops]
+    assert kinds.count("MaxPoolChainI8") == 1 and kinds.count("MaxPool") == 0  # SPPF
     assert kinds.count("Split") == 0 and kinds.count("Concat") == 4  # C2f and SPPF concats are views now
     assert kinds.count("Conv2dAddI8") == 2 and kinds.count("AddQuantized") == 4  # c_out 16 and 128 bottlenecks
     for t, (parent, off) in g.views.items():
