@@ -55,17 +55,23 @@ __device__ __forceinline__ uint32_t f32_to_i8_byte_nonan(float v) {
 // ---- SiLU fast path with a certified result -------------------------------
 // t = fl(fl(y * fl(1/fl(1 + exp(-y)))) * inv_s_out) computed with the PTX
 // approximations ex2.approx / rcp.approx instead of the exact exp and division.
-// Error analysis (relative error of t_fast against the exact chain):
-//   * exp(-y) = 2^(y * -log2(e)): the argument is one RN product (relative error
-//     <= 1.5 * 2^-24, i.e. <= 2.2e-6 absolute for |y| <= 17), and ex2.approx adds
-//     ~2^-22.5; for |y| <= 17 this is <= 2e-6 relative in e;
-//   * for y > 17, e < 2^-24.5 so 1 + e rounds to 1 (or its neighbour) either way;
-//     for y < -17, |t| < 1e-4 * |inv_s_out| / 100 is far from any rounding boundary;
-//   * the remaining ops (1 + e, the reciprocal, two products) add a few 2^-24 each.
-// So |t_fast - t| <= 2^-17 * |t| with a margin of about 3x.  The int8 result of
-// t_fast is certified when no rounding boundary (a half-integer) lies within
-// that distance; otherwise the caller recomputes the element exactly.
-constexpr float kSiluRelErr = 7.62939453125e-06f;  // 2^-17
+// Relative error of t_fast against the reference's t (first order; every term
+// taken generously):
+//   * exp(-y) = 2^(y * -log2(e)): the RN product and the f32 constant put a
+//     relative error of at most 1.5 * 2^-24 on the exponent y * log2(e), which
+//     moves e by at most |y| * 1.5 * 2^-24 relative (log2(e) * ln(2) = 1);
+//   * ex2.approx: at most 2^-21 (4 ulp); rcp.approx: at most 2^-22; the
+//     reference's own expf: at most 2^-23; six RN roundings (1 + e, y * sig and
+//     the scaling, on each side): 6 * 2^-24;
+//   * a relative error r in e moves 1 + e, and so sig, by at most r relative;
+//     when e overflows (y < -88) both sides give sig = 0 and t = -0.
+// So |t_fast - t| <= |t| * (|y| * 8.9e-8 + 1.19e-6); the certificate takes
+// three times that.  The int8 result of t_fast is certified when no rounding
+// boundary (a half-integer) lies within that distance; otherwise the caller
+// recomputes the element exactly.  A tighter certificate matters: a warp takes
+// the exact path when any of its 512 elements is uncertain.
+constexpr float kSiluErrPerY = 2.7e-7f;  // 3 * 1.5 * 2^-24 (rounded up)
+constexpr float kSiluErr0 = 3.6e-6f;     // 3 * (2^-21 + 2^-22 + 2^-23 + 6 * 2^-24) (rounded up)
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float r;
@@ -90,7 +96,7 @@ __device__ __forceinline__ uint32_t silu_fast_bits(float fa, float dsc, float in
     const float c = fminf(fmaxf(t, -128.0f), 127.0f);
     const float r = __fadd_rn(c, kMagic);
     const float d = fabsf(__fsub_rn(c, __fsub_rn(r, kMagic)));
-    uncertain |= !(__fsub_rn(0.5f, d) > __fmul_rn(fabsf(t), 2.0f * kSiluRelErr));
+    uncertain |= !(__fsub_rn(0.5f, d) > __fmul_rn(fabsf(t), __fmaf_rn(fabsf(y), kSiluErrPerY, kSiluErr0)));
     return __float_as_uint(r);
 }
 
