@@ -100,6 +100,26 @@ __device__ __forceinline__ uint32_t silu_fast_bits(float fa, float dsc, float in
     return __float_as_uint(r);
 }
 
+// silu_fast_bits for two accumulators (|a| < 2^22) at once, the arithmetic on
+// f32 pairs: each lane of a packed operation is the same RN operation, so the
+// error bound and the certificate are those of silu_fast_bits.
+__device__ __forceinline__ void silu_fast_bits2(int32_t a0, int32_t a1, float d0, float d1, float inv, uint32_t &b0,
+                                                uint32_t &b1, bool &u0, bool &u1) {
+    const float2 mag = make_float2(kMagic, kMagic), nmag = make_float2(-kMagic, -kMagic);
+    const float2 fa = __fadd2_rn(make_float2(__int_as_float(a0 + kMagicBits), __int_as_float(a1 + kMagicBits)), nmag);
+    const float2 y = __fmul2_rn(fa, make_float2(d0, d1));
+    const float2 arg = __fmul2_rn(y, make_float2(-1.44269502162933349609375f, -1.44269502162933349609375f));
+    const float2 onep = __fadd2_rn(make_float2(ex2_approx(arg.x), ex2_approx(arg.y)), make_float2(1.0f, 1.0f));
+    const float2 t = __fmul2_rn(__fmul2_rn(y, make_float2(rcp_approx(onep.x), rcp_approx(onep.y))), make_float2(inv, inv));
+    const float2 c = make_float2(fminf(fmaxf(t.x, -128.0f), 127.0f), fminf(fmaxf(t.y, -128.0f), 127.0f));
+    const float2 r = __fadd2_rn(c, mag);
+    const float2 d = __ffma2_rn(__fadd2_rn(r, nmag), make_float2(-1.0f, -1.0f), c);  // c - rint(c), exact
+    u0 |= !(__fsub_rn(0.5f, fabsf(d.x)) > __fmul_rn(fabsf(t.x), __fmaf_rn(fabsf(y.x), kSiluErrPerY, kSiluErr0)));
+    u1 |= !(__fsub_rn(0.5f, fabsf(d.y)) > __fmul_rn(fabsf(t.y), __fmaf_rn(fabsf(y.y), kSiluErrPerY, kSiluErr0)));
+    b0 = __float_as_uint(r.x);
+    b1 = __float_as_uint(r.y);
+}
+
 // The fused epilogue for one accumulator (contract in include/dw_cuda.h):
 // every float operation is a separately rounded IEEE op, as in the reference
 // (Rust does not contract a*b+c), so the result is bit-exact.

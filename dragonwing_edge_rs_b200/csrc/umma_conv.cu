@@ -269,10 +269,11 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
             for (int q = 0; q < 4; q++) {
                 uint32_t bq[4];
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    bool u = false;
-                    bq[j] = silu_fast_bits(i2f_small(a[q * 4 + j]), sd[q * 4 + j], p.ep.inv_s_out, u);
-                    unc |= (uint32_t)u << (q * 4 + j);
+                for (int j = 0; j < 4; j += 2) {
+                    bool u0 = false, u1 = false;
+                    silu_fast_bits2(a[q * 4 + j], a[q * 4 + j + 1], sd[q * 4 + j], sd[q * 4 + j + 1], p.ep.inv_s_out,
+                                    bq[j], bq[j + 1], u0, u1);
+                    unc |= ((uint32_t)u0 | (uint32_t)u1 << 1) << (q * 4 + j);
                 }
                 w[q] = __byte_perm(__byte_perm(bq[0], bq[1], 0x0040), __byte_perm(bq[2], bq[3], 0x0040), 0x5410);
             }
