@@ -86,6 +86,7 @@ SIGNATURES = {
     "dw_stream": ([vp], vp),
     "dw_sm_count": ([vp], i32),
     "dw_launch_count": ([vp], ctypes.c_uint64),
+    "dw_scratch_bytes": ([vp], ctypes.c_size_t),
     "dw_debug_expire_wait": ([vp, u32], i32),
     "dw_capture_begin": ([vp], i32),
     "dw_capture_end": ([vp, PVP], i32),

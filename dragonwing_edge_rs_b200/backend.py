@@ -192,6 +192,10 @@ class CudaBackend:
     def launch_count(self) -> int:
         return int(self._lib.dw_launch_count(self.handle))
 
+    def scratch_bytes(self) -> int:
+        """Device scratch the backend holds (grown by ops that need temporaries)."""
+        return int(self._lib.dw_scratch_bytes(self.handle))
+
     def last_error(self) -> str:
         return self._lib.dw_last_error(self.handle).decode(errors="replace")
 

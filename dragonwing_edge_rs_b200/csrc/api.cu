@@ -315,6 +315,7 @@ DW_API dw_status dw_host_free(dw_backend *be, void *ptr) {
 DW_API void *dw_stream(dw_backend *be) { return be ? (void *)be->stream : nullptr; }
 DW_API int dw_sm_count(const dw_backend *be) { return be ? be->sm_count : 0; }
 DW_API uint64_t dw_launch_count(const dw_backend *be) { return be ? be->launches : 0; }
+DW_API size_t dw_scratch_bytes(const dw_backend *be) { return be ? be->scratch_len : 0; }
 
 struct dw_graph {
     cudaGraph_t graph = nullptr;

@@ -56,6 +56,9 @@ dw_status dw_cuda_check(dw_backend *be, cudaError_t e, const char *what);
 dw_status dw_after_launch(dw_backend *be, const char *what);
 // Grows (never shrinks) the backend scratch to at least `len` bytes.
 dw_status dw_scratch(dw_backend *be, size_t len, void **out);
+// Validates a conv descriptor (positive dims, non-negative pads, the kernel
+// within the padded input, supported group and epilogue); computes the output dims.
+dw_status dw_check_conv_desc(dw_backend *be, const dw_conv_desc *d, int *ho, int *wo, const char *op);
 
 // ---- launchers implemented in the kernel translation units ----
 namespace dw {

@@ -15,14 +15,18 @@
 // that lives in the library instead, and calls no allocator.
 //
 // The array (kNoAllocBytes) is a file-scope __device__ variable: every GPU that
-// loads this library holds it until the process exits.  Its device address is
-// looked up once per device with cudaGetSymbolAddress (a host-side use of the
-// variable's name is only a stand-in, not a device address); the first call on
-// a device does that look-up, so make that first call before any stream
-// capture begins on the device.  All calls on a device share the array and every
-// call fully rewrites the part it uses (no state carries over); calls whose
-// kernels overlap on the GPU (different streams or backends on one device)
-// race on it and must be serialised by the caller.
+// loads this library holds it until the process exits.  Host code cannot use the
+// variable's name as a device address (on the host it names a stand-in), so the
+// address is looked up with cudaGetSymbolAddress, with the device current, and
+// cached per device together with the unique ID of the CUDA context it belongs
+// to.  A later call in another context of that device (after cudaDeviceReset, or
+// a reset of the primary context) sees a different ID and looks the address up
+// again, so no stale address is ever used.  The first call on a device (and the
+// first after such a reset) does that look-up: make it before any stream capture
+// begins on the device.  All calls on a device share the array and every call
+// fully rewrites the part it uses (no state carries over); calls whose kernels
+// overlap on the GPU (different streams or backends on one device) race on it
+// and must be serialised by the caller.
 
 #include <mutex>
 
@@ -37,25 +41,59 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char dw_noalloc_scratch[kNoAllocBytes];
 
-std::mutex g_addr_mu;
-void *g_addr[kMaxDevices] = {};
+using PFN_ctxGetCurrent = CUresult (*)(CUcontext *);
+using PFN_ctxGetId = CUresult (*)(CUcontext, unsigned long long *);
 
-// Device address of dw_noalloc_scratch on the backend's device (looked up once
-// per device, with that device current).
+struct CachedAddress {
+    unsigned long long ctx_id = 0;  // unique ID of the context the address belongs to (0: none yet)
+    void *addr = nullptr;
+};
+
+std::mutex g_addr_mu;
+CachedAddress g_addr[kMaxDevices];
+PFN_ctxGetCurrent g_ctx_get_current = nullptr;
+PFN_ctxGetId g_ctx_get_id = nullptr;
+
+dw_status driver_fn(dw_backend *be, const char *name, void **fn) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint(name, fn, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess ||
+        !*fn)
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "conv_fused_noalloc: driver entry point %s unavailable", name);
+    return DW_OK;
+}
+
+// Device address of dw_noalloc_scratch in the context now current on the
+// backend's device (looked up again whenever that context changes).
 dw_status scratch_address(dw_backend *be, void **out) {
     if (be->device < 0 || be->device >= kMaxDevices)
         return dw_fail(be, DW_ERR_UNSUPPORTED, "conv_fused_noalloc: device ordinal %d out of range", be->device);
     std::lock_guard<std::mutex> lock(g_addr_mu);
-    if (!g_addr[be->device]) {
-        dw_status st = dw_cuda_check(be, cudaSetDevice(be->device), "conv_fused_noalloc: set device");
-        if (st != DW_OK) return st;
+    dw_status st = dw_cuda_check(be, cudaSetDevice(be->device), "conv_fused_noalloc: set device");
+    if (st != DW_OK) return st;
+    if (!g_ctx_get_current) {
+        void *f = nullptr;
+        if ((st = driver_fn(be, "cuCtxGetCurrent", &f)) != DW_OK) return st;
+        g_ctx_get_current = reinterpret_cast<PFN_ctxGetCurrent>(f);
+    }
+    if (!g_ctx_get_id) {
+        void *f = nullptr;
+        if ((st = driver_fn(be, "cuCtxGetId", &f)) != DW_OK) return st;
+        g_ctx_get_id = reinterpret_cast<PFN_ctxGetId>(f);
+    }
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || !ctx || g_ctx_get_id(ctx, &id) != CUDA_SUCCESS || id == 0)
+        return dw_fail(be, DW_ERR_DEVICE, "conv_fused_noalloc: no current CUDA context on device %d", be->device);
+    CachedAddress &c = g_addr[be->device];
+    if (c.ctx_id != id || !c.addr) {
         void *p = nullptr;
         st = dw_cuda_check(be, cudaGetSymbolAddress(&p, dw_noalloc_scratch),
                            "conv_fused_noalloc: cudaGetSymbolAddress(dw_noalloc_scratch)");
         if (st != DW_OK) return st;
-        g_addr[be->device] = p;
+        c.ctx_id = id;
+        c.addr = p;
     }
-    *out = g_addr[be->device];
+    *out = c.addr;
     return DW_OK;
 }
 
@@ -100,8 +138,10 @@ extern "C" DW_API dw_status dw_conv2d_requant_relu_i8_noalloc(dw_backend *be, co
                        "conv_fused_noalloc: kernel of %zu bytes and %zu output channels exceeds the fixed scratch "
                        "(at most %zu bytes of weights and %zu output channels); use dw_conv2d_requant_relu_i8",
                        expected_kernel, c_out, kNoAllocWeightBytes, kNoAllocMaxChannels);
-    if (n > 0x7fffffff || h_in > 0x7fffffff || w_in > 0x7fffffff)
-        return dw_fail(be, DW_ERR_INVALID_ARG, "conv_fused_noalloc: dimension exceeds int32");
+    // Every size the descriptor narrows to int32 (the allocating entry point's
+    // descriptor holds the same fields).
+    for (size_t v : {n, h_in, w_in, c_in, c_out, k_h, k_w, stride_h, stride_w, pad_h, pad_w})
+        if (v > 0x7fffffff) return dw_fail(be, DW_ERR_INVALID_ARG, "conv_fused_noalloc: dimension exceeds int32");
     dw_conv_desc d{};
     d.n = (int32_t)n; d.h = (int32_t)h_in; d.w = (int32_t)w_in; d.c_in = (int32_t)c_in; d.c_out = (int32_t)c_out;
     d.k_h = (int32_t)k_h; d.k_w = (int32_t)k_w; d.stride_h = (int32_t)stride_h; d.stride_w = (int32_t)stride_w;
@@ -109,10 +149,14 @@ extern "C" DW_API dw_status dw_conv2d_requant_relu_i8_noalloc(dw_backend *be, co
     d.group = 1;
     d.epilogue = do_relu ? DW_EPI_RELU : DW_EPI_NONE;
     d.q6 = 127;
+    // The allocating entry point's descriptor checks (zero channels included), same messages.
+    int ho_chk = 0, wo_chk = 0;
+    dw_status st = dw_check_conv_desc(be, &d, &ho_chk, &wo_chk, "conv_fused");
+    if (st != DW_OK) return st;
     const int ho = (int)h_out, wo = (int)w_out;
 
     void *base = nullptr;
-    dw_status st = scratch_address(be, &base);
+    st = scratch_address(be, &base);
     if (st != DW_OK) return st;
     st = dw_cuda_check(be, cudaSetDevice(be->device), "conv_fused_noalloc: set device");
     if (st != DW_OK) return st;

@@ -28,8 +28,10 @@ dw_status check_len(dw_backend *be, const dw_buf *b, size_t expected, const char
         if (_st != DW_OK) return _st; \
     } while (0)
 
+}  // namespace
+
 // Validates a conv descriptor; computes the output dims.
-dw_status check_desc(dw_backend *be, const dw_conv_desc *d, int *ho, int *wo, const char *op) {
+dw_status dw_check_conv_desc(dw_backend *be, const dw_conv_desc *d, int *ho, int *wo, const char *op) {
     if (!d) return dw_fail(be, DW_ERR_INVALID_ARG, "%s: descriptor is null", op);
     if (d->n <= 0 || d->h <= 0 || d->w <= 0 || d->c_in <= 0 || d->c_out <= 0 || d->k_h <= 0 || d->k_w <= 0 ||
         d->stride_h <= 0 || d->stride_w <= 0 || d->pad_t < 0 || d->pad_l < 0 || d->pad_b < 0 || d->pad_r < 0)
@@ -50,6 +52,12 @@ dw_status check_desc(dw_backend *be, const dw_conv_desc *d, int *ho, int *wo, co
     if (d->epilogue == DW_EPI_RELU6 && (d->q6 < 0 || d->q6 > 127))
         return dw_fail(be, DW_ERR_INVALID_ARG, "%s: q6=%d outside [0,127]", op, d->q6);
     return DW_OK;
+}
+
+namespace {
+
+inline dw_status check_desc(dw_backend *be, const dw_conv_desc *d, int *ho, int *wo, const char *op) {
+    return dw_check_conv_desc(be, d, ho, wo, op);
 }
 
 size_t weight_len(const dw_conv_desc *d) {

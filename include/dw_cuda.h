@@ -147,6 +147,11 @@ DW_API void *dw_stream(dw_backend *be);
 DW_API int dw_sm_count(const dw_backend *be);
 /* Counts kernel launches made through this backend (diagnostics / benchmarks). */
 DW_API uint64_t dw_launch_count(const dw_backend *be);
+/* Bytes of device scratch the backend holds.  Ops that need temporaries (the
+ * reference-signature conv's repacked weights, GEMM transposes, post-processing
+ * workspaces) grow it with cudaMalloc and keep it until dw_destroy.  A
+ * diagnostic with no counterpart in the reference. */
+DW_API size_t dw_scratch_bytes(const dw_backend *be);
 /* CUDA-graph capture of an op sequence enqueued on the backend stream (the
  * reference's OpsRecorder single-command-buffer recording,
  * crates/dragonwing-vulkan/src/record.rs:49-679): between dw_capture_begin and
@@ -206,8 +211,11 @@ DW_API dw_status dw_conv2d_requant_relu_i8(dw_backend *be, const dw_buf *input, 
  * GPU that loads it until exit; it accepts kernels of at most 1 MiB
  * (k_h*k_w*c_in*c_out bytes) and at most 4096 output channels and rejects larger
  * ones with DW_ERR_INVALID_ARG.  The first call on a device looks the array's
- * address up; make it before any stream capture on that device.  Calls share the
- * array: calls that overlap on the GPU race and must be serialised. */
+ * address up (again after the device's context was reset, e.g. by
+ * cudaDeviceReset); make that call before any stream capture on the device.
+ * It never grows the backend's scratch (dw_scratch_bytes stays unchanged).
+ * Calls share the array: calls that overlap on the GPU race and must be
+ * serialised. */
 DW_API dw_status dw_conv2d_requant_relu_i8_noalloc(dw_backend *be, const dw_buf *input, const dw_buf *kernel_hwio,
                                                    dw_buf *output, size_t n, size_t h_in, size_t w_in, size_t c_in,
                                                    size_t c_out, size_t k_h, size_t k_w, size_t stride_h,

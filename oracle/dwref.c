@@ -202,6 +202,21 @@ float dwref_requant_scale(float s_in, float s_w, float s_out) {
 float dwref_expf(float x) { return dw_expf(x); }
 float dwref_silu_f32(float x) { return dw_silu_f32(x); }
 
+/* Measurement switch: 1 computes the SiLU epilogue with the host libm's expf,
+ * the function behind the reference's f32::exp in sigmoid_f32_scalar
+ * (crates/dragonwing-cpu/src/ops.rs:1865-1870), instead of the contract's
+ * shared exp; used to count the int8 results the choice changes. */
+static volatile int g_silu_libm = 0;
+void dwref_set_silu_exp_libm(int on) { g_silu_libm = on ? 1 : 0; }
+
+static float silu_epilogue(float y) {
+    if (!g_silu_libm) return dw_silu_f32(y);
+    const float e = expf(-y);
+    const float sig = 1.0f / (1.0f + e);
+    return y * sig;
+}
+float dwref_silu_epilogue_f32(float y) { return silu_epilogue(y); }
+
 int dwref_conv_out_hw(const dwref_conv_desc *d, int32_t *h_out, int32_t *w_out) {
     if (d->n < 0 || d->h <= 0 || d->w <= 0 || d->c_in <= 0 || d->c_out <= 0 || d->k_h <= 0 ||
         d->k_w <= 0 || d->stride_h <= 0 || d->stride_w <= 0 || d->pad_t < 0 || d->pad_l < 0 ||
@@ -219,7 +234,7 @@ int8_t dwref_epilogue_one(int32_t acc, int32_t bias, float m, float dsc, const d
     int32_t a = (int32_t)((uint32_t)acc + (uint32_t)bias);
     if (d->epilogue == DWREF_EPI_SILU) {
         float y = (float)a * dsc;
-        float z = dw_silu_f32(y);
+        float z = silu_epilogue(y);
         return dwref_f32_to_i8(z * d->inv_s_out);
     }
     int8_t q = dwref_f32_to_i8((float)a * m);

@@ -81,6 +81,8 @@ void dwref_qgemm_i8(int8_t *y, const int8_t *a, const int8_t *b, const int32_t *
                     int threads);
 float dwref_expf(float x);
 float dwref_silu_f32(float x);
+void dwref_set_silu_exp_libm(int on);
+float dwref_silu_epilogue_f32(float y);
 
 /* ---- glue (int8 data with a shared scale moves unchanged) ---- */
 void dwref_maxpool_i8_nhwc(int8_t *y, const int8_t *x, size_t n, size_t h, size_t w, size_t c,

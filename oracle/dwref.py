@@ -113,6 +113,10 @@ def _declare(L):
     L.dwref_expf.restype = f32
     L.dwref_silu_f32.argtypes = [f32]
     L.dwref_silu_f32.restype = f32
+    L.dwref_set_silu_exp_libm.argtypes = [ctypes.c_int]
+    L.dwref_set_silu_exp_libm.restype = None
+    L.dwref_silu_epilogue_f32.argtypes = [f32]
+    L.dwref_silu_epilogue_f32.restype = f32
     L.dwref_f16_from_f32.argtypes = [f32]
     L.dwref_f16_from_f32.restype = ctypes.c_uint16
     L.dwref_f16_to_f32.argtypes = [ctypes.c_uint16]
@@ -283,6 +287,17 @@ def qgemm_i8(a, b, bias, M, m, n, k, epilogue=EPI_NONE, q6=127, threads=1):
 
 def expf(x: float) -> float:
     return float(lib().dwref_expf(x))
+
+
+def set_silu_exp_libm(on: bool) -> None:
+    """Measurement switch: the SiLU epilogue uses the host libm's expf (the
+    reference's f32::exp, ops.rs:1865-1870) instead of the shared exp."""
+    lib().dwref_set_silu_exp_libm(1 if on else 0)
+
+
+def silu_epilogue_f32(y: float) -> float:
+    """The float SiLU the int8 epilogue uses under the current exp switch."""
+    return lib().dwref_silu_epilogue_f32(y)
 
 
 def silu_f32(x: float) -> float:

@@ -29,10 +29,11 @@ import numpy as np
 from oracle import dwref
 
 
-def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
+def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None, return_all: bool = False) -> dict:
     """Runs `graph` on the CPU.  `feeds` maps input names to arrays.  With
     `batch_slice` = (b0, b1), only images b0..b1-1 are computed (every op is
-    per-image), which bounds the CPU time of large-batch graphs."""
+    per-image), which bounds the CPU time of large-batch graphs.  `return_all`
+    returns every tensor, not only the graph outputs."""
     b0, b1 = batch_slice if batch_slice else (0, None)
     vals = {}
     for name in graph.inputs:
@@ -152,6 +153,8 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None) -> dict:
             vals[op.outputs[0]] = dwref.f16_to_f32_array(x).reshape(x.shape)
         else:
             raise ValueError(f"unsupported op {t}")
+    if return_all:
+        return vals
     return {name: vals[name] for name in graph.outputs}
 
 
