@@ -836,6 +836,7 @@ class CudaGraphRuntime:
         self.bufs: dict[str, CudaBuffer] = {}
         self._dispatch = []
         self._cgraph = None
+        self._slot_graphs = []
         for name, t in graph.tensors.items():
             if name not in graph.views:
                 self.bufs[name] = backend.alloc(t.nbytes)
@@ -855,14 +856,20 @@ class CudaGraphRuntime:
             off += o
         return self.bufs[root], off, self.graph.tensors[root].shape[3], root != name
 
+    def _cached(self, key, make):
+        """A prepared constant (repacked weights, tables, workspaces), made once:
+        compiling the op list again (slot graphs) reuses it."""
+        if key not in self._consts:
+            self._consts[key] = make()
+        return self._consts[key]
+
     def _compile(self, op: CompiledOp):
         be, bufs, consts = self.be, self.bufs, self._consts
         t = op.op_type
         if t == "Conv2dRequantReluI8Nhwc":
             desc: ConvDesc = op.params["desc"]
             x, wn, bn, mn, dn = op.inputs
-            wp = ops.prepare_weights_i8(be, desc, consts[wn])
-            consts[wn + "_prep"] = wp
+            wp = self._cached(wn + "_prep", lambda: ops.prepare_weights_i8(be, desc, consts[wn]))
             bb, bm, bd = consts[bn], consts[mn], consts[dn]
             xl, yl = self._loc(x), self._loc(op.outputs[0])
             if xl[3] or yl[3]:
@@ -872,8 +879,7 @@ class CudaGraphRuntime:
         if t == "Conv2dAddI8":
             desc = op.params["desc"]
             x, wn, bn, mn, dn, rn = op.inputs
-            wp = ops.prepare_weights_i8(be, desc, consts[wn])
-            consts[wn + "_prep"] = wp
+            wp = self._cached(wn + "_prep", lambda: ops.prepare_weights_i8(be, desc, consts[wn]))
             bb, bm, bd = consts[bn], consts[mn], consts[dn]
             xl, rl, yl = self._loc(x), self._loc(rn), self._loc(op.outputs[0])
             ra, rb = op.params["ra"], op.params["rb"]
@@ -936,16 +942,14 @@ class CudaGraphRuntime:
             grids = [tuple(self.graph.tensors[x].shape[1:3]) for x in op.inputs[0::2]]
             desc = ops.YoloDetectDesc(n, pr["nc"], grids, pr["strides"], pr["box_scales"], pr["cls_scales"],
                                       pr["reg_max"])
-            tables = ops.prepare_yolo_detect(be, desc)
-            consts[op.name + "_tables"] = tables
+            tables = self._cached(op.name + "_tables", lambda: ops.prepare_yolo_detect(be, desc))
             boxes, clss = [bufs[x] for x in op.inputs[0::2]], [bufs[x] for x in op.inputs[1::2]]
             y = bufs[op.outputs[0]]
             return lambda: ops.yolo_detect_i8(be, desc, tables, boxes, clss, y)
         if t == "YoloPostprocess":
             pr = op.params
             n, A = self.graph.tensors[op.inputs[0]].shape[0], pr["num_detections"]
-            ws = be.alloc(ops.postprocess_yolo_workspace(n, A))
-            consts[op.name + "_workspace"] = ws
+            ws = self._cached(op.name + "_workspace", lambda: be.alloc(ops.postprocess_yolo_workspace(n, A)))
             x, dets, cnt = bufs[op.inputs[0]], bufs[op.outputs[0]], bufs[op.outputs[1]]
             return lambda: ops.postprocess_yolo_device(be, x, n, pr["nc"], A, pr["img_width"], pr["img_height"],
                                                        pr["conf_threshold"], pr["iou_threshold"], pr["flags"], ws,
@@ -965,15 +969,13 @@ class CudaGraphRuntime:
         if t == "Conv2dF16":
             desc = op.params["desc"]
             x, wn, bn = op.inputs
-            wp = ops.prepare_weights_f16(be, desc, consts[wn])
-            consts[wn + "_prep"] = wp
+            wp = self._cached(wn + "_prep", lambda: ops.prepare_weights_f16(be, desc, consts[wn]))
             bx, bb, y = bufs[x], consts[bn], bufs[op.outputs[0]]
             return lambda: ops.conv2d_f16(be, desc, bx, wp, bb, y)
         if t == "Conv2dAddF16":
             desc = op.params["desc"]
             x, wn, bn, rn = op.inputs
-            wp = ops.prepare_weights_f16(be, desc, consts[wn])
-            consts[wn + "_prep"] = wp
+            wp = self._cached(wn + "_prep", lambda: ops.prepare_weights_f16(be, desc, consts[wn]))
             bx, bb, br, y = bufs[x], consts[bn], bufs[rn], bufs[op.outputs[0]]
             return lambda: ops.conv2d_add_f16(be, desc, bx, wp, bb, br, y)
         if t == "AddF16":
@@ -993,8 +995,7 @@ class CudaGraphRuntime:
         if t == "GemmF16":
             m, n, k = op.params["m"], op.params["n"], op.params["k"]
             x, wn, bn = op.inputs
-            wp = ops.prepare_gemm_b_f16(be, consts[wn], k, n)
-            consts[wn + "_prep"] = wp
+            wp = self._cached(wn + "_prep", lambda: ops.prepare_gemm_b_f16(be, consts[wn], k, n))
             bx, bb, y = bufs[x], consts[bn], bufs[op.outputs[0]]
             return lambda: ops.gemm_f16_bias(be, bx, wp, bb, y, m, n, k)
         if t == "CastF16ToF32":
@@ -1022,28 +1023,64 @@ class CudaGraphRuntime:
         for fn in self._dispatch:
             fn()
 
-    def capture(self) -> int:
-        """Records the op list once as a CUDA graph; returns its kernel count."""
+    def _record(self, dispatch) -> ctypes.c_void_p:
         lib = L.load()
-        before = self.be.launch_count()
         self.be._check(lib.dw_capture_begin(self.be.handle))
         try:
-            for fn in self._dispatch:
+            for fn in dispatch:
                 fn()
         finally:
             g = ctypes.c_void_p()
             st = lib.dw_capture_end(self.be.handle, ctypes.byref(g))
         self.be._check(st)
-        self._cgraph = g
+        return g
+
+    def capture(self) -> int:
+        """Records the op list once as a CUDA graph; returns its kernel count."""
+        before = self.be.launch_count()
+        self._cgraph = self._record(self._dispatch)
         # a launch records its kernels; count them by replaying once
         self.run()
         self.be.synchronize(60000)
         return self.be.launch_count() - before
 
+    def capture_slots(self, depth: int) -> list:
+        """Records `depth` CUDA graphs of the op list for a serving loop.  Graph d
+        reads the graph input from its own buffer and writes the graph outputs to
+        its own buffers (slot 0: the runtime's buffers), so step i + 1's input can
+        be uploaded and step i - 1's outputs read back while step i runs, with no
+        device-side staging copies.  Intermediate tensors are shared: the graphs
+        must run one after another on the backend stream.  Returns one
+        (graph, {tensor name: buffer}) pair per slot."""
+        g = self.graph
+        if len(g.inputs) != 1:
+            raise BackendError(L.DW_ERR_UNSUPPORTED, "capture_slots: one graph input expected")
+        names = [g.inputs[0]] + list(g.outputs)
+        if any(n in g.views for n in names):
+            raise BackendError(L.DW_ERR_UNSUPPORTED, "capture_slots: graph input or output is a view")
+        if self._slot_graphs:
+            return self._slot_graphs
+        base = {n: self.bufs[n] for n in names}
+        try:
+            for d in range(depth):
+                slot = dict(base) if d == 0 else {n: self.be.alloc(g.tensors[n].nbytes) for n in names}
+                self.bufs.update(slot)
+                dispatch = [self._compile(op) for op in g.ops]
+                self._slot_graphs.append((self._record(dispatch), slot))
+        finally:
+            self.bufs.update(base)
+        return self._slot_graphs
+
+    def launch_slot(self, d: int) -> None:
+        self.be._check(L.load().dw_graph_launch(self.be.handle, self._slot_graphs[d][0]))
+
     def release(self) -> None:
         if self._cgraph is not None:
             L.load().dw_graph_destroy(self._cgraph)
             self._cgraph = None
+        for graph, _ in self._slot_graphs:
+            L.load().dw_graph_destroy(graph)
+        self._slot_graphs = []
 
     def __del__(self):
         try:
@@ -1056,52 +1093,50 @@ class PipelinedRunner:
     """Serving loop over a CudaGraphRuntime with the host copies overlapped.
 
     Two copy backends (their own streams on the same GPU) move data while the
-    compute backend runs: step i's input is uploaded into a device staging slot
-    while step i-1 computes, and step i's outputs are copied on the device into
-    a staging slot and read back while step i+1 computes.  `depth` slots of each;
-    events order the three streams.  Every step still copies its whole input to
-    the device and its whole output to the host (what `run_steps` returns)."""
+    compute backend runs.  The runtime records `depth` CUDA graphs, each bound
+    to its own input and output buffers (CudaGraphRuntime.capture_slots): step
+    i uploads straight into slot i % depth's input buffer while step i - 1
+    computes, runs that slot's graph, and its outputs are read back from the
+    slot's output buffers while step i + 1 computes.  Events order the three
+    streams; no device-to-device copy is made.  Every step copies its whole
+    input to the device and its whole output to the host (what `run_steps`
+    returns)."""
 
     def __init__(self, rt: "CudaGraphRuntime", depth: int = 2):
         self.rt, self.depth = rt, depth
         be = rt.be
-        self.up, self.down = CudaBackend(be.device), CudaBackend(be.device)
         g = rt.graph
         if len(g.inputs) != 1:
             raise BackendError(L.DW_ERR_UNSUPPORTED, "PipelinedRunner: one graph input expected")
+        self.up, self.down = CudaBackend(be.device), CudaBackend(be.device)
         self.in_name = g.inputs[0]
         self.in_bytes = g.tensors[self.in_name].nbytes
         self.out_names = list(g.outputs)
         self.out_sizes = [g.tensors[o].nbytes for o in self.out_names]
         self.out_bytes = sum(self.out_sizes)
-        self.stage_in = [be.alloc(self.in_bytes) for _ in range(depth)]
-        self.stage_out = [[be.alloc(n) for n in self.out_sizes] for _ in range(depth)]
+        self.slots = rt.capture_slots(depth)
         ev = lambda b: [b.event() for _ in range(depth)]  # noqa: E731
-        self.h2d_done, self.in_free = ev(self.up), ev(be)
-        self.out_ready, self.d2h_done = ev(be), ev(self.down)
+        self.h2d_done, self.run_done, self.d2h_done = ev(self.up), ev(be), ev(self.down)
         self.steps = 0
 
     def step(self, host_in_ptr: int, host_out_ptr: int) -> None:
         """Enqueues one step: upload `in_bytes` from pinned `host_in_ptr`, run the
         graph, read all outputs back (concatenated) into pinned `host_out_ptr`."""
         i, d, be, rt = self.steps, self.steps % self.depth, self.rt.be, self.rt
+        bufs = self.slots[d][1]
         if i >= self.depth:
-            self.up.wait(self.in_free[d])  # the slot's previous input was copied into the graph
-        self.up.upload_async(self.stage_in[d], host_in_ptr, self.in_bytes)
+            self.up.wait(self.run_done[d])  # the slot's previous step has read its input
+        self.up.upload_async(bufs[self.in_name], host_in_ptr, self.in_bytes)
         self.up.record(self.h2d_done[d])
         be.wait(self.h2d_done[d])
-        be.copy_async(rt.bufs[self.in_name], self.stage_in[d], self.in_bytes)
-        be.record(self.in_free[d])
-        rt.run()
         if i >= self.depth:
             be.wait(self.d2h_done[d])  # the slot's previous outputs reached the host
-        for o, n, dst in zip(self.out_names, self.out_sizes, self.stage_out[d]):
-            be.copy_async(dst, rt.bufs[o], n)
-        be.record(self.out_ready[d])
-        self.down.wait(self.out_ready[d])
+        rt.launch_slot(d)
+        be.record(self.run_done[d])
+        self.down.wait(self.run_done[d])
         off = 0
-        for n, src in zip(self.out_sizes, self.stage_out[d]):
-            self.down.download_async(src, host_out_ptr + off, n)
+        for name, n in zip(self.out_names, self.out_sizes):
+            self.down.download_async(bufs[name], host_out_ptr + off, n)
             off += n
         self.down.record(self.d2h_done[d])
         self.steps += 1
@@ -1112,7 +1147,7 @@ class PipelinedRunner:
 
     def close(self) -> None:
         self.synchronize()
-        for evs in (self.h2d_done, self.in_free, self.out_ready, self.d2h_done):
+        for evs in (self.h2d_done, self.run_done, self.d2h_done):
             for e in evs:
                 e.close()
         self.up.close()

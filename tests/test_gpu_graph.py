@@ -105,8 +105,10 @@ def test_mobilenetv2_block_full_batch_sampled(be):
     rt.release()
 
 
-def test_pipelined_runner_matches_sequential_runs(be):
-    """PipelinedRunner (uploads and read-backs on copy streams, two steps in
+@pytest.mark.parametrize("depth", [2, 3])
+def test_pipelined_runner_matches_sequential_runs(be, depth):
+    """PipelinedRunner (one CUDA graph per slot bound to the slot's own input and
+    output buffers; uploads and read-backs on copy streams, `depth` steps in
     flight) returns, per step, exactly what a plain run of that step's input
     returns."""
     from dragonwing_edge_rs_b200.graph import CudaGraphRuntime, PipelinedRunner, yolov8n
@@ -123,7 +125,7 @@ def test_pipelined_runner_matches_sequential_runs(be):
         rt.set_input_bytes(name, x)
         rt.run()
         expected.append(np.concatenate([rt.get_output_bytes(o) for o in outs]))
-    pr = PipelinedRunner(rt, depth=2)
+    pr = PipelinedRunner(rt, depth=depth)
     hin = [be.host_alloc(n_in) for _ in inputs]
     hout = [be.host_alloc(n_out) for _ in inputs]
     for (p_in, a_in), x in zip(hin, inputs):
