@@ -77,6 +77,17 @@ struct UmmaParams {
     int swz;                                // fp16 path: staging in 64-channel slabs, 128-byte swizzle (bn % 64 == 0)
     int nbuf;                               // staging buffers (2: a tile's store overlaps the next tile's epilogue)
     uint32_t out_bytes;                     // bytes of one staging buffer
+    // mode 2 (halo tiles, stride-1 convs with several taps): the A operand of a
+    // K block is one zero-padded halo tile per 16-byte channel chunk, planes of
+    // [hh rows][hw columns][16 bytes]; output tiles are 8 columns x 16 rows per
+    // 128-row block, so the 8 rows of a core matrix are 8 neighbouring pixels
+    // and each tap is the same tile read at a shifted start address.
+    int hw, hh;                             // halo columns (8 + k_w - 1) and rows (16 R + k_h - 1)
+    int chunks;                             // 16-byte channel chunks of c_in
+    int cps;                                // chunks per K block (bk / 16)
+    int chunk_elems;                        // elements per chunk (16 / esize)
+    uint32_t plane_stride;                  // bytes between chunk planes of a stage (128-byte aligned)
+    uint32_t b_tap_bytes;                   // bytes of one tap's weight slice in a stage (bn * bk)
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
@@ -506,6 +517,15 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint64_t hi) {
     return hi | (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16);
 }
 
+// Shared-memory matrix descriptor, K-major without swizzle: core matrices of 8
+// rows x 16 bytes (rows 16 bytes apart); `lbo` = bytes between the two 16-byte
+// halves of a 32-byte K step, `sbo` = bytes between 8-row groups; version 1,
+// layout type 0 (no swizzle).
+__device__ __forceinline__ uint64_t smem_desc_noswz(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
 // ------------------------------------------------------------------- kernel
 // Tile = R blocks of 128 output pixels x bn output channels.  Row block r of a
 // tile covers pixels [tile_m0 + 128 r, +128) in flat mode, or the spatial
@@ -521,7 +541,7 @@ __device__ __forceinline__ TileCoord tile_coord(const UmmaParams &p, int tile) {
     t.nt = tile % p.n_tiles;
     t.n0 = t.nt * p.bn;
     t.img = t.oh0 = t.ow0 = 0;
-    if (p.mode == 1) {
+    if (p.mode != 0) {
         const int tw_i = t.mt % p.tiles_w;
         const int t2 = t.mt / p.tiles_w;
         t.oh0 = (t2 % p.tiles_h) * p.th * p.R;
@@ -596,6 +616,9 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // Tap table: mode 1, the producer's per-tap view coordinates; mode 2, the
+    // MMA issuer's per-tap halo offsets (each written and read by one warp).
+    __shared__ int4 tapc[kTapTable];
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; s++) {
@@ -625,14 +648,13 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int k_iters = p.taps * p.cblocks;
+    const int k_iters = p.mode == 2 ? p.cblocks : p.taps * p.cblocks;  // halo mode: one stage per K block, all taps
     const uint32_t acc_cols = (uint32_t)(p.R * p.bn);
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         // per-tap coordinates of the 5-D activation view (mode 1), computed once:
         // x offset (column phase * c_in), column shift, row phase, row shift
-        __shared__ int4 tapc[kTapTable];
         if (p.mode == 1)
             for (int tap = lane; tap < min(p.taps, kTapTable); tap += 32) tapc[tap] = tap_coord(p, tap);
         __syncwarp();
@@ -656,9 +678,26 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                     }
                     if (!mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1, p, abort_flag, 1)) { ok = false; break; }
                     const uint32_t fb = smem_u32(&full_bar[s]);
-                    mbar_expect_tx(fb, (uint32_t)nrb * p.a_tx_bytes + p.b_tx_bytes);
                     const uint32_t a_dst = smem_u32(a_smem + (size_t)s * p.a_stage_bytes);
                     const uint32_t b_dst = smem_u32(b_smem + (size_t)s * p.b_stage_bytes);
+                    if (p.mode == 2) {
+                        // halo mode: K block `it` = chunks [it * cps, +real) of every tap;
+                        // one halo box per chunk (zero fill = the conv's padding), one
+                        // weight box per tap
+                        const int real = min(p.cps, p.chunks - it * p.cps);
+                        mbar_expect_tx(fb, (uint32_t)real * (uint32_t)(p.hw * p.hh * 16) +
+                                               (uint32_t)p.taps * p.b_tx_bytes);
+                        for (int j = 0; j < real; j++)
+                            tma_load_4d(a_dst + (uint32_t)j * p.plane_stride, &tmap_a, fb,
+                                        it * p.bk_elems + j * p.chunk_elems, tc.ow0 - p.pl, tc.oh0 - p.pt, tc.img);
+                        for (int t = 0; t < p.taps; t++)
+                            tma_load_3d(b_dst + (uint32_t)t * p.b_tap_bytes, &tmap_b, fb, it * p.bk_elems, t, tc.n0);
+                        issued_mask |= 1u << s;
+                        last_parity = (last_parity & ~(1u << s)) | (ph << s);
+                        if (++s == p.stages) { s = 0; ph ^= 1; }
+                        continue;
+                    }
+                    mbar_expect_tx(fb, (uint32_t)nrb * p.a_tx_bytes + p.b_tx_bytes);
                     if (p.mode == 0) {
                         for (int r = 0; r < nrb; r++)
                             tma_load_2d(a_dst + (uint32_t)(r * kBM * p.bk), &tmap_a, fb, cb * p.bk_elems,
@@ -688,6 +727,12 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        // halo mode: byte offset of tap (kh, kw) inside a halo plane (the tap
+        // table's x; the producer does not use the table in this mode)
+        if (p.mode == 2)
+            for (int t = lane; t < min(p.taps, kTapTable); t += 32)
+                tapc[t].x = ((t / p.kw) * p.hw + (t % p.kw)) * 16;
+        __syncwarp();
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
@@ -707,6 +752,34 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(a_smem + (size_t)s * p.a_stage_bytes);
                     const uint32_t b_addr = smem_u32(b_smem + (size_t)s * p.b_stage_bytes);
+                    if (p.mode == 2) {
+                        // every tap of K block `it`: the A tile is the halo plane read from the
+                        // tap's offset (8-row groups one halo row apart); a K step covers two
+                        // chunk planes.  With an odd chunk count the last step's second half
+                        // reads the neighbouring pixel (finite int8; its weights are the
+                        // zero-filled channels past c_in), so no plane is left unloaded.
+                        const int real = min(p.cps, p.chunks - it * p.cps);
+                        const int kn = (real + 1) >> 1;
+                        const uint32_t sbo = (uint32_t)p.hw * 16u;
+                        const uint32_t rb = 16u * sbo;  // 16 output rows per row block
+                        for (int t = 0; t < p.taps; t++) {
+                            const uint32_t at = a_addr + (uint32_t)tapc[t].x;
+                            const uint32_t bt = b_addr + (uint32_t)t * p.b_tap_bytes;
+                            for (int k = 0; k < kn; k++) {
+                                const uint32_t lbo = (2 * k + 1 < real) ? p.plane_stride : 16u;
+                                const uint64_t bd = smem_desc(bt + 32 * k, p.desc_hi);
+                                const uint32_t accf = (it > 0 || t > 0 || k > 0) ? 1u : 0u;
+                                for (int r = 0; r < p.R; r++) {
+                                    const uint64_t ad =
+                                        smem_desc_noswz(at + (uint32_t)(2 * k) * p.plane_stride + (uint32_t)r * rb, lbo, sbo);
+                                    tc_mma<kF16>(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, accf);
+                                }
+                            }
+                        }
+                        tc_commit(smem_u32(&empty_bar[s]));
+                        if (++s == p.stages) { s = 0; ph ^= 1; }
+                        continue;
+                    }
                     // 32-byte K steps holding channels below c_in (the rest of the block is zero)
                     const int kn = cb == p.cblocks - 1 ? kn_last : kn_full;
                     if (++cb == p.cblocks) cb = 0;
@@ -1047,6 +1120,103 @@ CUtensorMapSwizzle swizzle_enum(int bk) {
 
 constexpr size_t kSmemLimit = 227 * 1024 - sizeof(int4) * kTapTable;  // dynamic share (the tap table is static)
 
+// Halo mode plan (stride-1 convs with several taps).  Output tiles are 8
+// columns x 16 rows per 128-row block, R blocks stacked vertically; a stage
+// holds, for one K block of bk bytes, the halo plane of each 16-byte chunk and
+// every tap's bn x bk weight slice.
+struct HaloPlan {
+    bool ok = false;
+    int R = 1, bn = 16, bk = 32, tiles_w = 1, tiles_h = 1, n_tiles = 1;
+    uint32_t plane = 0;
+};
+
+uint32_t halo_plane_bytes(const dw_conv_desc &d, int R) {
+    return (uint32_t)(((size_t)(16 * R + d.k_h - 1) * (size_t)(8 + d.k_w - 1) * 16 + 127) & ~size_t(127));
+}
+
+// Output-channel tile for the halo mode: all of c_out when the taps' weight
+// slices stay small, else the width <= cap with the fewest padded columns.
+int halo_bn(int c_out16, int taps) {
+    int cap = (int)(40 * 1024 / ((size_t)taps * 32)) / 16 * 16;
+    cap = std::max(16, std::min(256, cap));
+    if (c_out16 <= cap) return c_out16;
+    int best = 16;
+    long best_cost = -1;
+    for (int bn = cap; bn >= 16; bn -= 16) {
+        const long cost = (long)((c_out16 + bn - 1) / bn) * bn;
+        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; }
+    }
+    return best;
+}
+
+HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, int esize, bool flat) {
+    HaloPlan h;
+    const int taps = d.k_h * d.k_w;
+    if (flat || d.stride_h != 1 || d.stride_w != 1 || taps < 2 || taps > kTapTable) return h;
+    if ((d.c_in * esize) % 16 || (esize == 2 && d.c_in % 16)) return h;  // fp16: whole 32-byte K steps
+    // Channel rows of at most 32 bytes: there the per-tap producer's boxes are
+    // half empty and re-read every pixel nine times, and the halo stage (every
+    // tap's weight slice) stays small.  With wider rows a stage's weight boxes
+    // need 32-byte K blocks to fit, whose TMA requests cost more than the halo
+    // saves (measured on B200: YOLOv8n's 64-channel 3x3s 23 -> 27 us, ResNet-50's
+    // 14x14 256-channel fp16 3x3s 51 -> 141 us; 16 and 32 channels 77 -> 59 and
+    // 40 -> 30 us).
+    if (d.c_in * esize > 32 && !getenv("DW_UMMA_HALO_WIDE")) return h;
+    if (8 + d.k_w - 1 > 256 || 16 + d.k_h - 1 > 256) return h;
+    if (const char *e = getenv("DW_UMMA_HALO"))  // tuning switch: 0 keeps the per-tap producer
+        if (atoi(e) == 0) return h;
+    // pixel utilisation of 8 x 16 tiles; small maps keep the per-tap producer
+    // (whole images side by side in one row block)
+    const int tiles_w = (wo + 7) / 8;
+    const double util = (double)ho * wo / ((double)tiles_w * 8 * (double)((ho + 15) / 16) * 16);
+    if (util < 0.7) return h;
+    const int c_out16 = ((d.c_out + 15) / 16) * 16;
+    h.bn = halo_bn(c_out16, taps);
+    h.n_tiles = (d.c_out + h.bn - 1) / h.bn;
+    h.tiles_w = tiles_w;
+    const int rmax = std::max(1, std::min(8, 256 / h.bn));
+    // row blocks per tile: the fewest padded rows; among those the most blocks
+    // that still give every SM a tile, else the fewest blocks
+    long min_pad = -1;
+    for (int R = 1; R <= rmax; R++) {
+        const long pad = (long)((ho + 16 * R - 1) / (16 * R)) * 16 * R;
+        if (min_pad < 0 || pad < min_pad) min_pad = pad;
+    }
+    int pick = 0;
+    for (int R = rmax; R >= 1 && !pick; R--) {
+        const long pad = (long)((ho + 16 * R - 1) / (16 * R)) * 16 * R;
+        const long tiles = (long)d.n * tiles_w * ((ho + 16 * R - 1) / (16 * R)) * h.n_tiles;
+        if (pad * 20 <= min_pad * 21 && tiles >= be->sm_count) pick = R;
+    }
+    for (int R = 1; R <= rmax && !pick; R++) {
+        const long pad = (long)((ho + 16 * R - 1) / (16 * R)) * 16 * R;
+        if (pad * 20 <= min_pad * 21) pick = R;
+    }
+    const size_t chan = al1k(sizeof(ChanSmem));
+    const int chunks = d.c_in * esize / 16;
+    const int cap_bk = ((d.c_in * esize + 31) / 32) * 32;
+    // K block: the widest that leaves room for three stages (two at bk = 32),
+    // then fewer row blocks
+    for (int R = pick; R >= 1; R--) {
+        const uint32_t plane = halo_plane_bytes(d, R);
+        const size_t fixed = 1024 + al1k((size_t)R * kBM * h.bn * esize) + chan + 512;
+        for (int bk : {128, 64, 32}) {
+            if (bk > cap_bk && bk != 32) continue;
+            const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane) + al1k((size_t)taps * h.bn * bk);
+            const size_t fit = fixed < kSmemLimit ? (kSmemLimit - fixed) / stage : 0;
+            if (fit >= 3 || (bk == 32 && fit >= 2)) {
+                h.R = R;
+                h.bk = bk;
+                h.plane = plane;
+                h.tiles_h = (ho + 16 * R - 1) / (16 * R);
+                h.ok = true;
+                return h;
+            }
+        }
+    }
+    return h;
+}
+
 }  // namespace
 
 bool umma_supported(const dw_backend *be, const dw_conv_desc &d, int ho, int wo) {
@@ -1118,73 +1288,97 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     p.n_img = d.n; p.ho = ho; p.wo = wo; p.c_out = d.c_out;
     p.taps = d.k_h * d.k_w; p.kw = d.k_w; p.sh = d.stride_h; p.sw = d.stride_w; p.pt = d.pad_t; p.pl = d.pad_l;
     p.c_in = d.c_in;
-    p.bk = flat ? pick_bk(d.c_in * esize) : pick_bk_taps(d.c_in * esize);
-    if (const char *e = getenv("DW_UMMA_BK")) {  // tuning override: 32, 64 or 128 bytes of K per stage
-        const int v = atoi(e);
-        if (v == 32 || v == 64 || v == 128) p.bk = v;
-    }
-    if (esize == 2 && !flat && d.stride_w > 1 && (d.c_in * esize) % p.bk) p.bk = pick_bk(d.c_in * esize);
-    p.bn = pick_bn(((d.c_out + 15) / 16) * 16);
-    // 1x1 convs (epilogue-bound: few K steps per tile): a narrower K block when
-    // that lets the staging be double-buffered (the fp16 staging of a 128 x 256
-    // tile is 64 KiB) -- more K steps, but a tile's stores overlap the next
-    // tile's epilogue.
-    if (d.k_h * d.k_w == 1) {
-        const size_t chan = al1k(sizeof(ChanSmem));
-        auto fits2 = [&](int bk) {
-            const int r = std::max(1, std::min({8, 256 / p.bn, 32768 / (kBM * bk)}));
-            const size_t ob = al1k((size_t)r * kBM * p.bn * esize);
-            const size_t sp = al1k((size_t)r * kBM * bk) + al1k((size_t)p.bn * bk);
-            return 1024 + 2 * ob + chan + 512 + 2 * sp <= kSmemLimit;
-        };
-        if (!fits2(p.bk))
-            for (int bk = p.bk / 2; bk >= 32; bk /= 2)
-                if (fits2(bk)) {
-                    p.bk = bk;
-                    break;
-                }
-    }
-    p.bk_elems = p.bk / esize;
-    p.cblocks = (d.c_in + p.bk_elems - 1) / p.bk_elems;
-    // Tiles for a tile width bn and at most r_cap row blocks per tile: R * bn <=
-    // 256 (two TMEM accumulator buffers within 512 columns), at most 8, and an A
-    // stage (R * 128 rows * bk) of at most 32 KiB.
-    auto plan_tiles = [&](int bn, int r_cap) {
-        p.bn = bn;
-        p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
-        int R = std::max(1, std::min({r_cap, 8, 256 / p.bn, 32768 / (kBM * p.bk)}));
-        if (flat) {
-            p.rows = (long long)d.n * d.h * d.w;
-            const long long blocks = (p.rows + kBM - 1) / kBM;
-            R = (int)std::min<long long>(R, blocks);
-            p.R = R;
-            p.m_tiles = (int)((blocks + R - 1) / R);
-            p.tw = kBM; p.th = 1; p.nb = 1;
-            p.a_tx_bytes = (uint32_t)(kBM * p.bk);
-        } else {
-            pick_tile(ho, wo, &p.tw, &p.th);
-            // small maps: a row block holds whole images side by side (7x7: 2 per block)
-            p.nb = (p.tw == wo && p.th == ho) ? std::max(1, std::min(kBM / (wo * ho), d.n)) : 1;
-            R = std::min(R, (ho + p.th - 1) / p.th);
-            p.R = R;
-            p.tiles_w = (wo + p.tw - 1) / p.tw;
-            p.tiles_h = (ho + p.th * R - 1) / (p.th * R);
-            p.m_tiles = ((d.n + p.nb - 1) / p.nb) * p.tiles_w * p.tiles_h;
-            p.a_tx_bytes = (uint32_t)(p.tw * p.th * p.nb * p.bk);
-        }
+    const HaloPlan hp = plan_halo(be, d, ho, wo, esize, flat);
+    if (hp.ok) {
+        p.mode = 2;
+        p.bk = hp.bk;
+        p.bk_elems = p.bk / esize;
+        p.cblocks = (d.c_in + p.bk_elems - 1) / p.bk_elems;
+        p.bn = hp.bn;
+        p.n_tiles = hp.n_tiles;
+        p.R = hp.R;
+        p.tw = 8; p.th = 16; p.nb = 1;
+        p.tiles_w = hp.tiles_w;
+        p.tiles_h = hp.tiles_h;
+        p.m_tiles = d.n * p.tiles_w * p.tiles_h;
         p.num_tiles = p.m_tiles * p.n_tiles;
-    };
-    if (const char *e = getenv("DW_UMMA_BN")) {  // tuning override: tile width (a multiple of 16, <= 256)
-        const int v = atoi(e);
-        if (v >= 16 && v <= 256 && v % 16 == 0) p.bn = v;
-    }
-    plan_tiles(p.bn, 8);
-    // Small problems (tiles for fewer than half the SMs): fewer row blocks per
-    // tile, then narrower tiles (down to 64 channels), until half the SMs have a
-    // tile -- more CTAs stream the long K loops side by side; the extra reads of
-    // the A tiles come from L2.
-    while (2 * p.num_tiles < be->sm_count && p.R > 1) plan_tiles(p.bn, p.R - 1);
-    while (2 * p.num_tiles < be->sm_count && p.bn >= 128 && (p.bn / 2) % 16 == 0) plan_tiles(p.bn / 2, 1);
+        p.hw = 8 + d.k_w - 1;
+        p.hh = 16 * p.R + d.k_h - 1;
+        p.chunks = d.c_in * esize / 16;
+        p.cps = p.bk / 16;
+        p.chunk_elems = 16 / esize;
+        p.plane_stride = hp.plane;
+        p.b_tap_bytes = (uint32_t)(p.bn * p.bk);
+        p.a_tx_bytes = 0;  // per chunk: hw * hh * 16 bytes (the producer counts them)
+    } else {
+        p.bk = flat ? pick_bk(d.c_in * esize) : pick_bk_taps(d.c_in * esize);
+        if (const char *e = getenv("DW_UMMA_BK")) {  // tuning override: 32, 64 or 128 bytes of K per stage
+            const int v = atoi(e);
+            if (v == 32 || v == 64 || v == 128) p.bk = v;
+        }
+        if (esize == 2 && !flat && d.stride_w > 1 && (d.c_in * esize) % p.bk) p.bk = pick_bk(d.c_in * esize);
+        p.bn = pick_bn(((d.c_out + 15) / 16) * 16);
+        // 1x1 convs (epilogue-bound: few K steps per tile): a narrower K block when
+        // that lets the staging be double-buffered (the fp16 staging of a 128 x 256
+        // tile is 64 KiB) -- more K steps, but a tile's stores overlap the next
+        // tile's epilogue.
+        if (d.k_h * d.k_w == 1) {
+            const size_t chan = al1k(sizeof(ChanSmem));
+            auto fits2 = [&](int bk) {
+                const int r = std::max(1, std::min({8, 256 / p.bn, 32768 / (kBM * bk)}));
+                const size_t ob = al1k((size_t)r * kBM * p.bn * esize);
+                const size_t sp = al1k((size_t)r * kBM * bk) + al1k((size_t)p.bn * bk);
+                return 1024 + 2 * ob + chan + 512 + 2 * sp <= kSmemLimit;
+            };
+            if (!fits2(p.bk))
+                for (int bk = p.bk / 2; bk >= 32; bk /= 2)
+                    if (fits2(bk)) {
+                        p.bk = bk;
+                        break;
+                    }
+        }
+        p.bk_elems = p.bk / esize;
+        p.cblocks = (d.c_in + p.bk_elems - 1) / p.bk_elems;
+        // Tiles for a tile width bn and at most r_cap row blocks per tile: R * bn <=
+        // 256 (two TMEM accumulator buffers within 512 columns), at most 8, and an A
+        // stage (R * 128 rows * bk) of at most 32 KiB.
+        auto plan_tiles = [&](int bn, int r_cap) {
+            p.bn = bn;
+            p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
+            int R = std::max(1, std::min({r_cap, 8, 256 / p.bn, 32768 / (kBM * p.bk)}));
+            if (flat) {
+                p.rows = (long long)d.n * d.h * d.w;
+                const long long blocks = (p.rows + kBM - 1) / kBM;
+                R = (int)std::min<long long>(R, blocks);
+                p.R = R;
+                p.m_tiles = (int)((blocks + R - 1) / R);
+                p.tw = kBM; p.th = 1; p.nb = 1;
+                p.a_tx_bytes = (uint32_t)(kBM * p.bk);
+            } else {
+                pick_tile(ho, wo, &p.tw, &p.th);
+                // small maps: a row block holds whole images side by side (7x7: 2 per block)
+                p.nb = (p.tw == wo && p.th == ho) ? std::max(1, std::min(kBM / (wo * ho), d.n)) : 1;
+                R = std::min(R, (ho + p.th - 1) / p.th);
+                p.R = R;
+                p.tiles_w = (wo + p.tw - 1) / p.tw;
+                p.tiles_h = (ho + p.th * R - 1) / (p.th * R);
+                p.m_tiles = ((d.n + p.nb - 1) / p.nb) * p.tiles_w * p.tiles_h;
+                p.a_tx_bytes = (uint32_t)(p.tw * p.th * p.nb * p.bk);
+            }
+            p.num_tiles = p.m_tiles * p.n_tiles;
+        };
+        if (const char *e = getenv("DW_UMMA_BN")) {  // tuning override: tile width (a multiple of 16, <= 256)
+            const int v = atoi(e);
+            if (v >= 16 && v <= 256 && v % 16 == 0) p.bn = v;
+        }
+        plan_tiles(p.bn, 8);
+        // Small problems (tiles for fewer than half the SMs): fewer row blocks per
+        // tile, then narrower tiles (down to 64 channels), until half the SMs have a
+        // tile -- more CTAs stream the long K loops side by side; the extra reads of
+        // the A tiles come from L2.
+        while (2 * p.num_tiles < be->sm_count && p.R > 1) plan_tiles(p.bn, p.R - 1);
+        while (2 * p.num_tiles < be->sm_count && p.bn >= 128 && (p.bn / 2) % 16 == 0) plan_tiles(p.bn / 2, 1);
+    }  // per-tap producer plan
     // fp16 staging in swizzled 64-channel slabs (conflict-free epilogue stores)
     // when every tile's channels split into whole slabs.
     if (esize == 2 && p.bn % 64 == 0 && !getenv("DW_F16_NOSWZ")) p.swz = 1;
@@ -1192,6 +1386,10 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     p.b_tx_bytes = (uint32_t)(p.bn * p.bk);
     p.a_stage_bytes = (uint32_t)al1k((size_t)p.R * kBM * p.bk);
     p.b_stage_bytes = (uint32_t)al1k((size_t)p.bn * p.bk);
+    if (p.mode == 2) {  // the loaded chunk planes; every tap's weight slice
+        p.a_stage_bytes = (uint32_t)al1k((size_t)std::min(p.cps, p.chunks) * p.plane_stride);
+        p.b_stage_bytes = (uint32_t)al1k((size_t)p.taps * p.b_tap_bytes);
+    }
     const size_t out_bytes = al1k((size_t)p.R * kBM * p.bn * esize);
     const size_t chan_bytes = al1k(sizeof(ChanSmem));
     // two staging buffers when they fit beside at least two pipeline stages
@@ -1230,7 +1428,18 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     CUtensorMap ta, tb;
     CUresult r;
     const CUtensorMapSwizzle sw = swizzle_enum(p.bk);
-    if (flat) {
+    if (p.mode == 2) {
+        // halo boxes: one 16-byte channel chunk of (16 R + k_h - 1) x (8 + k_w - 1)
+        // pixels, no swizzle; out-of-range pixels (the padding) are zero-filled
+        cuuint64_t dims[4] = {(cuuint64_t)d.c_in, (cuuint64_t)d.w, (cuuint64_t)d.h, (cuuint64_t)d.n};
+        cuuint64_t strides[3] = {(cuuint64_t)x_pitch * es, (cuuint64_t)d.w * x_pitch * es,
+                                 (cuuint64_t)d.h * d.w * x_pitch * es};
+        cuuint32_t box[4] = {(cuuint32_t)p.chunk_elems, (cuuint32_t)p.hw, (cuuint32_t)p.hh, 1};
+        cuuint32_t estr[4] = {1, 1, 1, 1};
+        r = be->encode_tiled(&ta, dt, 4, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else if (flat) {
         cuuint64_t dims[2] = {(cuuint64_t)d.c_in, (cuuint64_t)p.rows};
         cuuint64_t strides[1] = {(cuuint64_t)x_pitch * es};
         cuuint32_t box[2] = {(cuuint32_t)p.bk_elems, (cuuint32_t)kBM};

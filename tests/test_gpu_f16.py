@@ -300,7 +300,31 @@ UMMA_CASES = [
     (3, 7, 7, 512, 512, 3, 1, 1, True),   # two whole 7x7 images per row block
     (3, 14, 14, 256, 512, 1, 2, 0, False),
     (5, 6, 6, 32, 64, 3, 1, 1, True),
+    (2, 28, 28, 128, 128, 3, 1, 1, True),
+    (2, 14, 14, 256, 256, 3, 1, 1, True),
 ]
+
+# the halo producer (stride-1 multi-tap convs on maps the 8 x 16 tiles cover);
+# DW_UMMA_HALO_WIDE=1 sends the wider channel rows there too
+HALO_CASES = [
+    (2, 28, 28, 128, 128, 3, 1, 1, True),
+    (2, 14, 14, 256, 256, 3, 1, 1, True),  # channel tiles of 128
+    (1, 40, 24, 32, 48, 3, 1, 1, False),
+    (1, 30, 36, 16, 32, 5, 1, 2, True),
+    (2, 56, 56, 64, 64, 3, 1, 1, True),
+]
+
+
+@pytest.mark.parametrize("case", HALO_CASES)
+def test_conv_f16_halo_within_tolerance(be_umma, case, monkeypatch):
+    monkeypatch.setenv("DW_UMMA_HALO_WIDE", "1")
+    n, h, w, ci, co, k, s, p, relu = case
+    rng = np.random.default_rng(sum(case) + 2)
+    desc = ConvDesc(n, h, w, ci, co, k, k, s, s, (p,) * 4, 1, dw.EPI_RELU if relu else dw.EPI_NONE)
+    x, wt, b = conv_inputs(rng, desc)
+    got = run_conv_f16(be_umma, desc, x, wt, b)
+    exp = oracle_conv_f16(desc, x, wt, b)
+    print(tol_check(got, exp, str(case)))
 
 
 @pytest.mark.parametrize("case", UMMA_CASES)
@@ -327,6 +351,24 @@ def test_conv_f16_inf_input_stays_local(be_umma):
     nonfinite_got = (got & 0x7C00) == 0x7C00
     nonfinite_exp = (exp & 0x7C00) == 0x7C00
     assert np.array_equal(nonfinite_got.any(axis=2), nonfinite_exp.any(axis=2))
+
+
+def test_conv_f16_halo_inf_input_stays_local(be_umma, monkeypatch):
+    """Halo mode (stride 1, 3x3): an infinity in one pixel reaches only the
+    outputs whose windows hold it; the zero-filled halo and the shifted tap
+    reads touch no other pixel."""
+    monkeypatch.setenv("DW_UMMA_HALO_WIDE", "1")
+    desc = ConvDesc(1, 32, 32, 32, 16, 3, 3, 1, 1, (1,) * 4, 1, dw.EPI_NONE)
+    rng = np.random.default_rng(22)
+    x, wt, b = conv_inputs(rng, desc)
+    x = x.reshape(32, 32, 32)
+    x[9, 13, 5] = 0x7C00
+    got = run_conv_f16(be_umma, desc, x.ravel(), wt, b).reshape(32, 32, 16)
+    exp = oracle_conv_f16(desc, x.ravel(), wt, b).reshape(32, 32, 16)
+    nonfinite_got = (got & 0x7C00) == 0x7C00
+    nonfinite_exp = (exp & 0x7C00) == 0x7C00
+    assert np.array_equal(nonfinite_got.any(axis=2), nonfinite_exp.any(axis=2))
+    assert nonfinite_got.any(axis=2).sum() <= 9
 
 
 @pytest.mark.parametrize("case", [(2, 28, 28, 64, 256, 1, 1, 0, True), (2, 28, 28, 64, 256, 1, 1, 0, False),
