@@ -80,6 +80,10 @@ class Graph:
                 c_in = op.params.get("c_in_real", d.c_in)  # a lowered conv counts its real channels
                 per = d.k_h * d.k_w * (c_in if d.group == 1 else 1)
                 total += 2 * d.n * ho * wo * d.c_out * per
+            elif op.op_type == "Conv":  # the reference's unfused int8 conv (int32 accumulators)
+                d = conv_desc_of(self, op)
+                ho, wo = d.out_hw()
+                total += 2 * d.n * ho * wo * d.c_out * d.k_h * d.k_w * (d.c_in if d.group == 1 else 1)
             elif op.op_type == "GemmF16":
                 total += 2 * op.params["m"] * op.params["n"] * op.params["k"]
         return total
@@ -98,11 +102,18 @@ class GraphBuilder:
     from ``act_scale_range``, and M / D / q6 are derived with the reference
     formulas (quantize.rs:245, ops.rs:3503-3525)."""
 
-    def __init__(self, seed: int, act_scale_range=(0.01, 0.05)):
+    def __init__(self, seed: int, act_scale_range=(0.01, 0.05), unfused: bool = False):
         self.rng = np.random.default_rng(seed)
         self.lo, self.hi = act_scale_range
         self.g = Graph({}, [], {}, [], [])
         self._n = 0
+        # unfused: every conv in the form the reference's QuantizedGraphCompiler
+        # emits (quantize.rs:176-191, 218-249) -- a Conv writing int32
+        # accumulators, then Requantize (+ Relu / Clip) or, for SiLU, the f32
+        # chain DequantizeLinear -> Sigmoid -> Mul -> QuantizeLinear -- for the
+        # fusion passes (apply_fusion_passes) to collapse.  The same seed draws
+        # the same weights and scales in both modes.
+        self.unfused = unfused
 
     def _name(self, base):
         self._n += 1
@@ -146,11 +157,45 @@ class GraphBuilder:
         desc.inv_s_out = float(np.float32(1.0) / np.float32(s_out))
         ho, wo = desc.out_hw()
         y = g.add_tensor(name + "_out", (n, ho, wo, c_out), "i8", s_out)
+        if self.unfused:
+            return self._conv_unfused(name, x, y, w_layout, bias, s_in, s_w, s_out, desc, act)
         for suffix, arr in (("_w", w_layout), ("_b", bias), ("_M", Q.requant_scales(s_in, s_w, s_out)),
                             ("_D", Q.dequant_scales(s_in, s_w))):
             g.initializers[name + suffix] = arr
         g.ops.append(CompiledOp(name, "Conv2dRequantReluI8Nhwc", [x, name + "_w", name + "_b", name + "_M", name + "_D"],
                                 [y], {"desc": desc}))
+        return y
+
+    def _conv_unfused(self, name, x, y, w_layout, bias, s_in, s_w, s_out, desc, act):
+        """The conv as the reference's quantizer leaves it, with its defects fixed:
+        the int32 accumulator is a tensor of its own (`{y}_i32`, shaped), the bias
+        is a Conv input, and the requantisation is per output channel (an
+        initializer M), not the average of the channel scales."""
+        g = self.g
+        shape = g.tensors[y].shape
+        g.initializers[name + "_w"] = w_layout
+        g.initializers[name + "_b"] = bias
+        acc = g.add_tensor(y + "_i32", shape, "i32")
+        g.ops.append(CompiledOp(name, "Conv", [x, name + "_w", name + "_b"], [acc],
+                                {"kernel_shape": (desc.k_h, desc.k_w), "strides": (desc.stride_h, desc.stride_w),
+                                 "pads": tuple(desc.pads), "dilations": (1, 1), "group": desc.group}))
+        if act == "silu":
+            g.initializers[name + "_D"] = Q.dequant_scales(s_in, s_w)
+            yf = g.add_tensor(name + "_deq", shape, "f32")
+            sig = g.add_tensor(name + "_sig", shape, "f32")
+            z = g.add_tensor(name + "_silu", shape, "f32")
+            g.ops.append(CompiledOp(name + "_dequant", "DequantizeLinear", [acc, name + "_D"], [yf], {}))
+            g.ops.append(CompiledOp(name + "_sigmoid", "Sigmoid", [yf], [sig], {}))
+            g.ops.append(CompiledOp(name + "_mul", "Mul", [yf, sig], [z], {}))
+            g.ops.append(CompiledOp(name + "_quant", "QuantizeLinear", [z], [y], {"scale": s_out}))
+            return y
+        g.initializers[name + "_M"] = Q.requant_scales(s_in, s_w, s_out)
+        rq = y if act == "none" else g.add_tensor(name + "_rq", shape, "i8", s_out)
+        g.ops.append(CompiledOp(name + "_requant", "Requantize", [acc, name + "_M"], [rq], {"scale": None}))
+        if act == "relu":
+            g.ops.append(CompiledOp(name + "_relu", "Relu", [rq], [y], {}))
+        elif act == "relu6":
+            g.ops.append(CompiledOp(name + "_clip", "Clip", [rq], [y], {"min": 0.0, "max": 6.0}))
         return y
 
     def add(self, a, b, out_scale=None, name=None):
@@ -640,11 +685,217 @@ def lower_concat_views_i8(graph: Graph) -> Graph:
                  list(graph.inputs), list(graph.outputs), views)
 
 
+# ---------------------------------------------------------------------------
+# the reference's op-fusion passes over the unfused int8 IR
+# (crates/dragonwing-onnx/src/fusion.rs:42-334), extended to the contract
+# ---------------------------------------------------------------------------
+
+UNFUSED_OPS = ("Conv", "Requantize", "DequantizeLinear", "Sigmoid", "Mul", "SiLU", "QuantizeLinear", "Relu", "Clip")
+
+
+def conv_desc_of(graph: Graph, op: CompiledOp, epilogue: int = L.EPI_NONE) -> ConvDesc:
+    """ConvDesc of an unfused Conv op from its OpParams::Conv2d fields
+    (builder.rs:204-361) and its tensors' NHWC shapes."""
+    n, h, w, c_in = graph.tensors[op.inputs[0]].shape
+    c_out = graph.tensors[op.outputs[0]].shape[3]
+    kh, kw = op.params["kernel_shape"]
+    sh, sw = op.params["strides"]
+    return ConvDesc(n, h, w, c_in, c_out, kh, kw, sh, sw, tuple(op.params["pads"]), op.params["group"], epilogue)
+
+
+@dataclass
+class FusionStats:
+    """Fuseable patterns of a graph (fusion.rs:404-420, FusionStats)."""
+    conv_relu: int = 0            # f32 Conv -> Relu
+    silu: int = 0                 # Mul(x, Sigmoid(x))
+    conv_requant_relu_i8: int = 0  # int8 Conv -> Requantize / DequantizeLinear
+
+    def total(self) -> int:
+        return self.conv_relu + self.silu + self.conv_requant_relu_i8
+
+
+def _producers(graph: Graph) -> dict:
+    return {o: i for i, op in enumerate(graph.ops) for o in op.outputs}
+
+
+def _consumers(graph: Graph) -> dict:
+    cons = {}
+    for i, op in enumerate(graph.ops):
+        for t in op.inputs:
+            cons.setdefault(t, []).append(i)
+    return cons
+
+
+def count_fuseable_patterns(graph: Graph) -> FusionStats:
+    """count_fuseable_patterns (fusion.rs:351-402): Relu fed by a Conv with a
+    float output, Mul with a Sigmoid operand, and the int8 anchor -- a
+    Requantize (or, for SiLU, a DequantizeLinear) fed by a Conv's int32
+    accumulators."""
+    prod = _producers(graph)
+    st = FusionStats()
+    for op in graph.ops:
+        src = [graph.ops[prod[t]] for t in op.inputs if t in prod]
+        if op.op_type == "Relu" and src and src[0].op_type == "Conv" and \
+                graph.tensors[src[0].outputs[0]].dtype in ("f32", "f16"):
+            st.conv_relu += 1
+        if op.op_type == "Mul" and len(op.inputs) == 2 and any(s.op_type == "Sigmoid" for s in src):
+            st.silu += 1
+        if op.op_type in ("Requantize", "DequantizeLinear") and src and src[0].op_type == "Conv":
+            st.conv_requant_relu_i8 += 1
+    return st
+
+
+def _rebuild(graph: Graph, ops: list) -> Graph:
+    used = {t for op in ops for t in op.inputs + op.outputs} | set(graph.inputs) | set(graph.outputs)
+    tensors = {k: v for k, v in graph.tensors.items() if k in used}
+    inits = {k: v for k, v in graph.initializers.items() if k in used}
+    return Graph(tensors, ops, inits, list(graph.inputs), list(graph.outputs), dict(graph.views))
+
+
+def fuse_silu(graph: Graph) -> Graph:
+    """Pass 2 (fusion.rs:126-190): Mul(x, Sigmoid(x)), either operand order,
+    where the Sigmoid's output feeds only that Mul, becomes one SiLU(x) op
+    (y = x * sigmoid(x), the reference's order of the two ops)."""
+    prod, cons = _producers(graph), _consumers(graph)
+    drop, repl = set(), {}
+    for i, op in enumerate(graph.ops):
+        if op.op_type != "Mul" or len(op.inputs) != 2:
+            continue
+        a, b = op.inputs
+        match = None
+        for sig_in, x in ((a, b), (b, a)):
+            j = prod.get(sig_in)
+            if j is not None and graph.ops[j].op_type == "Sigmoid" and graph.ops[j].inputs[0] == x:
+                match = (j, x)
+                break
+        if match is None:
+            continue
+        j, x = match
+        sig_out = graph.ops[j].outputs[0]
+        if len(cons.get(sig_out, [])) != 1 or sig_out in graph.outputs:
+            continue
+        drop.add(j)
+        repl[i] = CompiledOp(op.name + "_silu", "SiLU", [x], list(op.outputs), {})
+    ops = [repl.get(i, op) for i, op in enumerate(graph.ops) if i not in drop]
+    return _rebuild(graph, ops)
+
+
+def fuse_conv_requant_i8(graph: Graph) -> Graph:
+    """Pass 3 (fusion.rs:192-334), extended to the contract.  The reference
+    collapses Conv -> Requantize (-> Relu) into Conv2dRequantReluI8Nhwc for
+    unbiased group-1 convs with a scalar scale.  Here the anchor is a
+    Requantize (or a DequantizeLinear, for SiLU) that is the only reader of a
+    Conv's int32 accumulators, and the op absorbs:
+      * the Conv's int32 bias (BN-folded convs: reference defect 4),
+      * a per-channel M initializer or the reference's scalar scale,
+      * Relu, or Clip(0, 6) (ReLU6, bound q6 = quantize(6, s_out)) when it is
+        the requantised tensor's only reader (the reference's live-consumer rule),
+      * SiLU: DequantizeLinear(D) -> SiLU -> QuantizeLinear(s_out), each the
+        previous op's only reader,
+      * depthwise convs (group == c_in, c_out a multiple of c_in).
+    Dilation must be 1 and other groups are refused, as the reference refuses
+    every group != 1.  The fused op keeps the Conv's name and writes the
+    chain's last tensor; a tensor the chain would swallow that is a graph
+    output stops the chain there."""
+    prod, cons = _producers(graph), _consumers(graph)
+    drop, repl = set(), {}
+    inits = dict(graph.initializers)
+
+    def only_reader(t, i):
+        c = cons.get(t, [])
+        return len(c) == 1 and c[0] == i and t not in graph.outputs
+
+    for i, op in enumerate(graph.ops):
+        if op.op_type not in ("Requantize", "DequantizeLinear") or i in drop:
+            continue
+        j = prod.get(op.inputs[0])
+        if j is None or j in drop or graph.ops[j].op_type != "Conv":
+            continue
+        conv = graph.ops[j]
+        if not only_reader(conv.outputs[0], i):
+            continue
+        pr = conv.params
+        if tuple(pr["dilations"]) != (1, 1):
+            continue
+        d = conv_desc_of(graph, conv)
+        if d.group != 1 and not (d.group == d.c_in and d.c_out % d.c_in == 0):
+            continue
+        chain = [i]
+        if op.op_type == "Requantize":
+            if len(op.inputs) > 1:
+                M = np.asarray(inits[op.inputs[1]], np.float32)
+            else:
+                M = np.full(d.c_out, np.float32(op.params["scale"]), np.float32)
+            D = M
+            out = op.outputs[0]
+            s_out = graph.tensors[out].scale
+            d.epilogue = L.EPI_NONE
+            nxt = cons.get(out, [])
+            if len(nxt) == 1 and out not in graph.outputs:
+                k = nxt[0]
+                a = graph.ops[k]
+                if a.op_type == "Relu":
+                    d.epilogue, out = L.EPI_RELU, a.outputs[0]
+                    chain.append(k)
+                elif a.op_type == "Clip" and float(a.params.get("min", 0.0)) == 0.0 and \
+                        float(a.params.get("max", 0.0)) == 6.0 and s_out:
+                    d.epilogue, out = L.EPI_RELU6, a.outputs[0]
+                    chain.append(k)
+            d.q6 = Q.relu6_ceiling(s_out) if s_out else 127
+            d.inv_s_out = float(np.float32(1.0) / np.float32(s_out)) if s_out else 0.0
+        else:
+            # SiLU: DequantizeLinear -> SiLU -> QuantizeLinear, each the previous one's only reader
+            D = np.asarray(inits[op.inputs[1]], np.float32)
+            M = D
+            t1 = op.outputs[0]
+            c1 = cons.get(t1, [])
+            if len(c1) != 1 or t1 in graph.outputs or graph.ops[c1[0]].op_type != "SiLU":
+                continue
+            k1 = c1[0]
+            t2 = graph.ops[k1].outputs[0]
+            c2 = cons.get(t2, [])
+            if len(c2) != 1 or t2 in graph.outputs or graph.ops[c2[0]].op_type != "QuantizeLinear":
+                continue
+            k2 = c2[0]
+            s_out = float(graph.ops[k2].params["scale"])
+            out = graph.ops[k2].outputs[0]
+            chain += [k1, k2]
+            d.epilogue = L.EPI_SILU
+            d.q6 = Q.relu6_ceiling(s_out)
+            d.inv_s_out = float(np.float32(1.0) / np.float32(s_out))
+        x, wn = conv.inputs[0], conv.inputs[1]
+        bn = conv.inputs[2] if len(conv.inputs) > 2 and conv.inputs[2] else None
+        if bn is None:
+            bn = conv.name + "_b"
+            inits[bn] = np.zeros(d.c_out, np.int32)
+        mn, dn = conv.name + "_M", conv.name + "_D"
+        inits[mn] = np.ascontiguousarray(M, np.float32)
+        inits[dn] = np.ascontiguousarray(D, np.float32)
+        repl[j] = CompiledOp(conv.name, "Conv2dRequantReluI8Nhwc", [x, wn, bn, mn, dn], [out], {"desc": d})
+        drop.update(chain)
+    ops = [repl.get(i, op) for i, op in enumerate(graph.ops) if i not in drop]
+    g = Graph(dict(graph.tensors), ops, inits, list(graph.inputs), list(graph.outputs), dict(graph.views))
+    return _rebuild(g, ops)
+
+
+def apply_fusion_passes(graph: Graph) -> Graph:
+    """apply_fusion_passes (fusion.rs:42): the SiLU pass, then the int8
+    Conv -> Requantize / DequantizeLinear chain pass."""
+    if any(op.op_type == "Sigmoid" for op in graph.ops):
+        graph = fuse_silu(graph)
+    if any(op.op_type in ("Requantize", "DequantizeLinear") for op in graph.ops):
+        graph = fuse_conv_requant_i8(graph)
+    return graph
+
+
 def lower_for_device(graph: Graph, residual_i8: bool = False) -> Graph:
-    """The device passes: fp16 residual fusion, the input-conv unfold / im2col,
+    """The device passes: the op-fusion passes over an unfused int8 graph, fp16
+    residual fusion, the input-conv unfold / im2col,
     int8 residual fusion (opt-in, `residual_i8`: on YOLOv8n at batch 32 the
     two pairs it takes are faster per kernel, yet the whole step measured
     2.177 ms against 2.159 without it), chained maxpools, then concat views."""
+    if any(op.op_type in UNFUSED_OPS for op in graph.ops):
+        graph = apply_fusion_passes(graph)
     if any(op.op_type == "AddF16" for op in graph.ops):
         graph = fuse_residual_f16(graph)
     if any(op.op_type == "CastF32ToF16" for op in graph.ops):
@@ -693,10 +944,11 @@ def resnet50_fp16(batch=128, size=224, classes=1000, seed=50, stages=(3, 4, 6, 3
     return b.g
 
 
-def mobilenetv2_block(batch=32, h=112, w=112, c=96, expand=6, seed=2):
+def mobilenetv2_block(batch=32, h=112, w=112, c=96, expand=6, seed=2, unfused=False):
     """MobileNetV2 inverted-residual block: 1x1 expand + ReLU6, depthwise 3x3 s1
-    + ReLU6, 1x1 project (linear), residual add with requantisation."""
-    b = GraphBuilder(seed)
+    + ReLU6, 1x1 project (linear), residual add with requantisation.
+    `unfused`: the convs in the reference quantizer's unfused form."""
+    b = GraphBuilder(seed, unfused=unfused)
     x = b.input("x", (batch, h, w, c), "i8", b.act_scale())
     e = b.conv(x, c * expand, k=1, act="relu6", name="expand")
     d = b.conv(e, c * expand, k=3, group=c * expand, act="relu6", name="dw")
@@ -710,7 +962,8 @@ def mobilenetv2_block(batch=32, h=112, w=112, c=96, expand=6, seed=2):
 YOLO_POSTPROCESS = {"img_width": 640, "img_height": 640, "conf_threshold": 0.25, "iou_threshold": 0.45}
 
 
-def yolov8n(batch=1, size=640, nc=80, reg_max=16, seed=8, width=0.25, depth=0.33, head="detections"):
+def yolov8n(batch=1, size=640, nc=80, reg_max=16, seed=8, width=0.25, depth=0.33, head="detections",
+            unfused=False):
     """YOLOv8n-architecture INT8 graph (BASELINE config 4): width 0.25, depth 0.33;
     CSPDarknet backbone of Conv(+folded BN)+SiLU layers and C2f blocks, SPPF with
     5x5 max pooling, PAN neck with nearest 2x upsampling and channel concat, and
@@ -724,10 +977,12 @@ def yolov8n(batch=1, size=640, nc=80, reg_max=16, seed=8, width=0.25, depth=0.33
     adds the exported model's Detect tail (YoloDetect: output0 f32
     [batch, 4 + nc, 8400]); "detections" also runs postprocess_yolo on the
     device (YoloPostprocess: `detections` = dw_detection records [batch, 8400],
-    image i's first `num_detections[i]` records its detections, the rest zero)."""
+    image i's first `num_detections[i]` records its detections, the rest zero).
+    `unfused`: every conv in the reference quantizer's unfused form (Conv ->
+    Requantize, or the f32 SiLU chain), for the fusion passes."""
     ch = lambda c: int(round(c * width))  # noqa: E731
     rep = lambda n: max(round(n * depth), 1)  # noqa: E731
-    b = GraphBuilder(seed, act_scale_range=(0.01, 0.1))
+    b = GraphBuilder(seed, act_scale_range=(0.01, 0.1), unfused=unfused)
     img = b.input("image", (batch, size, size, 3), "u8", None)
     s_img = float(np.float32(1.0) / np.float32(127.0))
     x = b.g.add_tensor("image_q", (batch, size, size, 3), "i8", s_img)
@@ -1001,6 +1256,30 @@ class CudaGraphRuntime:
         if t == "CastF16ToF32":
             x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
             return lambda: ops.cast_f16_to_f32(be, x, y)
+        # ---- the reference's unfused int8 ops, where the fusion passes left them
+        # (a conv whose accumulators have several readers): its own op set
+        if t == "Conv":
+            d = conv_desc_of(self.graph, op)
+            pt, pl, pb, pr = d.pads
+            bias = self.graph.initializers.get(op.inputs[2]) if len(op.inputs) > 2 and op.inputs[2] else None
+            if d.group != 1 or pt != pb or pl != pr or (bias is not None and np.any(bias)):
+                raise BackendError(L.DW_ERR_UNSUPPORTED, f"unfused Conv {op.name}: only the reference's form "
+                                   "(group 1, symmetric pads, no bias) runs unfused; it did not fuse")
+            x, wk, y = bufs[op.inputs[0]], consts[op.inputs[1]], bufs[op.outputs[0]]
+            return lambda: ops.conv2d_i8_nhwc_packed(be, x, wk, y, d.n, d.h, d.w, d.c_in, d.c_out, d.k_h, d.k_w,
+                                                     d.stride_h, d.stride_w, pt, pl)
+        if t == "Requantize":
+            M = (np.asarray(self.graph.initializers[op.inputs[1]], np.float32) if len(op.inputs) > 1
+                 else np.array([op.params["scale"]], np.float32))
+            if np.any(M != M[0]):
+                raise BackendError(L.DW_ERR_UNSUPPORTED, f"unfused Requantize {op.name}: per-channel scales run "
+                                   "only fused into the conv")
+            x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
+            scale = float(M[0])
+            return lambda: ops.requantize_i32_to_i8_packed(be, x, y, scale)
+        if t == "Relu":
+            x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
+            return lambda: ops.relu_i8_packed(be, x, y)
         raise BackendError(L.DW_ERR_UNSUPPORTED, f"unsupported op type {t} ({op.name})")
 
     # -- reference-style API ----------------------------------------------------

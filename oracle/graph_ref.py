@@ -11,6 +11,12 @@ QuantizeU8 to u8*(1/255) -> quantize_f32_to_i8 (ops.rs:3503-3525),
 YoloDetect to the exported Detect tail's f32 ops (softmax_f32, the DFL conv,
 Sub/Add/Div/Mul, sigmoid_f32_scalar; dwref_yolo_detect_i8), YoloPostprocess to
 postprocess_yolo (crates/dragonwing-onnx/src/postprocess.rs:319-340).
+The unfused int8 ops the reference's quantizer emits (quantize.rs:176-249) run
+as themselves: Conv to conv2d_i8_nhwc's int32 accumulators (+ the bias),
+Requantize to requantize_i32_to_i8 per channel, Relu to relu_i8, Clip to the
+int8 bounds quantize(min) / quantize(max), DequantizeLinear / Sigmoid / Mul /
+QuantizeLinear to the f32 SiLU chain (sigmoid_f32_scalar with the host libm's
+expf, ops.rs:1865-1870; quantize_f32_to_i8).
 
 UnfoldF32ToF16 (a device lowering of the input conv, see
 dragonwing_edge_rs_b200.graph.lower_unfold_stem_f16) is the input conversion
@@ -26,6 +32,8 @@ from __future__ import annotations
 
 import numpy as np
 
+from dragonwing_edge_rs_b200 import quantization as Q
+from dragonwing_edge_rs_b200.graph import conv_desc_of
 from oracle import dwref
 
 
@@ -60,6 +68,59 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None, return_all
             D = graph.initializers[op.inputs[4]]
             y = dwref.conv2d_fused_i8(x, w, bias, M, D if d.epilogue == dwref.EPI_SILU else None, od, threads)
             vals[op.outputs[0]] = y.reshape(shape_of(op.outputs[0]))
+        elif t == "Conv":
+            # the unfused int8 conv: conv2d_i8_nhwc (ops.rs:3086-3142) to int32
+            # accumulators, plus the int32 bias with wrapping adds
+            d = conv_desc_of(graph, op)
+            x = vals[op.inputs[0]]
+            n = x.shape[0]
+            od = dwref.conv_desc(n, d.h, d.w, d.c_in, d.c_out, d.k_h, d.k_w, d.stride_h, d.stride_w, d.pads,
+                                 d.group, 0, 127, 0.0)
+            acc = dwref.conv2d_acc_i32(x, graph.initializers[op.inputs[1]], od, threads)
+            if len(op.inputs) > 2 and op.inputs[2]:
+                bias = np.asarray(graph.initializers[op.inputs[2]], np.int32)
+                acc = (acc.reshape(-1, d.c_out).astype(np.int64) + bias).astype(np.uint32).view(np.int32)
+            vals[op.outputs[0]] = acc.reshape(shape_of(op.outputs[0]))
+        elif t == "Requantize":
+            # requantize_i32_to_i8_scalar (ops.rs:3380-3386) per output channel:
+            # (i8) roundf(clamp((f32)acc * M[c], -128, 127))
+            acc = vals[op.inputs[0]]
+            c = acc.shape[-1]
+            if len(op.inputs) > 1:
+                M = np.asarray(graph.initializers[op.inputs[1]], np.float32)
+            else:
+                M = np.full(c, np.float32(op.params["scale"]), np.float32)
+            f = acc.astype(np.float32) * M
+            q = Q.roundf_away(np.clip(f, np.float32(-128.0), np.float32(127.0)))
+            vals[op.outputs[0]] = q.astype(np.int8)
+        elif t == "Relu":
+            x = vals[op.inputs[0]]
+            vals[op.outputs[0]] = dwref.relu_i8(x).reshape(x.shape)
+        elif t == "Clip":
+            # Clip on an int8 tensor of scale s: bounds quantised with
+            # quantize_f32_to_i8 (ops.rs:3503-3525)
+            x = vals[op.inputs[0]]
+            s = graph.tensors[op.inputs[0]].scale
+            lo = int(dwref.quantize_f32_to_i8(np.array([op.params["min"]], np.float32), s)[0])
+            hi = int(dwref.quantize_f32_to_i8(np.array([op.params["max"]], np.float32), s)[0])
+            vals[op.outputs[0]] = np.minimum(np.maximum(x, np.int8(lo)), np.int8(hi)).astype(np.int8)
+        elif t == "DequantizeLinear":
+            # int32 accumulators (bias included) to f32 with the per-channel D = s_in * s_w[c]
+            acc = vals[op.inputs[0]]
+            D = np.asarray(graph.initializers[op.inputs[1]], np.float32)
+            vals[op.outputs[0]] = acc.astype(np.float32) * D
+        elif t == "Sigmoid":
+            x = vals[op.inputs[0]]
+            vals[op.outputs[0]] = dwref.sigmoid_f32(x).reshape(x.shape)
+        elif t == "Mul":
+            vals[op.outputs[0]] = vals[op.inputs[0]] * vals[op.inputs[1]]
+        elif t == "SiLU":
+            # x * sigmoid(x): the fused form of Mul(x, Sigmoid(x)), same two roundings
+            x = vals[op.inputs[0]]
+            vals[op.outputs[0]] = x * dwref.sigmoid_f32(x).reshape(x.shape)
+        elif t == "QuantizeLinear":
+            x = vals[op.inputs[0]]
+            vals[op.outputs[0]] = dwref.quantize_f32_to_i8(x, op.params["scale"]).reshape(x.shape)
         elif t == "Conv2dAddI8":  # device fusion of Conv2dRequantReluI8Nhwc -> AddQuantized(residual, conv)
             d = op.params["desc"]
             x = vals[op.inputs[0]]

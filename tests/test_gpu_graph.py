@@ -139,3 +139,68 @@ def test_pipelined_runner_matches_sequential_runs(be, depth):
     for p_, _ in hin + hout:
         be.host_free(p_)
     rt.release()
+
+
+# ------------------------------------------------- graphs in the reference's unfused form
+
+@pytest.mark.parametrize("head", ["raw", "detections"])
+def test_unfused_yolov8n_fused_on_device_matches_unfused_oracle(be, head):
+    """YOLOv8n built in the reference quantizer's unfused form (Conv ->
+    Requantize, the f32 SiLU chain DequantizeLinear -> Sigmoid -> Mul ->
+    QuantizeLinear): the runtime's fusion passes collapse it to the fused op and
+    the device's outputs are identical to the oracle running the unfused graph op
+    by op (its Sigmoid with the host libm's expf, as the reference's f32::exp)."""
+    g = G.yolov8n(batch=1, seed=8, head=head, unfused=True)
+    rt = G.CudaGraphRuntime(g, be)
+    assert not any(op.op_type in G.UNFUSED_OPS for op in rt.graph.ops)
+    x = np.random.default_rng(41).integers(0, 256, g.tensors[g.inputs[0]].nbytes).astype(np.uint8)
+    rt.set_input_bytes(g.inputs[0], x)
+    rt.run()
+    ref = run_graph(g, {g.inputs[0]: x}, threads=16)
+    for name in g.outputs:
+        got = rt.get_output_bytes(name)
+        exp = np.ascontiguousarray(ref[name]).view(np.uint8).reshape(-1)
+        assert np.array_equal(got, exp), f"{name}: {int((got != exp).sum())} of {got.size} bytes differ"
+    rt.release()
+
+
+def test_unfused_mbv2_block_fused_on_device(be):
+    g = G.mobilenetv2_block(batch=2, seed=7, unfused=True)
+    rt = G.CudaGraphRuntime(g, be)
+    assert [op.op_type for op in rt.graph.ops].count("Conv2dRequantReluI8Nhwc") == 3
+    x = np.random.default_rng(5).integers(-128, 128, g.tensors["x"].nbytes).astype(np.int8)
+    rt.set_input_bytes("x", x)
+    rt.run()
+    y = rt.get_output(g.outputs[0])
+    ref = run_graph(g, {"x": x}, threads=16)[g.outputs[0]]
+    assert np.array_equal(y, ref.reshape(y.shape))
+    rt.release()
+
+
+def test_unfused_reference_form_ops_run_on_device(be):
+    """A conv whose accumulators have two readers stays unfused; its ops in the
+    reference's own form (unbiased Conv to int32, scalar Requantize, Relu) run as
+    the device's unfused entry points and match the oracle."""
+    from dragonwing_edge_rs_b200.graph import CompiledOp, Graph
+    rng = np.random.default_rng(17)
+    g = Graph({}, [], {}, ["x"], ["r1", "q2"])
+    g.add_tensor("x", (2, 12, 10, 16), "i8", 0.02)
+    g.add_tensor("acc", (2, 12, 10, 32), "i32")
+    g.initializers["w"] = rng.integers(-127, 128, (3, 3, 16, 32)).astype(np.int8)
+    g.ops.append(CompiledOp("conv", "Conv", ["x", "w"], ["acc"],
+                            {"kernel_shape": (3, 3), "strides": (1, 1), "pads": (1, 1, 1, 1), "dilations": (1, 1),
+                             "group": 1}))
+    for t in ("q1", "r1", "q2"):
+        g.add_tensor(t, (2, 12, 10, 32), "i8", 0.05)
+    g.ops += [CompiledOp("rq1", "Requantize", ["acc"], ["q1"], {"scale": 0.0021}),
+              CompiledOp("relu", "Relu", ["q1"], ["r1"], {}),
+              CompiledOp("rq2", "Requantize", ["acc"], ["q2"], {"scale": 0.0013})]
+    rt = G.CudaGraphRuntime(g, be)
+    assert [op.op_type for op in rt.graph.ops] == ["Conv", "Requantize", "Relu", "Requantize"]
+    x = rng.integers(-64, 64, g.tensors["x"].nbytes).astype(np.int8)
+    rt.set_input_bytes("x", x)
+    rt.run()
+    ref = run_graph(g, {"x": x}, threads=8)
+    for name in g.outputs:
+        assert np.array_equal(rt.get_output(name), ref[name].reshape(g.tensors[name].shape)), name
+    rt.release()
