@@ -28,6 +28,7 @@
 // TMA is used anywhere (the same code runs on 1..8 GPUs).
 
 #include <algorithm>
+#include <tuple>
 #include <cstdlib>
 
 #include "dw_device.cuh"
@@ -88,6 +89,10 @@ struct UmmaParams {
     int chunk_elems;                        // elements per chunk (16 / esize)
     uint32_t plane_stride;                  // bytes between chunk planes of a stage (128-byte aligned)
     uint32_t b_tap_bytes;                   // bytes of one tap's weight slice in a stage (bn * bk)
+    int rw;                                 // row blocks side by side in a tile (R / rw stacked); 1 outside mode 2
+    int wres;                               // mode 2: every weight of the (single) channel tile resident in
+                                            // shared memory, loaded once per CTA; stages carry halo planes only
+    uint32_t off_w, w_bytes;                // resident weights: offset and bytes ([tap][K block][bn][bk])
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
@@ -544,12 +549,17 @@ __device__ __forceinline__ TileCoord tile_coord(const UmmaParams &p, int tile) {
     if (p.mode != 0) {
         const int tw_i = t.mt % p.tiles_w;
         const int t2 = t.mt / p.tiles_w;
-        t.oh0 = (t2 % p.tiles_h) * p.th * p.R;
+        t.oh0 = (t2 % p.tiles_h) * p.th * (p.R / p.rw);
         t.img = (t2 / p.tiles_h) * p.nb;
-        t.ow0 = tw_i * p.tw;
+        t.ow0 = tw_i * p.tw * p.rw;
     }
     return t;
 }
+
+// Output origin of row block r of a spatial tile: blocks fill the tile rw
+// across, then down.
+__device__ __forceinline__ int block_x(const UmmaParams &p, const TileCoord &t, int r) { return t.ow0 + (r % p.rw) * p.tw; }
+__device__ __forceinline__ int block_y(const UmmaParams &p, const TileCoord &t, int r) { return t.oh0 + (r / p.rw) * p.th; }
 
 // Row blocks of the tile that hold at least one in-range output pixel (the
 // others are neither loaded nor stored).
@@ -561,6 +571,13 @@ __device__ __forceinline__ int valid_blocks(const UmmaParams &p, const TileCoord
     }
     const int left = (p.ho - t.oh0 + p.th - 1) / p.th;
     return left < p.R ? left : p.R;
+}
+
+// Row block r holds at least one in-range output pixel (its TMA store starts
+// inside the output; a block past the right or bottom edge is skipped).
+__device__ __forceinline__ bool block_valid(const UmmaParams &p, const TileCoord &t, int r, int nrb) {
+    if (p.mode != 2) return r < nrb;
+    return block_x(p, t, r) < p.wo && block_y(p, t, r) < p.ho;
 }
 
 // int8 residual (kFm & 2): the staging unit already holds the residual's 16
@@ -611,7 +628,8 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
     uint64_t *drain_bar = tempty_bar + 2;           // [1] MMA drain on abort
     uint64_t *res_bar = drain_bar + 1;              // [2] staging buffer free for the next tile (fp16: residual in)
     uint64_t *ready_bar = res_bar + 2;              // [2] staging buffer holds a finished tile
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ready_bar + 2);
+    uint64_t *w_bar = ready_bar + 2;                // [1] resident weights landed (mode 2, wres)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(w_bar + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -630,6 +648,7 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
             mbar_init(smem_u32(&tempty_bar[a]), kEpiWarps);
         }
         mbar_init(smem_u32(drain_bar), 1);
+        mbar_init(smem_u32(w_bar), 1);
         for (int b = 0; b < 2; b++) {
             mbar_init(smem_u32(&res_bar[b]), 1);
             mbar_init(smem_u32(&ready_bar[b]), kEpiWarps);
@@ -665,6 +684,17 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
             uint32_t ph = 0;
             uint32_t issued_mask = 0, last_parity = 0;  // per stage: issued at least once / parity of last issue
             bool ok = true;
+            const bool w_issued = p.wres && (int)blockIdx.x < p.num_tiles;
+            if (w_issued) {
+                // resident weights: every (tap, K block) slice of the channel tile, once
+                const uint32_t wb = smem_u32(&w_bar[0]);
+                mbar_expect_tx(wb, p.w_bytes);
+                const uint32_t w_dst = smem_u32(smem + p.off_w);
+                for (int t = 0; t < p.taps; t++)
+                    for (int cb = 0; cb < p.cblocks; cb++)
+                        tma_load_3d(w_dst + (uint32_t)(t * p.cblocks + cb) * p.b_tap_bytes, &tmap_b, wb,
+                                    cb * p.bk_elems, t, 0);
+            }
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 const TileCoord tc = tile_coord(p, tile);
                 const int nrb = valid_blocks(p, tc);
@@ -686,12 +716,14 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                         // weight box per tap
                         const int real = min(p.cps, p.chunks - it * p.cps);
                         mbar_expect_tx(fb, (uint32_t)real * (uint32_t)(p.hw * p.hh * 16) +
-                                               (uint32_t)p.taps * p.b_tx_bytes);
+                                               (p.wres ? 0u : (uint32_t)p.taps * p.b_tx_bytes));
                         for (int j = 0; j < real; j++)
                             tma_load_4d(a_dst + (uint32_t)j * p.plane_stride, &tmap_a, fb,
                                         it * p.bk_elems + j * p.chunk_elems, tc.ow0 - p.pl, tc.oh0 - p.pt, tc.img);
-                        for (int t = 0; t < p.taps; t++)
-                            tma_load_3d(b_dst + (uint32_t)t * p.b_tap_bytes, &tmap_b, fb, it * p.bk_elems, t, tc.n0);
+                        if (!p.wres)
+                            for (int t = 0; t < p.taps; t++)
+                                tma_load_3d(b_dst + (uint32_t)t * p.b_tap_bytes, &tmap_b, fb, it * p.bk_elems, t,
+                                            tc.n0);
                         issued_mask |= 1u << s;
                         last_parity = (last_parity & ~(1u << s)) | (ph << s);
                         if (++s == p.stages) { s = 0; ph ^= 1; }
@@ -716,6 +748,11 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
             }
             if (!ok) {
                 // Abort: wait (bounded) for this CTA's own copies still in flight.
+                if (w_issued) {
+                    const uint64_t t0 = globaltimer_ns();
+                    while (!mbar_try_wait(smem_u32(&w_bar[0]), 0) && globaltimer_ns() - t0 < p.wait_cap_ns) {
+                    }
+                }
                 for (int st = 0; st < p.stages; st++) {
                     if (!(issued_mask & (1u << st))) continue;
                     const uint32_t par = (last_parity >> st) & 1u;
@@ -740,6 +777,21 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
             bool ok = true;
             const int kn_full = p.bk >> 5;
             const int kn_last = (p.c_in * p.esize - (p.cblocks - 1) * p.bk + 31) >> 5;
+            const uint32_t w_base = smem_u32(smem + p.off_w);
+            if (p.wres && (int)blockIdx.x < p.num_tiles && !mbar_wait(smem_u32(&w_bar[0]), 0, p, abort_flag, 7))
+                ok = false;
+            // halo mode: per row block, its 16 B units from the tile's halo origin
+            // ((r / rw) * 16 halo rows + (r % rw) * 8 pixels), and the descriptor's
+            // constant bits (SBO = one halo row, version 1, no swizzle): computed
+            // once, so the issue loop does no division
+            const uint32_t h_sbo = (uint32_t)p.hw * 16u;
+            uint32_t roff16[8];
+#pragma unroll
+            for (int r = 0; r < 8; r++)
+                roff16[r] = p.mode == 2 ? (((uint32_t)(r / p.rw) * 16u * h_sbo) + (uint32_t)(r % p.rw) * 128u) >> 4 : 0u;
+            const uint64_t a_hi = ((uint64_t)((h_sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+            const uint64_t lbo_plane = (uint64_t)((p.plane_stride >> 4) & 0x3FFFu) << 16;
+            const uint64_t lbo_16 = (uint64_t)1u << 16;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, local++) {
                 const int acc = local & 1;
                 const uint32_t acc_ph = (local >> 1) & 1;
@@ -760,19 +812,23 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                         // zero-filled channels past c_in), so no plane is left unloaded.
                         const int real = min(p.cps, p.chunks - it * p.cps);
                         const int kn = (real + 1) >> 1;
-                        const uint32_t sbo = (uint32_t)p.hw * 16u;
-                        const uint32_t rb = 16u * sbo;  // 16 output rows per row block
-                        for (int t = 0; t < p.taps; t++) {
-                            const uint32_t at = a_addr + (uint32_t)tapc[t].x;
-                            const uint32_t bt = b_addr + (uint32_t)t * p.b_tap_bytes;
+                        const uint32_t bstep = (uint32_t)p.cblocks * p.b_tap_bytes;  // resident: next tap's slice
+                        uint32_t bt = p.wres ? w_base + (uint32_t)it * p.b_tap_bytes : b_addr;
+                        const uint32_t bt_step = p.wres ? bstep : p.b_tap_bytes;
+                        for (int t = 0; t < p.taps; t++, bt += bt_step) {
+                            const uint32_t at16 = (a_addr + (uint32_t)tapc[t].x) >> 4;
                             for (int k = 0; k < kn; k++) {
-                                const uint32_t lbo = (2 * k + 1 < real) ? p.plane_stride : 16u;
+                                const uint64_t hi = a_hi | ((2 * k + 1 < real) ? lbo_plane : lbo_16);
+                                const uint32_t a16 = at16 + (uint32_t)(2 * k) * (p.plane_stride >> 4);
                                 const uint64_t bd = smem_desc(bt + 32 * k, p.desc_hi);
                                 const uint32_t accf = (it > 0 || t > 0 || k > 0) ? 1u : 0u;
-                                for (int r = 0; r < p.R; r++) {
-                                    const uint64_t ad =
-                                        smem_desc_noswz(at + (uint32_t)(2 * k) * p.plane_stride + (uint32_t)r * rb, lbo, sbo);
-                                    tc_mma<kF16>(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, accf);
+#pragma unroll
+                                for (int r = 0; r < 8; r++) {
+                                    if (r < p.R) {
+                                        // block r: 16 output rows x 8 columns of the tile
+                                        const uint64_t ad = hi | (uint64_t)((a16 + roff16[r]) & 0x3FFFu);
+                                        tc_mma<kF16>(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, accf);
+                                    }
                                 }
                             }
                         }
@@ -993,16 +1049,21 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                     uint8_t *stage = out_stage + (size_t)sb * p.out_bytes;
                     // bytes per row block: its box (128 rows, or tw x th x nb pixels in mode 1)
                     const int box_rows = p.mode == 0 ? kBM : p.tw * p.th * p.nb;
-                    mbar_expect_tx(bar, (uint32_t)(nrb * box_rows * p.bn * es));
-                    for (int r = 0; r < nrb; r++)
+                    int nvalid = 0;
+                    for (int r = 0; r < p.R; r++) nvalid += block_valid(p, tc, r, nrb) ? 1 : 0;
+                    mbar_expect_tx(bar, (uint32_t)(nvalid * box_rows * p.bn * es));
+                    for (int r = 0; r < p.R; r++) {
+                        if (!block_valid(p, tc, r, nrb)) continue;
                         for (int sl = 0; sl < slabs; sl++) {
                             const uint32_t dst =
                                 smem_u32(stage + (size_t)r * kBM * p.bn * es + (size_t)sl * kBM * sw_ch * es);
                             if (p.mode == 0)
                                 tma_load_2d(dst, &tmap_r, bar, tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
                             else
-                                tma_load_4d(dst, &tmap_r, bar, tc.n0 + sl * sw_ch, tc.ow0, tc.oh0 + r * p.th, tc.img);
+                                tma_load_4d(dst, &tmap_r, bar, tc.n0 + sl * sw_ch, block_x(p, tc, r),
+                                            block_y(p, tc, r), tc.img);
                         }
+                    }
                     res_out[sb] = true;
                 } else {
                     mbar_arrive(bar);
@@ -1022,14 +1083,16 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                 const TileCoord tc = tile_coord(p, tile);
                 const int nrb = valid_blocks(p, tc);
                 uint8_t *stage = out_stage + (size_t)sb * p.out_bytes;
-                for (int r = 0; r < nrb; r++) {
+                for (int r = 0; r < p.R; r++) {
+                    if (!block_valid(p, tc, r, nrb)) continue;
                     for (int sl = 0; sl < slabs; sl++) {
                         const uint32_t src =
                             smem_u32(stage + (size_t)r * kBM * p.bn * es + (size_t)sl * kBM * sw_ch * es);
                         if (p.mode == 0)
                             tma_store_2d(&tmap_y, src, tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
                         else
-                            tma_store_4d(&tmap_y, src, tc.n0 + sl * sw_ch, tc.ow0, tc.oh0 + r * p.th, tc.img);
+                            tma_store_4d(&tmap_y, src, tc.n0 + sl * sw_ch, block_x(p, tc, r), block_y(p, tc, r),
+                                         tc.img);
                     }
                 }
                 bulk_commit();
@@ -1120,22 +1183,25 @@ CUtensorMapSwizzle swizzle_enum(int bk) {
 
 constexpr size_t kSmemLimit = 227 * 1024 - sizeof(int4) * kTapTable;  // dynamic share (the tap table is static)
 
-// Halo mode plan (stride-1 convs with several taps).  Output tiles are 8
-// columns x 16 rows per 128-row block, R blocks stacked vertically; a stage
-// holds, for one K block of bk bytes, the halo plane of each 16-byte chunk and
-// every tap's bn x bk weight slice.
+// Halo mode plan (stride-1 convs with several taps).  A row block is 8 output
+// columns x 16 rows (the 8 rows of a core matrix are 8 neighbouring pixels);
+// a tile is rw blocks across and R / rw down.  A stage holds, for one K block
+// of bk bytes, the halo plane of each 16-byte channel chunk, and either every
+// tap's bn x bk weight slice or -- resident weights, when the conv has a single
+// channel tile and all its weights fit beside the stages -- nothing else (the
+// weights are loaded once per CTA).
 struct HaloPlan {
     bool ok = false;
-    int R = 1, bn = 16, bk = 32, tiles_w = 1, tiles_h = 1, n_tiles = 1;
-    uint32_t plane = 0;
+    int R = 1, rw = 1, bn = 16, bk = 32, tiles_w = 1, tiles_h = 1, n_tiles = 1, wres = 0;
+    uint32_t plane = 0, w_bytes = 0;
 };
 
-uint32_t halo_plane_bytes(const dw_conv_desc &d, int R) {
-    return (uint32_t)(((size_t)(16 * R + d.k_h - 1) * (size_t)(8 + d.k_w - 1) * 16 + 127) & ~size_t(127));
+uint32_t halo_plane_bytes(const dw_conv_desc &d, int rw, int rh) {
+    return (uint32_t)(((size_t)(16 * rh + d.k_h - 1) * (size_t)(8 * rw + d.k_w - 1) * 16 + 127) & ~size_t(127));
 }
 
-// Output-channel tile for the halo mode: all of c_out when the taps' weight
-// slices stay small, else the width <= cap with the fewest padded columns.
+// Output-channel tile for the per-stage weights: all of c_out when the taps'
+// weight slices stay small, else the width <= cap with the fewest padded columns.
 int halo_bn(int c_out16, int taps) {
     int cap = (int)(40 * 1024 / ((size_t)taps * 32)) / 16 * 16;
     cap = std::max(16, std::min(256, cap));
@@ -1154,62 +1220,123 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
     const int taps = d.k_h * d.k_w;
     if (flat || d.stride_h != 1 || d.stride_w != 1 || taps < 2 || taps > kTapTable) return h;
     if ((d.c_in * esize) % 16 || (esize == 2 && d.c_in % 16)) return h;  // fp16: whole 32-byte K steps
-    // Channel rows of at most 32 bytes: there the per-tap producer's boxes are
-    // half empty and re-read every pixel nine times, and the halo stage (every
-    // tap's weight slice) stays small.  With wider rows a stage's weight boxes
-    // need 32-byte K blocks to fit, whose TMA requests cost more than the halo
-    // saves (measured on B200: YOLOv8n's 64-channel 3x3s 23 -> 27 us, ResNet-50's
-    // 14x14 256-channel fp16 3x3s 51 -> 141 us; 16 and 32 channels 77 -> 59 and
-    // 40 -> 30 us).
-    if (d.c_in * esize > 32 && !getenv("DW_UMMA_HALO_WIDE")) return h;
     if (8 + d.k_w - 1 > 256 || 16 + d.k_h - 1 > 256) return h;
     if (const char *e = getenv("DW_UMMA_HALO"))  // tuning switch: 0 keeps the per-tap producer
         if (atoi(e) == 0) return h;
-    // pixel utilisation of 8 x 16 tiles; small maps keep the per-tap producer
+    // pixel utilisation of 8 x 16 blocks; small maps keep the per-tap producer
     // (whole images side by side in one row block)
-    const int tiles_w = (wo + 7) / 8;
-    const double util = (double)ho * wo / ((double)tiles_w * 8 * (double)((ho + 15) / 16) * 16);
+    const double util = (double)ho * wo / ((double)((wo + 7) / 8) * 8 * (double)((ho + 15) / 16) * 16);
     if (util < 0.7) return h;
     const int c_out16 = ((d.c_out + 15) / 16) * 16;
+    const int cbytes = d.c_in * esize;
+    const int chunks = cbytes / 16;
+    const size_t chan = al1k(sizeof(ChanSmem));
+    int r_env = 8;
+    if (const char *e = getenv("DW_UMMA_RMAX")) {  // tuning override, as for the per-tap producer
+        const int v = atoi(e);
+        if (v >= 1 && v <= 8) r_env = v;
+    }
+    // K blocks: the fewest padded bytes (cblocks * bk - c_in bytes), then the widest
+    auto pick_bk_res = [&]() {
+        int best = 32;
+        long best_pad = -1;
+        for (int bk : {128, 64, 32}) {
+            const long pad = (long)((cbytes + bk - 1) / bk) * bk - cbytes;
+            if (best_pad < 0 || pad < best_pad) { best_pad = pad; best = bk; }
+        }
+        return best;
+    };
+    // Block arrangements, cheapest first.  Cost = waves of tiles over the SMs x
+    // (blocks per tile + 2 for a tile's fixed overhead), so padding (more
+    // tiles), wave quantisation and per-tile overhead all count; then the least
+    // halo per output pixel.  The overhead constant reproduces the ranking
+    // measured on B200 for YOLOv8n's 3x3 layers (160x160 c16, 80x80 c32/c64,
+    // 40x40 c64, every arrangement).  A lexicographic key: a strict weak ordering.
+    struct Arr { int rw, rh; long tiles; };
+    auto arrangements = [&](int n_tiles, int rmax, Arr *out) {
+        int n = 0;
+        for (int rw : {1, 2, 4, 8})
+            for (int rh = 1; rw * rh <= rmax; rh++) {
+                const long tw = (wo + 8 * rw - 1) / (8 * rw), th = (ho + 16 * rh - 1) / (16 * rh);
+                out[n++] = Arr{rw, rh, (long)d.n * tw * th * n_tiles};
+            }
+        auto key = [&](const Arr &a) {
+            const long waves = (a.tiles + be->sm_count - 1) / be->sm_count;
+            const long cost = waves * (a.rw * a.rh + 2);
+            const double halo = (double)(16 * a.rh + d.k_h - 1) * (8 * a.rw + d.k_w - 1) / (double)(a.rw * a.rh * kBM);
+            return std::make_tuple(cost, halo, a.rw);
+        };
+        std::sort(out, out + n, [&](const Arr &a, const Arr &b) { return key(a) < key(b); });
+        if (const char *e = getenv("DW_UMMA_ARR")) {  // tuning override "rw,rh": that arrangement only
+            int rw = 0, rh = 0;
+            if (sscanf(e, "%d,%d", &rw, &rh) == 2)
+                for (int i = 0; i < n; i++)
+                    if (out[i].rw == rw && out[i].rh == rh) {
+                        out[0] = out[i];
+                        return 1;
+                    }
+        }
+        return n;
+    };
+    Arr arr[64];
+    // 1. resident weights: one channel tile, all weights beside >= 3 halo
+    // stages.  Arrangements in cost order; for each, the K block with the least
+    // padding first, then narrower ones (smaller stages).  A single row block
+    // per tile loses to the per-tap producer once channel rows are wider than
+    // 32 bytes (measured: YOLOv8n's 40x40 128 -> 80 3x3 42 vs 32 us, ResNet-50's
+    // 56x56 fp16 64 -> 64 3x3 185 vs 122 us), so such plans are not taken.
+    if (c_out16 <= 256 && !getenv("DW_UMMA_NO_WRES")) {
+        const int bn = c_out16, bk0 = pick_bk_res();
+        const int n = arrangements(1, std::min(r_env, std::max(1, std::min(8, 256 / bn))), arr);
+        for (int i = 0; i < n; i++) {
+            const int R = arr[i].rw * arr[i].rh;
+            if (R == 1 && cbytes > 32) continue;
+            // wide rows on maps the tiles cover with > 30% padding (40x40 under
+            // 16 x 16 tiles): the per-tap producer's tiles fit them closer
+            // (YOLOv8n's 40x40 3x3s: 24.4 vs 24.9 us at 64 channels, 31 vs 33-35 us at 128)
+            if (cbytes > 32 && (double)arr[i].tiles * R * kBM > 1.3 * (double)d.n * ho * wo) continue;
+            const uint32_t plane = halo_plane_bytes(d, arr[i].rw, arr[i].rh);
+            for (int bk : {bk0, 64, 32}) {
+                if (bk > bk0) continue;
+                const int cblocks = (cbytes + bk - 1) / bk;
+                const size_t w_bytes = (size_t)taps * cblocks * bn * bk;
+                const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane);
+                const size_t fixed = 1024 + al1k((size_t)R * kBM * bn * esize) + al1k(w_bytes) + chan + 512;
+                if (fixed < kSmemLimit && (kSmemLimit - fixed) / stage >= 3) {
+                    h.ok = true; h.wres = 1; h.R = R; h.rw = arr[i].rw; h.bn = bn; h.bk = bk; h.n_tiles = 1;
+                    h.tiles_w = (wo + 8 * h.rw - 1) / (8 * h.rw);
+                    h.tiles_h = (ho + 16 * arr[i].rh - 1) / (16 * arr[i].rh);
+                    h.plane = plane;
+                    h.w_bytes = (uint32_t)w_bytes;
+                    return h;
+                }
+            }
+        }
+    }
+    // 2. per-stage weights, for channel rows of at most 32 bytes: there the
+    // per-tap producer's boxes are half empty and re-read every pixel nine
+    // times, and a stage with every tap's weight slice stays small.  With wider
+    // rows a stage's weight boxes need 32-byte K blocks to fit, whose TMA
+    // requests cost more than the halo saves (measured on B200: YOLOv8n's
+    // 64-channel 3x3s 23 -> 27 us, ResNet-50's 14x14 256-channel fp16 3x3s
+    // 51 -> 141 us; 16 and 32 channels 77 -> 59 and 40 -> 30 us).
+    if (cbytes > 32 && !getenv("DW_UMMA_HALO_WIDE")) return h;
     h.bn = halo_bn(c_out16, taps);
     h.n_tiles = (d.c_out + h.bn - 1) / h.bn;
-    h.tiles_w = tiles_w;
-    const int rmax = std::max(1, std::min(8, 256 / h.bn));
-    // row blocks per tile: the fewest padded rows; among those the most blocks
-    // that still give every SM a tile, else the fewest blocks
-    long min_pad = -1;
-    for (int R = 1; R <= rmax; R++) {
-        const long pad = (long)((ho + 16 * R - 1) / (16 * R)) * 16 * R;
-        if (min_pad < 0 || pad < min_pad) min_pad = pad;
-    }
-    int pick = 0;
-    for (int R = rmax; R >= 1 && !pick; R--) {
-        const long pad = (long)((ho + 16 * R - 1) / (16 * R)) * 16 * R;
-        const long tiles = (long)d.n * tiles_w * ((ho + 16 * R - 1) / (16 * R)) * h.n_tiles;
-        if (pad * 20 <= min_pad * 21 && tiles >= be->sm_count) pick = R;
-    }
-    for (int R = 1; R <= rmax && !pick; R++) {
-        const long pad = (long)((ho + 16 * R - 1) / (16 * R)) * 16 * R;
-        if (pad * 20 <= min_pad * 21) pick = R;
-    }
-    const size_t chan = al1k(sizeof(ChanSmem));
-    const int chunks = d.c_in * esize / 16;
-    const int cap_bk = ((d.c_in * esize + 31) / 32) * 32;
-    // K block: the widest that leaves room for three stages (two at bk = 32),
-    // then fewer row blocks
-    for (int R = pick; R >= 1; R--) {
-        const uint32_t plane = halo_plane_bytes(d, R);
+    const int cap_bk = ((cbytes + 31) / 32) * 32;
+    const int n = arrangements(h.n_tiles, std::min(r_env, std::max(1, std::min(8, 256 / h.bn))), arr);
+    for (int i = 0; i < n; i++) {
+        const int R = arr[i].rw * arr[i].rh;
+        const uint32_t plane = halo_plane_bytes(d, arr[i].rw, arr[i].rh);
         const size_t fixed = 1024 + al1k((size_t)R * kBM * h.bn * esize) + chan + 512;
         for (int bk : {128, 64, 32}) {
             if (bk > cap_bk && bk != 32) continue;
             const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane) + al1k((size_t)taps * h.bn * bk);
             const size_t fit = fixed < kSmemLimit ? (kSmemLimit - fixed) / stage : 0;
             if (fit >= 3 || (bk == 32 && fit >= 2)) {
-                h.R = R;
-                h.bk = bk;
-                h.plane = plane;
-                h.tiles_h = (ho + 16 * R - 1) / (16 * R);
-                h.ok = true;
+                h.ok = true; h.R = R; h.rw = arr[i].rw; h.bk = bk; h.plane = plane;
+                h.tiles_w = (wo + 8 * h.rw - 1) / (8 * h.rw);
+                h.tiles_h = (ho + 16 * arr[i].rh - 1) / (16 * arr[i].rh);
                 return h;
             }
         }
@@ -1288,6 +1415,7 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     p.n_img = d.n; p.ho = ho; p.wo = wo; p.c_out = d.c_out;
     p.taps = d.k_h * d.k_w; p.kw = d.k_w; p.sh = d.stride_h; p.sw = d.stride_w; p.pt = d.pad_t; p.pl = d.pad_l;
     p.c_in = d.c_in;
+    p.rw = 1;
     const HaloPlan hp = plan_halo(be, d, ho, wo, esize, flat);
     if (hp.ok) {
         p.mode = 2;
@@ -1297,13 +1425,16 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         p.bn = hp.bn;
         p.n_tiles = hp.n_tiles;
         p.R = hp.R;
+        p.rw = hp.rw;
         p.tw = 8; p.th = 16; p.nb = 1;
         p.tiles_w = hp.tiles_w;
         p.tiles_h = hp.tiles_h;
         p.m_tiles = d.n * p.tiles_w * p.tiles_h;
         p.num_tiles = p.m_tiles * p.n_tiles;
-        p.hw = 8 + d.k_w - 1;
-        p.hh = 16 * p.R + d.k_h - 1;
+        p.hw = 8 * p.rw + d.k_w - 1;
+        p.hh = 16 * (p.R / p.rw) + d.k_h - 1;
+        p.wres = hp.wres;
+        p.w_bytes = hp.w_bytes;
         p.chunks = d.c_in * esize / 16;
         p.cps = p.bk / 16;
         p.chunk_elems = 16 / esize;
@@ -1371,7 +1502,12 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
             const int v = atoi(e);
             if (v >= 16 && v <= 256 && v % 16 == 0) p.bn = v;
         }
-        plan_tiles(p.bn, 8);
+        int r_cap = 8;
+        if (const char *e = getenv("DW_UMMA_RMAX")) {  // tuning override: at most this many row blocks per tile
+            const int v = atoi(e);
+            if (v >= 1 && v <= 8) r_cap = v;
+        }
+        plan_tiles(p.bn, r_cap);
         // Small problems (tiles for fewer than half the SMs): fewer row blocks per
         // tile, then narrower tiles (down to 64 channels), until half the SMs have a
         // tile -- more CTAs stream the long K loops side by side; the extra reads of
@@ -1386,20 +1522,26 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     p.b_tx_bytes = (uint32_t)(p.bn * p.bk);
     p.a_stage_bytes = (uint32_t)al1k((size_t)p.R * kBM * p.bk);
     p.b_stage_bytes = (uint32_t)al1k((size_t)p.bn * p.bk);
-    if (p.mode == 2) {  // the loaded chunk planes; every tap's weight slice
+    if (p.mode == 2) {  // the loaded chunk planes; every tap's weight slice unless they are resident
         p.a_stage_bytes = (uint32_t)al1k((size_t)std::min(p.cps, p.chunks) * p.plane_stride);
-        p.b_stage_bytes = (uint32_t)al1k((size_t)p.taps * p.b_tap_bytes);
+        p.b_stage_bytes = p.wres ? 0u : (uint32_t)al1k((size_t)p.taps * p.b_tap_bytes);
     }
+    const size_t w_region = p.wres ? al1k(p.w_bytes) : 0;
     const size_t out_bytes = al1k((size_t)p.R * kBM * p.bn * esize);
     const size_t chan_bytes = al1k(sizeof(ChanSmem));
     // two staging buffers when they fit beside at least two pipeline stages
     const size_t stage_pair = p.a_stage_bytes + p.b_stage_bytes;
-    p.nbuf = (1024 + 2 * out_bytes + chan_bytes + 512 + 2 * stage_pair <= kSmemLimit) ? 2 : 1;
+    const size_t min_stages = p.wres ? 3 : 2;
+    p.nbuf = (1024 + 2 * out_bytes + chan_bytes + 512 + w_region + min_stages * stage_pair <= kSmemLimit) ? 2 : 1;
+    if (const char *e = getenv("DW_UMMA_NBUF"))  // tuning override: 1 staging buffer (room for more stages)
+        if (atoi(e) == 1) p.nbuf = 1;
     p.out_bytes = (uint32_t)out_bytes;
-    const size_t fixed = 1024 /*align slack*/ + p.nbuf * out_bytes + chan_bytes + 512 /*barriers*/;
+    const size_t fixed = 1024 /*align slack*/ + p.nbuf * out_bytes + chan_bytes + 512 /*barriers*/ + w_region;
     int stages = (int)((kSmemLimit - fixed) / stage_pair);
     p.stages = std::max(2, std::min(stages, kMaxStages));
-    p.off_out = (uint32_t)((size_t)p.stages * stage_pair);
+    // [stages x (A, B)] [resident weights] [staging x nbuf] [channel parameters] [barriers]
+    p.off_w = (uint32_t)((size_t)p.stages * stage_pair);
+    p.off_out = (uint32_t)(p.off_w + w_region);
     p.off_chan = (uint32_t)(p.off_out + p.nbuf * out_bytes);
     p.off_bars = (uint32_t)(p.off_chan + chan_bytes);
     p.acc_bound = (long long)p.taps * d.c_in * 16384ll;
