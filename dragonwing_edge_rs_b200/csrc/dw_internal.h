@@ -90,6 +90,9 @@ dw_status launch_resize_nearest_i8(dw_backend *be, const int8_t *x, int8_t *y, i
                                    int wo, int c);
 dw_status launch_repack_hwio_to_ohwi(dw_backend *be, const int8_t *w, int8_t *out, int taps, int c_in,
                                      int c_out);
+// The repack plus m[0..c_out) = v, in one launch.
+dw_status launch_repack_hwio_to_ohwi_fill(dw_backend *be, const int8_t *w, int8_t *out, int taps, int c_in, int c_out,
+                                          float *m, float v);
 dw_status launch_transpose_kn_to_nk(dw_backend *be, const int8_t *b, int8_t *out, int k, int n);
 dw_status launch_expire_wait(dw_backend *be, uint64_t cap_ns);
 

@@ -541,6 +541,23 @@ __global__ void k_repack_hwio_to_ohwi(const T *__restrict__ w, T *__restrict__ o
     }
 }
 
+// The reference-signature fused conv's per-call preparation in one launch: the
+// HWIO -> OHWI repack, and its scalar requant scale spread over c_out slots.
+__global__ void k_repack_hwio_to_ohwi_fill(const int8_t *__restrict__ w, int8_t *__restrict__ o, int taps, int c_in,
+                                           int c_out, float *__restrict__ m, float v) {
+    const size_t total = (size_t)taps * c_in * c_out;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t first = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    for (size_t i = first; i < (size_t)c_out; i += stride) m[i] = v;
+    for (size_t i = first; i < total; i += stride) {
+        const int ic = (int)(i % c_in);
+        const size_t r = i / c_in;
+        const int t = (int)(r % taps);
+        const int oc = (int)(r / taps);
+        o[i] = w[((size_t)t * c_in + ic) * c_out + oc];
+    }
+}
+
 // B [k][n] row-major -> [n][k] (K-major).
 template <typename T>
 __global__ void k_transpose_kn_to_nk(const T *__restrict__ b, T *__restrict__ o, int k, int n) {
@@ -799,6 +816,13 @@ dw_status launch_repack_hwio_to_ohwi(dw_backend *be, const int8_t *w, int8_t *ou
     size_t items = (size_t)taps * c_in * c_out;
     k_repack_hwio_to_ohwi<int8_t><<<grid_for(be, items), kThreads, 0, be->stream>>>(w, out, taps, c_in, c_out);
     return dw_after_launch(be, "repack_hwio_to_ohwi");
+}
+
+dw_status launch_repack_hwio_to_ohwi_fill(dw_backend *be, const int8_t *w, int8_t *out, int taps, int c_in, int c_out,
+                                          float *m, float v) {
+    const size_t items = std::max<size_t>((size_t)taps * c_in * c_out, (size_t)c_out);
+    k_repack_hwio_to_ohwi_fill<<<grid_for(be, items), kThreads, 0, be->stream>>>(w, out, taps, c_in, c_out, m, v);
+    return dw_after_launch(be, "repack_hwio_to_ohwi_fill");
 }
 
 dw_status launch_repack_hwio_to_ohwi_f16(dw_backend *be, const uint16_t *w, uint16_t *out, int taps, int c_in,

@@ -181,13 +181,11 @@ DW_API dw_status dw_conv2d_requant_relu_i8(dw_backend *be, const dw_buf *input, 
     DW_TRY(dw_scratch(be, off_m + 4 * c_out, &scr));
     dw_buf wprep{scr, expected_kernel, false};
     dw_buf mbuf{(char *)scr + off_m, 4 * c_out, false};
-    DW_TRY(dw::launch_repack_hwio_to_ohwi(be, (const int8_t *)kernel_hwio->ptr, (int8_t *)wprep.ptr, (int)(k_h * k_w),
-                                          (int)c_in, (int)c_out));
-    std::vector<float> ms(c_out, requant_scale);
-    DW_TRY(dw_cuda_check(be, cudaMemcpyAsync(mbuf.ptr, ms.data(), 4 * c_out, cudaMemcpyHostToDevice, be->stream),
-                         "conv_fused: upload requant scale"));
-    // The host vector must outlive the async copy from pageable memory: cudaMemcpyAsync
-    // from pageable memory is staged synchronously before it returns.
+    // the weights repacked and the scalar scale spread per channel by one kernel on
+    // the backend stream (no host copy: the call stays asynchronous)
+    DW_TRY(dw::launch_repack_hwio_to_ohwi_fill(be, (const int8_t *)kernel_hwio->ptr, (int8_t *)wprep.ptr,
+                                               (int)(k_h * k_w), (int)c_in, (int)c_out, (float *)mbuf.ptr,
+                                               requant_scale));
     dw::EpiParams ep{nullptr, (const float *)mbuf.ptr, nullptr, d.epilogue, 127, 0.0f};
     return conv_dispatch(be, &d, ho, wo, input, &wprep, ep, output, "conv_fused");
 }

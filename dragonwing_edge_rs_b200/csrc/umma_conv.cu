@@ -89,10 +89,6 @@ struct UmmaParams {
     int chunk_elems;                        // elements per chunk (16 / esize)
     uint32_t plane_stride;                  // bytes between chunk planes of a stage (128-byte aligned)
     uint32_t b_tap_bytes;                   // bytes of one tap's weight slice in a stage (bn * bk)
-    int cw;                                 // mode 2: bytes of channels per halo plane row (16: one chunk, no
-                                            // swizzle; 128: a natural-layout slab with the 128-byte swizzle)
-    uint64_t a_desc_hi;                     // mode 2, cw = 128: A descriptor high word (SBO = one halo row,
-                                            // version 1, 128-byte swizzle); the base offset is added per start
     int rw;                                 // row blocks side by side in a tile (R / rw stacked); 1 outside mode 2
     int wres;                               // mode 2: every weight of the (single) channel tile resident in
                                             // shared memory, loaded once per CTA; stages carry halo planes only
@@ -719,7 +715,7 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                         // one halo box per chunk (zero fill = the conv's padding), one
                         // weight box per tap
                         const int real = min(p.cps, p.chunks - it * p.cps);
-                        mbar_expect_tx(fb, (uint32_t)real * (uint32_t)(p.hw * p.hh * p.cw) +
+                        mbar_expect_tx(fb, (uint32_t)real * (uint32_t)(p.hw * p.hh * 16) +
                                                (p.wres ? 0u : (uint32_t)p.taps * p.b_tx_bytes));
                         for (int j = 0; j < real; j++)
                             tma_load_4d(a_dst + (uint32_t)j * p.plane_stride, &tmap_a, fb,
@@ -772,7 +768,7 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
         // table's x; the producer does not use the table in this mode)
         if (p.mode == 2)
             for (int t = lane; t < min(p.taps, kTapTable); t += 32)
-                tapc[t].x = ((t / p.kw) * p.hw + (t % p.kw)) * p.cw;
+                tapc[t].x = ((t / p.kw) * p.hw + (t % p.kw)) * 16;
         __syncwarp();
         if (lane == 0) {
             int s = 0;
@@ -788,13 +784,11 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
             // ((r / rw) * 16 halo rows + (r % rw) * 8 pixels), and the descriptor's
             // constant bits (SBO = one halo row, version 1, no swizzle): computed
             // once, so the issue loop does no division
-            const uint32_t h_sbo = (uint32_t)p.hw * (uint32_t)p.cw;  // one halo row
+            const uint32_t h_sbo = (uint32_t)p.hw * 16u;
             uint32_t roff16[8];
 #pragma unroll
             for (int r = 0; r < 8; r++)
-                roff16[r] = p.mode == 2
-                                ? (((uint32_t)(r / p.rw) * 16u * h_sbo) + (uint32_t)(r % p.rw) * 8u * (uint32_t)p.cw) >> 4
-                                : 0u;
+                roff16[r] = p.mode == 2 ? (((uint32_t)(r / p.rw) * 16u * h_sbo) + (uint32_t)(r % p.rw) * 128u) >> 4 : 0u;
             const uint64_t a_hi = ((uint64_t)((h_sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
             const uint64_t lbo_plane = (uint64_t)((p.plane_stride >> 4) & 0x3FFFu) << 16;
             const uint64_t lbo_16 = (uint64_t)1u << 16;
@@ -821,35 +815,6 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                         const uint32_t bstep = (uint32_t)p.cblocks * p.b_tap_bytes;  // resident: next tap's slice
                         uint32_t bt = p.wres ? w_base + (uint32_t)it * p.b_tap_bytes : b_addr;
                         const uint32_t bt_step = p.wres ? bstep : p.b_tap_bytes;
-                        if (p.cw == 128) {
-                            // natural-layout slabs of 128 channel bytes a pixel (128-byte
-                            // swizzle): a tap is the slab read from a whole-pixel offset; the
-                            // descriptor's base offset ((start >> 7) & 7) carries the swizzle
-                            // phase of a start that is not on the 1 KiB pattern boundary; K
-                            // steps of 32 bytes advance inside the row
-                            for (int t = 0; t < p.taps; t++, bt += bt_step) {
-                                const uint32_t at = a_addr + (uint32_t)tapc[t].x;
-                                for (int j = 0; j < real; j++) {
-                                    const uint32_t aj = at + (uint32_t)j * p.plane_stride;
-                                    for (int k = 0; k < 4; k++) {
-                                        const uint64_t bd = smem_desc(bt + (uint32_t)(j * 128 + 32 * k), p.desc_hi);
-                                        const uint32_t accf = (it > 0 || t > 0 || j > 0 || k > 0) ? 1u : 0u;
-#pragma unroll
-                                        for (int r = 0; r < 8; r++) {
-                                            if (r < p.R) {
-                                                const uint32_t row = aj + (roff16[r] << 4);
-                                                const uint64_t ad = p.a_desc_hi | ((uint64_t)((row >> 7) & 7u) << 49) |
-                                                                    (uint64_t)(((row + 32u * k) >> 4) & 0x3FFFu);
-                                                tc_mma<kF16>(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, accf);
-                                            }
-                                        }
-                                    }
-                                }
-                            }
-                            tc_commit(smem_u32(&empty_bar[s]));
-                            if (++s == p.stages) { s = 0; ph ^= 1; }
-                            continue;
-                        }
                         for (int t = 0; t < p.taps; t++, bt += bt_step) {
                             const uint32_t at16 = (a_addr + (uint32_t)tapc[t].x) >> 4;
                             for (int k = 0; k < kn; k++) {
@@ -1227,26 +1192,12 @@ constexpr size_t kSmemLimit = 227 * 1024 - sizeof(int4) * kTapTable;  // dynamic
 // weights are loaded once per CTA).
 struct HaloPlan {
     bool ok = false;
-    int R = 1, rw = 1, bn = 16, bk = 32, tiles_w = 1, tiles_h = 1, n_tiles = 1, wres = 0, cw = 16;
+    int R = 1, rw = 1, bn = 16, bk = 32, tiles_w = 1, tiles_h = 1, n_tiles = 1, wres = 0;
     uint32_t plane = 0, w_bytes = 0;
 };
 
-// Bytes of one halo plane: (16 rh + k_h - 1) rows x (8 rw + k_w - 1) pixels x cw
-// bytes; 128-byte aligned, or 1 KiB (the swizzle pattern's span) for cw = 128.
-uint32_t halo_plane_bytes(const dw_conv_desc &d, int rw, int rh, int cw) {
-    const size_t b = (size_t)(16 * rh + d.k_h - 1) * (size_t)(8 * rw + d.k_w - 1) * cw;
-    return (uint32_t)(cw == 128 ? al1k(b) : ((b + 127) & ~size_t(127)));
-}
-
-// Channel bytes a pixel contributes to one halo plane: 128 when the channel row
-// is a multiple of it (a natural-layout slab with the 128-byte swizzle: one TMA
-// row per pixel instead of eight), else 16 (chunk planes without swizzle).
-// Slabs of 32 or 64 bytes are not used: a tap's whole-pixel start offset inside
-// their swizzle pattern gave wrong products on B200, while the 128-byte
-// pattern's row-aligned starts with the descriptor's base offset were exact.
-int halo_cw(int cbytes) {
-    if (getenv("DW_UMMA_HALO_CW16")) return 16;  // tuning switch: chunk planes only
-    return cbytes % 128 == 0 ? 128 : 16;
+uint32_t halo_plane_bytes(const dw_conv_desc &d, int rw, int rh) {
+    return (uint32_t)(((size_t)(16 * rh + d.k_h - 1) * (size_t)(8 * rw + d.k_w - 1) * 16 + 127) & ~size_t(127));
 }
 
 // Output-channel tile for the per-stage weights: all of c_out when the taps'
@@ -1278,8 +1229,7 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
     if (util < 0.7) return h;
     const int c_out16 = ((d.c_out + 15) / 16) * 16;
     const int cbytes = d.c_in * esize;
-    const int cw = halo_cw(cbytes);
-    const int chunks = cbytes / cw;  // halo planes per channel row
+    const int chunks = cbytes / 16;
     const size_t chan = al1k(sizeof(ChanSmem));
     int r_env = 8;
     if (const char *e = getenv("DW_UMMA_RMAX")) {  // tuning override, as for the per-tap producer
@@ -1345,15 +1295,15 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
             // 16 x 16 tiles): the per-tap producer's tiles fit them closer
             // (YOLOv8n's 40x40 3x3s: 24.4 vs 24.9 us at 64 channels, 31 vs 33-35 us at 128)
             if (cbytes > 32 && (double)arr[i].tiles * R * kBM > 1.3 * (double)d.n * ho * wo) continue;
-            const uint32_t plane = halo_plane_bytes(d, arr[i].rw, arr[i].rh, cw);
+            const uint32_t plane = halo_plane_bytes(d, arr[i].rw, arr[i].rh);
             for (int bk : {bk0, 64, 32}) {
-                if (bk > bk0 || bk % cw) continue;
+                if (bk > bk0) continue;
                 const int cblocks = (cbytes + bk - 1) / bk;
                 const size_t w_bytes = (size_t)taps * cblocks * bn * bk;
-                const size_t stage = al1k((size_t)std::min(bk / cw, chunks) * plane);
+                const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane);
                 const size_t fixed = 1024 + al1k((size_t)R * kBM * bn * esize) + al1k(w_bytes) + chan + 512;
                 if (fixed < kSmemLimit && (kSmemLimit - fixed) / stage >= 3) {
-                    h.ok = true; h.wres = 1; h.R = R; h.rw = arr[i].rw; h.bn = bn; h.bk = bk; h.n_tiles = 1; h.cw = cw;
+                    h.ok = true; h.wres = 1; h.R = R; h.rw = arr[i].rw; h.bn = bn; h.bk = bk; h.n_tiles = 1;
                     h.tiles_w = (wo + 8 * h.rw - 1) / (8 * h.rw);
                     h.tiles_h = (ho + 16 * arr[i].rh - 1) / (16 * arr[i].rh);
                     h.plane = plane;
@@ -1377,14 +1327,14 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
     const int n = arrangements(h.n_tiles, std::min(r_env, std::max(1, std::min(8, 256 / h.bn))), arr);
     for (int i = 0; i < n; i++) {
         const int R = arr[i].rw * arr[i].rh;
-        const uint32_t plane = halo_plane_bytes(d, arr[i].rw, arr[i].rh, cw);
+        const uint32_t plane = halo_plane_bytes(d, arr[i].rw, arr[i].rh);
         const size_t fixed = 1024 + al1k((size_t)R * kBM * h.bn * esize) + chan + 512;
         for (int bk : {128, 64, 32}) {
-            if ((bk > cap_bk && bk != 32) || bk % cw) continue;
-            const size_t stage = al1k((size_t)std::min(bk / cw, chunks) * plane) + al1k((size_t)taps * h.bn * bk);
+            if (bk > cap_bk && bk != 32) continue;
+            const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane) + al1k((size_t)taps * h.bn * bk);
             const size_t fit = fixed < kSmemLimit ? (kSmemLimit - fixed) / stage : 0;
             if (fit >= 3 || (bk == 32 && fit >= 2)) {
-                h.ok = true; h.R = R; h.rw = arr[i].rw; h.bk = bk; h.plane = plane; h.cw = cw;
+                h.ok = true; h.R = R; h.rw = arr[i].rw; h.bk = bk; h.plane = plane;
                 h.tiles_w = (wo + 8 * h.rw - 1) / (8 * h.rw);
                 h.tiles_h = (ho + 16 * arr[i].rh - 1) / (16 * arr[i].rh);
                 return h;
@@ -1466,7 +1416,6 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     p.taps = d.k_h * d.k_w; p.kw = d.k_w; p.sh = d.stride_h; p.sw = d.stride_w; p.pt = d.pad_t; p.pl = d.pad_l;
     p.c_in = d.c_in;
     p.rw = 1;
-    p.cw = 16;
     const HaloPlan hp = plan_halo(be, d, ho, wo, esize, flat);
     if (hp.ok) {
         p.mode = 2;
@@ -1486,15 +1435,12 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         p.hh = 16 * (p.R / p.rw) + d.k_h - 1;
         p.wres = hp.wres;
         p.w_bytes = hp.w_bytes;
-        p.cw = hp.cw;
-        p.chunks = d.c_in * esize / p.cw;
-        p.cps = p.bk / p.cw;
-        p.chunk_elems = p.cw / esize;
+        p.chunks = d.c_in * esize / 16;
+        p.cps = p.bk / 16;
+        p.chunk_elems = 16 / esize;
         p.plane_stride = hp.plane;
         p.b_tap_bytes = (uint32_t)(p.bn * p.bk);
-        p.a_tx_bytes = 0;  // per plane: hw * hh * cw bytes (the producer counts them)
-        p.a_desc_hi = ((uint64_t)((((uint32_t)p.hw * p.cw) >> 4) & 0x3FFFu) << 32) | (1ull << 46) |
-                      ((uint64_t)(p.cw == 128 ? swizzle_layout(128) : 0u) << 61);
+        p.a_tx_bytes = 0;  // per chunk: hw * hh * 16 bytes (the producer counts them)
     } else {
         p.bk = flat ? pick_bk(d.c_in * esize) : pick_bk_taps(d.c_in * esize);
         if (const char *e = getenv("DW_UMMA_BK")) {  // tuning override: 32, 64 or 128 bytes of K per stage
@@ -1625,17 +1571,16 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     CUresult r;
     const CUtensorMapSwizzle sw = swizzle_enum(p.bk);
     if (p.mode == 2) {
-        // halo boxes: cw bytes of channels of (16 R/rw + k_h - 1) x (8 rw + k_w - 1)
-        // pixels (16: no swizzle; 128: the 128-byte swizzle); out-of-range pixels
-        // (the padding) are zero-filled
+        // halo boxes: one 16-byte channel chunk of (16 R + k_h - 1) x (8 + k_w - 1)
+        // pixels, no swizzle; out-of-range pixels (the padding) are zero-filled
         cuuint64_t dims[4] = {(cuuint64_t)d.c_in, (cuuint64_t)d.w, (cuuint64_t)d.h, (cuuint64_t)d.n};
         cuuint64_t strides[3] = {(cuuint64_t)x_pitch * es, (cuuint64_t)d.w * x_pitch * es,
                                  (cuuint64_t)d.h * d.w * x_pitch * es};
         cuuint32_t box[4] = {(cuuint32_t)p.chunk_elems, (cuuint32_t)p.hw, (cuuint32_t)p.hh, 1};
         cuuint32_t estr[4] = {1, 1, 1, 1};
         r = be->encode_tiled(&ta, dt, 4, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             p.cw == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else if (flat) {
         cuuint64_t dims[2] = {(cuuint64_t)d.c_in, (cuuint64_t)p.rows};
         cuuint64_t strides[1] = {(cuuint64_t)x_pitch * es};
