@@ -55,7 +55,7 @@ struct UmmaParams {
     int tiles_w, tiles_h;
     int m_tiles, n_tiles, num_tiles;
     long long rows;      // flat mode: total pixels
-    int taps, kw, sh, sw, pt, pl, c_in;
+    int taps, k_h, kw, sh, sw, pt, pl, c_in;
     int cblocks;         // k-blocks per tap
     int bk;              // bytes of K per stage (32/64/128)
     int bn;              // N per tile
@@ -93,6 +93,9 @@ struct UmmaParams {
     int wres;                               // mode 2: every weight of the (single) channel tile resident in
                                             // shared memory, loaded once per CTA; stages carry halo planes only
     uint32_t off_w, w_bytes;                // resident weights: offset and bytes ([tap][K block][bn][bk])
+    int tpair;                              // resident weights of a 16-byte channel row: [tap + 1][bn][16 B]
+                                            // slices without swizzle (the last all zero), so that one 32-byte
+                                            // K step takes two horizontal taps
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
@@ -690,10 +693,17 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                 const uint32_t wb = smem_u32(&w_bar[0]);
                 mbar_expect_tx(wb, p.w_bytes);
                 const uint32_t w_dst = smem_u32(smem + p.off_w);
-                for (int t = 0; t < p.taps; t++)
-                    for (int cb = 0; cb < p.cblocks; cb++)
-                        tma_load_3d(w_dst + (uint32_t)(t * p.cblocks + cb) * p.b_tap_bytes, &tmap_b, wb,
-                                    cb * p.bk_elems, t, 0);
+                if (p.tpair) {
+                    // one 16-byte slice per tap, then one past the last tap: out of range,
+                    // so TMA fills it with zeros
+                    for (int t = 0; t <= p.taps; t++)
+                        tma_load_3d(w_dst + (uint32_t)t * p.b_tap_bytes, &tmap_b, wb, 0, t, 0);
+                } else {
+                    for (int t = 0; t < p.taps; t++)
+                        for (int cb = 0; cb < p.cblocks; cb++)
+                            tma_load_3d(w_dst + (uint32_t)(t * p.cblocks + cb) * p.b_tap_bytes, &tmap_b, wb,
+                                        cb * p.bk_elems, t, 0);
+                }
             }
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 const TileCoord tc = tile_coord(p, tile);
@@ -812,6 +822,37 @@ __global__ void __launch_bounds__(umma_threads(kF16), 1)
                         // zero-filled channels past c_in), so no plane is left unloaded.
                         const int real = min(p.cps, p.chunks - it * p.cps);
                         const int kn = (real + 1) >> 1;
+                        if (p.tpair) {
+                            // 16-byte channel rows: a K step takes taps (kh, kw) and (kh, kw + 1).
+                            // A's second half is the pixel one to the right (LBO 16 bytes), which
+                            // is tap kw + 1's pixel; B's second half is tap kw + 1's slice (LBO one
+                            // slice), or the zero slice past the last tap when kw is the row's last.
+                            const uint64_t a_hi16 = a_hi | lbo_16;
+                            const uint32_t zero_slice = (uint32_t)p.taps;
+                            int first = 1;
+                            for (int kh = 0; kh < p.k_h; kh++) {
+                                for (int kw = 0; kw < p.kw; kw += 2, first = 0) {
+                                    const int t = kh * p.kw + kw;
+                                    const uint32_t t2 = kw + 1 < p.kw ? (uint32_t)(t + 1) : zero_slice;
+                                    const uint32_t b0 = w_base + (uint32_t)t * p.b_tap_bytes;
+                                    const uint64_t bd = ((uint64_t)((b0 >> 4) & 0x3FFFu)) |
+                                                        ((uint64_t)((((t2 - (uint32_t)t) * p.b_tap_bytes) >> 4) & 0x3FFFu) << 16) |
+                                                        ((uint64_t)(128u >> 4) << 32) | (1ull << 46);
+                                    const uint32_t a16 = (a_addr + (uint32_t)tapc[t].x) >> 4;
+                                    const uint32_t accf = first ? 0u : 1u;
+#pragma unroll
+                                    for (int r = 0; r < 8; r++) {
+                                        if (r < p.R) {
+                                            const uint64_t ad = a_hi16 | (uint64_t)((a16 + roff16[r]) & 0x3FFFu);
+                                            tc_mma<kF16>(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, accf);
+                                        }
+                                    }
+                                }
+                            }
+                            tc_commit(smem_u32(&empty_bar[s]));
+                            if (++s == p.stages) { s = 0; ph ^= 1; }
+                            continue;
+                        }
                         const uint32_t bstep = (uint32_t)p.cblocks * p.b_tap_bytes;  // resident: next tap's slice
                         uint32_t bt = p.wres ? w_base + (uint32_t)it * p.b_tap_bytes : b_addr;
                         const uint32_t bt_step = p.wres ? bstep : p.b_tap_bytes;
@@ -1192,7 +1233,7 @@ constexpr size_t kSmemLimit = 227 * 1024 - sizeof(int4) * kTapTable;  // dynamic
 // weights are loaded once per CTA).
 struct HaloPlan {
     bool ok = false;
-    int R = 1, rw = 1, bn = 16, bk = 32, tiles_w = 1, tiles_h = 1, n_tiles = 1, wres = 0;
+    int R = 1, rw = 1, bn = 16, bk = 32, tiles_w = 1, tiles_h = 1, n_tiles = 1, wres = 0, tpair = 0;
     uint32_t plane = 0, w_bytes = 0;
 };
 
@@ -1287,6 +1328,8 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
     // 56x56 fp16 64 -> 64 3x3 185 vs 122 us), so such plans are not taken.
     if (c_out16 <= 256 && !getenv("DW_UMMA_NO_WRES")) {
         const int bn = c_out16, bk0 = pick_bk_res();
+        // 16-byte channel rows (int8 c_in = 16): no-swizzle weight slices, two taps per K step
+        const bool tpair = cbytes == 16 && esize == 1 && !getenv("DW_UMMA_NO_TPAIR");
         const int n = arrangements(1, std::min(r_env, std::max(1, std::min(8, 256 / bn))), arr);
         for (int i = 0; i < n; i++) {
             const int R = arr[i].rw * arr[i].rh;
@@ -1299,11 +1342,12 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
             for (int bk : {bk0, 64, 32}) {
                 if (bk > bk0) continue;
                 const int cblocks = (cbytes + bk - 1) / bk;
-                const size_t w_bytes = (size_t)taps * cblocks * bn * bk;
+                const size_t w_bytes = tpair ? (size_t)(taps + 1) * bn * 16 : (size_t)taps * cblocks * bn * bk;
                 const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane);
                 const size_t fixed = 1024 + al1k((size_t)R * kBM * bn * esize) + al1k(w_bytes) + chan + 512;
                 if (fixed < kSmemLimit && (kSmemLimit - fixed) / stage >= 3) {
                     h.ok = true; h.wres = 1; h.R = R; h.rw = arr[i].rw; h.bn = bn; h.bk = bk; h.n_tiles = 1;
+                    h.tpair = tpair ? 1 : 0;
                     h.tiles_w = (wo + 8 * h.rw - 1) / (8 * h.rw);
                     h.tiles_h = (ho + 16 * arr[i].rh - 1) / (16 * arr[i].rh);
                     h.plane = plane;
@@ -1413,7 +1457,7 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     if (res_f16 && (!flat || ((uintptr_t)res_f16 & 15)))
         return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: a fused residual needs a 1x1 stride-1 conv and a 16-byte aligned buffer", op);
     p.n_img = d.n; p.ho = ho; p.wo = wo; p.c_out = d.c_out;
-    p.taps = d.k_h * d.k_w; p.kw = d.k_w; p.sh = d.stride_h; p.sw = d.stride_w; p.pt = d.pad_t; p.pl = d.pad_l;
+    p.taps = d.k_h * d.k_w; p.k_h = d.k_h; p.kw = d.k_w; p.sh = d.stride_h; p.sw = d.stride_w; p.pt = d.pad_t; p.pl = d.pad_l;
     p.c_in = d.c_in;
     p.rw = 1;
     const HaloPlan hp = plan_halo(be, d, ho, wo, esize, flat);
@@ -1439,7 +1483,8 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         p.cps = p.bk / 16;
         p.chunk_elems = 16 / esize;
         p.plane_stride = hp.plane;
-        p.b_tap_bytes = (uint32_t)(p.bn * p.bk);
+        p.tpair = hp.tpair;
+        p.b_tap_bytes = (uint32_t)(p.bn * (p.tpair ? 16 : p.bk));
         p.a_tx_bytes = 0;  // per chunk: hw * hh * 16 bytes (the producer counts them)
     } else {
         p.bk = flat ? pick_bk(d.c_in * esize) : pick_bk_taps(d.c_in * esize);
@@ -1603,11 +1648,12 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     {
         cuuint64_t dims[3] = {(cuuint64_t)d.c_in, (cuuint64_t)p.taps, (cuuint64_t)d.c_out};
         cuuint64_t strides[2] = {(cuuint64_t)d.c_in * es, (cuuint64_t)p.taps * d.c_in * es};
-        cuuint32_t box[3] = {(cuuint32_t)p.bk_elems, 1, (cuuint32_t)p.bn};
+        // two-tap K steps: one tap's 16 bytes per row, no swizzle (8-row core matrices)
+        cuuint32_t box[3] = {(cuuint32_t)(p.tpair ? 16 / esize : p.bk_elems), 1, (cuuint32_t)p.bn};
         cuuint32_t estr[3] = {1, 1, 1};
         r = be->encode_tiled(&tb, dt, 3, const_cast<void *>(w_ohwi), dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, p.tpair ? CU_TENSOR_MAP_SWIZZLE_NONE : sw,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
     if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: weight tensor map rejected (%d)", op, (int)r);
     // Output: TMA stores of the staged [rows][bn] tile (swizzled fp16 staging:

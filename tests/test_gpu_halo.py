@@ -4,7 +4,8 @@ config 1, the MobileNet/ResNet-style 3x3s).  Per K block the producer loads
 one zero-padded halo tile per 16-byte channel chunk and every tap reads it at
 a shifted address.  The shapes cover every branch of that path: one to eight
 row blocks per tile, odd chunk counts (the last K step's second half reads a
-neighbouring pixel against zero weights), several channel tiles, 5x5 and 1x3
+neighbouring pixel against zero weights), two taps per K step for 16-channel
+inputs, several channel tiles, 5x5 and 1x3
 kernels, asymmetric pads, ragged right and bottom edges, channel-range views,
 every epilogue, and accumulators beyond 2^24.  int8 results must be identical
 to the oracle's (tolerance 0)."""
@@ -83,6 +84,29 @@ def test_halo_rectangular_kernels_and_asymmetric_pads(be, kh, kw, pads):
     b = rng.integers(-1000, 1001, co).astype(np.int32)
     desc.q6, desc.inv_s_out = 127, float(np.float32(1.0) / np.float32(0.05))
     assert halo_eligible(desc, wide=True)
+    y = cuda_conv(be, desc, x, wt, b, M, D)
+    ref = oracle_conv(desc, x, wt, b, M, D)
+    assert np.array_equal(y, ref), mismatch_report(y, ref)
+
+
+@pytest.mark.parametrize("kh,kw,pads", [(3, 3, (1, 1, 1, 1)), (5, 5, (2, 2, 2, 2)), (1, 3, (0, 1, 0, 1)),
+                                        (3, 1, (1, 0, 1, 0)), (2, 2, (0, 0, 1, 1)), (3, 4, (1, 1, 1, 2))])
+@pytest.mark.parametrize("epi", [dw.EPI_SILU, dw.EPI_RELU])
+def test_halo_two_tap_k_steps_c16(be, kh, kw, pads, epi):
+    """16 input channels: one 32-byte K step takes two horizontal taps (the
+    pixel one to the right is the next tap's pixel), the row's last tap of an
+    odd-width kernel pairs with an all-zero weight slice."""
+    rng = np.random.default_rng(kh * 13 + kw * 7 + sum(pads) + epi)
+    n, h, w, ci, co = 2, 46, 40, 16, 32
+    desc = ConvDesc(n, h, w, ci, co, kh, kw, 1, 1, pads, 1, epi)
+    x = rng.integers(-128, 128, n * h * w * ci).astype(np.int8)
+    wt = rng.integers(-127, 128, kh * kw * ci * co).astype(np.int8)
+    s_w = rng.uniform(0.001, 0.01, co).astype(np.float32)
+    M = Q.requant_scales(0.02, s_w, 0.05)
+    D = Q.dequant_scales(0.02, s_w)
+    b = rng.integers(-1000, 1001, co).astype(np.int32)
+    desc.q6, desc.inv_s_out = Q.relu6_ceiling(0.05), float(np.float32(1.0) / np.float32(0.05))
+    assert halo_eligible(desc)
     y = cuda_conv(be, desc, x, wt, b, M, D)
     ref = oracle_conv(desc, x, wt, b, M, D)
     assert np.array_equal(y, ref), mismatch_report(y, ref)
