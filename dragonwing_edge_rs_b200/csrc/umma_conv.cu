@@ -40,11 +40,14 @@ namespace {
 constexpr int kBM = 128;            // MMA M (rows per tile = pixels)
 // Warp roles: 0 producer, 1 MMA, then the epilogue warps (4 per part: warps
 // sharing a TMEM lane quarter split its (row block, chunk) items), then the
-// store warp.  12 epilogue warps: three interleaved epilogue streams per
-// scheduler, 128 registers a thread (the fp16 epilogue then keeps two TMEM
-// loads in flight per wait instead of four).
-constexpr int epi_warps(bool) { return 12; }
-constexpr int umma_threads(bool f16) { return 64 + 32 * epi_warps(f16) + 32; }
+// store warp.  The int8 SiLU epilogue (issue-bound) runs 16 epilogue warps, four
+// streams per scheduler at 96 registers a thread (YOLOv8n b32's stem conv 125 ->
+// 111 us, the step 1.995 -> 1.971 ms); the others keep 12 at 128 registers
+// (with 16 the ReLU6 / linear int8 epilogue spills and the MobileNetV2 block
+// went 0.336 -> 0.351 ms; the fp16 epilogue keeps two TMEM loads in flight per
+// wait instead of four).
+constexpr int epi_warps(bool silu, bool f16) { return (silu && !f16) ? 16 : 12; }
+constexpr int umma_threads(bool silu, bool f16) { return 64 + 32 * epi_warps(silu, f16) + 32; }
 constexpr int kMaxStages = 12;
 
 struct UmmaParams {
@@ -608,11 +611,11 @@ __device__ __forceinline__ int4 tap_coord(const UmmaParams &p, int tap) {
 // kSilu: int8 SiLU epilogue.  kF16: fp16 operands (kind::f16) with the fp16
 // epilogue; kFm its bias / residual / ReLU flags.
 template <bool kSilu, bool kF16, int kFm>
-__global__ void __launch_bounds__(umma_threads(kF16), 1)
+__global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
     k_umma_conv_i8(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_r,
                    const __grid_constant__ UmmaParams p) {
-    constexpr int kEpiWarps = epi_warps(kF16);
+    constexpr int kEpiWarps = epi_warps(kSilu, kF16);
     constexpr int kF16Batch = kEpiWarps > 8 ? 2 : 4;  // fp16 TMEM loads per wait (registers)
     constexpr int kEpiParts = kEpiWarps / 4;
     constexpr int kStoreWarp = 2 + kEpiWarps;
@@ -1736,16 +1739,16 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     const int grid = std::min(p.num_tiles, be->sm_count);
     if (esize == 2) {
         const int fm = (bias_f16 ? 1 : 0) | (res_f16 ? 2 : 0) | (relu ? 4 : 0);
-        f16_kernels[fm]<<<grid, umma_threads(true), smem, be->stream>>>(ta, tb, ty, tr, p);
+        f16_kernels[fm]<<<grid, umma_threads(false, true), smem, be->stream>>>(ta, tb, ty, tr, p);
     } else if (res_i8) {
         if (ep.epilogue == DW_EPI_SILU)
-            k_umma_conv_i8<true, false, 2><<<grid, umma_threads(false), smem, be->stream>>>(ta, tb, ty, tr, p);
+            k_umma_conv_i8<true, false, 2><<<grid, umma_threads(true, false), smem, be->stream>>>(ta, tb, ty, tr, p);
         else
-            k_umma_conv_i8<false, false, 2><<<grid, umma_threads(false), smem, be->stream>>>(ta, tb, ty, tr, p);
+            k_umma_conv_i8<false, false, 2><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr, p);
     } else if (ep.epilogue == DW_EPI_SILU) {
-        k_umma_conv_i8<true, false, 0><<<grid, umma_threads(false), smem, be->stream>>>(ta, tb, ty, tr, p);
+        k_umma_conv_i8<true, false, 0><<<grid, umma_threads(true, false), smem, be->stream>>>(ta, tb, ty, tr, p);
     } else {
-        k_umma_conv_i8<false, false, 0><<<grid, umma_threads(false), smem, be->stream>>>(ta, tb, ty, tr, p);
+        k_umma_conv_i8<false, false, 0><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr, p);
     }
     return dw_after_launch(be, esize == 2 ? "umma_conv_f16" : "umma_conv_i8");
 }
