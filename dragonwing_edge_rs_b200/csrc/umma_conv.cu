@@ -1349,6 +1349,10 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
                 const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane);
                 const size_t fixed = 1024 + al1k((size_t)R * kBM * bn * esize) + al1k(w_bytes) + chan + 512;
                 if (fixed < kSmemLimit && (kSmemLimit - fixed) / stage >= 3) {
+                    // too few tiles to give half the SMs one (batch 1): the per-tap
+                    // planner spreads such problems wider (fewer row blocks, narrower
+                    // tiles); DW_UMMA_HALO_ANY_SIZE keeps them here (tests of the halo path)
+                    if (2 * arr[i].tiles < be->sm_count && !getenv("DW_UMMA_HALO_ANY_SIZE")) return h;
                     h.ok = true; h.wres = 1; h.R = R; h.rw = arr[i].rw; h.bn = bn; h.bk = bk; h.n_tiles = 1;
                     h.tpair = tpair ? 1 : 0;
                     h.tiles_w = (wo + 8 * h.rw - 1) / (8 * h.rw);
@@ -1381,6 +1385,7 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
             const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane) + al1k((size_t)taps * h.bn * bk);
             const size_t fit = fixed < kSmemLimit ? (kSmemLimit - fixed) / stage : 0;
             if (fit >= 3 || (bk == 32 && fit >= 2)) {
+                if (2 * arr[i].tiles < be->sm_count && !getenv("DW_UMMA_HALO_ANY_SIZE")) return h;  // as above
                 h.ok = true; h.R = R; h.rw = arr[i].rw; h.bk = bk; h.plane = plane;
                 h.tiles_w = (wo + 8 * h.rw - 1) / (8 * h.rw);
                 h.tiles_h = (ho + 16 * arr[i].rh - 1) / (16 * arr[i].rh);

@@ -318,6 +318,7 @@ HALO_CASES = [
 @pytest.mark.parametrize("case", HALO_CASES)
 def test_conv_f16_halo_within_tolerance(be_umma, case, monkeypatch):
     monkeypatch.setenv("DW_UMMA_HALO_WIDE", "1")
+    monkeypatch.setenv("DW_UMMA_HALO_ANY_SIZE", "1")
     n, h, w, ci, co, k, s, p, relu = case
     rng = np.random.default_rng(sum(case) + 2)
     desc = ConvDesc(n, h, w, ci, co, k, k, s, s, (p,) * 4, 1, dw.EPI_RELU if relu else dw.EPI_NONE)
@@ -358,6 +359,7 @@ def test_conv_f16_halo_inf_input_stays_local(be_umma, monkeypatch):
     outputs whose windows hold it; the zero-filled halo and the shifted tap
     reads touch no other pixel."""
     monkeypatch.setenv("DW_UMMA_HALO_WIDE", "1")
+    monkeypatch.setenv("DW_UMMA_HALO_ANY_SIZE", "1")
     desc = ConvDesc(1, 32, 32, 32, 16, 3, 3, 1, 1, (1,) * 4, 1, dw.EPI_NONE)
     rng = np.random.default_rng(22)
     x, wt, b = conv_inputs(rng, desc)

@@ -33,9 +33,11 @@ def halo_eligible(desc: ConvDesc, esize=1, wide=False) -> bool:
 
 @pytest.fixture(autouse=True)
 def _wide_halo(monkeypatch):
-    """Every shape here runs the halo producer, the wide-row ones too (the
-    planner reads DW_UMMA_HALO_WIDE at each launch)."""
+    """Every shape here runs the halo producer: the wide-row ones too, and the
+    small ones that the planner would otherwise give the per-tap producer (it
+    reads DW_UMMA_HALO_WIDE and DW_UMMA_HALO_ANY_SIZE at each launch)."""
     monkeypatch.setenv("DW_UMMA_HALO_WIDE", "1")
+    monkeypatch.setenv("DW_UMMA_HALO_ANY_SIZE", "1")
 
 
 @pytest.fixture(scope="module")
