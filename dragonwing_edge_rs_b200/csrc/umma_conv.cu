@@ -99,6 +99,12 @@ struct UmmaParams {
     int tpair;                              // resident weights of a 16-byte channel row: [tap + 1][bn][16 B]
                                             // slices without swizzle (the last all zero), so that one 32-byte
                                             // K step takes two horizontal taps
+    int flat_in;                            // mode 2, a dense 16-byte channel row: the activation map is
+                                            // [n][h][w * 16 bytes], so a halo tile is one box of hh rows of
+                                            // hw * 16 contiguous bytes (not hw * hh 16-byte rows)
+    int flat_out;                           // mode 2, int8 output of exactly bn dense channels: the output
+                                            // map is [n][ho][wo * bn bytes]; a row block stores as 16 rows
+                                            // of 8 * bn bytes (not 128 rows of bn bytes)
     uint64_t wait_cap_ns;
     int32_t *err;
     EpiParams ep;
@@ -125,13 +131,13 @@ struct ChanSmem {
 // CTA is aborting or the cap expired (then the failure is recorded).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const UmmaParams &p,
                                           volatile int *abort_flag, int site) {
-#pragma unroll 1
-    for (int i = 0; i < 256; i++)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
 #pragma unroll 1
     for (;;) {
-        if (mbar_try_wait(bar, parity)) return true;
+        // suspended in hardware while the phase is open (at most ~20 us per try):
+        // waiting warps leave the issue slots to the MMA issuer and the epilogue
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > p.wait_cap_ns) {
             *abort_flag = 1;
@@ -537,6 +543,117 @@ __device__ __forceinline__ uint64_t smem_desc_noswz(uint32_t addr, uint32_t lbo,
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
+// One MMA with both descriptors given as 32-bit halves; kAcc folds the
+// enable-input-d predicate into a constant (accumulate into D, or overwrite it).
+template <bool kF16, bool kAcc>
+__device__ __forceinline__ void tc_mma_w(uint32_t d, uint32_t alo, uint32_t ahi, uint32_t blo, uint32_t bhi,
+                                         uint32_t idesc) {
+    if (kF16)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t.reg .b64 a, b;\n\tsetp.ne.b32 p, %6, 0;\n\t"
+            "mov.b64 a, {%1, %2};\n\tmov.b64 b, {%3, %4};\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %5, p;\n\t}" ::"r"(d),
+            "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc), "n"(kAcc ? 1 : 0)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t.reg .b64 a, b;\n\tsetp.ne.b32 p, %6, 0;\n\t"
+            "mov.b64 a, {%1, %2};\n\tmov.b64 b, {%3, %4};\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], a, b, %5, p;\n\t}" ::"r"(d),
+            "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc), "n"(kAcc ? 1 : 0)
+            : "memory");
+}
+
+// Halo mode: the MMAs of one K block, kR row blocks each.  Entry q of `tab` is
+// one 32-byte K step: x = the A descriptor's low word relative to the stage's
+// first plane (the tap's offset, and the LBO between the step's two 16-byte
+// halves), y = the B descriptor's low word (added to b16: 0 for resident
+// weights, else the stage's B tile).  Row block r reads A roff16[r] 16-byte
+// units further and accumulates into columns [r * bn, +bn).  `first`: the first
+// step overwrites the accumulators.
+template <int kR, bool kF16>
+__device__ __forceinline__ void halo_mmas(const int2 *tab, int n, uint32_t a16, uint32_t b16, uint32_t ahi,
+                                          uint32_t bhi, uint32_t d_tmem, uint32_t bn, const uint32_t (&roff16)[8],
+                                          uint32_t idesc, bool first) {
+    uint32_t dcol[kR], ar[kR];
+#pragma unroll
+    for (int r = 0; r < kR; r++) {
+        dcol[r] = d_tmem + (uint32_t)r * bn;
+        ar[r] = a16 + roff16[r];
+    }
+    int q = 0;
+    if (first) {
+        const int2 v = tab[0];
+#pragma unroll
+        for (int r = 0; r < kR; r++)
+            tc_mma_w<kF16, false>(dcol[r], ar[r] + (uint32_t)v.x, ahi, b16 + (uint32_t)v.y, bhi, idesc);
+        q = 1;
+    }
+    for (; q < n; q++) {
+        const int2 v = tab[q];
+#pragma unroll
+        for (int r = 0; r < kR; r++)
+            tc_mma_w<kF16, true>(dcol[r], ar[r] + (uint32_t)v.x, ahi, b16 + (uint32_t)v.y, bhi, idesc);
+    }
+}
+
+template <bool kF16>
+__device__ __forceinline__ void halo_mmas_r(int R, const int2 *tab, int n, uint32_t a16, uint32_t b16, uint32_t ahi,
+                                            uint32_t bhi, uint32_t d_tmem, uint32_t bn, const uint32_t (&roff16)[8],
+                                            uint32_t idesc, bool first) {
+    switch (R) {
+        case 1: halo_mmas<1, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
+        case 2: halo_mmas<2, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
+        case 3: halo_mmas<3, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
+        case 4: halo_mmas<4, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
+        case 5: halo_mmas<5, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
+        case 6: halo_mmas<6, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
+        case 7: halo_mmas<7, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
+        default: halo_mmas<8, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
+    }
+}
+
+// Modes 0 and 1: the MMAs of one stage -- kn 32-byte K steps (two 16-byte units
+// each) of kR row blocks, block r's A tile r * rstride16 units into the stage;
+// a16 / b16 are the descriptors' low words (address and LBO field), hi their
+// common high word (SBO, version, swizzle).
+template <int kR, bool kF16>
+__device__ __forceinline__ void tile_mmas(int kn, uint32_t a16, uint32_t b16, uint32_t hi, uint32_t d_tmem,
+                                          uint32_t bn, uint32_t rstride16, uint32_t idesc, bool first) {
+    uint32_t dcol[kR], ar[kR];
+#pragma unroll
+    for (int r = 0; r < kR; r++) {
+        dcol[r] = d_tmem + (uint32_t)r * bn;
+        ar[r] = a16 + (uint32_t)r * rstride16;
+    }
+    int k = 0;
+    if (first) {
+#pragma unroll
+        for (int r = 0; r < kR; r++) tc_mma_w<kF16, false>(dcol[r], ar[r], hi, b16, hi, idesc);
+        k = 1;
+    }
+    for (; k < kn; k++) {
+        const uint32_t k2 = 2u * (uint32_t)k;
+#pragma unroll
+        for (int r = 0; r < kR; r++) tc_mma_w<kF16, true>(dcol[r], ar[r] + k2, hi, b16 + k2, hi, idesc);
+    }
+}
+
+template <bool kF16>
+__device__ __forceinline__ void tile_mmas_r(int R, int kn, uint32_t a16, uint32_t b16, uint32_t hi, uint32_t d_tmem,
+                                            uint32_t bn, uint32_t rstride16, uint32_t idesc, bool first) {
+    switch (R) {
+        case 1: tile_mmas<1, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
+        case 2: tile_mmas<2, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
+        case 3: tile_mmas<3, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
+        case 4: tile_mmas<4, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
+        case 5: tile_mmas<5, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
+        case 6: tile_mmas<6, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
+        case 7: tile_mmas<7, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
+        default: tile_mmas<8, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
+    }
+}
+
 // ------------------------------------------------------------------- kernel
 // Tile = R blocks of 128 output pixels x bn output channels.  Row block r of a
 // tile covers pixels [tile_m0 + 128 r, +128) in flat mode, or the spatial
@@ -598,6 +715,7 @@ __device__ __forceinline__ uint4 with_residual(uint4 conv, uint32_t staged, cons
 }
 
 constexpr int kTapTable = 64;  // taps whose view coordinates the producer keeps in shared memory
+constexpr int kMmaTable = 256; // halo mode: K steps (per CTA, all K blocks) the MMA issuer keeps descriptors of
 
 // Coordinates of tap (kh, kw) in the 5-D activation view: the column phase's
 // channel offset, the column shift, the row phase and the row shift.
@@ -643,6 +761,7 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
     // Tap table: mode 1, the producer's per-tap view coordinates; mode 2, the
     // MMA issuer's per-tap halo offsets (each written and read by one warp).
     __shared__ int4 tapc[kTapTable];
+    __shared__ int2 mtab[kMmaTable];  // halo mode: the MMA issuer's K-step descriptor table
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; s++) {
@@ -730,9 +849,13 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                         const int real = min(p.cps, p.chunks - it * p.cps);
                         mbar_expect_tx(fb, (uint32_t)real * (uint32_t)(p.hw * p.hh * 16) +
                                                (p.wres ? 0u : (uint32_t)p.taps * p.b_tx_bytes));
-                        for (int j = 0; j < real; j++)
-                            tma_load_4d(a_dst + (uint32_t)j * p.plane_stride, &tmap_a, fb,
-                                        it * p.bk_elems + j * p.chunk_elems, tc.ow0 - p.pl, tc.oh0 - p.pt, tc.img);
+                        if (p.flat_in)  // one chunk: x counts 8-byte units, two per pixel
+                            tma_load_3d(a_dst, &tmap_a, fb, 2 * (tc.ow0 - p.pl), tc.oh0 - p.pt, tc.img);
+                        else
+                            for (int j = 0; j < real; j++)
+                                tma_load_4d(a_dst + (uint32_t)j * p.plane_stride, &tmap_a, fb,
+                                            it * p.bk_elems + j * p.chunk_elems, tc.ow0 - p.pl, tc.oh0 - p.pt,
+                                            tc.img);
                         if (!p.wres)
                             for (int t = 0; t < p.taps; t++)
                                 tma_load_3d(b_dst + (uint32_t)t * p.b_tap_bytes, &tmap_b, fb, it * p.bk_elems, t,
@@ -777,11 +900,46 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        // halo mode: byte offset of tap (kh, kw) inside a halo plane (the tap
-        // table's x; the producer does not use the table in this mode)
-        if (p.mode == 2)
-            for (int t = lane; t < min(p.taps, kTapTable); t += 32)
-                tapc[t].x = ((t / p.kw) * p.hw + (t % p.kw)) * 16;
+        // The issue loop is latency-bound (one thread; each tcgen05.mma takes
+        // tens of cycles to issue), so the descriptors are precomputed: halo
+        // mode, one table entry per 32-byte K step (built once per CTA by the
+        // warp's lanes); every mode, the row blocks unrolled for the tile's R.
+        const uint32_t w_base = smem_u32(smem + p.off_w);
+        const int kn2_full = (p.cps + 1) >> 1;  // halo mode: K steps of a full K block
+        const int kn2_last = (min(p.cps, p.chunks - (p.cblocks - 1) * p.cps) + 1) >> 1;
+        if (p.mode == 2) {
+            const uint32_t hw16 = (uint32_t)p.hw * 16u;
+            auto tap_off = [&](int t) { return ((uint32_t)(t / p.kw) * hw16) + (uint32_t)(t % p.kw) * 16u; };
+            if (p.tpair) {
+                // taps (2q, 2q + 1) in one K step: A's second half is tap 2q + 1's
+                // pixel (LBO = the offset between the two taps' pixels), B's the
+                // next slice (the all-zero slice past the last tap)
+                for (int q = lane; q < (p.taps + 1) / 2; q += 32) {
+                    const int t = 2 * q;
+                    const uint32_t off = tap_off(t);
+                    const uint32_t lbo = t + 1 < p.taps ? tap_off(t + 1) - off : 16u;
+                    mtab[q] = make_int2((int)((off >> 4) | ((lbo >> 4) << 16)),
+                                        (int)(((w_base + (uint32_t)t * p.b_tap_bytes) >> 4) | ((p.b_tap_bytes >> 4) << 16)));
+                }
+            } else {
+                // K block `it`, tap t, K step k: chunk planes 2k and 2k + 1 (with an
+                // odd chunk count the last step's second half is the neighbouring
+                // pixel, LBO 16 bytes, against zero weights)
+                const int per = p.taps * kn2_full;
+                const int total = (p.cblocks - 1) * per + p.taps * kn2_last;
+                for (int i = lane; i < total; i += 32) {
+                    const int it = i / per, rem = i - it * per;
+                    const int knb = it == p.cblocks - 1 ? kn2_last : kn2_full;
+                    const int t = rem / knb, k = rem - t * knb;
+                    const int real = min(p.cps, p.chunks - it * p.cps);
+                    const uint32_t off = tap_off(t) + (uint32_t)(2 * k) * p.plane_stride;
+                    const uint32_t lbo = 2 * k + 1 < real ? p.plane_stride : 16u;
+                    const uint32_t b = p.wres ? w_base + (uint32_t)(t * p.cblocks + it) * p.b_tap_bytes + 32u * k
+                                              : (uint32_t)t * p.b_tap_bytes + 32u * k;
+                    mtab[i] = make_int2((int)((off >> 4) | ((lbo >> 4) << 16)), (int)((b >> 4) | (1u << 16)));
+                }
+            }
+        }
         __syncwarp();
         if (lane == 0) {
             int s = 0;
@@ -790,21 +948,21 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
             bool ok = true;
             const int kn_full = p.bk >> 5;
             const int kn_last = (p.c_in * p.esize - (p.cblocks - 1) * p.bk + 31) >> 5;
-            const uint32_t w_base = smem_u32(smem + p.off_w);
             if (p.wres && (int)blockIdx.x < p.num_tiles && !mbar_wait(smem_u32(&w_bar[0]), 0, p, abort_flag, 7))
                 ok = false;
             // halo mode: per row block, its 16 B units from the tile's halo origin
-            // ((r / rw) * 16 halo rows + (r % rw) * 8 pixels), and the descriptor's
-            // constant bits (SBO = one halo row, version 1, no swizzle): computed
-            // once, so the issue loop does no division
+            // ((r / rw) * 16 halo rows + (r % rw) * 8 pixels); descriptor high
+            // words: A, SBO = one halo row; B, SBO = 8 rows of 16 bytes (two-tap
+            // slices) or of bk bytes (swizzled); version 1
             const uint32_t h_sbo = (uint32_t)p.hw * 16u;
             uint32_t roff16[8];
 #pragma unroll
             for (int r = 0; r < 8; r++)
                 roff16[r] = p.mode == 2 ? (((uint32_t)(r / p.rw) * 16u * h_sbo) + (uint32_t)(r % p.rw) * 128u) >> 4 : 0u;
-            const uint64_t a_hi = ((uint64_t)((h_sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
-            const uint64_t lbo_plane = (uint64_t)((p.plane_stride >> 4) & 0x3FFFu) << 16;
-            const uint64_t lbo_16 = (uint64_t)1u << 16;
+            const uint32_t hi_sw = (uint32_t)(p.desc_hi >> 32);
+            const uint32_t a_hi2 = (h_sbo >> 4) | (1u << 14);
+            const uint32_t b_hi2 = p.tpair ? ((128u >> 4) | (1u << 14)) : hi_sw;
+            const uint32_t rstride16 = (uint32_t)(kBM * p.bk) >> 4;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, local++) {
                 const int acc = local & 1;
                 const uint32_t acc_ph = (local >> 1) & 1;
@@ -818,84 +976,19 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                     const uint32_t a_addr = smem_u32(a_smem + (size_t)s * p.a_stage_bytes);
                     const uint32_t b_addr = smem_u32(b_smem + (size_t)s * p.b_stage_bytes);
                     if (p.mode == 2) {
-                        // every tap of K block `it`: the A tile is the halo plane read from the
-                        // tap's offset (8-row groups one halo row apart); a K step covers two
-                        // chunk planes.  With an odd chunk count the last step's second half
-                        // reads the neighbouring pixel (finite int8; its weights are the
-                        // zero-filled channels past c_in), so no plane is left unloaded.
-                        const int real = min(p.cps, p.chunks - it * p.cps);
-                        const int kn = (real + 1) >> 1;
-                        if (p.tpair) {
-                            // 16-byte channel rows: a K step takes taps (kh, kw) and (kh, kw + 1).
-                            // A's second half is the pixel one to the right (LBO 16 bytes), which
-                            // is tap kw + 1's pixel; B's second half is tap kw + 1's slice (LBO one
-                            // slice), or the zero slice past the last tap when kw is the row's last.
-                            const uint64_t a_hi16 = a_hi | lbo_16;
-                            const uint32_t zero_slice = (uint32_t)p.taps;
-                            int first = 1;
-                            for (int kh = 0; kh < p.k_h; kh++) {
-                                for (int kw = 0; kw < p.kw; kw += 2, first = 0) {
-                                    const int t = kh * p.kw + kw;
-                                    const uint32_t t2 = kw + 1 < p.kw ? (uint32_t)(t + 1) : zero_slice;
-                                    const uint32_t b0 = w_base + (uint32_t)t * p.b_tap_bytes;
-                                    const uint64_t bd = ((uint64_t)((b0 >> 4) & 0x3FFFu)) |
-                                                        ((uint64_t)((((t2 - (uint32_t)t) * p.b_tap_bytes) >> 4) & 0x3FFFu) << 16) |
-                                                        ((uint64_t)(128u >> 4) << 32) | (1ull << 46);
-                                    const uint32_t a16 = (a_addr + (uint32_t)tapc[t].x) >> 4;
-                                    const uint32_t accf = first ? 0u : 1u;
-#pragma unroll
-                                    for (int r = 0; r < 8; r++) {
-                                        if (r < p.R) {
-                                            const uint64_t ad = a_hi16 | (uint64_t)((a16 + roff16[r]) & 0x3FFFu);
-                                            tc_mma<kF16>(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, accf);
-                                        }
-                                    }
-                                }
-                            }
-                            tc_commit(smem_u32(&empty_bar[s]));
-                            if (++s == p.stages) { s = 0; ph ^= 1; }
-                            continue;
-                        }
-                        const uint32_t bstep = (uint32_t)p.cblocks * p.b_tap_bytes;  // resident: next tap's slice
-                        uint32_t bt = p.wres ? w_base + (uint32_t)it * p.b_tap_bytes : b_addr;
-                        const uint32_t bt_step = p.wres ? bstep : p.b_tap_bytes;
-                        for (int t = 0; t < p.taps; t++, bt += bt_step) {
-                            const uint32_t at16 = (a_addr + (uint32_t)tapc[t].x) >> 4;
-                            for (int k = 0; k < kn; k++) {
-                                const uint64_t hi = a_hi | ((2 * k + 1 < real) ? lbo_plane : lbo_16);
-                                const uint32_t a16 = at16 + (uint32_t)(2 * k) * (p.plane_stride >> 4);
-                                const uint64_t bd = smem_desc(bt + 32 * k, p.desc_hi);
-                                const uint32_t accf = (it > 0 || t > 0 || k > 0) ? 1u : 0u;
-#pragma unroll
-                                for (int r = 0; r < 8; r++) {
-                                    if (r < p.R) {
-                                        // block r: 16 output rows x 8 columns of the tile
-                                        const uint64_t ad = hi | (uint64_t)((a16 + roff16[r]) & 0x3FFFu);
-                                        tc_mma<kF16>(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, accf);
-                                    }
-                                }
-                            }
-                        }
-                        tc_commit(smem_u32(&empty_bar[s]));
-                        if (++s == p.stages) { s = 0; ph ^= 1; }
-                        continue;
-                    }
-                    // 32-byte K steps holding channels below c_in (the rest of the block is zero)
-                    const int kn = cb == p.cblocks - 1 ? kn_last : kn_full;
-                    if (++cb == p.cblocks) cb = 0;
-                    if (p.R == 1) {  // the common single-block issue loop (measurably faster)
-                        for (int k = 0; k < kn; k++) {
-                            const uint64_t ad = smem_desc(a_addr + 32 * k, p.desc_hi);
-                            const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
-                            tc_mma<kF16>(d_tmem, ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
-                        }
-                    } else
-                    for (int k = 0; k < kn; k++) {
-                        const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
-                        for (int r = 0; r < p.R; r++) {
-                            const uint64_t ad = smem_desc(a_addr + (uint32_t)(r * kBM * p.bk) + 32 * k, p.desc_hi);
-                            tc_mma<kF16>(d_tmem + (uint32_t)(r * p.bn), ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
-                        }
+                        // every tap of K block `it`: the A tile is the halo plane read from
+                        // the tap's offset (8-row groups one halo row apart)
+                        const int2 *tab = p.tpair ? mtab : mtab + it * p.taps * kn2_full;
+                        const int n = p.tpair ? (p.taps + 1) / 2 : p.taps * (it == p.cblocks - 1 ? kn2_last : kn2_full);
+                        halo_mmas_r<kF16>(p.R, tab, n, a_addr >> 4, p.wres ? 0u : (b_addr >> 4), a_hi2, b_hi2, d_tmem,
+                                          (uint32_t)p.bn, roff16, p.idesc, it == 0);
+                    } else {
+                        // 32-byte K steps holding channels below c_in (the rest of the block is zero)
+                        const int kn = cb == p.cblocks - 1 ? kn_last : kn_full;
+                        if (++cb == p.cblocks) cb = 0;
+                        tile_mmas_r<kF16>(p.R, kn, ((a_addr >> 4) & 0x3FFFu) | (1u << 16),
+                                          ((b_addr >> 4) & 0x3FFFu) | (1u << 16), hi_sw, d_tmem, (uint32_t)p.bn,
+                                          rstride16, p.idesc, it == 0);
                     }
                     tc_commit(smem_u32(&empty_bar[s]));  // frees the stage when these MMAs finish
                     if (++s == p.stages) { s = 0; ph ^= 1; }
@@ -1134,6 +1227,8 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                             smem_u32(stage + (size_t)r * kBM * p.bn * es + (size_t)sl * kBM * sw_ch * es);
                         if (p.mode == 0)
                             tma_store_2d(&tmap_y, src, tc.n0 + sl * sw_ch, (tc.mt * p.R + r) * kBM);
+                        else if (p.flat_out)  // x counts 8-byte units: bn / 8 per pixel
+                            tma_store_3d(&tmap_y, src, block_x(p, tc, r) * (p.bn >> 3), block_y(p, tc, r), tc.img);
                         else
                             tma_store_4d(&tmap_y, src, tc.n0 + sl * sw_ch, block_x(p, tc, r), block_y(p, tc, r),
                                          tc.img);
@@ -1225,7 +1320,8 @@ CUtensorMapSwizzle swizzle_enum(int bk) {
     return bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
-constexpr size_t kSmemLimit = 227 * 1024 - sizeof(int4) * kTapTable;  // dynamic share (the tap table is static)
+// dynamic share (the tap and K-step tables are static)
+constexpr size_t kSmemLimit = 227 * 1024 - sizeof(int4) * kTapTable - sizeof(int2) * kMmaTable;
 
 // Halo mode plan (stride-1 convs with several taps).  A row block is 8 output
 // columns x 16 rows (the 8 rows of a core matrix are 8 neighbouring pixels);
@@ -1345,6 +1441,7 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
             for (int bk : {bk0, 64, 32}) {
                 if (bk > bk0) continue;
                 const int cblocks = (cbytes + bk - 1) / bk;
+                if (!tpair && cblocks * taps * (bk / 32) > kMmaTable) continue;  // the MMA issuer's K-step table
                 const size_t w_bytes = tpair ? (size_t)(taps + 1) * bn * 16 : (size_t)taps * cblocks * bn * bk;
                 const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane);
                 const size_t fixed = 1024 + al1k((size_t)R * kBM * bn * esize) + al1k(w_bytes) + chan + 512;
@@ -1382,6 +1479,7 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
         const size_t fixed = 1024 + al1k((size_t)R * kBM * h.bn * esize) + chan + 512;
         for (int bk : {128, 64, 32}) {
             if (bk > cap_bk && bk != 32) continue;
+            if ((cbytes + bk - 1) / bk * taps * (bk / 32) > kMmaTable) continue;  // the MMA issuer's K-step table
             const size_t stage = al1k((size_t)std::min(bk / 16, chunks) * plane) + al1k((size_t)taps * h.bn * bk);
             const size_t fit = fixed < kSmemLimit ? (kSmemLimit - fixed) / stage : 0;
             if (fit >= 3 || (bk == 32 && fit >= 2)) {
@@ -1494,6 +1592,12 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         p.tpair = hp.tpair;
         p.b_tap_bytes = (uint32_t)(p.bn * (p.tpair ? 16 : p.bk));
         p.a_tx_bytes = 0;  // per chunk: hw * hh * 16 bytes (the producer counts them)
+        // Whole-row boxes where the data is contiguous: the TMA moves a box row by
+        // row, so a halo of hw * hh 16-byte rows costs far more than hh rows of
+        // hw * 16 bytes (and likewise for the stores).
+        const bool no_flat = getenv("DW_UMMA_NO_FLAT") != nullptr;  // tuning switch: 16-byte rows throughout
+        p.flat_in = (!no_flat && p.chunks == 1 && x_pitch == d.c_in && 2 * p.hw <= 256) ? 1 : 0;
+        p.flat_out = (!no_flat && esize == 1 && p.bn == d.c_out && y_pitch == d.c_out) ? 1 : 0;
     } else {
         p.bk = flat ? pick_bk(d.c_in * esize) : pick_bk_taps(d.c_in * esize);
         if (const char *e = getenv("DW_UMMA_BK")) {  // tuning override: 32, 64 or 128 bytes of K per stage
@@ -1623,7 +1727,18 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     CUtensorMap ta, tb;
     CUresult r;
     const CUtensorMapSwizzle sw = swizzle_enum(p.bk);
-    if (p.mode == 2) {
+    if (p.mode == 2 && p.flat_in) {
+        // one 16-byte chunk per pixel, dense: [n][h][w * 2] 8-byte units; a halo
+        // box is hh rows of hw pixels, zero-filled left and right of the row and
+        // above and below the map (the padding)
+        cuuint64_t dims[3] = {(cuuint64_t)d.w * 2, (cuuint64_t)d.h, (cuuint64_t)d.n};
+        cuuint64_t strides[2] = {(cuuint64_t)d.w * 16, (cuuint64_t)d.h * d.w * 16};
+        cuuint32_t box[3] = {(cuuint32_t)(2 * p.hw), (cuuint32_t)p.hh, 1};
+        cuuint32_t estr[3] = {1, 1, 1};
+        r = be->encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void *>(x), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else if (p.mode == 2) {
         // halo boxes: one 16-byte channel chunk of (16 R + k_h - 1) x (8 + k_w - 1)
         // pixels, no swizzle; out-of-range pixels (the padding) are zero-filled
         cuuint64_t dims[4] = {(cuuint64_t)d.c_in, (cuuint64_t)d.w, (cuuint64_t)d.h, (cuuint64_t)d.n};
@@ -1676,6 +1791,16 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         cuuint32_t estr[2] = {1, 1};
         r = be->encode_tiled(&ty, dt, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, st_sw,
                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else if (p.mode == 2 && p.flat_out) {
+        // [n][ho][wo * bn / 8] 8-byte units: a row block's staging [16][8][bn] is
+        // 16 rows of 8 * bn contiguous bytes; pixels past the map are clipped
+        cuuint64_t dims[3] = {(cuuint64_t)wo * (p.bn / 8), (cuuint64_t)ho, (cuuint64_t)d.n};
+        cuuint64_t strides[2] = {(cuuint64_t)wo * d.c_out, (cuuint64_t)ho * wo * d.c_out};
+        cuuint32_t box[3] = {(cuuint32_t)p.bn, (cuuint32_t)p.th, 1};
+        cuuint32_t estr[3] = {1, 1, 1};
+        r = be->encode_tiled(&ty, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, y, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
         cuuint64_t dims[4] = {(cuuint64_t)d.c_out, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)d.n};
         cuuint64_t strides[3] = {(cuuint64_t)y_pitch * es, (cuuint64_t)wo * y_pitch * es,

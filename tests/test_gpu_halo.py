@@ -127,24 +127,32 @@ def test_halo_extreme_accumulators(be):
     assert np.array_equal(y, ref), mismatch_report(y, ref)
 
 
-def test_halo_channel_range_views(be):
-    """Input and output as channel ranges of wider tensors (the C2f concat
-    views): the halo boxes read only the view's channels."""
-    rng = np.random.default_rng(7)
-    n, h, w, ci, co, c_tot_in, c_tot_out = 2, 40, 40, 32, 32, 96, 64
+@pytest.mark.parametrize("ci", [16, 32])
+@pytest.mark.parametrize("in_view,out_view", [(True, True), (True, False), (False, True)])
+def test_halo_channel_range_views(be, ci, in_view, out_view):
+    """Input and/or output as channel ranges of wider tensors (the C2f concat
+    views): the halo boxes read only the view's channels, the stores write only
+    the view's.  A dense side takes the whole-row boxes (16-channel input rows,
+    outputs of exactly one channel tile), the view side the 16-byte rows."""
+    rng = np.random.default_rng(7 + ci + 2 * in_view + out_view)
+    n, h, w, co = 2, 41, 37, 32
+    c_tot_in = 96 if in_view else ci
+    c_tot_out = 64 if out_view else co
+    in_off, out_off = (32 if in_view else 0), (16 if out_view else 0)
     desc, x, wt, b, M, D = conv_case(rng, n, h, w, ci, co, k=3, s=1, epilogue=dw.EPI_SILU)
     big_in = rng.integers(-128, 128, (n, h, w, c_tot_in)).astype(np.int8)
-    big_in[..., 32:64] = x.reshape(n, h, w, ci)
+    big_in[..., in_off:in_off + ci] = x.reshape(n, h, w, ci)
     bx = be.upload_array(big_in.reshape(-1))
     wp = ops.prepare_weights_i8(be, desc, be.upload_array(wt))
     bb, bm, bd = be.upload_array(b), be.upload_array(M), be.upload_array(D)
     out0 = rng.integers(-128, 128, (n, h, w, c_tot_out)).astype(np.int8)
     by = be.upload_array(out0.reshape(-1))
-    ops.conv2d_i8_view(be, desc, (bx, 32, c_tot_in), wp, bb, bm, bd, (by, 16, c_tot_out))
+    ops.conv2d_i8_view(be, desc, (bx, in_off, c_tot_in), wp, bb, bm, bd, (by, out_off, c_tot_out))
     got = be.download_array(by, np.int8).reshape(n, h, w, c_tot_out)
     be.synchronize(20000)
     ref = oracle_conv(desc, x, wt, b, M, D).reshape(n, h, w, co)
-    assert np.array_equal(got[..., 16:48], ref), mismatch_report(got[..., 16:48].reshape(-1), ref.reshape(-1))
+    sel = got[..., out_off:out_off + co]
+    assert np.array_equal(sel, ref), mismatch_report(sel.reshape(-1), ref.reshape(-1))
     # channels outside the view are untouched
-    assert np.array_equal(got[..., :16], out0[..., :16])
-    assert np.array_equal(got[..., 48:], out0[..., 48:])
+    assert np.array_equal(got[..., :out_off], out0[..., :out_off])
+    assert np.array_equal(got[..., out_off + co:], out0[..., out_off + co:])
