@@ -279,6 +279,79 @@ __global__ void k_im2col_stem3_rows(const uint8_t *__restrict__ x, int8_t *__res
     }
 }
 
+// The same stem, one block per band of kStemBand output rows: the band's
+// (kStemBand - 1) * sh + 3 input rows are quantised into shared memory once
+// (rows shared by neighbouring output rows are not re-read), then the band's
+// pixels are packed as in k_im2col_stem3_rows.  The quantisation table is
+// replicated per lane (word (u / 4) * 32 + lane holds bytes u & ~3 .. | 3), so
+// the 32 lanes of a lookup hit 32 different banks.
+constexpr int kStemBand = 8;
+__global__ void __launch_bounds__(256) k_im2col_stem3_band(const uint8_t *__restrict__ x, int8_t *__restrict__ y, int h,
+                                                           int w, int sh, int sw, int pt, int pl, int ho, int wo,
+                                                           int row_bytes, int nbands, float inv255, float inv) {
+    extern __shared__ __align__(16) uint8_t rows[];  // [(kStemBand - 1) * sh + 3][row_bytes]
+    __shared__ uint8_t q8[256];
+    __shared__ uint32_t lutw[64 * 32];
+    for (int u = threadIdx.x; u < 256; u += blockDim.x)
+        q8[u] = (uint8_t)f32_to_i8(__fmul_rn(__fmul_rn(i2f_small(u), inv255), inv));
+    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * 32; i += blockDim.x) {
+        const int k = i >> 5;
+        lutw[i] = (uint32_t)q8[4 * k] | (uint32_t)q8[4 * k + 1] << 8 | (uint32_t)q8[4 * k + 2] << 16 |
+                  (uint32_t)q8[4 * k + 3] << 24;
+    }
+    __syncthreads();
+    const uint8_t *lut = reinterpret_cast<const uint8_t *>(lutw) + (threadIdx.x & 31) * 4;
+    auto quant4 = [&](uint32_t v) {
+        uint32_t r = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t u = (v >> (8 * k)) & 0xFFu;
+            r |= (uint32_t)lut[((u & 0xFCu) << 5) | (u & 3u)] << (8 * k);
+        }
+        return r;
+    };
+    const int band = blockIdx.x % nbands, b = blockIdx.x / nbands;
+    const int i0 = band * kStemBand;
+    const int nr = (kStemBand - 1) * sh + 3;
+    const int units = row_bytes / 16, data_units = w * 3 / 16;
+    const int ih0 = i0 * sh - pt;
+    for (int t = threadIdx.x; t < nr * units; t += blockDim.x) {
+        const int a = t / units, u = t - a * units;
+        const int ih = ih0 + a;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (u >= 1 && u <= data_units && ih >= 0 && ih < h) {
+            const uint4 s = __ldg(reinterpret_cast<const uint4 *>(x + ((size_t)b * h + ih) * w * 3) + (u - 1));
+            v = make_uint4(quant4(s.x), quant4(s.y), quant4(s.z), quant4(s.w));
+        }
+        *reinterpret_cast<uint4 *>(rows + a * row_bytes + u * 16) = v;
+    }
+    __syncthreads();
+    for (int r = 0; r < kStemBand; r++) {
+        const int oi = i0 + r;
+        if (oi >= ho) break;
+        int8_t *yrow = y + ((size_t)b * ho + oi) * wo * 32;
+        const uint8_t *rr = rows + r * sh * row_bytes;
+        for (int j = threadIdx.x; j < wo; j += blockDim.x) {
+            const int s0 = 16 + (j * sw - pl) * 3;  // first of the 9 bytes, >= 16 - 3 * pl >= 1
+            const int base = s0 & ~3, sh8 = (s0 & 3) * 8;
+            uint32_t q[3][3];
+#pragma unroll
+            for (int a = 0; a < 3; a++) {
+                const uint32_t *wp = reinterpret_cast<const uint32_t *>(rr + a * row_bytes + base);
+                const uint32_t w0 = wp[0], w1 = wp[1], w2 = wp[2];
+                q[a][0] = __funnelshift_r(w0, w1, sh8);
+                q[a][1] = __funnelshift_r(w1, w2, sh8);
+                q[a][2] = (w2 >> sh8) & 0xffu;
+            }
+            uint4 *dst = reinterpret_cast<uint4 *>(yrow + (size_t)j * 32);
+            dst[0] = make_uint4(q[0][0], q[0][1], q[0][2] | q[1][0] << 8, q[1][0] >> 24 | q[1][1] << 8);
+            dst[1] = make_uint4(q[1][1] >> 24 | q[1][2] << 8 | q[2][0] << 16, q[2][0] >> 16 | q[2][1] << 16,
+                                q[2][1] >> 16 | q[2][2] << 16, 0u);
+        }
+    }
+}
+
 // --- dequantize: ops.rs:3453-3457 ---------------------------------------------
 __global__ void k_dequantize(const int8_t *__restrict__ in, float *__restrict__ out, size_t n, float s) {
     size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
@@ -695,6 +768,13 @@ dw_status launch_im2col_u8_i8(dw_backend *be, const uint8_t *x, int8_t *y, int n
         const long long last = 16 + ((long long)(wo - 1) * sw - pl) * 3 + 12;
         const long long need = std::max<long long>(16 + (long long)w * 3, last);
         const long long row_bytes = (need + 15) / 16 * 16;
+        const long long band_rows = (long long)(kStemBand - 1) * sh + 3;
+        const int nbands = (ho + kStemBand - 1) / kStemBand;
+        if (band_rows * row_bytes <= 38 * 1024 && (long long)n * nbands < (1LL << 31)) {
+            k_im2col_stem3_band<<<n * nbands, 256, (size_t)(band_rows * row_bytes), be->stream>>>(
+                x, y, h, w, sh, sw, pt, pl, ho, wo, (int)row_bytes, nbands, inv255, inv);
+            return dw_after_launch(be, "im2col_u8_i8");
+        }
         if (3 * row_bytes <= 40 * 1024) {
             k_im2col_stem3_rows<<<n * ho, kThreads, (size_t)(3 * row_bytes), be->stream>>>(
                 x, y, h, w, sh, sw, pt, pl, ho, wo, (int)row_bytes, inv255, inv);

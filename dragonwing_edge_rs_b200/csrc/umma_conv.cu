@@ -99,6 +99,10 @@ struct UmmaParams {
     int tpair;                              // resident weights of a 16-byte channel row: [tap + 1][bn][16 B]
                                             // slices without swizzle (the last all zero), so that one 32-byte
                                             // K step takes two horizontal taps
+    int epi_pipe;                           // int8 epilogue without SiLU: the next TMEM load in flight
+                                            // during the requantisation (convs with several taps, whose
+                                            // MMAs overlap the epilogue; a kernel instance of its own),
+                                            // else two loads per wait
     int flat_in;                            // mode 2, a dense 16-byte channel row: the activation map is
                                             // [n][h][w * 16 bytes], so a halo tile is one box of hh rows of
                                             // hw * 16 contiguous bytes (not hw * hh 16-byte rows)
@@ -244,9 +248,13 @@ __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs,
     // |(acc + bias) * M| < 2^21 for every accumulator (kept below 2e6), so
     // v + 1.5 * 2^22 + 0.5 stays in [2^22, 2^23)
     const bool r16 = safe && isfinite(m) && fabsf(m) * (float)(p.acc_bound + b) < 2.0e6f;
+    // bit3: the same path applies to any tile whose |acc + bias| < 2^22 (checked
+    // per 16 accumulators by the epilogue): |M| < 0.47 keeps |v| below 2e6 there
+    const bool mfast = isfinite(m) && fabsf(m) < 0.47f;
     const uint32_t bf = __ballot_sync(0xffffffffu, finite);
     const uint32_t bs = __ballot_sync(0xffffffffu, safe);
     const uint32_t br = __ballot_sync(0xffffffffu, r16);
+    const uint32_t bm = __ballot_sync(0xffffffffu, mfast);
     if (write) {
         cs->bias[slot] = bias;
         cs->m[slot] = m;
@@ -258,7 +266,7 @@ __device__ __forceinline__ void stage_channel(const UmmaParams &p, ChanSmem *cs,
     if ((lane & 15) == 0 && write) {
         const uint32_t sh = lane;  // 0 or 16
         const uint32_t f = (((bf >> sh) & 0xFFFFu) == 0xFFFFu ? 1u : 0u) | (((bs >> sh) & 0xFFFFu) == 0xFFFFu ? 2u : 0u) |
-                           (((br >> sh) & 0xFFFFu) == 0xFFFFu ? 4u : 0u);
+                           (((br >> sh) & 0xFFFFu) == 0xFFFFu ? 4u : 0u) | (((bm >> sh) & 0xFFFFu) == 0xFFFFu ? 8u : 0u);
         cs->cflags[slot >> 4] = f;
     }
 }
@@ -318,7 +326,7 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
         }
         return make_uint4(w[0], w[1], w[2], w[3]);
     }
-    if ((epi == DW_EPI_RELU || (epi == DW_EPI_RELU6 && p.ep.q6 >= 0)) && __all_sync(0xffffffffu, (fl & 4u) != 0)) {
+    if ((epi == DW_EPI_RELU || (epi == DW_EPI_RELU6 && p.ep.q6 >= 0)) && __all_sync(0xffffffffu, (fl & 12u) != 0)) {
         // ReLU / ReLU6, exact and branch-free: v = fl((acc + bias) * M) as the
         // reference (acc + bias + magic bits read as a float, minus 1.5 * 2^23);
         // one add rounded toward zero of 1.5 * 2^22 + 0.5 (the spacing there is
@@ -335,6 +343,20 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
         const uint4 m4[4] = {lds_v4(ma), lds_v4(ma + 16), lds_v4(ma + 32), lds_v4(ma + 48)};
         const int32_t *bm = reinterpret_cast<const int32_t *>(d4);
         const float *mm = reinterpret_cast<const float *>(m4);
+        // u = acc + bias + the magic bits (wrapping, as the reference's i32 add)
+        uint32_t u[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) u[k] = (uint32_t)v[k] + (uint32_t)bm[k];
+        bool fast = true;
+        if (!(fl & 4u)) {
+            // the shape's bound on |acc| does not keep acc + bias within 2^22: check
+            // these 16 (u - magic + 2^22 in [0, 2^23) for each; one OR covers all)
+            uint32_t orr = 0;
+#pragma unroll
+            for (int k = 0; k < 16; k++) orr |= u[k] - (uint32_t)(kMagicBits - (1 << 22));
+            fast = orr < (1u << 23);
+        }
+        if (__all_sync(0xffffffffu, fast)) {
         const int hi = epi == DW_EPI_RELU6 ? min(p.ep.q6, 127) : 127;
         const float2 nmag = make_float2(-kMagic, -kMagic);
         const float2 mag = make_float2(6291456.5f, 6291456.5f);  // 1.5 * 2^22 + 0.5
@@ -344,9 +366,7 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 const int k0 = q * 4 + 2 * h;
-                const float2 f = __fadd2_rn(make_float2(__int_as_float((int32_t)((uint32_t)v[k0] + (uint32_t)bm[k0])),
-                                                        __int_as_float((int32_t)((uint32_t)v[k0 + 1] + (uint32_t)bm[k0 + 1]))),
-                                            nmag);
+                const float2 f = __fadd2_rn(make_float2(__uint_as_float(u[k0]), __uint_as_float(u[k0 + 1])), nmag);
                 const float2 r = __fadd2_rz(__fmul2_rn(f, make_float2(mm[k0], mm[k0 + 1])), mag);
                 t[2 * h] = __viaddmin_s32_relu(__float_as_int(r.x), -0x4AC00000, 2 * hi + 1);
                 t[2 * h + 1] = __viaddmin_s32_relu(__float_as_int(r.y), -0x4AC00000, 2 * hi + 1);
@@ -355,6 +375,7 @@ __device__ __forceinline__ uint4 requant16(const int32_t (&v)[16], const ChanSme
             w[q] = (packed >> 1) & 0x7F7F7F7Fu;
         }
         return make_uint4(w[0], w[1], w[2], w[3]);
+        }
     }
     const uint32_t ba = smem_u32(sb), ma = smem_u32(sm);
     const uint4 b4[4] = {lds_v4(ba), lds_v4(ba + 16), lds_v4(ba + 32), lds_v4(ba + 48)};
@@ -728,7 +749,7 @@ __device__ __forceinline__ int4 tap_coord(const UmmaParams &p, int tap) {
 
 // kSilu: int8 SiLU epilogue.  kF16: fp16 operands (kind::f16) with the fp16
 // epilogue; kFm its bias / residual / ReLU flags.
-template <bool kSilu, bool kF16, int kFm>
+template <bool kSilu, bool kF16, int kFm, bool kPipe = false>
 __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
     k_umma_conv_i8(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_r,
@@ -1116,7 +1137,59 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                         }
                     }
                 }
-            } else if (p.R == 1) {  // one row block: contiguous chunk halves, one TMEM load per wait
+            } else if constexpr (kPipe) {
+                // int8 (instances without SiLU): each part of the warps takes a
+                // contiguous run of (row block, chunk) items, kB per TMEM round.  The next round's loads are in
+                // flight while this round is requantised: a TMEM load waits long
+                // while the MMAs write the other accumulator buffer.  (The loads'
+                // registers are read only after the wait that covers them.)
+                constexpr int kB = 1;
+                const int per = (items + kEpiParts - 1) / kEpiParts;
+                const int i_begin = part * per, i_end = min(items, i_begin + per);
+                const int rounds = i_end > i_begin ? (i_end - i_begin + kB - 1) / kB : 0;
+                int cur_r = 0, cur_c = i_begin;  // the next item to load
+                while (cur_c >= chunks) { cur_c -= chunks; cur_r++; }
+                int lr0[kB], lc0[kB], lr1[kB], lc1[kB];
+                int32_t v0[kB][16], v1[kB][16];
+                // loads round j (items past the run repeat the last one: the loads are collective)
+                auto load_round = [&](int j, int (&lr)[kB], int (&lc)[kB], int32_t (&v)[kB][16]) {
+#pragma unroll
+                    for (int q = 0; q < kB; q++) {
+                        if (q == 0 || i_begin + j * kB + q < i_end) {
+                            lr[q] = cur_r;
+                            lc[q] = cur_c;
+                            if (++cur_c == chunks) { cur_c = 0; cur_r++; }
+                        } else {
+                            lr[q] = lr[q - 1];
+                            lc[q] = lc[q - 1];
+                        }
+                        tc_ld16(tacc + (uint32_t)(lr[q] * p.bn + lc[q] * 16), v[q]);
+                    }
+                };
+                auto store_round = [&](int j, const int (&lr)[kB], const int (&lc)[kB], const int32_t (&v)[kB][16]) {
+#pragma unroll
+                    for (int q = 0; q < kB; q++) {
+                        if (q == 0 || i_begin + j * kB + q < i_end) {
+                            const uint32_t dst = smem_u32(stage + ((size_t)(lr[q] * kBM + row)) * p.bn + lc[q] * 16);
+                            sts_v4(dst, with_residual<kFm>(requant16<kSilu>(v[q], chan, slot_base + lc[q] * 16, p), dst, p));
+                        }
+                    }
+                };
+                if (rounds > 0) {
+                    load_round(0, lr0, lc0, v0);
+                    tc_wait_ld();
+                }
+                for (int j = 0; j < rounds; j += 2) {
+                    if (j + 1 < rounds) load_round(j + 1, lr1, lc1, v1);
+                    store_round(j, lr0, lc0, v0);
+                    tc_wait_ld();
+                    if (j + 1 < rounds) {
+                        if (j + 2 < rounds) load_round(j + 2, lr0, lc0, v0);
+                        store_round(j + 1, lr1, lc1, v1);
+                        tc_wait_ld();
+                    }
+                }
+            } else if (p.R == 1) {  // one row block: contiguous chunk halves, two TMEM loads per wait
                 const int per1 = (chunks + kEpiParts - 1) / kEpiParts;
                 const int cb = part * per1, ce = min(chunks, cb + per1);
                 // two TMEM loads in flight per wait (the loads are collective: past
@@ -1676,6 +1749,13 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     // when every tile's channels split into whole slabs.
     if (esize == 2 && p.bn % 64 == 0 && !getenv("DW_F16_NOSWZ")) p.swz = 1;
     p.chan_all = p.n_tiles * p.bn <= kChanSlots ? 1 : 0;  // every slot a tile reads lies in the arrays
+    // Convs with several taps run long MMA phases beside the epilogue, and a TMEM
+    // load waits long while the MMAs write the other accumulator buffer: keep the
+    // next load in flight (int8 epilogues other than SiLU).  1x1 convs (short MMA
+    // phases) do better with two loads per wait (measured on B200: config 1 at
+    // N=256 +3%, MobileNetV2's 96 -> 576 expand 173 -> 148 us).
+    p.epi_pipe = d.k_h * d.k_w > 1 ? 1 : 0;
+    if (const char *e = getenv("DW_UMMA_EPI_PIPE")) p.epi_pipe = atoi(e) != 0;  // tuning override
     p.b_tx_bytes = (uint32_t)(p.bn * p.bk);
     p.a_stage_bytes = (uint32_t)al1k((size_t)p.R * kBM * p.bk);
     p.b_stage_bytes = (uint32_t)al1k((size_t)p.bn * p.bk);
@@ -1862,6 +1942,10 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
                              (int)kSmemLimit);
         cudaFuncSetAttribute(k_umma_conv_i8<true, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<false, false, 0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemLimit);
+        cudaFuncSetAttribute(k_umma_conv_i8<false, false, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemLimit);
         for (KernelFn f : f16_kernels)
             cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
         attr_set[dev] = true;
@@ -1873,10 +1957,15 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     } else if (res_i8) {
         if (ep.epilogue == DW_EPI_SILU)
             k_umma_conv_i8<true, false, 2><<<grid, umma_threads(true, false), smem, be->stream>>>(ta, tb, ty, tr, p);
+        else if (p.epi_pipe)
+            k_umma_conv_i8<false, false, 2, true><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr,
+                                                                                                      p);
         else
             k_umma_conv_i8<false, false, 2><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr, p);
     } else if (ep.epilogue == DW_EPI_SILU) {
         k_umma_conv_i8<true, false, 0><<<grid, umma_threads(true, false), smem, be->stream>>>(ta, tb, ty, tr, p);
+    } else if (p.epi_pipe) {
+        k_umma_conv_i8<false, false, 0, true><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr, p);
     } else {
         k_umma_conv_i8<false, false, 0><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr, p);
     }

@@ -261,6 +261,36 @@ def test_conv_relu_requant_edges(be_umma, be_direct, k, epi, q6):
         _check_conv(be_, (desc, x, wt, b, M, D))
 
 
+@pytest.mark.parametrize("epi,q6", [(dw.EPI_RELU, 127), (dw.EPI_RELU6, 6)])
+def test_conv_relu_accumulators_beyond_2_22(be_umma, epi, q6):
+    """ReLU / ReLU6 where the shape's accumulator bound is above 2^22, so the
+    one-add path checks each 16 accumulators (+ bias) at run time: saturated
+    pixels and weights put |acc + bias| above 2^22 (up to 9.3e6) in some
+    16-channel groups and rows, small values in the rest, so the two paths
+    meet inside one tile; scales small enough for the one-add path, and some
+    that are not (0.5)."""
+    rng = np.random.default_rng(4122 + q6)
+    n, h, w, c_in, c_out = 2, 20, 24, 64, 64
+    desc, x, wt, b, M, D = conv_case(rng, n, h, w, c_in, c_out, k=3, epilogue=epi, x_range=(-20, 20))
+    x = x.reshape(n, h, w, c_in)
+    x[0, 4:12, :, :] = 127          # a band of saturated pixels in image 0
+    x[1, :, 10:14, :] = -128        # and a column band in image 1
+    x = x.reshape(-1)
+    wt = wt.reshape(3, 3, c_in, c_out)
+    wt[..., 0:16] = 127             # group 0: |acc| up to 9 * 64 * 127 * 128 on the bands
+    wt[..., 16:20] = -127
+    wt = wt.reshape(-1)
+    M = M.copy()
+    M[0:16] = np.float32(1.3e-5)
+    M[16:20] = np.float32(-2.1e-5)
+    M[20:24] = np.float32(0.5)
+    b = b.copy()
+    b[24:28] = 4_000_000            # bias alone near 2^22 for a group of the small-valued channels
+    b[28:32] = -4_000_000
+    desc.q6 = q6
+    _check_conv(be_umma, (desc, x, wt, b, M, D))
+
+
 @pytest.mark.parametrize("c_in,k,s", [(64, 1, 1), (32, 3, 1), (3, 3, 2)])
 def test_silu_stress_full_range(be, be_direct, c_in, k, s):
     """SiLU over y in about [-20, 20] with t = silu(y)/s_out spanning the whole
