@@ -40,14 +40,16 @@ namespace {
 constexpr int kBM = 128;            // MMA M (rows per tile = pixels)
 // Warp roles: 0 producer, 1 MMA, then the epilogue warps (4 per part: warps
 // sharing a TMEM lane quarter split its (row block, chunk) items), then the
-// store warp.  The int8 SiLU epilogue (issue-bound) runs 16 epilogue warps, four
+// store warp, then a second MMA warp (tiles of several row blocks: the two
+// issue alternate row blocks -- one thread issues a tcgen05.mma only every
+// ~50 cycles, and the issue competes with the epilogue for its scheduler).  The int8 SiLU epilogue (issue-bound) runs 16 epilogue warps, four
 // streams per scheduler at 96 registers a thread (YOLOv8n b32's stem conv 125 ->
 // 111 us, the step 1.995 -> 1.971 ms); the others keep 12 at 128 registers
 // (with 16 the ReLU6 / linear int8 epilogue spills and the MobileNetV2 block
 // went 0.336 -> 0.351 ms; the fp16 epilogue keeps two TMEM loads in flight per
 // wait instead of four).
 constexpr int epi_warps(bool silu, bool f16) { return (silu && !f16) ? 16 : 12; }
-constexpr int umma_threads(bool silu, bool f16) { return 64 + 32 * epi_warps(silu, f16) + 32; }
+constexpr int umma_threads(bool silu, bool f16) { return 64 + 32 * epi_warps(silu, f16) + 64; }
 constexpr int kMaxStages = 12;
 
 struct UmmaParams {
@@ -99,6 +101,7 @@ struct UmmaParams {
     int tpair;                              // resident weights of a 16-byte channel row: [tap + 1][bn][16 B]
                                             // slices without swizzle (the last all zero), so that one 32-byte
                                             // K step takes two horizontal taps
+    int n_issuers;                          // MMA warps (2: alternate row blocks; 1 when R == 1)
     int epi_pipe;                           // int8 epilogue without SiLU: the next TMEM load in flight
                                             // during the requantisation (convs with several taps, whose
                                             // MMAs overlap the epilogue; a kernel instance of its own),
@@ -589,17 +592,17 @@ __device__ __forceinline__ void tc_mma_w(uint32_t d, uint32_t alo, uint32_t ahi,
 // one 32-byte K step: x = the A descriptor's low word relative to the stage's
 // first plane (the tap's offset, and the LBO between the step's two 16-byte
 // halves), y = the B descriptor's low word (added to b16: 0 for resident
-// weights, else the stage's B tile).  Row block r reads A roff16[r] 16-byte
-// units further and accumulates into columns [r * bn, +bn).  `first`: the first
-// step overwrites the accumulators.
+// weights, else the stage's B tile).  The i-th issued row block reads A
+// roff16[i] 16-byte units further and accumulates into the columns from
+// d_tmem + i * dstride.  `first`: the first step overwrites the accumulators.
 template <int kR, bool kF16>
 __device__ __forceinline__ void halo_mmas(const int2 *tab, int n, uint32_t a16, uint32_t b16, uint32_t ahi,
-                                          uint32_t bhi, uint32_t d_tmem, uint32_t bn, const uint32_t (&roff16)[8],
+                                          uint32_t bhi, uint32_t d_tmem, uint32_t dstride, const uint32_t (&roff16)[8],
                                           uint32_t idesc, bool first) {
     uint32_t dcol[kR], ar[kR];
 #pragma unroll
     for (int r = 0; r < kR; r++) {
-        dcol[r] = d_tmem + (uint32_t)r * bn;
+        dcol[r] = d_tmem + (uint32_t)r * dstride;
         ar[r] = a16 + roff16[r];
     }
     int q = 0;
@@ -621,7 +624,7 @@ __device__ __forceinline__ void halo_mmas(const int2 *tab, int n, uint32_t a16, 
 template <bool kF16>
 __device__ __forceinline__ void halo_mmas_r(int R, const int2 *tab, int n, uint32_t a16, uint32_t b16, uint32_t ahi,
                                             uint32_t bhi, uint32_t d_tmem, uint32_t bn, const uint32_t (&roff16)[8],
-                                            uint32_t idesc, bool first) {
+                                            uint32_t idesc, bool first) {  // bn: the column stride
     switch (R) {
         case 1: halo_mmas<1, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
         case 2: halo_mmas<2, kF16>(tab, n, a16, b16, ahi, bhi, d_tmem, bn, roff16, idesc, first); break;
@@ -635,7 +638,8 @@ __device__ __forceinline__ void halo_mmas_r(int R, const int2 *tab, int n, uint3
 }
 
 // Modes 0 and 1: the MMAs of one stage -- kn 32-byte K steps (two 16-byte units
-// each) of kR row blocks, block r's A tile r * rstride16 units into the stage;
+// each) of kR row blocks, the i-th one's A tile i * rstride16 units into the
+// stage and its accumulators at columns d_tmem + i * bn (bn: the column stride);
 // a16 / b16 are the descriptors' low words (address and LBO field), hi their
 // common high word (SBO, version, swizzle).
 template <int kR, bool kF16>
@@ -758,6 +762,7 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
     constexpr int kF16Batch = kEpiWarps > 8 ? 2 : 4;  // fp16 TMEM loads per wait (registers)
     constexpr int kEpiParts = kEpiWarps / 4;
     constexpr int kStoreWarp = 2 + kEpiWarps;
+    constexpr int kMma2Warp = kStoreWarp + 1;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1 KiB-aligned base (swizzle patterns repeat every 1 KiB).
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -774,7 +779,8 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
     uint64_t *res_bar = drain_bar + 1;              // [2] staging buffer free for the next tile (fp16: residual in)
     uint64_t *ready_bar = res_bar + 2;              // [2] staging buffer holds a finished tile
     uint64_t *w_bar = ready_bar + 2;                // [1] resident weights landed (mode 2, wres)
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(w_bar + 1);
+    uint64_t *drain2_bar = w_bar + 1;               // [1] the second MMA warp's drain on abort
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain2_bar + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -787,13 +793,14 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; s++) {
             mbar_init(smem_u32(&full_bar[s]), 1);
-            mbar_init(smem_u32(&empty_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), p.n_issuers);
         }
         for (int a = 0; a < 2; a++) {
-            mbar_init(smem_u32(&tfull_bar[a]), 1);
+            mbar_init(smem_u32(&tfull_bar[a]), p.n_issuers);
             mbar_init(smem_u32(&tempty_bar[a]), kEpiWarps);
         }
         mbar_init(smem_u32(drain_bar), 1);
+        mbar_init(smem_u32(drain2_bar), 1);
         mbar_init(smem_u32(w_bar), 1);
         for (int b = 0; b < 2; b++) {
             mbar_init(smem_u32(&res_bar[b]), 1);
@@ -808,6 +815,44 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                      "r"(p.tmem_cols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        // halo mode: the MMA warps' K-step descriptor table (visible to both
+        // after the barrier below)
+        const uint32_t w_base = smem_u32(smem + p.off_w);
+        const int kn2_full = (p.cps + 1) >> 1;  // halo mode: K steps of a full K block
+        const int kn2_last = (min(p.cps, p.chunks - (p.cblocks - 1) * p.cps) + 1) >> 1;
+        if (p.mode == 2) {
+            const uint32_t hw16 = (uint32_t)p.hw * 16u;
+            auto tap_off = [&](int t) { return ((uint32_t)(t / p.kw) * hw16) + (uint32_t)(t % p.kw) * 16u; };
+            if (p.tpair) {
+                // taps (2q, 2q + 1) in one K step: A's second half is tap 2q + 1's
+                // pixel (LBO = the offset between the two taps' pixels), B's the
+                // next slice (the all-zero slice past the last tap)
+                for (int q = lane; q < (p.taps + 1) / 2; q += 32) {
+                    const int t = 2 * q;
+                    const uint32_t off = tap_off(t);
+                    const uint32_t lbo = t + 1 < p.taps ? tap_off(t + 1) - off : 16u;
+                    mtab[q] = make_int2((int)((off >> 4) | ((lbo >> 4) << 16)),
+                                        (int)(((w_base + (uint32_t)t * p.b_tap_bytes) >> 4) | ((p.b_tap_bytes >> 4) << 16)));
+                }
+            } else {
+                // K block `it`, tap t, K step k: chunk planes 2k and 2k + 1 (with an
+                // odd chunk count the last step's second half is the neighbouring
+                // pixel, LBO 16 bytes, against zero weights)
+                const int per = p.taps * kn2_full;
+                const int total = (p.cblocks - 1) * per + p.taps * kn2_last;
+                for (int i = lane; i < total; i += 32) {
+                    const int it = i / per, rem = i - it * per;
+                    const int knb = it == p.cblocks - 1 ? kn2_last : kn2_full;
+                    const int t = rem / knb, k = rem - t * knb;
+                    const int real = min(p.cps, p.chunks - it * p.cps);
+                    const uint32_t off = tap_off(t) + (uint32_t)(2 * k) * p.plane_stride;
+                    const uint32_t lbo = 2 * k + 1 < real ? p.plane_stride : 16u;
+                    const uint32_t b = p.wres ? w_base + (uint32_t)(t * p.cblocks + it) * p.b_tap_bytes + 32u * k
+                                              : (uint32_t)t * p.b_tap_bytes + 32u * k;
+                    mtab[i] = make_int2((int)((off >> 4) | ((lbo >> 4) << 16)), (int)((b >> 4) | (1u << 16)));
+                }
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -919,8 +964,8 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                 }
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || warp == kMma2Warp) {
+        // ------------------------------------------------------------ MMA issuers
         // The issue loop is latency-bound (one thread; each tcgen05.mma takes
         // tens of cycles to issue), so the descriptors are precomputed: halo
         // mode, one table entry per 32-byte K step (built once per CTA by the
@@ -928,41 +973,8 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
         const uint32_t w_base = smem_u32(smem + p.off_w);
         const int kn2_full = (p.cps + 1) >> 1;  // halo mode: K steps of a full K block
         const int kn2_last = (min(p.cps, p.chunks - (p.cblocks - 1) * p.cps) + 1) >> 1;
-        if (p.mode == 2) {
-            const uint32_t hw16 = (uint32_t)p.hw * 16u;
-            auto tap_off = [&](int t) { return ((uint32_t)(t / p.kw) * hw16) + (uint32_t)(t % p.kw) * 16u; };
-            if (p.tpair) {
-                // taps (2q, 2q + 1) in one K step: A's second half is tap 2q + 1's
-                // pixel (LBO = the offset between the two taps' pixels), B's the
-                // next slice (the all-zero slice past the last tap)
-                for (int q = lane; q < (p.taps + 1) / 2; q += 32) {
-                    const int t = 2 * q;
-                    const uint32_t off = tap_off(t);
-                    const uint32_t lbo = t + 1 < p.taps ? tap_off(t + 1) - off : 16u;
-                    mtab[q] = make_int2((int)((off >> 4) | ((lbo >> 4) << 16)),
-                                        (int)(((w_base + (uint32_t)t * p.b_tap_bytes) >> 4) | ((p.b_tap_bytes >> 4) << 16)));
-                }
-            } else {
-                // K block `it`, tap t, K step k: chunk planes 2k and 2k + 1 (with an
-                // odd chunk count the last step's second half is the neighbouring
-                // pixel, LBO 16 bytes, against zero weights)
-                const int per = p.taps * kn2_full;
-                const int total = (p.cblocks - 1) * per + p.taps * kn2_last;
-                for (int i = lane; i < total; i += 32) {
-                    const int it = i / per, rem = i - it * per;
-                    const int knb = it == p.cblocks - 1 ? kn2_last : kn2_full;
-                    const int t = rem / knb, k = rem - t * knb;
-                    const int real = min(p.cps, p.chunks - it * p.cps);
-                    const uint32_t off = tap_off(t) + (uint32_t)(2 * k) * p.plane_stride;
-                    const uint32_t lbo = 2 * k + 1 < real ? p.plane_stride : 16u;
-                    const uint32_t b = p.wres ? w_base + (uint32_t)(t * p.cblocks + it) * p.b_tap_bytes + 32u * k
-                                              : (uint32_t)t * p.b_tap_bytes + 32u * k;
-                    mtab[i] = make_int2((int)((off >> 4) | ((lbo >> 4) << 16)), (int)((b >> 4) | (1u << 16)));
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) {
+        const int issuer = warp == 1 ? 0 : 1;
+        if (lane == 0 && issuer < p.n_issuers) {
             int s = 0;
             uint32_t ph = 0;
             int local = 0;
@@ -971,15 +983,20 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
             const int kn_last = (p.c_in * p.esize - (p.cblocks - 1) * p.bk + 31) >> 5;
             if (p.wres && (int)blockIdx.x < p.num_tiles && !mbar_wait(smem_u32(&w_bar[0]), 0, p, abort_flag, 7))
                 ok = false;
-            // halo mode: per row block, its 16 B units from the tile's halo origin
-            // ((r / rw) * 16 halo rows + (r % rw) * 8 pixels); descriptor high
-            // words: A, SBO = one halo row; B, SBO = 8 rows of 16 bytes (two-tap
-            // slices) or of bk bytes (swizzled); version 1
+            // this warp's row blocks: issuer, issuer + n_issuers, ...
+            const int nis = p.n_issuers;
+            const int my_r = (p.R - issuer + nis - 1) / nis;
+            // halo mode: per issued row block r, its 16 B units from the tile's halo
+            // origin ((r / rw) * 16 halo rows + (r % rw) * 8 pixels); descriptor
+            // high words: A, SBO = one halo row; B, SBO = 8 rows of 16 bytes
+            // (two-tap slices) or of bk bytes (swizzled); version 1
             const uint32_t h_sbo = (uint32_t)p.hw * 16u;
             uint32_t roff16[8];
 #pragma unroll
-            for (int r = 0; r < 8; r++)
-                roff16[r] = p.mode == 2 ? (((uint32_t)(r / p.rw) * 16u * h_sbo) + (uint32_t)(r % p.rw) * 128u) >> 4 : 0u;
+            for (int i = 0; i < 8; i++) {
+                const int r = issuer + i * nis;
+                roff16[i] = p.mode == 2 ? (((uint32_t)(r / p.rw) * 16u * h_sbo) + (uint32_t)(r % p.rw) * 128u) >> 4 : 0u;
+            }
             const uint32_t hi_sw = (uint32_t)(p.desc_hi >> 32);
             const uint32_t a_hi2 = (h_sbo >> 4) | (1u << 14);
             const uint32_t b_hi2 = p.tpair ? ((128u >> 4) | (1u << 14)) : hi_sw;
@@ -989,7 +1006,7 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                 const uint32_t acc_ph = (local >> 1) & 1;
                 if (!mbar_wait(smem_u32(&tempty_bar[acc]), acc_ph ^ 1, p, abort_flag, 2)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)acc * acc_cols;
+                const uint32_t d_tmem = tmem_base + (uint32_t)acc * acc_cols + (uint32_t)(issuer * p.bn);
                 int cb = 0;  // channel block of this iteration (it % cblocks, kept incrementally)
                 for (int it = 0; it < k_iters; it++) {
                     if (!mbar_wait(smem_u32(&full_bar[s]), ph, p, abort_flag, 3)) { ok = false; break; }
@@ -1001,15 +1018,15 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                         // the tap's offset (8-row groups one halo row apart)
                         const int2 *tab = p.tpair ? mtab : mtab + it * p.taps * kn2_full;
                         const int n = p.tpair ? (p.taps + 1) / 2 : p.taps * (it == p.cblocks - 1 ? kn2_last : kn2_full);
-                        halo_mmas_r<kF16>(p.R, tab, n, a_addr >> 4, p.wres ? 0u : (b_addr >> 4), a_hi2, b_hi2, d_tmem,
-                                          (uint32_t)p.bn, roff16, p.idesc, it == 0);
+                        halo_mmas_r<kF16>(my_r, tab, n, a_addr >> 4, p.wres ? 0u : (b_addr >> 4), a_hi2, b_hi2, d_tmem,
+                                          (uint32_t)(nis * p.bn), roff16, p.idesc, it == 0);
                     } else {
                         // 32-byte K steps holding channels below c_in (the rest of the block is zero)
                         const int kn = cb == p.cblocks - 1 ? kn_last : kn_full;
                         if (++cb == p.cblocks) cb = 0;
-                        tile_mmas_r<kF16>(p.R, kn, ((a_addr >> 4) & 0x3FFFu) | (1u << 16),
-                                          ((b_addr >> 4) & 0x3FFFu) | (1u << 16), hi_sw, d_tmem, (uint32_t)p.bn,
-                                          rstride16, p.idesc, it == 0);
+                        tile_mmas_r<kF16>(my_r, kn, (((a_addr >> 4) & 0x3FFFu) + (uint32_t)issuer * rstride16) | (1u << 16),
+                                          ((b_addr >> 4) & 0x3FFFu) | (1u << 16), hi_sw, d_tmem, (uint32_t)(nis * p.bn),
+                                          (uint32_t)nis * rstride16, p.idesc, it == 0);
                     }
                     tc_commit(smem_u32(&empty_bar[s]));  // frees the stage when these MMAs finish
                     if (++s == p.stages) { s = 0; ph ^= 1; }
@@ -1018,11 +1035,12 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                 tc_commit(smem_u32(&tfull_bar[acc]));  // accumulators ready for the epilogue
             }
             if (!ok) {
-                // Abort: wait (bounded) until the MMAs already issued have retired,
+                // Abort: wait (bounded) until the MMAs this warp issued have retired,
                 // so TMEM is not freed under them.
-                tc_commit(smem_u32(drain_bar));
+                const uint32_t db = smem_u32(issuer ? drain2_bar : drain_bar);
+                tc_commit(db);
                 const uint64_t t0 = globaltimer_ns();
-                while (!mbar_try_wait(smem_u32(drain_bar), 0) && globaltimer_ns() - t0 < p.wait_cap_ns) {
+                while (!mbar_try_wait(db, 0) && globaltimer_ns() - t0 < p.wait_cap_ns) {
                 }
             }
         }
@@ -1755,6 +1773,7 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
     // phases) do better with two loads per wait (measured on B200: config 1 at
     // N=256 +3%, MobileNetV2's 96 -> 576 expand 173 -> 148 us).
     p.epi_pipe = d.k_h * d.k_w > 1 ? 1 : 0;
+    p.n_issuers = (p.R >= 2 && !getenv("DW_UMMA_ONE_ISSUER")) ? 2 : 1;  // DW_UMMA_ONE_ISSUER: tuning switch
     if (const char *e = getenv("DW_UMMA_EPI_PIPE")) p.epi_pipe = atoi(e) != 0;  // tuning override
     p.b_tx_bytes = (uint32_t)(p.bn * p.bk);
     p.a_stage_bytes = (uint32_t)al1k((size_t)p.R * kBM * p.bk);
