@@ -138,12 +138,15 @@ struct ChanSmem {
 // CTA is aborting or the cap expired (then the failure is recorded).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const UmmaParams &p,
                                           volatile int *abort_flag, int site) {
-    if (mbar_try_wait(bar, parity)) return true;
+    // polls first (a pipeline stage is usually only a little late, and a thread
+    // woken from a suspended try_wait resumes late), then waits suspended in
+    // hardware while the phase stays open (at most ~20 us per try)
+#pragma unroll 1
+    for (int i = 0; i < 256; i++)
+        if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
 #pragma unroll 1
     for (;;) {
-        // suspended in hardware while the phase is open (at most ~20 us per try):
-        // waiting warps leave the issue slots to the MMA issuer and the epilogue
         if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > p.wait_cap_ns) {
@@ -637,48 +640,6 @@ __device__ __forceinline__ void halo_mmas_r(int R, const int2 *tab, int n, uint3
     }
 }
 
-// Modes 0 and 1: the MMAs of one stage -- kn 32-byte K steps (two 16-byte units
-// each) of kR row blocks, the i-th one's A tile i * rstride16 units into the
-// stage and its accumulators at columns d_tmem + i * bn (bn: the column stride);
-// a16 / b16 are the descriptors' low words (address and LBO field), hi their
-// common high word (SBO, version, swizzle).
-template <int kR, bool kF16>
-__device__ __forceinline__ void tile_mmas(int kn, uint32_t a16, uint32_t b16, uint32_t hi, uint32_t d_tmem,
-                                          uint32_t bn, uint32_t rstride16, uint32_t idesc, bool first) {
-    uint32_t dcol[kR], ar[kR];
-#pragma unroll
-    for (int r = 0; r < kR; r++) {
-        dcol[r] = d_tmem + (uint32_t)r * bn;
-        ar[r] = a16 + (uint32_t)r * rstride16;
-    }
-    int k = 0;
-    if (first) {
-#pragma unroll
-        for (int r = 0; r < kR; r++) tc_mma_w<kF16, false>(dcol[r], ar[r], hi, b16, hi, idesc);
-        k = 1;
-    }
-    for (; k < kn; k++) {
-        const uint32_t k2 = 2u * (uint32_t)k;
-#pragma unroll
-        for (int r = 0; r < kR; r++) tc_mma_w<kF16, true>(dcol[r], ar[r] + k2, hi, b16 + k2, hi, idesc);
-    }
-}
-
-template <bool kF16>
-__device__ __forceinline__ void tile_mmas_r(int R, int kn, uint32_t a16, uint32_t b16, uint32_t hi, uint32_t d_tmem,
-                                            uint32_t bn, uint32_t rstride16, uint32_t idesc, bool first) {
-    switch (R) {
-        case 1: tile_mmas<1, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
-        case 2: tile_mmas<2, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
-        case 3: tile_mmas<3, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
-        case 4: tile_mmas<4, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
-        case 5: tile_mmas<5, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
-        case 6: tile_mmas<6, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
-        case 7: tile_mmas<7, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
-        default: tile_mmas<8, kF16>(kn, a16, b16, hi, d_tmem, bn, rstride16, idesc, first); break;
-    }
-}
-
 // ------------------------------------------------------------------- kernel
 // Tile = R blocks of 128 output pixels x bn output channels.  Row block r of a
 // tile covers pixels [tile_m0 + 128 r, +128) in flat mode, or the spatial
@@ -967,9 +928,9 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
     } else if (warp == 1 || warp == kMma2Warp) {
         // ------------------------------------------------------------ MMA issuers
         // The issue loop is latency-bound (one thread; each tcgen05.mma takes
-        // tens of cycles to issue), so the descriptors are precomputed: halo
-        // mode, one table entry per 32-byte K step (built once per CTA by the
-        // warp's lanes); every mode, the row blocks unrolled for the tile's R.
+        // tens of cycles to issue), so in halo mode (many small MMAs per stage)
+        // the descriptors are precomputed: one table entry per 32-byte K step
+        // (built once per CTA) and the row blocks unrolled for the tile's R.
         const uint32_t w_base = smem_u32(smem + p.off_w);
         const int kn2_full = (p.cps + 1) >> 1;  // halo mode: K steps of a full K block
         const int kn2_last = (min(p.cps, p.chunks - (p.cblocks - 1) * p.cps) + 1) >> 1;
@@ -1000,7 +961,6 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
             const uint32_t hi_sw = (uint32_t)(p.desc_hi >> 32);
             const uint32_t a_hi2 = (h_sbo >> 4) | (1u << 14);
             const uint32_t b_hi2 = p.tpair ? ((128u >> 4) | (1u << 14)) : hi_sw;
-            const uint32_t rstride16 = (uint32_t)(kBM * p.bk) >> 4;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, local++) {
                 const int acc = local & 1;
                 const uint32_t acc_ph = (local >> 1) & 1;
@@ -1024,9 +984,27 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                         // 32-byte K steps holding channels below c_in (the rest of the block is zero)
                         const int kn = cb == p.cblocks - 1 ? kn_last : kn_full;
                         if (++cb == p.cblocks) cb = 0;
-                        tile_mmas_r<kF16>(my_r, kn, (((a_addr >> 4) & 0x3FFFu) + (uint32_t)issuer * rstride16) | (1u << 16),
-                                          ((b_addr >> 4) & 0x3FFFu) | (1u << 16), hi_sw, d_tmem, (uint32_t)(nis * p.bn),
-                                          (uint32_t)nis * rstride16, p.idesc, it == 0);
+                        // plain loops: for 128 x 256 tiles they keep the tensor pipe busier than
+                        // an unrolled per-R issue (measured on B200: QGemm 4096^3 1,768 against
+                        // 1,523 TOPS); with several row blocks this warp's (issuer, issuer +
+                        // n_issuers, ...) for each K step
+                        if (p.R == 1) {
+                            for (int k = 0; k < kn; k++) {
+                                const uint64_t ad = smem_desc(a_addr + 32 * k, p.desc_hi);
+                                const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
+                                tc_mma<kF16>(d_tmem, ad, bd, p.idesc, (it > 0 || k > 0) ? 1u : 0u);
+                            }
+                        } else {
+                            for (int k = 0; k < kn; k++) {
+                                const uint64_t bd = smem_desc(b_addr + 32 * k, p.desc_hi);
+                                for (int i = 0; i < my_r; i++) {
+                                    const int r = issuer + i * nis;
+                                    const uint64_t ad = smem_desc(a_addr + (uint32_t)(r * kBM * p.bk) + 32 * k, p.desc_hi);
+                                    tc_mma<kF16>(d_tmem + (uint32_t)(i * nis * p.bn), ad, bd, p.idesc,
+                                                 (it > 0 || k > 0) ? 1u : 0u);
+                                }
+                            }
+                        }
                     }
                     tc_commit(smem_u32(&empty_bar[s]));  // frees the stage when these MMAs finish
                     if (++s == p.stages) { s = 0; ph ^= 1; }
