@@ -356,7 +356,7 @@ def load_traffic():
         return {}
 
 
-def roofline_of(graph, per_op, workload, peaks, f16, exclude_types=("YoloPostprocess",)):
+def roofline_of(graph, per_op, workload, peaks, f16, exclude_types=("YoloPostprocess",), config_key=None):
     """Roofline block of the unit with the largest device time."""
     peak_d, peak_src = peaks
     hbm_peak = float(peak_d.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
@@ -375,7 +375,9 @@ def roofline_of(graph, per_op, workload, peaks, f16, exclude_types=("YoloPostpro
         ach = dom["bytes"] / (dom["ms"] * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(ach / hbm_peak, 4)}
-    tr = load_traffic().get(workload, {})
+    # per-config captures (a workload timed at several batches) are keyed by the config
+    tr_all = load_traffic()
+    tr = tr_all.get(config_key) if config_key in tr_all else tr_all.get(workload, {})
     parts = [tr.get(o) for o in dom["ops_in_unit"]]
     traffic = sum(parts) if parts and all(isinstance(t, (int, float)) for t in parts) else None
     roof.update({"kernel": dom["kernel"], "kernel_ms": round(dom["ms"], 5), "algorithmic_bytes": dom["bytes"],
@@ -637,7 +639,7 @@ def run_configs(be, stream, args):
             "pct_of_tensor_peak": round(100.0 * tops / tensor_peak, 2),
             "kernels_per_step": kernels,
             "l2": "flushed between timed launches (256 MB write, outside the events)",
-            "roofline": roofline_of(g, per_op, name, peaks, f16),
+            "roofline": roofline_of(g, per_op, name, peaks, f16, config_key=key),
             "per_op": per_op if len(per_op) <= 8 else None,
         }
         rt.release()
