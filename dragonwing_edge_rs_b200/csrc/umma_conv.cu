@@ -1185,24 +1185,6 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                         tc_wait_ld();
                     }
                 }
-            } else if (p.R == 1) {  // one row block: contiguous chunk halves, two TMEM loads per wait
-                const int per1 = (chunks + kEpiParts - 1) / kEpiParts;
-                const int cb = part * per1, ce = min(chunks, cb + per1);
-                // two TMEM loads in flight per wait (the loads are collective: past
-                // the end the last chunk is loaded again and not stored)
-                const uint32_t dst0 = smem_u32(stage) + (uint32_t)(row * p.bn);
-                for (int c = cb; c < ce; c += 2) {
-                    const int c2 = min(c + 1, ce - 1);
-                    int32_t v1[16], v2[16];
-                    tc_ld16(tacc + (uint32_t)(c * 16), v1);
-                    tc_ld16(tacc + (uint32_t)(c2 * 16), v2);
-                    tc_wait_ld();
-                    sts_v4(dst0 + (uint32_t)(c * 16),
-                           with_residual<kFm>(requant16<kSilu>(v1, chan, slot_base + c * 16, p), dst0 + (uint32_t)(c * 16), p));
-                    if (c + 1 < ce)
-                        sts_v4(dst0 + (uint32_t)(c2 * 16), with_residual<kFm>(requant16<kSilu>(v2, chan, slot_base + c2 * 16, p),
-                                                                              dst0 + (uint32_t)(c2 * 16), p));
-                }
             } else {
             const int per = (items + kEpiParts - 1) / kEpiParts;
             const int i_begin = part * per, i_end = min(items, i_begin + per);
