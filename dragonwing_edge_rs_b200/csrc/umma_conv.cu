@@ -106,6 +106,13 @@ struct UmmaParams {
                                             // during the requantisation (convs with several taps, whose
                                             // MMAs overlap the epilogue; a kernel instance of its own),
                                             // else two loads per wait
+    int s2;                                 // mode 2 for a stride-2 conv: a stride-1 conv over the input's
+                                            // four (row, column) parity planes, x'[i][j][(ph, pw, c)] =
+                                            // x[2i + ph][2j + pw][c]: chunk j of x' is parity plane
+                                            // (ph, pw) = (j / (2 chunks0), j / chunks0 % 2) of 16-byte
+                                            // channel chunk j % chunks0; taps (dy, dx) of tkh x tkw from
+                                            // (dy0, dx0); weights resident as 16-byte slices [tap][chunk]
+    int tkh, tkw, dy0, dx0;
     int flat_in;                            // mode 2, a dense 16-byte channel row: the activation map is
                                             // [n][h][w * 16 bytes], so a halo tile is one box of hh rows of
                                             // hw * 16 contiguous bytes (not hw * hh 16-byte rows)
@@ -783,7 +790,9 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
         const int kn2_last = (min(p.cps, p.chunks - (p.cblocks - 1) * p.cps) + 1) >> 1;
         if (p.mode == 2) {
             const uint32_t hw16 = (uint32_t)p.hw * 16u;
-            auto tap_off = [&](int t) { return ((uint32_t)(t / p.kw) * hw16) + (uint32_t)(t % p.kw) * 16u; };
+            // the halo's taps: the conv's own, or (stride 2) the taps over the parity planes
+            const int hkw = p.s2 ? p.tkw : p.kw, htaps = p.s2 ? p.tkh * p.tkw : p.taps;
+            auto tap_off = [&](int t) { return ((uint32_t)(t / hkw) * hw16) + (uint32_t)(t % hkw) * 16u; };
             if (p.tpair) {
                 // taps (2q, 2q + 1) in one K step: A's second half is tap 2q + 1's
                 // pixel (LBO = the offset between the two taps' pixels), B's the
@@ -799,8 +808,8 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                 // K block `it`, tap t, K step k: chunk planes 2k and 2k + 1 (with an
                 // odd chunk count the last step's second half is the neighbouring
                 // pixel, LBO 16 bytes, against zero weights)
-                const int per = p.taps * kn2_full;
-                const int total = (p.cblocks - 1) * per + p.taps * kn2_last;
+                const int per = htaps * kn2_full;
+                const int total = (p.cblocks - 1) * per + htaps * kn2_last;
                 for (int i = lane; i < total; i += 32) {
                     const int it = i / per, rem = i - it * per;
                     const int knb = it == p.cblocks - 1 ? kn2_last : kn2_full;
@@ -808,6 +817,14 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                     const int real = min(p.cps, p.chunks - it * p.cps);
                     const uint32_t off = tap_off(t) + (uint32_t)(2 * k) * p.plane_stride;
                     const uint32_t lbo = 2 * k + 1 < real ? p.plane_stride : 16u;
+                    if (p.s2) {
+                        // 16-byte weight slices [tap][chunk]: the step's two chunks are
+                        // consecutive slices (LBO one slice)
+                        const uint32_t b = w_base + (uint32_t)(t * p.chunks + it * p.cps + 2 * k) * p.b_tap_bytes;
+                        mtab[i] = make_int2((int)((off >> 4) | ((lbo >> 4) << 16)),
+                                            (int)((b >> 4) | ((p.b_tap_bytes >> 4) << 16)));
+                        continue;
+                    }
                     const uint32_t b = p.wres ? w_base + (uint32_t)(t * p.cblocks + it) * p.b_tap_bytes + 32u * k
                                               : (uint32_t)t * p.b_tap_bytes + 32u * k;
                     mtab[i] = make_int2((int)((off >> 4) | ((lbo >> 4) << 16)), (int)((b >> 4) | (1u << 16)));
@@ -847,6 +864,20 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                     // so TMA fills it with zeros
                     for (int t = 0; t <= p.taps; t++)
                         tma_load_3d(w_dst + (uint32_t)t * p.b_tap_bytes, &tmap_b, wb, 0, t, 0);
+                } else if (p.s2) {
+                    // parity planes: slice (tap (dy, dx), chunk (ph, pw, cc)) holds kernel tap
+                    // (2 dy + ph + pt, 2 dx + pw + pl)'s chunk cc, or zeros (tap index past
+                    // the last: out of range) when no kernel tap lands there
+                    const int chunks0 = p.chunks / 4;
+                    for (int t2 = 0; t2 < p.tkh * p.tkw; t2++)
+                        for (int c2 = 0; c2 < p.chunks; c2++) {
+                            const int ph = c2 / (2 * chunks0), pw = (c2 / chunks0) & 1, cc = c2 % chunks0;
+                            const int kh = 2 * (t2 / p.tkw + p.dy0) + ph + p.pt;
+                            const int kw = 2 * (t2 % p.tkw + p.dx0) + pw + p.pl;
+                            const int tap = (kh >= 0 && kh < p.k_h && kw >= 0 && kw < p.kw) ? kh * p.kw + kw : p.taps;
+                            tma_load_3d(w_dst + (uint32_t)(t2 * p.chunks + c2) * p.b_tap_bytes, &tmap_b, wb,
+                                        cc * p.chunk_elems, tap, 0);
+                        }
                 } else {
                     for (int t = 0; t < p.taps; t++)
                         for (int cb = 0; cb < p.cblocks; cb++)
@@ -878,7 +909,17 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                                                (p.wres ? 0u : (uint32_t)p.taps * p.b_tx_bytes));
                         if (p.flat_in)  // one chunk: x counts 8-byte units, two per pixel
                             tma_load_3d(a_dst, &tmap_a, fb, 2 * (tc.ow0 - p.pl), tc.oh0 - p.pt, tc.img);
-                        else
+                        else if (p.s2) {
+                            // chunk it * cps + j of the parity planes: phase (ph, pw), channel chunk cc
+                            const int chunks0 = p.chunks / 4;
+                            for (int j = 0; j < real; j++) {
+                                const int c2 = it * p.cps + j;
+                                const int ph = c2 / (2 * chunks0), pw = (c2 / chunks0) & 1, cc = c2 % chunks0;
+                                tma_load_5d(a_dst + (uint32_t)j * p.plane_stride, &tmap_a, fb,
+                                            pw * p.c_in + cc * p.chunk_elems, tc.ow0 + p.dx0, ph, tc.oh0 + p.dy0,
+                                            tc.img);
+                            }
+                        } else
                             for (int j = 0; j < real; j++)
                                 tma_load_4d(a_dst + (uint32_t)j * p.plane_stride, &tmap_a, fb,
                                             it * p.bk_elems + j * p.chunk_elems, tc.ow0 - p.pl, tc.oh0 - p.pt,
@@ -960,7 +1001,7 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
             }
             const uint32_t hi_sw = (uint32_t)(p.desc_hi >> 32);
             const uint32_t a_hi2 = (h_sbo >> 4) | (1u << 14);
-            const uint32_t b_hi2 = p.tpair ? ((128u >> 4) | (1u << 14)) : hi_sw;
+            const uint32_t b_hi2 = (p.tpair || p.s2) ? ((128u >> 4) | (1u << 14)) : hi_sw;  // 16-byte slices
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, local++) {
                 const int acc = local & 1;
                 const uint32_t acc_ph = (local >> 1) & 1;
@@ -976,8 +1017,9 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
                     if (p.mode == 2) {
                         // every tap of K block `it`: the A tile is the halo plane read from
                         // the tap's offset (8-row groups one halo row apart)
-                        const int2 *tab = p.tpair ? mtab : mtab + it * p.taps * kn2_full;
-                        const int n = p.tpair ? (p.taps + 1) / 2 : p.taps * (it == p.cblocks - 1 ? kn2_last : kn2_full);
+                        const int htaps = p.s2 ? p.tkh * p.tkw : p.taps;
+                        const int2 *tab = p.tpair ? mtab : mtab + it * htaps * kn2_full;
+                        const int n = p.tpair ? (p.taps + 1) / 2 : htaps * (it == p.cblocks - 1 ? kn2_last : kn2_full);
                         halo_mmas_r<kF16>(my_r, tab, n, a_addr >> 4, p.wres ? 0u : (b_addr >> 4), a_hi2, b_hi2, d_tmem,
                                           (uint32_t)(nis * p.bn), roff16, p.idesc, it == 0);
                     } else {
@@ -1384,8 +1426,25 @@ constexpr size_t kSmemLimit = 227 * 1024 - sizeof(int4) * kTapTable - sizeof(int
 struct HaloPlan {
     bool ok = false;
     int R = 1, rw = 1, bn = 16, bk = 32, tiles_w = 1, tiles_h = 1, n_tiles = 1, wres = 0, tpair = 0;
+    int s2 = 0, tkh = 0, tkw = 0, dy0 = 0, dx0 = 0;  // stride-2 plan over the parity planes
     uint32_t plane = 0, w_bytes = 0;
 };
+
+// The taps of a stride-2 conv over the parity planes: kernel row kh reads input
+// row 2 oy + kh - pt = 2 (oy + dy) + ph with ph = (kh - pt) mod 2, so dy runs
+// from floor(-pt / 2) to floor((k_h - 1 - pt) / 2); likewise the columns.
+struct S2Taps {
+    int dy0, dx0, tkh, tkw;
+};
+S2Taps s2_taps(const dw_conv_desc &d) {
+    auto fl2 = [](int v) { return v >= 0 ? v / 2 : -((1 - v) / 2); };
+    S2Taps t;
+    t.dy0 = fl2(-d.pad_t);
+    t.dx0 = fl2(-d.pad_l);
+    t.tkh = fl2(d.k_h - 1 - d.pad_t) - t.dy0 + 1;
+    t.tkw = fl2(d.k_w - 1 - d.pad_l) - t.dx0 + 1;
+    return t;
+}
 
 uint32_t halo_plane_bytes(const dw_conv_desc &d, int rw, int rh) {
     return (uint32_t)(((size_t)(16 * rh + d.k_h - 1) * (size_t)(8 * rw + d.k_w - 1) * 16 + 127) & ~size_t(127));
@@ -1409,11 +1468,25 @@ int halo_bn(int c_out16, int taps) {
 HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, int esize, bool flat) {
     HaloPlan h;
     const int taps = d.k_h * d.k_w;
-    if (flat || d.stride_h != 1 || d.stride_w != 1 || taps < 2 || taps > kTapTable) return h;
+    // stride 2 (int8, 16 input channels): the parity-plane form.  It pays where
+    // the per-tap producer's boxes are half empty (16-byte rows): YOLOv8n b32's
+    // 16 -> 32 stem conv 80 -> 67 us; with 32 or 64 input channels the 4 x c_in
+    // K of the regrouped taps costs more MMAs than the per-tap producer's TMA
+    // boxes cost (47 -> 49, 29 -> 49 us).  Its zero weight slices would meet
+    // infinities in fp16 (0 * inf), so fp16 stays with the per-tap producer.
+    // DW_UMMA_HALO_S2: 0 = never, 2 = any channel count (tests and tuning).
+    const char *s2_env = getenv("DW_UMMA_HALO_S2");
+    const int s2_mode = s2_env ? atoi(s2_env) : 1;
+    const bool s2 = d.stride_h == 2 && d.stride_w == 2 && esize == 1 && d.h % 2 == 0 && d.w % 2 == 0 &&
+                    s2_mode != 0 && (s2_mode == 2 || d.c_in == 16);
+    if (flat || (!s2 && (d.stride_h != 1 || d.stride_w != 1)) || taps < 2 || taps > kTapTable) return h;
     if ((d.c_in * esize) % 16 || (esize == 2 && d.c_in % 16)) return h;  // fp16: whole 32-byte K steps
     if (8 + d.k_w - 1 > 256 || 16 + d.k_h - 1 > 256) return h;
     if (const char *e = getenv("DW_UMMA_HALO"))  // tuning switch: 0 keeps the per-tap producer
         if (atoi(e) == 0) return h;
+    const S2Taps st = s2_taps(d);
+    // the halo's kernel extent: the conv's own, or the taps over the parity planes
+    const int ekh = s2 ? st.tkh : d.k_h, ekw = s2 ? st.tkw : d.k_w;
     // pixel utilisation of 8 x 16 blocks; small maps keep the per-tap producer
     // (whole images side by side in one row block)
     const double util = (double)ho * wo / ((double)((wo + 7) / 8) * 8 * (double)((ho + 15) / 16) * 16);
@@ -1454,7 +1527,7 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
         auto key = [&](const Arr &a) {
             const long waves = (a.tiles + be->sm_count - 1) / be->sm_count;
             const long cost = waves * (a.rw * a.rh + 2);
-            const double halo = (double)(16 * a.rh + d.k_h - 1) * (8 * a.rw + d.k_w - 1) / (double)(a.rw * a.rh * kBM);
+            const double halo = (double)(16 * a.rh + ekh - 1) * (8 * a.rw + ekw - 1) / (double)(a.rw * a.rh * kBM);
             return std::make_tuple(cost, halo, a.rw);
         };
         std::sort(out, out + n, [&](const Arr &a, const Arr &b) { return key(a) < key(b); });
@@ -1470,6 +1543,37 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
         return n;
     };
     Arr arr[64];
+    if (s2) {
+        // stride 2: resident weights as 16-byte slices [tap][chunk] over the 4 x
+        // c_in / 16 chunks of the parity planes (zero slices for the (tap, parity)
+        // pairs no kernel tap maps to); a K block = cps chunk planes, every tap
+        const int chunks2 = 4 * chunks, taps2 = st.tkh * st.tkw;
+        if (c_out16 > 256 || taps2 * chunks2 / 2 > kMmaTable) return h;
+        const int bn = c_out16;
+        const size_t w_bytes = (size_t)taps2 * chunks2 * bn * 16;
+        const int n = arrangements(1, std::min(r_env, std::max(1, std::min(8, 256 / bn))), arr);
+        for (int i = 0; i < n; i++) {
+            const int R = arr[i].rw * arr[i].rh;
+            const uint32_t plane = (uint32_t)(((size_t)(16 * arr[i].rh + st.tkh - 1) *
+                                                   (size_t)(8 * arr[i].rw + st.tkw - 1) * 16 + 127) & ~size_t(127));
+            for (int cps : {8, 4, 2}) {
+                if (chunks2 % cps) continue;
+                const size_t stage = al1k((size_t)cps * plane);
+                const size_t fixed = 1024 + al1k((size_t)R * kBM * bn) + al1k(w_bytes) + chan + 512;
+                if (fixed < kSmemLimit && (kSmemLimit - fixed) / stage >= 3) {
+                    if (2 * arr[i].tiles < be->sm_count && !getenv("DW_UMMA_HALO_ANY_SIZE")) return h;
+                    h.ok = true; h.wres = 1; h.R = R; h.rw = arr[i].rw; h.bn = bn; h.bk = 16 * cps; h.n_tiles = 1;
+                    h.s2 = 1; h.tkh = st.tkh; h.tkw = st.tkw; h.dy0 = st.dy0; h.dx0 = st.dx0;
+                    h.tiles_w = (wo + 8 * h.rw - 1) / (8 * h.rw);
+                    h.tiles_h = (ho + 16 * arr[i].rh - 1) / (16 * arr[i].rh);
+                    h.plane = plane;
+                    h.w_bytes = (uint32_t)w_bytes;
+                    return h;
+                }
+            }
+        }
+        return h;
+    }
     // 1. resident weights: one channel tile, all weights beside >= 3 halo
     // stages.  Arrangements in cost order; for each, the K block with the least
     // padding first, then narrower ones (smaller stages).  A single row block
@@ -1632,22 +1736,25 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         p.tiles_h = hp.tiles_h;
         p.m_tiles = d.n * p.tiles_w * p.tiles_h;
         p.num_tiles = p.m_tiles * p.n_tiles;
-        p.hw = 8 * p.rw + d.k_w - 1;
-        p.hh = 16 * (p.R / p.rw) + d.k_h - 1;
+        p.s2 = hp.s2;
+        p.tkh = hp.tkh; p.tkw = hp.tkw; p.dy0 = hp.dy0; p.dx0 = hp.dx0;
+        p.hw = 8 * p.rw + (p.s2 ? p.tkw : d.k_w) - 1;
+        p.hh = 16 * (p.R / p.rw) + (p.s2 ? p.tkh : d.k_h) - 1;
         p.wres = hp.wres;
         p.w_bytes = hp.w_bytes;
-        p.chunks = d.c_in * esize / 16;
+        p.chunks = d.c_in * esize / 16 * (p.s2 ? 4 : 1);
         p.cps = p.bk / 16;
+        if (p.s2) p.cblocks = p.chunks / p.cps;  // K blocks over the parity planes' chunks
         p.chunk_elems = 16 / esize;
         p.plane_stride = hp.plane;
         p.tpair = hp.tpair;
-        p.b_tap_bytes = (uint32_t)(p.bn * (p.tpair ? 16 : p.bk));
+        p.b_tap_bytes = (uint32_t)(p.bn * ((p.tpair || p.s2) ? 16 : p.bk));
         p.a_tx_bytes = 0;  // per chunk: hw * hh * 16 bytes (the producer counts them)
         // Whole-row boxes where the data is contiguous: the TMA moves a box row by
         // row, so a halo of hw * hh 16-byte rows costs far more than hh rows of
         // hw * 16 bytes (and likewise for the stores).
         const bool no_flat = getenv("DW_UMMA_NO_FLAT") != nullptr;  // tuning switch: 16-byte rows throughout
-        p.flat_in = (!no_flat && p.chunks == 1 && x_pitch == d.c_in && 2 * p.hw <= 256) ? 1 : 0;
+        p.flat_in = (!no_flat && !p.s2 && p.chunks == 1 && x_pitch == d.c_in && 2 * p.hw <= 256) ? 1 : 0;
         p.flat_out = (!no_flat && esize == 1 && p.bn == d.c_out && y_pitch == d.c_out) ? 1 : 0;
     } else {
         p.bk = flat ? pick_bk(d.c_in * esize) : pick_bk_taps(d.c_in * esize);
@@ -1797,6 +1904,18 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         r = be->encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void *>(x), dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else if (p.mode == 2 && p.s2) {
+        // parity planes: the stride-2 view [n][h/2][2 row phases][w/2][2 column
+        // phases x c_in]; a box is one 16-byte chunk of one (row, column) phase,
+        // hh x hw positions, zero-filled outside the image (the padding)
+        cuuint64_t dims[5] = {2 * (cuuint64_t)d.c_in, (cuuint64_t)(d.w / 2), 2, (cuuint64_t)(d.h / 2), (cuuint64_t)d.n};
+        cuuint64_t strides[4] = {2 * (cuuint64_t)x_pitch * es, (cuuint64_t)d.w * x_pitch * es,
+                                 2 * (cuuint64_t)d.w * x_pitch * es, (cuuint64_t)d.h * d.w * x_pitch * es};
+        cuuint32_t box[5] = {(cuuint32_t)p.chunk_elems, (cuuint32_t)p.hw, 1, (cuuint32_t)p.hh, 1};
+        cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+        r = be->encode_tiled(&ta, dt, 5, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else if (p.mode == 2) {
         // halo boxes: one 16-byte channel chunk of (16 R + k_h - 1) x (8 + k_w - 1)
         // pixels, no swizzle; out-of-range pixels (the padding) are zero-filled
@@ -1831,10 +1950,10 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         cuuint64_t dims[3] = {(cuuint64_t)d.c_in, (cuuint64_t)p.taps, (cuuint64_t)d.c_out};
         cuuint64_t strides[2] = {(cuuint64_t)d.c_in * es, (cuuint64_t)p.taps * d.c_in * es};
         // two-tap K steps: one tap's 16 bytes per row, no swizzle (8-row core matrices)
-        cuuint32_t box[3] = {(cuuint32_t)(p.tpair ? 16 / esize : p.bk_elems), 1, (cuuint32_t)p.bn};
+        cuuint32_t box[3] = {(cuuint32_t)((p.tpair || p.s2) ? 16 / esize : p.bk_elems), 1, (cuuint32_t)p.bn};
         cuuint32_t estr[3] = {1, 1, 1};
         r = be->encode_tiled(&tb, dt, 3, const_cast<void *>(w_ohwi), dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, p.tpair ? CU_TENSOR_MAP_SWIZZLE_NONE : sw,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, (p.tpair || p.s2) ? CU_TENSOR_MAP_SWIZZLE_NONE : sw,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
     if (r != CUDA_SUCCESS) return dw_fail(be, DW_ERR_DEVICE, "%s: weight tensor map rejected (%d)", op, (int)r);

@@ -33,11 +33,13 @@ def halo_eligible(desc: ConvDesc, esize=1, wide=False) -> bool:
 
 @pytest.fixture(autouse=True)
 def _wide_halo(monkeypatch):
-    """Every shape here runs the halo producer: the wide-row ones too, and the
-    small ones that the planner would otherwise give the per-tap producer (it
-    reads DW_UMMA_HALO_WIDE and DW_UMMA_HALO_ANY_SIZE at each launch)."""
+    """Every shape here runs the halo producer: the wide-row ones too, the
+    small ones that the planner would otherwise give the per-tap producer, and
+    stride-2 convs of any channel count (it reads DW_UMMA_HALO_WIDE,
+    DW_UMMA_HALO_ANY_SIZE and DW_UMMA_HALO_S2 at each launch)."""
     monkeypatch.setenv("DW_UMMA_HALO_WIDE", "1")
     monkeypatch.setenv("DW_UMMA_HALO_ANY_SIZE", "1")
+    monkeypatch.setenv("DW_UMMA_HALO_S2", "2")
 
 
 @pytest.fixture(scope="module")
@@ -156,3 +158,58 @@ def test_halo_channel_range_views(be, ci, in_view, out_view):
     # channels outside the view are untouched
     assert np.array_equal(got[..., :out_off], out0[..., :out_off])
     assert np.array_equal(got[..., out_off + co:], out0[..., out_off + co:])
+
+
+S2_SHAPES = [
+    # n, h, w, c_in, c_out, k, pads (t, l, b, r), epilogue -- stride 2
+    (2, 64, 64, 16, 32, 3, (1, 1, 1, 1), dw.EPI_SILU),     # YOLOv8n's conv_2 shape class
+    (1, 80, 96, 32, 64, 3, (1, 1, 1, 1), dw.EPI_SILU),     # conv_10 class
+    (1, 60, 44, 64, 64, 3, (1, 1, 1, 1), dw.EPI_RELU),     # ragged output (30 x 22)
+    (2, 64, 48, 16, 48, 3, (0, 0, 1, 1), dw.EPI_RELU6),    # asymmetric pads: taps from (0, 0)
+    (1, 48, 64, 32, 32, 5, (2, 2, 2, 2), dw.EPI_NONE),     # 5x5: 3 x 3 taps over the parity planes
+    (2, 32, 48, 48, 16, 2, (0, 0, 0, 0), dw.EPI_SILU),     # 2x2: one tap, every parity in K
+]
+
+
+@pytest.mark.parametrize("shape", S2_SHAPES, ids=lambda s: "x".join(map(str, s[:6])) + f"_p{''.join(map(str, s[6]))}")
+def test_halo_stride2_parity_planes(be, shape):
+    """Stride-2 convs through the halo producer over the input's four parity
+    planes: a stride-1 conv over x'[i][j][(ph, pw, c)] = x[2i + ph][2j + pw][c]
+    with the kernel taps regrouped (zero weight slices where no tap lands)."""
+    n, h, w, ci, co, k, pads, epi = shape
+    rng = np.random.default_rng(sum(shape[:6]) + 7 * sum(pads) + epi)
+    desc = ConvDesc(n, h, w, ci, co, k, k, 2, 2, pads, 1, epi)
+    x = rng.integers(-128, 128, n * h * w * ci).astype(np.int8)
+    wt = rng.integers(-127, 128, k * k * ci * co).astype(np.int8)
+    s_w = rng.uniform(0.001, 0.01, co).astype(np.float32)
+    M = Q.requant_scales(0.02, s_w, 0.05)
+    D = Q.dequant_scales(0.02, s_w)
+    b = rng.integers(-1000, 1001, co).astype(np.int32)
+    desc.q6, desc.inv_s_out = Q.relu6_ceiling(0.05), float(np.float32(1.0) / np.float32(0.05))
+    y = cuda_conv(be, desc, x, wt, b, M, D)
+    ref = oracle_conv(desc, x, wt, b, M, D)
+    assert np.array_equal(y, ref), mismatch_report(y, ref)
+
+
+def test_halo_stride2_extreme_and_views(be):
+    """Saturated inputs and weights (|acc| > 2^24) through the parity planes,
+    the output written into a channel range of a wider tensor."""
+    rng = np.random.default_rng(2202)
+    n, h, w, ci, co, c_tot_out = 2, 64, 48, 64, 32, 96
+    desc, x, wt, b, M, D = conv_case(rng, n, h, w, ci, co, k=3, s=2, epilogue=dw.EPI_NONE)
+    x = np.where(rng.random(x.size) < 0.5, -128, 127).astype(np.int8)
+    wt = np.where(rng.random(wt.size) < 0.9, -128, 127).astype(np.int8)
+    M = (M * np.float32(1e-3)).astype(np.float32)
+    bx = be.upload_array(x)
+    wp = ops.prepare_weights_i8(be, desc, be.upload_array(wt))
+    bb, bm, bd = be.upload_array(b), be.upload_array(M), be.upload_array(D)
+    ho, wo = desc.out_hw()
+    out0 = rng.integers(-128, 128, (n, ho, wo, c_tot_out)).astype(np.int8)
+    by = be.upload_array(out0.reshape(-1))
+    ops.conv2d_i8_view(be, desc, (bx, 0, ci), wp, bb, bm, bd, (by, 32, c_tot_out))
+    got = be.download_array(by, np.int8).reshape(n, ho, wo, c_tot_out)
+    be.synchronize(20000)
+    ref = oracle_conv(desc, x, wt, b, M, D).reshape(n, ho, wo, co)
+    assert np.array_equal(got[..., 32:64], ref), mismatch_report(got[..., 32:64].reshape(-1), ref.reshape(-1))
+    assert np.array_equal(got[..., :32], out0[..., :32])
+    assert np.array_equal(got[..., 64:], out0[..., 64:])
