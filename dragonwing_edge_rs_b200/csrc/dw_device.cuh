@@ -55,23 +55,35 @@ __device__ __forceinline__ uint32_t f32_to_i8_byte_nonan(float v) {
 // ---- SiLU fast path with a certified result -------------------------------
 // t = fl(fl(y * fl(1/fl(1 + exp(-y)))) * inv_s_out) computed with the PTX
 // approximations ex2.approx / rcp.approx instead of the exact exp and division.
-// Relative error of t_fast against the reference's t (first order; every term
-// taken generously):
-//   * exp(-y) = 2^(y * -log2(e)): the RN product and the f32 constant put a
-//     relative error of at most 1.5 * 2^-24 on the exponent y * log2(e), which
-//     moves e by at most |y| * 1.5 * 2^-24 relative (log2(e) * ln(2) = 1);
-//   * ex2.approx: at most 2^-21 (4 ulp); rcp.approx: at most 2^-22; the
-//     reference's own expf: at most 2^-23; six RN roundings (1 + e, y * sig and
-//     the scaling, on each side): 6 * 2^-24;
+// Relative error of t_fast against the reference's t (first order):
+//   * exp(-y) = 2^(y * -log2(e)): the f32 constant (relative error 0.23 * 2^-24)
+//     and the RN product put a relative error of at most 1.23 * 2^-24 on the
+//     exponent y * log2(e), which moves e by at most |y| * 1.23 * 2^-24 relative
+//     (log2(e) * ln(2) = 1);
+//   * ex2.approx.ftz: at most 1.459e-7 relative, rcp.approx.ftz: at most
+//     9.83e-8 -- the maxima over every input these paths see (ex2 of [-126, 128),
+//     whose results are normal floats; rcp of [1, 2^126]), measured exhaustively
+//     on B200 and re-checked by tests/test_gpu_fast_math_bounds.py; budgeted as
+//     1.5e-7 and 1.0e-7.  Outside those ranges both sides agree exactly or round
+//     to the same int8 (1 + e == 1; e = inf gives sig = 0; a flushed rcp result
+//     makes |t| < 1e-30 on both sides);
+//   * the reference's expf (the shared dw_expf, correctly rounded): 2^-24;
+//   * seven RN roundings: 1 + e, y * sig and the scaling on the fast side; 1 + e,
+//     the division, y * sig and the scaling on the reference's: 7 * 2^-24;
 //   * a relative error r in e moves 1 + e, and so sig, by at most r relative;
 //     when e overflows (y < -88) both sides give sig = 0 and t = -0.
-// So |t_fast - t| <= |t| * (|y| * 8.9e-8 + 1.19e-6); the certificate takes
-// three times that.  The int8 result of t_fast is certified when no rounding
-// boundary (a half-integer) lies within that distance; otherwise the caller
-// recomputes the element exactly.  A tighter certificate matters: a warp takes
-// the exact path when any of its 512 elements is uncertain.
-constexpr float kSiluErrPerY = 2.7e-7f;  // 3 * 1.5 * 2^-24 (rounded up)
-constexpr float kSiluErr0 = 3.6e-6f;     // 3 * (2^-21 + 2^-22 + 2^-23 + 6 * 2^-24) (rounded up)
+// So |t_fast - t| <= |t| * (|y| * 7.33e-8 + 7.27e-7); the certificate takes 1.25
+// times that (second-order terms and |t_fast| for |t| are far below the margin).
+// The int8 result of t_fast is certified when no rounding boundary (a
+// half-integer) lies within that distance; otherwise the caller recomputes the
+// element exactly.  A tight certificate matters: the exact path is about 300
+// cycles of dependent double arithmetic that a warp waits out, and the epilogue
+// warps meet at every tile (3.6e-6 / 2.7e-7 here cost YOLOv8n b32 11% of its
+// step).
+constexpr float kEx2RelErr = 1.5e-7f;   // budget for ex2.approx.ftz (measured max 1.4584e-7)
+constexpr float kRcpRelErr = 1.0e-7f;   // budget for rcp.approx.ftz (measured max 9.8292e-8)
+constexpr float kSiluErrPerY = 9.2e-8f;  // 1.25 * 1.23 * 2^-24 (rounded up)
+constexpr float kSiluErr0 = 9.1e-7f;     // 1.25 * (1.5e-7 + 1.0e-7 + 2^-24 + 7 * 2^-24) (rounded up)
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float r;
