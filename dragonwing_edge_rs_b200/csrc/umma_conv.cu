@@ -1101,8 +1101,14 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
             bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), acc_ph, p, abort_flag, 4);
             if (ok) ok = mbar_wait(smem_u32(&res_bar[sb]), sb_ph, p, abort_flag, 5);
             // Barrier A (epilogue threads only): all-or-none abort decision; this
-            // tile's staged channel parameters are visible.
-            if (named_barrier_or(1, kEpiWarps * 32, !ok)) break;
+            // tile's staged channel parameters are visible.  With every channel
+            // staged once (chan_all) only the first tile needs it: later tiles let
+            // each warp run on (one slow warp no longer holds the others at every
+            // tile; a warp that aborts alone leaves its arrivals missing, and the
+            // MMA and store warps' bounded waits end the CTA).
+            if (p.chan_all && local > 0) {
+                if (!ok) break;
+            } else if (named_barrier_or(1, kEpiWarps * 32, !ok)) break;
             if (!p.chan_all) {  // next tile's channels into the other half (its readers finished before barrier A)
                 const int next = tile + (int)gridDim.x;
                 if (next < p.num_tiles)
