@@ -148,6 +148,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const U
     // polls first (a pipeline stage is usually only a little late, and a thread
     // woken from a suspended try_wait resumes late), then waits suspended in
     // hardware while the phase stays open (at most ~20 us per try)
+    if (mbar_test_wait(bar, parity)) return true;
 #pragma unroll 1
     for (int i = 0; i < 256; i++)
         if (mbar_try_wait(bar, parity)) return true;
@@ -1096,8 +1097,10 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
             const int sb = p.nbuf == 2 ? (local & 1) : 0;
             const uint32_t sb_ph = p.nbuf == 2 ? ((local >> 1) & 1) : (local & 1);
             uint8_t *const stage = out_stage + (size_t)sb * p.out_bytes;
-            const TileCoord tc = tile_coord(p, tile);
-            const int slot_base = p.chan_all ? tc.n0 : acc * (kChanSlots / 2);
+            // the tile's first channel (tile_coord's n0 without its divisions: the
+            // per-tile bookkeeping sits between every tile's requantisations)
+            const int n0 = p.n_tiles == 1 ? 0 : (tile % p.n_tiles) * p.bn;
+            const int slot_base = p.chan_all ? n0 : acc * (kChanSlots / 2);
             bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), acc_ph, p, abort_flag, 4);
             if (ok) ok = mbar_wait(smem_u32(&res_bar[sb]), sb_ph, p, abort_flag, 5);
             // Barrier A (epilogue threads only): all-or-none abort decision; this
@@ -1792,12 +1795,17 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         p.bk_elems = p.bk / esize;
         p.cblocks = (d.c_in + p.bk_elems - 1) / p.bk_elems;
         // Tiles for a tile width bn and at most r_cap row blocks per tile: R * bn <=
-        // 256 (two TMEM accumulator buffers within 512 columns), at most 8, and an A
-        // stage (R * 128 rows * bk) of at most 32 KiB.
+        // 256 (two TMEM accumulator buffers within 512 columns), at most 8 (16 for
+        // the 16-channel 1x1 case below), and an A stage (R * 128 rows * bk) of at
+        // most 32 KiB (64 KiB there).
         auto plan_tiles = [&](int bn, int r_cap) {
             p.bn = bn;
             p.n_tiles = (d.c_out + p.bn - 1) / p.bn;
-            int R = std::max(1, std::min({r_cap, 8, 256 / p.bn, 32768 / (kBM * p.bk)}));
+            // 1x1 int8 convs with 16 output channels (YOLOv8n's stem): up to 16 row
+            // blocks (all 512 TMEM columns, 64 KiB A stages) -- twice the work per
+            // tile hand-off (the stem conv 102 -> 86 us at b32)
+            const bool r16 = flat && bn == 16 && esize == 1;
+            int R = std::max(1, std::min({r_cap, r16 ? 16 : 8, 256 / p.bn, (r16 ? 65536 : 32768) / (kBM * p.bk)}));
             if (flat) {
                 p.rows = (long long)d.n * d.h * d.w;
                 const long long blocks = (p.rows + kBM - 1) / kBM;
@@ -1823,10 +1831,10 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
             const int v = atoi(e);
             if (v >= 16 && v <= 256 && v % 16 == 0) p.bn = v;
         }
-        int r_cap = 8;
+        int r_cap = 16;  // (the per-shape caps above keep most convs at 8)
         if (const char *e = getenv("DW_UMMA_RMAX")) {  // tuning override: at most this many row blocks per tile
             const int v = atoi(e);
-            if (v >= 1 && v <= 8) r_cap = v;
+            if (v >= 1 && v <= 16) r_cap = v;
         }
         plan_tiles(p.bn, r_cap);
         // Small problems (tiles for fewer than half the SMs): fewer row blocks per
