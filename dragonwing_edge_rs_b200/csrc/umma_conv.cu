@@ -145,12 +145,18 @@ struct ChanSmem {
 // CTA is aborting or the cap expired (then the failure is recorded).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const UmmaParams &p,
                                           volatile int *abort_flag, int site) {
-    // polls first (a pipeline stage is usually only a little late, and a thread
-    // woken from a suspended try_wait resumes late), then waits suspended in
-    // hardware while the phase stays open (at most ~20 us per try)
+    // The MMA warp's wait for a loaded stage (site 3) and the epilogue's wait for
+    // its accumulators (site 4) poll first: they are usually only a little late,
+    // and a thread woken from a suspended try_wait resumes late.  The other
+    // waits (a free stage, a free accumulator or staging buffer, a staged tile)
+    // are long and each poll is an instruction issued beside the epilogue warps
+    // of the same scheduler: they suspend at once (measured on B200: MobileNetV2's
+    // expand 173 -> 166 us, YOLOv8n b32 1.809 -> 1.797 ms).  Then all wait
+    // suspended in hardware while the phase stays open (at most ~20 us per try).
     if (mbar_test_wait(bar, parity)) return true;
+    const int polls = (site == 3 || site == 4) ? 256 : 0;
 #pragma unroll 1
-    for (int i = 0; i < 256; i++)
+    for (int i = 0; i < polls; i++)
         if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
 #pragma unroll 1
@@ -1766,13 +1772,24 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         p.flat_in = (!no_flat && !p.s2 && p.chunks == 1 && x_pitch == d.c_in && 2 * p.hw <= 256) ? 1 : 0;
         p.flat_out = (!no_flat && esize == 1 && p.bn == d.c_out && y_pitch == d.c_out) ? 1 : 0;
     } else {
-        p.bk = flat ? pick_bk(d.c_in * esize) : pick_bk_taps(d.c_in * esize);
+        // the fewest K blocks (then the least padding), 1x1 convs included: a
+        // block's padding costs no memory reads (TMA zero fill) and no MMAs (the
+        // issuer skips the 32-byte K steps past c_in), while every extra block is
+        // a pipeline stage more per tile (MobileNetV2's expand, K = 96: 3 x 32-byte
+        // blocks 166 us, one 128-byte block 159 us; its project, K = 576: 9 x 64
+        // bytes 86 us, 5 x 128 bytes 80 us; measured on B200)
+        p.bk = pick_bk_taps(d.c_in * esize);
         if (const char *e = getenv("DW_UMMA_BK")) {  // tuning override: 32, 64 or 128 bytes of K per stage
             const int v = atoi(e);
             if (v == 32 || v == 64 || v == 128) p.bk = v;
         }
         if (esize == 2 && !flat && d.stride_w > 1 && (d.c_in * esize) % p.bk) p.bk = pick_bk(d.c_in * esize);
         p.bn = pick_bn(((d.c_out + 15) / 16) * 16);
+        // 1x1 convs with a short K and more than 256 output channels (epilogue-
+        // bound): half-width tiles of two row blocks, both MMA issuers busy
+        // (MobileNetV2's 96 -> 576 expand at b32: 128 x 192 tiles 159 us,
+        // 256 x 96 tiles 151 us, measured on B200)
+        if (flat && d.c_out > 256 && d.c_in * esize <= 256 && p.bn > 128 && (p.bn / 2) % 16 == 0) p.bn /= 2;
         // 1x1 convs (epilogue-bound: few K steps per tile): a narrower K block when
         // that lets the staging be double-buffered (the fp16 staging of a 128 x 256
         // tile is 64 KiB) -- more K steps, but a tile's stores overlap the next
