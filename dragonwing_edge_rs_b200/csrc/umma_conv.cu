@@ -1772,24 +1772,32 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         p.flat_in = (!no_flat && !p.s2 && p.chunks == 1 && x_pitch == d.c_in && 2 * p.hw <= 256) ? 1 : 0;
         p.flat_out = (!no_flat && esize == 1 && p.bn == d.c_out && y_pitch == d.c_out) ? 1 : 0;
     } else {
-        // the fewest K blocks (then the least padding), 1x1 convs included: a
-        // block's padding costs no memory reads (TMA zero fill) and no MMAs (the
-        // issuer skips the 32-byte K steps past c_in), while every extra block is
-        // a pipeline stage more per tile (MobileNetV2's expand, K = 96: 3 x 32-byte
-        // blocks 166 us, one 128-byte block 159 us; its project, K = 576: 9 x 64
-        // bytes 86 us, 5 x 128 bytes 80 us; measured on B200)
-        p.bk = pick_bk_taps(d.c_in * esize);
-        if (const char *e = getenv("DW_UMMA_BK")) {  // tuning override: 32, 64 or 128 bytes of K per stage
-            const int v = atoi(e);
-            if (v == 32 || v == 64 || v == 128) p.bk = v;
-        }
-        if (esize == 2 && !flat && d.stride_w > 1 && (d.c_in * esize) % p.bk) p.bk = pick_bk(d.c_in * esize);
         p.bn = pick_bn(((d.c_out + 15) / 16) * 16);
         // 1x1 convs with a short K and more than 256 output channels (epilogue-
         // bound): half-width tiles of two row blocks, both MMA issuers busy
         // (MobileNetV2's 96 -> 576 expand at b32: 128 x 192 tiles 159 us,
         // 256 x 96 tiles 151 us, measured on B200)
         if (flat && d.c_out > 256 && d.c_in * esize <= 256 && p.bn > 128 && (p.bn / 2) % 16 == 0) p.bn /= 2;
+        // The fewest K blocks (then the least padding): a block's padding costs no
+        // memory reads (TMA zero fill) and no MMAs (the issuer skips the 32-byte K
+        // steps past c_in), while every extra block is a pipeline stage more per
+        // tile.  1x1 convs take it unless the wider A stage leaves fewer row blocks
+        // per tile (R is capped by a 32 KiB A stage): MobileNetV2's expand (K = 96,
+        // R = 2 either way) 3 x 32-byte blocks 166 us, one 128-byte block 159 us,
+        // its project (K = 576) 9 x 64 bytes 86 us, 5 x 128 bytes 80 us; YOLOv8n's
+        // 96 -> 32 C2f convs keep 32-byte blocks and 8 row blocks (128-byte blocks
+        // allow 2: 1.5 us slower each); measured on B200.
+        p.bk = pick_bk_taps(d.c_in * esize);
+        if (flat) {
+            const int bk_pad = pick_bk(d.c_in * esize);
+            auto rows_per_tile = [&](int bk) { return std::min({8, 256 / p.bn, 32768 / (kBM * bk)}); };
+            if (rows_per_tile(p.bk) < rows_per_tile(bk_pad)) p.bk = bk_pad;
+        }
+        if (const char *e = getenv("DW_UMMA_BK")) {  // tuning override: 32, 64 or 128 bytes of K per stage
+            const int v = atoi(e);
+            if (v == 32 || v == 64 || v == 128) p.bk = v;
+        }
+        if (esize == 2 && !flat && d.stride_w > 1 && (d.c_in * esize) % p.bk) p.bk = pick_bk(d.c_in * esize);
         // 1x1 convs (epilogue-bound: few K steps per tile): a narrower K block when
         // that lets the staging be double-buffered (the fp16 staging of a 128 x 256
         // tile is 64 KiB) -- more K steps, but a tile's stores overlap the next
