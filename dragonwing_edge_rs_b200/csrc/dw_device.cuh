@@ -126,8 +126,15 @@ __device__ __forceinline__ void silu_fast_bits2(int32_t a0, int32_t a1, float d0
     const float2 c = make_float2(fminf(fmaxf(t.x, -128.0f), 127.0f), fminf(fmaxf(t.y, -128.0f), 127.0f));
     const float2 r = __fadd2_rn(c, mag);
     const float2 d = __ffma2_rn(__fadd2_rn(r, nmag), make_float2(-1.0f, -1.0f), c);  // c - rint(c), exact
-    u0 |= !(__fsub_rn(0.5f, fabsf(d.x)) > __fmul_rn(fabsf(t.x), __fmaf_rn(fabsf(y.x), kSiluErrPerY, kSiluErr0)));
-    u1 |= !(__fsub_rn(0.5f, fabsf(d.y)) > __fmul_rn(fabsf(t.y), __fmaf_rn(fabsf(y.y), kSiluErrPerY, kSiluErr0)));
+    // the certificate on pairs as well: 0.5 + (-|d|) is the RN subtraction
+    // 0.5 - |d|, and the fma and product are the scalar ones lane by lane
+    // (YOLOv8n b32 step 1.797 -> 1.784 ms on B200)
+    const float2 margin = __fadd2_rn(make_float2(0.5f, 0.5f), make_float2(-fabsf(d.x), -fabsf(d.y)));
+    const float2 bound = __fmul2_rn(make_float2(fabsf(t.x), fabsf(t.y)),
+                                    __ffma2_rn(make_float2(fabsf(y.x), fabsf(y.y)), make_float2(kSiluErrPerY, kSiluErrPerY),
+                                               make_float2(kSiluErr0, kSiluErr0)));
+    u0 |= !(margin.x > bound.x);
+    u1 |= !(margin.y > bound.y);
     b0 = __float_as_uint(r.x);
     b1 = __float_as_uint(r.y);
 }
