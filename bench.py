@@ -226,7 +226,7 @@ def op_flops(op):
     """Algorithmic ops (2 x MACs; a zero-padded input channel does not count)."""
     if op.op_type == "GemmF16":
         return 2 * op.params["m"] * op.params["n"] * op.params["k"]
-    if op.op_type not in ("Conv2dRequantReluI8Nhwc", "Conv2dAddI8", "Conv2dF16", "Conv2dAddF16"):
+    if op.op_type not in ("Conv2dRequantReluI8Nhwc", "Conv2dAddI8", "Conv2dF16", "Conv2dAddF16", "Conv2dStemU8I8"):
         return 0
     d = op.params["desc"]
     ho, wo = d.out_hw()
@@ -309,9 +309,11 @@ def per_op_records(graph, op_ms):
 
 
 def roofline_units(graph, per_op):
-    """Groups per-op records into roofline units.  The stem pair the device
-    lowering makes of a 3-channel image conv (Im2colU8ToI8, then the 1x1 conv
-    that reads its 27 -> 32 channel rows) is one unit whose compulsory bytes
+    """Groups per-op records into roofline units.  The 3x3 stem on a 3-channel
+    image is one op (Conv2dStemU8I8: uint8 image in, conv output out) where
+    its shape allows; otherwise the stem pair the device lowering makes of it
+    (Im2colU8ToI8, then the 1x1 conv that reads its 27 -> 32 channel rows) is
+    one unit whose compulsory bytes
     are the uint8 image, the conv's weights and per-channel arrays, and its
     output: the im2col tensor is an artefact of the lowering, not algorithmic
     traffic.  Every other op is its own unit."""

@@ -132,6 +132,7 @@ SIGNATURES = {
     "dw_cast_f16_to_f32": ([vp, vp, vp], i32),
     "dw_unfold_w_f32_to_f16": ([vp, vp, vp] + [sz] * 9, i32),
     "dw_im2col_u8_to_i8": ([vp, vp, vp] + [sz] * 13 + [f32], i32),
+    "dw_conv2d_stem_u8_i8": ([vp, PDESC, vp, f32, vp, vp, vp, vp, vp], i32),
     # channel-range views
     "dw_conv2d_i8_view": ([vp, PDESC, ctypes.POINTER(DwView), vp, vp, vp, vp, ctypes.POINTER(DwView)], i32),
     "dw_conv2d_add_i8_view": ([vp, PDESC, ctypes.POINTER(DwView), vp, vp, vp, vp, ctypes.POINTER(DwView), f32, f32,

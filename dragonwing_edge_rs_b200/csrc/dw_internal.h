@@ -126,6 +126,9 @@ dw_status launch_umma_conv_f16(dw_backend *be, const dw_conv_desc &d, int ho, in
 
 dw_status launch_im2col_u8_i8(dw_backend *be, const uint8_t *x, int8_t *y, int n, int h, int w, int c, int kh, int kw,
                               int sh, int sw, int pt, int pl, int ho, int wo, int c_dst, float scale);
+dw_status launch_stem3_conv_u8_i8(dw_backend *be, const uint8_t *x, const int8_t *w_hwio, const EpiParams &ep,
+                                 int8_t *y, int n, int h, int w, int sh, int sw, int pt, int pl, int ho, int wo, int c_out,
+                                 float scale);
 
 // dwconv_tma.cu (TMA-fed int8 depthwise 3x3 stride 1; DW_ERR_UNSUPPORTED when the shape does not fit)
 dw_status launch_dwconv3x3_stream_i8(dw_backend *be, const dw_conv_desc &d, int ho, int wo, const int8_t *x,

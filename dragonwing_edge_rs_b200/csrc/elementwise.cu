@@ -352,6 +352,174 @@ __global__ void __launch_bounds__(256) k_im2col_stem3_band(const uint8_t *__rest
     }
 }
 
+// Fused input stem: quantisation of a 3-channel uint8 image + 3x3 conv (any
+// stride and padding the band staging covers) + bias + requantisation epilogue,
+// one pass.  The band of input rows is staged and quantised in shared memory as
+// in k_im2col_stem3_band; each thread then packs one output pixel's 27 taps in
+// (kh, kw, c) order into 7 words (the im2col's packing) and takes every output
+// channel as 7 __dp4a against that channel's staged weight words: the same
+// exact int32 sums as the reference's conv over the quantised image
+// (conv2d_i8_nhwc, ops.rs:2964-2995, the padding taps 0).  The epilogue is the
+// fused op's (SiLU: the certified fast path with the exact fall-back per
+// element, as the tensor-core epilogue; the others: epilogue_one).  The
+// 27-channel im2col tensor never reaches memory: the unit reads the uint8
+// image and writes the conv output once.
+constexpr int kStemMaxCout = 64;
+constexpr int kStemConvBand = 4;  // output rows per block
+constexpr int kStemConvRowsBytes = 36 * 1024;  // dynamic shared memory: with ~11 KB static, within the 48 KB default
+template <bool kSilu>
+__global__ void __launch_bounds__(256, 4) k_stem3_conv(const uint8_t *__restrict__ x, const int8_t *__restrict__ w_hwio,
+                                                    EpiParams ep, int8_t *__restrict__ y, int h, int w, int sh, int sw,
+                                                    int pt, int pl, int ho, int wo, int c_out, int row_bytes,
+                                                    int nbands, float inv255, float inv) {
+    extern __shared__ __align__(16) uint8_t rows[];  // [(kStemConvBand - 1) * sh + 3][row_bytes]
+    __shared__ uint8_t q8[256];
+    __shared__ uint32_t lutw[64 * 32];
+    __shared__ __align__(16) uint32_t wsm[kStemMaxCout * 8];  // [oc][k word]: taps 4k .. 4k + 3, zero past 26
+    __shared__ __align__(16) int32_t bias_s[kStemMaxCout];
+    __shared__ __align__(16) float par_s[kStemMaxCout];  // D (SiLU) or M
+    __shared__ int fast_s;
+    for (int u = threadIdx.x; u < 256; u += blockDim.x)
+        q8[u] = (uint8_t)f32_to_i8(__fmul_rn(__fmul_rn(i2f_small(u), inv255), inv));
+    for (int i = threadIdx.x; i < c_out * 8; i += blockDim.x) {
+        const int oc = i >> 3, kw4 = i & 7;
+        uint32_t v = 0;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            const int k = kw4 * 4 + b;
+            if (k < 27) v |= (uint32_t)(uint8_t)w_hwio[(size_t)k * c_out + oc] << (8 * b);
+        }
+        wsm[i] = v;
+    }
+    if (threadIdx.x == 0) fast_s = 1;
+    __syncthreads();
+    for (int oc = threadIdx.x; oc < c_out; oc += blockDim.x) {
+        bias_s[oc] = ep.bias ? __ldg(ep.bias + oc) : 0;
+        const float pv = kSilu ? (ep.D ? __ldg(ep.D + oc) : 0.0f) : (ep.M ? __ldg(ep.M + oc) : 0.0f);
+        par_s[oc] = pv;
+        if (kSilu && !(isfinite(pv) && isfinite(ep.inv_s_out))) fast_s = 0;
+    }
+    for (int i = threadIdx.x; i < 64 * 32; i += blockDim.x) {
+        const int k = i >> 5;
+        lutw[i] = (uint32_t)q8[4 * k] | (uint32_t)q8[4 * k + 1] << 8 | (uint32_t)q8[4 * k + 2] << 16 |
+                  (uint32_t)q8[4 * k + 3] << 24;
+    }
+    __syncthreads();
+    const uint8_t *lut = reinterpret_cast<const uint8_t *>(lutw) + (threadIdx.x & 31) * 4;
+    auto quant4 = [&](uint32_t v) {
+        uint32_t r = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t u = (v >> (8 * k)) & 0xFFu;
+            r |= (uint32_t)lut[((u & 0xFCu) << 5) | (u & 3u)] << (8 * k);
+        }
+        return r;
+    };
+    const int band = blockIdx.x % nbands, b = blockIdx.x / nbands;
+    const int i0 = band * kStemConvBand;
+    const int nr = (kStemConvBand - 1) * sh + 3;
+    const int units = row_bytes / 16, data_units = w * 3 / 16;
+    const int ih0 = i0 * sh - pt;
+    for (int t = threadIdx.x; t < nr * units; t += blockDim.x) {
+        const int a = t / units, u = t - a * units;
+        const int ih = ih0 + a;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (u >= 1 && u <= data_units && ih >= 0 && ih < h) {
+            const uint4 s = __ldg(reinterpret_cast<const uint4 *>(x + ((size_t)b * h + ih) * w * 3) + (u - 1));
+            v = make_uint4(quant4(s.x), quant4(s.y), quant4(s.z), quant4(s.w));
+        }
+        *reinterpret_cast<uint4 *>(rows + a * row_bytes + u * 16) = v;
+    }
+    __syncthreads();
+    const bool fast = fast_s != 0;
+    const int groups = c_out >> 3;
+    for (int r = 0; r < kStemConvBand; r++) {
+        const int oi = i0 + r;
+        if (oi >= ho) break;
+        int8_t *yrow = y + ((size_t)b * ho + oi) * wo * c_out;
+        const uint8_t *rr = rows + r * sh * row_bytes;
+        for (int j = threadIdx.x; j < wo; j += blockDim.x) {
+            const int s0 = 16 + (j * sw - pl) * 3;  // first of the 9 bytes, >= 16 - 3 * pl >= 1
+            const int base = s0 & ~3, sh8 = (s0 & 3) * 8;
+            uint32_t q[3][3];
+#pragma unroll
+            for (int a = 0; a < 3; a++) {
+                const uint32_t *wp = reinterpret_cast<const uint32_t *>(rr + a * row_bytes + base);
+                const uint32_t w0 = wp[0], w1 = wp[1], w2 = wp[2];
+                q[a][0] = __funnelshift_r(w0, w1, sh8);
+                q[a][1] = __funnelshift_r(w1, w2, sh8);
+                q[a][2] = (w2 >> sh8) & 0xffu;
+            }
+            // the 27 taps in (kh, kw, c) order, 4 per word (the im2col's packing)
+            const int X[7] = {(int)q[0][0], (int)q[0][1], (int)(q[0][2] | q[1][0] << 8),
+                              (int)(q[1][0] >> 24 | q[1][1] << 8), (int)(q[1][1] >> 24 | q[1][2] << 8 | q[2][0] << 16),
+                              (int)(q[2][0] >> 16 | q[2][1] << 16), (int)(q[2][1] >> 16 | q[2][2] << 16)};
+            // eight output channels at a time (fewer live registers: more warps per SM)
+            for (int g = 0; g < groups; g++) {
+                int32_t acc[8];
+#pragma unroll
+                for (int o = 0; o < 8; o++) {
+                    const uint4 wa = *reinterpret_cast<const uint4 *>(&wsm[(g * 8 + o) * 8]);
+                    const uint4 wb = *reinterpret_cast<const uint4 *>(&wsm[(g * 8 + o) * 8 + 4]);
+                    int32_t s = __dp4a(X[0], (int)wa.x, 0);
+                    s = __dp4a(X[1], (int)wa.y, s);
+                    s = __dp4a(X[2], (int)wa.z, s);
+                    s = __dp4a(X[3], (int)wa.w, s);
+                    s = __dp4a(X[4], (int)wb.x, s);
+                    s = __dp4a(X[5], (int)wb.y, s);
+                    acc[o] = __dp4a(X[6], (int)wb.z, s);
+                }
+                uint32_t wq[2] = {0u, 0u};
+                const int c0 = g * 8;
+                if (kSilu) {
+                    int32_t av[8];
+                    bool inr = true;
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        av[k] = (int32_t)((uint32_t)acc[k] + (uint32_t)bias_s[c0 + k]);
+                        inr &= (uint32_t)(av[k] + (1 << 22)) < (1u << 23);
+                    }
+                    uint32_t unc = 0xFFu;
+                    if (fast && inr) {
+                        unc = 0;
+#pragma unroll
+                        for (int qq = 0; qq < 2; qq++) {
+                            uint32_t bq[4];
+#pragma unroll
+                            for (int jj = 0; jj < 4; jj += 2) {
+                                const int k = qq * 4 + jj;
+                                bool u0 = false, u1 = false;
+                                silu_fast_bits2(av[k], av[k + 1], par_s[c0 + k], par_s[c0 + k + 1], ep.inv_s_out, bq[jj],
+                                                bq[jj + 1], u0, u1);
+                                unc |= ((uint32_t)u0 | (uint32_t)u1 << 1) << k;
+                            }
+                            wq[qq] = __byte_perm(__byte_perm(bq[0], bq[1], 0x0040), __byte_perm(bq[2], bq[3], 0x0040),
+                                                 0x5410);
+                        }
+                    }
+                    if (unc) {
+#pragma unroll
+                        for (int k = 0; k < 8; k++) {
+                            if (unc & (1u << k)) {
+                                const uint32_t bb = (uint8_t)epilogue_one_slow(acc[k], bias_s[c0 + k], 0.0f, par_s[c0 + k],
+                                                                               DW_EPI_SILU, ep.q6, ep.inv_s_out);
+                                wq[k >> 2] = (wq[k >> 2] & ~(0xFFu << (8 * (k & 3)))) | (bb << (8 * (k & 3)));
+                            }
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        wq[k >> 2] |= (uint32_t)(uint8_t)epilogue_one(acc[k], bias_s[c0 + k], par_s[c0 + k], 0.0f,
+                                                                      ep.epilogue, ep.q6, ep.inv_s_out)
+                                      << (8 * (k & 3));
+                }
+                *reinterpret_cast<uint2 *>(yrow + (size_t)j * c_out + c0) = make_uint2(wq[0], wq[1]);
+            }
+        }
+    }
+}
+
 // --- dequantize: ops.rs:3453-3457 ---------------------------------------------
 __global__ void k_dequantize(const int8_t *__restrict__ in, float *__restrict__ out, size_t n, float s) {
     size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
@@ -789,6 +957,34 @@ dw_status launch_im2col_u8_i8(dw_backend *be, const uint8_t *x, int8_t *y, int n
         k_im2col_u8_i8<0, 0, 0><<<grid, kThreads, 0, be->stream>>>(x, y, n, h, w, c, kh, kw, sh, sw, pt, pl, ho, wo,
                                                                     c_dst, inv255, inv);
     return dw_after_launch(be, "im2col_u8_i8");
+}
+
+dw_status launch_stem3_conv_u8_i8(dw_backend *be, const uint8_t *x, const int8_t *w_hwio, const EpiParams &ep,
+                                 int8_t *y, int n, int h, int w, int sh, int sw, int pt, int pl, int ho, int wo, int c_out,
+                                 float scale) {
+    const float inv255 = 1.0f / 255.0f, inv = 1.0f / scale;
+    // the band staging of k_im2col_stem3_band: whole 16-byte units per input row,
+    // the row at byte 16, the last pixel's 12-byte read inside the row
+    const long long last = 16 + ((long long)(wo - 1) * sw - pl) * 3 + 12;
+    const long long need = std::max<long long>(16 + (long long)w * 3, last);
+    const long long row_bytes = (need + 15) / 16 * 16;
+    const long long band_rows = (long long)(kStemConvBand - 1) * sh + 3;
+    const int nbands = (ho + kStemConvBand - 1) / kStemConvBand;
+    if (w % 16 != 0 || ((uintptr_t)x & 15) != 0 || ((uintptr_t)y & 15) != 0 || pl < 0 || pl > 5 || pt < 0 ||
+        c_out % 16 != 0 || c_out > kStemMaxCout || band_rows * row_bytes > kStemConvRowsBytes ||
+        (long long)n * nbands >= (1LL << 31))
+        return dw_fail(be, DW_ERR_UNSUPPORTED,
+                       "conv2d_stem_u8_i8: shape outside the fused stem (width a multiple of 16, c_out a multiple of 16 "
+                       "<= %d, left pad <= 5, 16-byte aligned buffers, staged rows <= %d bytes)",
+                       kStemMaxCout, kStemConvRowsBytes);
+    const size_t smem = (size_t)(band_rows * row_bytes);
+    if (ep.epilogue == DW_EPI_SILU)
+        k_stem3_conv<true><<<n * nbands, 256, smem, be->stream>>>(x, w_hwio, ep, y, h, w, sh, sw, pt, pl, ho, wo, c_out,
+                                                                  (int)row_bytes, nbands, inv255, inv);
+    else
+        k_stem3_conv<false><<<n * nbands, 256, smem, be->stream>>>(x, w_hwio, ep, y, h, w, sh, sw, pt, pl, ho, wo, c_out,
+                                                                   (int)row_bytes, nbands, inv255, inv);
+    return dw_after_launch(be, "conv2d_stem_u8_i8");
 }
 
 dw_status launch_dequantize(dw_backend *be, const int8_t *in, float *out, size_t n, float scale) {

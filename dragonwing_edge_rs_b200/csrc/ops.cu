@@ -332,6 +332,40 @@ DW_API dw_status dw_quantize_u8_to_i8(dw_backend *be, const dw_buf *in_u8, dw_bu
     return dw::launch_quantize_u8(be, (const uint8_t *)in_u8->ptr, (int8_t *)out_i8->ptr, out_i8->len, scale);
 }
 
+DW_API dw_status dw_conv2d_stem_u8_i8(dw_backend *be, const dw_conv_desc *d, const dw_buf *x_u8, float in_scale,
+                                      const dw_buf *kernel_hwio, const dw_buf *bias, const dw_buf *M, const dw_buf *D,
+                                      dw_buf *y) {
+    const char *op = "conv2d_stem_u8_i8";
+    if (!be) return DW_ERR_INVALID_ARG;
+    int ho, wo;
+    DW_TRY(check_desc(be, d, &ho, &wo, op));
+    if (d->c_in != 3 || d->k_h != 3 || d->k_w != 3 || d->group != 1)
+        return dw_fail(be, DW_ERR_UNSUPPORTED, "%s: only the 3x3 conv on a 3-channel image (c_in=%d, %dx%d, group %d)",
+                       op, d->c_in, d->k_h, d->k_w, d->group);
+    if (!(in_scale > 0.0f) || !std::isfinite(in_scale))
+        return dw_fail(be, DW_ERR_INVALID_ARG, "%s: input scale must be positive and finite", op);
+    DW_TRY(need(be, x_u8, op, "input"));
+    DW_TRY(need(be, kernel_hwio, op, "kernel"));
+    DW_TRY(need(be, y, op, "output"));
+    DW_TRY(check_len(be, x_u8, (size_t)d->n * d->h * d->w * 3, op, "input"));
+    DW_TRY(check_len(be, kernel_hwio, (size_t)27 * d->c_out, op, "kernel"));
+    DW_TRY(check_len(be, y, (size_t)d->n * ho * wo * d->c_out, op, "output"));
+    if (bias) DW_TRY(check_len(be, bias, 4 * (size_t)d->c_out, op, "bias"));
+    if (d->epilogue == DW_EPI_SILU) {
+        DW_TRY(need(be, D, op, "D (dequant scales, required by SILU)"));
+        DW_TRY(check_len(be, D, 4 * (size_t)d->c_out, op, "D"));
+    } else {
+        DW_TRY(need(be, M, op, "M (requant scales)"));
+        DW_TRY(check_len(be, M, 4 * (size_t)d->c_out, op, "M"));
+    }
+    cudaSetDevice(be->device);
+    dw::EpiParams ep{bias ? (const int32_t *)bias->ptr : nullptr, M ? (const float *)M->ptr : nullptr,
+                     D ? (const float *)D->ptr : nullptr, d->epilogue, d->q6, d->inv_s_out};
+    return dw::launch_stem3_conv_u8_i8(be, (const uint8_t *)x_u8->ptr, (const int8_t *)kernel_hwio->ptr, ep,
+                                       (int8_t *)y->ptr, d->n, d->h, d->w, d->stride_h, d->stride_w, d->pad_t,
+                                       d->pad_l, ho, wo, d->c_out, in_scale);
+}
+
 DW_API dw_status dw_im2col_u8_to_i8(dw_backend *be, const dw_buf *x_u8, dw_buf *y_i8, size_t n, size_t h, size_t w,
                                     size_t c, size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t, size_t p_l,
                                     size_t h_out, size_t w_out, size_t c_dst, float scale) {

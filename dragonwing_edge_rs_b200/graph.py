@@ -466,10 +466,30 @@ def lower_unfold_stem_f16(graph: Graph) -> Graph:
     return Graph(tensors, ops_, inits, list(graph.inputs), list(graph.outputs))
 
 
+def stem_conv_fits(n, h, w, c, d) -> bool:
+    """The shapes dw_conv2d_stem_u8_i8 takes (csrc/elementwise.cu,
+    launch_stem3_conv_u8_i8): a 3x3 group-1 conv on 3 channels, c_out a
+    multiple of 16 up to 64, the image width a multiple of 16, left padding
+    <= 5, and a band of input rows within the kernel's shared-memory budget."""
+    if c != 3 or d.k_h != 3 or d.k_w != 3 or d.group != 1 or d.c_out % 16 or d.c_out > 64 or w % 16:
+        return False
+    pt, pl, _, _ = d.pads
+    if pl > 5 or pt < 0:
+        return False
+    ho, wo = d.out_hw()
+    last = 16 + ((wo - 1) * d.stride_w - pl) * 3 + 12
+    row_bytes = (max(16 + w * 3, last) + 15) // 16 * 16
+    return (3 * d.stride_h + 3) * row_bytes <= 36 * 1024 and n * ((ho + 3) // 4) < 2 ** 31
+
+
 def lower_im2col_input_i8(graph: Graph) -> Graph:
     """Device lowering of an int8 network's first conv on a few-channel image:
     QuantizeU8 (c channels, c % 16 != 0) -> Conv2dRequantReluI8Nhwc (k_h x k_w,
-    k_h*k_w*c <= 64) becomes Im2colU8ToI8 (the quantisation fused with an
+    k_h*k_w*c <= 64).  The 3x3 conv on a 3-channel image (YOLOv8n's stem)
+    becomes one Conv2dStemU8I8 (quantisation, conv and epilogue in one kernel
+    on the CUDA cores: the conv is 27 MACs per output, and the 32-byte im2col
+    rows the tensor cores need would be written and read again); other shapes
+    become Im2colU8ToI8 (the quantisation fused with an
     im2col into c_dst = k_h*k_w*c rounded up to 16 channels) -> a 1x1 conv
     whose kernel rows are the original taps in (kh, kw, c) order, zero rows for
     the padding channels.  The integer products are the same, so the result is
@@ -494,6 +514,13 @@ def lower_im2col_input_i8(graph: Graph) -> Graph:
         if d.group != 1 or kc > 64:
             continue
         ho, wo = d.out_hw()
+        if stem_conv_fits(n, h, w, c, d):
+            # one pass: quantisation + the 3x3 conv on the CUDA cores (dw_conv2d_stem_u8_i8)
+            tensors.pop(q.outputs[0], None)
+            stem = CompiledOp(conv.name, "Conv2dStemU8I8", [q.inputs[0]] + list(conv.inputs[1:]), list(conv.outputs),
+                              dict(conv.params, in_scale=q.params["scale"]))
+            ops_ = [stem if op is conv else op for op in ops_ if op is not q]
+            break
         c_dst = (kc + 15) // 16 * 16
         u = q.outputs[0] + "_im2col"
         tensors[u] = TensorInfo(u, (n, ho, wo, c_dst), "i8", t.scale)
@@ -1177,6 +1204,12 @@ class CudaGraphRuntime:
             _, ho, wo, _ = self.graph.tensors[op.outputs[0]].shape
             x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
             return lambda: ops.resize_nearest_i8(be, x, y, n, h, w, ho, wo, c)
+        if t == "Conv2dStemU8I8":
+            desc = op.params["desc"]
+            x, wn, bn, mn, dn = op.inputs
+            bx, y = bufs[x], bufs[op.outputs[0]]
+            bw, bb, bm, bd = consts[wn], consts[bn], consts[mn], consts[dn]
+            return lambda: ops.conv2d_stem_u8_i8(be, desc, bx, op.params["in_scale"], bw, bb, bm, bd, y)
         if t == "Im2colU8ToI8":
             x, y = bufs[op.inputs[0]], bufs[op.outputs[0]]
             n, h, w, c = self.graph.tensors[op.inputs[0]].shape

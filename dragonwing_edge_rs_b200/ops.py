@@ -308,6 +308,15 @@ def unfold_w_f32_to_f16(backend, x, y, n, h, w, c, k_w, stride_w, pad_l, w_out, 
                                                    pad_l, w_out, c_dst))
 
 
+def conv2d_stem_u8_i8(backend: CudaBackend, desc: ConvDesc, x_u8: CudaBuffer, in_scale: float, w_hwio: CudaBuffer,
+                      bias, M, D, y: CudaBuffer):
+    """The input stem in one pass: the uint8 image's quantisation and the fused
+    3x3 conv on its 3 channels (contract in include/dw_cuda.h)."""
+    d = desc.to_c()
+    backend._check(L.load().dw_conv2d_stem_u8_i8(backend.handle, ctypes.byref(d), x_u8.handle, float(in_scale),
+                                                 w_hwio.handle, _h(bias), _h(M), _h(D), y.handle))
+
+
 def im2col_u8_to_i8(backend, x, y, n, h, w, c, k_h, k_w, s_h, s_w, p_t, p_l, h_out, w_out, c_dst, scale):
     """im2col of a uint8 image fused with its quantisation (contract in include/dw_cuda.h)."""
     backend._check(L.load().dw_im2col_u8_to_i8(backend.handle, x.handle, y.handle, n, h, w, c, k_h, k_w, s_h, s_w,

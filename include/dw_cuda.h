@@ -271,6 +271,22 @@ DW_API dw_status dw_quantize_u8_to_i8(dw_backend *be, const dw_buf *in_u8, dw_bu
 DW_API dw_status dw_im2col_u8_to_i8(dw_backend *be, const dw_buf *x_u8, dw_buf *y_i8, size_t n, size_t h, size_t w,
                                     size_t c, size_t k_h, size_t k_w, size_t s_h, size_t s_w, size_t p_t, size_t p_l,
                                     size_t h_out, size_t w_out, size_t c_dst, float scale);
+/* The network's input stem in one pass: dw_quantize_u8_to_i8 of a 3-channel
+ * uint8 NHWC image (scale in_scale) followed by the fused op of dw_conv2d_i8
+ * (d: the 3x3 conv on c_in = 3, group 1, any stride and padding; the same
+ * epilogue contract and bit-exact result) without the quantised image or an
+ * im2col tensor in memory.  Replaces the input path of the reference's YOLO
+ * graph: QuantizeLinear of the /255 image (quantize_f32_to_i8_scalar,
+ * crates/dragonwing-cpu/src/ops.rs:3503-3525) then its first
+ * Conv2dRequantReluI8Nhwc (conv2d_requant_relu_i8_packed,
+ * crates/dragonwing-vulkan/src/ops.rs:2294-2417).  kernel_hwio: int8 HWIO
+ * [3][3][3][c_out] as given to dw_prepare_weights_i8 (not prepared); c_out a
+ * multiple of 16 and <= 64; the image width a multiple of 16, pad_l <= 5,
+ * 16-byte aligned input and output; other shapes return DW_ERR_UNSUPPORTED
+ * (run dw_im2col_u8_to_i8 and a 1x1 dw_conv2d_i8 instead). */
+DW_API dw_status dw_conv2d_stem_u8_i8(dw_backend *be, const dw_conv_desc *d, const dw_buf *x_u8, float in_scale,
+                                      const dw_buf *kernel_hwio, const dw_buf *bias, const dw_buf *M, const dw_buf *D,
+                                      dw_buf *y);
 /* dequantize_i8_packed_to_f32 (vulkan ops.rs:2069) / cpu ops.rs:3439-3457. */
 DW_API dw_status dw_dequantize_i8_to_f32(dw_backend *be, const dw_buf *in_i8, dw_buf *out_f32, float scale);
 /* maxpool2d (cpu ops.rs:1513-1551) on int8 NHWC, with pads [t,l,b,r] taken as -inf. */

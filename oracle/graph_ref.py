@@ -56,9 +56,11 @@ def run_graph(graph, feeds: dict, threads: int = 1, batch_slice=None, return_all
 
     for op in graph.ops:
         t = op.op_type
-        if t == "Conv2dRequantReluI8Nhwc":
+        if t in ("Conv2dRequantReluI8Nhwc", "Conv2dStemU8I8"):
             d = op.params["desc"]
             x = vals[op.inputs[0]]
+            if t == "Conv2dStemU8I8":  # device lowering of QuantizeU8 + the input conv: the same two steps
+                x = dwref.quantize_u8_to_i8(x, op.params["in_scale"]).reshape(x.shape)
             n = x.shape[0]
             od = dwref.conv_desc(n, d.h, d.w, d.c_in, d.c_out, d.k_h, d.k_w, d.stride_h, d.stride_w, d.pads,
                                  d.group, d.epilogue, d.q6, d.inv_s_out)
