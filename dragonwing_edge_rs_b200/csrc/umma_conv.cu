@@ -905,6 +905,14 @@ __global__ void __launch_bounds__(umma_threads(kSilu, kF16), 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Programmatic dependent launch: this grid may start while the previous
+    // kernel on the stream finishes (its CTAs take the SMs the previous grid's
+    // last CTAs free, and run the prologue above: barriers, TMEM, descriptor
+    // table).  Every read of memory another kernel writes -- inputs, weights,
+    // per-channel arrays, residuals -- and every write come after this wait,
+    // which returns once the previous grid has completed and its writes are
+    // visible (a no-op when the launch carries no programmatic dependency).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t tmem_base = *tmem_slot;
     const int k_iters = p.mode == 2 ? p.cblocks : p.taps * p.cblocks;  // halo mode: one stage per K block, all taps
     const uint32_t acc_cols = (uint32_t)(p.R * p.bn);
@@ -2160,24 +2168,43 @@ dw_status launch_umma_conv(dw_backend *be, const dw_conv_desc &d, int ho, int wo
         attr_set[dev] = true;
     }
     const int grid = std::min(p.num_tiles, be->sm_count);
+    // Launched as a programmatic dependent of the previous kernel on the stream
+    // (the kernel waits for it after its prologue: griddepcontrol.wait), so the
+    // launch and the prologue overlap the previous grid's last wave.
+    // DW_PDL=0: tuning switch, plain stream order.
+    static const bool pdl = !(getenv("DW_PDL") && atoi(getenv("DW_PDL")) == 0);
+    auto launch = [&](KernelFn k, int threads) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3((unsigned)threads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = be->stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 1 : 0;
+        return cudaLaunchKernelEx(&cfg, k, ta, tb, ty, tr, p);
+    };
+    cudaError_t le;
     if (esize == 2) {
         const int fm = (bias_f16 ? 1 : 0) | (res_f16 ? 2 : 0) | (relu ? 4 : 0);
-        f16_kernels[fm]<<<grid, umma_threads(false, true), smem, be->stream>>>(ta, tb, ty, tr, p);
+        le = launch(f16_kernels[fm], umma_threads(false, true));
     } else if (res_i8) {
         if (ep.epilogue == DW_EPI_SILU)
-            k_umma_conv_i8<true, false, 2><<<grid, umma_threads(true, false), smem, be->stream>>>(ta, tb, ty, tr, p);
+            le = launch(k_umma_conv_i8<true, false, 2>, umma_threads(true, false));
         else if (p.epi_pipe)
-            k_umma_conv_i8<false, false, 2, true><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr,
-                                                                                                      p);
+            le = launch(k_umma_conv_i8<false, false, 2, true>, umma_threads(false, false));
         else
-            k_umma_conv_i8<false, false, 2><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr, p);
+            le = launch(k_umma_conv_i8<false, false, 2>, umma_threads(false, false));
     } else if (ep.epilogue == DW_EPI_SILU) {
-        k_umma_conv_i8<true, false, 0><<<grid, umma_threads(true, false), smem, be->stream>>>(ta, tb, ty, tr, p);
+        le = launch(k_umma_conv_i8<true, false, 0>, umma_threads(true, false));
     } else if (p.epi_pipe) {
-        k_umma_conv_i8<false, false, 0, true><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr, p);
+        le = launch(k_umma_conv_i8<false, false, 0, true>, umma_threads(false, false));
     } else {
-        k_umma_conv_i8<false, false, 0><<<grid, umma_threads(false, false), smem, be->stream>>>(ta, tb, ty, tr, p);
+        le = launch(k_umma_conv_i8<false, false, 0>, umma_threads(false, false));
     }
+    if (le != cudaSuccess) return dw_cuda_check(be, le, esize == 2 ? "umma_conv_f16 launch" : "umma_conv_i8 launch");
     return dw_after_launch(be, esize == 2 ? "umma_conv_f16" : "umma_conv_i8");
 }
 
