@@ -1606,11 +1606,16 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
         return best;
     };
     // Block arrangements, cheapest first.  Cost = waves of tiles over the SMs x
-    // (blocks per tile + 2 for a tile's fixed overhead), so padding (more
+    // (blocks per tile + a tile's fixed overhead in blocks), so padding (more
     // tiles), wave quantisation and per-tile overhead all count; then the least
-    // halo per output pixel.  The overhead constant reproduces the ranking
-    // measured on B200 for YOLOv8n's 3x3 layers (160x160 c16, 80x80 c32/c64,
-    // 40x40 c64, every arrangement).  A lexicographic key: a strict weak ordering.
+    // halo per output pixel.  A lexicographic key: a strict weak ordering.  The
+    // overhead: 2 blocks for 16-byte channel rows (paired taps, a short K per
+    // block), 0.5 for wider rows, whose longer K loop per block leaves the fixed
+    // hand-offs a smaller share (measured on B200 for YOLOv8n b32's 3x3 layers:
+    // at 80x80 with 32 and 64 channels 16 x 16-pixel tiles beat the 32 x 32 and
+    // 16 x 32 ones, conv_78 and conv_79 -8 us each, the step 1.779 -> 1.749 ms;
+    // the 16-channel 160x160 layers keep their 32 x 32 tiles).
+    const double tile_overhead = cbytes == 16 ? 2.0 : 0.5;
     struct Arr { int rw, rh; long tiles; };
     auto arrangements = [&](int n_tiles, int rmax, Arr *out) {
         int n = 0;
@@ -1621,7 +1626,7 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
             }
         auto key = [&](const Arr &a) {
             const long waves = (a.tiles + be->sm_count - 1) / be->sm_count;
-            const long cost = waves * (a.rw * a.rh + 2);
+            const double cost = (double)waves * (a.rw * a.rh + tile_overhead);
             const double halo = (double)(16 * a.rh + ekh - 1) * (8 * a.rw + ekw - 1) / (double)(a.rw * a.rh * kBM);
             return std::make_tuple(cost, halo, a.rw);
         };
