@@ -1588,7 +1588,7 @@ HaloPlan plan_halo(const dw_backend *be, const dw_conv_desc &d, int ho, int wo, 
     if (util < 0.7) return h;
     // maps of at most 40x40 pixels with 64- or 128-byte channel rows: the per-tap
     // producer's tiles fit them closer than 16 x 16-pixel halo blocks (YOLOv8n
-XX
+    // b32's 40x40 3x3s with 64 channels 27 -> 23 us, the step 1.747 -> 1.725 ms;
     // with 80 channels the halo stays ahead, 29 vs 37 us)
     if (d.c_in * esize > 32 && (d.c_in * esize) % 32 == 0 && (long)ho * wo <= 40 * 40) return h;
     const int c_out16 = ((d.c_out + 15) / 16) * 16;
